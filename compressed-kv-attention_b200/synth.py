@@ -1,0 +1,135 @@
+"""Seeded synthetic KV inputs for the benchmark configurations (numpy, host side).
+
+The same generator exists as a CUDA kernel (csrc/synth.cu, entry point kvx_synth_bf16); both
+use only integer arithmetic plus IEEE round-to-nearest float32 multiplies, so host and device
+produce bit-identical BF16 tensors.  This stands in for the reference's real Qwen2.5-0.5B dump
+(KVD1 files written by python/dump_kv.py), which is not available offline.
+
+Element value for tensor `stream`, token t, channel c (index i = t * dim + c):
+  h1 = mix64(seed * G0 + stream * G1 + i), h2 = mix64(h1 ^ G2)
+  z  = (sum of the four 16-bit lanes of h1 - 131070) * (1 / 37837.59)   ~ N(0, 1) (Irwin-Hall 4)
+  value = z * 2**s  (profile-dependent s), outliers multiply by 2**(+-9), round to BF16 (RNE).
+
+Profiles:
+  PROFILE_K       K[t,c] = N(0,1) * 2**s_c, s_c ~ U{-4..4} per channel, escape outliers
+  PROFILE_V       V ~ N(0, 0.25) (sigma 0.5), escape outliers
+  PROFILE_Q       Q ~ N(0,1)/8
+  PROFILE_NARROW  exponent uniform over 3 octaves from 2**s_c, s_c ~ U{-1..1}, 8 % outliers with
+                  exponent shifted by +-(5..9): encodes as 2-bit (config[1] layer-0 K)
+  PROFILE_WIDE_K / PROFILE_WIDE_V  as K / V, plus a fraction of 128-token blocks whose exponents
+                  spread over 61 values so the encoder must pick raw (config[4])
+"""
+from __future__ import annotations
+
+import numpy as np
+
+PROFILE_K = 0
+PROFILE_V = 1
+PROFILE_Q = 2
+PROFILE_NARROW = 3
+PROFILE_WIDE_K = 4
+PROFILE_WIDE_V = 5
+
+G0 = np.uint64(0x9E3779B97F4A7C15)
+G1 = np.uint64(0xD1B54A32D192ED03)
+G2 = np.uint64(0x5851F42D4C957F2D)
+M1 = np.uint64(0xBF58476D1CE4E5B9)
+M2 = np.uint64(0x94D049BB133111EB)
+CHAN_SALT = np.uint64(1 << 40)
+BLOCK_SALT = np.uint64(1 << 41)
+INV_SIGMA = np.float32(1.0 / 37837.59)
+
+# default outlier rates in parts per 2**32
+RATE_0P3 = int(0.003 * 2**32)
+RATE_2 = int(0.02 * 2**32)
+RATE_8 = int(0.08 * 2**32)
+RAW_BLOCK_PERCENT = 5
+
+
+def mix64(x):
+    x = np.asarray(x, dtype=np.uint64)
+    with np.errstate(over="ignore"):
+        x = x ^ (x >> np.uint64(30))
+        x = x * M1
+        x = x ^ (x >> np.uint64(27))
+        x = x * M2
+        x = x ^ (x >> np.uint64(31))
+    return x
+
+
+def _key(seed, stream, idx):
+    with np.errstate(over="ignore"):
+        return np.uint64(seed) * G0 + np.uint64(stream) * G1 + np.asarray(idx, dtype=np.uint64)
+
+
+def f32_to_bf16(x: np.ndarray) -> np.ndarray:
+    """Round-to-nearest-even float32 -> bf16 bits (inputs are finite)."""
+    b = np.asarray(x, dtype=np.float32).view(np.uint32).astype(np.uint64)
+    r = (b + np.uint64(0x7FFF) + ((b >> np.uint64(16)) & np.uint64(1))) >> np.uint64(16)
+    return (r & np.uint64(0xFFFF)).astype(np.uint16)
+
+
+def _normal(h1):
+    s = np.zeros(h1.shape, dtype=np.int64)
+    for k in range(4):
+        s += ((h1 >> np.uint64(16 * k)) & np.uint64(0xFFFF)).astype(np.int64)
+    return (s - 131070).astype(np.float32) * INV_SIGMA
+
+
+def _pow2(e):
+    return np.ldexp(np.float32(1.0), np.asarray(e, dtype=np.int32)).astype(np.float32)
+
+
+def synth_bf16(seed: int, stream: int, seq: int, dim: int, profile: int, rate: int | None = None,
+               t0: int = 0) -> np.ndarray:
+    """Generate tokens [t0, t0+seq) of a [*, dim] BF16 tensor as uint16 bits, shape [seq, dim]."""
+    t = np.arange(t0, t0 + seq, dtype=np.uint64)[:, None]
+    c = np.arange(dim, dtype=np.uint64)[None, :]
+    idx = t * np.uint64(dim) + c
+    h1 = mix64(_key(seed, stream, idx))
+    with np.errstate(over="ignore"):
+        h2 = mix64(h1 ^ G2)
+    chan = mix64(_key(seed, stream, CHAN_SALT + c))
+    if rate is None:
+        rate = {PROFILE_NARROW: RATE_8, PROFILE_WIDE_K: RATE_2, PROFILE_WIDE_V: RATE_2}.get(
+            profile, RATE_0P3)
+    outlier = (h2 & np.uint64(0xFFFFFFFF)) < np.uint64(rate)
+    up = ((h2 >> np.uint64(32)) & np.uint64(1)) == 1
+
+    if profile == PROFILE_NARROW:
+        s_c = (chan % np.uint64(3)).astype(np.int64) - 1
+        e = 127 + s_c + (h1 % np.uint64(3)).astype(np.int64)
+        shift = 5 + ((h2 >> np.uint64(40)) % np.uint64(5)).astype(np.int64)
+        e = np.where(outlier, np.where(up, e + shift, e - shift), e)
+        mant = ((h1 >> np.uint64(8)) & np.uint64(0x7F)).astype(np.int64)
+        sign = ((h1 >> np.uint64(15)) & np.uint64(1)).astype(np.int64)
+        return ((sign << 15) | ((e & 0xFF) << 7) | mant).astype(np.uint16)
+
+    z = _normal(h1)
+    if profile in (PROFILE_K, PROFILE_WIDE_K):
+        s = (chan % np.uint64(9)).astype(np.int64) - 4
+        x = z * _pow2(s)
+    elif profile in (PROFILE_V, PROFILE_WIDE_V):
+        x = z * np.float32(0.5)
+    elif profile == PROFILE_Q:
+        x = z * np.float32(0.125)
+        outlier = np.zeros_like(outlier)
+    else:
+        raise ValueError(f"unknown profile {profile}")
+    x = np.where(outlier, x * np.where(up, np.float32(512.0), np.float32(1.0 / 512.0)), x)
+    out = f32_to_bf16(x.astype(np.float32))
+    if profile in (PROFILE_WIDE_K, PROFILE_WIDE_V):
+        blk = (t // np.uint64(128))
+        bh = mix64(_key(seed, stream, BLOCK_SALT + blk))
+        wide = (bh % np.uint64(100)) < np.uint64(RAW_BLOCK_PERCENT)
+        e = 97 + ((h1 >> np.uint64(8)) % np.uint64(61)).astype(np.int64)
+        mant = ((h1 >> np.uint64(20)) & np.uint64(0x7F)).astype(np.int64)
+        sign = ((h1 >> np.uint64(27)) & np.uint64(1)).astype(np.int64)
+        wv = ((sign << 15) | (e << 7) | mant).astype(np.uint16)
+        out = np.where(np.broadcast_to(wide, out.shape), wv, out)
+    return out.astype(np.uint16)
+
+
+def stream_id(unit: int, kind: int) -> int:
+    """Stream number of tensor `kind` (0 K, 1 V, 2 Q) of unit `unit`."""
+    return unit * 3 + kind
