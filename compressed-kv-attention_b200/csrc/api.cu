@@ -1,0 +1,954 @@
+// api.cu -- host side of the C ABI (include/kvexp_b200.h).
+//
+// Mirrors the reference's public API and error behaviour (include/kvexp/attention.hpp,
+// include/kvexp/codec.hpp): the same argument checks in the same order, with each C++
+// exception type turned into a status code and its message kept in kvx_last_error().
+// Everything that computes runs on the GPU; host code only validates, walks block headers of
+// host-resident blobs (the same walk the reference does in include/kvexp/scan.hpp), moves
+// buffers and launches kernels.
+#include "codec.cuh"
+
+#include <algorithm>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+namespace kvx {
+namespace {
+
+thread_local std::string g_err;
+
+int fail(int code, const std::string &msg) {
+    g_err = msg;
+    return code;
+}
+
+#define KVX_CUDA(call)                                                                         \
+    do {                                                                                       \
+        cudaError_t e_ = (call);                                                               \
+        if (e_ != cudaSuccess)                                                                 \
+            return fail(KVX_ERR_CUDA, std::string(#call) + ": " + cudaGetErrorString(e_));     \
+    } while (0)
+
+const char *detail_message(int code, int detail) {
+    switch (detail) {
+    case DERR_TRUNC_HEADER: return "truncated xkv block header";
+    case DERR_DIM_LEN: return "xkv block dimension or length mismatch";
+    case DERR_TRUNC_RAW: return "truncated raw xkv block";
+    case DERR_MODE: return "unknown xkv block mode";
+    case DERR_TRUNC_CODED: return "truncated coded xkv block";
+    case DERR_OUT_OF_TOKENS: return "xkv decode ran out of blocks";
+    case DERR_ESC_OVERRUN:
+        return code == KVX_ERR_LOGIC ? "escape count drifted from the size model"
+                                     : "xkv escape stream overrun";
+    case DERR_KV_MISMATCH: return "xkv K and V blocks cover different token counts";
+    case DERR_TIMEOUT: return "a bounded device wait timed out";
+    case DERR_INDEX_CAP: return "xkv block index capacity exceeded";
+    case DERR_RANGE: return "xkv block index entry outside its blob";
+    default: return "device error";
+    }
+}
+
+uint32_t wait_limit_us() {
+    static uint32_t v = [] {
+        const char *e = std::getenv("KVX_WAIT_TIMEOUT_US");
+        long x = e ? std::atol(e) : 0;
+        return uint32_t(x > 0 ? x : 1000000);  // one second
+    }();
+    return v;
+}
+
+// RAII device buffer (stream-ordered allocator).
+struct DevBuf {
+    void *p = nullptr;
+    cudaStream_t s = nullptr;
+    DevBuf() = default;
+    DevBuf(const DevBuf &) = delete;
+    DevBuf &operator=(const DevBuf &) = delete;
+    ~DevBuf() {
+        if (p) cudaFreeAsync(p, s);
+    }
+    cudaError_t alloc(size_t n, cudaStream_t st) {
+        s = st;
+        return cudaMallocAsync(&p, n ? n : 16, st);
+    }
+    template <class T> T *as() const { return static_cast<T *>(p); }
+};
+
+bool is_device_ptr(const void *p) {
+    if (p == nullptr) return false;
+    cudaPointerAttributes a{};
+    if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    return a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged;
+}
+
+int check_device() {
+    int dev = 0;
+    KVX_CUDA(cudaGetDevice(&dev));
+    int major = 0;
+    KVX_CUDA(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev));
+    if (major != 10) return fail(KVX_ERR_RUNTIME, "kvexp_b200 needs an sm_100 (B200) device");
+    return KVX_OK;
+}
+
+int sm_count() {
+    int dev = 0, n = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    return n;
+}
+
+// ---- host header walk (include/kvexp/scan.hpp:28-66, :94-123) ----------------------------------
+
+struct HostIndex {
+    std::vector<kvx_block> blocks;
+    std::vector<long long> tok_start;  // first token of each block
+    long long tokens = 0;
+};
+
+int host_walk(const uint8_t *blob, size_t bytes, int dim, HostIndex &idx) {
+    idx.blocks.clear();
+    idx.tok_start.clear();
+    idx.tokens = 0;
+    size_t off = 0;
+    while (off < bytes) {
+        if (bytes - off < 8) return fail(KVX_ERR_RUNTIME, "truncated xkv block header");
+        const uint8_t *p = blob + off;
+        const int mode = p[0], nt = p[1];
+        const int nesc = int(p[2]) | (int(p[3]) << 8);
+        const int hdim = int(p[4]) | (int(p[5]) << 8);
+        if (hdim != dim || nt <= 0) return fail(KVX_ERR_RUNTIME, "xkv block dimension or length mismatch");
+        const size_t rest = bytes - off - 8;
+        size_t need;
+        if (mode == 0) {
+            need = size_t(nt) * dim * 2;
+            if (rest < need) return fail(KVX_ERR_RUNTIME, "truncated raw xkv block");
+        } else if (mode != 2 && mode != 4) {
+            return fail(KVX_ERR_RUNTIME, "unknown xkv block mode");
+        } else {
+            need = size_t(dim) + size_t(nt) * dim + size_t(exp_payload_bytes(nt, dim, mode)) +
+                   2u * size_t(nesc);
+            if (rest < need) return fail(KVX_ERR_RUNTIME, "truncated coded xkv block");
+        }
+        if (off > 0xFFFFFFFFull)
+            return fail(KVX_ERR_UNSUPPORTED, "xkv blob larger than 4 GiB per tensor");
+        kvx_block b;
+        b.offset = uint32_t(off);
+        b.n_escape = uint16_t(mode == 0 ? 0 : nesc);
+        b.mode = uint8_t(mode);
+        b.n_tokens = uint8_t(nt);
+        idx.blocks.push_back(b);
+        idx.tok_start.push_back(idx.tokens);
+        idx.tokens += nt;
+        off += 8 + need;
+    }
+    return KVX_OK;
+}
+
+// token_bounds, reference src/dispatch.cpp:17-23
+void token_bounds(int seq, int tile, int tid, int nthreads, int &a, int &b) {
+    const int ntiles = (seq + tile - 1) / tile;
+    const int b0 = int((long long)tid * ntiles / nthreads);
+    const int b1 = int((long long)(tid + 1) * ntiles / nthreads);
+    a = std::min(seq, b0 * tile);
+    b = std::min(seq, b1 * tile);
+}
+
+// The reference throws when a thread's range starts inside an encoded block
+// (include/kvexp/scan.hpp:107-109); reproduce that check for the caller's n_threads/split.
+int check_split(const std::vector<long long> &tok_start, long long tokens, int seq, int n_threads,
+                int split) {
+    const int ntiles = (seq + split - 1) / split;
+    int threads = std::max(1, n_threads);
+    threads = std::min(threads, ntiles);
+    if (threads == 1) return KVX_OK;
+    for (int t = 0; t < threads; ++t) {
+        int a, b;
+        token_bounds(seq, split, t, threads, a, b);
+        if (a >= b || a == 0) continue;
+        if (a > tokens) return fail(KVX_ERR_RUNTIME, "xkv seek past end");
+        if (a == tokens) continue;
+        if (!std::binary_search(tok_start.begin(), tok_start.end(), (long long)a))
+            return fail(KVX_ERR_RUNTIME, "token split is not aligned to an encoded block");
+    }
+    return KVX_OK;
+}
+
+// ---- shape rules of the reference backends --------------------------------------------------------
+
+int check_attention_args(int backend, const uint16_t *q, const uint16_t *k_raw,
+                         const uint16_t *v_raw, const uint8_t *k_xkv, const uint8_t *v_xkv,
+                         const float *out, int n_q, int dim, int seq, int split_tokens) {
+    // src/dispatch.cpp:31-38
+    if (q == nullptr || out == nullptr || n_q <= 0 || dim <= 0 || seq <= 0 || split_tokens <= 0)
+        return fail(KVX_ERR_INVALID_ARGUMENT, "attention_decode: bad argument");
+    const bool raw = k_raw != nullptr, xkv = k_xkv != nullptr;
+    if (raw == xkv || (v_raw != nullptr) != raw || (v_xkv != nullptr) != xkv)
+        return fail(KVX_ERR_INVALID_ARGUMENT,
+                    "attention_decode: pass raw K and V or xkv K and V, not both");
+    if (backend != KVX_BACKEND_SCALAR && backend != KVX_BACKEND_AVX2 &&
+        backend != KVX_BACKEND_AVX512BF16)
+        return fail(KVX_ERR_INVALID_ARGUMENT, "attention_decode: unknown backend");
+    // range_* shape checks (src/attention_scalar.cpp:50-52, avx2 :142-144, avx512 :157-159)
+    if (backend == KVX_BACKEND_AVX512BF16) {
+        if (dim % 32 != 0 || dim > kMaxHeadDim)
+            return fail(KVX_ERR_INVALID_ARGUMENT,
+                        "avx512 attention: head_dim must be a multiple of 32");
+    } else if (dim % 8 != 0 || dim > kMaxHeadDim) {
+        return fail(KVX_ERR_INVALID_ARGUMENT, backend == KVX_BACKEND_AVX2
+                                                  ? "avx2 attention: bad shape"
+                                                  : "scalar attention: bad shape");
+    }
+    if (!attention_dim_supported(dim))
+        return fail(KVX_ERR_UNSUPPORTED,
+                    "kvexp_b200: head_dim must be 32, 64, 128 or 256 for the GPU kernels");
+    return KVX_OK;
+}
+
+}  // namespace
+}  // namespace kvx
+
+using namespace kvx;
+
+// ---- plans -------------------------------------------------------------------------------------------
+
+struct kvx_plan_s {
+    int dim = 0;
+    bool bf16 = false;
+    int n_units = 0;      // device units (query groups of <= 8)
+    int64_t n_blocks = 0;
+    int n_teams = 0;
+    int grid = 0;
+    int n_split = 0;
+    cudaStream_t s = nullptr;
+    UnitDev *units = nullptr;
+    FlatBlock *flat = nullptr;
+    int32_t *flat_unit = nullptr;
+    int64_t *team_begin = nullptr;
+    float *partials = nullptr;
+    int32_t *split_units = nullptr;
+    int *status = nullptr;
+    std::vector<void *> owned;
+    ~kvx_plan_s() {
+        for (void *p : owned) cudaFree(p);
+    }
+};
+
+namespace {
+
+template <class T> cudaError_t plan_alloc(kvx_plan_s *p, T **dst, size_t n) {
+    void *q = nullptr;
+    cudaError_t e = cudaMalloc(&q, n ? n * sizeof(T) : 16);
+    if (e == cudaSuccess) {
+        p->owned.push_back(q);
+        *dst = static_cast<T *>(q);
+    }
+    return e;
+}
+
+int read_status(int *dev_status, bool reset) {
+    int st[2] = {0, 0};
+    KVX_CUDA(cudaMemcpy(st, dev_status, sizeof st, cudaMemcpyDeviceToHost));
+    if (st[0] == 0) return KVX_OK;
+    if (reset) cudaMemset(dev_status, 0, sizeof st);
+    return fail(st[0], detail_message(st[0], st[1]));
+}
+
+}  // namespace
+
+extern "C" {
+
+const char *kvx_last_error(void) { return g_err.c_str(); }
+
+const char *kvx_version(void) { return "kvexp_b200 0.1 (sm_100a)"; }
+
+int kvx_device_info(int *sm_major, int *sm_minor, int *sms, size_t *hbm_bytes) {
+    int dev = 0;
+    KVX_CUDA(cudaGetDevice(&dev));
+    int ma = 0, mi = 0, n = 0;
+    KVX_CUDA(cudaDeviceGetAttribute(&ma, cudaDevAttrComputeCapabilityMajor, dev));
+    KVX_CUDA(cudaDeviceGetAttribute(&mi, cudaDevAttrComputeCapabilityMinor, dev));
+    KVX_CUDA(cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev));
+    size_t fr = 0, tot = 0;
+    KVX_CUDA(cudaMemGetInfo(&fr, &tot));
+    if (sm_major) *sm_major = ma;
+    if (sm_minor) *sm_minor = mi;
+    if (sms) *sms = n;
+    if (hbm_bytes) *hbm_bytes = tot;
+    if (ma != 10) return fail(KVX_ERR_RUNTIME, "kvexp_b200 needs an sm_100 (B200) device");
+    g_err.clear();
+    return KVX_OK;
+}
+
+int kvx_plan_create(const kvx_unit *units, int n_units, int n_q, int dim, int block_tokens,
+                    kvx_plan *out) {
+    if (out == nullptr || units == nullptr || n_units <= 0 || n_q <= 0 || block_tokens <= 0 ||
+        block_tokens > 255)
+        return fail(KVX_ERR_INVALID_ARGUMENT, "kvx_plan_create: bad argument");
+    *out = nullptr;
+    if (int rc = check_device()) return rc;
+    if (!attention_dim_supported(dim))
+        return fail(KVX_ERR_UNSUPPORTED,
+                    "kvexp_b200: head_dim must be 32, 64, 128 or 256 for the GPU kernels");
+    const bool bf16 = units[0].k_index == nullptr;
+    const int groups = (n_q + 7) / 8;
+    std::vector<kvx_unit> vu;
+    std::vector<UnitDev> ud;
+    std::vector<int64_t> begin;
+    int64_t total = 0;
+    vu.reserve(size_t(n_units) * groups);
+    for (int u = 0; u < n_units; ++u) {
+        const kvx_unit &x = units[u];
+        if ((x.k_index == nullptr) != bf16 || (x.v_index == nullptr) != bf16)
+            return fail(KVX_ERR_INVALID_ARGUMENT, "kvx_plan_create: mixed raw and xkv units");
+        if (x.k == nullptr || x.v == nullptr || x.q == nullptr || x.out == nullptr || x.seq <= 0)
+            return fail(KVX_ERR_INVALID_ARGUMENT, "kvx_plan_create: bad unit");
+        if ((reinterpret_cast<uintptr_t>(x.k) | reinterpret_cast<uintptr_t>(x.v)) & 15u)
+            return fail(KVX_ERR_INVALID_ARGUMENT,
+                        "kvx_plan_create: K/V buffers must be 16-byte aligned");
+        const int nb = bf16 ? (x.seq + block_tokens - 1) / block_tokens : x.n_blocks;
+        if (nb <= 0) return fail(KVX_ERR_INVALID_ARGUMENT, "kvx_plan_create: unit without blocks");
+        for (int g = 0; g < groups; ++g) {
+            kvx_unit y = x;
+            y.n_blocks = nb;
+            vu.push_back(y);
+            UnitDev d{};
+            d.k = static_cast<const uint8_t *>(x.k);
+            d.v = static_cast<const uint8_t *>(x.v);
+            d.q = x.q + size_t(8) * g * dim;
+            d.out = x.out + size_t(8) * g * dim;
+            d.block_begin = total;
+            d.n_blocks = nb;
+            d.n_q = std::min(8, n_q - 8 * g);
+            d.q_stride = dim;
+            ud.push_back(d);
+            begin.push_back(total);
+            total += nb;
+        }
+    }
+    auto *p = new kvx_plan_s();
+    p->dim = dim;
+    p->bf16 = bf16;
+    p->n_units = int(vu.size());
+    p->n_blocks = total;
+    const int per_cta = attention_teams_per_cta(dim);
+    const int max_teams = sm_count() * per_cta;
+    p->n_teams = int(std::min<int64_t>(max_teams, total));
+    p->grid = (p->n_teams + per_cta - 1) / per_cta;
+    std::vector<int64_t> tb(size_t(p->n_teams) + 1);
+    for (int t = 0; t <= p->n_teams; ++t) tb[size_t(t)] = (int64_t)t * total / p->n_teams;
+    std::vector<int32_t> split;
+    for (int u = 0; u < p->n_units; ++u) {
+        const int t0 = team_of_block(tb.data(), p->n_teams, ud[size_t(u)].block_begin);
+        const int t1 = team_of_block(tb.data(), p->n_teams,
+                                     ud[size_t(u)].block_begin + ud[size_t(u)].n_blocks - 1);
+        if (t0 != t1) split.push_back(u);
+    }
+    p->n_split = int(split.size());
+    kvx_unit *dvu = nullptr;
+    int64_t *dbegin = nullptr;
+    cudaError_t e = cudaSuccess;
+    if ((e = plan_alloc(p, &p->units, ud.size())) != cudaSuccess ||
+        (e = plan_alloc(p, &p->flat, size_t(total))) != cudaSuccess ||
+        (e = plan_alloc(p, &p->flat_unit, size_t(total))) != cudaSuccess ||
+        (e = plan_alloc(p, &p->team_begin, tb.size())) != cudaSuccess ||
+        (e = plan_alloc(p, &p->partials, size_t(p->n_teams) * 2 * partial_stride(dim))) != cudaSuccess ||
+        (e = plan_alloc(p, &p->split_units, split.size())) != cudaSuccess ||
+        (e = plan_alloc(p, &p->status, 2)) != cudaSuccess ||
+        (e = plan_alloc(p, &dvu, vu.size())) != cudaSuccess ||
+        (e = plan_alloc(p, &dbegin, begin.size())) != cudaSuccess) {
+        delete p;
+        return fail(KVX_ERR_CUDA, std::string("kvx_plan_create: ") + cudaGetErrorString(e));
+    }
+    cudaMemcpy(p->units, ud.data(), ud.size() * sizeof(UnitDev), cudaMemcpyHostToDevice);
+    cudaMemcpy(p->team_begin, tb.data(), tb.size() * sizeof(int64_t), cudaMemcpyHostToDevice);
+    if (!split.empty())
+        cudaMemcpy(p->split_units, split.data(), split.size() * sizeof(int32_t),
+                   cudaMemcpyHostToDevice);
+    cudaMemcpy(dvu, vu.data(), vu.size() * sizeof(kvx_unit), cudaMemcpyHostToDevice);
+    cudaMemcpy(dbegin, begin.data(), begin.size() * sizeof(int64_t), cudaMemcpyHostToDevice);
+    cudaMemset(p->status, 0, 2 * sizeof(int));
+    e = launch_build_flat(dvu, dbegin, p->n_units, dim, block_tokens, bf16, p->flat, p->flat_unit,
+                          p->status, nullptr);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) {
+        delete p;
+        return fail(KVX_ERR_CUDA, std::string("kvx_plan_create: ") + cudaGetErrorString(e));
+    }
+    if (int rc = read_status(p->status, true)) {
+        delete p;
+        return rc;
+    }
+    *out = p;
+    g_err.clear();
+    return KVX_OK;
+}
+
+int kvx_plan_run(kvx_plan p, void *stream) {
+    if (p == nullptr) return fail(KVX_ERR_INVALID_ARGUMENT, "kvx_plan_run: null plan");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    AttnArgs a{};
+    a.units = p->units;
+    a.flat = p->flat;
+    a.flat_unit = p->flat_unit;
+    a.team_begin = p->team_begin;
+    a.partials = p->partials;
+    a.status = p->status;
+    a.n_teams = p->n_teams;
+    a.wait_limit = wait_limit_us();
+    KVX_CUDA(launch_attention(p->dim, p->bf16, a, p->grid, 0, s));
+    if (p->n_split > 0) {
+        CombineArgs c{};
+        c.units = p->units;
+        c.split_units = p->split_units;
+        c.team_begin = p->team_begin;
+        c.partials = p->partials;
+        c.n_teams = p->n_teams;
+        KVX_CUDA(launch_combine(p->dim, c, p->n_split, s));
+    }
+    return KVX_OK;
+}
+
+int kvx_plan_check(kvx_plan p) {
+    if (p == nullptr) return fail(KVX_ERR_INVALID_ARGUMENT, "kvx_plan_check: null plan");
+    KVX_CUDA(cudaDeviceSynchronize());
+    if (int rc = read_status(p->status, true)) return rc;
+    g_err.clear();
+    return KVX_OK;
+}
+
+int kvx_plan_launches(kvx_plan p) { return p ? 1 + (p->n_split > 0 ? 1 : 0) : 0; }
+
+void kvx_plan_destroy(kvx_plan p) { delete p; }
+
+}  // extern "C"
+
+// ---- drop-in attention ---------------------------------------------------------------------------
+
+namespace {
+
+// Device-side copy of one XKV blob (or its original pointer when already on the device) plus
+// its block index on the device.
+struct DevBlob {
+    DevBuf buf;                 // owned copy of a host blob (16-byte padded)
+    DevBuf idx;                 // device index
+    const uint8_t *ptr = nullptr;
+    int n_blocks = 0;
+    long long tokens = 0;
+    std::vector<long long> tok_start;
+};
+
+int prepare_blob(const uint8_t *blob, size_t bytes, int dim, int seq, DevBlob &db,
+                 cudaStream_t s) {
+    HostIndex hi;
+    if (!is_device_ptr(blob)) {
+        if (int rc = host_walk(blob, bytes, dim, hi)) return rc;
+        KVX_CUDA(db.buf.alloc((bytes + 31) & ~size_t(15), s));
+        KVX_CUDA(cudaMemcpyAsync(db.buf.p, blob, bytes, cudaMemcpyHostToDevice, s));
+        db.ptr = db.buf.as<uint8_t>();
+    } else {
+        if (reinterpret_cast<uintptr_t>(blob) & 15u) {
+            // keep the 16-byte alignment the bulk copies rely on
+            KVX_CUDA(db.buf.alloc((bytes + 31) & ~size_t(15), s));
+            KVX_CUDA(cudaMemcpyAsync(db.buf.p, blob, bytes, cudaMemcpyDeviceToDevice, s));
+            db.ptr = db.buf.as<uint8_t>();
+        } else {
+            db.ptr = blob;
+        }
+        // device walk, then bring the index home for the split check
+        const int cap = int(std::min<size_t>(bytes / 8 + 1, size_t(1) << 30));
+        DevBuf d_idx, d_tok, d_cnt;
+        KVX_CUDA(d_idx.alloc(size_t(cap) * sizeof(kvx_block), s));
+        KVX_CUDA(d_tok.alloc(size_t(cap) * sizeof(uint32_t), s));
+        KVX_CUDA(d_cnt.alloc(4 * sizeof(long long), s));
+        KVX_CUDA(cudaMemsetAsync(d_cnt.p, 0, 4 * sizeof(long long), s));
+        int *counts = d_cnt.as<int>();
+        long long *ntok = d_cnt.as<long long>() + 1;
+        int *status = d_cnt.as<int>() + 4;
+        KVX_CUDA(launch_index_walk(db.ptr, bytes, dim, d_idx.as<kvx_block>(), d_tok.as<uint32_t>(),
+                                   cap, counts, ntok, status, s));
+        long long host_cnt[4];
+        KVX_CUDA(cudaMemcpyAsync(host_cnt, d_cnt.p, sizeof host_cnt, cudaMemcpyDeviceToHost, s));
+        KVX_CUDA(cudaStreamSynchronize(s));
+        const int *hc = reinterpret_cast<const int *>(host_cnt);
+        if (hc[4] != 0) return fail(hc[4], detail_message(hc[4], hc[5]));
+        const int nb = hc[0];
+        hi.blocks.resize(static_cast<size_t>(nb));
+        std::vector<uint32_t> ts(static_cast<size_t>(nb));
+        KVX_CUDA(cudaMemcpy(hi.blocks.data(), d_idx.p, size_t(nb) * sizeof(kvx_block),
+                            cudaMemcpyDeviceToHost));
+        KVX_CUDA(cudaMemcpy(ts.data(), d_tok.p, size_t(nb) * sizeof(uint32_t),
+                            cudaMemcpyDeviceToHost));
+        hi.tok_start.assign(ts.begin(), ts.end());
+        hi.tokens = host_cnt[1];
+    }
+    if (hi.tokens < seq) return fail(KVX_ERR_RUNTIME, "xkv decode ran out of blocks");
+    // blocks covering [0, seq)
+    int nb = 0;
+    while (nb < int(hi.blocks.size()) && hi.tok_start[size_t(nb)] < seq) ++nb;
+    db.n_blocks = nb;
+    db.tokens = hi.tokens;
+    db.tok_start = hi.tok_start;
+    KVX_CUDA(db.idx.alloc(size_t(std::max(nb, 1)) * sizeof(kvx_block), s));
+    if (nb > 0)
+        KVX_CUDA(cudaMemcpyAsync(db.idx.p, hi.blocks.data(), size_t(nb) * sizeof(kvx_block),
+                                 cudaMemcpyHostToDevice, s));
+    // the host copy above reads hi.blocks: finish before it goes out of scope
+    KVX_CUDA(cudaStreamSynchronize(s));
+    return KVX_OK;
+}
+
+// Copy (or alias) a host/device array to the device.
+int to_device(const void *src, size_t bytes, DevBuf &buf, const void *&dptr, cudaStream_t s) {
+    if (is_device_ptr(src) && (reinterpret_cast<uintptr_t>(src) & 15u) == 0) {
+        dptr = src;
+        return KVX_OK;
+    }
+    KVX_CUDA(buf.alloc((bytes + 31) & ~size_t(15), s));
+    KVX_CUDA(cudaMemcpyAsync(buf.p, src, bytes,
+                             is_device_ptr(src) ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice,
+                             s));
+    dptr = buf.p;
+    return KVX_OK;
+}
+
+int run_units(std::vector<kvx_unit> &units, int n_q, int dim, int block_tokens, cudaStream_t s) {
+    KVX_CUDA(cudaStreamSynchronize(s));
+    kvx_plan plan = nullptr;
+    if (int rc = kvx_plan_create(units.data(), int(units.size()), n_q, dim, block_tokens, &plan))
+        return rc;
+    int rc = kvx_plan_run(plan, s);
+    if (rc == KVX_OK) rc = kvx_plan_check(plan);
+    kvx_plan_destroy(plan);
+    return rc;
+}
+
+}  // namespace
+
+extern "C" int kvx_attention_decode(int backend, const uint16_t *q, const uint16_t *k_raw,
+                                    const uint16_t *v_raw, const uint8_t *k_xkv, size_t k_bytes,
+                                    const uint8_t *v_xkv, size_t v_bytes, float *out, int n_q,
+                                    int dim, int seq, int n_threads, int split_tokens) {
+    if (int rc = check_attention_args(backend, q, k_raw, v_raw, k_xkv, v_xkv, out, n_q, dim, seq,
+                                      split_tokens))
+        return rc;
+    if (int rc = check_device()) return rc;
+    cudaStream_t s = nullptr;
+    const bool xkv = k_xkv != nullptr;
+    DevBlob kb, vb;
+    DevBuf kr, vr, qb, ob;
+    kvx_unit u{};
+    int block = split_tokens;
+    if (xkv) {
+        if (int rc = prepare_blob(k_xkv, k_bytes, dim, seq, kb, s)) return rc;
+        if (int rc = prepare_blob(v_xkv, v_bytes, dim, seq, vb, s)) return rc;
+        if (int rc = check_split(kb.tok_start, kb.tokens, seq, n_threads, split_tokens)) return rc;
+        if (int rc = check_split(vb.tok_start, vb.tokens, seq, n_threads, split_tokens)) return rc;
+        if (kb.n_blocks != vb.n_blocks)
+            return fail(KVX_ERR_RUNTIME, "xkv K and V blocks cover different token counts");
+        u.k = kb.ptr;
+        u.v = vb.ptr;
+        u.k_index = kb.idx.as<kvx_block>();
+        u.v_index = vb.idx.as<kvx_block>();
+        u.k_bytes = k_bytes;
+        u.v_bytes = v_bytes;
+        u.n_blocks = kb.n_blocks;
+        block = 128;
+    } else {
+        if (block > 255) block = 255;
+        const void *kp = nullptr, *vp = nullptr;
+        if (int rc = to_device(k_raw, size_t(seq) * dim * 2, kr, kp, s)) return rc;
+        if (int rc = to_device(v_raw, size_t(seq) * dim * 2, vr, vp, s)) return rc;
+        u.k = kp;
+        u.v = vp;
+    }
+    const void *qp = nullptr;
+    if (int rc = to_device(q, size_t(n_q) * dim * 2, qb, qp, s)) return rc;
+    const bool out_dev = is_device_ptr(out) && (reinterpret_cast<uintptr_t>(out) & 3u) == 0;
+    float *op = out;
+    if (!out_dev) {
+        KVX_CUDA(ob.alloc(size_t(n_q) * dim * 4, s));
+        op = ob.as<float>();
+    }
+    u.q = static_cast<const uint16_t *>(qp);
+    u.out = op;
+    u.seq = seq;
+    std::vector<kvx_unit> us{u};
+    if (int rc = run_units(us, n_q, dim, block, s)) return rc;
+    if (!out_dev) KVX_CUDA(cudaMemcpy(out, op, size_t(n_q) * dim * 4, cudaMemcpyDeviceToHost));
+    g_err.clear();
+    return KVX_OK;
+}
+
+extern "C" int kvx_attention_decode_units(int backend, int n_units, const uint16_t *const *q,
+                                          const uint8_t *const *k_xkv, const size_t *k_bytes,
+                                          const uint8_t *const *v_xkv, const size_t *v_bytes,
+                                          float *const *out, int n_q, int dim, int seq,
+                                          int split_tokens) {
+    if (n_units <= 0 || q == nullptr || k_xkv == nullptr || v_xkv == nullptr ||
+        k_bytes == nullptr || v_bytes == nullptr || out == nullptr)
+        return fail(KVX_ERR_INVALID_ARGUMENT, "attention_decode: bad argument");
+    for (int u = 0; u < n_units; ++u)
+        if (int rc = check_attention_args(backend, q[u], nullptr, nullptr, k_xkv[u], v_xkv[u],
+                                          out[u], n_q, dim, seq, split_tokens))
+            return rc;
+    if (int rc = check_device()) return rc;
+    cudaStream_t s = nullptr;
+    // one device arena for every host blob and query, copied with one transfer per buffer
+    std::vector<size_t> koff(static_cast<size_t>(n_units)), voff(static_cast<size_t>(n_units)), qoff(static_cast<size_t>(n_units));
+    size_t arena = 0;
+    auto place = [&](size_t bytes) {
+        const size_t at = arena;
+        arena += (bytes + 31) & ~size_t(15);
+        return at;
+    };
+    for (int u = 0; u < n_units; ++u) {
+        koff[size_t(u)] = is_device_ptr(k_xkv[u]) ? SIZE_MAX : place(k_bytes[u]);
+        voff[size_t(u)] = is_device_ptr(v_xkv[u]) ? SIZE_MAX : place(v_bytes[u]);
+        qoff[size_t(u)] = is_device_ptr(q[u]) ? SIZE_MAX : place(size_t(n_q) * dim * 2);
+    }
+    const size_t out_bytes = size_t(n_q) * dim * 4;
+    const size_t out_at = arena;
+    arena += size_t(n_units) * out_bytes;
+    DevBuf ar;
+    KVX_CUDA(ar.alloc(arena, s));
+    uint8_t *A = ar.as<uint8_t>();
+    std::vector<HostIndex> kidx(static_cast<size_t>(n_units)), vidx(static_cast<size_t>(n_units));
+    for (int u = 0; u < n_units; ++u) {
+        if (koff[size_t(u)] != SIZE_MAX)
+            KVX_CUDA(cudaMemcpyAsync(A + koff[size_t(u)], k_xkv[u], k_bytes[u], cudaMemcpyHostToDevice, s));
+        if (voff[size_t(u)] != SIZE_MAX)
+            KVX_CUDA(cudaMemcpyAsync(A + voff[size_t(u)], v_xkv[u], v_bytes[u], cudaMemcpyHostToDevice, s));
+        if (qoff[size_t(u)] != SIZE_MAX)
+            KVX_CUDA(cudaMemcpyAsync(A + qoff[size_t(u)], q[u], size_t(n_q) * dim * 2,
+                                     cudaMemcpyHostToDevice, s));
+    }
+    // header walks of the host blobs overlap the transfers
+    std::vector<DevBlob> dk(static_cast<size_t>(n_units)), dv(static_cast<size_t>(n_units));
+    std::vector<kvx_unit> units(static_cast<size_t>(n_units));
+    std::vector<std::vector<kvx_block>> hostblocks;
+    size_t idx_entries = 0;
+    for (int u = 0; u < n_units; ++u) {
+        for (int t = 0; t < 2; ++t) {
+            const uint8_t *blob = t == 0 ? k_xkv[u] : v_xkv[u];
+            const size_t bytes = t == 0 ? k_bytes[u] : v_bytes[u];
+            const size_t at = t == 0 ? koff[size_t(u)] : voff[size_t(u)];
+            HostIndex &hi = t == 0 ? kidx[size_t(u)] : vidx[size_t(u)];
+            if (at == SIZE_MAX) {
+                DevBlob &db = t == 0 ? dk[size_t(u)] : dv[size_t(u)];
+                if (int rc = prepare_blob(blob, bytes, dim, seq, db, s)) return rc;
+                hi.tok_start = db.tok_start;
+                hi.tokens = db.tokens;
+                hi.blocks.resize(size_t(db.n_blocks));
+                KVX_CUDA(cudaMemcpy(hi.blocks.data(), db.idx.p,
+                                    size_t(db.n_blocks) * sizeof(kvx_block), cudaMemcpyDeviceToHost));
+            } else {
+                if (int rc = host_walk(blob, bytes, dim, hi)) return rc;
+                if (hi.tokens < seq) return fail(KVX_ERR_RUNTIME, "xkv decode ran out of blocks");
+                int nb = 0;
+                while (nb < int(hi.blocks.size()) && hi.tok_start[size_t(nb)] < seq) ++nb;
+                hi.blocks.resize(static_cast<size_t>(nb));
+            }
+            idx_entries += hi.blocks.size();
+        }
+        if (kidx[size_t(u)].blocks.size() != vidx[size_t(u)].blocks.size())
+            return fail(KVX_ERR_RUNTIME, "xkv K and V blocks cover different token counts");
+    }
+    std::vector<kvx_block> all;
+    all.reserve(idx_entries);
+    std::vector<size_t> kstart(static_cast<size_t>(n_units)), vstart(static_cast<size_t>(n_units));
+    for (int u = 0; u < n_units; ++u) {
+        kstart[size_t(u)] = all.size();
+        all.insert(all.end(), kidx[size_t(u)].blocks.begin(), kidx[size_t(u)].blocks.end());
+        vstart[size_t(u)] = all.size();
+        all.insert(all.end(), vidx[size_t(u)].blocks.begin(), vidx[size_t(u)].blocks.end());
+    }
+    DevBuf didx;
+    KVX_CUDA(didx.alloc(std::max<size_t>(all.size(), 1) * sizeof(kvx_block), s));
+    KVX_CUDA(cudaMemcpyAsync(didx.p, all.data(), all.size() * sizeof(kvx_block),
+                             cudaMemcpyHostToDevice, s));
+    for (int u = 0; u < n_units; ++u) {
+        kvx_unit &x = units[size_t(u)];
+        x.k = koff[size_t(u)] == SIZE_MAX ? dk[size_t(u)].ptr : A + koff[size_t(u)];
+        x.v = voff[size_t(u)] == SIZE_MAX ? dv[size_t(u)].ptr : A + voff[size_t(u)];
+        x.k_index = didx.as<kvx_block>() + kstart[size_t(u)];
+        x.v_index = didx.as<kvx_block>() + vstart[size_t(u)];
+        x.q = qoff[size_t(u)] == SIZE_MAX ? q[u]
+                                          : reinterpret_cast<const uint16_t *>(A + qoff[size_t(u)]);
+        x.out = reinterpret_cast<float *>(A + out_at + size_t(u) * out_bytes);
+        x.k_bytes = k_bytes[u];
+        x.v_bytes = v_bytes[u];
+        x.n_blocks = int(kidx[size_t(u)].blocks.size());
+        x.seq = seq;
+    }
+    if (int rc = run_units(units, n_q, dim, 128, s)) return rc;
+    for (int u = 0; u < n_units; ++u)
+        KVX_CUDA(cudaMemcpyAsync(out[u], A + out_at + size_t(u) * out_bytes, out_bytes,
+                                 is_device_ptr(out[u]) ? cudaMemcpyDeviceToDevice
+                                                       : cudaMemcpyDeviceToHost,
+                                 s));
+    KVX_CUDA(cudaStreamSynchronize(s));
+    g_err.clear();
+    return KVX_OK;
+}
+
+// ---- codec -----------------------------------------------------------------------------------------
+
+namespace {
+
+int check_encode_args(const void *kv, int seq_len, int head_dim, int block_tokens) {
+    // src/codec.cpp:40-52
+    if (kv == nullptr || seq_len <= 0 || head_dim <= 0 || block_tokens <= 0)
+        return fail(KVX_ERR_INVALID_ARGUMENT, "encode_bf16: empty input");
+    if (head_dim % 4 != 0 || head_dim > kMaxHeadDim)
+        return fail(KVX_ERR_INVALID_ARGUMENT,
+                    "encode_bf16: head_dim must be a multiple of 4 and at most 256");
+    if (block_tokens > 255)
+        return fail(KVX_ERR_INVALID_ARGUMENT, "encode_bf16: block_tokens must fit in a byte");
+    if ((long long)block_tokens * head_dim > 65535)
+        return fail(KVX_ERR_INVALID_ARGUMENT, "encode_bf16: block escape count would not fit in u16");
+    return KVX_OK;
+}
+
+size_t blob_bound(int seq, int dim, int bt) {
+    const size_t nb = (size_t(seq) + size_t(bt) - 1) / size_t(bt);
+    return nb * 8u + 2u * size_t(seq) * size_t(dim);
+}
+
+// Encode n device tensors: analyze, lay out, emit.  Offsets are relative to `arena`.
+int encode_device(const uint16_t *const *dev_tensors_host, int n, int seq, int dim, int bt,
+                  uint8_t *arena, size_t cap, kvx_block *index, uint64_t *blob_off,
+                  uint64_t *blob_bytes, cudaStream_t s) {
+    const int nb_per = (seq + bt - 1) / bt;
+    const size_t nb = size_t(n) * size_t(nb_per);
+    DevBuf tens, blocks, bases, boff, toff, status;
+    KVX_CUDA(tens.alloc(size_t(n) * sizeof(void *), s));
+    KVX_CUDA(cudaMemcpyAsync(tens.p, dev_tensors_host, size_t(n) * sizeof(void *),
+                             cudaMemcpyHostToDevice, s));
+    KVX_CUDA(blocks.alloc(nb * sizeof(EncBlock), s));
+    KVX_CUDA(bases.alloc(nb * size_t(dim), s));
+    KVX_CUDA(status.alloc(2 * sizeof(int), s));
+    KVX_CUDA(cudaMemsetAsync(status.p, 0, 2 * sizeof(int), s));
+    const uint16_t *const *dt = tens.as<const uint16_t *const>();
+    KVX_CUDA(launch_encode_analyze(dt, n, seq, dim, bt, blocks.as<EncBlock>(), bases.as<uint8_t>(), s));
+    std::vector<EncBlock> hb(nb);
+    KVX_CUDA(cudaMemcpyAsync(hb.data(), blocks.p, nb * sizeof(EncBlock), cudaMemcpyDeviceToHost, s));
+    KVX_CUDA(cudaStreamSynchronize(s));
+    std::vector<uint64_t> bo(nb), to(static_cast<size_t>(n));
+    uint64_t at = 0;
+    for (int t = 0; t < n; ++t) {
+        to[size_t(t)] = at;
+        uint64_t sz = 0;
+        for (int b = 0; b < nb_per; ++b) {
+            bo[size_t(t) * nb_per + b] = at + sz;
+            sz += hb[size_t(t) * nb_per + b].bytes;
+        }
+        if (sz > 0xFFFFFFFFull)
+            return fail(KVX_ERR_UNSUPPORTED, "xkv blob larger than 4 GiB per tensor");
+        blob_bytes[t] = sz;
+        blob_off[t] = at;
+        at += (sz + 16 + 15) & ~uint64_t(15);
+    }
+    if (at > cap) return fail(KVX_ERR_INVALID_ARGUMENT, "encode: arena capacity too small");
+    KVX_CUDA(boff.alloc(nb * sizeof(uint64_t), s));
+    KVX_CUDA(toff.alloc(size_t(n) * sizeof(uint64_t), s));
+    KVX_CUDA(cudaMemcpyAsync(boff.p, bo.data(), nb * sizeof(uint64_t), cudaMemcpyHostToDevice, s));
+    KVX_CUDA(cudaMemcpyAsync(toff.p, to.data(), size_t(n) * sizeof(uint64_t), cudaMemcpyHostToDevice, s));
+    KVX_CUDA(launch_encode_emit(dt, n, seq, dim, bt, blocks.as<EncBlock>(), bases.as<uint8_t>(),
+                                boff.as<uint64_t>(), arena, index, toff.as<uint64_t>(),
+                                status.as<int>(), s));
+    KVX_CUDA(cudaStreamSynchronize(s));
+    return read_status(status.as<int>(), false);
+}
+
+}  // namespace
+
+extern "C" size_t kvx_encode_bound(int seq_len, int head_dim, int block_tokens) {
+    if (seq_len <= 0 || head_dim <= 0 || block_tokens <= 0) return 0;
+    return blob_bound(seq_len, head_dim, block_tokens);
+}
+
+extern "C" int kvx_encode_bf16(const uint16_t *kv, int seq_len, int head_dim, int block_tokens,
+                               uint8_t *out, size_t out_capacity, size_t *out_bytes) {
+    if (int rc = check_encode_args(kv, seq_len, head_dim, block_tokens)) return rc;
+    if (out == nullptr) return fail(KVX_ERR_INVALID_ARGUMENT, "encode_bf16: null output");
+    if (int rc = check_device()) return rc;
+    cudaStream_t s = nullptr;
+    DevBuf src, arena, index;
+    const void *dsrc = nullptr;
+    if (int rc = to_device(kv, size_t(seq_len) * head_dim * 2, src, dsrc, s)) return rc;
+    const size_t cap = blob_bound(seq_len, head_dim, block_tokens) + 64;
+    KVX_CUDA(arena.alloc(cap, s));
+    const int nb = (seq_len + block_tokens - 1) / block_tokens;
+    KVX_CUDA(index.alloc(size_t(nb) * sizeof(kvx_block), s));
+    const uint16_t *tp = static_cast<const uint16_t *>(dsrc);
+    uint64_t boff = 0, bbytes = 0;
+    if (int rc = encode_device(&tp, 1, seq_len, head_dim, block_tokens, arena.as<uint8_t>(), cap,
+                               index.as<kvx_block>(), &boff, &bbytes, s))
+        return rc;
+    if (bbytes > out_capacity) return fail(KVX_ERR_INVALID_ARGUMENT, "encode_bf16: output capacity too small");
+    KVX_CUDA(cudaMemcpy(out, arena.as<uint8_t>() + boff, bbytes,
+                        is_device_ptr(out) ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost));
+    if (out_bytes) *out_bytes = bbytes;
+    g_err.clear();
+    return KVX_OK;
+}
+
+extern "C" int kvx_decode_bf16(const uint8_t *blob, size_t bytes, int seq_len, int head_dim,
+                               uint16_t *out) {
+    if (blob == nullptr || out == nullptr || seq_len <= 0 || head_dim <= 0)
+        return fail(KVX_ERR_INVALID_ARGUMENT, "decode_bf16: bad argument");
+    if (int rc = check_device()) return rc;
+    cudaStream_t s = nullptr;
+    DevBlob db;
+    if (int rc = prepare_blob(blob, bytes, head_dim, seq_len, db, s)) return rc;
+    DevBuf tok, ob, st;
+    std::vector<uint32_t> ts(db.tok_start.begin(), db.tok_start.begin() + db.n_blocks);
+    KVX_CUDA(tok.alloc(std::max<size_t>(ts.size(), 1) * 4, s));
+    KVX_CUDA(cudaMemcpyAsync(tok.p, ts.data(), ts.size() * 4, cudaMemcpyHostToDevice, s));
+    const size_t ob_bytes = size_t(seq_len) * head_dim * 2;
+    const bool out_dev = is_device_ptr(out);
+    uint16_t *op = out;
+    if (!out_dev) {
+        KVX_CUDA(ob.alloc(ob_bytes, s));
+        op = ob.as<uint16_t>();
+    }
+    KVX_CUDA(st.alloc(2 * sizeof(int), s));
+    KVX_CUDA(cudaMemsetAsync(st.p, 0, 2 * sizeof(int), s));
+    KVX_CUDA(launch_decode(db.ptr, db.idx.as<kvx_block>(), tok.as<uint32_t>(), db.n_blocks,
+                           head_dim, seq_len, op, st.as<int>(), s));
+    KVX_CUDA(cudaStreamSynchronize(s));
+    if (int rc = read_status(st.as<int>(), false)) return rc;
+    if (!out_dev) KVX_CUDA(cudaMemcpy(out, op, ob_bytes, cudaMemcpyDeviceToHost));
+    g_err.clear();
+    return KVX_OK;
+}
+
+extern "C" int kvx_xkv_index(const uint8_t *blob, size_t bytes, int head_dim, kvx_block *index,
+                             int max_blocks, int *n_blocks, long long *n_tokens) {
+    if (blob == nullptr || index == nullptr || max_blocks <= 0 || head_dim <= 0)
+        return fail(KVX_ERR_INVALID_ARGUMENT, "kvx_xkv_index: bad argument");
+    if (!is_device_ptr(blob) || !is_device_ptr(index))
+        return fail(KVX_ERR_INVALID_ARGUMENT, "kvx_xkv_index: blob and index must be device memory");
+    cudaStream_t s = nullptr;
+    DevBuf cnt;
+    KVX_CUDA(cnt.alloc(4 * sizeof(long long), s));
+    KVX_CUDA(cudaMemsetAsync(cnt.p, 0, 4 * sizeof(long long), s));
+    KVX_CUDA(launch_index_walk(blob, bytes, head_dim, index, nullptr, max_blocks, cnt.as<int>(),
+                               cnt.as<long long>() + 1, cnt.as<int>() + 4, s));
+    long long h[4];
+    KVX_CUDA(cudaMemcpyAsync(h, cnt.p, sizeof h, cudaMemcpyDeviceToHost, s));
+    KVX_CUDA(cudaStreamSynchronize(s));
+    const int *hc = reinterpret_cast<const int *>(h);
+    if (hc[4] != 0) return fail(hc[4], detail_message(hc[4], hc[5]));
+    if (n_blocks) *n_blocks = hc[0];
+    if (n_tokens) *n_tokens = h[1];
+    g_err.clear();
+    return KVX_OK;
+}
+
+extern "C" int kvx_encode_batch_bounds(int n_tensors, int seq, int head_dim, int block_tokens,
+                                       size_t *arena_bytes, size_t *index_entries) {
+    if (n_tensors <= 0) return fail(KVX_ERR_INVALID_ARGUMENT, "encode_batch: bad argument");
+    if (int rc = check_encode_args(reinterpret_cast<const void *>(1), seq, head_dim, block_tokens))
+        return rc;
+    const size_t per = (blob_bound(seq, head_dim, block_tokens) + 16 + 15) & ~size_t(15);
+    if (arena_bytes) *arena_bytes = per * size_t(n_tensors) + 64;
+    if (index_entries)
+        *index_entries = size_t(n_tensors) * size_t((seq + block_tokens - 1) / block_tokens);
+    return KVX_OK;
+}
+
+extern "C" int kvx_encode_batch(int n_tensors, const uint16_t *const *kv, int seq, int head_dim,
+                                int block_tokens, uint8_t *arena, size_t arena_capacity,
+                                kvx_block *index, uint64_t *blob_offset, uint64_t *blob_bytes,
+                                void *stream) {
+    if (n_tensors <= 0 || kv == nullptr || arena == nullptr || index == nullptr ||
+        blob_offset == nullptr || blob_bytes == nullptr)
+        return fail(KVX_ERR_INVALID_ARGUMENT, "encode_batch: bad argument");
+    if (int rc = check_encode_args(kv[0], seq, head_dim, block_tokens)) return rc;
+    if (reinterpret_cast<uintptr_t>(arena) & 15u)
+        return fail(KVX_ERR_INVALID_ARGUMENT, "encode_batch: arena must be 16-byte aligned");
+    if (int rc = encode_device(kv, n_tensors, seq, head_dim, block_tokens, arena, arena_capacity,
+                               index, blob_offset, blob_bytes, static_cast<cudaStream_t>(stream)))
+        return rc;
+    g_err.clear();
+    return KVX_OK;
+}
+
+extern "C" int kvx_cache_append(const uint16_t *kv_new, int n_new, int head_dim, int block_tokens,
+                                uint8_t *blob, size_t at, size_t capacity, kvx_block *index,
+                                size_t *bytes_written, int *blocks_written, void *stream) {
+    if (int rc = check_encode_args(kv_new, n_new, head_dim, block_tokens)) return rc;
+    if (blob == nullptr || index == nullptr)
+        return fail(KVX_ERR_INVALID_ARGUMENT, "cache_append: bad argument");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const size_t cap = blob_bound(n_new, head_dim, block_tokens) + 64;
+    DevBuf tmp;
+    KVX_CUDA(tmp.alloc(cap, s));
+    uint64_t boff = 0, bbytes = 0;
+    const int nb = (n_new + block_tokens - 1) / block_tokens;
+    if (int rc = encode_device(&kv_new, 1, n_new, head_dim, block_tokens, tmp.as<uint8_t>(), cap,
+                               index, &boff, &bbytes, s))
+        return rc;
+    if (at + bbytes > capacity) return fail(KVX_ERR_INVALID_ARGUMENT, "cache_append: blob capacity too small");
+    KVX_CUDA(cudaMemcpyAsync(blob + at, tmp.as<uint8_t>() + boff, bbytes, cudaMemcpyDeviceToDevice, s));
+    // shift the new index entries by `at`
+    std::vector<kvx_block> hi(static_cast<size_t>(nb));
+    KVX_CUDA(cudaMemcpyAsync(hi.data(), index, size_t(nb) * sizeof(kvx_block), cudaMemcpyDeviceToHost, s));
+    KVX_CUDA(cudaStreamSynchronize(s));
+    for (auto &b : hi) {
+        if (uint64_t(b.offset) + at > 0xFFFFFFFFull)
+            return fail(KVX_ERR_UNSUPPORTED, "xkv blob larger than 4 GiB per tensor");
+        b.offset = uint32_t(b.offset + at);
+    }
+    KVX_CUDA(cudaMemcpyAsync(index, hi.data(), size_t(nb) * sizeof(kvx_block), cudaMemcpyHostToDevice, s));
+    KVX_CUDA(cudaStreamSynchronize(s));
+    if (bytes_written) *bytes_written = bbytes;
+    if (blocks_written) *blocks_written = nb;
+    g_err.clear();
+    return KVX_OK;
+}
+
+extern "C" int kvx_synth_bf16(uint16_t *out, int seq, int dim, uint64_t seed, uint64_t stream_id,
+                              int profile, uint32_t rate, void *stream) {
+    if (out == nullptr || seq <= 0 || dim <= 0 || profile < 0 || profile > 5)
+        return fail(KVX_ERR_INVALID_ARGUMENT, "kvx_synth_bf16: bad argument");
+    KVX_CUDA(launch_synth(out, seq, dim, seed, stream_id, profile, rate,
+                          static_cast<cudaStream_t>(stream)));
+    return KVX_OK;
+}
+
+extern "C" int kvx_hbm_read_probe(const void *buf, size_t bytes, int reps, double *gbps) {
+    if (buf == nullptr || bytes < 16 || reps <= 0 || gbps == nullptr)
+        return fail(KVX_ERR_INVALID_ARGUMENT, "kvx_hbm_read_probe: bad argument");
+    DevBuf sink;
+    KVX_CUDA(sink.alloc(16, nullptr));
+    const size_t n16 = bytes / 16;
+    const int grid = sm_count() * 4;
+    cudaEvent_t a, b;
+    KVX_CUDA(cudaEventCreate(&a));
+    KVX_CUDA(cudaEventCreate(&b));
+    KVX_CUDA(launch_read_probe(static_cast<const uint4 *>(buf), n16, sink.as<uint32_t>(), grid, nullptr));
+    float best = 1e30f;
+    for (int r = 0; r < reps; ++r) {
+        cudaEventRecord(a, nullptr);
+        launch_read_probe(static_cast<const uint4 *>(buf), n16, sink.as<uint32_t>(), grid, nullptr);
+        cudaEventRecord(b, nullptr);
+        cudaEventSynchronize(b);
+        float ms = 0;
+        cudaEventElapsedTime(&ms, a, b);
+        best = std::min(best, ms);
+    }
+    cudaEventDestroy(a);
+    cudaEventDestroy(b);
+    KVX_CUDA(cudaGetLastError());
+    *gbps = double(n16) * 16.0 / (double(best) * 1e-3) / 1e9;
+    return KVX_OK;
+}

@@ -1,0 +1,553 @@
+// codec.cu -- device side of the XKV codec (reference src/codec.cpp, include/kvexp/scan.hpp).
+//
+//  * index_walk_kernel   header walk of a device blob: the block index that the reference rebuilds
+//                        by linear seeks (scan.hpp:94-123, :192-218), validated like parse_block
+//                        (scan.hpp:28-66).
+//  * build_flat_kernel   turns per-unit indexes into the flat block list of a batched plan.
+//  * decode_kernel       XKV -> BF16, bit-exact to decode_bf16 (codec.cpp:166-174): one warp per
+//                        block, escapes matched to sentinels in scan order with warp ballots.
+//  * enc_analyze_kernel  per block: exponent histograms per channel, best base per width (smallest
+//                        base with the largest window count, codec.cpp:18-35), escape counts and
+//                        the mode choice with the reference tie rules (codec.cpp:75-103).
+//  * enc_emit_kernel     writes header, bases, sign/mantissa bytes, packed residuals and escapes
+//                        (codec.cpp:105-161); byte-identical to encode_bf16.
+#include "codec.cuh"
+
+namespace kvx {
+namespace {
+
+constexpr uint32_t FULL = 0xFFFFFFFFu;
+
+__device__ __forceinline__ uint32_t rd_u16(const uint8_t *p) {
+    return uint32_t(p[0]) | (uint32_t(p[1]) << 8);
+}
+
+__global__ void index_walk_kernel(const uint8_t *blob, uint64_t bytes, int dim, kvx_block *index,
+                                  uint32_t *tok_start, int cap, int *counts, long long *n_tokens,
+                                  int *status) {
+    if (threadIdx.x != 0 || blockIdx.x != 0) return;
+    uint64_t off = 0;
+    int n = 0;
+    long long tok = 0;
+    while (off < bytes) {
+        if (bytes - off < 8) {
+            report(status, KVX_ERR_RUNTIME, DERR_TRUNC_HEADER);
+            break;
+        }
+        const uint8_t *p = blob + off;
+        const int mode = p[0], nt = p[1];
+        const int nesc = int(rd_u16(p + 2));
+        const int hdim = int(rd_u16(p + 4));
+        if (hdim != dim || nt <= 0) {
+            report(status, KVX_ERR_RUNTIME, DERR_DIM_LEN);
+            break;
+        }
+        const uint64_t rest = bytes - off - 8;
+        uint64_t need;
+        if (mode == 0) {
+            need = uint64_t(nt) * dim * 2;
+            if (rest < need) {
+                report(status, KVX_ERR_RUNTIME, DERR_TRUNC_RAW);
+                break;
+            }
+        } else if (mode != 2 && mode != 4) {
+            report(status, KVX_ERR_RUNTIME, DERR_MODE);
+            break;
+        } else {
+            need = uint64_t(dim) + uint64_t(nt) * dim + uint64_t(exp_payload_bytes(nt, dim, mode)) +
+                   2ull * uint64_t(nesc);
+            if (rest < need) {
+                report(status, KVX_ERR_RUNTIME, DERR_TRUNC_CODED);
+                break;
+            }
+        }
+        if (n >= cap) {
+            report(status, KVX_ERR_RUNTIME, DERR_INDEX_CAP);
+            break;
+        }
+        if (off > 0xFFFFFFFFull) {
+            report(status, KVX_ERR_UNSUPPORTED, DERR_RANGE);
+            break;
+        }
+        kvx_block b;
+        b.offset = uint32_t(off);
+        b.n_escape = uint16_t(mode == 0 ? 0 : nesc);
+        b.mode = uint8_t(mode);
+        b.n_tokens = uint8_t(nt);
+        index[n] = b;
+        if (tok_start) tok_start[n] = uint32_t(tok);
+        tok += nt;
+        ++n;
+        off += 8 + need;
+    }
+    counts[0] = n;
+    *n_tokens = tok;
+}
+
+__global__ void build_flat_kernel(const kvx_unit *units, const int64_t *block_begin, int dim,
+                                  int bt, bool bf16, FlatBlock *flat, int32_t *flat_unit,
+                                  int *status) {
+    const int u = blockIdx.x;
+    const kvx_unit U = units[u];
+    const int64_t b0 = block_begin[u];
+    __shared__ int last_valid;
+    if (threadIdx.x == 0) {
+        if (bf16) {
+            last_valid = U.seq - (U.n_blocks - 1) * bt;
+        } else {
+            long long before = 0;
+            for (int j = 0; j + 1 < U.n_blocks; ++j) before += U.k_index[j].n_tokens;
+            const int nl = U.k_index[U.n_blocks - 1].n_tokens;
+            long long rem = (long long)U.seq - before;
+            if (rem <= 0 || rem > nl) {
+                report(status, KVX_ERR_RUNTIME, DERR_OUT_OF_TOKENS);
+                rem = rem <= 0 ? 1 : nl;
+            }
+            last_valid = int(rem);
+        }
+    }
+    __syncthreads();
+    for (int j = threadIdx.x; j < U.n_blocks; j += blockDim.x) {
+        FlatBlock f;
+        if (bf16) {
+            const int tok0 = j * bt;
+            const int n = min(bt, U.seq - tok0);
+            f.k_off = f.v_off = uint32_t(tok0);
+            f.k_nesc = f.v_nesc = 0;
+            f.k_mode = f.v_mode = 0;
+            f.n_tok = uint8_t(n);
+            f.valid = uint8_t(n);
+        } else {
+            const kvx_block ke = U.k_index[j], ve = U.v_index[j];
+            if (ke.n_tokens != ve.n_tokens) report(status, KVX_ERR_RUNTIME, DERR_KV_MISMATCH);
+            const bool km = ke.mode == 0 || ke.mode == 2 || ke.mode == 4;
+            const bool vm = ve.mode == 0 || ve.mode == 2 || ve.mode == 4;
+            if (!km || !vm) report(status, KVX_ERR_RUNTIME, DERR_MODE);
+            if (uint64_t(ke.offset) + block_bytes(ke, dim) > U.k_bytes ||
+                uint64_t(ve.offset) + block_bytes(ve, dim) > U.v_bytes)
+                report(status, KVX_ERR_RUNTIME, DERR_RANGE);
+            f.k_off = ke.offset;
+            f.v_off = ve.offset;
+            f.k_nesc = ke.mode ? ke.n_escape : 0;
+            f.v_nesc = ve.mode ? ve.n_escape : 0;
+            f.k_mode = km ? ke.mode : 0;
+            f.v_mode = vm ? ve.mode : 0;
+            f.n_tok = ke.n_tokens;
+            f.valid = uint8_t(j + 1 == U.n_blocks ? last_valid : ke.n_tokens);
+        }
+        flat[b0 + j] = f;
+        flat_unit[b0 + j] = u;
+    }
+}
+
+// Exclusive prefix of per-lane counts (0..15) across the warp, and the warp total.
+__device__ __forceinline__ uint32_t warp_prefix(uint32_t cnt, uint32_t &total) {
+    const uint32_t lt = lanemask_lt();
+    uint32_t pre = 0;
+    total = 0;
+#pragma unroll
+    for (int b = 0; b < 4; ++b) {
+        const uint32_t bb = __ballot_sync(FULL, (cnt >> b) & 1u);
+        pre += uint32_t(__popc(bb & lt)) << b;
+        total += uint32_t(__popc(bb)) << b;
+    }
+    return pre;
+}
+
+__global__ void decode_kernel(const uint8_t *blob, const kvx_block *index,
+                              const uint32_t *tok_start, int n_blocks, int dim, int seq,
+                              uint16_t *out, int *status) {
+    const int gw = int((blockIdx.x * blockDim.x + threadIdx.x) >> 5);
+    const int lane = threadIdx.x & 31;
+    if (gw >= n_blocks) return;
+    const kvx_block blk = index[gw];
+    const long long t0 = tok_start[gw];
+    const int rows = int(min((long long)blk.n_tokens, (long long)seq - t0));
+    if (rows <= 0) return;
+    const uint8_t *p = blob + blk.offset + kHeaderBytes;
+    uint16_t *o = out + t0 * dim;
+    const int nel = rows * dim;
+    if (blk.mode == 0) {
+        for (int i = lane; i < nel; i += 32) o[i] = uint16_t(rd_u16(p + 2 * i));
+        return;
+    }
+    const int bits = blk.mode;
+    const int sentinel = (1 << bits) - 1;
+    const uint8_t *base = p, *sm = p + dim, *ex = sm + blk.n_tokens * dim;
+    const uint8_t *esc = ex + exp_payload_bytes(blk.n_tokens, dim, bits);
+    uint32_t run = 0;
+    for (int c0 = 0; c0 < nel; c0 += 256) {
+        uint32_t code[8];
+        uint32_t cnt = 0;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            const int i = c0 + 8 * lane + k;
+            uint32_t c = 0;
+            if (i < nel) {
+                c = bits == 4 ? ((ex[i >> 1] >> ((i & 1) * 4)) & 0xF)
+                              : ((ex[i >> 2] >> ((i & 3) * 2)) & 0x3);
+                cnt += c == uint32_t(sentinel);
+            }
+            code[k] = c;
+        }
+        uint32_t total;
+        uint32_t r = run + warp_prefix(cnt, total);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            const int i = c0 + 8 * lane + k;
+            if (i >= nel) continue;
+            uint16_t v;
+            if (code[k] == uint32_t(sentinel)) {
+                if (r >= blk.n_escape) {
+                    report(status, KVX_ERR_RUNTIME, DERR_ESC_OVERRUN);
+                    v = 0;
+                } else {
+                    v = uint16_t(rd_u16(esc + 2 * r));
+                }
+                ++r;
+            } else {
+                const uint32_t s = sm[i];
+                const uint32_t e = (uint32_t(base[i % dim]) + code[k]) & 0xFF;
+                v = uint16_t(((s & 0x80) << 8) | (e << 7) | (s & 0x7F));
+            }
+            o[i] = v;
+        }
+        run += total;
+    }
+}
+
+// ---- encoder ------------------------------------------------------------------------------------
+
+__global__ void enc_analyze_kernel(const uint16_t *const *tensors, int seq, int dim, int bt,
+                                   EncBlock *blocks, uint8_t *bases) {
+    extern __shared__ uint32_t hist[];  // dim * 128 words: two 16-bit bins per word
+    __shared__ uint8_t b3[kMaxHeadDim], b15[kMaxHeadDim];
+    __shared__ int red[2][32];
+    const int nb_per = (seq + bt - 1) / bt;
+    const int gb = blockIdx.x;
+    const int t = gb / nb_per, b = gb % nb_per;
+    const int n = min(bt, seq - b * bt);
+    const uint16_t *src = tensors[t] + size_t(b) * bt * dim;
+    for (int i = threadIdx.x; i < dim * 128; i += blockDim.x) hist[i] = 0;
+    __syncthreads();
+    for (int i = threadIdx.x; i < n * dim; i += blockDim.x) {
+        const uint32_t e = (uint32_t(src[i]) >> 7) & 0xFF;
+        const int d = i % dim;
+        atomicAdd(&hist[d * 128 + (e >> 1)], 1u << (16 * (e & 1)));
+    }
+    __syncthreads();
+    int cov3 = 0, cov15 = 0;
+    for (int d = threadIdx.x; d < dim; d += blockDim.x) {
+        const uint32_t *h = hist + d * 128;
+        auto bin = [&](int e) { return int((h[e >> 1] >> (16 * (e & 1))) & 0xFFFF); };
+        // sliding windows of width 3 and 15; strictly-greater keeps the smallest base
+        int c3 = bin(0) + bin(1) + bin(2), best3 = c3, bb3 = 0;
+        int c15 = 0;
+        for (int e = 0; e < 15; ++e) c15 += bin(e);
+        int best15 = c15, bb15 = 0;
+        for (int base = 1; base <= 256 - 3; ++base) {
+            c3 += bin(base + 2) - bin(base - 1);
+            if (c3 > best3) {
+                best3 = c3;
+                bb3 = base;
+            }
+            if (base <= 256 - 15) {
+                c15 += bin(base + 14) - bin(base - 1);
+                if (c15 > best15) {
+                    best15 = c15;
+                    bb15 = base;
+                }
+            }
+        }
+        b3[d] = uint8_t(bb3);
+        b15[d] = uint8_t(bb15);
+        cov3 += best3;
+        cov15 += best15;
+    }
+    // block reduction of the covered counts
+    for (int o = 16; o > 0; o >>= 1) {
+        cov3 += __shfl_xor_sync(FULL, cov3, o);
+        cov15 += __shfl_xor_sync(FULL, cov15, o);
+    }
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (lane == 0) {
+        red[0][warp] = cov3;
+        red[1][warp] = cov15;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int s3 = 0, s15 = 0;
+        for (int i = 0; i < int(blockDim.x >> 5); ++i) {
+            s3 += red[0][i];
+            s15 += red[1][i];
+        }
+        const int esc[2] = {n * dim - s3, n * dim - s15};
+        // mode choice, src/codec.cpp:75-103
+        int best_mode = 0, best_bytes = raw_block_bytes(n, dim), best_esc = 0;
+        for (int k = 0; k < 2; ++k) {
+            const int bits = k == 0 ? 2 : 4;
+            const int c_bytes = coded_block_bytes(n, dim, bits, esc[k]);
+            const bool better_size = c_bytes < best_bytes;
+            const bool tie = c_bytes == best_bytes;
+            const bool better_tie = tie && best_mode != 0 &&
+                                    (esc[k] < best_esc || (esc[k] == best_esc && bits < best_mode));
+            if (better_size || better_tie) {
+                best_mode = bits;
+                best_bytes = c_bytes;
+                best_esc = esc[k];
+            }
+        }
+        EncBlock eb;
+        eb.bytes = uint32_t(best_bytes);
+        eb.n_esc = uint16_t(best_mode == 0 ? 0 : best_esc);
+        eb.mode = uint8_t(best_mode);
+        eb.n_tok = uint8_t(n);
+        blocks[gb] = eb;
+        red[0][0] = best_mode;
+    }
+    __syncthreads();
+    const int mode = red[0][0];
+    for (int d = threadIdx.x; d < dim; d += blockDim.x)
+        bases[size_t(gb) * dim + d] = mode == 2 ? b3[d] : (mode == 4 ? b15[d] : 0);
+}
+
+__global__ void enc_emit_kernel(const uint16_t *const *tensors, int seq, int dim, int bt,
+                                const EncBlock *blocks, const uint8_t *bases,
+                                const uint64_t *block_off, uint8_t *arena, kvx_block *index,
+                                const uint64_t *blob_off, int *status) {
+    __shared__ uint32_t wsum[32];
+    __shared__ uint32_t running;
+    const int nb_per = (seq + bt - 1) / bt;
+    const int gb = blockIdx.x;
+    const int t = gb / nb_per, b = gb % nb_per;
+    const EncBlock eb = blocks[gb];
+    const int n = eb.n_tok;
+    const uint16_t *src = tensors[t] + size_t(b) * bt * dim;
+    const uint64_t off = block_off[gb];
+    uint8_t *out = arena + off;
+    if (threadIdx.x == 0) {
+        out[0] = eb.mode;
+        out[1] = uint8_t(n);
+        out[2] = uint8_t(eb.n_esc & 0xFF);
+        out[3] = uint8_t(eb.n_esc >> 8);
+        out[4] = uint8_t(dim & 0xFF);
+        out[5] = uint8_t(dim >> 8);
+        out[6] = 0;
+        out[7] = 0;
+        kvx_block ib;
+        ib.offset = uint32_t(off - blob_off[t]);
+        ib.n_escape = eb.n_esc;
+        ib.mode = eb.mode;
+        ib.n_tokens = uint8_t(n);
+        index[gb] = ib;
+        running = 0;
+    }
+    const int nel = n * dim;
+    if (eb.mode == 0) {
+        for (int i = threadIdx.x; i < nel; i += blockDim.x) {
+            out[8 + 2 * i] = uint8_t(src[i] & 0xFF);
+            out[9 + 2 * i] = uint8_t(src[i] >> 8);
+        }
+        return;
+    }
+    const int bits = eb.mode;
+    const int width = (1 << bits) - 1;
+    const uint8_t *base = bases + size_t(gb) * dim;
+    uint8_t *obase = out + 8, *osm = obase + dim, *oex = osm + nel;
+    uint8_t *oesc = oex + exp_payload_bytes(n, dim, bits);
+    for (int d = threadIdx.x; d < dim; d += blockDim.x) obase[d] = base[d];
+    auto code_of = [&](int i) {
+        const int e = (int(src[i]) >> 7) & 0xFF;
+        const int delta = e - int(base[i % dim]);
+        return (delta >= 0 && delta < width) ? delta : width;
+    };
+    for (int i = threadIdx.x; i < nel; i += blockDim.x)
+        osm[i] = uint8_t(((src[i] >> 8) & 0x80) | (src[i] & 0x7F));
+    const int per = 8 / bits;  // elements per packed byte
+    const int nbytes = exp_payload_bytes(n, dim, bits);
+    for (int j = threadIdx.x; j < nbytes; j += blockDim.x) {
+        uint32_t v = 0;
+        for (int k = 0; k < per; ++k) {
+            const int i = j * per + k;
+            if (i < nel) v |= uint32_t(code_of(i)) << (k * bits);
+        }
+        oex[j] = uint8_t(v);
+    }
+    // escapes in scan order
+    __syncthreads();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    for (int c0 = 0; c0 < nel; c0 += blockDim.x) {
+        const int i = c0 + threadIdx.x;
+        const bool s = i < nel && code_of(i) == width;
+        const uint32_t bal = __ballot_sync(FULL, s);
+        if (lane == 0) wsum[warp] = __popc(bal);
+        __syncthreads();
+        uint32_t before = running;
+        for (int k = 0; k < warp; ++k) before += wsum[k];
+        before += __popc(bal & lanemask_lt());
+        if (s) {
+            if (before < eb.n_esc) {
+                oesc[2 * before] = uint8_t(src[i] & 0xFF);
+                oesc[2 * before + 1] = uint8_t(src[i] >> 8);
+            } else {
+                report(status, KVX_ERR_LOGIC, DERR_ESC_OVERRUN);
+            }
+        }
+        __syncthreads();
+        if (threadIdx.x == 0)
+            for (int k = 0; k < nw; ++k) running += wsum[k];
+        __syncthreads();
+    }
+    if (threadIdx.x == 0 && running != eb.n_esc) report(status, KVX_ERR_LOGIC, DERR_ESC_OVERRUN);
+}
+
+// ---- synthetic inputs (bit-identical to synth.py) ------------------------------------------------
+
+__device__ __forceinline__ uint64_t mix64(uint64_t x) {
+    x ^= x >> 30;
+    x *= 0xBF58476D1CE4E5B9ull;
+    x ^= x >> 27;
+    x *= 0x94D049BB133111EBull;
+    x ^= x >> 31;
+    return x;
+}
+__device__ __forceinline__ uint64_t key(uint64_t seed, uint64_t stream, uint64_t idx) {
+    return seed * 0x9E3779B97F4A7C15ull + stream * 0xD1B54A32D192ED03ull + idx;
+}
+__device__ __forceinline__ uint16_t to_bf16(float x) {
+    const uint32_t b = __float_as_uint(x);
+    return uint16_t((b + 0x7FFFu + ((b >> 16) & 1u)) >> 16);
+}
+
+__global__ void synth_kernel(uint16_t *out, int seq, int dim, uint64_t seed, uint64_t sid,
+                             int profile, uint32_t rate) {
+    const int64_t n = int64_t(seq) * dim;
+    for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < n;
+         i += int64_t(gridDim.x) * blockDim.x) {
+        const uint64_t t = uint64_t(i / dim), c = uint64_t(i % dim);
+        const uint64_t h1 = mix64(key(seed, sid, uint64_t(i)));
+        const uint64_t h2 = mix64(h1 ^ 0x5851F42D4C957F2Dull);
+        const uint64_t chan = mix64(key(seed, sid, (1ull << 40) + c));
+        const bool outlier = (h2 & 0xFFFFFFFFull) < rate;
+        const bool up = ((h2 >> 32) & 1ull) == 1ull;
+        uint16_t v;
+        if (profile == 3) {  // narrow
+            int e = 127 + int(chan % 3ull) - 1 + int(h1 % 3ull);
+            const int shift = 5 + int((h2 >> 40) % 5ull);
+            if (outlier) e = up ? e + shift : e - shift;
+            const int mant = int((h1 >> 8) & 0x7Full), sign = int((h1 >> 15) & 1ull);
+            v = uint16_t((sign << 15) | ((e & 0xFF) << 7) | mant);
+        } else {
+            int s = 0;
+            for (int k = 0; k < 4; ++k) s += int((h1 >> (16 * k)) & 0xFFFFull);
+            const float z = __fmul_rn(float(s - 131070), float(1.0 / 37837.59));
+            float x;
+            bool use_out = outlier;
+            if (profile == 0 || profile == 4) {
+                const int sc = int(chan % 9ull) - 4;
+                x = __fmul_rn(z, ldexpf(1.0f, sc));
+            } else if (profile == 1 || profile == 5) {
+                x = __fmul_rn(z, 0.5f);
+            } else {
+                x = __fmul_rn(z, 0.125f);
+                use_out = false;
+            }
+            if (use_out) x = __fmul_rn(x, up ? 512.0f : (1.0f / 512.0f));
+            v = to_bf16(x);
+            if (profile == 4 || profile == 5) {
+                const uint64_t bh = mix64(key(seed, sid, (1ull << 41) + t / 128ull));
+                if (bh % 100ull < 5ull) {
+                    const int e = 97 + int((h1 >> 8) % 61ull);
+                    const int mant = int((h1 >> 20) & 0x7Full), sign = int((h1 >> 27) & 1ull);
+                    v = uint16_t((sign << 15) | (e << 7) | mant);
+                }
+            }
+        }
+        out[i] = v;
+    }
+}
+
+__global__ void read_probe_kernel(const uint4 *buf, size_t n16, uint32_t *sink) {
+    uint32_t acc = 0;
+    for (size_t i = blockIdx.x * size_t(blockDim.x) + threadIdx.x; i < n16;
+         i += size_t(gridDim.x) * blockDim.x) {
+        const uint4 v = __ldcs(buf + i);
+        acc ^= v.x ^ v.y ^ v.z ^ v.w;
+    }
+    if (acc == 0x9E3779B9u) sink[0] = acc;  // keeps the loads alive
+}
+
+}  // namespace
+
+cudaError_t launch_index_walk(const uint8_t *blob, uint64_t bytes, int dim, kvx_block *index,
+                              uint32_t *tok_start, int cap, int *counts, long long *n_tokens,
+                              int *status, cudaStream_t s) {
+    index_walk_kernel<<<1, 32, 0, s>>>(blob, bytes, dim, index, tok_start, cap, counts, n_tokens,
+                                       status);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_build_flat(const kvx_unit *units, const int64_t *block_begin, int n_units,
+                              int dim, int block_tokens, bool bf16, FlatBlock *flat,
+                              int32_t *flat_unit, int *status, cudaStream_t s) {
+    if (n_units <= 0) return cudaSuccess;
+    build_flat_kernel<<<n_units, 256, 0, s>>>(units, block_begin, dim, block_tokens, bf16, flat,
+                                              flat_unit, status);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_decode(const uint8_t *blob, const kvx_block *index, const uint32_t *tok_start,
+                          int n_blocks, int dim, int seq, uint16_t *out, int *status,
+                          cudaStream_t s) {
+    if (n_blocks <= 0) return cudaSuccess;
+    const int warps_per_cta = 8;
+    const int grid = (n_blocks + warps_per_cta - 1) / warps_per_cta;
+    decode_kernel<<<grid, 32 * warps_per_cta, 0, s>>>(blob, index, tok_start, n_blocks, dim, seq,
+                                                       out, status);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_encode_analyze(const uint16_t *const *tensors, int n_tensors, int seq, int dim,
+                                  int block_tokens, EncBlock *blocks, uint8_t *bases,
+                                  cudaStream_t s) {
+    const int nb = n_tensors * ((seq + block_tokens - 1) / block_tokens);
+    if (nb <= 0) return cudaSuccess;
+    const size_t sm = size_t(dim) * 128 * 4;
+    static bool configured = false;
+    if (!configured) {
+        cudaFuncSetAttribute(enc_analyze_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             int(kMaxHeadDim * 128 * 4));
+        configured = true;
+    }
+    enc_analyze_kernel<<<nb, 256, sm, s>>>(tensors, seq, dim, block_tokens, blocks, bases);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_encode_emit(const uint16_t *const *tensors, int n_tensors, int seq, int dim,
+                               int block_tokens, const EncBlock *blocks, const uint8_t *bases,
+                               const uint64_t *block_off, uint8_t *arena, kvx_block *index,
+                               const uint64_t *blob_off, int *status, cudaStream_t s) {
+    const int nb = n_tensors * ((seq + block_tokens - 1) / block_tokens);
+    if (nb <= 0) return cudaSuccess;
+    enc_emit_kernel<<<nb, 256, 0, s>>>(tensors, seq, dim, block_tokens, blocks, bases, block_off,
+                                       arena, index, blob_off, status);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_synth(uint16_t *out, int seq, int dim, uint64_t seed, uint64_t stream_id,
+                         int profile, uint32_t rate, cudaStream_t s) {
+    const int64_t n = int64_t(seq) * dim;
+    int grid = int((n + 255) / 256);
+    if (grid > 148 * 64) grid = 148 * 64;
+    if (grid < 1) grid = 1;
+    synth_kernel<<<grid, 256, 0, s>>>(out, seq, dim, seed, stream_id, profile, rate);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_read_probe(const uint4 *buf, size_t n16, uint32_t *sink, int grid,
+                              cudaStream_t s) {
+    read_probe_kernel<<<grid, 512, 0, s>>>(buf, n16, sink);
+    return cudaGetLastError();
+}
+
+}  // namespace kvx

@@ -1,0 +1,174 @@
+/*
+ * kvexp_b200.h -- C ABI of the B200 (sm_100a) implementation of kvexp's compressed-KV decode
+ * attention and XKV codec.
+ *
+ * The first block of entry points replaces the reference library's public C++ API one for one
+ * (same argument order and meaning; a C++ exception becomes a status code whose kind says which
+ * exception type the reference throws, and kvx_last_error() holds its message).  Pointers in
+ * those calls may be host or device memory; the library detects which.  The second block is the
+ * GPU-native batched interface for device-resident caches (no reference counterpart except the
+ * per-head loop it replaces).
+ *
+ * Every entry point returns KVX_OK (0) or a kvx_status.  Calls are synchronous unless they take a
+ * stream.  Device pointers given to the batched interface must be 16-byte aligned, and the
+ * allocation behind an XKV blob must stay readable up to the next 16-byte boundary after its
+ * last byte (cudaMalloc and the PyTorch caching allocator both guarantee this).
+ */
+#ifndef KVEXP_B200_H
+#define KVEXP_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define KVX_API __attribute__((visibility("default")))
+#else
+#define KVX_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes.  1..3 name the C++ exception type the reference throws for the same failure. */
+typedef enum kvx_status {
+    KVX_OK = 0,
+    KVX_ERR_INVALID_ARGUMENT = 1, /* std::invalid_argument */
+    KVX_ERR_RUNTIME = 2,          /* std::runtime_error: malformed blob, backend, ... */
+    KVX_ERR_LOGIC = 3,            /* std::logic_error: encoder size-model drift */
+    KVX_ERR_CUDA = 4,             /* a CUDA runtime call failed */
+    KVX_ERR_TIMEOUT = 5,          /* a bounded device-side wait expired */
+    KVX_ERR_UNSUPPORTED = 6       /* shape outside this library's kernels */
+} kvx_status;
+
+/* Backend selector of the reference (include/kvexp/attention.hpp:10-14).  All three run the same
+ * GPU kernels here; the value only selects which shape rule and error text the reference applies
+ * (dim % 8 for Scalar/Avx2, dim % 32 for Avx512Bf16). */
+enum { KVX_BACKEND_SCALAR = 0, KVX_BACKEND_AVX2 = 1, KVX_BACKEND_AVX512BF16 = 2 };
+
+/* Message of the last failure on the calling thread ("" after success). */
+KVX_API const char *kvx_last_error(void);
+
+/* Library version string. */
+KVX_API const char *kvx_version(void);
+
+/* ---- drop-in replacements of the reference API ------------------------------------------- */
+
+/* Replaces kvexp::detect_cpu (include/kvexp/attention.hpp:21, src/cpu.cpp:35-61): instead of
+ * CPUID it reports the current CUDA device.  Returns KVX_ERR_RUNTIME when no sm_100 device. */
+KVX_API int kvx_device_info(int *sm_major, int *sm_minor, int *sm_count, size_t *hbm_bytes);
+
+/* Replaces kvexp::attention_decode (include/kvexp/attention.hpp:58-61, src/dispatch.cpp:27-104).
+ * One decode step for n_q queries sharing one KV head: out[n_q, dim] (FP32) =
+ * softmax(q K^T) V with the online-softmax semantics of src/softmax.hpp.  Exactly one of
+ * (k_raw, k_xkv) and of (v_raw, v_xkv) is non-NULL.  n_threads and split_tokens keep their
+ * reference meaning for validation (a thread split that falls inside an encoded block is an
+ * error, as in the reference); the GPU chooses its own parallel split.  For XKV input the GPU
+ * result is bit-identical to the same call with raw K/V of the decoded values. */
+KVX_API int kvx_attention_decode(int backend, const uint16_t *q, const uint16_t *k_raw,
+                         const uint16_t *v_raw, const uint8_t *k_xkv, size_t k_bytes,
+                         const uint8_t *v_xkv, size_t v_bytes, float *out, int n_q, int dim,
+                         int seq, int n_threads, int split_tokens);
+
+/* Batched form of the reference's per-head loop (src/bench.cpp:711-728 `model_heads`): n_units
+ * independent attention_decode calls over XKV blobs, all with the same n_q, dim, seq, run as one
+ * GPU job.  Pointer arrays live in host memory; the pointers they hold may be host or device.
+ * With host buffers the library streams blobs to the GPU and overlaps copies with compute. */
+KVX_API int kvx_attention_decode_units(int backend, int n_units, const uint16_t *const *q,
+                               const uint8_t *const *k_xkv, const size_t *k_bytes,
+                               const uint8_t *const *v_xkv, const size_t *v_bytes,
+                               float *const *out, int n_q, int dim, int seq, int split_tokens);
+
+/* Replaces kvexp::encode_bf16 (include/kvexp/codec.hpp:45-46, src/codec.cpp:39-164): encodes
+ * [seq_len, head_dim] BF16 bits into the XKV container, byte-identical to the reference.
+ * `out` must hold kvx_encode_bound() bytes; *out_bytes receives the container size. */
+KVX_API size_t kvx_encode_bound(int seq_len, int head_dim, int block_tokens);
+KVX_API int kvx_encode_bf16(const uint16_t *kv, int seq_len, int head_dim, int block_tokens,
+                    uint8_t *out, size_t out_capacity, size_t *out_bytes);
+
+/* Replaces kvexp::decode_bf16 (include/kvexp/codec.hpp:48, src/codec.cpp:166-174). */
+KVX_API int kvx_decode_bf16(const uint8_t *blob, size_t bytes, int seq_len, int head_dim,
+                    uint16_t *out);
+
+/* ---- GPU-native batched interface (device-resident caches) -------------------------------- */
+
+/* One entry per encoded block: the block-offset index that the reference recomputes by walking
+ * headers (include/kvexp/scan.hpp:94-123, :192-218).  Written by the GPU encoder or built once
+ * by kvx_xkv_index. */
+typedef struct kvx_block {
+    uint32_t offset;   /* byte offset of the block header inside its blob */
+    uint16_t n_escape; /* escape words (0 for raw blocks) */
+    uint8_t mode;      /* 0 raw, 2 or 4 bits */
+    uint8_t n_tokens;  /* tokens in the block */
+} kvx_block;
+
+/* Walk the headers of a device-resident blob and write its index (device memory, capacity
+ * max_blocks).  Validates every header like parse_block (include/kvexp/scan.hpp:28-66).
+ * *n_blocks and *n_tokens receive the counts (host).  Synchronous. */
+KVX_API int kvx_xkv_index(const uint8_t *blob, size_t bytes, int head_dim, kvx_block *index,
+                  int max_blocks, int *n_blocks, long long *n_tokens);
+
+/* One (layer, KV head[, sequence]) unit of a batched decode step.  All pointers are device
+ * pointers.  For XKV caches k_index/v_index are the blobs' block indexes; for the uncompressed
+ * BF16 kernel they are NULL and k/v point at [seq, dim] BF16 arrays. */
+typedef struct kvx_unit {
+    const void *k;
+    const void *v;
+    const kvx_block *k_index;
+    const kvx_block *v_index;
+    const uint16_t *q; /* [n_q, dim] BF16 */
+    float *out;        /* [n_q, dim] FP32 */
+    uint64_t k_bytes;  /* blob sizes (XKV) */
+    uint64_t v_bytes;
+    int32_t n_blocks;  /* XKV blocks covering the first `seq` tokens */
+    int32_t seq;       /* tokens attended */
+} kvx_unit;
+
+typedef struct kvx_plan_s *kvx_plan;
+
+/* Build a reusable launch plan for a fixed set of units (host array of n_units descriptors).
+ * block_tokens is the encode block size (the tile split of the BF16 kernel).  The plan uploads
+ * the descriptors, balances HBM bytes across the GPU and owns the scratch for split units. */
+KVX_API int kvx_plan_create(const kvx_unit *units, int n_units, int n_q, int dim, int block_tokens,
+                    kvx_plan *plan);
+/* Launch one decode step for every unit on `stream` (a cudaStream_t; NULL = default stream). */
+KVX_API int kvx_plan_run(kvx_plan plan, void *stream);
+/* Synchronise the plan's last run and report device-side errors (malformed blocks, timeouts). */
+KVX_API int kvx_plan_check(kvx_plan plan);
+/* Number of kernel launches one kvx_plan_run makes. */
+KVX_API int kvx_plan_launches(kvx_plan plan);
+KVX_API void kvx_plan_destroy(kvx_plan plan);
+
+/* GPU encoder for caches built on the device: encodes n_tensors [seq, head_dim] BF16 tensors
+ * (device pointers in a host array) into one device arena.  Blob t starts at arena +
+ * blob_offset[t] (16-byte aligned), its index at index + index_offset[t].  Capacities from
+ * kvx_encode_batch_bounds.  Byte-identical to kvexp::encode_bf16 per tensor.  Synchronous. */
+KVX_API int kvx_encode_batch_bounds(int n_tensors, int seq, int head_dim, int block_tokens,
+                            size_t *arena_bytes, size_t *index_entries);
+KVX_API int kvx_encode_batch(int n_tensors, const uint16_t *const *kv, int seq, int head_dim,
+                     int block_tokens, uint8_t *arena, size_t arena_capacity,
+                     kvx_block *index, uint64_t *blob_offset, uint64_t *blob_bytes,
+                     void *stream);
+
+/* Append tokens to a device-resident cache: encode [n_new, head_dim] BF16 (device) as whole
+ * blocks starting at byte `at` of `blob` (capacity `capacity`), writing the new blocks' index
+ * entries at `index`.  *bytes_written / *blocks_written receive the growth.  Synchronous. */
+KVX_API int kvx_cache_append(const uint16_t *kv_new, int n_new, int head_dim, int block_tokens,
+                     uint8_t *blob, size_t at, size_t capacity, kvx_block *index,
+                     size_t *bytes_written, int *blocks_written, void *stream);
+
+/* ---- benchmark support -------------------------------------------------------------------- */
+
+/* Fill [seq, dim] BF16 on the device with the seeded synthetic distribution `profile`
+ * (bit-identical to the numpy generator in synth.py). */
+KVX_API int kvx_synth_bf16(uint16_t *out, int seq, int dim, uint64_t seed, uint64_t stream_id,
+                   int profile, uint32_t rate, void *stream);
+
+/* Device HBM read probe: streams `bytes` of `buf` with 16-byte loads, returns GB/s (1e9). */
+KVX_API int kvx_hbm_read_probe(const void *buf, size_t bytes, int reps, double *gbps);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* KVEXP_B200_H */

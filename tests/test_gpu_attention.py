@@ -1,0 +1,188 @@
+"""GPU parity of the fused XKV decode attention (the hot path), through the C ABI.
+
+Three checks, mirroring the reference's own invariants (tests/test_main.cpp:124-157):
+  * XKV output == uncompressed-BF16 output of the same GPU kernel, bit for bit;
+  * GPU output within an FP32 tolerance (helpers.assert_attention_close) of the reference's
+    scalar kernel restated in oracle/ (and of the reference library itself when built);
+  * the batched plan gives the same bits as the one-unit drop-in call.
+"""
+import numpy as np
+import pytest
+
+import synth as S
+from helpers import (XorShift32, assert_attention_close, attention_f64, attn_scale, clustered,
+                     make_bf16, soften)
+
+pytestmark = pytest.mark.gpu
+
+
+def _case(dim, n_q, seq, seed=7, k_profile=S.PROFILE_K, soft=0):
+    k = S.synth_bf16(seed, 0, seq, dim, k_profile)
+    v = S.synth_bf16(seed, 1, seq, dim, S.PROFILE_V)
+    q = S.synth_bf16(seed, 2, n_q, dim, S.PROFILE_Q)
+    return (soften(q, soft) if soft else q), k, v
+
+
+def _gpu(kvx, q, k=None, v=None, kx=None, vx=None, seq=None, threads=1, split=128,
+         backend=0):
+    n_q, dim = q.shape
+    out = np.zeros((n_q, dim), dtype=np.float32)
+    kvx.attention_decode(backend, q, k, v, kx, 0 if kx is None else kx.size, vx,
+                         0 if vx is None else vx.size, out, n_q, dim, seq, threads, split)
+    return out
+
+
+def _bits(x):
+    return np.asarray(x, dtype=np.float32).view(np.uint32)
+
+
+@pytest.mark.parametrize("dim,n_q,seq,soft", [
+    (64, 7, 1, 0), (64, 7, 17, 0), (64, 7, 128, 0), (64, 7, 300, 0), (64, 1, 1000, 0),
+    (64, 3, 4096, 0), (32, 2, 90, 0), (128, 4, 513, 0), (256, 4, 300, 0), (64, 14, 700, 0),
+    (128, 8, 2048, 0), (64, 5, 8192, 0), (64, 7, 4096, 6), (128, 4, 8192, 6), (256, 4, 3000, 7),
+    (32, 8, 5000, 5), (64, 16, 1500, 6),
+])
+def test_xkv_vs_raw_and_oracle(kvx, cuda, oracle, dim, n_q, seq, soft):
+    q, k, v = _case(dim, n_q, seq, soft=soft)
+    kx = oracle.encode(k, 128)
+    vx = oracle.encode(v, 128)
+    g_raw = _gpu(kvx, q, k, v, seq=seq)
+    g_xkv = _gpu(kvx, q, kx=kx, vx=vx, seq=seq)
+    assert np.array_equal(_bits(g_raw), _bits(g_xkv)), "XKV and BF16 GPU outputs differ"
+    cpu = oracle.attention(q, kx=kx, vx=vx, seq=seq)
+    assert_attention_close(g_xkv, cpu, attn_scale(q, k, v), f"dim={dim} n_q={n_q} seq={seq}",
+                           seq=seq)
+
+
+@pytest.mark.parametrize("dim,n_q,seq,soft", [(64, 7, 8192, 6), (128, 4, 16384, 7),
+                                              (256, 4, 4096, 7), (64, 7, 32768, 8)])
+def test_accuracy_vs_float64(kvx, cuda, oracle, dim, n_q, seq, soft):
+    """Against a float64 softmax, the GPU error stays within the reference scalar kernel's own
+    fp32 error (plus 2e-5 of the output scale)."""
+    q, k, v = _case(dim, n_q, seq, seed=21, soft=soft)
+    kx, vx = oracle.encode(k, 128), oracle.encode(v, 128)
+    g = _gpu(kvx, q, kx=kx, vx=vx, seq=seq)
+    cpu = oracle.attention(q, kx=kx, vx=vx, seq=seq)
+    truth = attention_f64(q, k, v)
+    scale = attn_scale(q, k, v)
+    gerr = np.max(np.abs(g - truth) / scale)
+    cerr = np.max(np.abs(cpu - truth) / scale)
+    assert gerr <= cerr + 2e-5, (gerr, cerr)
+
+
+@pytest.mark.parametrize("dim,n_q,seq,block,threads", [
+    (64, 1, 1, 128, 1), (64, 7, 17, 128, 1), (64, 7, 128, 128, 1), (64, 3, 200, 64, 1),
+    (64, 7, 300, 64, 4), (32, 2, 90, 32, 1), (64, 7, 256, 128, 4),
+])
+def test_reference_matrix(kvx, cuda, oracle, dim, n_q, seq, block, threads):
+    """The reference test matrix (tests/test_main.cpp:165-172) on clustered data."""
+    rng = XorShift32()
+    k = clustered(rng, seq * dim, 108, 8).reshape(seq, dim)
+    v = clustered(rng, seq * dim, 112, 5).reshape(seq, dim)
+    q = np.array([make_bf16(120, rng() & 0x7F, rng() & 1) for _ in range(n_q * dim)],
+                 dtype=np.uint16).reshape(n_q, dim)
+    kx = oracle.encode(k, block)
+    vx = oracle.encode(v, block)
+    g_raw = _gpu(kvx, q, k, v, seq=seq, threads=threads, split=block)
+    g_xkv = _gpu(kvx, q, kx=kx, vx=vx, seq=seq, threads=threads, split=block)
+    assert np.array_equal(_bits(g_raw), _bits(g_xkv))
+    cpu = oracle.attention(q, kx=kx, vx=vx, seq=seq, threads=threads, split=block)
+    assert_attention_close(g_xkv, cpu, attn_scale(q, k, v), "reference matrix", seq=seq)
+
+
+def test_narrow_two_bit_blocks(kvx, cuda, oracle):
+    """2-bit blocks with 8 % escapes (the config[1] layer-0 K distribution)."""
+    q, k, v = _case(64, 7, 2048, seed=11, k_profile=S.PROFILE_NARROW)
+    kx, modes = oracle.encode(k, 128, with_modes=True)
+    assert (modes == 2).all()
+    vx = oracle.encode(v, 128)
+    g_raw = _gpu(kvx, q, k, v, seq=2048)
+    g_xkv = _gpu(kvx, q, kx=kx, vx=vx, seq=2048)
+    assert np.array_equal(_bits(g_raw), _bits(g_xkv))
+    cpu = oracle.attention(q, kx=kx, vx=vx, seq=2048)
+    assert_attention_close(g_xkv, cpu, attn_scale(q, k, v), "2-bit", seq=2048)
+
+
+def test_raw_blocks(kvx, cuda, oracle):
+    """Blocks the encoder stores raw (config[4] distribution), mixed with coded blocks."""
+    q, k, v = _case(256, 4, 128 * 40, seed=5, k_profile=S.PROFILE_WIDE_K)
+    v = S.synth_bf16(5, 1, 128 * 40, 256, S.PROFILE_WIDE_V)
+    kx, modes = oracle.encode(k, 128, with_modes=True)
+    assert (modes == 0).any() and (modes == 4).any()
+    vx = oracle.encode(v, 128)
+    g_raw = _gpu(kvx, q, k, v, seq=k.shape[0])
+    g_xkv = _gpu(kvx, q, kx=kx, vx=vx, seq=k.shape[0])
+    assert np.array_equal(_bits(g_raw), _bits(g_xkv))
+    cpu = oracle.attention(q, kx=kx, vx=vx, seq=k.shape[0])
+    assert_attention_close(g_xkv, cpu, attn_scale(q, k, v), "raw blocks", seq=k.shape[0])
+
+
+def test_identity_token(kvx, cuda):
+    """seq 1, q = k = 1.0: out == v exactly (tests/test_main.cpp:102-122, at dim 32)."""
+    dim = 32
+    q = np.full((1, dim), 0x3F80, dtype=np.uint16)
+    k = q.copy()
+    v = np.full((1, dim), 0x3F80, dtype=np.uint16)
+    v[0, 0] = 0x4000
+    out = _gpu(kvx, q, k, v, seq=1)
+    assert out[0, 0] == 2.0 and (out[0, 1:] == 1.0).all()
+
+
+def test_device_pointers_match_host(kvx, cuda, oracle):
+    torch = cuda
+    q, k, v = _case(64, 7, 1000)
+    kx = oracle.encode(k, 128)
+    vx = oracle.encode(v, 128)
+    host = _gpu(kvx, q, kx=kx, vx=vx, seq=1000)
+    dq = torch.from_numpy(q.view(np.int16)).cuda()
+    dk = torch.from_numpy(kx.view(np.int8)).cuda()
+    dv = torch.from_numpy(vx.view(np.int8)).cuda()
+    out = torch.zeros((7, 64), dtype=torch.float32, device="cuda")
+    kvx.attention_decode(0, dq, None, None, dk, kx.size, dv, vx.size, out, 7, 64, 1000, 1)
+    assert np.array_equal(_bits(out.cpu().numpy()), _bits(host))
+
+
+def test_units_batch_matches_single(kvx, cuda, oracle):
+    dim, n_q, seq = 64, 7, 1500
+    qs, kxs, vxs, singles = [], [], [], []
+    for u in range(6):
+        q, k, v = _case(dim, n_q, seq, seed=100 + u)
+        kx, vx = oracle.encode(k, 128), oracle.encode(v, 128)
+        qs.append(q); kxs.append(kx); vxs.append(vx)
+        singles.append(_gpu(kvx, q, kx=kx, vx=vx, seq=seq))
+    runs = []
+    for _ in range(2):
+        outs = [np.zeros((n_q, dim), dtype=np.float32) for _ in range(6)]
+        kvx.attention_decode_units(0, qs, kxs, [x.size for x in kxs], vxs,
+                                   [x.size for x in vxs], outs, n_q, dim, seq)
+        runs.append(outs)
+    for a, b in zip(*runs):  # deterministic
+        assert np.array_equal(_bits(a), _bits(b))
+    for a, b, q in zip(runs[0], singles, qs):
+        scale = np.maximum(np.abs(b), 1e-3)
+        assert np.max(np.abs(a - b) / scale) < 1e-4
+
+
+def test_errors_mirror_reference(kvx, cuda, oracle):
+    q, k, v = _case(64, 7, 300)
+    kx = oracle.encode(k, 128)
+    vx = oracle.encode(v, 128)
+    with pytest.raises(ValueError, match="bad argument"):
+        _gpu(kvx, q, kx=kx, vx=vx, seq=0)
+    with pytest.raises(ValueError, match="not both"):
+        out = np.zeros((7, 64), dtype=np.float32)
+        kvx.attention_decode(0, q, k, v, kx, kx.size, vx, vx.size, out, 7, 64, 300, 1)
+    with pytest.raises(RuntimeError, match="truncated"):
+        _gpu(kvx, q, kx=kx[:-3], vx=vx, seq=300)
+    bad = kx.copy()
+    bad[4] ^= 1  # head_dim field
+    with pytest.raises(RuntimeError, match="dimension or length mismatch"):
+        _gpu(kvx, q, kx=bad, vx=vx, seq=300)
+    bad = kx.copy()
+    bad[0] = 3  # mode
+    with pytest.raises(RuntimeError, match="unknown xkv block mode"):
+        _gpu(kvx, q, kx=bad, vx=vx, seq=300)
+    with pytest.raises(RuntimeError, match="ran out of blocks"):
+        _gpu(kvx, q, kx=kx, vx=vx, seq=301)
+    with pytest.raises(RuntimeError, match="not aligned"):
+        _gpu(kvx, q, kx=kx, vx=vx, seq=300, threads=3, split=64)
