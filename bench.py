@@ -1,0 +1,416 @@
+#!/usr/bin/env python
+"""Benchmark of the fused compressed-KV (XKV) decode attention on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config C] [--impl kvx|reference]
+
+One step = one decode-attention pass over every (layer, KV head) unit of the workload (the
+reference's `model_heads` scope, src/bench.cpp:711-728) with the KV cache resident in HBM.
+Default workload: BASELINE.json config[1] (24 layers x 2 KV heads x GQA 7 x head_dim 64 x
+32768 tokens, block 128), synthetic seeded data.  With N > 1 (torchrun) every rank decodes its own
+full config[1] cache (weak scaling, no collective on the data path); time is the max over ranks.
+
+Prints one JSON line (rank 0).  `--impl reference` times the unmodified reference library
+(compiled from its own sources into oracle/_ref) on this host's cores on the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+for p in ("compressed-kv-attention_b200", "oracle"):
+    sys.path.insert(0, os.path.join(ROOT, p))
+
+METRIC = "compressed-KV decode GB/s and % of HBM peak; µs/step at 32K (1/2/4/8 B200)"
+# Reference's published number for this metric (model_heads, AVX-512 BF16, 4 threads,
+# seq 32768, XKV container bandwidth; README.md:159, results/bench.json:172).
+PUBLISHED_GBPS = 2.129
+FALLBACK_HBM_GBS = 6650.0
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--config", type=int, default=1)
+    ap.add_argument("--impl", default="kvx", choices=["kvx", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--e2e-steps", type=int, default=8)
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    return ap.parse_args()
+
+
+def env_rank():
+    return (int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)),
+            int(os.environ.get("LOCAL_RANK", 0)))
+
+
+def hbm_peak():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "of measured (MEASURED_PEAKS.json hbm_gbs: copy, read+write)"
+    except Exception:
+        return FALLBACK_HBM_GBS, "of fallback (6.65 TB/s)"
+
+
+def ncu_traffic(config):
+    """DRAM bytes per launch of the attention kernel from the committed ncu summary, if any."""
+    path = os.path.join(ROOT, "profiles", "ncu_traffic.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        e = d.get(str(config))
+        return None if e is None else float(e["dram_bytes_per_launch"])
+    except Exception:
+        return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index, interval_ms=50):
+        self.dev = device_index
+        self.interval = interval_ms
+        self.lines = []
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-i", str(self.dev), "-lms", str(self.interval)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+            return
+        self.t = threading.Thread(target=self._read, daemon=True)
+        self.t.start()
+        time.sleep(0.3)
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.1)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        sm, mx, pw, reasons = [], [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx.append(float(parts[2]))
+                pw.append(float(parts[3]))
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None,
+                "power_w_max": max(pw) if pw else None,
+                "samples": len(sm), "reasons": sorted(reasons)}
+
+
+# ---- CPU reference timing ------------------------------------------------------------------------
+
+def cpu_reference_rate(qs, ks, vs, cfg, seconds, max_passes=50):
+    """Time the reference library's model_heads loop (oracle/_ref) on all usable host cores;
+    falls back to the C restatement (oracle/) when the reference was not built."""
+    import numpy as np
+    import oracle as O
+    n = len(qs)
+    outs = [np.zeros((cfg.group, cfg.dim), dtype=np.float32) for _ in range(n)]
+    total = sum(k.size for k in ks) + sum(v.size for v in vs)
+    threads = max(1, min(n, os.cpu_count() or 1))
+    ref = O.reference()
+    if ref is not None:
+        be = O.AVX512BF16 if ref.avx512_bf16 else (O.AVX2 if ref.avx2 else O.SCALAR)
+        bname = {O.AVX512BF16: "AVX-512 BF16", O.AVX2: "AVX2", O.SCALAR: "scalar"}[be]
+        run = lambda: ref.model_heads(be, qs, ks, vs, outs, cfg.group, cfg.dim, cfg.seq, threads)
+        kind = "reference"
+        what = f"reference kvexp model_heads, {bname}, {threads} OpenMP threads"
+    else:
+        from concurrent.futures import ThreadPoolExecutor
+        orc = O.oracle()
+        pool = ThreadPoolExecutor(threads)
+
+        def run():
+            list(pool.map(lambda u: orc.attention(qs[u], kx=ks[u], vx=vs[u], seq=cfg.seq),
+                          range(n)))
+        kind = "port"
+        what = f"C restatement (oracle/), {threads} threads"
+    run()  # warm-up
+    t0 = time.perf_counter()
+    passes = 0
+    while True:
+        run()
+        passes += 1
+        el = time.perf_counter() - t0
+        if el >= seconds or passes >= max_passes:
+            break
+    gbps = total * passes / el / 1e9
+    return {"value": gbps, "unit": "GB/s", "cores": threads, "kind": kind,
+            "sample": f"{passes} full passes over all {n} units of {cfg.name} "
+                      f"({total / 1e6:.1f} MB of XKV containers per pass), {what}, "
+                      f"{el:.1f} s wall"}, el / passes
+
+
+def host_workload(cfg, seed):
+    """Host-side inputs for the reference arm: numpy synthetic data encoded by the reference's
+    own encoder (no GPU code)."""
+    import numpy as np
+    import oracle as O
+    import synth as S
+    import workloads as W
+    ref = O.reference()
+    enc = ref.encode if ref is not None else O.oracle().encode
+    qs, ks, vs = [], [], []
+    for u in range(cfg.units):
+        kp = W.k_profile_of(cfg, u)
+        k = S.synth_bf16(seed, S.stream_id(u, 0), cfg.seq, cfg.dim, kp, W.rate_of(kp))
+        v = S.synth_bf16(seed, S.stream_id(u, 1), cfg.seq, cfg.dim, cfg.v_profile,
+                         W.rate_of(cfg.v_profile))
+        q = S.synth_bf16(seed, S.stream_id(u, 2), cfg.group, cfg.dim, S.PROFILE_Q, 0)
+        ks.append(enc(k, cfg.block))
+        vs.append(enc(v, cfg.block))
+        qs.append(np.ascontiguousarray(q))
+    return qs, ks, vs
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return
+    import workloads as W
+    cfg = W.CONFIGS[args.config]
+    if cfg.units * cfg.seq * cfg.dim * 4 > 64 << 30:
+        print(json.dumps({"impl": "reference", "unavailable":
+                          f"{cfg.name} does not fit host memory for the CPU reference"}))
+        return
+    qs, ks, vs = host_workload(cfg, 0x12345678)
+    import numpy as np
+    import oracle as O
+    ref = O.reference()
+    if ref is None:
+        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref was not built"}))
+        return
+    n = len(qs)
+    outs = [np.zeros((cfg.group, cfg.dim), dtype=np.float32) for _ in range(n)]
+    threads = max(1, min(n, os.cpu_count() or 1))
+    be = O.AVX512BF16 if ref.avx512_bf16 else (O.AVX2 if ref.avx2 else O.SCALAR)
+    bname = {O.AVX512BF16: "AVX-512 BF16", O.AVX2: "AVX2", O.SCALAR: "scalar"}[be]
+    total = sum(k.size for k in ks) + sum(v.size for v in vs)
+    step = lambda: ref.model_heads(be, qs, ks, vs, outs, cfg.group, cfg.dim, cfg.seq, threads)
+    # a step is one model_heads pass; keep the run within a few minutes
+    for _ in range(max(1, args.warmup)):
+        step()
+    t0 = time.perf_counter()
+    step()
+    one = time.perf_counter() - t0
+    steps = max(1, min(args.steps, int(120.0 / max(one, 1e-6))))
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        step()
+    el = time.perf_counter() - t0
+    gbps = total * steps / el / 1e9
+    line = {
+        "metric": METRIC, "impl": "reference", "value": gbps, "unit": "GB/s", "n_gpus": world,
+        "steps": steps, "warmup": max(1, args.warmup), "ms_per_step": el / steps * 1e3,
+        "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": gbps / PUBLISHED_GBPS, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": cfg.name, "units": n, "compressed_bytes_per_step": total,
+                   "backend": bname, "threads": threads},
+        "cpu_baseline": {"value": gbps, "unit": "GB/s", "cores": threads, "kind": "reference",
+                         "sample": f"{steps} model_heads passes over {n} units, {bname}"},
+        "e2e": {"value": gbps, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---- GPU arm ----------------------------------------------------------------------------------------
+
+def run_kvx(args, rank, world, local):
+    import numpy as np
+    import torch
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    import kvexp_b200 as kvx
+    import workloads as W
+    cfg = W.CONFIGS[args.config]
+    seed = 0x12345678 + 7919 * rank
+    cache = W.build_cache(cfg, seed=seed)
+    replica = W.build_cache(cfg, seed=seed)  # second copy: consecutive steps read other buffers
+    caches = [cache, replica]
+    plans = [kvx.Plan(c.kvx_units(), cfg.group, cfg.dim, cfg.block) for c in caches]
+    comp = cache.compressed_bytes
+    q_bytes = cfg.units * cfg.group * cfg.dim * 2
+    o_bytes = cfg.units * cfg.group * cfg.dim * 4
+    algo_bytes = comp + q_bytes + o_bytes
+    stream = torch.cuda.current_stream()
+    h = stream.cuda_stream
+
+    # own device read probe (the reference's peak.hpp read bandwidth, on HBM)
+    probe_buf = torch.empty(1 << 30, dtype=torch.uint8, device="cuda")
+    probe_gbs = kvx.hbm_read_probe(probe_buf, reps=5)
+    del probe_buf
+
+    for i in range(max(3, args.warmup)):
+        plans[i % 2].run(h)
+    plans[0].check()
+    plans[1].check()
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    sampler = ClockSampler(local)
+    sampler.start()
+    K = args.steps
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(K)]
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    start.record(stream)
+    for i in range(K):
+        p = plans[i % 2]
+        evs[i][0].record(stream)
+        p.run_part(0, h)
+        evs[i][1].record(stream)
+        p.run_part(1, h)
+    end.record(stream)
+    end.synchronize()
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    clocks = sampler.stop()
+    elapsed_ms = start.elapsed_time(end)
+    kern_ms = statistics.fmean(a.elapsed_time(b) for a, b in evs)
+    for p in plans:
+        p.check()
+    if dist:
+        t = torch.tensor([elapsed_ms, kern_ms], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        elapsed_ms, kern_ms = float(t[0]), float(t[1])
+    ms_step = elapsed_ms / K
+    value = comp * world * K / (elapsed_ms * 1e-3) / 1e9
+
+    # end to end through the reference-facing C ABI with pinned host buffers
+    e2e = None
+    if not args.no_e2e:
+        qs, ks, vs = cache.host_blobs()
+        pk = [torch.from_numpy(x).pin_memory() for x in ks]
+        pv = [torch.from_numpy(x).pin_memory() for x in vs]
+        pq = [torch.from_numpy(x.view(np.int16)).pin_memory() for x in qs]
+        po = [torch.zeros((cfg.group, cfg.dim), dtype=torch.float32).pin_memory()
+              for _ in range(cfg.units)]
+        call = lambda: kvx.attention_decode_units(
+            0, pq, pk, [x.numel() for x in pk], pv, [x.numel() for x in pv], po, cfg.group,
+            cfg.dim, cfg.seq)
+        call()
+        call()
+        ts = []
+        for _ in range(args.e2e_steps):
+            t0 = time.perf_counter()
+            call()
+            ts.append(time.perf_counter() - t0)
+        e2e_s = sum(ts) / len(ts)
+        if dist:
+            t = torch.tensor([e2e_s], dtype=torch.float64, device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            e2e_s = float(t[0])
+        e2e = {"value": comp * world / e2e_s / 1e9, "unit": "GB/s",
+               "h2d_bytes_per_step": comp + q_bytes, "d2h_bytes_per_step": o_bytes,
+               "ms_per_step": e2e_s * 1e3, "steps": args.e2e_steps,
+               "path": "kvx_attention_decode_units (C ABI) with pinned host blobs, one call "
+                       "per step: H2D of every blob and query, header walks, decode attention, "
+                       "D2H of outputs"}
+        # the outputs of the host path must equal the device-resident plan's outputs
+        got = np.stack([o.numpy() for o in po])
+        want = cache.out.cpu().numpy()
+        if not np.array_equal(got.view(np.uint32), want.view(np.uint32)):
+            rel = np.max(np.abs(got - want) / np.maximum(np.abs(want), 1e-3))
+            e2e["check"] = f"host-path outputs differ from the device plan (max rel {rel:.2e})"
+        else:
+            e2e["check"] = "bit-identical to the device-resident plan"
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        qs, ks, vs = cache.host_blobs()
+        cpu, _ = cpu_reference_rate(qs, ks, vs, cfg, args.cpu_seconds)
+
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    peak, peak_src = hbm_peak()
+    achieved = algo_bytes / (kern_ms * 1e-3) / 1e9
+    traffic = ncu_traffic(args.config)
+    line = {
+        "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": K,
+        "warmup": max(3, args.warmup), "ms_per_step": ms_step, "us_per_step": ms_step * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": value / PUBLISHED_GBPS,
+        "dtype": "bf16", "data": "synthetic (seeded generator; BASELINE.json distributions)",
+        "config": {
+            "workload": cfg.name, "units_per_gpu": cfg.units, "block_tokens": cfg.block,
+            "compressed_bytes_per_gpu_step": comp, "tight_bytes_per_gpu_step": cfg.tight_bytes,
+            "container_ratio": comp / cfg.tight_bytes,
+            "parallelism": f"dp{world}: an independent cache per GPU, no collective",
+            "l2": "inputs larger than L2 (container > 126 MB) and two cache copies alternate "
+                  "between steps",
+        },
+        "tight_equiv_gbps": cfg.tight_bytes * world * K / (elapsed_ms * 1e-3) / 1e9,
+        "pct_of_hbm_peak": 100.0 * (value / world) / peak,
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": achieved / peak, "traffic": traffic,
+                     "kernel": "attn_kernel (fused XKV decode + QK + online softmax + PV)",
+                     "algorithmic_bytes_per_launch": algo_bytes,
+                     "kernel_ms_per_launch": kern_ms, "peak_source": peak_src,
+                     "device_read_probe_gbs": probe_gbs},
+        "cpu_baseline": cpu,
+        "e2e": e2e,
+        "gpu_launches": K * plans[0].launches,
+        "clocks": clocks,
+        "impl": "kvexp_b200",
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    rank, world, local = env_rank()
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+    else:
+        run_kvx(args, rank, world, local)
+
+
+if __name__ == "__main__":
+    main()

@@ -391,8 +391,26 @@ int kvx_plan_create(const kvx_unit *units, int n_units, int n_q, int dim, int bl
 }
 
 int kvx_plan_run(kvx_plan p, void *stream) {
+    if (int rc = kvx_plan_run_part(p, 0, stream)) return rc;
+    return kvx_plan_run_part(p, 1, stream);
+}
+
+int kvx_plan_run_part(kvx_plan p, int part, void *stream) {
     if (p == nullptr) return fail(KVX_ERR_INVALID_ARGUMENT, "kvx_plan_run: null plan");
     cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (part == 1) {
+        if (p->n_split > 0) {
+            CombineArgs c{};
+            c.units = p->units;
+            c.split_units = p->split_units;
+            c.team_begin = p->team_begin;
+            c.partials = p->partials;
+            c.n_teams = p->n_teams;
+            KVX_CUDA(launch_combine(p->dim, c, p->n_split, s));
+        }
+        return KVX_OK;
+    }
+    if (part != 0) return fail(KVX_ERR_INVALID_ARGUMENT, "kvx_plan_run_part: part is 0 or 1");
     AttnArgs a{};
     a.units = p->units;
     a.flat = p->flat;
@@ -403,15 +421,6 @@ int kvx_plan_run(kvx_plan p, void *stream) {
     a.n_teams = p->n_teams;
     a.wait_limit = wait_limit_us();
     KVX_CUDA(launch_attention(p->dim, p->bf16, a, p->grid, 0, s));
-    if (p->n_split > 0) {
-        CombineArgs c{};
-        c.units = p->units;
-        c.split_units = p->split_units;
-        c.team_begin = p->team_begin;
-        c.partials = p->partials;
-        c.n_teams = p->n_teams;
-        KVX_CUDA(launch_combine(p->dim, c, p->n_split, s));
-    }
     return KVX_OK;
 }
 

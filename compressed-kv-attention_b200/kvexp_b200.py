@@ -101,6 +101,7 @@ _xkv_index = _sig("kvx_xkv_index", C.c_int,
 _plan_create = _sig("kvx_plan_create", C.c_int,
                     [_vp, C.c_int, C.c_int, C.c_int, C.c_int, C.POINTER(_vp)])
 _plan_run = _sig("kvx_plan_run", C.c_int, [_vp, _vp])
+_plan_run_part = _sig("kvx_plan_run_part", C.c_int, [_vp, C.c_int, _vp])
 _plan_check = _sig("kvx_plan_check", C.c_int, [_vp])
 _plan_launches = _sig("kvx_plan_launches", C.c_int, [_vp])
 _plan_destroy = _sig("kvx_plan_destroy", None, [_vp])
@@ -119,7 +120,7 @@ _probe = _sig("kvx_hbm_read_probe", C.c_int, [_vp, _sz, C.c_int, C.POINTER(C.c_d
 EXPORTED = [
     "kvx_last_error", "kvx_version", "kvx_device_info", "kvx_attention_decode",
     "kvx_attention_decode_units", "kvx_encode_bound", "kvx_encode_bf16", "kvx_decode_bf16",
-    "kvx_xkv_index", "kvx_plan_create", "kvx_plan_run", "kvx_plan_check", "kvx_plan_launches",
+    "kvx_xkv_index", "kvx_plan_create", "kvx_plan_run", "kvx_plan_run_part", "kvx_plan_check", "kvx_plan_launches",
     "kvx_plan_destroy", "kvx_encode_batch_bounds", "kvx_encode_batch", "kvx_cache_append",
     "kvx_synth_bf16", "kvx_hbm_read_probe",
 ]
@@ -246,6 +247,13 @@ class Plan:
 
     def run(self, stream=None):
         _check(_plan_run(self._h, stream))
+
+    def run_part(self, part, stream=None):
+        _check(_plan_run_part(self._h, int(part), stream))
+
+    @property
+    def n_split(self) -> int:
+        return self.launches - 1
 
     def check(self):
         _check(_plan_check(self._h))
