@@ -31,35 +31,40 @@ namespace {
 
 constexpr uint32_t FULL = 0xFFFFFFFFu;
 constexpr int TT = 16;  // tokens per tile (one m16 row block of the QK MMA)
+constexpr float kLog2e = 1.4426950408889634f;
+
+// 2^x by the SFU (ex2.approx.f32, subnormal results kept).
+__device__ __forceinline__ float ex2(float x) {
+    float y;
+    asm("ex2.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
 
 __host__ __device__ constexpr int round16(int x) { return (x + 15) & ~15; }
 
 template <int D> struct Cfg {
-    static constexpr int CH = D / 8;         // 16-byte chunks per BF16 row
-    static constexpr int STEPS = D / 16;     // 256-element warp steps per 16-row tile
-    static constexpr int ESC_CAP = 2048;     // escape bytes staged per block and tensor
-    static constexpr int INFO = 64;
+    static constexpr int CH = D / 8;          // 16-byte chunks per BF16 row
+    static constexpr int STEPS = D / 16;      // 256-element warp steps per 16-row tile
+    static constexpr int ESC_CAP = 1536;      // escape bytes staged per block and tensor
+    static constexpr int SLOT = 32 * D + 32;  // one tensor tile: raw rows, or sm + residual rows
+    static constexpr int NSTAGE = D <= 64 ? 4 : 3;
     static constexpr int BASE_SLOT = round16(D + 32);
-    static constexpr int ESC_SLOT = ESC_CAP + 32;
-    static constexpr int META = INFO + 2 * BASE_SLOT + 2 * ESC_SLOT;
-    static constexpr int TILE = TT * D * 2;                 // bytes of one BF16 tile
-    static constexpr int MAXTILE = 2 * (TT * D * 2 + 32);   // largest K+V allocation (raw)
-    static constexpr int RING = D == 32 ? 8192 : D == 64 ? 16384 : D == 128 ? 20480 : 36864;
-    static constexpr int NB = 8;                            // tile barriers
-    static constexpr int PSLOT = 640;                       // P fragments + alpha + m + l
-    static constexpr int OFF_META = RING;
-    static constexpr int OFF_KT = RING + 2 * META;
-    static constexpr int OFF_VT = OFF_KT + TILE;
-    static constexpr int OFF_PS = OFF_VT + TILE;
+    static constexpr int MSLOT = BASE_SLOT + ESC_CAP + 32;  // base + escapes of one block
+    static constexpr int TILE = TT * D * 2;                  // bytes of one BF16 tile
+    static constexpr int PSLOT = 640;                        // p values + alpha + m + l
+    // per-warp region: ring | meta x2 | BF16 tile | stage barriers
+    static constexpr int W_META = NSTAGE * SLOT;
+    static constexpr int W_TILE = W_META + 2 * MSLOT;
+    static constexpr int W_BAR = W_TILE + TILE;
+    static constexpr int WARP_BYTES = (W_BAR + NSTAGE * 8 + 127) & ~127;
+    // team: K-warp region | V-warp region | P slots x2 | full x2, empty x2 | abort flag
+    static constexpr int OFF_PS = 2 * WARP_BYTES;
     static constexpr int OFF_BAR = OFF_PS + 2 * PSLOT;
-    static constexpr int NBARS = NB + 6;                    // tiles, meta x2, full x2, empty x2
-    static constexpr int OFF_FLAG = OFF_BAR + NBARS * 8;
+    static constexpr int OFF_FLAG = OFF_BAR + 4 * 8;
     static constexpr int TEAM = (OFF_FLAG + 16 + 127) & ~127;
     static constexpr int BY_SMEM = 232448 / TEAM;
-    static constexpr int BY_REGS = D <= 64 ? 6 : (D == 128 ? 6 : 4);
-    static constexpr int TEAMS = BY_SMEM < BY_REGS ? BY_SMEM : BY_REGS;
+    static constexpr int TEAMS = BY_SMEM < 8 ? BY_SMEM : 8;
     static_assert(TEAMS >= 1, "team does not fit in shared memory");
-    static_assert(RING >= 2 * MAXTILE, "ring must hold two of the largest tiles");
 };
 
 // Swizzle of 16-byte chunks inside a BF16 tile row, so that ldmatrix row reads and the decoder's
@@ -145,12 +150,6 @@ template <int RING> __device__ __forceinline__ uint32_t place(uint32_t pos, uint
 
 // ---- decode of one tensor tile into a swizzled BF16 tile ---------------------------------------
 
-// 32-bit word at a 2-byte aligned shared address; sel = 0x3210 (aligned) or 0x5432 (2 mod 4).
-__device__ __forceinline__ uint32_t ldw(const uint8_t *p, uint32_t mis, uint32_t sel) {
-    const uint32_t *q = reinterpret_cast<const uint32_t *>(p - mis);
-    return prmt(q[0], q[1], sel);
-}
-
 // Exponent/sign merge per 16-bit half: sign and mantissa from the sign-replicated sm byte pair,
 // exponent bits from (code + base) << 7.  The bit-select drops the carry out of bit 14, so the
 // exponent wraps modulo 256 exactly like bf16_from_delta's uint8 sum (include/kvexp/bf16.hpp:35-37).
@@ -173,51 +172,70 @@ struct Esc {
     const uint8_t *gm;   // escape words in global memory
 };
 
-// Sentinel elements of this lane (mask bit SH*k for element k of its 8) take the next escape words
-// in scan order: lane order inside the 256-element step, element order inside the lane.  The
-// BF16 value is written straight into the tile slot of that element: element k sits at half
-// (k >> 2) of 32-bit word (k & 3) of the lane's 16-byte chunk.
+__device__ __forceinline__ uint32_t esc_word(uint32_t r, uint32_t n, const uint8_t *sm,
+                                             const uint8_t *gm, int *status) {
+    if (r >= n) {
+        report(status, KVX_ERR_RUNTIME, DERR_ESC_OVERRUN);
+        return 0;
+    }
+    return sm != nullptr ? *reinterpret_cast<const uint16_t *>(sm + 2 * r)
+                         : __ldg(reinterpret_cast<const unsigned short *>(gm) + r);
+}
+
+// General case of escape patching (some lane holds two or more sentinels).  Sentinel elements
+// take the next escape words in scan order: lane order inside the 256-element step, element
+// order inside the lane.  Element k of a lane sits at half (k >> 2) of 32-bit word (k & 3) of the
+// lane's 16-byte tile chunk.  Returns the new running escape count.
 template <int SH>
-__device__ __noinline__ void patch_escapes(uint8_t *chunk, uint32_t m, Esc &es, int *status) {
+__device__ __noinline__ uint32_t patch_general(uint8_t *chunk, uint32_t m, uint32_t run, uint32_t n,
+                                               const uint8_t *sm, const uint8_t *gm, int *status) {
     const uint32_t cnt = __popc(m);
     const uint32_t lt = lanemask_lt();
-    const uint32_t c0 = __ballot_sync(FULL, cnt & 1u);
-    const uint32_t big = __ballot_sync(FULL, cnt > 1u);
-    uint32_t pre, tot;
-    if (big == 0u) {
-        pre = __popc(c0 & lt);
-        tot = __popc(c0);
-    } else {
-        const uint32_t c1 = __ballot_sync(FULL, cnt & 2u), c2 = __ballot_sync(FULL, cnt & 4u);
-        const uint32_t c3 = __ballot_sync(FULL, cnt & 8u);
-        pre = __popc(c0 & lt) + 2 * __popc(c1 & lt) + 4 * __popc(c2 & lt) + 8 * __popc(c3 & lt);
-        tot = __popc(c0) + 2 * __popc(c1) + 4 * __popc(c2) + 8 * __popc(c3);
-    }
-    uint32_t r = es.run + pre;
-    es.run += tot;
+    const uint32_t c0 = __ballot_sync(FULL, cnt & 1u), c1 = __ballot_sync(FULL, cnt & 2u);
+    const uint32_t c2 = __ballot_sync(FULL, cnt & 4u), c3 = __ballot_sync(FULL, cnt & 8u);
+    uint32_t r = run + __popc(c0 & lt) + 2 * __popc(c1 & lt) + 4 * __popc(c2 & lt) +
+                 8 * __popc(c3 & lt);
+    const uint32_t tot = __popc(c0) + 2 * __popc(c1) + 4 * __popc(c2) + 8 * __popc(c3);
     while (m != 0u) {
         const int k = (__ffs(m) - 1) / SH;
         m &= m - 1u;
-        uint32_t v = 0;
-        if (r < es.n) {
-            v = es.sm != nullptr ? *reinterpret_cast<const uint16_t *>(es.sm + 2 * r)
-                                 : __ldg(reinterpret_cast<const unsigned short *>(es.gm) + r);
-        } else {
-            report(status, KVX_ERR_RUNTIME, DERR_ESC_OVERRUN);
-        }
+        *reinterpret_cast<uint16_t *>(chunk + 4 * (k & 3) + 2 * (k >> 2)) =
+            uint16_t(esc_word(r, n, sm, gm, status));
         ++r;
-        *reinterpret_cast<uint16_t *>(chunk + 4 * (k & 3) + 2 * (k >> 2)) = uint16_t(v);
+    }
+    return run + tot;
+}
+
+// Escape patching for one 256-element step: fast path when every lane holds at most one sentinel.
+template <int SH>
+__device__ __forceinline__ void patch(uint8_t *chunk, uint32_t m, Esc &es, int *status) {
+    const uint32_t has = __ballot_sync(FULL, m != 0u);
+    if (has == 0u) return;
+    if (__ballot_sync(FULL, (m & (m - 1u)) != 0u) == 0u) {
+        if (m != 0u) {
+            const uint32_t r = es.run + __popc(has & lanemask_lt());
+            const int k = (__ffs(m) - 1) / SH;
+            *reinterpret_cast<uint16_t *>(chunk + 4 * (k & 3) + 2 * (k >> 2)) =
+                uint16_t(esc_word(r, es.n, es.sm, es.gm, status));
+        }
+        es.run += __popc(has);
+    } else {
+        es.run = patch_general<SH>(chunk, m, es.run, es.n, es.sm, es.gm, status);
     }
 }
 
-template <int D>
-__device__ __forceinline__ void decode_tile(uint8_t *tile, int mode, int rows, const uint8_t *p0,
-                                            const uint8_t *p1, const uint32_t (&b7)[4], Esc &es,
-                                            int *status, int lane) {
+template <bool MIS> __device__ __forceinline__ uint32_t ldw2(const uint8_t *p) {
+    if (!MIS) return *reinterpret_cast<const uint32_t *>(p);
+    const uint32_t *q = reinterpret_cast<const uint32_t *>(p - 2);
+    return prmt(q[0], q[1], 0x5432);
+}
+
+template <int D, bool MIS>
+__device__ __forceinline__ void decode_tile_t(uint8_t *tile, int mode, int rows, const uint8_t *p0,
+                                              const uint8_t *p1, const uint32_t (&b7)[4], Esc &es,
+                                              int *status, int lane) {
     constexpr int CH = Cfg<D>::CH;
     const int ch = lane % CH;
-    const uint32_t mis = uint32_t(reinterpret_cast<uintptr_t>(p0) & 2u);
-    const uint32_t sel = mis ? 0x5432u : 0x3210u;
 #pragma unroll 1
     for (int c = 0; c < Cfg<D>::STEPS; ++c) {
         const int e0 = 256 * c + 8 * lane;
@@ -227,17 +245,17 @@ __device__ __forceinline__ void decode_tile(uint8_t *tile, int mode, int rows, c
         if (row < rows) {
             if (mode == 0) {
                 const uint8_t *p = p0 + 2 * e0;
-                const uint32_t w0 = ldw(p, mis, sel), w1 = ldw(p + 4, mis, sel);
-                const uint32_t w2 = ldw(p + 8, mis, sel), w3 = ldw(p + 12, mis, sel);
+                const uint32_t w0 = ldw2<MIS>(p), w1 = ldw2<MIS>(p + 4);
+                const uint32_t w2 = ldw2<MIS>(p + 8), w3 = ldw2<MIS>(p + 12);
                 bf0 = prmt(w0, w2, 0x5410);
                 bf1 = prmt(w0, w2, 0x7632);
                 bf2 = prmt(w1, w3, 0x5410);
                 bf3 = prmt(w1, w3, 0x7632);
             } else {
-                const uint32_t S0 = ldw(p0 + e0, mis, sel), S1 = ldw(p0 + e0 + 4, mis, sel);
+                const uint32_t S0 = ldw2<MIS>(p0 + e0), S1 = ldw2<MIS>(p0 + e0 + 4);
                 uint32_t X, sh, mask;
                 if (mode == 4) {
-                    X = ldw(p1 + e0 / 2, mis, sel);  // element k at bits 4k
+                    X = ldw2<MIS>(p1 + e0 / 2);  // element k at bits 4k
                     uint32_t t = X & (X >> 1);
                     t &= t >> 2;
                     m = t & 0x11111111u;
@@ -245,8 +263,8 @@ __device__ __forceinline__ void decode_tile(uint8_t *tile, int mode, int rows, c
                     mask = 0x000F000Fu;
                 } else {
                     const uint32_t C = *reinterpret_cast<const uint16_t *>(p1 + e0 / 4);
-                    m = C & (C >> 1) & 0x5555u;       // element k at bits 2k
-                    X = prmt(C, 0, 0x0110);           // elements 4..7 up to bits 16..23
+                    m = C & (C >> 1) & 0x5555u;   // element k at bits 2k
+                    X = prmt(C, 0, 0x0110);       // elements 4..7 up to bits 16..23
                     sh = 2;
                     mask = 0x00030003u;
                 }
@@ -258,18 +276,26 @@ __device__ __forceinline__ void decode_tile(uint8_t *tile, int mode, int rows, c
         }
         uint8_t *dst = tile + row * (2 * D) + 16 * (ch ^ swz<D>(row));
         *reinterpret_cast<uint4 *>(dst) = make_uint4(bf0, bf1, bf2, bf3);
-        if (mode != 0 && __any_sync(FULL, m != 0u)) {
-            if (mode == 4) patch_escapes<4>(dst, m, es, status);
-            else patch_escapes<2>(dst, m, es, status);
-        }
+        if (mode == 4) patch<4>(dst, m, es, status);
+        else if (mode == 2) patch<2>(dst, m, es, status);
     }
+}
+
+template <int D>
+__device__ __forceinline__ void decode_tile(uint8_t *tile, int mode, int rows, const uint8_t *p0,
+                                            const uint8_t *p1, const uint32_t (&b7)[4], Esc &es,
+                                            int *status, int lane) {
+    if (reinterpret_cast<uintptr_t>(p0) & 2u)
+        decode_tile_t<D, true>(tile, mode, rows, p0, p1, b7, es, status, lane);
+    else
+        decode_tile_t<D, false>(tile, mode, rows, p0, p1, b7, es, status, lane);
 }
 
 // b7[i] = (base[d0+i] << 7) | (base[d0+i+4] << 23)
 __device__ __forceinline__ void load_base(const uint8_t *p, uint32_t (&b7)[4]) {
-    const uint32_t mis = uint32_t(reinterpret_cast<uintptr_t>(p) & 2u);
-    const uint32_t sel = mis ? 0x5432u : 0x3210u;
-    const uint32_t B0 = ldw(p, mis, sel), B1 = ldw(p + 4, mis, sel);
+    const bool mis = (reinterpret_cast<uintptr_t>(p) & 2u) != 0u;
+    const uint32_t B0 = mis ? ldw2<true>(p) : ldw2<false>(p);
+    const uint32_t B1 = mis ? ldw2<true>(p + 4) : ldw2<false>(p + 4);
 #pragma unroll
     for (int i = 0; i < 4; ++i)
         b7[i] = (prmt(B0, B1, uint32_t(i) | (uint32_t(4 + i) << 8)) & 0x00FF00FFu) << 7;
@@ -299,15 +325,24 @@ __device__ __forceinline__ void load_q_frags(const uint16_t *q, int n_q, int str
 
 // ---- the kernel -------------------------------------------------------------------------------
 
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+// Arrive on `bar` once every cp.async this thread issued so far has landed.
+__device__ __forceinline__ void cp_async_arrive(uint32_t bar) {
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(bar) : "memory");
+}
+// The warp copies one piece: lane l moves 16-byte chunks l, l + 32, ...
+__device__ __forceinline__ void copy_piece(uint32_t dst, const Piece &p, int lane) {
+    const uint32_t n = p.alloc >> 4;
+    for (uint32_t j = lane; j < n; j += 32) cp_async16(dst + 16 * j, p.src + 16 * j);
+}
+
 struct Team {
     uint8_t *T;
-    uint32_t bar0;
+    uint32_t bar0;  // full x2, empty x2
     volatile int *abort;
 };
-
-template <int NB> __device__ __forceinline__ uint32_t tile_bar(uint32_t bar0, int i) {
-    return bar0 + 8u * uint32_t(i % NB);
-}
 
 // Bounded wait that also gives up when the partner warp aborted.
 __device__ __forceinline__ bool wait_bar(uint32_t bar, uint32_t parity, const Team &t,
@@ -326,145 +361,184 @@ __device__ __forceinline__ bool wait_bar(uint32_t bar, uint32_t parity, const Te
     return true;
 }
 
-struct BlockInfo {
-    FlatBlock fb;
-    int unit;
-    uint32_t staged;  // bit0: K escapes staged, bit1: V escapes staged
+// Walks the team's flat blocks with one block of prefetch.
+struct Walker {
+    int64_t fb, fb1;
+    FlatBlock cur, nxt;
+    int unit, nunit;
+    __device__ void init(const AttnArgs &a, int64_t b0, int64_t b1) {
+        fb = b0;
+        fb1 = b1;
+        cur = load_flat(a.flat, fb);
+        unit = __ldg(a.flat_unit + fb);
+        nunit = unit;
+        if (fb + 1 < fb1) {
+            nxt = load_flat(a.flat, fb + 1);
+            nunit = __ldg(a.flat_unit + fb + 1);
+        }
+    }
+    __device__ void next(const AttnArgs &a) {
+        ++fb;
+        if (fb < fb1) {
+            cur = nxt;
+            unit = nunit;
+            if (fb + 1 < fb1) {
+                nxt = load_flat(a.flat, fb + 1);
+                nunit = __ldg(a.flat_unit + fb + 1);
+            }
+        }
+    }
 };
 
-__device__ __forceinline__ BlockInfo read_info(const uint8_t *M) {
-    const uint4 w = *reinterpret_cast<const uint4 *>(M);
-    const uint2 x = *reinterpret_cast<const uint2 *>(M + 16);
-    BlockInfo b;
-    b.fb.k_off = w.x;
-    b.fb.v_off = w.y;
-    b.fb.k_nesc = uint16_t(w.z & 0xFFFF);
-    b.fb.v_nesc = uint16_t(w.z >> 16);
-    b.fb.k_mode = uint8_t(w.w & 0xFF);
-    b.fb.v_mode = uint8_t((w.w >> 8) & 0xFF);
-    b.fb.n_tok = uint8_t((w.w >> 16) & 0xFF);
-    b.fb.valid = uint8_t(w.w >> 24);
-    b.unit = int(x.x);
-    b.staged = x.y;
-    return b;
-}
+// One warp's own copy pipeline for its tensor (t = 0: K, 1: V): cp.async tiles into a ring of
+// NSTAGE slots, each completing on its own mbarrier; a block's first tile also brings the block's
+// base array and (when they fit) its escape words into a meta slot.
+template <int D, bool BF16IN> struct Pipe {
+    using C = Cfg<D>;
+    uint8_t *R;       // this warp's region
+    uint32_t sbar;    // stage barriers
+    int t;            // tensor
+    Walker pw;        // producer position
+    int p_tile = 0, p_stage = 0, p_bseq = 0;
+    int p_unit = -1;
+    const uint8_t *p_blob = nullptr;
 
-// Consumer-side position in the team's tile stream; both warps keep an identical copy.
-template <int D, bool BF16IN> struct Stream {
-    int64_t fb0, fb1, fb, seg_begin;
-    int tile = 0, i = 0, jb = 0;
-    uint32_t pos = 0;
-    BlockInfo bi{};
-    int unit = -1;
+    __device__ static int mode_of(const FlatBlock &f, int t) { return t == 0 ? f.k_mode : f.v_mode; }
+    __device__ static uint32_t off_of(const FlatBlock &f, int t) { return t == 0 ? f.k_off : f.v_off; }
+    __device__ static int nesc_of(const FlatBlock &f, int t) { return t == 0 ? f.k_nesc : f.v_nesc; }
+
+    // Escape words of a block and whether they are staged in the meta slot.
+    __device__ static Piece esc_piece(const Geo &g, int n_tok, int nesc, bool &staged) {
+        const Piece e = make_piece(g.s1 + size_t(n_tok) * D * g.mode / 8, uint32_t(2 * nesc));
+        staged = nesc > 0 && e.alloc <= uint32_t(C::ESC_CAP + 32);
+        return e;
+    }
+
+    // Issue tiles while a ring slot is free; block starts wait until the consumer is at most one
+    // block behind, so a meta slot is never overwritten while in use.
+    __device__ void produce(const AttnArgs &a, int c_stage, int64_t c_fb, int lane) {
+        while (pw.fb < pw.fb1 && p_stage - c_stage < C::NSTAGE) {
+            if (p_tile == 0 && pw.fb - c_fb >= 2) break;
+            const FlatBlock &f = pw.cur;
+            if (pw.unit != p_unit) {
+                p_unit = pw.unit;
+                p_blob = t == 0 ? a.units[p_unit].k : a.units[p_unit].v;
+            }
+            const Geo g = make_geo<D, BF16IN>(p_blob, off_of(f, t), mode_of(f, t), f.n_tok);
+            const int rows = min(TT, int(f.n_tok) - p_tile * TT);
+            Piece pc[2];
+            const int np = geo_pieces<D>(g, p_tile, rows, pc);
+            const uint32_t slot = smem_u32(R + (p_stage % C::NSTAGE) * C::SLOT);
+            copy_piece(slot, pc[0], lane);
+            if (np == 2) copy_piece(slot + pc[0].alloc, pc[1], lane);
+            if (!BF16IN && p_tile == 0 && g.mode != 0) {
+                const uint32_t ms = smem_u32(R + C::W_META + (p_bseq & 1) * C::MSLOT);
+                copy_piece(ms, make_piece(g.s0 - D, D), lane);
+                bool staged;
+                const Piece e = esc_piece(g, f.n_tok, nesc_of(f, t), staged);
+                if (staged) copy_piece(ms + C::BASE_SLOT, e, lane);
+            }
+            cp_async_arrive(sbar + 8u * uint32_t(p_stage % C::NSTAGE));
+            ++p_stage;
+            if (++p_tile * TT >= int(f.valid)) {
+                p_tile = 0;
+                ++p_bseq;
+                pw.next(a);
+            }
+        }
+    }
+};
+
+// Consumer-side position (both warps keep their own copy).
+template <int D, bool BF16IN> struct Cursor {
+    using C = Cfg<D>;
+    Walker cw;
+    int64_t fb0, seg_begin;
+    int tile = 0, stage = 0, bseq = 0, unit = -1;
     UnitDev cu{};
-    Geo gk{}, gv{};
-    // the current tile
-    Piece kp[2], vp[2];
-    int nk = 0, nv = 0, rows = 0;
-    uint32_t ksz = 0, size = 0, at = 0;
+    Geo g{};          // this warp's tensor in the current block
+    int rows = 0;
     bool first = true, last_tile = false, seg_end = false;
 
-    __device__ Stream(int64_t b0, int64_t b1) : fb0(b0), fb1(b1), fb(b0), seg_begin(b0) {}
-
-    // Block start: wait for the block's meta, read its info, set up this warp's tensor.
-    __device__ bool begin_block(const Team &tm, const AttnArgs &a, int w, int lane,
-                                uint32_t (&b7)[4], Esc &es) {
-        using C = Cfg<D>;
-        const uint8_t *M = tm.T + C::OFF_META + (jb & 1) * C::META;
-        const uint32_t meta_bar = tm.bar0 + 8u * C::NB + 8u * uint32_t(jb & 1);
-        if (!wait_bar(meta_bar, (jb >> 1) & 1, tm, a)) return false;
-        bi = read_info(M);
-        if (bi.unit != unit) {
-            unit = bi.unit;
-            cu = a.units[unit];
-        }
-        gk = make_geo<D, BF16IN>(cu.k, bi.fb.k_off, bi.fb.k_mode, bi.fb.n_tok);
-        gv = make_geo<D, BF16IN>(cu.v, bi.fb.v_off, bi.fb.v_mode, bi.fb.n_tok);
-        const Geo &mine = w == 0 ? gk : gv;
-        if (!BF16IN && mine.mode != 0) {
-            const uint8_t *b = mine.s0 - D;  // the block's base array
-            load_base(M + C::INFO + w * C::BASE_SLOT + (reinterpret_cast<uintptr_t>(b) & 15u) +
-                          8 * (lane % C::CH),
-                      b7);
-            const uint8_t *e = mine.s1 + size_t(bi.fb.n_tok) * D * mine.mode / 8;
-            es.run = 0;
-            es.n = w == 0 ? bi.fb.k_nesc : bi.fb.v_nesc;
-            es.gm = e;
-            es.sm = (bi.staged & (1u << w)) ? M + C::INFO + 2 * C::BASE_SLOT + w * C::ESC_SLOT +
-                                                  (reinterpret_cast<uintptr_t>(e) & 15u)
-                                            : nullptr;
-        }
-        return true;
+    __device__ void init(const AttnArgs &a, int64_t b0, int64_t b1) {
+        cw.init(a, b0, b1);
+        fb0 = b0;
+        seg_begin = b0;
     }
-
-    // Geometry of tile `tile` of the current block and where the producer put it in the ring.
-    __device__ void locate() {
-        using C = Cfg<D>;
+    // Set up the current tile; at a block start also the base registers and escape source
+    // (the meta slot was filled by the block's first stage, which the caller has waited for).
+    __device__ void setup(const AttnArgs &a, const uint8_t *R, int t, int lane, uint32_t (&b7)[4],
+                          Esc &es) {
+        const FlatBlock &f = cw.cur;
         first = tile == 0;
-        const int rows_layout = min(TT, int(bi.fb.n_tok) - tile * TT);
-        rows = min(TT, int(bi.fb.valid) - tile * TT);
-        nk = geo_pieces<D>(gk, tile, rows_layout, kp);
-        nv = geo_pieces<D>(gv, tile, rows_layout, vp);
-        ksz = kp[0].alloc + (nk == 2 ? kp[1].alloc : 0u);
-        size = ksz + vp[0].alloc + (nv == 2 ? vp[1].alloc : 0u);
-        at = place<C::RING>(pos, size);
-        last_tile = (tile + 1) * TT >= int(bi.fb.valid);
+        if (first) {
+            if (cw.unit != unit) {
+                unit = cw.unit;
+                cu = a.units[unit];
+            }
+            g = make_geo<D, BF16IN>(t == 0 ? cu.k : cu.v, Pipe<D, BF16IN>::off_of(f, t),
+                                    Pipe<D, BF16IN>::mode_of(f, t), f.n_tok);
+            if (!BF16IN && g.mode != 0) {
+                const uint8_t *ms = R + C::W_META + (bseq & 1) * C::MSLOT;
+                const uint8_t *b = g.s0 - D;
+                load_base(ms + (reinterpret_cast<uintptr_t>(b) & 15u) + 8 * (lane % C::CH), b7);
+                bool staged;
+                const Piece e = Pipe<D, BF16IN>::esc_piece(g, f.n_tok, Pipe<D, BF16IN>::nesc_of(f, t),
+                                                           staged);
+                es.run = 0;
+                es.n = Pipe<D, BF16IN>::nesc_of(f, t);
+                es.gm = e.src + e.data;
+                es.sm = staged ? ms + C::BASE_SLOT + e.data : nullptr;
+            }
+        }
+        rows = min(TT, int(f.valid) - tile * TT);
+        last_tile = (tile + 1) * TT >= int(f.valid);
         const int64_t ub = cu.block_begin + cu.n_blocks;
-        seg_end = last_tile && ((fb + 1 == fb1) || (fb + 1 == ub));
+        seg_end = last_tile && ((cw.fb + 1 == cw.fb1) || (cw.fb + 1 == ub));
     }
-
     __device__ bool whole_unit() const {
-        return seg_begin == cu.block_begin && fb + 1 == cu.block_begin + cu.n_blocks;
+        return seg_begin == cu.block_begin && cw.fb + 1 == cu.block_begin + cu.n_blocks;
     }
-
-    __device__ void advance() {
-        pos = at + size;
-        ++i;
+    // Where this tile's data starts in the slot.
+    __device__ void data(const uint8_t *R, const uint8_t *&p0, const uint8_t *&p1) const {
+        const FlatBlock &f = cw.cur;
+        const int rl = min(TT, int(f.n_tok) - tile * TT);
+        Piece pc[2];
+        const int np = geo_pieces<D>(g, tile, rl, pc);
+        const uint8_t *slot = R + (stage % C::NSTAGE) * C::SLOT;
+        p0 = slot + pc[0].data;
+        p1 = np == 2 ? slot + pc[0].alloc + pc[1].data : nullptr;
+    }
+    __device__ void advance(const AttnArgs &a) {
+        ++stage;
         if (last_tile) {
             tile = 0;
-            ++jb;
-            if (seg_end) seg_begin = fb + 1;
-            ++fb;
+            ++bseq;
+            if (seg_end) seg_begin = cw.fb + 1;
+            cw.next(a);
         } else {
             ++tile;
         }
     }
 };
 
-// K-warp: issues the TMA copies, rebuilds K, runs QK and the online softmax, hands P over.
+// K-warp: streams and rebuilds K, runs QK and the online softmax, hands p over to the V-warp.
 template <int D, bool BF16IN>
-__device__ __forceinline__ void k_warp(const AttnArgs &a, const Team &tm, int team, int64_t fb0,
+__device__ __forceinline__ void k_warp(const AttnArgs &a, const Team &tm, uint8_t *R, int64_t fb0,
                                        int64_t fb1, int lane) {
     using C = Cfg<D>;
-    uint8_t *ring = tm.T;
-    uint8_t *kt = tm.T + C::OFF_KT;
-    const uint32_t meta_bar = tm.bar0 + 8u * C::NB;
-    const uint32_t full_bar = meta_bar + 16u;
-    const uint32_t empty_bar = full_bar + 16u;
+    const uint32_t full_bar = tm.bar0, empty_bar = tm.bar0 + 16u;
     const int gi = lane >> 2, tig = lane & 3;
-    Stream<D, BF16IN> st(fb0, fb1);
+    Pipe<D, BF16IN> pp;
+    pp.R = R;
+    pp.sbar = smem_u32(R + C::W_BAR);
+    pp.t = 0;
+    pp.pw.init(a, fb0, fb1);
+    Cursor<D, BF16IN> cs;
+    cs.init(a, fb0, fb1);
     uint32_t b7[4] = {0, 0, 0, 0};
     Esc es{0, 0, nullptr, nullptr};
-    bool ok = true;
-
-    // producer state
-    int64_t p_fb = fb0;
-    int p_tile = 0, p_i = 0, p_jb = 0;
-    bool p_meta = false;
-    uint32_t p_pos = 0;
-    FlatBlock p_blk = load_flat(a.flat, p_fb), nx_blk{};
-    int p_unit = __ldg(a.flat_unit + p_fb), nx_unit = -1;
-    const uint8_t *pk = a.units[p_unit].k, *pv = a.units[p_unit].v;
-    int p_ntiles = (p_blk.valid + TT - 1) / TT;
-    if (p_fb + 1 < fb1) {
-        nx_blk = load_flat(a.flat, p_fb + 1);
-        nx_unit = __ldg(a.flat_unit + p_fb + 1);
-    }
-    uint32_t tail = 0;                // ring bytes before this position are free
-    uint32_t end_m1 = 0, end_m2 = 0;  // ring end of tiles i-1, i-2
-    int last_m1 = 0, last_m2 = 0;     // were they the last tile of their block
-    int rel_jb = 0;                   // blocks whose meta both warps are done with
-
+    uint8_t *kt = R + C::W_TILE;
     uint32_t qb[D / 16][2];
     float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
     const int mat = lane >> 3;
@@ -472,143 +546,25 @@ __device__ __forceinline__ void k_warp(const AttnArgs &a, const Team &tm, int te
     const int cadd = mat >> 1;
     const int sw = swz<D>(r);
     const uint32_t krow = smem_u32(kt) + uint32_t(r * 2 * D);
+    bool ok = true;
 
-    while (st.fb < fb1) {
-        const int slot = st.i & 1;
-        // The V-warp is done with tile i - 2: its ring bytes, its P slot and (for a block's last
-        // tile) its meta slot are free.  With that, tile i can always be issued: at most tiles
-        // i - 1 and i are live and the ring holds two of the largest tiles.
-        if (st.i >= 2) {
-            if (!wait_bar(empty_bar + 8u * uint32_t(slot), ((st.i - 2) >> 1) & 1, tm, a)) {
-                ok = false;
-                break;
-            }
-            tail = end_m2;
-            if (last_m2) ++rel_jb;
-        }
-        // ---- producer: issue tiles ahead ----
-        while (p_fb < fb1 && p_i - st.i < C::NB - 2) {
-            if (!p_meta) {
-                if (p_jb - rel_jb >= 2) break;
-                uint8_t *M = tm.T + C::OFF_META + (p_jb & 1) * C::META;
-                const uint32_t mbar = meta_bar + 8u * uint32_t(p_jb & 1);
-                uint32_t tx = 0;
-                Piece mp[4];
-                bool stage[4] = {false, false, false, false};
-                if (!BF16IN) {
-#pragma unroll
-                    for (int t = 0; t < 2; ++t) {
-                        const int mode = t == 0 ? p_blk.k_mode : p_blk.v_mode;
-                        if (mode == 0) continue;
-                        const uint8_t *b =
-                            (t == 0 ? pk + p_blk.k_off : pv + p_blk.v_off) + kHeaderBytes;
-                        const int nesc = t == 0 ? p_blk.k_nesc : p_blk.v_nesc;
-                        mp[2 * t] = make_piece(b, D);
-                        stage[2 * t] = true;
-                        const uint8_t *e = b + D + size_t(p_blk.n_tok) * D +
-                                           size_t(p_blk.n_tok) * D * mode / 8;
-                        mp[2 * t + 1] = make_piece(e, uint32_t(2 * nesc));
-                        stage[2 * t + 1] = nesc > 0 && mp[2 * t + 1].alloc <= uint32_t(C::ESC_SLOT);
-                    }
-#pragma unroll
-                    for (int t = 0; t < 4; ++t)
-                        if (stage[t]) tx += mp[t].alloc;
-                }
-                if (lane == 0) {
-                    *reinterpret_cast<uint4 *>(M) = make_uint4(
-                        p_blk.k_off, p_blk.v_off,
-                        uint32_t(p_blk.k_nesc) | (uint32_t(p_blk.v_nesc) << 16),
-                        uint32_t(p_blk.k_mode) | (uint32_t(p_blk.v_mode) << 8) |
-                            (uint32_t(p_blk.n_tok) << 16) | (uint32_t(p_blk.valid) << 24));
-                    *reinterpret_cast<uint2 *>(M + 16) =
-                        make_uint2(uint32_t(p_unit), (stage[1] ? 1u : 0u) | (stage[3] ? 2u : 0u));
-                    fence_proxy_async();
-                    if (tx == 0) {
-                        mbar_arrive(mbar);
-                    } else {
-                        mbar_arrive_expect_tx(mbar, tx);
-                        // mp order: K base, K escapes, V base, V escapes
-                        const uint32_t dst[4] = {
-                            smem_u32(M + C::INFO), smem_u32(M + C::INFO + 2 * C::BASE_SLOT),
-                            smem_u32(M + C::INFO + C::BASE_SLOT),
-                            smem_u32(M + C::INFO + 2 * C::BASE_SLOT + C::ESC_SLOT)};
-#pragma unroll
-                        for (int t = 0; t < 4; ++t)
-                            if (stage[t]) bulk_g2s(dst[t], mp[t].src, mp[t].alloc, mbar);
-                    }
-                }
-                p_meta = true;
-                ++p_jb;
-            }
-            const Geo g0 = make_geo<D, BF16IN>(pk, p_blk.k_off, p_blk.k_mode, p_blk.n_tok);
-            const Geo g1 = make_geo<D, BF16IN>(pv, p_blk.v_off, p_blk.v_mode, p_blk.n_tok);
-            const int prow = min(TT, int(p_blk.n_tok) - p_tile * TT);
-            Piece kp[2], vp[2];
-            const int nk = geo_pieces<D>(g0, p_tile, prow, kp);
-            const int nv = geo_pieces<D>(g1, p_tile, prow, vp);
-            const uint32_t size = kp[0].alloc + (nk == 2 ? kp[1].alloc : 0u) + vp[0].alloc +
-                                  (nv == 2 ? vp[1].alloc : 0u);
-            const uint32_t pos = place<C::RING>(p_pos, size);
-            if (pos + size - tail > uint32_t(C::RING)) break;
-            if (lane == 0) {
-                const uint32_t bar = tile_bar<C::NB>(tm.bar0, p_i);
-                fence_proxy_async();
-                mbar_arrive_expect_tx(bar, size);
-                uint32_t dst = smem_u32(ring + pos % C::RING);
-                bulk_g2s(dst, kp[0].src, kp[0].alloc, bar);
-                dst += kp[0].alloc;
-                if (nk == 2) {
-                    bulk_g2s(dst, kp[1].src, kp[1].alloc, bar);
-                    dst += kp[1].alloc;
-                }
-                bulk_g2s(dst, vp[0].src, vp[0].alloc, bar);
-                dst += vp[0].alloc;
-                if (nv == 2) bulk_g2s(dst, vp[1].src, vp[1].alloc, bar);
-            }
-            p_pos = pos + size;
-            ++p_i;
-            if (++p_tile == p_ntiles) {
-                p_tile = 0;
-                p_meta = false;
-                ++p_fb;
-                if (p_fb < fb1) {
-                    p_blk = nx_blk;
-                    p_ntiles = (p_blk.valid + TT - 1) / TT;
-                    if (nx_unit != p_unit) {
-                        p_unit = nx_unit;
-                        pk = a.units[p_unit].k;
-                        pv = a.units[p_unit].v;
-                    }
-                    if (p_fb + 1 < fb1) {
-                        nx_blk = load_flat(a.flat, p_fb + 1);
-                        nx_unit = __ldg(a.flat_unit + p_fb + 1);
-                    }
-                }
-            }
-        }
-
-        // ---- consume tile i ----
-        if (st.tile == 0) {
-            if (!st.begin_block(tm, a, 0, lane, b7, es)) {
-                ok = false;
-                break;
-            }
-            if (st.fb == st.seg_begin) {
-                load_q_frags<D>(st.cu.q, st.cu.n_q, st.cu.q_stride, qb, lane);
-                m0 = m1 = -INFINITY;
-                l0 = l1 = 0.f;
-            }
-        }
-        if (!wait_bar(tile_bar<C::NB>(tm.bar0, st.i), (st.i / C::NB) & 1, tm, a)) {
+    while (cs.cw.fb < fb1) {
+        pp.produce(a, cs.stage, cs.cw.fb, lane);
+        if (!wait_bar(pp.sbar + 8u * uint32_t(cs.stage % C::NSTAGE), (cs.stage / C::NSTAGE) & 1, tm,
+                      a)) {
             ok = false;
             break;
         }
-        st.locate();
-        const uint8_t *base = ring + st.at % C::RING;
-        const int rows = st.rows;
-        decode_tile<D>(kt, st.gk.mode, rows, base + st.kp[0].data,
-                       st.nk == 2 ? base + st.kp[0].alloc + st.kp[1].data : nullptr, b7, es,
-                       a.status, lane);
+        cs.setup(a, R, 0, lane, b7, es);
+        if (cs.first && cs.cw.fb == cs.seg_begin) {
+            load_q_frags<D>(cs.cu.q, cs.cu.n_q, cs.cu.q_stride, qb, lane);
+            m0 = m1 = -INFINITY;
+            l0 = l1 = 0.f;
+        }
+        const uint8_t *p0, *p1;
+        cs.data(R, p0, p1);
+        const int rows = cs.rows;
+        decode_tile<D>(kt, cs.g.mode, rows, p0, p1, b7, es, a.status, lane);
         __syncwarp();
         // S^T[16 tokens x 8 queries] = K[16 x D] * Q^T[D x 8]
         float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
@@ -626,101 +582,118 @@ __device__ __forceinline__ void k_warp(const AttnArgs &a, const Team &tm, int te
             t0 = fmaxf(t0, __shfl_xor_sync(FULL, t0, o));
             t1 = fmaxf(t1, __shfl_xor_sync(FULL, t1, o));
         }
+        // p = 2^(s log2e - m log2e): one FMA and one ex2 per score
         const float mn0 = fmaxf(m0, t0), mn1 = fmaxf(m1, t1);
-        const float al0 = expf(m0 - mn0), al1 = expf(m1 - mn1);
-        const float p0 = expf(s0 - mn0), p1 = expf(s1 - mn1);
-        const float p2 = expf(s2 - mn0), p3 = expf(s3 - mn1);
-        l0 = __fmaf_rn(l0, al0, __fadd_rn(p0, p2));
-        l1 = __fmaf_rn(l1, al1, __fadd_rn(p1, p3));
+        const float ml0 = __fmul_rn(mn0, kLog2e), ml1 = __fmul_rn(mn1, kLog2e);
+        const float al0 = ex2(__fmaf_rn(m0, kLog2e, -ml0)), al1 = ex2(__fmaf_rn(m1, kLog2e, -ml1));
+        const float p0v = ex2(__fmaf_rn(s0, kLog2e, -ml0)), p1v = ex2(__fmaf_rn(s1, kLog2e, -ml1));
+        const float p2v = ex2(__fmaf_rn(s2, kLog2e, -ml0)), p3v = ex2(__fmaf_rn(s3, kLog2e, -ml1));
+        l0 = __fmaf_rn(l0, al0, __fadd_rn(p0v, p2v));
+        l1 = __fmaf_rn(l1, al1, __fadd_rn(p1v, p3v));
         m0 = mn0;
         m1 = mn1;
-        // P^T tiles -> P A-fragments: rows 0-7 carry bf16(p), rows 8-15 bf16(p - bf16(p))
-        const uint32_t h01 = pack_bf16x2(p1, p0), h23 = pack_bf16x2(p3, p2);
-        const float r0 = __fsub_rn(p0, bf16lo_to_f32(h01));
-        const float r1 = __fsub_rn(p1, bf16hi_to_f32(h01));
-        const float r2 = __fsub_rn(p2, bf16lo_to_f32(h23));
-        const float r3 = __fsub_rn(p3, bf16hi_to_f32(h23));
-        const uint32_t mm01 = pack_bf16x2(r1, r0), mm23 = pack_bf16x2(r3, r2);
-        uint8_t *P = tm.T + C::OFF_PS + slot * C::PSLOT;
-        reinterpret_cast<uint4 *>(P)[lane] =
-            make_uint4(movm_t(h01), movm_t(mm01), movm_t(h23), movm_t(mm23));
-        float *pf = reinterpret_cast<float *>(P + 512);
-        if (st.seg_end) {
-            float lt0 = l0, lt1 = l1;
+        float lt0 = l0, lt1 = l1;
+        if (cs.seg_end) {
 #pragma unroll
             for (int o = 4; o < 32; o <<= 1) {
                 lt0 = __fadd_rn(lt0, __shfl_xor_sync(FULL, lt0, o));
                 lt1 = __fadd_rn(lt1, __shfl_xor_sync(FULL, lt1, o));
             }
-            if (gi == 0) {
+        }
+        // hand p over; slot reuse waits until the V-warp is done with tile stage - 2
+        const int slot = cs.stage & 1;
+        if (cs.stage >= 2 &&
+            !wait_bar(empty_bar + 8u * uint32_t(slot), ((cs.stage - 2) >> 1) & 1, tm, a)) {
+            ok = false;
+            break;
+        }
+        uint8_t *P = tm.T + C::OFF_PS + slot * C::PSLOT;
+        reinterpret_cast<float4 *>(P)[lane] = make_float4(p0v, p1v, p2v, p3v);
+        float *pf = reinterpret_cast<float *>(P + 512);
+        if (gi == 0) {
+            pf[2 * tig] = al0;
+            pf[2 * tig + 1] = al1;
+            if (cs.seg_end) {
                 pf[8 + 2 * tig] = m0;
                 pf[8 + 2 * tig + 1] = m1;
                 pf[16 + 2 * tig] = lt0;
                 pf[16 + 2 * tig + 1] = lt1;
             }
         }
-        if (gi == 0) {
-            pf[2 * tig] = al0;
-            pf[2 * tig + 1] = al1;
-        }
         __syncwarp();
         if (lane == 0) mbar_arrive(full_bar + 8u * uint32_t(slot));
-        end_m2 = end_m1;
-        last_m2 = last_m1;
-        end_m1 = st.at + st.size;
-        last_m1 = st.last_tile ? 1 : 0;
-        st.advance();
+        cs.advance(a);
     }
-
-    if (!ok && lane == 0) {
-        // bounded drain of the copies still in flight, then leave
-        for (int i = st.i; i < p_i; ++i)
-            mbar_wait_bounded(tile_bar<C::NB>(tm.bar0, i), (i / C::NB) & 1, a.wait_limit);
-        for (int j = st.jb; j < p_jb; ++j)
-            mbar_wait_bounded(meta_bar + 8u * uint32_t(j & 1), (j >> 1) & 1, a.wait_limit);
+    if (!ok) {
+        // bounded drain of this warp's copies still in flight
+        for (int i = cs.stage; i < pp.p_stage; ++i)
+            mbar_wait_bounded(pp.sbar + 8u * uint32_t(i % C::NSTAGE), (i / C::NSTAGE) & 1,
+                              a.wait_limit);
     }
 }
 
-// V-warp: rebuilds V, accumulates O += P V over the whole head dim, writes outputs or partials.
+// V-warp: streams and rebuilds V, accumulates O += P V over the whole head dim, writes outputs
+// or partial states.
 template <int D, bool BF16IN>
-__device__ __forceinline__ void v_warp(const AttnArgs &a, const Team &tm, int team, int64_t fb0,
-                                       int64_t fb1, int lane) {
+__device__ __forceinline__ void v_warp(const AttnArgs &a, const Team &tm, uint8_t *R, int team,
+                                       int64_t fb0, int64_t fb1, int lane) {
     using C = Cfg<D>;
-    uint8_t *ring = tm.T;
-    uint8_t *vt = tm.T + C::OFF_VT;
-    const uint32_t full_bar = tm.bar0 + 8u * C::NB + 16u;
-    const uint32_t empty_bar = full_bar + 16u;
+    const uint32_t full_bar = tm.bar0, empty_bar = tm.bar0 + 16u;
     const int gi = lane >> 2, tig = lane & 3;
-    Stream<D, BF16IN> st(fb0, fb1);
+    Pipe<D, BF16IN> pp;
+    pp.R = R;
+    pp.sbar = smem_u32(R + C::W_BAR);
+    pp.t = 1;
+    pp.pw.init(a, fb0, fb1);
+    Cursor<D, BF16IN> cs;
+    cs.init(a, fb0, fb1);
     uint32_t b7[4] = {0, 0, 0, 0};
     Esc es{0, 0, nullptr, nullptr};
+    uint8_t *vt = R + C::W_TILE;
     float acc[C::CH][4];  // rows gi: hi part, rows gi + 8: mid part of query gi
     const int mat = lane >> 3;
     const int r = (lane & 7) + 8 * (mat & 1);
     const int cadd = mat >> 1;
     const int sw = swz<D>(r);
     const uint32_t vrow = smem_u32(vt) + uint32_t(r * 2 * D);
+    bool ok = true;
 
-    while (st.fb < fb1) {
-        const int slot = st.i & 1;
-        if (st.tile == 0) {
-            if (!st.begin_block(tm, a, 1, lane, b7, es)) break;
-            if (st.fb == st.seg_begin) {
-#pragma unroll
-                for (int j = 0; j < C::CH; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
-            }
+    while (cs.cw.fb < fb1) {
+        pp.produce(a, cs.stage, cs.cw.fb, lane);
+        if (!wait_bar(pp.sbar + 8u * uint32_t(cs.stage % C::NSTAGE), (cs.stage / C::NSTAGE) & 1, tm,
+                      a)) {
+            ok = false;
+            break;
         }
-        if (!wait_bar(tile_bar<C::NB>(tm.bar0, st.i), (st.i / C::NB) & 1, tm, a)) break;
-        st.locate();
-        const uint8_t *base = ring + st.at % C::RING + st.ksz;
-        decode_tile<D>(vt, st.gv.mode, st.rows, base + st.vp[0].data,
-                       st.nv == 2 ? base + st.vp[0].alloc + st.vp[1].data : nullptr, b7, es,
-                       a.status, lane);
+        cs.setup(a, R, 1, lane, b7, es);
+        if (cs.first && cs.cw.fb == cs.seg_begin) {
+#pragma unroll
+            for (int j = 0; j < C::CH; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
+        }
+        const uint8_t *p0, *p1;
+        cs.data(R, p0, p1);
+        decode_tile<D>(vt, cs.g.mode, cs.rows, p0, p1, b7, es, a.status, lane);
         __syncwarp();
-        if (!wait_bar(full_bar + 8u * uint32_t(slot), (st.i >> 1) & 1, tm, a)) break;
+        const int slot = cs.stage & 1;
+        if (!wait_bar(full_bar + 8u * uint32_t(slot), (cs.stage >> 1) & 1, tm, a)) {
+            ok = false;
+            break;
+        }
         const uint8_t *P = tm.T + C::OFF_PS + slot * C::PSLOT;
-        const uint4 A = reinterpret_cast<const uint4 *>(P)[lane];
+        const float4 pv4 = reinterpret_cast<const float4 *>(P)[lane];
         const float *pf = reinterpret_cast<const float *>(P + 512);
+        // P^T tile (lane: tokens gi, gi+8 x queries 2tig, 2tig+1) -> P A-fragments: rows 0-7
+        // carry bf16(p), rows 8-15 bf16(p - bf16(p)), so P enters the MMA with 16 bits
+        uint4 A;
+        {
+            const uint32_t h01 = pack_bf16x2(pv4.y, pv4.x), h23 = pack_bf16x2(pv4.w, pv4.z);
+            const float r0 = __fsub_rn(pv4.x, bf16lo_to_f32(h01));
+            const float r1 = __fsub_rn(pv4.y, bf16hi_to_f32(h01));
+            const float r2 = __fsub_rn(pv4.z, bf16lo_to_f32(h23));
+            const float r3 = __fsub_rn(pv4.w, bf16hi_to_f32(h23));
+            const uint32_t mm01 = pack_bf16x2(r1, r0), mm23 = pack_bf16x2(r3, r2);
+            A = make_uint4(movm_t(h01), movm_t(mm01), movm_t(h23), movm_t(mm23));
+        }
         const float al = pf[gi];
         if (__any_sync(FULL, al != 1.0f)) {
 #pragma unroll
@@ -736,9 +709,9 @@ __device__ __forceinline__ void v_warp(const AttnArgs &a, const Team &tm, int te
             mma_bf16(acc[j + 1][0], acc[j + 1][1], acc[j + 1][2], acc[j + 1][3], A.x, A.y, A.z,
                      A.w, v2, v3);
         }
-        if (st.seg_end) {
-            const UnitDev &cu = st.cu;
-            if (st.whole_unit()) {
+        if (cs.seg_end) {
+            const UnitDev &cu = cs.cu;
+            if (cs.whole_unit()) {
                 if (gi < cu.n_q) {
                     const float inv = __frcp_rn(pf[16 + gi]);
                     float *o = cu.out + size_t(gi) * cu.q_stride;
@@ -749,7 +722,7 @@ __device__ __forceinline__ void v_warp(const AttnArgs &a, const Team &tm, int te
                     }
                 }
             } else {
-                const int ps = (st.seg_begin == fb0) ? 0 : 1;
+                const int ps = (cs.seg_begin == fb0) ? 0 : 1;
                 float *part = a.partials + (size_t(team) * 2 + ps) * partial_stride(D);
                 if (lane < 16) part[lane] = pf[8 + lane];  // m[8], l[8]
                 float *ac = part + 16 + gi * D;
@@ -762,7 +735,12 @@ __device__ __forceinline__ void v_warp(const AttnArgs &a, const Team &tm, int te
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(empty_bar + 8u * uint32_t(slot));
-        st.advance();
+        cs.advance(a);
+    }
+    if (!ok) {
+        for (int i = cs.stage; i < pp.p_stage; ++i)
+            mbar_wait_bounded(pp.sbar + 8u * uint32_t(i % C::NSTAGE), (i / C::NSTAGE) & 1,
+                              a.wait_limit);
     }
 }
 
@@ -771,7 +749,10 @@ __global__ void __launch_bounds__(64 * Cfg<D>::TEAMS, 1) attn_kernel(const AttnA
     using C = Cfg<D>;
     extern __shared__ __align__(128) uint8_t smem[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int tl = warp >> 1, w = warp & 1;
+    const int tl = warp >> 1;
+    // K-warp of team tl is warp 2*tl + ((tl >> 1) & 1): spreads the roles over all four SM
+    // sub-partitions (warp % 4).
+    const int w = (warp & 1) ^ ((tl >> 1) & 1);
     const int team = blockIdx.x * C::TEAMS + tl;
     if (team >= a.n_teams) return;
     const int64_t fb0 = a.team_begin[team], fb1 = a.team_begin[team + 1];
@@ -781,17 +762,23 @@ __global__ void __launch_bounds__(64 * Cfg<D>::TEAMS, 1) attn_kernel(const AttnA
     tm.T = smem + tl * C::TEAM;
     tm.bar0 = smem_u32(tm.T + C::OFF_BAR);
     tm.abort = reinterpret_cast<volatile int *>(tm.T + C::OFF_FLAG);
-    if (w == 0 && lane == 0) {
-        for (int i = 0; i < C::NBARS; ++i) mbar_init(tm.bar0 + 8 * i, 1);
-        *tm.abort = 0;
+    uint8_t *R = tm.T + w * C::WARP_BYTES;
+    if (lane == 0) {
+        // each warp initialises its own stage barriers (one arrival per lane); the K-warp the
+        // shared full / empty barriers
+        const uint32_t sbar = smem_u32(R + C::W_BAR);
+        for (int i = 0; i < C::NSTAGE; ++i) mbar_init(sbar + 8 * i, 32);
+        if (w == 0) {
+            for (int i = 0; i < 4; ++i) mbar_init(tm.bar0 + 8 * i, 1);
+            *tm.abort = 0;
+        }
         fence_mbar_init();
     }
     named_bar(tl + 1, 64);
-
     if (w == 0)
-        k_warp<D, BF16IN>(a, tm, team, fb0, fb1, lane);
+        k_warp<D, BF16IN>(a, tm, R, fb0, fb1, lane);
     else
-        v_warp<D, BF16IN>(a, tm, team, fb0, fb1, lane);
+        v_warp<D, BF16IN>(a, tm, R, team, fb0, fb1, lane);
 }
 
 // ---- combine ------------------------------------------------------------------------------------
