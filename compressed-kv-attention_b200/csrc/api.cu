@@ -52,14 +52,6 @@ const char *detail_message(int code, int detail) {
     }
 }
 
-uint32_t wait_limit_us() {
-    static uint32_t v = [] {
-        const char *e = std::getenv("KVX_WAIT_TIMEOUT_US");
-        long x = e ? std::atol(e) : 0;
-        return uint32_t(x > 0 ? x : 1000000);  // one second
-    }();
-    return v;
-}
 
 // RAII device buffer (stream-ordered allocator).
 struct DevBuf {
@@ -223,14 +215,14 @@ struct kvx_plan_s {
     bool bf16 = false;
     int n_units = 0;      // device units (query groups of <= 8)
     int64_t n_blocks = 0;
-    int n_teams = 0;
+    int n_workers = 0;
     int grid = 0;
     int n_split = 0;
     cudaStream_t s = nullptr;
     UnitDev *units = nullptr;
     FlatBlock *flat = nullptr;
     int32_t *flat_unit = nullptr;
-    int64_t *team_begin = nullptr;
+    int64_t *range_begin = nullptr;
     float *partials = nullptr;
     int32_t *split_units = nullptr;
     int *status = nullptr;
@@ -337,16 +329,16 @@ int kvx_plan_create(const kvx_unit *units, int n_units, int n_q, int dim, int bl
     p->bf16 = bf16;
     p->n_units = int(vu.size());
     p->n_blocks = total;
-    const int per_cta = attention_teams_per_cta(dim);
-    const int max_teams = sm_count() * per_cta;
-    p->n_teams = int(std::min<int64_t>(max_teams, total));
-    p->grid = (p->n_teams + per_cta - 1) / per_cta;
-    std::vector<int64_t> tb(size_t(p->n_teams) + 1);
-    for (int t = 0; t <= p->n_teams; ++t) tb[size_t(t)] = (int64_t)t * total / p->n_teams;
+    const int per_cta = attention_workers_per_cta(dim);
+    const int max_workers = sm_count() * per_cta;
+    p->n_workers = int(std::min<int64_t>(max_workers, total));
+    p->grid = (p->n_workers + per_cta - 1) / per_cta;
+    std::vector<int64_t> tb(size_t(p->n_workers) + 1);
+    for (int t = 0; t <= p->n_workers; ++t) tb[size_t(t)] = (int64_t)t * total / p->n_workers;
     std::vector<int32_t> split;
     for (int u = 0; u < p->n_units; ++u) {
-        const int t0 = team_of_block(tb.data(), p->n_teams, ud[size_t(u)].block_begin);
-        const int t1 = team_of_block(tb.data(), p->n_teams,
+        const int t0 = worker_of_block(tb.data(), p->n_workers, ud[size_t(u)].block_begin);
+        const int t1 = worker_of_block(tb.data(), p->n_workers,
                                      ud[size_t(u)].block_begin + ud[size_t(u)].n_blocks - 1);
         if (t0 != t1) split.push_back(u);
     }
@@ -357,8 +349,8 @@ int kvx_plan_create(const kvx_unit *units, int n_units, int n_q, int dim, int bl
     if ((e = plan_alloc(p, &p->units, ud.size())) != cudaSuccess ||
         (e = plan_alloc(p, &p->flat, size_t(total))) != cudaSuccess ||
         (e = plan_alloc(p, &p->flat_unit, size_t(total))) != cudaSuccess ||
-        (e = plan_alloc(p, &p->team_begin, tb.size())) != cudaSuccess ||
-        (e = plan_alloc(p, &p->partials, size_t(p->n_teams) * 2 * partial_stride(dim))) != cudaSuccess ||
+        (e = plan_alloc(p, &p->range_begin, tb.size())) != cudaSuccess ||
+        (e = plan_alloc(p, &p->partials, size_t(p->n_workers) * 2 * partial_stride(dim))) != cudaSuccess ||
         (e = plan_alloc(p, &p->split_units, split.size())) != cudaSuccess ||
         (e = plan_alloc(p, &p->status, 2)) != cudaSuccess ||
         (e = plan_alloc(p, &dvu, vu.size())) != cudaSuccess ||
@@ -367,7 +359,7 @@ int kvx_plan_create(const kvx_unit *units, int n_units, int n_q, int dim, int bl
         return fail(KVX_ERR_CUDA, std::string("kvx_plan_create: ") + cudaGetErrorString(e));
     }
     cudaMemcpy(p->units, ud.data(), ud.size() * sizeof(UnitDev), cudaMemcpyHostToDevice);
-    cudaMemcpy(p->team_begin, tb.data(), tb.size() * sizeof(int64_t), cudaMemcpyHostToDevice);
+    cudaMemcpy(p->range_begin, tb.data(), tb.size() * sizeof(int64_t), cudaMemcpyHostToDevice);
     if (!split.empty())
         cudaMemcpy(p->split_units, split.data(), split.size() * sizeof(int32_t),
                    cudaMemcpyHostToDevice);
@@ -403,9 +395,9 @@ int kvx_plan_run_part(kvx_plan p, int part, void *stream) {
             CombineArgs c{};
             c.units = p->units;
             c.split_units = p->split_units;
-            c.team_begin = p->team_begin;
+            c.range_begin = p->range_begin;
             c.partials = p->partials;
-            c.n_teams = p->n_teams;
+            c.n_workers = p->n_workers;
             KVX_CUDA(launch_combine(p->dim, c, p->n_split, s));
         }
         return KVX_OK;
@@ -415,12 +407,11 @@ int kvx_plan_run_part(kvx_plan p, int part, void *stream) {
     a.units = p->units;
     a.flat = p->flat;
     a.flat_unit = p->flat_unit;
-    a.team_begin = p->team_begin;
+    a.range_begin = p->range_begin;
     a.partials = p->partials;
     a.status = p->status;
-    a.n_teams = p->n_teams;
-    a.wait_limit = wait_limit_us();
-    KVX_CUDA(launch_attention(p->dim, p->bf16, a, p->grid, 0, s));
+    a.n_workers = p->n_workers;
+    KVX_CUDA(launch_attention(p->dim, p->bf16, a, p->grid, s));
     return KVX_OK;
 }
 

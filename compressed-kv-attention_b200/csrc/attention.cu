@@ -4,33 +4,36 @@
 // src/attention_{scalar,avx2,avx512}.cpp and the online softmax of src/softmax.hpp), restructured
 // for the GPU:
 //
-//  * The step's (unit, block) pairs are flattened; each team of two warps owns a contiguous range.
-//  * K-warp lane 0 streams the team's compressed tiles (16 tokens of K and V: sign/mantissa rows and
-//    packed exponent residuals, or raw rows) from HBM into a shared-memory byte ring with 1-D bulk
-//    async copies (TMA engine) completing on mbarriers; block bases and escape words go to two
-//    per-block meta slots.  Only the compressed bytes cross HBM.
-//  * The K-warp rebuilds the K tile as BF16 (exponent = base + residual, escapes patched in scan
-//    order), computes S^T = K Q^T on the tensor cores (mma.sync m16n8k16 bf16, fp32 accumulate,
-//    tokens as rows, the GQA group's queries as columns) and the online softmax, and hands P to the
-//    V-warp as ready MMA A-fragments (bf16 hi + mid parts, so P enters with 16 significant bits)
-//    together with the per-query rescale factors.
-//  * The V-warp rebuilds the V tile and accumulates O += P V for the whole head dimension.
-//  * The two warps synchronise only through mbarriers with bounded waits: a stuck wait ends the
-//    kernel with an error status instead of hanging.
-//  * Unit segments that span several teams leave (m, l, acc) partial states that combine_kernel
-//    folds in team order with merge_state semantics (src/softmax.hpp:16-30), then finalizes like
+//  * The step's (unit, block) pairs are flattened; each worker warp owns a contiguous range and
+//    streams the compressed 16-token tiles of K and V (sign/mantissa rows and packed exponent
+//    residuals, or raw BF16 rows) through its own shared-memory ring with cp.async, one cp.async
+//    group per tile.  A block's base exponents and escape words ride along with its first tile.
+//    Only the compressed bytes cross HBM, and no warp ever waits on another warp.
+//  * K rows are rebuilt straight into mma.sync A fragments: lane (g, t) rebuilds tokens g and g+8,
+//    head dims [t D/4, (t+1) D/4).  The MMA's k index runs over the head dims in that permuted
+//    order and the query B fragments use the same order, so S = K Q^T (tokens x queries, fp32
+//    accumulate) needs no shared-memory staging of a BF16 tile.
+//  * The online softmax runs on the S fragments: lane (g, t) holds queries 2t and 2t+1, which are
+//    also the output columns it accumulates, so the rescale factors never leave the lane.
+//  * V rows are rebuilt into A fragments of V^T: lane (g, t) rebuilds tokens 2t, 2t+1, 2t+8, 2t+9,
+//    head dims [g D/8, (g+1) D/8).  O^T += V^T P^T with P^T split into a bf16 part and a bf16
+//    residual part (two MMAs), so P enters with 16 significant bits.
+//  * Exponent escapes are patched in registers in the container's scan order (token-major); the
+//    lane order of both fragment layouts gives each sentinel its rank with a few warp ballots.
+//  * Unit segments that span several workers leave (m, l, acc) partial states that combine_kernel
+//    folds in worker order with merge_state semantics (src/softmax.hpp:16-30), then finalizes like
 //    finalize_state (src/softmax.hpp:32-41: reciprocal, then multiply).
 //
-// The BF16-input variant (BF16IN) is the same template with a loader that reads [seq, dim] BF16
-// rows; for the same blocks it produces bit-identical outputs to the XKV variant, because both
-// rebuild identical BF16 tiles and run identical arithmetic afterwards.
+// The BF16-input variant (BF16IN) is the same template reading [seq, dim] BF16 rows; for the same
+// blocks it produces bit-identical outputs to the XKV variant, because both rebuild identical BF16
+// fragments and run identical arithmetic afterwards.
 #include "attention.cuh"
 
 namespace kvx {
 namespace {
 
 constexpr uint32_t FULL = 0xFFFFFFFFu;
-constexpr int TT = 16;  // tokens per tile (one m16 row block of the QK MMA)
+constexpr int TT = 16;  // tokens per tile (one m16 block of the QK MMA)
 constexpr float kLog2e = 1.4426950408889634f;
 
 // 2^x by the SFU (ex2.approx.f32, subnormal results kept).
@@ -41,37 +44,40 @@ __device__ __forceinline__ float ex2(float x) {
 }
 
 __host__ __device__ constexpr int round16(int x) { return (x + 15) & ~15; }
+__host__ __device__ constexpr int cmin(int a, int b) { return a < b ? a : b; }
+__host__ __device__ constexpr int cmax(int a, int b) { return a > b ? a : b; }
+
+#ifndef KVX_NSTAGE64
+#define KVX_NSTAGE64 3
+#endif
+#ifndef KVX_MAXWARPS
+#define KVX_MAXWARPS 12
+#endif
 
 template <int D> struct Cfg {
-    static constexpr int CH = D / 8;          // 16-byte chunks per BF16 row
-    static constexpr int STEPS = D / 16;      // 256-element warp steps per 16-row tile
-    static constexpr int ESC_CAP = 1536;      // escape bytes staged per block and tensor
-    static constexpr int SLOT = 32 * D + 32;  // one tensor tile: raw rows, or sm + residual rows
-    static constexpr int NSTAGE = D <= 64 ? 4 : 3;
-    static constexpr int BASE_SLOT = round16(D + 32);
-    static constexpr int MSLOT = BASE_SLOT + ESC_CAP + 32;  // base + escapes of one block
-    static constexpr int TILE = TT * D * 2;                  // bytes of one BF16 tile
-    static constexpr int PSLOT = 640;                        // p values + alpha + m + l
-    // per-warp region: ring | meta x2 | BF16 tile | stage barriers
-    static constexpr int W_META = NSTAGE * SLOT;
-    static constexpr int W_TILE = W_META + 2 * MSLOT;
-    static constexpr int W_BAR = W_TILE + TILE;
-    static constexpr int WARP_BYTES = (W_BAR + NSTAGE * 8 + 127) & ~127;
-    // team: K-warp region | V-warp region | P slots x2 | full x2, empty x2 | abort flag
-    static constexpr int OFF_PS = 2 * WARP_BYTES;
-    static constexpr int OFF_BAR = OFF_PS + 2 * PSLOT;
-    static constexpr int OFF_FLAG = OFF_BAR + 4 * 8;
-    static constexpr int TEAM = (OFF_FLAG + 16 + 127) & ~127;
-    static constexpr int BY_SMEM = 232448 / TEAM;
-    static constexpr int TEAMS = BY_SMEM < 8 ? BY_SMEM : 8;
-    static_assert(TEAMS >= 1, "team does not fit in shared memory");
+    static constexpr int DK = D / 4;        // head dims per lane in a K row
+    static constexpr int NK = D / 8;        // K fragment registers per row (dim pairs)
+    static constexpr int DV = D / 8;        // head dims per lane in a V token (= V registers)
+    static constexpr int KS = D / 16;       // k-steps of QK = M-tiles of PV
+    static constexpr int NMK = cmax(1, DK / 8);  // sentinel mask words per K row
+    static constexpr int NMV = cmax(1, DV / 8);  // sentinel mask words per V token
+    static constexpr bool SPLIT = D > 128;  // rebuild row halves one at a time (register budget)
+    static constexpr bool B7REG = D <= 128; // keep the block's base exponents in registers
+    static constexpr int ESC_CAP = 1536;    // escape bytes staged per block and tensor
+    static constexpr int TR = 2 * TT * D + 32;    // one tensor tile: raw rows or sm + codes rows
+    static constexpr int CODE_OFF = TT * D + 16;  // residual-code rows inside a coded tensor tile
+    static constexpr int SLOT = 2 * TR;           // K tile | V tile
+    static constexpr int NSTAGE = D <= 32 ? 4 : D == 64 ? KVX_NSTAGE64 : D == 128 ? 3 : 2;
+    static_assert(NSTAGE >= 2 && NSTAGE <= 4, "stage waits cover at most 3 younger groups");
+    static constexpr int BASE = round16(D + 32);  // one block's base exponents (+ alignment slack)
+    static constexpr int ESCB = ESC_CAP + 32;
+    static constexpr int M_K = 0, M_V = BASE, M_EK = 2 * BASE, M_EV = 2 * BASE + ESCB;
+    static constexpr int MSLOT = 2 * BASE + 2 * ESCB;
+    static constexpr int W_META = NSTAGE * SLOT;  // per-warp region: ring | meta x2
+    static constexpr int WARP_BYTES = (W_META + 2 * MSLOT + 127) & ~127;
+    static constexpr int WARPS = cmin(KVX_MAXWARPS, 232448 / WARP_BYTES);
+    static_assert(WARPS >= 1, "worker does not fit in shared memory");
 };
-
-// Swizzle of 16-byte chunks inside a BF16 tile row, so that ldmatrix row reads and the decoder's
-// 16-byte stores hit distinct bank groups.
-template <int D> __device__ __forceinline__ int swz(int row) {
-    return D >= 64 ? (row & 7) : ((row >> 1) & 3);
-}
 
 __device__ __forceinline__ FlatBlock load_flat(const FlatBlock *f, int64_t i) {
     const uint4 r = __ldg(reinterpret_cast<const uint4 *>(f) + i);
@@ -87,7 +93,7 @@ __device__ __forceinline__ FlatBlock load_flat(const FlatBlock *f, int64_t i) {
     return b;
 }
 
-// ---- tile geometry ----------------------------------------------------------------------------
+// ---- copies ------------------------------------------------------------------------------------
 
 struct Piece {
     const uint8_t *src;  // 16-byte aligned source
@@ -102,266 +108,526 @@ __device__ __forceinline__ Piece make_piece(const uint8_t *p, uint32_t len) {
     return Piece{reinterpret_cast<const uint8_t *>(lo), uint32_t(hi - lo), uint32_t(a - lo)};
 }
 
-// One tensor of one block: where its sections start.
-struct Geo {
-    const uint8_t *s0;  // sign/mantissa rows (coded) or BF16 rows (raw)
-    const uint8_t *s1;  // packed residual rows (coded)
-    int mode;           // 0 raw, 2, 4
-};
-
-template <int D, bool BF16IN>
-__device__ __forceinline__ Geo make_geo(const uint8_t *blob, uint32_t off, int mode, int n_tok) {
-    Geo g;
-    if (BF16IN) {
-        g.s0 = blob + size_t(off) * (2 * D);
-        g.s1 = nullptr;
-        g.mode = 0;
-        return g;
-    }
-    const uint8_t *b = blob + off + kHeaderBytes;
-    g.mode = mode;
-    if (mode == 0) {
-        g.s0 = b;
-        g.s1 = nullptr;
-    } else {
-        g.s0 = b + D;
-        g.s1 = b + D + size_t(n_tok) * D;
-    }
-    return g;
-}
-
-// Pieces of one tensor's tile `tile` (rows rows): [0] sm or raw rows, [1] residual rows.
-template <int D>
-__device__ __forceinline__ int geo_pieces(const Geo &g, int tile, int rows, Piece (&pc)[2]) {
-    const int t0 = tile * TT;
-    if (g.mode == 0) {
-        pc[0] = make_piece(g.s0 + t0 * (2 * D), uint32_t(rows * 2 * D));
-        return 1;
-    }
-    pc[0] = make_piece(g.s0 + t0 * D, uint32_t(rows * D));
-    pc[1] = make_piece(g.s1 + t0 * D * g.mode / 8, uint32_t(rows * D * g.mode / 8));
-    return 2;
-}
-
-// Ring placement: a tile never wraps; it starts at 0 when it does not fit before the end.
-template <int RING> __device__ __forceinline__ uint32_t place(uint32_t pos, uint32_t size) {
-    return (pos % RING) + size > uint32_t(RING) ? pos + (RING - pos % RING) : pos;
-}
-
-// ---- decode of one tensor tile into a swizzled BF16 tile ---------------------------------------
-
-// Exponent/sign merge per 16-bit half: sign and mantissa from the sign-replicated sm byte pair,
-// exponent bits from (code + base) << 7.  The bit-select drops the carry out of bit 14, so the
-// exponent wraps modulo 256 exactly like bf16_from_delta's uint8 sum (include/kvexp/bf16.hpp:35-37).
-__device__ __forceinline__ uint32_t merge(uint32_t sg, uint32_t code_pair, uint32_t b7) {
-    const uint32_t e = code_pair * 128u + b7;
-    return (sg & 0x807F807Fu) | (e & 0x7F807F80u);
-}
-
-// Sign-replicating byte pairs of element i (from S0) and i + 4 (from S1).
-__device__ __forceinline__ uint32_t sm_pair(uint32_t s0, uint32_t s1, int i) {
-    const uint32_t sel = uint32_t(i) | (uint32_t(i | 8) << 4) | (uint32_t(4 + i) << 8) |
-                         (uint32_t((4 + i) | 8) << 12);
-    return prmt(s0, s1, sel);
-}
-
-struct Esc {
-    uint32_t run;        // escapes consumed so far in this block
-    uint32_t n;          // escape words in this block
-    const uint8_t *sm;   // staged escape words in shared memory (nullptr: read global)
-    const uint8_t *gm;   // escape words in global memory
-};
-
-__device__ __forceinline__ uint32_t esc_word(uint32_t r, uint32_t n, const uint8_t *sm,
-                                             const uint8_t *gm, int *status) {
-    if (r >= n) {
-        report(status, KVX_ERR_RUNTIME, DERR_ESC_OVERRUN);
-        return 0;
-    }
-    return sm != nullptr ? *reinterpret_cast<const uint16_t *>(sm + 2 * r)
-                         : __ldg(reinterpret_cast<const unsigned short *>(gm) + r);
-}
-
-// General case of escape patching (some lane holds two or more sentinels).  Sentinel elements
-// take the next escape words in scan order: lane order inside the 256-element step, element
-// order inside the lane.  Element k of a lane sits at half (k >> 2) of 32-bit word (k & 3) of the
-// lane's 16-byte tile chunk.  Returns the new running escape count.
-template <int SH>
-__device__ __noinline__ uint32_t patch_general(uint8_t *chunk, uint32_t m, uint32_t run, uint32_t n,
-                                               const uint8_t *sm, const uint8_t *gm, int *status) {
-    const uint32_t cnt = __popc(m);
-    const uint32_t lt = lanemask_lt();
-    const uint32_t c0 = __ballot_sync(FULL, cnt & 1u), c1 = __ballot_sync(FULL, cnt & 2u);
-    const uint32_t c2 = __ballot_sync(FULL, cnt & 4u), c3 = __ballot_sync(FULL, cnt & 8u);
-    uint32_t r = run + __popc(c0 & lt) + 2 * __popc(c1 & lt) + 4 * __popc(c2 & lt) +
-                 8 * __popc(c3 & lt);
-    const uint32_t tot = __popc(c0) + 2 * __popc(c1) + 4 * __popc(c2) + 8 * __popc(c3);
-    while (m != 0u) {
-        const int k = (__ffs(m) - 1) / SH;
-        m &= m - 1u;
-        *reinterpret_cast<uint16_t *>(chunk + 4 * (k & 3) + 2 * (k >> 2)) =
-            uint16_t(esc_word(r, n, sm, gm, status));
-        ++r;
-    }
-    return run + tot;
-}
-
-// Escape patching for one 256-element step: fast path when every lane holds at most one sentinel.
-template <int SH>
-__device__ __forceinline__ void patch(uint8_t *chunk, uint32_t m, Esc &es, int *status) {
-    const uint32_t has = __ballot_sync(FULL, m != 0u);
-    if (has == 0u) return;
-    if (__ballot_sync(FULL, (m & (m - 1u)) != 0u) == 0u) {
-        if (m != 0u) {
-            const uint32_t r = es.run + __popc(has & lanemask_lt());
-            const int k = (__ffs(m) - 1) / SH;
-            *reinterpret_cast<uint16_t *>(chunk + 4 * (k & 3) + 2 * (k >> 2)) =
-                uint16_t(esc_word(r, es.n, es.sm, es.gm, status));
-        }
-        es.run += __popc(has);
-    } else {
-        es.run = patch_general<SH>(chunk, m, es.run, es.n, es.sm, es.gm, status);
-    }
-}
-
-template <bool MIS> __device__ __forceinline__ uint32_t ldw2(const uint8_t *p) {
-    if (!MIS) return *reinterpret_cast<const uint32_t *>(p);
-    const uint32_t *q = reinterpret_cast<const uint32_t *>(p - 2);
-    return prmt(q[0], q[1], 0x5432);
-}
-
-template <int D, bool MIS>
-__device__ __forceinline__ void decode_tile_t(uint8_t *tile, int mode, int rows, const uint8_t *p0,
-                                              const uint8_t *p1, const uint32_t (&b7)[4], Esc &es,
-                                              int *status, int lane) {
-    constexpr int CH = Cfg<D>::CH;
-    const int ch = lane % CH;
-#pragma unroll 1
-    for (int c = 0; c < Cfg<D>::STEPS; ++c) {
-        const int e0 = 256 * c + 8 * lane;
-        const int row = e0 / D;
-        uint32_t bf0 = 0, bf1 = 0, bf2 = 0, bf3 = 0;
-        uint32_t m = 0;
-        if (row < rows) {
-            if (mode == 0) {
-                const uint8_t *p = p0 + 2 * e0;
-                const uint32_t w0 = ldw2<MIS>(p), w1 = ldw2<MIS>(p + 4);
-                const uint32_t w2 = ldw2<MIS>(p + 8), w3 = ldw2<MIS>(p + 12);
-                bf0 = prmt(w0, w2, 0x5410);
-                bf1 = prmt(w0, w2, 0x7632);
-                bf2 = prmt(w1, w3, 0x5410);
-                bf3 = prmt(w1, w3, 0x7632);
-            } else {
-                const uint32_t S0 = ldw2<MIS>(p0 + e0), S1 = ldw2<MIS>(p0 + e0 + 4);
-                uint32_t X, sh, mask;
-                if (mode == 4) {
-                    X = ldw2<MIS>(p1 + e0 / 2);  // element k at bits 4k
-                    uint32_t t = X & (X >> 1);
-                    t &= t >> 2;
-                    m = t & 0x11111111u;
-                    sh = 4;
-                    mask = 0x000F000Fu;
-                } else {
-                    const uint32_t C = *reinterpret_cast<const uint16_t *>(p1 + e0 / 4);
-                    m = C & (C >> 1) & 0x5555u;   // element k at bits 2k
-                    X = prmt(C, 0, 0x0110);       // elements 4..7 up to bits 16..23
-                    sh = 2;
-                    mask = 0x00030003u;
-                }
-                bf0 = merge(sm_pair(S0, S1, 0), X & mask, b7[0]);
-                bf1 = merge(sm_pair(S0, S1, 1), (X >> sh) & mask, b7[1]);
-                bf2 = merge(sm_pair(S0, S1, 2), (X >> (2 * sh)) & mask, b7[2]);
-                bf3 = merge(sm_pair(S0, S1, 3), (X >> (3 * sh)) & mask, b7[3]);
-            }
-        }
-        uint8_t *dst = tile + row * (2 * D) + 16 * (ch ^ swz<D>(row));
-        *reinterpret_cast<uint4 *>(dst) = make_uint4(bf0, bf1, bf2, bf3);
-        if (mode == 4) patch<4>(dst, m, es, status);
-        else if (mode == 2) patch<2>(dst, m, es, status);
-    }
-}
-
-template <int D>
-__device__ __forceinline__ void decode_tile(uint8_t *tile, int mode, int rows, const uint8_t *p0,
-                                            const uint8_t *p1, const uint32_t (&b7)[4], Esc &es,
-                                            int *status, int lane) {
-    if (reinterpret_cast<uintptr_t>(p0) & 2u)
-        decode_tile_t<D, true>(tile, mode, rows, p0, p1, b7, es, status, lane);
-    else
-        decode_tile_t<D, false>(tile, mode, rows, p0, p1, b7, es, status, lane);
-}
-
-// b7[i] = (base[d0+i] << 7) | (base[d0+i+4] << 23)
-__device__ __forceinline__ void load_base(const uint8_t *p, uint32_t (&b7)[4]) {
-    const bool mis = (reinterpret_cast<uintptr_t>(p) & 2u) != 0u;
-    const uint32_t B0 = mis ? ldw2<true>(p) : ldw2<false>(p);
-    const uint32_t B1 = mis ? ldw2<true>(p + 4) : ldw2<false>(p + 4);
-#pragma unroll
-    for (int i = 0; i < 4; ++i)
-        b7[i] = (prmt(B0, B1, uint32_t(i) | (uint32_t(4 + i) << 8)) & 0x00FF00FFu) << 7;
-}
-
-// Q B-fragments of the QK MMA: qb[s][0] = (Q[gi][16s+tig], Q[gi][16s+4+tig]),
-// qb[s][1] = (Q[gi][16s+8+tig], Q[gi][16s+12+tig]) -- the column order the decoder stores:
-// 16-byte chunk c of a BF16 tile row holds dims 8c + {0,4,1,5,2,6,3,7}.
-template <int D>
-__device__ __forceinline__ void load_q_frags(const uint16_t *q, int n_q, int stride,
-                                             uint32_t (&qb)[D / 16][2], int lane) {
-    const int gi = lane >> 2, tig = lane & 3;
-#pragma unroll
-    for (int s = 0; s < D / 16; ++s) {
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-            uint32_t v = 0;
-            if (gi < n_q) {
-                const uint16_t *row = q + size_t(gi) * stride + 16 * s + 8 * h + tig;
-                v = uint32_t(__ldg(reinterpret_cast<const unsigned short *>(row))) |
-                    (uint32_t(__ldg(reinterpret_cast<const unsigned short *>(row + 4))) << 16);
-            }
-            qb[s][h] = v;
-        }
-    }
-}
-
-// ---- the kernel -------------------------------------------------------------------------------
-
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void *src) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
 }
-// Arrive on `bar` once every cp.async this thread issued so far has landed.
-__device__ __forceinline__ void cp_async_arrive(uint32_t bar) {
-    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(bar) : "memory");
+// One cp.async group per ring stage; a consumer waits until at most `younger` groups issued after
+// the stage it needs are still in flight.  These waits end by themselves: they wait for this
+// thread's own copies only.
+__device__ __forceinline__ void cp_async_commit() {
+    asm volatile("cp.async.commit_group;" ::: "memory");
+}
+__device__ __forceinline__ void cp_async_wait(int younger) {
+    switch (younger) {
+    case 0: asm volatile("cp.async.wait_group 0;" ::: "memory"); break;
+    case 1: asm volatile("cp.async.wait_group 1;" ::: "memory"); break;
+    case 2: asm volatile("cp.async.wait_group 2;" ::: "memory"); break;
+    default: asm volatile("cp.async.wait_group 3;" ::: "memory"); break;
+    }
 }
 // The warp copies one piece: lane l moves 16-byte chunks l, l + 32, ...
-__device__ __forceinline__ void copy_piece(uint32_t dst, const Piece &p, int lane) {
+__device__ __forceinline__ void copy_piece(uint8_t *dst, const Piece &p, int lane) {
+    const uint32_t d = smem_u32(dst);
     const uint32_t n = p.alloc >> 4;
-    for (uint32_t j = lane; j < n; j += 32) cp_async16(dst + 16 * j, p.src + 16 * j);
+    for (uint32_t j = lane; j < n; j += 32) cp_async16(d + 16 * j, p.src + 16 * j);
 }
 
-struct Team {
-    uint8_t *T;
-    uint32_t bar0;  // full x2, empty x2
-    volatile int *abort;
+// Section pointers of one tensor of one block.
+struct Sections {
+    const uint8_t *rows;   // coded: sign/mantissa rows; raw / BF16: BF16 rows
+    const uint8_t *codes;  // coded: packed residual codes
+    const uint8_t *esc;    // coded: escape words
 };
 
-// Bounded wait that also gives up when the partner warp aborted.
-__device__ __forceinline__ bool wait_bar(uint32_t bar, uint32_t parity, const Team &t,
-                                         const AttnArgs &a) {
-    if (mbar_try_wait(bar, parity)) return true;
-    const uint64_t t0 = global_ns();
-    const uint64_t lim = uint64_t(a.wait_limit) * 1000ull;
-    while (!mbar_try_wait(bar, parity)) {
-        if (*t.abort) return false;
-        if (global_ns() - t0 > lim) {
-            *t.abort = 1;
-            report(a.status, KVX_ERR_TIMEOUT, DERR_TIMEOUT);
-            return false;
-        }
+template <int D, bool BF16IN>
+__device__ __forceinline__ Sections sections(const uint8_t *blob, uint32_t off, int mode, int n_tok) {
+    Sections s;
+    if (BF16IN) {
+        s.rows = blob + size_t(off) * (2 * D);
+        s.codes = s.esc = nullptr;
+    } else if (mode == 0) {
+        s.rows = blob + off + kHeaderBytes;
+        s.codes = s.esc = nullptr;
+    } else {
+        s.rows = blob + off + kHeaderBytes + D;
+        s.codes = s.rows + size_t(n_tok) * D;
+        s.esc = s.codes + size_t(n_tok) * D * mode / 8;
     }
-    return true;
+    return s;
 }
 
-// Walks the team's flat blocks with one block of prefetch.
+// Whether a block's escape words fit its meta slot (producer and consumer agree on this).
+template <int D> __device__ __forceinline__ bool esc_staged(const Piece &e, int nesc) {
+    return nesc > 0 && e.alloc <= uint32_t(Cfg<D>::ESCB);
+}
+
+// ---- decode helpers ----------------------------------------------------------------------------
+
+// NW 32-bit words of shared memory starting at any byte address (byte 0 in bits 0-7 of w[0]).
+template <int NW> __device__ __forceinline__ void lds_words(const uint8_t *p, uint32_t (&w)[NW]) {
+    const uintptr_t a = reinterpret_cast<uintptr_t>(p);
+    const uint32_t *q = reinterpret_cast<const uint32_t *>(a & ~uintptr_t(3));
+    const uint32_t sh = uint32_t(a & 3u) * 8u;
+    uint32_t x[NW + 1];
+#pragma unroll
+    for (int i = 0; i <= NW; ++i) x[i] = q[i];
+#pragma unroll
+    for (int i = 0; i < NW; ++i) w[i] = __funnelshift_r(x[i], x[i + 1], sh);
+}
+
+__host__ __device__ constexpr uint32_t sel_pair(int j) {  // bytes j, j+1 of A with sign bytes
+    return uint32_t(j) | (uint32_t(j | 8) << 4) | (uint32_t(j + 1) << 8) | (uint32_t((j + 1) | 8) << 12);
+}
+__host__ __device__ constexpr uint32_t sel_cross(int b) {  // byte b of A and of B with sign bytes
+    return uint32_t(b) | (uint32_t(b | 8) << 4) | (uint32_t(4 + b) << 8) | (uint32_t((4 + b) | 8) << 12);
+}
+__host__ __device__ constexpr uint32_t sel_code(int j) {  // byte j of A -> bits 0-7, of B -> 16-23
+    return uint32_t(j) | (uint32_t(j) << 4) | (uint32_t(4 + j) << 8) | (uint32_t(4 + j) << 12);
+}
+__host__ __device__ constexpr uint32_t low_bytes(int nb) {
+    return nb >= 4 ? 0xFFFFFFFFu : (1u << (8 * nb)) - 1u;
+}
+
+// Two BF16 values from a sign-replicated sm pair and a code pair (codes in bits 0-3 and 16-19;
+// the other bytes of cw hold small codes that the masks drop).  Exponent = base + code modulo 256
+// like bf16_from_delta's uint8 sum (include/kvexp/bf16.hpp:35-37 of the reference): the carry out
+// of bit 14 is masked away.
+__device__ __forceinline__ uint32_t merge(uint32_t sg, uint32_t cw, uint32_t b7) {
+    const uint32_t e = cw * 128u + b7;
+    return (sg & 0x807F807Fu) | (e & 0x7F807F80u);
+}
+
+__device__ __forceinline__ uint32_t sent4(uint32_t x) {  // nibble == 15 -> bit 4k
+    uint32_t t = x & (x >> 1);
+    t &= t >> 2;
+    return t & 0x11111111u;
+}
+__device__ __forceinline__ uint32_t sent2(uint32_t x) {  // 2-bit code == 3 -> bit 2k
+    return x & (x >> 1) & 0x55555555u;
+}
+
+// b7 of a K register (dims d, d+1): base[d] << 7 | base[d+1] << 23; of a V register (one dim,
+// two tokens): base[d] << 7 | base[d] << 23.
+template <int D>
+__device__ __forceinline__ void load_b7k(const uint8_t *base, uint32_t (&b7)[Cfg<D>::NK]) {
+    uint32_t B[Cfg<D>::DK / 4];
+    lds_words<Cfg<D>::DK / 4>(base, B);
+#pragma unroll
+    for (int p = 0; p < Cfg<D>::NK; ++p) {
+        const int j = 2 * (p & 1);
+        b7[p] = prmt(B[p >> 1], 0u, uint32_t(j) | (4u << 4) | (uint32_t(j + 1) << 8) | (4u << 12)) << 7;
+    }
+}
+template <int D>
+__device__ __forceinline__ void load_b7v(const uint8_t *base, uint32_t (&b7)[Cfg<D>::DV]) {
+    uint32_t B[Cfg<D>::DV / 4];
+    lds_words<Cfg<D>::DV / 4>(base, B);
+#pragma unroll
+    for (int e = 0; e < Cfg<D>::DV; ++e) {
+        const int j = e & 3;
+        b7[e] = prmt(B[e >> 2], 0u, uint32_t(j) | (4u << 4) | (uint32_t(j) << 8) | (4u << 12)) << 7;
+    }
+}
+
+// One K row of this lane (DK dims): NK registers of BF16 pairs, and the row's sentinel masks.
+template <int D, int MODE>
+__device__ __forceinline__ void dec_k(const uint8_t *rp, const uint8_t *cp,
+                                      const uint32_t (&b7)[Cfg<D>::NK], uint32_t (&o)[Cfg<D>::NK],
+                                      uint32_t (&mk)[Cfg<D>::NMK]) {
+    using C = Cfg<D>;
+#pragma unroll
+    for (int i = 0; i < C::NMK; ++i) mk[i] = 0u;
+    if (MODE == 0) {
+        lds_words<C::NK>(rp, o);
+        return;
+    }
+    uint32_t S[C::DK / 4];
+    lds_words<C::DK / 4>(rp, S);
+    if (MODE == 4) {
+        constexpr int NW = C::DK / 8;
+        uint32_t N[NW], NL[NW], NH[NW];
+        lds_words<NW>(cp, N);
+#pragma unroll
+        for (int i = 0; i < NW; ++i) {
+            NL[i] = N[i] & 0x0F0F0F0Fu;
+            NH[i] = (N[i] >> 4) & 0x0F0F0F0Fu;
+            mk[i] = sent4(N[i]);
+        }
+#pragma unroll
+        for (int p = 0; p < C::NK; ++p) {
+            const uint32_t sg = prmt(S[p >> 1], 0u, sel_pair(2 * (p & 1)));
+            const uint32_t cw = prmt(NL[p >> 2], NH[p >> 2], sel_code(p & 3));
+            o[p] = merge(sg, cw, b7[p]);
+        }
+    } else {
+        constexpr int NB = C::DK / 4;
+        constexpr int NW = (NB + 3) / 4;
+        uint32_t W[NW], Ck[4][NW];
+        lds_words<NW>(cp, W);
+#pragma unroll
+        for (int i = 0; i < NW; ++i) {
+            mk[i] = sent2(W[i]) & low_bytes(NB);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) Ck[k][i] = (W[i] >> (2 * k)) & 0x03030303u;
+        }
+#pragma unroll
+        for (int p = 0; p < C::NK; ++p) {
+            const int e = 2 * p, i = e >> 4, j = (e & 15) >> 2, k = e & 3;
+            const uint32_t sg = prmt(S[p >> 1], 0u, sel_pair(2 * (p & 1)));
+            const uint32_t cw = prmt(Ck[k][i], Ck[k + 1][i], sel_code(j));
+            o[p] = merge(sg, cw, b7[p]);
+        }
+    }
+}
+
+// Two V tokens (A -> low halves, B -> high halves) of this lane (DV dims): DV registers, one per
+// dim, and the tokens' sentinel masks.
+template <int D, int MODE>
+__device__ __forceinline__ void dec_v(const uint8_t *ra, const uint8_t *rb, const uint8_t *ca,
+                                      const uint8_t *cb, const uint32_t (&b7)[Cfg<D>::DV],
+                                      uint32_t (&o)[Cfg<D>::DV], uint32_t (&ma)[Cfg<D>::NMV],
+                                      uint32_t (&mb)[Cfg<D>::NMV]) {
+    using C = Cfg<D>;
+#pragma unroll
+    for (int i = 0; i < C::NMV; ++i) ma[i] = mb[i] = 0u;
+    if (MODE == 0) {
+        uint32_t RA[C::DV / 2], RB[C::DV / 2];
+        lds_words<C::DV / 2>(ra, RA);
+        lds_words<C::DV / 2>(rb, RB);
+#pragma unroll
+        for (int e = 0; e < C::DV; ++e) o[e] = prmt(RA[e >> 1], RB[e >> 1], (e & 1) ? 0x7632u : 0x5410u);
+        return;
+    }
+    uint32_t SA[C::DV / 4], SB[C::DV / 4];
+    lds_words<C::DV / 4>(ra, SA);
+    lds_words<C::DV / 4>(rb, SB);
+    if (MODE == 4) {
+        constexpr int NB = C::DV / 2;
+        constexpr int NW = (NB + 3) / 4;
+        uint32_t NA[NW], NBw[NW], LA[NW], HA[NW], LB[NW], HB[NW];
+        lds_words<NW>(ca, NA);
+        lds_words<NW>(cb, NBw);
+#pragma unroll
+        for (int i = 0; i < NW; ++i) {
+            LA[i] = NA[i] & 0x0F0F0F0Fu;
+            HA[i] = (NA[i] >> 4) & 0x0F0F0F0Fu;
+            LB[i] = NBw[i] & 0x0F0F0F0Fu;
+            HB[i] = (NBw[i] >> 4) & 0x0F0F0F0Fu;
+            ma[i] = sent4(NA[i]) & low_bytes(NB);
+            mb[i] = sent4(NBw[i]) & low_bytes(NB);
+        }
+#pragma unroll
+        for (int e = 0; e < C::DV; ++e) {
+            const int i = e >> 3, j = (e & 7) >> 1;
+            const uint32_t sg = prmt(SA[e >> 2], SB[e >> 2], sel_cross(e & 3));
+            const uint32_t cw = (e & 1) ? prmt(HA[i], HB[i], sel_code(j)) : prmt(LA[i], LB[i], sel_code(j));
+            o[e] = merge(sg, cw, b7[e]);
+        }
+    } else {
+        constexpr int NB = C::DV / 4;
+        constexpr int NW = (NB + 3) / 4;
+        uint32_t WA[NW], WB[NW], CA[4][NW], CB[4][NW];
+        lds_words<NW>(ca, WA);
+        lds_words<NW>(cb, WB);
+#pragma unroll
+        for (int i = 0; i < NW; ++i) {
+            ma[i] = sent2(WA[i]) & low_bytes(NB);
+            mb[i] = sent2(WB[i]) & low_bytes(NB);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                CA[k][i] = (WA[i] >> (2 * k)) & 0x03030303u;
+                CB[k][i] = (WB[i] >> (2 * k)) & 0x03030303u;
+            }
+        }
+#pragma unroll
+        for (int e = 0; e < C::DV; ++e) {
+            const int i = e >> 4, j = (e & 15) >> 2, k = e & 3;
+            const uint32_t sg = prmt(SA[e >> 2], SB[e >> 2], sel_cross(e & 3));
+            const uint32_t cw = prmt(CA[k][i], CB[k][i], sel_code(j));
+            o[e] = merge(sg, cw, b7[e]);
+        }
+    }
+}
+
+// ---- escapes -----------------------------------------------------------------------------------
+
+struct Esc {
+    uint32_t run;               // escapes consumed so far in this block
+    uint32_t n;                 // escape words in this block
+    const uint8_t *sm;          // staged escape words (shared memory), or nullptr
+    const unsigned short *gm;   // escape words in global memory
+};
+
+__device__ __forceinline__ uint32_t esc_word(uint32_t r, const Esc &es, int *status) {
+    if (r >= es.n) {
+        report(status, KVX_ERR_RUNTIME, DERR_ESC_OVERRUN);
+        return 0u;
+    }
+    return es.sm != nullptr ? uint32_t(*reinterpret_cast<const uint16_t *>(es.sm + 2 * r))
+                            : uint32_t(__ldg(es.gm + r));
+}
+
+// Replace the low (hi = 0) or high half of register idx.
+template <int N>
+__device__ __forceinline__ void put_half(uint32_t (&o)[N], int idx, int hi, uint32_t v) {
+    const uint32_t keep = hi ? 0x0000FFFFu : 0xFFFF0000u;
+    const uint32_t val = hi ? (v << 16) : (v & 0xFFFFu);
+#pragma unroll
+    for (int i = 0; i < N; ++i)
+        if (i == idx) o[i] = (o[i] & keep) | val;
+}
+
+template <int N> __device__ __forceinline__ uint32_t count_bits(const uint32_t (&m)[N]) {
+    uint32_t c = 0;
+#pragma unroll
+    for (int i = 0; i < N; ++i) c += __popc(m[i]);
+    return c;
+}
+
+// Sentinels of one K row half (rows 0-7 or 8-15 of the tile).  Scan order inside the half is
+// (row, dim) = (lane, element), since lane 4g + t holds row g, dims [t D/4, (t+1) D/4).
+template <int D, int MODE>
+__device__ __forceinline__ void esc_k(uint32_t (&o)[Cfg<D>::NK], const uint32_t (&mk)[Cfg<D>::NMK],
+                                      Esc &es, int *status) {
+    const uint32_t cnt = count_bits(mk);
+    const uint32_t any = __ballot_sync(FULL, cnt != 0u);
+    if (any == 0u) return;
+    const uint32_t lt = lanemask_lt();
+    uint32_t r;
+    if (__ballot_sync(FULL, cnt > 1u) == 0u) {
+        r = es.run + __popc(any & lt);
+        es.run += __popc(any);
+    } else {
+        const int bits = 32 - __clz(__reduce_max_sync(FULL, cnt));
+        uint32_t pre = 0, tot = 0;
+        for (int b = 0; b < bits; ++b) {
+            const uint32_t B = __ballot_sync(FULL, (cnt >> b) & 1u);
+            pre += uint32_t(__popc(B & lt)) << b;
+            tot += uint32_t(__popc(B)) << b;
+        }
+        r = es.run + pre;
+        es.run += tot;
+    }
+    constexpr int SH = MODE == 4 ? 2 : 1, PER = MODE == 4 ? 8 : 16;
+#pragma unroll
+    for (int i = 0; i < Cfg<D>::NMK; ++i) {
+        uint32_t mm = mk[i];
+        while (mm != 0u) {
+            const int e = i * PER + ((__ffs(mm) - 1) >> SH);
+            put_half(o, e >> 1, e & 1, esc_word(r, es, status));
+            ++r;
+            mm &= mm - 1u;
+        }
+    }
+}
+
+// Sentinels of one V token half (tokens 0-7 or 8-15).  Lane 4g + t holds tokens 2t (A) and 2t+1
+// (B) of the half, dims [g D/8, (g+1) D/8); scan order inside the half is (t, A/B, g, element).
+template <int D, int MODE>
+__device__ __forceinline__ void esc_v(uint32_t (&o)[Cfg<D>::DV], const uint32_t (&ma)[Cfg<D>::NMV],
+                                      const uint32_t (&mb)[Cfg<D>::NMV], Esc &es, int *status,
+                                      int lane) {
+    const uint32_t ca = count_bits(ma), cb = count_bits(mb);
+    if (__ballot_sync(FULL, (ca | cb) != 0u) == 0u) return;
+    const uint32_t lt = lanemask_lt();
+    const int tig = lane & 3;
+    const uint32_t G = 0x11111111u << tig;                // lanes with this t
+    const uint32_t L = 0x11111111u * ((1u << tig) - 1u);  // lanes with a smaller t
+    uint32_t ra, rb;
+    if (__ballot_sync(FULL, ca > 1u || cb > 1u) == 0u) {
+        const uint32_t BA = __ballot_sync(FULL, ca != 0u), BB = __ballot_sync(FULL, cb != 0u);
+        const uint32_t before = es.run + __popc(BA & L) + __popc(BB & L);
+        ra = before + __popc(BA & G & lt);
+        rb = before + __popc(BA & G) + __popc(BB & G & lt);
+        es.run += __popc(BA) + __popc(BB);
+    } else {
+        const int bits = 32 - __clz(__reduce_max_sync(FULL, ca > cb ? ca : cb));
+        uint32_t sl = 0, sag = 0, saglt = 0, sbglt = 0, tot = 0;
+        for (int b = 0; b < bits; ++b) {
+            const uint32_t BA = __ballot_sync(FULL, (ca >> b) & 1u);
+            const uint32_t BB = __ballot_sync(FULL, (cb >> b) & 1u);
+            sl += uint32_t(__popc(BA & L) + __popc(BB & L)) << b;
+            sag += uint32_t(__popc(BA & G)) << b;
+            saglt += uint32_t(__popc(BA & G & lt)) << b;
+            sbglt += uint32_t(__popc(BB & G & lt)) << b;
+            tot += uint32_t(__popc(BA) + __popc(BB)) << b;
+        }
+        ra = es.run + sl + saglt;
+        rb = es.run + sl + sag + sbglt;
+        es.run += tot;
+    }
+    constexpr int SH = MODE == 4 ? 2 : 1, PER = MODE == 4 ? 8 : 16;
+#pragma unroll
+    for (int i = 0; i < Cfg<D>::NMV; ++i) {
+        uint32_t mm = ma[i];
+        while (mm != 0u) {
+            put_half(o, i * PER + ((__ffs(mm) - 1) >> SH), 0, esc_word(ra, es, status));
+            ++ra;
+            mm &= mm - 1u;
+        }
+        mm = mb[i];
+        while (mm != 0u) {
+            put_half(o, i * PER + ((__ffs(mm) - 1) >> SH), 1, esc_word(rb, es, status));
+            ++rb;
+            mm &= mm - 1u;
+        }
+    }
+}
+
+// ---- per-tile stages ----------------------------------------------------------------------------
+
+// Where the current tile's tensors sit in the ring slot (with the block's source alignment
+// already applied), and the block's base exponents in its meta slot.
+struct TileView {
+    const uint8_t *k_rows, *k_codes, *v_rows, *v_codes;
+    const uint8_t *k_base, *v_base;  // this lane's first base byte
+    int rows;                        // valid tokens in the tile
+};
+
+// S^T fragment of the tile: s0/s1 token g (queries 2t, 2t+1), s2/s3 token g + 8.
+template <int D, int MODE>
+__device__ __forceinline__ void qk_tile(const TileView &tv, const uint32_t (&b7r)[Cfg<D>::NK],
+                                        const uint32_t (&qb)[Cfg<D>::KS][2], Esc &es, int *status,
+                                        int lane, float (&s)[4]) {
+    using C = Cfg<D>;
+    const int gi = lane >> 2, tig = lane & 3;
+    constexpr int RS = MODE == 0 ? 2 * D : D;  // row stride of the row section
+    constexpr int CS = D * MODE / 8;           // row stride of the code section
+    const int c0 = tig * C::DK;
+    const uint8_t *r0 = tv.k_rows + gi * RS + (MODE == 0 ? 2 * c0 : c0);
+    const uint8_t *q0 = tv.k_codes + gi * CS + c0 * MODE / 8;
+    s[0] = s[1] = s[2] = s[3] = 0.f;
+    uint32_t b7[C::NK];
+#pragma unroll
+    for (int p = 0; p < C::NK; ++p) b7[p] = b7r[p];
+    if (!C::B7REG && MODE != 0) load_b7k<D>(tv.k_base, b7);
+    if (!C::SPLIT) {
+        uint32_t ka0[C::NK], ka1[C::NK], m0[C::NMK], m1[C::NMK];
+        dec_k<D, MODE>(r0, q0, b7, ka0, m0);
+        dec_k<D, MODE>(r0 + 8 * RS, q0 + 8 * CS, b7, ka1, m1);
+        if (MODE != 0) {
+            if (gi >= tv.rows)
+#pragma unroll
+                for (int i = 0; i < C::NMK; ++i) m0[i] = 0u;
+            if (gi + 8 >= tv.rows)
+#pragma unroll
+                for (int i = 0; i < C::NMK; ++i) m1[i] = 0u;
+            esc_k<D, MODE>(ka0, m0, es, status);
+            esc_k<D, MODE>(ka1, m1, es, status);
+        }
+#pragma unroll
+        for (int k = 0; k < C::KS; ++k)
+            mma_bf16(s[0], s[1], s[2], s[3], ka0[2 * k], ka1[2 * k], ka0[2 * k + 1], ka1[2 * k + 1],
+                     qb[k][0], qb[k][1]);
+    } else {
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            uint32_t ka[C::NK], mk[C::NMK];
+            dec_k<D, MODE>(r0 + 8 * h * RS, q0 + 8 * h * CS, b7, ka, mk);
+            if (MODE != 0) {
+                if (gi + 8 * h >= tv.rows)
+#pragma unroll
+                    for (int i = 0; i < C::NMK; ++i) mk[i] = 0u;
+                esc_k<D, MODE>(ka, mk, es, status);
+            }
+#pragma unroll
+            for (int k = 0; k < C::KS; ++k) {
+                if (h == 0)
+                    mma_bf16(s[0], s[1], s[2], s[3], ka[2 * k], 0u, ka[2 * k + 1], 0u, qb[k][0], qb[k][1]);
+                else
+                    mma_bf16(s[0], s[1], s[2], s[3], 0u, ka[2 * k], 0u, ka[2 * k + 1], qb[k][0], qb[k][1]);
+            }
+        }
+    }
+}
+
+// One V token half of this lane: tokens 2t + 8h (low halves) and 2t + 8h + 1 (high halves),
+// escapes patched, tokens past the tile's valid rows zeroed.
+template <int D, int MODE>
+__device__ __forceinline__ void v_half(const TileView &tv, const uint32_t (&b7)[Cfg<D>::DV],
+                                       int h, Esc &es, int *status, int lane,
+                                       uint32_t (&va)[Cfg<D>::DV]) {
+    using C = Cfg<D>;
+    const int gi = lane >> 2, tig = lane & 3;
+    constexpr int RS = MODE == 0 ? 2 * D : D;
+    constexpr int CS = D * MODE / 8;
+    const int v0 = gi * C::DV;
+    const int t = 2 * tig + 8 * h;
+    const uint8_t *r0 = tv.v_rows + t * RS + (MODE == 0 ? 2 * v0 : v0);
+    const uint8_t *q0 = tv.v_codes + t * CS + v0 * MODE / 8;
+    uint32_t ma[C::NMV], mb[C::NMV];
+    dec_v<D, MODE>(r0, r0 + RS, q0, q0 + CS, b7, va, ma, mb);
+    if (MODE != 0) {
+        if (t >= tv.rows)
+#pragma unroll
+            for (int i = 0; i < C::NMV; ++i) ma[i] = 0u;
+        if (t + 1 >= tv.rows)
+#pragma unroll
+            for (int i = 0; i < C::NMV; ++i) mb[i] = 0u;
+        esc_v<D, MODE>(va, ma, mb, es, status, lane);
+    }
+    if (tv.rows < TT) {
+        const uint32_t keep = (t < tv.rows ? 0x0000FFFFu : 0u) | (t + 1 < tv.rows ? 0xFFFF0000u : 0u);
+#pragma unroll
+        for (int e = 0; e < C::DV; ++e) va[e] &= keep;
+    }
+}
+
+// O^T += V^T P^T for the tile (P^T as B fragments: bh = bf16 part, bm = residual part).
+template <int D, int MODE>
+__device__ __forceinline__ void pv_tile(const TileView &tv, const uint32_t (&b7r)[Cfg<D>::DV],
+                                        const uint32_t (&bh)[2], const uint32_t (&bm)[2], Esc &es,
+                                        int *status, int lane, float (&acc)[Cfg<D>::KS][4]) {
+    using C = Cfg<D>;
+    uint32_t b7[C::DV];
+#pragma unroll
+    for (int e = 0; e < C::DV; ++e) b7[e] = b7r[e];
+    if (!C::B7REG && MODE != 0) load_b7v<D>(tv.v_base, b7);
+    if (!C::SPLIT) {
+        uint32_t va0[C::DV], va1[C::DV];
+        v_half<D, MODE>(tv, b7, 0, es, status, lane, va0);
+        v_half<D, MODE>(tv, b7, 1, es, status, lane, va1);
+#pragma unroll
+        for (int m = 0; m < C::KS; ++m) {
+            mma_bf16(acc[m][0], acc[m][1], acc[m][2], acc[m][3], va0[2 * m], va0[2 * m + 1],
+                     va1[2 * m], va1[2 * m + 1], bh[0], bh[1]);
+            mma_bf16(acc[m][0], acc[m][1], acc[m][2], acc[m][3], va0[2 * m], va0[2 * m + 1],
+                     va1[2 * m], va1[2 * m + 1], bm[0], bm[1]);
+        }
+    } else {
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            uint32_t va[C::DV];
+            v_half<D, MODE>(tv, b7, h, es, status, lane, va);
+#pragma unroll
+            for (int m = 0; m < C::KS; ++m) {
+                const uint32_t x0 = h == 0 ? va[2 * m] : 0u, x1 = h == 0 ? va[2 * m + 1] : 0u;
+                const uint32_t x2 = h == 0 ? 0u : va[2 * m], x3 = h == 0 ? 0u : va[2 * m + 1];
+                mma_bf16(acc[m][0], acc[m][1], acc[m][2], acc[m][3], x0, x1, x2, x3, bh[0], bh[1]);
+                mma_bf16(acc[m][0], acc[m][1], acc[m][2], acc[m][3], x0, x1, x2, x3, bm[0], bm[1]);
+            }
+        }
+    }
+}
+
+// Q B fragments: qb[k][0] = Q[g][t D/4 + 4k + {0,1}], qb[k][1] = Q[g][t D/4 + 4k + {2,3}] -- the
+// head-dim order of the K fragments.
+template <int D>
+__device__ __forceinline__ void load_q(const uint16_t *q, int n_q, int stride,
+                                       uint32_t (&qb)[Cfg<D>::KS][2], int lane) {
+    const int gi = lane >> 2, tig = lane & 3;
+    const uint32_t *row =
+        reinterpret_cast<const uint32_t *>(q + size_t(gi < n_q ? gi : 0) * stride + tig * Cfg<D>::DK);
+#pragma unroll
+    for (int k = 0; k < Cfg<D>::KS; ++k) {
+        qb[k][0] = gi < n_q ? __ldg(row + 2 * k) : 0u;
+        qb[k][1] = gi < n_q ? __ldg(row + 2 * k + 1) : 0u;
+    }
+}
+
+// ---- the worker -------------------------------------------------------------------------------
+
+// Walks the worker's flat blocks with one block of prefetch.
 struct Walker {
     int64_t fb, fb1;
     FlatBlock cur, nxt;
@@ -390,126 +656,243 @@ struct Walker {
     }
 };
 
-// One warp's own copy pipeline for its tensor (t = 0: K, 1: V): cp.async tiles into a ring of
-// NSTAGE slots, each completing on its own mbarrier; a block's first tile also brings the block's
-// base array and (when they fit) its escape words into a meta slot.
-template <int D, bool BF16IN> struct Pipe {
+// Copy side of the worker's ring.
+template <int D, bool BF16IN> struct Producer {
     using C = Cfg<D>;
-    uint8_t *R;       // this warp's region
-    uint32_t sbar;    // stage barriers
-    int t;            // tensor
-    Walker pw;        // producer position
-    int p_tile = 0, p_stage = 0, p_bseq = 0;
-    int p_unit = -1;
-    const uint8_t *p_blob = nullptr;
+    Walker w;
+    int tile = 0, stage = 0, bseq = 0, unit = -1;
+    const uint8_t *kb = nullptr, *vb = nullptr;
 
-    __device__ static int mode_of(const FlatBlock &f, int t) { return t == 0 ? f.k_mode : f.v_mode; }
-    __device__ static uint32_t off_of(const FlatBlock &f, int t) { return t == 0 ? f.k_off : f.v_off; }
-    __device__ static int nesc_of(const FlatBlock &f, int t) { return t == 0 ? f.k_nesc : f.v_nesc; }
-
-    // Escape words of a block and whether they are staged in the meta slot.
-    __device__ static Piece esc_piece(const Geo &g, int n_tok, int nesc, bool &staged) {
-        const Piece e = make_piece(g.s1 + size_t(n_tok) * D * g.mode / 8, uint32_t(2 * nesc));
-        staged = nesc > 0 && e.alloc <= uint32_t(C::ESC_CAP + 32);
-        return e;
+    __device__ static void tensor(uint8_t *dst, const Sections &s, int mode, int tile, int rows,
+                                  int lane) {
+        const int t0 = tile * TT;
+        if (BF16IN || mode == 0) {
+            copy_piece(dst, make_piece(s.rows + size_t(t0) * (2 * D), uint32_t(rows * 2 * D)), lane);
+        } else {
+            copy_piece(dst, make_piece(s.rows + size_t(t0) * D, uint32_t(rows * D)), lane);
+            copy_piece(dst + C::CODE_OFF,
+                       make_piece(s.codes + size_t(t0) * D * mode / 8, uint32_t(rows * D * mode / 8)),
+                       lane);
+        }
+    }
+    __device__ static void meta(uint8_t *base, uint8_t *escs, const Sections &s, int nesc, int lane) {
+        copy_piece(base, make_piece(s.rows - D, D), lane);
+        const Piece e = make_piece(s.esc, uint32_t(2 * nesc));
+        if (esc_staged<D>(e, nesc)) copy_piece(escs, e, lane);
     }
 
-    // Issue tiles while a ring slot is free; block starts wait until the consumer is at most one
-    // block behind, so a meta slot is never overwritten while in use.
-    __device__ void produce(const AttnArgs &a, int c_stage, int64_t c_fb, int lane) {
-        while (pw.fb < pw.fb1 && p_stage - c_stage < C::NSTAGE) {
-            if (p_tile == 0 && pw.fb - c_fb >= 2) break;
-            const FlatBlock &f = pw.cur;
-            if (pw.unit != p_unit) {
-                p_unit = pw.unit;
-                p_blob = t == 0 ? a.units[p_unit].k : a.units[p_unit].v;
+    // Issue tiles while a ring slot is free; a block start waits until the consumer is at most
+    // one block behind, so a meta slot is never overwritten while in use.
+    __device__ void produce(const AttnArgs &a, uint8_t *ring, uint8_t *metas, int c_stage,
+                            int64_t c_fb, int lane) {
+        while (w.fb < w.fb1 && stage - c_stage < C::NSTAGE) {
+            if (tile == 0 && w.fb - c_fb >= 2) break;
+            const FlatBlock &f = w.cur;
+            if (w.unit != unit) {
+                unit = w.unit;
+                kb = a.units[unit].k;
+                vb = a.units[unit].v;
             }
-            const Geo g = make_geo<D, BF16IN>(p_blob, off_of(f, t), mode_of(f, t), f.n_tok);
-            const int rows = min(TT, int(f.n_tok) - p_tile * TT);
-            Piece pc[2];
-            const int np = geo_pieces<D>(g, p_tile, rows, pc);
-            const uint32_t slot = smem_u32(R + (p_stage % C::NSTAGE) * C::SLOT);
-            copy_piece(slot, pc[0], lane);
-            if (np == 2) copy_piece(slot + pc[0].alloc, pc[1], lane);
-            if (!BF16IN && p_tile == 0 && g.mode != 0) {
-                const uint32_t ms = smem_u32(R + C::W_META + (p_bseq & 1) * C::MSLOT);
-                copy_piece(ms, make_piece(g.s0 - D, D), lane);
-                bool staged;
-                const Piece e = esc_piece(g, f.n_tok, nesc_of(f, t), staged);
-                if (staged) copy_piece(ms + C::BASE_SLOT, e, lane);
+            const int rows = min(TT, int(f.valid) - tile * TT);
+            uint8_t *slot = ring + (stage % C::NSTAGE) * C::SLOT;
+            const int km = BF16IN ? 0 : f.k_mode, vm = BF16IN ? 0 : f.v_mode;
+            const Sections sk = sections<D, BF16IN>(kb, f.k_off, km, f.n_tok);
+            const Sections sv = sections<D, BF16IN>(vb, f.v_off, vm, f.n_tok);
+            tensor(slot, sk, km, tile, rows, lane);
+            tensor(slot + C::TR, sv, vm, tile, rows, lane);
+            if (!BF16IN && tile == 0) {
+                uint8_t *ms = metas + (bseq & 1) * C::MSLOT;
+                if (km != 0) meta(ms + C::M_K, ms + C::M_EK, sk, f.k_nesc, lane);
+                if (vm != 0) meta(ms + C::M_V, ms + C::M_EV, sv, f.v_nesc, lane);
             }
-            cp_async_arrive(sbar + 8u * uint32_t(p_stage % C::NSTAGE));
-            ++p_stage;
-            if (++p_tile * TT >= int(f.valid)) {
-                p_tile = 0;
-                ++p_bseq;
-                pw.next(a);
+            cp_async_commit();
+            ++stage;
+            if (++tile * TT >= int(f.valid)) {
+                tile = 0;
+                ++bseq;
+                w.next(a);
             }
         }
     }
 };
 
-// Consumer-side position (both warps keep their own copy).
-template <int D, bool BF16IN> struct Cursor {
+template <int D, bool BF16IN>
+__device__ __forceinline__ void worker(const AttnArgs &a, uint8_t *R, int wk, int64_t fb0,
+                                       int64_t fb1, int lane) {
     using C = Cfg<D>;
+    const int gi = lane >> 2, tig = lane & 3;
+    uint8_t *ring = R;
+    uint8_t *metas = R + C::W_META;
+    Producer<D, BF16IN> pp;
+    pp.w.init(a, fb0, fb1);
     Walker cw;
-    int64_t fb0, seg_begin;
+    cw.init(a, fb0, fb1);
     int tile = 0, stage = 0, bseq = 0, unit = -1;
+    int64_t seg_begin = fb0;
     UnitDev cu{};
-    Geo g{};          // this warp's tensor in the current block
-    int rows = 0;
-    bool first = true, last_tile = false, seg_end = false;
+    int kmode = 0, vmode = 0;
+    uint32_t kd = 0, vd = 0;  // source alignment of the block's row sections
+    const uint8_t *kbase = metas, *vbase = metas;
+    Esc ek{0, 0, nullptr, nullptr}, ev{0, 0, nullptr, nullptr};
+    uint32_t b7k[C::NK], b7v[C::DV];
+#pragma unroll
+    for (int p = 0; p < C::NK; ++p) b7k[p] = 0u;
+#pragma unroll
+    for (int e = 0; e < C::DV; ++e) b7v[e] = 0u;
+    uint32_t qb[C::KS][2];
+    float acc[C::KS][4];
+    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
 
-    __device__ void init(const AttnArgs &a, int64_t b0, int64_t b1) {
-        cw.init(a, b0, b1);
-        fb0 = b0;
-        seg_begin = b0;
-    }
-    // Set up the current tile; at a block start also the base registers and escape source
-    // (the meta slot was filled by the block's first stage, which the caller has waited for).
-    __device__ void setup(const AttnArgs &a, const uint8_t *R, int t, int lane, uint32_t (&b7)[4],
-                          Esc &es) {
-        const FlatBlock &f = cw.cur;
-        first = tile == 0;
-        if (first) {
+    while (cw.fb < fb1) {
+        pp.produce(a, ring, metas, stage, cw.fb, lane);
+        cp_async_wait(pp.stage - stage - 1);
+        __syncwarp();
+        const FlatBlock f = cw.cur;
+        if (tile == 0) {
             if (cw.unit != unit) {
                 unit = cw.unit;
                 cu = a.units[unit];
             }
-            g = make_geo<D, BF16IN>(t == 0 ? cu.k : cu.v, Pipe<D, BF16IN>::off_of(f, t),
-                                    Pipe<D, BF16IN>::mode_of(f, t), f.n_tok);
-            if (!BF16IN && g.mode != 0) {
-                const uint8_t *ms = R + C::W_META + (bseq & 1) * C::MSLOT;
-                const uint8_t *b = g.s0 - D;
-                load_base(ms + (reinterpret_cast<uintptr_t>(b) & 15u) + 8 * (lane % C::CH), b7);
-                bool staged;
-                const Piece e = Pipe<D, BF16IN>::esc_piece(g, f.n_tok, Pipe<D, BF16IN>::nesc_of(f, t),
-                                                           staged);
-                es.run = 0;
-                es.n = Pipe<D, BF16IN>::nesc_of(f, t);
-                es.gm = e.src + e.data;
-                es.sm = staged ? ms + C::BASE_SLOT + e.data : nullptr;
+            kmode = BF16IN ? 0 : f.k_mode;
+            vmode = BF16IN ? 0 : f.v_mode;
+            const Sections sk = sections<D, BF16IN>(cu.k, f.k_off, kmode, f.n_tok);
+            const Sections sv = sections<D, BF16IN>(cu.v, f.v_off, vmode, f.n_tok);
+            kd = uint32_t(reinterpret_cast<uintptr_t>(sk.rows) & 15u);
+            vd = uint32_t(reinterpret_cast<uintptr_t>(sv.rows) & 15u);
+            const uint8_t *ms = metas + (bseq & 1) * C::MSLOT;
+            kbase = ms + C::M_K + kd + tig * C::DK;
+            vbase = ms + C::M_V + vd + gi * C::DV;
+            if (kmode != 0) {
+                if (C::B7REG) load_b7k<D>(kbase, b7k);
+                const Piece e = make_piece(sk.esc, uint32_t(2 * f.k_nesc));
+                ek.run = 0;
+                ek.n = f.k_nesc;
+                ek.gm = reinterpret_cast<const unsigned short *>(sk.esc);
+                ek.sm = esc_staged<D>(e, f.k_nesc) ? ms + C::M_EK + e.data : nullptr;
+            }
+            if (vmode != 0) {
+                if (C::B7REG) load_b7v<D>(vbase, b7v);
+                const Piece e = make_piece(sv.esc, uint32_t(2 * f.v_nesc));
+                ev.run = 0;
+                ev.n = f.v_nesc;
+                ev.gm = reinterpret_cast<const unsigned short *>(sv.esc);
+                ev.sm = esc_staged<D>(e, f.v_nesc) ? ms + C::M_EV + e.data : nullptr;
+            }
+            if (cw.fb == seg_begin) {
+                load_q<D>(cu.q, cu.n_q, cu.q_stride, qb, lane);
+                m0 = m1 = -INFINITY;
+                l0 = l1 = 0.f;
+#pragma unroll
+                for (int m = 0; m < C::KS; ++m) acc[m][0] = acc[m][1] = acc[m][2] = acc[m][3] = 0.f;
             }
         }
-        rows = min(TT, int(f.valid) - tile * TT);
-        last_tile = (tile + 1) * TT >= int(f.valid);
+        const uint8_t *slot = ring + (stage % C::NSTAGE) * C::SLOT;
+        TileView tv;
+        tv.rows = min(TT, int(f.valid) - tile * TT);
+        tv.k_rows = slot + kd;
+        tv.k_codes = slot + C::CODE_OFF + kd;
+        tv.v_rows = slot + C::TR + vd;
+        tv.v_codes = slot + C::TR + C::CODE_OFF + vd;
+        tv.k_base = kbase;
+        tv.v_base = vbase;
+        const bool last_tile = (tile + 1) * TT >= int(f.valid);
         const int64_t ub = cu.block_begin + cu.n_blocks;
-        seg_end = last_tile && ((cw.fb + 1 == cw.fb1) || (cw.fb + 1 == ub));
-    }
-    __device__ bool whole_unit() const {
-        return seg_begin == cu.block_begin && cw.fb + 1 == cu.block_begin + cu.n_blocks;
-    }
-    // Where this tile's data starts in the slot.
-    __device__ void data(const uint8_t *R, const uint8_t *&p0, const uint8_t *&p1) const {
-        const FlatBlock &f = cw.cur;
-        const int rl = min(TT, int(f.n_tok) - tile * TT);
-        Piece pc[2];
-        const int np = geo_pieces<D>(g, tile, rl, pc);
-        const uint8_t *slot = R + (stage % C::NSTAGE) * C::SLOT;
-        p0 = slot + pc[0].data;
-        p1 = np == 2 ? slot + pc[0].alloc + pc[1].data : nullptr;
-    }
-    __device__ void advance(const AttnArgs &a) {
+        const bool seg_end = last_tile && (cw.fb + 1 == fb1 || cw.fb + 1 == ub);
+
+        // S^T = K Q^T
+        float s[4];
+        if (kmode == 4) qk_tile<D, 4>(tv, b7k, qb, ek, a.status, lane, s);
+        else if (kmode == 2) qk_tile<D, 2>(tv, b7k, qb, ek, a.status, lane, s);
+        else qk_tile<D, 0>(tv, b7k, qb, ek, a.status, lane, s);
+        if (gi >= tv.rows) s[0] = s[1] = -INFINITY;
+        if (gi + 8 >= tv.rows) s[2] = s[3] = -INFINITY;
+
+        // online softmax over the tile's tokens; p = 2^(s log2e - m log2e)
+        float t0 = fmaxf(s[0], s[2]), t1 = fmaxf(s[1], s[3]);
+#pragma unroll
+        for (int o = 4; o < 32; o <<= 1) {
+            t0 = fmaxf(t0, __shfl_xor_sync(FULL, t0, o));
+            t1 = fmaxf(t1, __shfl_xor_sync(FULL, t1, o));
+        }
+        const float mn0 = fmaxf(m0, t0), mn1 = fmaxf(m1, t1);
+        const float ml0 = __fmul_rn(mn0, kLog2e), ml1 = __fmul_rn(mn1, kLog2e);
+        const float al0 = ex2(__fmaf_rn(m0, kLog2e, -ml0)), al1 = ex2(__fmaf_rn(m1, kLog2e, -ml1));
+        const float p0 = ex2(__fmaf_rn(s[0], kLog2e, -ml0)), p1 = ex2(__fmaf_rn(s[1], kLog2e, -ml1));
+        const float p2 = ex2(__fmaf_rn(s[2], kLog2e, -ml0)), p3 = ex2(__fmaf_rn(s[3], kLog2e, -ml1));
+        l0 = __fmaf_rn(l0, al0, __fadd_rn(p0, p2));
+        l1 = __fmaf_rn(l1, al1, __fadd_rn(p1, p3));
+        m0 = mn0;
+        m1 = mn1;
+
+        // P^T B fragments: bf16(p) and bf16(p - bf16(p))
+        uint32_t bh[2], bm[2];
+        {
+            const uint32_t h01 = pack_bf16x2(p1, p0), h23 = pack_bf16x2(p3, p2);
+            const float r0 = __fsub_rn(p0, bf16lo_to_f32(h01)), r1 = __fsub_rn(p1, bf16hi_to_f32(h01));
+            const float r2 = __fsub_rn(p2, bf16lo_to_f32(h23)), r3 = __fsub_rn(p3, bf16hi_to_f32(h23));
+            bh[0] = movm_t(h01);
+            bh[1] = movm_t(h23);
+            bm[0] = movm_t(pack_bf16x2(r1, r0));
+            bm[1] = movm_t(pack_bf16x2(r3, r2));
+        }
+        if (__any_sync(FULL, al0 != 1.0f || al1 != 1.0f)) {
+#pragma unroll
+            for (int m = 0; m < C::KS; ++m) {
+                acc[m][0] = __fmul_rn(acc[m][0], al0);
+                acc[m][1] = __fmul_rn(acc[m][1], al1);
+                acc[m][2] = __fmul_rn(acc[m][2], al0);
+                acc[m][3] = __fmul_rn(acc[m][3], al1);
+            }
+        }
+        // O^T += V^T P^T
+        if (vmode == 4) pv_tile<D, 4>(tv, b7v, bh, bm, ev, a.status, lane, acc);
+        else if (vmode == 2) pv_tile<D, 2>(tv, b7v, bh, bm, ev, a.status, lane, acc);
+        else pv_tile<D, 0>(tv, b7v, bh, bm, ev, a.status, lane, acc);
+
+        if (seg_end) {
+            float lt0 = l0, lt1 = l1;
+#pragma unroll
+            for (int o = 4; o < 32; o <<= 1) {
+                lt0 = __fadd_rn(lt0, __shfl_xor_sync(FULL, lt0, o));
+                lt1 = __fadd_rn(lt1, __shfl_xor_sync(FULL, lt1, o));
+            }
+            const int qa = 2 * tig, qc = 2 * tig + 1;
+            const int d0 = gi * C::DV;
+            if (seg_begin == cu.block_begin && cw.fb + 1 == ub) {
+                const float inv0 = __frcp_rn(lt0), inv1 = __frcp_rn(lt1);
+                if (qa < cu.n_q) {
+                    float *o = cu.out + size_t(qa) * cu.q_stride + d0;
+#pragma unroll
+                    for (int m = 0; m < C::KS; ++m)
+                        *reinterpret_cast<float2 *>(o + 2 * m) =
+                            make_float2(__fmul_rn(acc[m][0], inv0), __fmul_rn(acc[m][2], inv0));
+                }
+                if (qc < cu.n_q) {
+                    float *o = cu.out + size_t(qc) * cu.q_stride + d0;
+#pragma unroll
+                    for (int m = 0; m < C::KS; ++m)
+                        *reinterpret_cast<float2 *>(o + 2 * m) =
+                            make_float2(__fmul_rn(acc[m][1], inv1), __fmul_rn(acc[m][3], inv1));
+                }
+            } else {
+                const int ps = (seg_begin == fb0) ? 0 : 1;
+                float *part = a.partials + (size_t(wk) * 2 + ps) * partial_stride(D);
+                if (gi == 0) {
+                    part[qa] = m0;
+                    part[qc] = m1;
+                    part[8 + qa] = lt0;
+                    part[8 + qc] = lt1;
+                }
+                float *oa = part + 16 + qa * D + d0;
+                float *oc = part + 16 + qc * D + d0;
+#pragma unroll
+                for (int m = 0; m < C::KS; ++m) {
+                    *reinterpret_cast<float2 *>(oa + 2 * m) = make_float2(acc[m][0], acc[m][2]);
+                    *reinterpret_cast<float2 *>(oc + 2 * m) = make_float2(acc[m][1], acc[m][3]);
+                }
+            }
+        }
+        __syncwarp();  // every lane is done with this ring slot before it is refilled
         ++stage;
         if (last_tile) {
             tile = 0;
@@ -520,283 +903,36 @@ template <int D, bool BF16IN> struct Cursor {
             ++tile;
         }
     }
-};
-
-// K-warp: streams and rebuilds K, runs QK and the online softmax, hands p over to the V-warp.
-template <int D, bool BF16IN>
-__device__ __forceinline__ void k_warp(const AttnArgs &a, const Team &tm, uint8_t *R, int64_t fb0,
-                                       int64_t fb1, int lane) {
-    using C = Cfg<D>;
-    const uint32_t full_bar = tm.bar0, empty_bar = tm.bar0 + 16u;
-    const int gi = lane >> 2, tig = lane & 3;
-    Pipe<D, BF16IN> pp;
-    pp.R = R;
-    pp.sbar = smem_u32(R + C::W_BAR);
-    pp.t = 0;
-    pp.pw.init(a, fb0, fb1);
-    Cursor<D, BF16IN> cs;
-    cs.init(a, fb0, fb1);
-    uint32_t b7[4] = {0, 0, 0, 0};
-    Esc es{0, 0, nullptr, nullptr};
-    uint8_t *kt = R + C::W_TILE;
-    uint32_t qb[D / 16][2];
-    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
-    const int mat = lane >> 3;
-    const int r = (lane & 7) + 8 * (mat & 1);
-    const int cadd = mat >> 1;
-    const int sw = swz<D>(r);
-    const uint32_t krow = smem_u32(kt) + uint32_t(r * 2 * D);
-    bool ok = true;
-
-    while (cs.cw.fb < fb1) {
-        pp.produce(a, cs.stage, cs.cw.fb, lane);
-        if (!wait_bar(pp.sbar + 8u * uint32_t(cs.stage % C::NSTAGE), (cs.stage / C::NSTAGE) & 1, tm,
-                      a)) {
-            ok = false;
-            break;
-        }
-        cs.setup(a, R, 0, lane, b7, es);
-        if (cs.first && cs.cw.fb == cs.seg_begin) {
-            load_q_frags<D>(cs.cu.q, cs.cu.n_q, cs.cu.q_stride, qb, lane);
-            m0 = m1 = -INFINITY;
-            l0 = l1 = 0.f;
-        }
-        const uint8_t *p0, *p1;
-        cs.data(R, p0, p1);
-        const int rows = cs.rows;
-        decode_tile<D>(kt, cs.g.mode, rows, p0, p1, b7, es, a.status, lane);
-        __syncwarp();
-        // S^T[16 tokens x 8 queries] = K[16 x D] * Q^T[D x 8]
-        float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
-#pragma unroll
-        for (int s = 0; s < D / 16; ++s) {
-            uint32_t a0, a1, a2, a3;
-            ldsm_x4(krow + 16u * uint32_t((2 * s + cadd) ^ sw), a0, a1, a2, a3);
-            mma_bf16(s0, s1, s2, s3, a0, a1, a2, a3, qb[s][0], qb[s][1]);
-        }
-        if (gi >= rows) s0 = s1 = -INFINITY;
-        if (gi + 8 >= rows) s2 = s3 = -INFINITY;
-        float t0 = fmaxf(s0, s2), t1 = fmaxf(s1, s3);
-#pragma unroll
-        for (int o = 4; o < 32; o <<= 1) {
-            t0 = fmaxf(t0, __shfl_xor_sync(FULL, t0, o));
-            t1 = fmaxf(t1, __shfl_xor_sync(FULL, t1, o));
-        }
-        // p = 2^(s log2e - m log2e): one FMA and one ex2 per score
-        const float mn0 = fmaxf(m0, t0), mn1 = fmaxf(m1, t1);
-        const float ml0 = __fmul_rn(mn0, kLog2e), ml1 = __fmul_rn(mn1, kLog2e);
-        const float al0 = ex2(__fmaf_rn(m0, kLog2e, -ml0)), al1 = ex2(__fmaf_rn(m1, kLog2e, -ml1));
-        const float p0v = ex2(__fmaf_rn(s0, kLog2e, -ml0)), p1v = ex2(__fmaf_rn(s1, kLog2e, -ml1));
-        const float p2v = ex2(__fmaf_rn(s2, kLog2e, -ml0)), p3v = ex2(__fmaf_rn(s3, kLog2e, -ml1));
-        l0 = __fmaf_rn(l0, al0, __fadd_rn(p0v, p2v));
-        l1 = __fmaf_rn(l1, al1, __fadd_rn(p1v, p3v));
-        m0 = mn0;
-        m1 = mn1;
-        float lt0 = l0, lt1 = l1;
-        if (cs.seg_end) {
-#pragma unroll
-            for (int o = 4; o < 32; o <<= 1) {
-                lt0 = __fadd_rn(lt0, __shfl_xor_sync(FULL, lt0, o));
-                lt1 = __fadd_rn(lt1, __shfl_xor_sync(FULL, lt1, o));
-            }
-        }
-        // hand p over; slot reuse waits until the V-warp is done with tile stage - 2
-        const int slot = cs.stage & 1;
-        if (cs.stage >= 2 &&
-            !wait_bar(empty_bar + 8u * uint32_t(slot), ((cs.stage - 2) >> 1) & 1, tm, a)) {
-            ok = false;
-            break;
-        }
-        uint8_t *P = tm.T + C::OFF_PS + slot * C::PSLOT;
-        reinterpret_cast<float4 *>(P)[lane] = make_float4(p0v, p1v, p2v, p3v);
-        float *pf = reinterpret_cast<float *>(P + 512);
-        if (gi == 0) {
-            pf[2 * tig] = al0;
-            pf[2 * tig + 1] = al1;
-            if (cs.seg_end) {
-                pf[8 + 2 * tig] = m0;
-                pf[8 + 2 * tig + 1] = m1;
-                pf[16 + 2 * tig] = lt0;
-                pf[16 + 2 * tig + 1] = lt1;
-            }
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(full_bar + 8u * uint32_t(slot));
-        cs.advance(a);
-    }
-    if (!ok) {
-        // bounded drain of this warp's copies still in flight
-        for (int i = cs.stage; i < pp.p_stage; ++i)
-            mbar_wait_bounded(pp.sbar + 8u * uint32_t(i % C::NSTAGE), (i / C::NSTAGE) & 1,
-                              a.wait_limit);
-    }
-}
-
-// V-warp: streams and rebuilds V, accumulates O += P V over the whole head dim, writes outputs
-// or partial states.
-template <int D, bool BF16IN>
-__device__ __forceinline__ void v_warp(const AttnArgs &a, const Team &tm, uint8_t *R, int team,
-                                       int64_t fb0, int64_t fb1, int lane) {
-    using C = Cfg<D>;
-    const uint32_t full_bar = tm.bar0, empty_bar = tm.bar0 + 16u;
-    const int gi = lane >> 2, tig = lane & 3;
-    Pipe<D, BF16IN> pp;
-    pp.R = R;
-    pp.sbar = smem_u32(R + C::W_BAR);
-    pp.t = 1;
-    pp.pw.init(a, fb0, fb1);
-    Cursor<D, BF16IN> cs;
-    cs.init(a, fb0, fb1);
-    uint32_t b7[4] = {0, 0, 0, 0};
-    Esc es{0, 0, nullptr, nullptr};
-    uint8_t *vt = R + C::W_TILE;
-    float acc[C::CH][4];  // rows gi: hi part, rows gi + 8: mid part of query gi
-    const int mat = lane >> 3;
-    const int r = (lane & 7) + 8 * (mat & 1);
-    const int cadd = mat >> 1;
-    const int sw = swz<D>(r);
-    const uint32_t vrow = smem_u32(vt) + uint32_t(r * 2 * D);
-    bool ok = true;
-
-    while (cs.cw.fb < fb1) {
-        pp.produce(a, cs.stage, cs.cw.fb, lane);
-        if (!wait_bar(pp.sbar + 8u * uint32_t(cs.stage % C::NSTAGE), (cs.stage / C::NSTAGE) & 1, tm,
-                      a)) {
-            ok = false;
-            break;
-        }
-        cs.setup(a, R, 1, lane, b7, es);
-        if (cs.first && cs.cw.fb == cs.seg_begin) {
-#pragma unroll
-            for (int j = 0; j < C::CH; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
-        }
-        const uint8_t *p0, *p1;
-        cs.data(R, p0, p1);
-        decode_tile<D>(vt, cs.g.mode, cs.rows, p0, p1, b7, es, a.status, lane);
-        __syncwarp();
-        const int slot = cs.stage & 1;
-        if (!wait_bar(full_bar + 8u * uint32_t(slot), (cs.stage >> 1) & 1, tm, a)) {
-            ok = false;
-            break;
-        }
-        const uint8_t *P = tm.T + C::OFF_PS + slot * C::PSLOT;
-        const float4 pv4 = reinterpret_cast<const float4 *>(P)[lane];
-        const float *pf = reinterpret_cast<const float *>(P + 512);
-        // P^T tile (lane: tokens gi, gi+8 x queries 2tig, 2tig+1) -> P A-fragments: rows 0-7
-        // carry bf16(p), rows 8-15 bf16(p - bf16(p)), so P enters the MMA with 16 bits
-        uint4 A;
-        {
-            const uint32_t h01 = pack_bf16x2(pv4.y, pv4.x), h23 = pack_bf16x2(pv4.w, pv4.z);
-            const float r0 = __fsub_rn(pv4.x, bf16lo_to_f32(h01));
-            const float r1 = __fsub_rn(pv4.y, bf16hi_to_f32(h01));
-            const float r2 = __fsub_rn(pv4.z, bf16lo_to_f32(h23));
-            const float r3 = __fsub_rn(pv4.w, bf16hi_to_f32(h23));
-            const uint32_t mm01 = pack_bf16x2(r1, r0), mm23 = pack_bf16x2(r3, r2);
-            A = make_uint4(movm_t(h01), movm_t(mm01), movm_t(h23), movm_t(mm23));
-        }
-        const float al = pf[gi];
-        if (__any_sync(FULL, al != 1.0f)) {
-#pragma unroll
-            for (int j = 0; j < C::CH; ++j)
-#pragma unroll
-                for (int e = 0; e < 4; ++e) acc[j][e] = __fmul_rn(acc[j][e], al);
-        }
-#pragma unroll
-        for (int j = 0; j < C::CH; j += 2) {
-            uint32_t v0, v1, v2, v3;
-            ldsm_x4_t(vrow + 16u * uint32_t((j + cadd) ^ sw), v0, v1, v2, v3);
-            mma_bf16(acc[j][0], acc[j][1], acc[j][2], acc[j][3], A.x, A.y, A.z, A.w, v0, v1);
-            mma_bf16(acc[j + 1][0], acc[j + 1][1], acc[j + 1][2], acc[j + 1][3], A.x, A.y, A.z,
-                     A.w, v2, v3);
-        }
-        if (cs.seg_end) {
-            const UnitDev &cu = cs.cu;
-            if (cs.whole_unit()) {
-                if (gi < cu.n_q) {
-                    const float inv = __frcp_rn(pf[16 + gi]);
-                    float *o = cu.out + size_t(gi) * cu.q_stride;
-#pragma unroll
-                    for (int j = 0; j < C::CH; ++j) {
-                        o[8 * j + tig] = __fmul_rn(__fadd_rn(acc[j][0], acc[j][2]), inv);
-                        o[8 * j + 4 + tig] = __fmul_rn(__fadd_rn(acc[j][1], acc[j][3]), inv);
-                    }
-                }
-            } else {
-                const int ps = (cs.seg_begin == fb0) ? 0 : 1;
-                float *part = a.partials + (size_t(team) * 2 + ps) * partial_stride(D);
-                if (lane < 16) part[lane] = pf[8 + lane];  // m[8], l[8]
-                float *ac = part + 16 + gi * D;
-#pragma unroll
-                for (int j = 0; j < C::CH; ++j) {
-                    ac[8 * j + tig] = __fadd_rn(acc[j][0], acc[j][2]);
-                    ac[8 * j + 4 + tig] = __fadd_rn(acc[j][1], acc[j][3]);
-                }
-            }
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(empty_bar + 8u * uint32_t(slot));
-        cs.advance(a);
-    }
-    if (!ok) {
-        for (int i = cs.stage; i < pp.p_stage; ++i)
-            mbar_wait_bounded(pp.sbar + 8u * uint32_t(i % C::NSTAGE), (i / C::NSTAGE) & 1,
-                              a.wait_limit);
-    }
 }
 
 template <int D, bool BF16IN>
-__global__ void __launch_bounds__(64 * Cfg<D>::TEAMS, 1) attn_kernel(const AttnArgs a) {
+__global__ void __launch_bounds__(32 * Cfg<D>::WARPS, 1) attn_kernel(const AttnArgs a) {
     using C = Cfg<D>;
     extern __shared__ __align__(128) uint8_t smem[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int tl = warp >> 1;
-    // K-warp of team tl is warp 2*tl + ((tl >> 1) & 1): spreads the roles over all four SM
-    // sub-partitions (warp % 4).
-    const int w = (warp & 1) ^ ((tl >> 1) & 1);
-    const int team = blockIdx.x * C::TEAMS + tl;
-    if (team >= a.n_teams) return;
-    const int64_t fb0 = a.team_begin[team], fb1 = a.team_begin[team + 1];
+    const int wk = blockIdx.x * C::WARPS + warp;
+    if (wk >= a.n_workers) return;
+    const int64_t fb0 = a.range_begin[wk], fb1 = a.range_begin[wk + 1];
     if (fb0 >= fb1) return;
-
-    Team tm;
-    tm.T = smem + tl * C::TEAM;
-    tm.bar0 = smem_u32(tm.T + C::OFF_BAR);
-    tm.abort = reinterpret_cast<volatile int *>(tm.T + C::OFF_FLAG);
-    uint8_t *R = tm.T + w * C::WARP_BYTES;
-    if (lane == 0) {
-        // each warp initialises its own stage barriers (one arrival per lane); the K-warp the
-        // shared full / empty barriers
-        const uint32_t sbar = smem_u32(R + C::W_BAR);
-        for (int i = 0; i < C::NSTAGE; ++i) mbar_init(sbar + 8 * i, 32);
-        if (w == 0) {
-            for (int i = 0; i < 4; ++i) mbar_init(tm.bar0 + 8 * i, 1);
-            *tm.abort = 0;
-        }
-        fence_mbar_init();
-    }
-    named_bar(tl + 1, 64);
-    if (w == 0)
-        k_warp<D, BF16IN>(a, tm, R, fb0, fb1, lane);
-    else
-        v_warp<D, BF16IN>(a, tm, R, team, fb0, fb1, lane);
+    worker<D, BF16IN>(a, smem + warp * C::WARP_BYTES, wk, fb0, fb1, lane);
 }
 
 // ---- combine ------------------------------------------------------------------------------------
 
-// Fold the partial states of a unit in team order (merge_state, src/softmax.hpp:16-30) and
+// Fold the partial states of a unit in worker order (merge_state, src/softmax.hpp:16-30) and
 // finalize (finalize_state, src/softmax.hpp:32-41).
 template <int D>
 __global__ void __launch_bounds__(256) combine_kernel(const CombineArgs a) {
     const int u = a.split_units[blockIdx.x];
     const UnitDev unit = a.units[u];
-    const int t0 = team_of_block(a.team_begin, a.n_teams, unit.block_begin);
-    const int t1 = team_of_block(a.team_begin, a.n_teams, unit.block_begin + unit.n_blocks - 1);
+    const int t0 = worker_of_block(a.range_begin, a.n_workers, unit.block_begin);
+    const int t1 = worker_of_block(a.range_begin, a.n_workers, unit.block_begin + unit.n_blocks - 1);
     const int ps = partial_stride(D);
     for (int idx = threadIdx.x; idx < unit.n_q * D; idx += blockDim.x) {
         const int g = idx / D, d = idx % D;
         float m = 0.f, l = 0.f, acc = 0.f;
         for (int t = t0; t <= t1; ++t) {
-            const int slot = (a.team_begin[t] >= unit.block_begin) ? 0 : 1;
+            const int slot = (a.range_begin[t] >= unit.block_begin) ? 0 : 1;
             const float *p = a.partials + (size_t(t) * 2 + slot) * ps;
             const float mb = p[g], lb = p[8 + g], ab = p[16 + g * D + d];
             if (t == t0) {
@@ -821,18 +957,18 @@ template <int D> void configure(bool bf16) {
     if (done[bf16]) return;
     if (bf16)
         cudaFuncSetAttribute(attn_kernel<D, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             Cfg<D>::TEAM * Cfg<D>::TEAMS);
+                             Cfg<D>::WARP_BYTES * Cfg<D>::WARPS);
     else
         cudaFuncSetAttribute(attn_kernel<D, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             Cfg<D>::TEAM * Cfg<D>::TEAMS);
+                             Cfg<D>::WARP_BYTES * Cfg<D>::WARPS);
     done[bf16] = true;
 }
 
 template <int D>
 cudaError_t launch_d(bool bf16, const AttnArgs &a, int grid, cudaStream_t s) {
     configure<D>(bf16);
-    const int threads = 64 * Cfg<D>::TEAMS;
-    const size_t sm = size_t(Cfg<D>::TEAM) * Cfg<D>::TEAMS;
+    const int threads = 32 * Cfg<D>::WARPS;
+    const size_t sm = size_t(Cfg<D>::WARP_BYTES) * Cfg<D>::WARPS;
     if (bf16)
         attn_kernel<D, true><<<grid, threads, sm, s>>>(a);
     else
@@ -846,28 +982,27 @@ bool attention_dim_supported(int dim) {
     return dim == 32 || dim == 64 || dim == 128 || dim == 256;
 }
 
-int attention_teams_per_cta(int dim) {
+int attention_workers_per_cta(int dim) {
     switch (dim) {
-    case 32: return Cfg<32>::TEAMS;
-    case 64: return Cfg<64>::TEAMS;
-    case 128: return Cfg<128>::TEAMS;
-    case 256: return Cfg<256>::TEAMS;
+    case 32: return Cfg<32>::WARPS;
+    case 64: return Cfg<64>::WARPS;
+    case 128: return Cfg<128>::WARPS;
+    case 256: return Cfg<256>::WARPS;
     default: return 0;
     }
 }
 
 size_t attention_smem_bytes(int dim) {
     switch (dim) {
-    case 32: return size_t(Cfg<32>::TEAM) * Cfg<32>::TEAMS;
-    case 64: return size_t(Cfg<64>::TEAM) * Cfg<64>::TEAMS;
-    case 128: return size_t(Cfg<128>::TEAM) * Cfg<128>::TEAMS;
-    case 256: return size_t(Cfg<256>::TEAM) * Cfg<256>::TEAMS;
+    case 32: return size_t(Cfg<32>::WARP_BYTES) * Cfg<32>::WARPS;
+    case 64: return size_t(Cfg<64>::WARP_BYTES) * Cfg<64>::WARPS;
+    case 128: return size_t(Cfg<128>::WARP_BYTES) * Cfg<128>::WARPS;
+    case 256: return size_t(Cfg<256>::WARP_BYTES) * Cfg<256>::WARPS;
     default: return 0;
     }
 }
 
-cudaError_t launch_attention(int dim, bool bf16_input, const AttnArgs &a, int grid, int /*teams*/,
-                             cudaStream_t s) {
+cudaError_t launch_attention(int dim, bool bf16_input, const AttnArgs &a, int grid, cudaStream_t s) {
     switch (dim) {
     case 32: return launch_d<32>(bf16_input, a, grid, s);
     case 64: return launch_d<64>(bf16_input, a, grid, s);

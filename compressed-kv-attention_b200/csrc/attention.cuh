@@ -38,39 +38,37 @@ struct AttnArgs {
     const UnitDev *units;
     const FlatBlock *flat;      // [n_blocks]
     const int32_t *flat_unit;   // [n_blocks] unit of each flat block
-    const int64_t *team_begin;  // [n_teams + 1] flat-block range of each team
-    float *partials;            // [n_teams][2][8 + 8 + 8 * dim]
+    const int64_t *range_begin; // [n_workers + 1] flat-block range of each worker warp
+    float *partials;            // [n_workers][2][8 + 8 + 8 * dim]
     int *status;                // [2] first error (code, detail)
-    int n_teams;
-    uint32_t wait_limit;
+    int n_workers;
 };
 
 struct CombineArgs {
     const UnitDev *units;
-    const int32_t *split_units;   // units whose blocks span several teams
-    const int64_t *team_begin;    // [n_teams + 1]
+    const int32_t *split_units;   // units whose blocks span several workers
+    const int64_t *range_begin;    // [n_workers + 1]
     const float *partials;
-    int n_teams;
+    int n_workers;
 };
 
-// Partial-state stride (floats) for one (team, slot): m[8], l[8], acc[8][dim].
+// Partial-state stride (floats) for one (worker, slot): m[8], l[8], acc[8][dim].
 __host__ __device__ inline int partial_stride(int dim) { return 16 + 8 * dim; }
 
-// Team that owns flat block b: the last team whose range starts at or before b.
-__host__ __device__ inline int team_of_block(const int64_t *team_begin, int n_teams, int64_t b) {
-    int lo = 0, hi = n_teams - 1;
+// Worker that owns flat block b: the last worker whose range starts at or before b.
+__host__ __device__ inline int worker_of_block(const int64_t *range_begin, int n_workers, int64_t b) {
+    int lo = 0, hi = n_workers - 1;
     while (lo < hi) {
         int mid = (lo + hi + 1) >> 1;
-        if (team_begin[mid] <= b) lo = mid; else hi = mid - 1;
+        if (range_begin[mid] <= b) lo = mid; else hi = mid - 1;
     }
     return lo;
 }
 
 // Launchers (attention.cu).  Return cudaError_t of the launch.
-cudaError_t launch_attention(int dim, bool bf16_input, const AttnArgs &a, int grid, int teams_per_cta,
-                             cudaStream_t s);
+cudaError_t launch_attention(int dim, bool bf16_input, const AttnArgs &a, int grid, cudaStream_t s);
 cudaError_t launch_combine(int dim, const CombineArgs &a, int n_split, cudaStream_t s);
-int attention_teams_per_cta(int dim);
+int attention_workers_per_cta(int dim);
 size_t attention_smem_bytes(int dim);
 bool attention_dim_supported(int dim);
 

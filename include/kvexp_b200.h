@@ -134,7 +134,7 @@ KVX_API int kvx_plan_create(const kvx_unit *units, int n_units, int n_q, int dim
 /* Launch one decode step for every unit on `stream` (a cudaStream_t; NULL = default stream). */
 KVX_API int kvx_plan_run(kvx_plan plan, void *stream);
 /* Launch one part of a step: 0 = the fused decode-attention kernel, 1 = the combine kernel of
- * units split across teams (a no-op when no unit is split).  kvx_plan_run = part 0 then 1. */
+ * units split across workers (a no-op when no unit is split).  kvx_plan_run = part 0 then 1. */
 KVX_API int kvx_plan_run_part(kvx_plan plan, int part, void *stream);
 /* Synchronise the plan's last run and report device-side errors (malformed blocks, timeouts). */
 KVX_API int kvx_plan_check(kvx_plan plan);
