@@ -334,15 +334,6 @@ int kvx_plan_create(const kvx_unit *units, int n_units, int n_q, int dim, int bl
     p->n_workers = int(std::min<int64_t>(max_workers, total));
     p->grid = (p->n_workers + per_cta - 1) / per_cta;
     std::vector<int64_t> tb(size_t(p->n_workers) + 1);
-    for (int t = 0; t <= p->n_workers; ++t) tb[size_t(t)] = (int64_t)t * total / p->n_workers;
-    std::vector<int32_t> split;
-    for (int u = 0; u < p->n_units; ++u) {
-        const int t0 = worker_of_block(tb.data(), p->n_workers, ud[size_t(u)].block_begin);
-        const int t1 = worker_of_block(tb.data(), p->n_workers,
-                                     ud[size_t(u)].block_begin + ud[size_t(u)].n_blocks - 1);
-        if (t0 != t1) split.push_back(u);
-    }
-    p->n_split = int(split.size());
     kvx_unit *dvu = nullptr;
     int64_t *dbegin = nullptr;
     cudaError_t e = cudaSuccess;
@@ -351,7 +342,7 @@ int kvx_plan_create(const kvx_unit *units, int n_units, int n_q, int dim, int bl
         (e = plan_alloc(p, &p->flat_unit, size_t(total))) != cudaSuccess ||
         (e = plan_alloc(p, &p->range_begin, tb.size())) != cudaSuccess ||
         (e = plan_alloc(p, &p->partials, size_t(p->n_workers) * 2 * partial_stride(dim))) != cudaSuccess ||
-        (e = plan_alloc(p, &p->split_units, split.size())) != cudaSuccess ||
+        (e = plan_alloc(p, &p->split_units, ud.size())) != cudaSuccess ||
         (e = plan_alloc(p, &p->status, 2)) != cudaSuccess ||
         (e = plan_alloc(p, &dvu, vu.size())) != cudaSuccess ||
         (e = plan_alloc(p, &dbegin, begin.size())) != cudaSuccess) {
@@ -359,10 +350,6 @@ int kvx_plan_create(const kvx_unit *units, int n_units, int n_q, int dim, int bl
         return fail(KVX_ERR_CUDA, std::string("kvx_plan_create: ") + cudaGetErrorString(e));
     }
     cudaMemcpy(p->units, ud.data(), ud.size() * sizeof(UnitDev), cudaMemcpyHostToDevice);
-    cudaMemcpy(p->range_begin, tb.data(), tb.size() * sizeof(int64_t), cudaMemcpyHostToDevice);
-    if (!split.empty())
-        cudaMemcpy(p->split_units, split.data(), split.size() * sizeof(int32_t),
-                   cudaMemcpyHostToDevice);
     cudaMemcpy(dvu, vu.data(), vu.size() * sizeof(kvx_unit), cudaMemcpyHostToDevice);
     cudaMemcpy(dbegin, begin.data(), begin.size() * sizeof(int64_t), cudaMemcpyHostToDevice);
     cudaMemset(p->status, 0, 2 * sizeof(int));
@@ -377,6 +364,35 @@ int kvx_plan_create(const kvx_unit *units, int n_units, int n_q, int dim, int bl
         delete p;
         return rc;
     }
+    // Worker ranges of about equal cost (tokens and escape words), then the units whose blocks
+    // span several workers (they need the combine pass).
+    // With no more blocks than workers every block is its own range, whatever the costs.
+    if (total <= max_workers) {
+        for (int t = 0; t <= p->n_workers; ++t) tb[size_t(t)] = t;
+        e = cudaMemcpy(p->range_begin, tb.data(), tb.size() * sizeof(int64_t), cudaMemcpyHostToDevice);
+    } else {
+        e = launch_split(p->flat, total, p->n_workers, p->range_begin, nullptr);
+        if (e == cudaSuccess)
+            e = cudaMemcpy(tb.data(), p->range_begin, tb.size() * sizeof(int64_t),
+                           cudaMemcpyDeviceToHost);
+    }
+    std::vector<int32_t> split;
+    if (e == cudaSuccess) {
+        for (int u = 0; u < p->n_units; ++u) {
+            const int t0 = worker_of_block(tb.data(), p->n_workers, ud[size_t(u)].block_begin);
+            const int t1 = worker_of_block(tb.data(), p->n_workers,
+                                           ud[size_t(u)].block_begin + ud[size_t(u)].n_blocks - 1);
+            if (t0 != t1) split.push_back(u);
+        }
+        if (!split.empty())
+            e = cudaMemcpy(p->split_units, split.data(), split.size() * sizeof(int32_t),
+                           cudaMemcpyHostToDevice);
+    }
+    if (e != cudaSuccess) {
+        delete p;
+        return fail(KVX_ERR_CUDA, std::string("kvx_plan_create: ") + cudaGetErrorString(e));
+    }
+    p->n_split = int(split.size());
     *out = p;
     g_err.clear();
     return KVX_OK;

@@ -18,15 +18,18 @@
 //  * V rows are rebuilt into A fragments of V^T: lane (g, t) rebuilds tokens 2t, 2t+1, 2t+8, 2t+9,
 //    head dims [g D/8, (g+1) D/8).  O^T += V^T P^T with P^T split into a bf16 part and a bf16
 //    residual part (two MMAs), so P enters with 16 significant bits.
-//  * Exponent escapes are patched in registers in the container's scan order (token-major); the
-//    lane order of both fragment layouts gives each sentinel its rank with a few warp ballots.
+//  * Exponent escapes are patched in the staged words before the rebuild, in the container's scan
+//    order (token-major); the lane order of both fragment layouts gives each sentinel its rank with
+//    a few warp ballots.
 //  * Unit segments that span several workers leave (m, l, acc) partial states that combine_kernel
 //    folds in worker order with merge_state semantics (src/softmax.hpp:16-30), then finalizes like
 //    finalize_state (src/softmax.hpp:32-41: reciprocal, then multiply).
 //
 // The BF16-input variant (BF16IN) is the same template reading [seq, dim] BF16 rows; for the same
-// blocks it produces bit-identical outputs to the XKV variant, because both rebuild identical BF16
-// fragments and run identical arithmetic afterwards.
+// blocks and worker ranges it produces bit-identical outputs to the XKV variant, because both
+// rebuild identical BF16 fragments and run identical arithmetic afterwards.  (Ranges are one block
+// per worker whenever the step has no more blocks than workers; beyond that they are balanced by
+// cost, and escape words count towards an XKV block's cost.)
 #include "attention.cuh"
 
 namespace kvx {
@@ -45,7 +48,6 @@ __device__ __forceinline__ float ex2(float x) {
 
 __host__ __device__ constexpr int round16(int x) { return (x + 15) & ~15; }
 __host__ __device__ constexpr int cmin(int a, int b) { return a < b ? a : b; }
-__host__ __device__ constexpr int cmax(int a, int b) { return a > b ? a : b; }
 
 #ifndef KVX_NSTAGE64
 #define KVX_NSTAGE64 3
@@ -59,8 +61,6 @@ template <int D> struct Cfg {
     static constexpr int NK = D / 8;        // K fragment registers per row (dim pairs)
     static constexpr int DV = D / 8;        // head dims per lane in a V token (= V registers)
     static constexpr int KS = D / 16;       // k-steps of QK = M-tiles of PV
-    static constexpr int NMK = cmax(1, DK / 8);  // sentinel mask words per K row
-    static constexpr int NMV = cmax(1, DV / 8);  // sentinel mask words per V token
     static constexpr bool SPLIT = D > 128;  // rebuild row halves one at a time (register budget)
     static constexpr bool B7REG = D <= 128; // keep the block's base exponents in registers
     static constexpr int ESC_CAP = 1536;    // escape bytes staged per block and tensor
@@ -108,8 +108,11 @@ __device__ __forceinline__ Piece make_piece(const uint8_t *p, uint32_t len) {
     return Piece{reinterpret_cast<const uint8_t *>(lo), uint32_t(hi - lo), uint32_t(a - lo)};
 }
 
+// No "memory" clobber: a clobber would pin every address-taken local in memory around each copy.
+// Ordering against this warp's own shared-memory reads comes from __syncwarp() before a slot is
+// refilled and from the clobber on cp_async_wait() before it is read.
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void *src) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src));
 }
 // One cp.async group per ring stage; a consumer waits until at most `younger` groups issued after
 // the stage it needs are still in flight.  These waits end by themselves: they wait for this
@@ -125,11 +128,16 @@ __device__ __forceinline__ void cp_async_wait(int younger) {
     default: asm volatile("cp.async.wait_group 3;" ::: "memory"); break;
     }
 }
-// The warp copies one piece: lane l moves 16-byte chunks l, l + 32, ...
-__device__ __forceinline__ void copy_piece(uint8_t *dst, const Piece &p, int lane) {
-    const uint32_t d = smem_u32(dst);
+// The warp copies one piece of at most MAXB bytes: lane l moves 16-byte chunks l, l + 32, ...
+template <int MAXB>
+__device__ __forceinline__ void copy_piece(uint8_t *dst, const Piece p, int lane) {
+    constexpr int MAXC = (MAXB / 16 + 31) / 32;
     const uint32_t n = p.alloc >> 4;
-    for (uint32_t j = lane; j < n; j += 32) cp_async16(d + 16 * j, p.src + 16 * j);
+    const uint32_t d = smem_u32(dst) + 16u * uint32_t(lane);
+    const uint8_t *src = p.src + 16 * lane;
+#pragma unroll
+    for (int k = 0; k < MAXC; ++k)
+        if (uint32_t(lane + 32 * k) < n) cp_async16(d + 512u * k, src + 512 * k);
 }
 
 // Section pointers of one tensor of one block.
@@ -188,12 +196,13 @@ __host__ __device__ constexpr uint32_t low_bytes(int nb) {
     return nb >= 4 ? 0xFFFFFFFFu : (1u << (8 * nb)) - 1u;
 }
 
-// Two BF16 values from a sign-replicated sm pair and a code pair (codes in bits 0-3 and 16-19;
-// the other bytes of cw hold small codes that the masks drop).  Exponent = base + code modulo 256
-// like bf16_from_delta's uint8 sum (include/kvexp/bf16.hpp:35-37 of the reference): the carry out
-// of bit 14 is masked away.
+// Two BF16 values from a sign-replicated sm pair and a code pair: exponent offsets in bytes 0 and
+// 2 of cw (bytes 1 and 3 hold other offsets and are masked off).  Offsets are 8-bit wide because
+// an escaped element carries its full offset (exponent - base) mod 256 there.  Exponent = base +
+// offset modulo 256 like bf16_from_delta's uint8 sum (include/kvexp/bf16.hpp:35-37 of the
+// reference): the carry out of bit 14 is masked away.
 __device__ __forceinline__ uint32_t merge(uint32_t sg, uint32_t cw, uint32_t b7) {
-    const uint32_t e = cw * 128u + b7;
+    const uint32_t e = (cw & 0x00FF00FFu) * 128u + b7;
     return (sg & 0x807F807Fu) | (e & 0x7F807F80u);
 }
 
@@ -229,127 +238,11 @@ __device__ __forceinline__ void load_b7v(const uint8_t *base, uint32_t (&b7)[Cfg
     }
 }
 
-// One K row of this lane (DK dims): NK registers of BF16 pairs, and the row's sentinel masks.
-template <int D, int MODE>
-__device__ __forceinline__ void dec_k(const uint8_t *rp, const uint8_t *cp,
-                                      const uint32_t (&b7)[Cfg<D>::NK], uint32_t (&o)[Cfg<D>::NK],
-                                      uint32_t (&mk)[Cfg<D>::NMK]) {
-    using C = Cfg<D>;
-#pragma unroll
-    for (int i = 0; i < C::NMK; ++i) mk[i] = 0u;
-    if (MODE == 0) {
-        lds_words<C::NK>(rp, o);
-        return;
-    }
-    uint32_t S[C::DK / 4];
-    lds_words<C::DK / 4>(rp, S);
-    if (MODE == 4) {
-        constexpr int NW = C::DK / 8;
-        uint32_t N[NW], NL[NW], NH[NW];
-        lds_words<NW>(cp, N);
-#pragma unroll
-        for (int i = 0; i < NW; ++i) {
-            NL[i] = N[i] & 0x0F0F0F0Fu;
-            NH[i] = (N[i] >> 4) & 0x0F0F0F0Fu;
-            mk[i] = sent4(N[i]);
-        }
-#pragma unroll
-        for (int p = 0; p < C::NK; ++p) {
-            const uint32_t sg = prmt(S[p >> 1], 0u, sel_pair(2 * (p & 1)));
-            const uint32_t cw = prmt(NL[p >> 2], NH[p >> 2], sel_code(p & 3));
-            o[p] = merge(sg, cw, b7[p]);
-        }
-    } else {
-        constexpr int NB = C::DK / 4;
-        constexpr int NW = (NB + 3) / 4;
-        uint32_t W[NW], Ck[4][NW];
-        lds_words<NW>(cp, W);
-#pragma unroll
-        for (int i = 0; i < NW; ++i) {
-            mk[i] = sent2(W[i]) & low_bytes(NB);
-#pragma unroll
-            for (int k = 0; k < 4; ++k) Ck[k][i] = (W[i] >> (2 * k)) & 0x03030303u;
-        }
-#pragma unroll
-        for (int p = 0; p < C::NK; ++p) {
-            const int e = 2 * p, i = e >> 4, j = (e & 15) >> 2, k = e & 3;
-            const uint32_t sg = prmt(S[p >> 1], 0u, sel_pair(2 * (p & 1)));
-            const uint32_t cw = prmt(Ck[k][i], Ck[k + 1][i], sel_code(j));
-            o[p] = merge(sg, cw, b7[p]);
-        }
-    }
-}
-
-// Two V tokens (A -> low halves, B -> high halves) of this lane (DV dims): DV registers, one per
-// dim, and the tokens' sentinel masks.
-template <int D, int MODE>
-__device__ __forceinline__ void dec_v(const uint8_t *ra, const uint8_t *rb, const uint8_t *ca,
-                                      const uint8_t *cb, const uint32_t (&b7)[Cfg<D>::DV],
-                                      uint32_t (&o)[Cfg<D>::DV], uint32_t (&ma)[Cfg<D>::NMV],
-                                      uint32_t (&mb)[Cfg<D>::NMV]) {
-    using C = Cfg<D>;
-#pragma unroll
-    for (int i = 0; i < C::NMV; ++i) ma[i] = mb[i] = 0u;
-    if (MODE == 0) {
-        uint32_t RA[C::DV / 2], RB[C::DV / 2];
-        lds_words<C::DV / 2>(ra, RA);
-        lds_words<C::DV / 2>(rb, RB);
-#pragma unroll
-        for (int e = 0; e < C::DV; ++e) o[e] = prmt(RA[e >> 1], RB[e >> 1], (e & 1) ? 0x7632u : 0x5410u);
-        return;
-    }
-    uint32_t SA[C::DV / 4], SB[C::DV / 4];
-    lds_words<C::DV / 4>(ra, SA);
-    lds_words<C::DV / 4>(rb, SB);
-    if (MODE == 4) {
-        constexpr int NB = C::DV / 2;
-        constexpr int NW = (NB + 3) / 4;
-        uint32_t NA[NW], NBw[NW], LA[NW], HA[NW], LB[NW], HB[NW];
-        lds_words<NW>(ca, NA);
-        lds_words<NW>(cb, NBw);
-#pragma unroll
-        for (int i = 0; i < NW; ++i) {
-            LA[i] = NA[i] & 0x0F0F0F0Fu;
-            HA[i] = (NA[i] >> 4) & 0x0F0F0F0Fu;
-            LB[i] = NBw[i] & 0x0F0F0F0Fu;
-            HB[i] = (NBw[i] >> 4) & 0x0F0F0F0Fu;
-            ma[i] = sent4(NA[i]) & low_bytes(NB);
-            mb[i] = sent4(NBw[i]) & low_bytes(NB);
-        }
-#pragma unroll
-        for (int e = 0; e < C::DV; ++e) {
-            const int i = e >> 3, j = (e & 7) >> 1;
-            const uint32_t sg = prmt(SA[e >> 2], SB[e >> 2], sel_cross(e & 3));
-            const uint32_t cw = (e & 1) ? prmt(HA[i], HB[i], sel_code(j)) : prmt(LA[i], LB[i], sel_code(j));
-            o[e] = merge(sg, cw, b7[e]);
-        }
-    } else {
-        constexpr int NB = C::DV / 4;
-        constexpr int NW = (NB + 3) / 4;
-        uint32_t WA[NW], WB[NW], CA[4][NW], CB[4][NW];
-        lds_words<NW>(ca, WA);
-        lds_words<NW>(cb, WB);
-#pragma unroll
-        for (int i = 0; i < NW; ++i) {
-            ma[i] = sent2(WA[i]) & low_bytes(NB);
-            mb[i] = sent2(WB[i]) & low_bytes(NB);
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                CA[k][i] = (WA[i] >> (2 * k)) & 0x03030303u;
-                CB[k][i] = (WB[i] >> (2 * k)) & 0x03030303u;
-            }
-        }
-#pragma unroll
-        for (int e = 0; e < C::DV; ++e) {
-            const int i = e >> 4, j = (e & 15) >> 2, k = e & 3;
-            const uint32_t sg = prmt(SA[e >> 2], SB[e >> 2], sel_cross(e & 3));
-            const uint32_t cw = prmt(CA[k][i], CB[k][i], sel_code(j));
-            o[e] = merge(sg, cw, b7[e]);
-        }
-    }
-}
-
 // ---- escapes -----------------------------------------------------------------------------------
+//
+// A sentinel element takes the next escape word in the block's scan order (token-major).  Its
+// sign/mantissa byte and its exponent offset are written into the staged words before the merge,
+// so the merge rebuilds the escape word exactly.
 
 struct Esc {
     uint32_t run;               // escapes consumed so far in this block
@@ -367,109 +260,361 @@ __device__ __forceinline__ uint32_t esc_word(uint32_t r, const Esc &es, int *sta
                             : uint32_t(__ldg(es.gm + r));
 }
 
-// Replace the low (hi = 0) or high half of register idx.
+__device__ __forceinline__ void set_byte(uint32_t &w, int b, uint32_t v) {
+    const uint32_t sh = 8u * uint32_t(b);
+    w = (w & ~(0xFFu << sh)) | ((v & 0xFFu) << sh);
+}
+__device__ __forceinline__ uint32_t esc_sm(uint32_t h) { return ((h >> 8) & 0x80u) | (h & 0x7Fu); }
+__device__ __forceinline__ uint32_t esc_off(uint32_t h, uint32_t base) {
+    return ((h >> 7) - base) & 0xFFu;
+}
+// Set word c of w[] (c warp-divergent, N compile-time) without dynamic register indexing.
 template <int N>
-__device__ __forceinline__ void put_half(uint32_t (&o)[N], int idx, int hi, uint32_t v) {
-    const uint32_t keep = hi ? 0x0000FFFFu : 0xFFFF0000u;
-    const uint32_t val = hi ? (v << 16) : (v & 0xFFFFu);
+__device__ __forceinline__ void set_byte_of(uint32_t (&w)[N], int c, int b, uint32_t v) {
 #pragma unroll
     for (int i = 0; i < N; ++i)
-        if (i == idx) o[i] = (o[i] & keep) | val;
+        if (i == c) set_byte(w[i], b, v);
 }
 
-template <int N> __device__ __forceinline__ uint32_t count_bits(const uint32_t (&m)[N]) {
-    uint32_t c = 0;
-#pragma unroll
-    for (int i = 0; i < N; ++i) c += __popc(m[i]);
-    return c;
-}
-
-// Sentinels of one K row half (rows 0-7 or 8-15 of the tile).  Scan order inside the half is
-// (row, dim) = (lane, element), since lane 4g + t holds row g, dims [t D/4, (t+1) D/4).
-template <int D, int MODE>
-__device__ __forceinline__ void esc_k(uint32_t (&o)[Cfg<D>::NK], const uint32_t (&mk)[Cfg<D>::NMK],
-                                      Esc &es, int *status) {
-    const uint32_t cnt = count_bits(mk);
-    const uint32_t any = __ballot_sync(FULL, cnt != 0u);
-    if (any == 0u) return;
+// First escape rank of this lane when the scan order is the lane order (K rows) and some lane
+// holds several sentinels: exclusive prefix of the per-lane counts, bit by bit.
+__device__ __forceinline__ uint32_t rank_lanes(uint32_t cnt, Esc &es) {
     const uint32_t lt = lanemask_lt();
-    uint32_t r;
-    if (__ballot_sync(FULL, cnt > 1u) == 0u) {
-        r = es.run + __popc(any & lt);
-        es.run += __popc(any);
-    } else {
-        const int bits = 32 - __clz(__reduce_max_sync(FULL, cnt));
-        uint32_t pre = 0, tot = 0;
-        for (int b = 0; b < bits; ++b) {
-            const uint32_t B = __ballot_sync(FULL, (cnt >> b) & 1u);
-            pre += uint32_t(__popc(B & lt)) << b;
-            tot += uint32_t(__popc(B)) << b;
-        }
-        r = es.run + pre;
-        es.run += tot;
+    const int bits = 32 - __clz(__reduce_max_sync(FULL, cnt));
+    uint32_t pre = 0, tot = 0;
+    for (int b = 0; b < bits; ++b) {
+        const uint32_t B = __ballot_sync(FULL, (cnt >> b) & 1u);
+        pre += uint32_t(__popc(B & lt)) << b;
+        tot += uint32_t(__popc(B)) << b;
     }
-    constexpr int SH = MODE == 4 ? 2 : 1, PER = MODE == 4 ? 8 : 16;
-#pragma unroll
-    for (int i = 0; i < Cfg<D>::NMK; ++i) {
-        uint32_t mm = mk[i];
-        while (mm != 0u) {
-            const int e = i * PER + ((__ffs(mm) - 1) >> SH);
-            put_half(o, e >> 1, e & 1, esc_word(r, es, status));
-            ++r;
-            mm &= mm - 1u;
-        }
-    }
+    const uint32_t r = es.run + pre;
+    es.run += tot;
+    return r;
 }
 
-// Sentinels of one V token half (tokens 0-7 or 8-15).  Lane 4g + t holds tokens 2t (A) and 2t+1
-// (B) of the half, dims [g D/8, (g+1) D/8); scan order inside the half is (t, A/B, g, element).
-template <int D, int MODE>
-__device__ __forceinline__ void esc_v(uint32_t (&o)[Cfg<D>::DV], const uint32_t (&ma)[Cfg<D>::NMV],
-                                      const uint32_t (&mb)[Cfg<D>::NMV], Esc &es, int *status,
-                                      int lane) {
-    const uint32_t ca = count_bits(ma), cb = count_bits(mb);
-    if (__ballot_sync(FULL, (ca | cb) != 0u) == 0u) return;
+// First escape ranks of tokens A and B of a V token half; true when every lane holds at most one
+// sentinel per token.  Lane 4g + t holds tokens 2t (A) and
+// 2t+1 (B) of the half, dims [g D/8, (g+1) D/8); the scan order inside the half is
+// (t, A/B, g, element).
+__device__ __forceinline__ bool rank_tokens(uint32_t ca, uint32_t cb, Esc &es, int lane,
+                                            uint32_t &ra, uint32_t &rb) {
     const uint32_t lt = lanemask_lt();
     const int tig = lane & 3;
     const uint32_t G = 0x11111111u << tig;                // lanes with this t
     const uint32_t L = 0x11111111u * ((1u << tig) - 1u);  // lanes with a smaller t
-    uint32_t ra, rb;
     if (__ballot_sync(FULL, ca > 1u || cb > 1u) == 0u) {
         const uint32_t BA = __ballot_sync(FULL, ca != 0u), BB = __ballot_sync(FULL, cb != 0u);
         const uint32_t before = es.run + __popc(BA & L) + __popc(BB & L);
         ra = before + __popc(BA & G & lt);
         rb = before + __popc(BA & G) + __popc(BB & G & lt);
         es.run += __popc(BA) + __popc(BB);
-    } else {
-        const int bits = 32 - __clz(__reduce_max_sync(FULL, ca > cb ? ca : cb));
-        uint32_t sl = 0, sag = 0, saglt = 0, sbglt = 0, tot = 0;
-        for (int b = 0; b < bits; ++b) {
-            const uint32_t BA = __ballot_sync(FULL, (ca >> b) & 1u);
-            const uint32_t BB = __ballot_sync(FULL, (cb >> b) & 1u);
-            sl += uint32_t(__popc(BA & L) + __popc(BB & L)) << b;
-            sag += uint32_t(__popc(BA & G)) << b;
-            saglt += uint32_t(__popc(BA & G & lt)) << b;
-            sbglt += uint32_t(__popc(BB & G & lt)) << b;
-            tot += uint32_t(__popc(BA) + __popc(BB)) << b;
-        }
-        ra = es.run + sl + saglt;
-        rb = es.run + sl + sag + sbglt;
-        es.run += tot;
+        return true;
     }
-    constexpr int SH = MODE == 4 ? 2 : 1, PER = MODE == 4 ? 8 : 16;
+    const int bits = 32 - __clz(__reduce_max_sync(FULL, ca > cb ? ca : cb));
+    uint32_t sl = 0, sag = 0, saglt = 0, sbglt = 0, tot = 0;
+    for (int b = 0; b < bits; ++b) {
+        const uint32_t BA = __ballot_sync(FULL, (ca >> b) & 1u);
+        const uint32_t BB = __ballot_sync(FULL, (cb >> b) & 1u);
+        sl += uint32_t(__popc(BA & L) + __popc(BB & L)) << b;
+        sag += uint32_t(__popc(BA & G)) << b;
+        saglt += uint32_t(__popc(BA & G & lt)) << b;
+        sbglt += uint32_t(__popc(BB & G & lt)) << b;
+        tot += uint32_t(__popc(BA) + __popc(BB)) << b;
+    }
+    ra = es.run + sl + saglt;
+    rb = es.run + sl + sag + sbglt;
+    es.run += tot;
+    return false;
+}
+
+// ---- decode ------------------------------------------------------------------------------------
+
+// One K row of this lane (DK dims starting at c0): NK registers of BF16 pairs (dims c0+2p,
+// c0+2p+1).  rp: row's sm (or raw) bytes, cp: row's codes, bp: the block's base exponents of the
+// same dims.  The caller calls rows in scan order; `valid` is false for rows past the tile's end.
+template <int D, int MODE>
+__device__ __forceinline__ void dec_k(const uint8_t *rp, const uint8_t *cp, const uint8_t *bp,
+                                      const uint32_t (&b7)[Cfg<D>::NK], bool valid, Esc &es,
+                                      int *status, uint32_t (&o)[Cfg<D>::NK]) {
+    using C = Cfg<D>;
+    if (MODE == 0) {
+        lds_words<C::NK>(rp, o);
+        return;
+    }
+    uint32_t S[C::DK / 4];
+    lds_words<C::DK / 4>(rp, S);
+    if (MODE == 4) {
+        constexpr int NW = C::DK / 8;
+        uint32_t N[NW], NL[NW], NH[NW], mk[NW];
+        lds_words<NW>(cp, N);
+        uint32_t cnt = 0;
 #pragma unroll
-    for (int i = 0; i < Cfg<D>::NMV; ++i) {
-        uint32_t mm = ma[i];
-        while (mm != 0u) {
-            put_half(o, i * PER + ((__ffs(mm) - 1) >> SH), 0, esc_word(ra, es, status));
-            ++ra;
-            mm &= mm - 1u;
+        for (int i = 0; i < NW; ++i) {
+            NL[i] = N[i] & 0x0F0F0F0Fu;
+            NH[i] = (N[i] >> 4) & 0x0F0F0F0Fu;
+            mk[i] = valid ? sent4(N[i]) : 0u;
+            cnt += __popc(mk[i]);
         }
-        mm = mb[i];
-        while (mm != 0u) {
-            put_half(o, i * PER + ((__ffs(mm) - 1) >> SH), 1, esc_word(rb, es, status));
-            ++rb;
-            mm &= mm - 1u;
+        const uint32_t any = __ballot_sync(FULL, cnt != 0u);
+        if (any != 0u) {
+            auto patch = [&](int i, int k, uint32_t h) {  // element 8i + k
+                const uint32_t off = esc_off(h, bp[8 * i + k]);
+                if (k & 1) set_byte(NH[i], k >> 1, off);
+                else set_byte(NL[i], k >> 1, off);
+                if (k & 4) set_byte(S[2 * i + 1], k & 3, esc_sm(h));
+                else set_byte(S[2 * i], k & 3, esc_sm(h));
+            };
+            if (__ballot_sync(FULL, cnt > 1u) == 0u) {
+                // at most one sentinel per lane: straight-line
+                const uint32_t r = es.run + __popc(any & lanemask_lt());
+                es.run += __popc(any);
+                if (cnt != 0u) {
+                    const uint32_t h = esc_word(r, es, status);
+#pragma unroll
+                    for (int i = 0; i < NW; ++i)
+                        if (mk[i] != 0u) patch(i, (__ffs(mk[i]) - 1) >> 2, h);
+                }
+            } else {
+                uint32_t r = rank_lanes(cnt, es);
+#pragma unroll
+                for (int i = 0; i < NW; ++i) {
+                    uint32_t mm = mk[i];
+                    while (mm != 0u) {
+                        const int k = (__ffs(mm) - 1) >> 2;
+                        mm &= mm - 1u;
+                        patch(i, k, esc_word(r++, es, status));
+                    }
+                }
+            }
+        }
+#pragma unroll
+        for (int p = 0; p < C::NK; ++p) {
+            const uint32_t sg = prmt(S[p >> 1], 0u, sel_pair(2 * (p & 1)));
+            const uint32_t cw = prmt(NL[p >> 2], NH[p >> 2], sel_code(p & 3));
+            o[p] = merge(sg, cw, b7[p]);
+        }
+    } else {
+        constexpr int NB = C::DK / 4;
+        constexpr int NW = (NB + 3) / 4;
+        uint32_t W[NW], Ck[4][NW], mk[NW];
+        lds_words<NW>(cp, W);
+        uint32_t cnt = 0;
+#pragma unroll
+        for (int i = 0; i < NW; ++i) {
+            mk[i] = valid ? (sent2(W[i]) & low_bytes(NB)) : 0u;
+            cnt += __popc(mk[i]);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) Ck[k][i] = (W[i] >> (2 * k)) & 0x03030303u;
+        }
+        const uint32_t any = __ballot_sync(FULL, cnt != 0u);
+        if (any != 0u) {
+            auto patch = [&](int i, int e, uint32_t h) {  // element 16i + e
+                const int j = e >> 2, k = e & 3;
+                const uint32_t off = esc_off(h, bp[16 * i + e]);
+#pragma unroll
+                for (int c = 0; c < 4; ++c)
+                    if (c == k) set_byte(Ck[c][i], j, off);
+#pragma unroll
+                for (int c = 0; c < 4 && 4 * i + c < C::DK / 4; ++c)
+                    if (c == j) set_byte(S[4 * i + c], k, esc_sm(h));
+            };
+            if (__ballot_sync(FULL, cnt > 1u) == 0u) {
+                const uint32_t r = es.run + __popc(any & lanemask_lt());
+                es.run += __popc(any);
+                if (cnt != 0u) {
+                    const uint32_t h = esc_word(r, es, status);
+#pragma unroll
+                    for (int i = 0; i < NW; ++i)
+                        if (mk[i] != 0u) patch(i, (__ffs(mk[i]) - 1) >> 1, h);
+                }
+            } else {
+                uint32_t r = rank_lanes(cnt, es);
+#pragma unroll
+                for (int i = 0; i < NW; ++i) {
+                    uint32_t mm = mk[i];
+                    while (mm != 0u) {
+                        const int e = (__ffs(mm) - 1) >> 1;
+                        mm &= mm - 1u;
+                        patch(i, e, esc_word(r++, es, status));
+                    }
+                }
+            }
+        }
+#pragma unroll
+        for (int p = 0; p < C::NK; ++p) {
+            const int e = 2 * p, i = e >> 4, j = (e & 15) >> 2, k = e & 3;
+            const uint32_t sg = prmt(S[p >> 1], 0u, sel_pair(2 * (p & 1)));
+            const uint32_t cw = prmt(Ck[k][i], Ck[k + 1][i], sel_code(j));
+            o[p] = merge(sg, cw, b7[p]);
+        }
+    }
+}
+
+// Two V tokens (A -> low halves, B -> high halves) of this lane (DV dims): DV registers, one per
+// dim.  va/vb: the tokens are inside the tile; bp: base exponents of the lane's dims.
+template <int D, int MODE>
+__device__ __forceinline__ void dec_v(const uint8_t *ra, const uint8_t *rb, const uint8_t *ca,
+                                      const uint8_t *cb, const uint8_t *bp,
+                                      const uint32_t (&b7)[Cfg<D>::DV], bool va, bool vb, Esc &es,
+                                      int *status, int lane, uint32_t (&o)[Cfg<D>::DV]) {
+    using C = Cfg<D>;
+    if (MODE == 0) {
+        uint32_t RA[C::DV / 2], RB[C::DV / 2];
+        lds_words<C::DV / 2>(ra, RA);
+        lds_words<C::DV / 2>(rb, RB);
+#pragma unroll
+        for (int e = 0; e < C::DV; ++e) o[e] = prmt(RA[e >> 1], RB[e >> 1], (e & 1) ? 0x7632u : 0x5410u);
+        return;
+    }
+    uint32_t SA[C::DV / 4], SB[C::DV / 4];
+    lds_words<C::DV / 4>(ra, SA);
+    lds_words<C::DV / 4>(rb, SB);
+    if (MODE == 4) {
+        constexpr int NB = C::DV / 2;
+        constexpr int NW = (NB + 3) / 4;
+        uint32_t NA[NW], NBw[NW], LA[NW], HA[NW], LB[NW], HB[NW], ma[NW], mb[NW];
+        lds_words<NW>(ca, NA);
+        lds_words<NW>(cb, NBw);
+        uint32_t cna = 0, cnb = 0;
+#pragma unroll
+        for (int i = 0; i < NW; ++i) {
+            LA[i] = NA[i] & 0x0F0F0F0Fu;
+            HA[i] = (NA[i] >> 4) & 0x0F0F0F0Fu;
+            LB[i] = NBw[i] & 0x0F0F0F0Fu;
+            HB[i] = (NBw[i] >> 4) & 0x0F0F0F0Fu;
+            ma[i] = va ? (sent4(NA[i]) & low_bytes(NB)) : 0u;
+            mb[i] = vb ? (sent4(NBw[i]) & low_bytes(NB)) : 0u;
+            cna += __popc(ma[i]);
+            cnb += __popc(mb[i]);
+        }
+        if (__ballot_sync(FULL, (cna | cnb) != 0u) != 0u) {
+            auto patch_a = [&](int i, int k, uint32_t h) {  // element 8i + k of token A
+                const int e = 8 * i + k;
+                const uint32_t off = esc_off(h, bp[e]);
+                if (k & 1) set_byte(HA[i], k >> 1, off);
+                else set_byte(LA[i], k >> 1, off);
+                set_byte_of(SA, e >> 2, e & 3, esc_sm(h));
+            };
+            auto patch_b = [&](int i, int k, uint32_t h) {
+                const int e = 8 * i + k;
+                const uint32_t off = esc_off(h, bp[e]);
+                if (k & 1) set_byte(HB[i], k >> 1, off);
+                else set_byte(LB[i], k >> 1, off);
+                set_byte_of(SB, e >> 2, e & 3, esc_sm(h));
+            };
+            uint32_t r_a, r_b;
+            if (rank_tokens(cna, cnb, es, lane, r_a, r_b)) {
+                if (cna != 0u) {
+                    const uint32_t h = esc_word(r_a, es, status);
+#pragma unroll
+                    for (int i = 0; i < NW; ++i)
+                        if (ma[i] != 0u) patch_a(i, (__ffs(ma[i]) - 1) >> 2, h);
+                }
+                if (cnb != 0u) {
+                    const uint32_t h = esc_word(r_b, es, status);
+#pragma unroll
+                    for (int i = 0; i < NW; ++i)
+                        if (mb[i] != 0u) patch_b(i, (__ffs(mb[i]) - 1) >> 2, h);
+                }
+            } else {
+#pragma unroll
+                for (int i = 0; i < NW; ++i) {
+                    uint32_t mm = ma[i];
+                    while (mm != 0u) {
+                        const int k = (__ffs(mm) - 1) >> 2;
+                        mm &= mm - 1u;
+                        patch_a(i, k, esc_word(r_a++, es, status));
+                    }
+                    mm = mb[i];
+                    while (mm != 0u) {
+                        const int k = (__ffs(mm) - 1) >> 2;
+                        mm &= mm - 1u;
+                        patch_b(i, k, esc_word(r_b++, es, status));
+                    }
+                }
+            }
+        }
+#pragma unroll
+        for (int e = 0; e < C::DV; ++e) {
+            const int i = e >> 3, j = (e & 7) >> 1;
+            const uint32_t sg = prmt(SA[e >> 2], SB[e >> 2], sel_cross(e & 3));
+            const uint32_t cw = (e & 1) ? prmt(HA[i], HB[i], sel_code(j)) : prmt(LA[i], LB[i], sel_code(j));
+            o[e] = merge(sg, cw, b7[e]);
+        }
+    } else {
+        constexpr int NB = C::DV / 4;
+        constexpr int NW = (NB + 3) / 4;
+        uint32_t WA[NW], WB[NW], CA[4][NW], CB[4][NW], ma[NW], mb[NW];
+        lds_words<NW>(ca, WA);
+        lds_words<NW>(cb, WB);
+        uint32_t cna = 0, cnb = 0;
+#pragma unroll
+        for (int i = 0; i < NW; ++i) {
+            ma[i] = va ? (sent2(WA[i]) & low_bytes(NB)) : 0u;
+            mb[i] = vb ? (sent2(WB[i]) & low_bytes(NB)) : 0u;
+            cna += __popc(ma[i]);
+            cnb += __popc(mb[i]);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                CA[k][i] = (WA[i] >> (2 * k)) & 0x03030303u;
+                CB[k][i] = (WB[i] >> (2 * k)) & 0x03030303u;
+            }
+        }
+        if (__ballot_sync(FULL, (cna | cnb) != 0u) != 0u) {
+            auto patch_a = [&](int i, int e4, uint32_t h) {  // element 16i + e4 of token A
+                const int e = 16 * i + e4;
+                const uint32_t off = esc_off(h, bp[e]);
+#pragma unroll
+                for (int c = 0; c < 4; ++c)
+                    if (c == (e & 3)) set_byte(CA[c][i], (e & 15) >> 2, off);
+                set_byte_of(SA, e >> 2, e & 3, esc_sm(h));
+            };
+            auto patch_b = [&](int i, int e4, uint32_t h) {
+                const int e = 16 * i + e4;
+                const uint32_t off = esc_off(h, bp[e]);
+#pragma unroll
+                for (int c = 0; c < 4; ++c)
+                    if (c == (e & 3)) set_byte(CB[c][i], (e & 15) >> 2, off);
+                set_byte_of(SB, e >> 2, e & 3, esc_sm(h));
+            };
+            uint32_t r_a, r_b;
+            if (rank_tokens(cna, cnb, es, lane, r_a, r_b)) {
+                if (cna != 0u) {
+                    const uint32_t h = esc_word(r_a, es, status);
+#pragma unroll
+                    for (int i = 0; i < NW; ++i)
+                        if (ma[i] != 0u) patch_a(i, (__ffs(ma[i]) - 1) >> 1, h);
+                }
+                if (cnb != 0u) {
+                    const uint32_t h = esc_word(r_b, es, status);
+#pragma unroll
+                    for (int i = 0; i < NW; ++i)
+                        if (mb[i] != 0u) patch_b(i, (__ffs(mb[i]) - 1) >> 1, h);
+                }
+            } else {
+#pragma unroll
+                for (int i = 0; i < NW; ++i) {
+                    uint32_t mm = ma[i];
+                    while (mm != 0u) {
+                        const int e4 = (__ffs(mm) - 1) >> 1;
+                        mm &= mm - 1u;
+                        patch_a(i, e4, esc_word(r_a++, es, status));
+                    }
+                    mm = mb[i];
+                    while (mm != 0u) {
+                        const int e4 = (__ffs(mm) - 1) >> 1;
+                        mm &= mm - 1u;
+                        patch_b(i, e4, esc_word(r_b++, es, status));
+                    }
+                }
+            }
+        }
+#pragma unroll
+        for (int e = 0; e < C::DV; ++e) {
+            const int i = e >> 4, j = (e & 15) >> 2, k = e & 3;
+            const uint32_t sg = prmt(SA[e >> 2], SB[e >> 2], sel_cross(e & 3));
+            const uint32_t cw = prmt(CA[k][i], CB[k][i], sel_code(j));
+            o[e] = merge(sg, cw, b7[e]);
         }
     }
 }
@@ -502,19 +647,9 @@ __device__ __forceinline__ void qk_tile(const TileView &tv, const uint32_t (&b7r
     for (int p = 0; p < C::NK; ++p) b7[p] = b7r[p];
     if (!C::B7REG && MODE != 0) load_b7k<D>(tv.k_base, b7);
     if (!C::SPLIT) {
-        uint32_t ka0[C::NK], ka1[C::NK], m0[C::NMK], m1[C::NMK];
-        dec_k<D, MODE>(r0, q0, b7, ka0, m0);
-        dec_k<D, MODE>(r0 + 8 * RS, q0 + 8 * CS, b7, ka1, m1);
-        if (MODE != 0) {
-            if (gi >= tv.rows)
-#pragma unroll
-                for (int i = 0; i < C::NMK; ++i) m0[i] = 0u;
-            if (gi + 8 >= tv.rows)
-#pragma unroll
-                for (int i = 0; i < C::NMK; ++i) m1[i] = 0u;
-            esc_k<D, MODE>(ka0, m0, es, status);
-            esc_k<D, MODE>(ka1, m1, es, status);
-        }
+        uint32_t ka0[C::NK], ka1[C::NK];
+        dec_k<D, MODE>(r0, q0, tv.k_base, b7, gi < tv.rows, es, status, ka0);
+        dec_k<D, MODE>(r0 + 8 * RS, q0 + 8 * CS, tv.k_base, b7, gi + 8 < tv.rows, es, status, ka1);
 #pragma unroll
         for (int k = 0; k < C::KS; ++k)
             mma_bf16(s[0], s[1], s[2], s[3], ka0[2 * k], ka1[2 * k], ka0[2 * k + 1], ka1[2 * k + 1],
@@ -522,14 +657,9 @@ __device__ __forceinline__ void qk_tile(const TileView &tv, const uint32_t (&b7r
     } else {
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
-            uint32_t ka[C::NK], mk[C::NMK];
-            dec_k<D, MODE>(r0 + 8 * h * RS, q0 + 8 * h * CS, b7, ka, mk);
-            if (MODE != 0) {
-                if (gi + 8 * h >= tv.rows)
-#pragma unroll
-                    for (int i = 0; i < C::NMK; ++i) mk[i] = 0u;
-                esc_k<D, MODE>(ka, mk, es, status);
-            }
+            uint32_t ka[C::NK];
+            dec_k<D, MODE>(r0 + 8 * h * RS, q0 + 8 * h * CS, tv.k_base, b7, gi + 8 * h < tv.rows, es,
+                           status, ka);
 #pragma unroll
             for (int k = 0; k < C::KS; ++k) {
                 if (h == 0)
@@ -555,17 +685,8 @@ __device__ __forceinline__ void v_half(const TileView &tv, const uint32_t (&b7)[
     const int t = 2 * tig + 8 * h;
     const uint8_t *r0 = tv.v_rows + t * RS + (MODE == 0 ? 2 * v0 : v0);
     const uint8_t *q0 = tv.v_codes + t * CS + v0 * MODE / 8;
-    uint32_t ma[C::NMV], mb[C::NMV];
-    dec_v<D, MODE>(r0, r0 + RS, q0, q0 + CS, b7, va, ma, mb);
-    if (MODE != 0) {
-        if (t >= tv.rows)
-#pragma unroll
-            for (int i = 0; i < C::NMV; ++i) ma[i] = 0u;
-        if (t + 1 >= tv.rows)
-#pragma unroll
-            for (int i = 0; i < C::NMV; ++i) mb[i] = 0u;
-        esc_v<D, MODE>(va, ma, mb, es, status, lane);
-    }
+    dec_v<D, MODE>(r0, r0 + RS, q0, q0 + CS, tv.v_base, b7, t < tv.rows, t + 1 < tv.rows, es, status,
+                   lane, va);
     if (tv.rows < TT) {
         const uint32_t keep = (t < tv.rows ? 0x0000FFFFu : 0u) | (t + 1 < tv.rows ? 0xFFFF0000u : 0u);
 #pragma unroll
@@ -632,7 +753,7 @@ struct Walker {
     int64_t fb, fb1;
     FlatBlock cur, nxt;
     int unit, nunit;
-    __device__ void init(const AttnArgs &a, int64_t b0, int64_t b1) {
+    __device__ __forceinline__ void init(const AttnArgs &a, int64_t b0, int64_t b1) {
         fb = b0;
         fb1 = b1;
         cur = load_flat(a.flat, fb);
@@ -643,7 +764,7 @@ struct Walker {
             nunit = __ldg(a.flat_unit + fb + 1);
         }
     }
-    __device__ void next(const AttnArgs &a) {
+    __device__ __forceinline__ void next(const AttnArgs &a) {
         ++fb;
         if (fb < fb1) {
             cur = nxt;
@@ -663,27 +784,28 @@ template <int D, bool BF16IN> struct Producer {
     int tile = 0, stage = 0, bseq = 0, unit = -1;
     const uint8_t *kb = nullptr, *vb = nullptr;
 
-    __device__ static void tensor(uint8_t *dst, const Sections &s, int mode, int tile, int rows,
+    __device__ __forceinline__ static void tensor(uint8_t *dst, const Sections &s, int mode, int tile, int rows,
                                   int lane) {
         const int t0 = tile * TT;
         if (BF16IN || mode == 0) {
-            copy_piece(dst, make_piece(s.rows + size_t(t0) * (2 * D), uint32_t(rows * 2 * D)), lane);
+            copy_piece<TT * 2 * D + 16>(
+                dst, make_piece(s.rows + size_t(t0) * (2 * D), uint32_t(rows * 2 * D)), lane);
         } else {
-            copy_piece(dst, make_piece(s.rows + size_t(t0) * D, uint32_t(rows * D)), lane);
-            copy_piece(dst + C::CODE_OFF,
-                       make_piece(s.codes + size_t(t0) * D * mode / 8, uint32_t(rows * D * mode / 8)),
-                       lane);
+            copy_piece<TT * D + 16>(dst, make_piece(s.rows + size_t(t0) * D, uint32_t(rows * D)), lane);
+            copy_piece<TT * D / 2 + 16>(
+                dst + C::CODE_OFF,
+                make_piece(s.codes + size_t(t0) * D * mode / 8, uint32_t(rows * D * mode / 8)), lane);
         }
     }
-    __device__ static void meta(uint8_t *base, uint8_t *escs, const Sections &s, int nesc, int lane) {
-        copy_piece(base, make_piece(s.rows - D, D), lane);
+    __device__ __forceinline__ static void meta(uint8_t *base, uint8_t *escs, const Sections &s, int nesc, int lane) {
+        copy_piece<D + 32>(base, make_piece(s.rows - D, D), lane);
         const Piece e = make_piece(s.esc, uint32_t(2 * nesc));
-        if (esc_staged<D>(e, nesc)) copy_piece(escs, e, lane);
+        if (esc_staged<D>(e, nesc)) copy_piece<C::ESCB>(escs, e, lane);
     }
 
     // Issue tiles while a ring slot is free; a block start waits until the consumer is at most
     // one block behind, so a meta slot is never overwritten while in use.
-    __device__ void produce(const AttnArgs &a, uint8_t *ring, uint8_t *metas, int c_stage,
+    __device__ __forceinline__ void produce(const AttnArgs &a, uint8_t *ring, uint8_t *metas, int c_stage,
                             int64_t c_fb, int lane) {
         while (w.fb < w.fb1 && stage - c_stage < C::NSTAGE) {
             if (tile == 0 && w.fb - c_fb >= 2) break;
@@ -910,7 +1032,8 @@ __global__ void __launch_bounds__(32 * Cfg<D>::WARPS, 1) attn_kernel(const AttnA
     using C = Cfg<D>;
     extern __shared__ __align__(128) uint8_t smem[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int wk = blockIdx.x * C::WARPS + warp;
+    // consecutive workers on different SMs: neighbouring ranges often share a cost profile
+    const int wk = warp * gridDim.x + blockIdx.x;
     if (wk >= a.n_workers) return;
     const int64_t fb0 = a.range_begin[wk], fb1 = a.range_begin[wk + 1];
     if (fb0 >= fb1) return;
@@ -950,6 +1073,51 @@ __global__ void __launch_bounds__(256) combine_kernel(const CombineArgs a) {
         const float inv = __frcp_rn(l);
         unit.out[size_t(g) * unit.q_stride + d] = __fmul_rn(acc, inv);
     }
+}
+
+// ---- worker ranges -----------------------------------------------------------------------------
+
+// Cost of one flat block for the worker split: 8 per attended token plus kEscCost per escape word
+// (a worker's time grows with its tokens and, on escape-dense blocks, with its escape words).
+constexpr uint32_t kEscCost = 2;
+__device__ __forceinline__ uint64_t block_cost(const FlatBlock &b) {
+    return 8ull * b.valid + kEscCost * (uint64_t(b.k_nesc) + b.v_nesc);
+}
+
+// One CTA: range_begin[w] = first block whose cost prefix reaches w * total / n_workers.
+__global__ void __launch_bounds__(1024) split_kernel(const FlatBlock *flat, int64_t n, int nw,
+                                                     int64_t *range_begin) {
+    __shared__ unsigned long long part[1024];
+    const int t = threadIdx.x, T = blockDim.x;
+    const int64_t chunk = (n + T - 1) / T;
+    const int64_t lo = min(n, t * chunk), hi = min(n, lo + chunk);
+    unsigned long long sum = 0;
+    for (int64_t b = lo; b < hi; ++b) sum += block_cost(load_flat(flat, b));
+    part[t] = sum;
+    __syncthreads();
+    for (int o = 1; o < T; o <<= 1) {  // inclusive scan
+        const unsigned long long v = t >= o ? part[t - o] : 0ull;
+        __syncthreads();
+        part[t] += v;
+        __syncthreads();
+    }
+    const unsigned long long total = part[T - 1];
+    unsigned long long c = part[t] - sum;  // cost before block lo
+    if (t == 0) {
+        range_begin[0] = 0;
+        range_begin[nw] = n;
+        for (int w0 = 1; w0 < nw && uint64_t(w0) * total / nw == 0; ++w0) range_begin[w0] = 0;
+    }
+    // worker w starts after the block whose cost interval (c, c + cost] holds w * total / nw
+    int w = int(c * uint64_t(nw) / (total ? total : 1));
+    for (int64_t b = lo; b < hi; ++b) {
+        const unsigned long long cn = c + block_cost(load_flat(flat, b));
+        while (w < nw && uint64_t(w) * total / nw <= c) ++w;
+        while (w < nw && uint64_t(w) * total / nw <= cn) range_begin[w++] = b + 1;
+        c = cn;
+    }
+    if (t == 0 && total == 0)
+        for (int w2 = 1; w2 < nw; ++w2) range_begin[w2] = n;
 }
 
 template <int D> void configure(bool bf16) {
@@ -1010,6 +1178,12 @@ cudaError_t launch_attention(int dim, bool bf16_input, const AttnArgs &a, int gr
     case 256: return launch_d<256>(bf16_input, a, grid, s);
     default: return cudaErrorInvalidValue;
     }
+}
+
+cudaError_t launch_split(const FlatBlock *flat, int64_t n_blocks, int n_workers, int64_t *range_begin,
+                         cudaStream_t s) {
+    split_kernel<<<1, 1024, 0, s>>>(flat, n_blocks, n_workers, range_begin);
+    return cudaGetLastError();
 }
 
 cudaError_t launch_combine(int dim, const CombineArgs &a, int n_split, cudaStream_t s) {

@@ -68,6 +68,9 @@ __host__ __device__ inline int worker_of_block(const int64_t *range_begin, int n
 // Launchers (attention.cu).  Return cudaError_t of the launch.
 cudaError_t launch_attention(int dim, bool bf16_input, const AttnArgs &a, int grid, cudaStream_t s);
 cudaError_t launch_combine(int dim, const CombineArgs &a, int n_split, cudaStream_t s);
+// Cost-balanced worker ranges over the flat block list: range_begin[0..n_workers].
+cudaError_t launch_split(const FlatBlock *flat, int64_t n_blocks, int n_workers, int64_t *range_begin,
+                         cudaStream_t s);
 int attention_workers_per_cta(int dim);
 size_t attention_smem_bytes(int dim);
 bool attention_dim_supported(int dim);
