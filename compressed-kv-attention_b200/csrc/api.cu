@@ -968,3 +968,192 @@ extern "C" int kvx_hbm_read_probe(const void *buf, size_t bytes, int reps, doubl
     *gbps = double(n16) * 16.0 / (double(best) * 1e-3) / 1e9;
     return KVX_OK;
 }
+
+// ---- decode attention without allocation ---------------------------------------------------
+//
+// kvx_attention_decode_noalloc is for callers that must not allocate GPU memory once they are
+// running: serving engines that reserve the device's memory for their KV-cache pool at start-up
+// and treat any later cudaMalloc as a failure, and decode loops that cannot afford the
+// device-wide synchronisation that cudaFree implies.  All of its scratch (the flat block list,
+// worker ranges, partial softmax states and the error word) lives in the file-scope device array
+// below, which every device that loads this library holds until the process exits.
+
+namespace kvx {
+namespace {
+constexpr size_t kNoAllocScratchBytes = size_t(8) << 20;  // 8 MiB per device
+constexpr int kNoAllocMaxBlocks = 8192;                   // XKV blocks per tensor
+constexpr int kNoAllocMaxQueries = 64;                    // queries per call (8 groups of 8)
+constexpr int kNoAllocMaxWorkers = 4096;
+}  // namespace
+}  // namespace kvx
+
+static __device__ __align__(256) unsigned char kvx_noalloc_scratch[kvx::kNoAllocScratchBytes];
+
+namespace kvx {
+namespace {
+
+size_t up256(size_t x) { return (x + 255) & ~size_t(255); }
+
+// Device address of the scratch array on the current device.  The array's name in host code is
+// only a host-side stand-in, so the address comes from cudaGetSymbolAddress, looked up once per
+// device (the first call on a device also loads the module there).
+int noalloc_scratch(uint8_t **out) {
+    static std::mutex mu;
+    static uint8_t *addr[64] = {};
+    int dev = 0;
+    KVX_CUDA(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64) return fail(KVX_ERR_RUNTIME, "kvx_attention_decode_noalloc: device index out of range");
+    std::lock_guard<std::mutex> lock(mu);
+    if (addr[dev] == nullptr) {
+        void *p = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&p, kvx_noalloc_scratch);
+        if (e != cudaSuccess)
+            return fail(KVX_ERR_CUDA,
+                        std::string("kvx_attention_decode_noalloc: cudaGetSymbolAddress: ") +
+                            cudaGetErrorString(e));
+        addr[dev] = static_cast<uint8_t *>(p);
+    }
+    *out = addr[dev];
+    return KVX_OK;
+}
+
+}  // namespace
+}  // namespace kvx
+
+extern "C" int kvx_attention_decode_noalloc(const uint16_t *q, const uint8_t *k_xkv, size_t k_bytes,
+                                            const kvx_block *k_index, const uint8_t *v_xkv,
+                                            size_t v_bytes, const kvx_block *v_index, int n_blocks,
+                                            float *out, int n_q, int dim, int seq, void *stream) {
+    const char *fn = "kvx_attention_decode_noalloc: ";
+    if (q == nullptr || k_xkv == nullptr || v_xkv == nullptr || k_index == nullptr ||
+        v_index == nullptr || out == nullptr)
+        return fail(KVX_ERR_INVALID_ARGUMENT, std::string(fn) + "null pointer");
+    if (n_q <= 0 || dim <= 0 || seq <= 0 || n_blocks <= 0 || k_bytes == 0 || v_bytes == 0)
+        return fail(KVX_ERR_INVALID_ARGUMENT, std::string(fn) + "sizes must be positive");
+    if (n_q > kNoAllocMaxQueries)
+        return fail(KVX_ERR_INVALID_ARGUMENT,
+                    std::string(fn) + "n_q exceeds the limit of 64 queries per call");
+    if (n_blocks > kNoAllocMaxBlocks)
+        return fail(KVX_ERR_INVALID_ARGUMENT,
+                    std::string(fn) + "n_blocks exceeds the scratch limit of 8192 blocks per tensor");
+    if (!attention_dim_supported(dim))
+        return fail(KVX_ERR_UNSUPPORTED,
+                    std::string(fn) + "head_dim must be 32, 64, 128 or 256 for the GPU kernels");
+    if (int rc = check_device()) return rc;
+    if (!is_device_ptr(q) || !is_device_ptr(k_xkv) || !is_device_ptr(v_xkv) ||
+        !is_device_ptr(k_index) || !is_device_ptr(v_index) || !is_device_ptr(out))
+        return fail(KVX_ERR_INVALID_ARGUMENT, std::string(fn) + "every pointer must be device memory");
+    if (((reinterpret_cast<uintptr_t>(k_xkv) | reinterpret_cast<uintptr_t>(v_xkv)) & 15u) ||
+        (reinterpret_cast<uintptr_t>(q) & 3u) || (reinterpret_cast<uintptr_t>(out) & 7u))
+        return fail(KVX_ERR_INVALID_ARGUMENT,
+                    std::string(fn) + "K/V blobs must be 16-byte aligned, q 4-byte, out 8-byte");
+    uint8_t *base = nullptr;
+    if (int rc = noalloc_scratch(&base)) return rc;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+
+    // Scratch layout (256-byte aligned pieces): status | units | unit descriptors | block
+    // begins | split units | flat blocks | flat units | worker ranges | partial states.
+    const int groups = (n_q + 7) / 8;
+    const int64_t total = int64_t(groups) * n_blocks;
+    size_t off = 0;
+    auto take = [&](size_t bytes) {
+        const size_t o = off;
+        off += up256(bytes);
+        return base + o;
+    };
+    int *status = reinterpret_cast<int *>(take(2 * sizeof(int)));
+    UnitDev *d_units = reinterpret_cast<UnitDev *>(take(kNoAllocMaxQueries / 8 * sizeof(UnitDev)));
+    kvx_unit *d_vu = reinterpret_cast<kvx_unit *>(take(kNoAllocMaxQueries / 8 * sizeof(kvx_unit)));
+    int64_t *d_begin = reinterpret_cast<int64_t *>(take(kNoAllocMaxQueries / 8 * sizeof(int64_t)));
+    int32_t *d_split = reinterpret_cast<int32_t *>(take(kNoAllocMaxQueries / 8 * sizeof(int32_t)));
+    FlatBlock *d_flat = reinterpret_cast<FlatBlock *>(
+        take(size_t(kNoAllocMaxQueries / 8) * kNoAllocMaxBlocks * sizeof(FlatBlock)));
+    int32_t *d_flat_unit = reinterpret_cast<int32_t *>(
+        take(size_t(kNoAllocMaxQueries / 8) * kNoAllocMaxBlocks * sizeof(int32_t)));
+    int64_t *d_range = reinterpret_cast<int64_t *>(take((kNoAllocMaxWorkers + 1) * sizeof(int64_t)));
+    float *d_partials = reinterpret_cast<float *>(base + off);
+    const size_t per_worker = 2 * size_t(partial_stride(dim)) * sizeof(float);
+    const int64_t fit = int64_t((kNoAllocScratchBytes - off) / per_worker);
+    const int per_cta = attention_workers_per_cta(dim);
+    const int n_workers = int(std::min<int64_t>(
+        std::min<int64_t>(total, int64_t(sm_count()) * per_cta), std::min<int64_t>(fit, kNoAllocMaxWorkers)));
+
+    // Host-side descriptors (plain stack / vector memory, copied into the scratch).
+    std::vector<kvx_unit> vu(static_cast<size_t>(groups));
+    std::vector<UnitDev> ud(static_cast<size_t>(groups));
+    std::vector<int64_t> begin(static_cast<size_t>(groups));
+    for (int g = 0; g < groups; ++g) {
+        kvx_unit &x = vu[size_t(g)];
+        x.k = k_xkv;
+        x.v = v_xkv;
+        x.k_index = k_index;
+        x.v_index = v_index;
+        x.q = q + size_t(8) * g * dim;
+        x.out = out + size_t(8) * g * dim;
+        x.k_bytes = k_bytes;
+        x.v_bytes = v_bytes;
+        x.n_blocks = n_blocks;
+        x.seq = seq;
+        UnitDev &d = ud[size_t(g)];
+        d = UnitDev{};
+        d.k = k_xkv;
+        d.v = v_xkv;
+        d.q = x.q;
+        d.out = x.out;
+        d.block_begin = int64_t(g) * n_blocks;
+        d.n_blocks = n_blocks;
+        d.n_q = std::min(8, n_q - 8 * g);
+        d.q_stride = dim;
+        begin[size_t(g)] = d.block_begin;
+    }
+    // Worker ranges: one block each when they fit, else an even split of the blocks.
+    std::vector<int64_t> tb(static_cast<size_t>(n_workers) + 1);
+    for (int t = 0; t <= n_workers; ++t) tb[size_t(t)] = int64_t(t) * total / n_workers;
+    std::vector<int32_t> split;
+    for (int g = 0; g < groups; ++g) {
+        const int t0 = worker_of_block(tb.data(), n_workers, ud[size_t(g)].block_begin);
+        const int t1 = worker_of_block(tb.data(), n_workers,
+                                       ud[size_t(g)].block_begin + ud[size_t(g)].n_blocks - 1);
+        if (t0 != t1) split.push_back(g);
+    }
+
+    // Every call shares the scratch and finds the previous call's contents there: the status
+    // word is cleared here; everything else is fully written before it is read.
+    KVX_CUDA(cudaMemsetAsync(status, 0, 2 * sizeof(int), s));
+    KVX_CUDA(cudaMemcpyAsync(d_units, ud.data(), ud.size() * sizeof(UnitDev), cudaMemcpyHostToDevice, s));
+    KVX_CUDA(cudaMemcpyAsync(d_vu, vu.data(), vu.size() * sizeof(kvx_unit), cudaMemcpyHostToDevice, s));
+    KVX_CUDA(cudaMemcpyAsync(d_begin, begin.data(), begin.size() * sizeof(int64_t), cudaMemcpyHostToDevice, s));
+    KVX_CUDA(cudaMemcpyAsync(d_range, tb.data(), tb.size() * sizeof(int64_t), cudaMemcpyHostToDevice, s));
+    if (!split.empty())
+        KVX_CUDA(cudaMemcpyAsync(d_split, split.data(), split.size() * sizeof(int32_t),
+                                 cudaMemcpyHostToDevice, s));
+    KVX_CUDA(launch_build_flat(d_vu, d_begin, groups, dim, kDefaultBlock, false, d_flat, d_flat_unit,
+                               status, s));
+    AttnArgs a{};
+    a.units = d_units;
+    a.flat = d_flat;
+    a.flat_unit = d_flat_unit;
+    a.range_begin = d_range;
+    a.partials = d_partials;
+    a.status = status;
+    a.n_workers = n_workers;
+    const int grid = (n_workers + per_cta - 1) / per_cta;
+    KVX_CUDA(launch_attention(dim, false, a, grid, s));
+    if (!split.empty()) {
+        CombineArgs c{};
+        c.units = d_units;
+        c.split_units = d_split;
+        c.range_begin = d_range;
+        c.partials = d_partials;
+        c.n_workers = n_workers;
+        KVX_CUDA(launch_combine(dim, c, int(split.size()), s));
+    }
+    // The host descriptors above are pageable stack/vector memory: wait for the stream before
+    // they go out of scope, then report device-side errors like kvx_attention_decode.
+    KVX_CUDA(cudaStreamSynchronize(s));
+    int st[2] = {0, 0};
+    KVX_CUDA(cudaMemcpy(st, status, sizeof st, cudaMemcpyDeviceToHost));
+    if (st[0] != 0) return fail(st[0], std::string(detail_message(st[0], st[1])));
+    g_err.clear();
+    return KVX_OK;
+}

@@ -115,6 +115,8 @@ _append = _sig("kvx_cache_append", C.c_int,
 _synth = _sig("kvx_synth_bf16", C.c_int,
               [_vp, C.c_int, C.c_int, C.c_uint64, C.c_uint64, C.c_int, C.c_uint32, _vp])
 _probe = _sig("kvx_hbm_read_probe", C.c_int, [_vp, _sz, C.c_int, C.POINTER(C.c_double)])
+_noalloc = _sig("kvx_attention_decode_noalloc", C.c_int,
+                [_vp, _vp, _sz, _vp, _vp, _sz, _vp, C.c_int, _vp, C.c_int, C.c_int, C.c_int, _vp])
 
 # Every symbol the C header declares, for load/export checks.
 EXPORTED = [
@@ -122,7 +124,7 @@ EXPORTED = [
     "kvx_attention_decode_units", "kvx_encode_bound", "kvx_encode_bf16", "kvx_decode_bf16",
     "kvx_xkv_index", "kvx_plan_create", "kvx_plan_run", "kvx_plan_run_part", "kvx_plan_check", "kvx_plan_launches",
     "kvx_plan_destroy", "kvx_encode_batch_bounds", "kvx_encode_batch", "kvx_cache_append",
-    "kvx_synth_bf16", "kvx_hbm_read_probe",
+    "kvx_synth_bf16", "kvx_hbm_read_probe", "kvx_attention_decode_noalloc",
 ]
 
 
@@ -233,6 +235,16 @@ def xkv_index(blob, nbytes, head_dim, index, max_blocks):
     _check(_xkv_index(_addr(blob), int(nbytes), int(head_dim), _addr(index), int(max_blocks),
                       C.byref(nb), C.byref(nt)))
     return nb.value, nt.value
+
+
+def attention_decode_noalloc(q, k_xkv, k_bytes, k_index, v_xkv, v_bytes, v_index, n_blocks, out,
+                             n_q, dim, seq, stream=None):
+    """One decode step over device-resident XKV K/V that allocates no GPU memory (for callers
+    whose device memory is all reserved up front; see kvx_attention_decode_noalloc).  Every
+    argument is device memory; the indexes come from xkv_index or the GPU encoder."""
+    _check(_noalloc(_addr(q), _addr(k_xkv), int(k_bytes), _addr(k_index), _addr(v_xkv),
+                    int(v_bytes), _addr(v_index), int(n_blocks), _addr(out), int(n_q), int(dim),
+                    int(seq), _addr(stream)))
 
 
 class Plan:

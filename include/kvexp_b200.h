@@ -160,6 +160,25 @@ KVX_API int kvx_cache_append(const uint16_t *kv_new, int n_new, int head_dim, in
                      uint8_t *blob, size_t at, size_t capacity, kvx_block *index,
                      size_t *bytes_written, int *blocks_written, void *stream);
 
+/* Decode attention that allocates no GPU memory.  No counterpart in the reference: it exists for
+ * callers that cannot allocate while they run, such as serving engines that reserve the
+ * device's memory for their KV-cache pool at start-up and treat a later cudaMalloc as a failure,
+ * or decode loops that cannot take the device-wide stall of cudaFree.  Same result as
+ * kvx_attention_decode for one KV head (within FP32 rounding), with every buffer in device
+ * memory: q [n_q, dim] BF16, the K/V XKV blobs (16-byte aligned) with their block indexes
+ * (n_blocks entries each, from kvx_xkv_index or the GPU encoder), out [n_q, dim] FP32.  Its
+ * scratch is one fixed 8 MiB array in the library's device image, held by every device that
+ * loads the library until the process exits; limits: n_blocks <= 8192, n_q <= 64 (larger calls
+ * fail with KVX_ERR_INVALID_ARGUMENT).  The first call on a device looks up the array's device
+ * address (and loads the module there); make that first call before any stream capture.  All
+ * calls share the array, so calls whose GPU work overlaps (other streams, other host threads)
+ * race; run them one after another.  Launches on `stream`, then synchronises it to report
+ * device-side errors. */
+KVX_API int kvx_attention_decode_noalloc(const uint16_t *q, const uint8_t *k_xkv, size_t k_bytes,
+                                 const kvx_block *k_index, const uint8_t *v_xkv, size_t v_bytes,
+                                 const kvx_block *v_index, int n_blocks, float *out, int n_q,
+                                 int dim, int seq, void *stream);
+
 /* ---- benchmark support -------------------------------------------------------------------- */
 
 /* Fill [seq, dim] BF16 on the device with the seeded synthetic distribution `profile`

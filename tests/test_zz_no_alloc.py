@@ -1,0 +1,67 @@
+"""The allocation-free decode entry point (kvx_attention_decode_noalloc), through the C ABI.
+
+Some callers cannot allocate GPU memory while they run -- serving engines that reserve the
+device's memory for their KV-cache pool at start-up, and decode loops that cannot take the
+device-wide stall of cudaFree.  This entry point keeps all of its scratch in one fixed device
+array inside the library.  The test checks two calls in a row (the second finds the first call's
+scratch contents) against the ordinary entry point kvx_attention_decode, within the same FP32
+tolerance as the other attention tests.  The file is named so that pytest collects it last.
+"""
+import numpy as np
+import pytest
+
+import synth as S
+from helpers import assert_attention_close, attn_scale
+
+pytestmark = pytest.mark.gpu
+
+
+def _case(dim, n_q, seq, seed):
+    k = S.synth_bf16(seed, 0, seq, dim, S.PROFILE_K)
+    v = S.synth_bf16(seed, 1, seq, dim, S.PROFILE_V)
+    q = S.synth_bf16(seed, 2, n_q, dim, S.PROFILE_Q)
+    return q, k, v
+
+
+def _device_index(kvx, torch, blob, dim):
+    """Device copy of an XKV blob and its device block index."""
+    d = torch.from_numpy(blob).cuda()
+    idx = torch.empty((blob.size // 8 + 16) * 8, dtype=torch.uint8, device="cuda")
+    nb, _ = kvx.xkv_index(d, blob.size, dim, idx, idx.numel() // 8)
+    return d, idx, nb
+
+
+@pytest.mark.parametrize("cases", [
+    [(64, 7, 3000, 11), (64, 7, 3000, 12)],     # same shape twice, new data
+    [(128, 12, 5000, 13), (64, 3, 700, 14)],    # shape changes between the calls
+])
+def test_noalloc_matches_attention_decode(kvx, cuda, oracle, cases):
+    torch = cuda
+    for dim, n_q, seq, seed in cases:
+        q, k, v = _case(dim, n_q, seq, seed)
+        kx, vx = oracle.encode(k, 128), oracle.encode(v, 128)
+        want = np.zeros((n_q, dim), dtype=np.float32)
+        kvx.attention_decode(0, q, None, None, kx, kx.size, vx, vx.size, want, n_q, dim, seq, 1,
+                             128)
+        kd, kidx, nb = _device_index(kvx, torch, kx, dim)
+        vd, vidx, nbv = _device_index(kvx, torch, vx, dim)
+        assert nb == nbv
+        qd = torch.from_numpy(q.view(np.int16)).cuda()
+        out = torch.full((n_q, dim), float("nan"), dtype=torch.float32, device="cuda")
+        kvx.attention_decode_noalloc(qd, kd, kx.size, kidx, vd, vx.size, vidx, nb, out, n_q, dim,
+                                     seq)
+        got = out.cpu().numpy()
+        assert np.all(np.isfinite(got))
+        assert_attention_close(got, want, attn_scale(q, k, v),
+                               f"noalloc dim={dim} n_q={n_q} seq={seq}", seq=seq)
+
+
+def test_noalloc_rejects_oversize(kvx, cuda):
+    torch = cuda
+    z = torch.zeros(4096, dtype=torch.uint8, device="cuda")
+    q = torch.zeros((4, 64), dtype=torch.int16, device="cuda")
+    out = torch.zeros((4, 64), dtype=torch.float32, device="cuda")
+    with pytest.raises(ValueError, match="8192 blocks"):
+        kvx.attention_decode_noalloc(q, z, 4096, z, z, 4096, z, 8193, out, 4, 64, 8193 * 128)
+    with pytest.raises(ValueError, match="64 queries"):
+        kvx.attention_decode_noalloc(q, z, 4096, z, z, 4096, z, 1, out, 65, 64, 128)
