@@ -1042,36 +1042,71 @@ __global__ void __launch_bounds__(32 * Cfg<D>::WARPS, 1) attn_kernel(const AttnA
 
 // ---- combine ------------------------------------------------------------------------------------
 
-// Fold the partial states of a unit in worker order (merge_state, src/softmax.hpp:16-30) and
-// finalize (finalize_state, src/softmax.hpp:32-41).
+// Combine the partial states of one query of a split unit: with M = max m_t over the unit's
+// segments, l = sum l_t e^(m_t - M) and acc = sum acc_t e^(m_t - M) (merge_state's arithmetic,
+// src/softmax.hpp:16-30, applied to all segments at once instead of a left fold), then
+// out = acc * (1 / l) like finalize_state (src/softmax.hpp:32-41).  One CTA per (unit, query);
+// the sums run over fixed slices of the segments, so the result is deterministic.
+constexpr int kCombineThreads = 256;
+constexpr int kMaxSegments = 4096;
+
 template <int D>
-__global__ void __launch_bounds__(256) combine_kernel(const CombineArgs a) {
+__global__ void __launch_bounds__(kCombineThreads) combine_kernel(const CombineArgs a) {
+    constexpr int S = kCombineThreads / D;  // segment slices summed in parallel
+    __shared__ float e[kMaxSegments];
+    __shared__ float red[kCombineThreads];
     const int u = a.split_units[blockIdx.x];
+    const int g = blockIdx.y;
     const UnitDev unit = a.units[u];
+    if (g >= unit.n_q) return;
     const int t0 = worker_of_block(a.range_begin, a.n_workers, unit.block_begin);
     const int t1 = worker_of_block(a.range_begin, a.n_workers, unit.block_begin + unit.n_blocks - 1);
+    const int nt = min(t1 - t0 + 1, kMaxSegments);
     const int ps = partial_stride(D);
-    for (int idx = threadIdx.x; idx < unit.n_q * D; idx += blockDim.x) {
-        const int g = idx / D, d = idx % D;
-        float m = 0.f, l = 0.f, acc = 0.f;
-        for (int t = t0; t <= t1; ++t) {
-            const int slot = (a.range_begin[t] >= unit.block_begin) ? 0 : 1;
-            const float *p = a.partials + (size_t(t) * 2 + slot) * ps;
-            const float mb = p[g], lb = p[8 + g], ab = p[16 + g * D + d];
-            if (t == t0) {
-                m = mb;
-                l = lb;
-                acc = ab;
-                continue;
-            }
-            const float mm = (m < mb) ? mb : m;
-            const float e1 = expf(m - mm), e2 = expf(mb - mm);
-            l = __fmaf_rn(l, e1, __fmul_rn(lb, e2));
-            acc = __fmaf_rn(acc, e1, __fmul_rn(ab, e2));
-            m = mm;
-        }
-        const float inv = __frcp_rn(l);
-        unit.out[size_t(g) * unit.q_stride + d] = __fmul_rn(acc, inv);
+    auto part = [&](int i) {
+        const int t = t0 + i;
+        const int slot = (a.range_begin[t] >= unit.block_begin) ? 0 : 1;
+        return a.partials + (size_t(t) * 2 + slot) * ps;
+    };
+    const int tid = threadIdx.x;
+    float mx = -INFINITY;
+    for (int i = tid; i < nt; i += kCombineThreads) {
+        const float m = part(i)[g];
+        e[i] = m;
+        mx = fmaxf(mx, m);
+    }
+    red[tid] = mx;
+    __syncthreads();
+    for (int o = kCombineThreads / 2; o > 0; o >>= 1) {
+        if (tid < o) red[tid] = fmaxf(red[tid], red[tid + o]);
+        __syncthreads();
+    }
+    const float M = red[0];
+    __syncthreads();
+    float ls = 0.f;
+    for (int i = tid; i < nt; i += kCombineThreads) {
+        const float w = expf(e[i] - M);
+        e[i] = w;
+        ls = __fmaf_rn(part(i)[8 + g], w, ls);
+    }
+    red[tid] = ls;
+    __syncthreads();
+    for (int o = kCombineThreads / 2; o > 0; o >>= 1) {
+        if (tid < o) red[tid] = __fadd_rn(red[tid], red[tid + o]);
+        __syncthreads();
+    }
+    const float inv = __frcp_rn(red[0]);
+    __syncthreads();
+    const int d = tid % D, sl = tid / D;
+    float acc = 0.f;
+    if (sl < S)
+        for (int i = sl; i < nt; i += S) acc = __fmaf_rn(part(i)[16 + g * D + d], e[i], acc);
+    red[tid] = acc;
+    __syncthreads();
+    if (sl == 0) {
+        float v = red[d];
+        for (int j = 1; j < S; ++j) v = __fadd_rn(v, red[j * D + d]);
+        unit.out[size_t(g) * unit.q_stride + d] = __fmul_rn(v, inv);
     }
 }
 
@@ -1188,11 +1223,12 @@ cudaError_t launch_split(const FlatBlock *flat, int64_t n_blocks, int n_workers,
 
 cudaError_t launch_combine(int dim, const CombineArgs &a, int n_split, cudaStream_t s) {
     if (n_split <= 0) return cudaSuccess;
+    const dim3 grid(n_split, 8);  // (split unit, query); units hold at most 8 queries
     switch (dim) {
-    case 32: combine_kernel<32><<<n_split, 256, 0, s>>>(a); break;
-    case 64: combine_kernel<64><<<n_split, 256, 0, s>>>(a); break;
-    case 128: combine_kernel<128><<<n_split, 256, 0, s>>>(a); break;
-    case 256: combine_kernel<256><<<n_split, 256, 0, s>>>(a); break;
+    case 32: combine_kernel<32><<<grid, kCombineThreads, 0, s>>>(a); break;
+    case 64: combine_kernel<64><<<grid, kCombineThreads, 0, s>>>(a); break;
+    case 128: combine_kernel<128><<<grid, kCombineThreads, 0, s>>>(a); break;
+    case 256: combine_kernel<256><<<grid, kCombineThreads, 0, s>>>(a); break;
     default: return cudaErrorInvalidValue;
     }
     return cudaGetLastError();
