@@ -324,6 +324,8 @@ int kvx_plan_create(const kvx_unit *units, int n_units, int n_q, int dim, int bl
             total += nb;
         }
     }
+    if (total > int64_t(0x7FFFFFFF))
+        return fail(KVX_ERR_UNSUPPORTED, "kvx_plan_create: more than 2^31 - 1 blocks in one step");
     auto *p = new kvx_plan_s();
     p->dim = dim;
     p->bf16 = bf16;

@@ -48,9 +48,10 @@ __device__ __forceinline__ float ex2(float x) {
 
 __host__ __device__ constexpr int round16(int x) { return (x + 15) & ~15; }
 __host__ __device__ constexpr int cmin(int a, int b) { return a < b ? a : b; }
+__host__ __device__ constexpr int cmax(int a, int b) { return a > b ? a : b; }
 
 #ifndef KVX_NSTAGE64
-#define KVX_NSTAGE64 3
+#define KVX_NSTAGE64 2
 #endif
 #ifndef KVX_MAXWARPS
 #define KVX_MAXWARPS 12
@@ -64,17 +65,25 @@ template <int D> struct Cfg {
     static constexpr bool SPLIT = D > 128;  // rebuild row halves one at a time (register budget)
     static constexpr bool B7REG = D <= 128; // keep the block's base exponents in registers
     static constexpr int ESC_CAP = 1536;    // escape bytes staged per block and tensor
-    static constexpr int TR = 2 * TT * D + 32;    // one tensor tile: raw rows or sm + codes rows
-    static constexpr int CODE_OFF = TT * D + 16;  // residual-code rows inside a coded tensor tile
-    static constexpr int SLOT = 2 * TR;           // K tile | V tile
-    static constexpr int NSTAGE = D <= 32 ? 4 : D == 64 ? KVX_NSTAGE64 : D == 128 ? 3 : 2;
+    // A ring stage holds TSC tokens of a coded block or TT tokens of a raw one (raw rows take
+    // two bytes per element, coded ones 1.25-1.5), for K and V.
+    static constexpr int TSC = D <= 128 ? 2 * TT : TT;
+    static constexpr int SUBS = TSC / TT;         // 16-token sub-tiles per stage at most
+    static constexpr int TR = round16(cmax(TSC * D * 3 / 2 + 48, TT * 2 * D + 32));  // one tensor
+    static constexpr int CODE_OFF = TSC * D + 16;  // residual-code rows inside a coded tensor stage
+    static constexpr int SLOT = 2 * TR;            // K stage | V stage
+    static constexpr int NSTAGE = D <= 32 ? 3 : D == 64 ? KVX_NSTAGE64 : 2;
     static_assert(NSTAGE >= 2 && NSTAGE <= 4, "stage waits cover at most 3 younger groups");
     static constexpr int BASE = round16(D + 32);  // one block's base exponents (+ alignment slack)
     static constexpr int ESCB = ESC_CAP + 32;
     static constexpr int M_K = 0, M_V = BASE, M_EK = 2 * BASE, M_EV = 2 * BASE + ESCB;
     static constexpr int MSLOT = 2 * BASE + 2 * ESCB;
-    static constexpr int W_META = NSTAGE * SLOT;  // per-warp region: ring | meta x2
-    static constexpr int WARP_BYTES = (W_META + 2 * MSLOT + 127) & ~127;
+    // Escape scratch: the consumed sm rows of the sub-tile, except when the row halves are rebuilt
+    // one at a time (then the second half's rows are still unread): a region of its own.
+    static constexpr int SCR = SPLIT ? TT * D : 0;
+    static constexpr int W_META = NSTAGE * SLOT;  // per-warp region: ring | meta x2 | scratch
+    static constexpr int W_SCR = W_META + 2 * MSLOT;
+    static constexpr int WARP_BYTES = (W_SCR + SCR + 127) & ~127;
     static constexpr int WARPS = cmin(KVX_MAXWARPS, 232448 / WARP_BYTES);
     static_assert(WARPS >= 1, "worker does not fit in shared memory");
 };
@@ -172,10 +181,12 @@ template <int D> __device__ __forceinline__ bool esc_staged(const Piece &e, int 
 // ---- decode helpers ----------------------------------------------------------------------------
 
 // NW 32-bit words of shared memory starting at any byte address (byte 0 in bits 0-7 of w[0]).
+// The aligned pointer is derived from p by pointer arithmetic (not through an integer), so the
+// compiler keeps these as 32-bit shared-memory loads.
 template <int NW> __device__ __forceinline__ void lds_words(const uint8_t *p, uint32_t (&w)[NW]) {
-    const uintptr_t a = reinterpret_cast<uintptr_t>(p);
-    const uint32_t *q = reinterpret_cast<const uint32_t *>(a & ~uintptr_t(3));
-    const uint32_t sh = uint32_t(a & 3u) * 8u;
+    const uint32_t mis = uint32_t(reinterpret_cast<uintptr_t>(p)) & 3u;
+    const uint32_t *q = reinterpret_cast<const uint32_t *>(p - mis);
+    const uint32_t sh = mis * 8u;
     uint32_t x[NW + 1];
 #pragma unroll
     for (int i = 0; i <= NW; ++i) x[i] = q[i];
@@ -240,9 +251,11 @@ __device__ __forceinline__ void load_b7v(const uint8_t *base, uint32_t (&b7)[Cfg
 
 // ---- escapes -----------------------------------------------------------------------------------
 //
-// A sentinel element takes the next escape word in the block's scan order (token-major).  Its
-// sign/mantissa byte and its exponent offset are written into the staged words before the merge,
-// so the merge rebuilds the escape word exactly.
+// A sentinel element takes the next escape word of its block in scan order (token-major).  The
+// rows are rebuilt first (a sentinel comes out with a wrong exponent).  When a row half holds a
+// sentinel, every lane writes its fragment registers to scratch in shared memory (the half's
+// sign/mantissa rows, already consumed), lanes write their escape words over the sentinel
+// elements in place, and every lane reads its registers back.  Ranks come from warp ballots.
 
 struct Esc {
     uint32_t run;               // escapes consumed so far in this block
@@ -260,28 +273,13 @@ __device__ __forceinline__ uint32_t esc_word(uint32_t r, const Esc &es, int *sta
                             : uint32_t(__ldg(es.gm + r));
 }
 
-__device__ __forceinline__ void set_byte(uint32_t &w, int b, uint32_t v) {
-    const uint32_t sh = 8u * uint32_t(b);
-    w = (w & ~(0xFFu << sh)) | ((v & 0xFFu) << sh);
-}
-__device__ __forceinline__ uint32_t esc_sm(uint32_t h) { return ((h >> 8) & 0x80u) | (h & 0x7Fu); }
-__device__ __forceinline__ uint32_t esc_off(uint32_t h, uint32_t base) {
-    return ((h >> 7) - base) & 0xFFu;
-}
-// Set word c of w[] (c warp-divergent, N compile-time) without dynamic register indexing.
-template <int N>
-__device__ __forceinline__ void set_byte_of(uint32_t (&w)[N], int c, int b, uint32_t v) {
-#pragma unroll
-    for (int i = 0; i < N; ++i)
-        if (i == c) set_byte(w[i], b, v);
-}
-
-// First escape rank of this lane when the scan order is the lane order (K rows) and some lane
-// holds several sentinels: exclusive prefix of the per-lane counts, bit by bit.
+// First escape rank of this lane when the scan order is the lane order (K rows): exclusive
+// prefix of the per-lane sentinel counts, bit by bit (one step when no lane holds two).
 __device__ __forceinline__ uint32_t rank_lanes(uint32_t cnt, Esc &es) {
     const uint32_t lt = lanemask_lt();
     const int bits = 32 - __clz(__reduce_max_sync(FULL, cnt));
     uint32_t pre = 0, tot = 0;
+#pragma unroll 1
     for (int b = 0; b < bits; ++b) {
         const uint32_t B = __ballot_sync(FULL, (cnt >> b) & 1u);
         pre += uint32_t(__popc(B & lt)) << b;
@@ -292,26 +290,18 @@ __device__ __forceinline__ uint32_t rank_lanes(uint32_t cnt, Esc &es) {
     return r;
 }
 
-// First escape ranks of tokens A and B of a V token half; true when every lane holds at most one
-// sentinel per token.  Lane 4g + t holds tokens 2t (A) and
+// First escape ranks of tokens A and B of a V token half.  Lane 4g + t holds tokens 2t (A) and
 // 2t+1 (B) of the half, dims [g D/8, (g+1) D/8); the scan order inside the half is
 // (t, A/B, g, element).
-__device__ __forceinline__ bool rank_tokens(uint32_t ca, uint32_t cb, Esc &es, int lane,
+__device__ __forceinline__ void rank_tokens(uint32_t ca, uint32_t cb, Esc &es, int lane,
                                             uint32_t &ra, uint32_t &rb) {
     const uint32_t lt = lanemask_lt();
     const int tig = lane & 3;
     const uint32_t G = 0x11111111u << tig;                // lanes with this t
     const uint32_t L = 0x11111111u * ((1u << tig) - 1u);  // lanes with a smaller t
-    if (__ballot_sync(FULL, ca > 1u || cb > 1u) == 0u) {
-        const uint32_t BA = __ballot_sync(FULL, ca != 0u), BB = __ballot_sync(FULL, cb != 0u);
-        const uint32_t before = es.run + __popc(BA & L) + __popc(BB & L);
-        ra = before + __popc(BA & G & lt);
-        rb = before + __popc(BA & G) + __popc(BB & G & lt);
-        es.run += __popc(BA) + __popc(BB);
-        return true;
-    }
     const int bits = 32 - __clz(__reduce_max_sync(FULL, ca > cb ? ca : cb));
     uint32_t sl = 0, sag = 0, saglt = 0, sbglt = 0, tot = 0;
+#pragma unroll 1
     for (int b = 0; b < bits; ++b) {
         const uint32_t BA = __ballot_sync(FULL, (ca >> b) & 1u);
         const uint32_t BB = __ballot_sync(FULL, (cb >> b) & 1u);
@@ -324,309 +314,201 @@ __device__ __forceinline__ bool rank_tokens(uint32_t ca, uint32_t cb, Esc &es, i
     ra = es.run + sl + saglt;
     rb = es.run + sl + sag + sbglt;
     es.run += tot;
-    return false;
+}
+
+template <int N>
+__device__ __forceinline__ void regs_to(uint32_t *p, const uint32_t (&o)[N]) {
+#pragma unroll
+    for (int i = 0; i < N; i += 4)
+        *reinterpret_cast<uint4 *>(p + i) = make_uint4(o[i], o[i + 1], o[i + 2], o[i + 3]);
+}
+template <int N> __device__ __forceinline__ void regs_from(const uint32_t *p, uint32_t (&o)[N]) {
+#pragma unroll
+    for (int i = 0; i < N; i += 4) {
+        const uint4 v = *reinterpret_cast<const uint4 *>(p + i);
+        o[i] = v.x;
+        o[i + 1] = v.y;
+        o[i + 2] = v.z;
+        o[i + 3] = v.w;
+    }
 }
 
 // ---- decode ------------------------------------------------------------------------------------
+//
+// A K row (one token, this lane's DK dims) or a V token pair (two tokens, this lane's DV dims) is
+// loaded into staged words (sign/mantissa bytes, one exponent code byte per element) and merged
+// into BF16 pairs; the sentinel masks are kept for the escape walk.
 
-// One K row of this lane (DK dims starting at c0): NK registers of BF16 pairs (dims c0+2p,
-// c0+2p+1).  rp: row's sm (or raw) bytes, cp: row's codes, bp: the block's base exponents of the
-// same dims.  The caller calls rows in scan order; `valid` is false for rows past the tile's end.
-template <int D, int MODE>
-__device__ __forceinline__ void dec_k(const uint8_t *rp, const uint8_t *cp, const uint8_t *bp,
-                                      const uint32_t (&b7)[Cfg<D>::NK], bool valid, Esc &es,
-                                      int *status, uint32_t (&o)[Cfg<D>::NK]) {
+// One K row of this lane (dims c0 .. c0 + DK - 1 of one token).
+template <int D, int MODE> struct KRow {
     using C = Cfg<D>;
-    if (MODE == 0) {
-        lds_words<C::NK>(rp, o);
-        return;
-    }
-    uint32_t S[C::DK / 4];
-    lds_words<C::DK / 4>(rp, S);
-    if (MODE == 4) {
-        constexpr int NW = C::DK / 8;
-        uint32_t N[NW], NL[NW], NH[NW], mk[NW];
+    static constexpr int NS = C::DK / 4;                                    // sm words
+    static constexpr int NW = MODE == 2 ? cmax(1, C::DK / 16) : C::DK / 8;  // code words
+    uint32_t S[NS], L[NW], H[NW], Cd[4][NW], mk[NW];
+    uint32_t cnt;
+
+    __device__ __forceinline__ void load(const uint8_t *rp, const uint8_t *cp, bool valid) {
+        lds_words<NS>(rp, S);
+        uint32_t N[NW];
         lds_words<NW>(cp, N);
-        uint32_t cnt = 0;
+        cnt = 0;
 #pragma unroll
         for (int i = 0; i < NW; ++i) {
-            NL[i] = N[i] & 0x0F0F0F0Fu;
-            NH[i] = (N[i] >> 4) & 0x0F0F0F0Fu;
-            mk[i] = valid ? sent4(N[i]) : 0u;
+            if (MODE == 4) {
+                L[i] = N[i] & 0x0F0F0F0Fu;
+                H[i] = (N[i] >> 4) & 0x0F0F0F0Fu;
+                mk[i] = valid ? sent4(N[i]) : 0u;
+            } else {
+#pragma unroll
+                for (int k = 0; k < 4; ++k) Cd[k][i] = (N[i] >> (2 * k)) & 0x03030303u;
+                mk[i] = valid ? (sent2(N[i]) & low_bytes(C::DK / 4)) : 0u;
+            }
             cnt += __popc(mk[i]);
         }
-        const uint32_t any = __ballot_sync(FULL, cnt != 0u);
-        if (any != 0u) {
-            auto patch = [&](int i, int k, uint32_t h) {  // element 8i + k
-                const uint32_t off = esc_off(h, bp[8 * i + k]);
-                if (k & 1) set_byte(NH[i], k >> 1, off);
-                else set_byte(NL[i], k >> 1, off);
-                if (k & 4) set_byte(S[2 * i + 1], k & 3, esc_sm(h));
-                else set_byte(S[2 * i], k & 3, esc_sm(h));
-            };
-            if (__ballot_sync(FULL, cnt > 1u) == 0u) {
-                // at most one sentinel per lane: straight-line
-                const uint32_t r = es.run + __popc(any & lanemask_lt());
-                es.run += __popc(any);
-                if (cnt != 0u) {
-                    const uint32_t h = esc_word(r, es, status);
-#pragma unroll
-                    for (int i = 0; i < NW; ++i)
-                        if (mk[i] != 0u) patch(i, (__ffs(mk[i]) - 1) >> 2, h);
-                }
-            } else {
-                uint32_t r = rank_lanes(cnt, es);
-#pragma unroll
-                for (int i = 0; i < NW; ++i) {
-                    uint32_t mm = mk[i];
-                    while (mm != 0u) {
-                        const int k = (__ffs(mm) - 1) >> 2;
-                        mm &= mm - 1u;
-                        patch(i, k, esc_word(r++, es, status));
-                    }
-                }
-            }
-        }
+    }
+    // element index of mask bit b of word i
+    __device__ __forceinline__ static int elem(int i, int b) {
+        return MODE == 4 ? 8 * i + (b >> 2) : 16 * i + (b >> 1);
+    }
+    __device__ __forceinline__ void merge_into(const uint32_t (&b7)[C::NK], uint32_t (&o)[C::NK]) const {
 #pragma unroll
         for (int p = 0; p < C::NK; ++p) {
             const uint32_t sg = prmt(S[p >> 1], 0u, sel_pair(2 * (p & 1)));
-            const uint32_t cw = prmt(NL[p >> 2], NH[p >> 2], sel_code(p & 3));
-            o[p] = merge(sg, cw, b7[p]);
-        }
-    } else {
-        constexpr int NB = C::DK / 4;
-        constexpr int NW = (NB + 3) / 4;
-        uint32_t W[NW], Ck[4][NW], mk[NW];
-        lds_words<NW>(cp, W);
-        uint32_t cnt = 0;
-#pragma unroll
-        for (int i = 0; i < NW; ++i) {
-            mk[i] = valid ? (sent2(W[i]) & low_bytes(NB)) : 0u;
-            cnt += __popc(mk[i]);
-#pragma unroll
-            for (int k = 0; k < 4; ++k) Ck[k][i] = (W[i] >> (2 * k)) & 0x03030303u;
-        }
-        const uint32_t any = __ballot_sync(FULL, cnt != 0u);
-        if (any != 0u) {
-            auto patch = [&](int i, int e, uint32_t h) {  // element 16i + e
-                const int j = e >> 2, k = e & 3;
-                const uint32_t off = esc_off(h, bp[16 * i + e]);
-#pragma unroll
-                for (int c = 0; c < 4; ++c)
-                    if (c == k) set_byte(Ck[c][i], j, off);
-#pragma unroll
-                for (int c = 0; c < 4 && 4 * i + c < C::DK / 4; ++c)
-                    if (c == j) set_byte(S[4 * i + c], k, esc_sm(h));
-            };
-            if (__ballot_sync(FULL, cnt > 1u) == 0u) {
-                const uint32_t r = es.run + __popc(any & lanemask_lt());
-                es.run += __popc(any);
-                if (cnt != 0u) {
-                    const uint32_t h = esc_word(r, es, status);
-#pragma unroll
-                    for (int i = 0; i < NW; ++i)
-                        if (mk[i] != 0u) patch(i, (__ffs(mk[i]) - 1) >> 1, h);
-                }
+            uint32_t cw;
+            if (MODE == 4) {
+                cw = prmt(L[p >> 2], H[p >> 2], sel_code(p & 3));
             } else {
-                uint32_t r = rank_lanes(cnt, es);
-#pragma unroll
-                for (int i = 0; i < NW; ++i) {
-                    uint32_t mm = mk[i];
-                    while (mm != 0u) {
-                        const int e = (__ffs(mm) - 1) >> 1;
-                        mm &= mm - 1u;
-                        patch(i, e, esc_word(r++, es, status));
-                    }
-                }
+                const int e = 2 * p, i = e >> 4, j = (e & 15) >> 2, k = e & 3;
+                cw = prmt(Cd[k][i], Cd[k + 1][i], sel_code(j));
             }
-        }
-#pragma unroll
-        for (int p = 0; p < C::NK; ++p) {
-            const int e = 2 * p, i = e >> 4, j = (e & 15) >> 2, k = e & 3;
-            const uint32_t sg = prmt(S[p >> 1], 0u, sel_pair(2 * (p & 1)));
-            const uint32_t cw = prmt(Ck[k][i], Ck[k + 1][i], sel_code(j));
             o[p] = merge(sg, cw, b7[p]);
         }
     }
+};
+
+// Escapes of one K row half (rows 0-7 or 8-15; scan order (row, dim) = (lane, element)), through
+// scratch: o holds dims c0 + 2p (low half) and c0 + 2p + 1 (high half), so element e sits at
+// 16-bit position e of the lane's words.  Called by the whole warp when some lane's row has one.
+template <int D, int MODE>
+__device__ __forceinline__ void esc_k_half(uint32_t (&o)[Cfg<D>::NK], const KRow<D, MODE> &w,
+                                           uint8_t *scr, Esc &es, int *status, int lane) {
+    uint32_t *mine = reinterpret_cast<uint32_t *>(scr) + lane * Cfg<D>::NK;
+    __syncwarp();  // every lane has read the rows this scratch overlays
+    regs_to(mine, o);
+    uint32_t r = rank_lanes(w.cnt, es);
+    uint16_t *h16 = reinterpret_cast<uint16_t *>(mine);
+#pragma unroll
+    for (int i = 0; i < KRow<D, MODE>::NW; ++i) {
+        uint32_t mm = w.mk[i];
+#pragma unroll 1
+        while (mm != 0u) {
+            const int e = KRow<D, MODE>::elem(i, __ffs(mm) - 1);
+            mm &= mm - 1u;
+            h16[e] = uint16_t(esc_word(r++, es, status));
+        }
+    }
+    regs_from(mine, o);
 }
 
-// Two V tokens (A -> low halves, B -> high halves) of this lane (DV dims): DV registers, one per
-// dim.  va/vb: the tokens are inside the tile; bp: base exponents of the lane's dims.
-template <int D, int MODE>
-__device__ __forceinline__ void dec_v(const uint8_t *ra, const uint8_t *rb, const uint8_t *ca,
-                                      const uint8_t *cb, const uint8_t *bp,
-                                      const uint32_t (&b7)[Cfg<D>::DV], bool va, bool vb, Esc &es,
-                                      int *status, int lane, uint32_t (&o)[Cfg<D>::DV]) {
+// Two V tokens (A -> low halves, B -> high halves; dims v0 .. v0 + DV - 1).
+template <int D, int MODE> struct VPair {
     using C = Cfg<D>;
-    if (MODE == 0) {
-        uint32_t RA[C::DV / 2], RB[C::DV / 2];
-        lds_words<C::DV / 2>(ra, RA);
-        lds_words<C::DV / 2>(rb, RB);
+    static constexpr int NS = C::DV / 4;
+    static constexpr int NB = MODE == 2 ? C::DV / 4 : C::DV / 2;  // code bytes per token
+    static constexpr int NW = (NB + 3) / 4;
+    uint32_t SA[NS], SB[NS], LA[NW], HA[NW], LB[NW], HB[NW], CA[4][NW], CB[4][NW], ma[NW], mb[NW];
+    uint32_t ca, cb;
+
+    __device__ __forceinline__ void load(const uint8_t *ra, const uint8_t *rb, const uint8_t *pa,
+                                         const uint8_t *pb, bool va, bool vb) {
+        lds_words<NS>(ra, SA);
+        lds_words<NS>(rb, SB);
+        uint32_t WA[NW], WB[NW];
+        lds_words<NW>(pa, WA);
+        lds_words<NW>(pb, WB);
+        ca = cb = 0;
 #pragma unroll
-        for (int e = 0; e < C::DV; ++e) o[e] = prmt(RA[e >> 1], RB[e >> 1], (e & 1) ? 0x7632u : 0x5410u);
-        return;
+        for (int i = 0; i < NW; ++i) {
+            if (MODE == 4) {
+                LA[i] = WA[i] & 0x0F0F0F0Fu;
+                HA[i] = (WA[i] >> 4) & 0x0F0F0F0Fu;
+                LB[i] = WB[i] & 0x0F0F0F0Fu;
+                HB[i] = (WB[i] >> 4) & 0x0F0F0F0Fu;
+                ma[i] = va ? (sent4(WA[i]) & low_bytes(NB)) : 0u;
+                mb[i] = vb ? (sent4(WB[i]) & low_bytes(NB)) : 0u;
+            } else {
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    CA[k][i] = (WA[i] >> (2 * k)) & 0x03030303u;
+                    CB[k][i] = (WB[i] >> (2 * k)) & 0x03030303u;
+                }
+                ma[i] = va ? (sent2(WA[i]) & low_bytes(NB)) : 0u;
+                mb[i] = vb ? (sent2(WB[i]) & low_bytes(NB)) : 0u;
+            }
+            ca += __popc(ma[i]);
+            cb += __popc(mb[i]);
+        }
     }
-    uint32_t SA[C::DV / 4], SB[C::DV / 4];
-    lds_words<C::DV / 4>(ra, SA);
-    lds_words<C::DV / 4>(rb, SB);
-    if (MODE == 4) {
-        constexpr int NB = C::DV / 2;
-        constexpr int NW = (NB + 3) / 4;
-        uint32_t NA[NW], NBw[NW], LA[NW], HA[NW], LB[NW], HB[NW], ma[NW], mb[NW];
-        lds_words<NW>(ca, NA);
-        lds_words<NW>(cb, NBw);
-        uint32_t cna = 0, cnb = 0;
-#pragma unroll
-        for (int i = 0; i < NW; ++i) {
-            LA[i] = NA[i] & 0x0F0F0F0Fu;
-            HA[i] = (NA[i] >> 4) & 0x0F0F0F0Fu;
-            LB[i] = NBw[i] & 0x0F0F0F0Fu;
-            HB[i] = (NBw[i] >> 4) & 0x0F0F0F0Fu;
-            ma[i] = va ? (sent4(NA[i]) & low_bytes(NB)) : 0u;
-            mb[i] = vb ? (sent4(NBw[i]) & low_bytes(NB)) : 0u;
-            cna += __popc(ma[i]);
-            cnb += __popc(mb[i]);
-        }
-        if (__ballot_sync(FULL, (cna | cnb) != 0u) != 0u) {
-            auto patch_a = [&](int i, int k, uint32_t h) {  // element 8i + k of token A
-                const int e = 8 * i + k;
-                const uint32_t off = esc_off(h, bp[e]);
-                if (k & 1) set_byte(HA[i], k >> 1, off);
-                else set_byte(LA[i], k >> 1, off);
-                set_byte_of(SA, e >> 2, e & 3, esc_sm(h));
-            };
-            auto patch_b = [&](int i, int k, uint32_t h) {
-                const int e = 8 * i + k;
-                const uint32_t off = esc_off(h, bp[e]);
-                if (k & 1) set_byte(HB[i], k >> 1, off);
-                else set_byte(LB[i], k >> 1, off);
-                set_byte_of(SB, e >> 2, e & 3, esc_sm(h));
-            };
-            uint32_t r_a, r_b;
-            if (rank_tokens(cna, cnb, es, lane, r_a, r_b)) {
-                if (cna != 0u) {
-                    const uint32_t h = esc_word(r_a, es, status);
-#pragma unroll
-                    for (int i = 0; i < NW; ++i)
-                        if (ma[i] != 0u) patch_a(i, (__ffs(ma[i]) - 1) >> 2, h);
-                }
-                if (cnb != 0u) {
-                    const uint32_t h = esc_word(r_b, es, status);
-#pragma unroll
-                    for (int i = 0; i < NW; ++i)
-                        if (mb[i] != 0u) patch_b(i, (__ffs(mb[i]) - 1) >> 2, h);
-                }
-            } else {
-#pragma unroll
-                for (int i = 0; i < NW; ++i) {
-                    uint32_t mm = ma[i];
-                    while (mm != 0u) {
-                        const int k = (__ffs(mm) - 1) >> 2;
-                        mm &= mm - 1u;
-                        patch_a(i, k, esc_word(r_a++, es, status));
-                    }
-                    mm = mb[i];
-                    while (mm != 0u) {
-                        const int k = (__ffs(mm) - 1) >> 2;
-                        mm &= mm - 1u;
-                        patch_b(i, k, esc_word(r_b++, es, status));
-                    }
-                }
-            }
-        }
+    __device__ __forceinline__ static int elem(int i, int b) {
+        return MODE == 4 ? 8 * i + (b >> 2) : 16 * i + (b >> 1);
+    }
+    __device__ __forceinline__ void merge_into(const uint32_t (&b7)[C::DV], uint32_t (&o)[C::DV]) const {
 #pragma unroll
         for (int e = 0; e < C::DV; ++e) {
-            const int i = e >> 3, j = (e & 7) >> 1;
             const uint32_t sg = prmt(SA[e >> 2], SB[e >> 2], sel_cross(e & 3));
-            const uint32_t cw = (e & 1) ? prmt(HA[i], HB[i], sel_code(j)) : prmt(LA[i], LB[i], sel_code(j));
-            o[e] = merge(sg, cw, b7[e]);
-        }
-    } else {
-        constexpr int NB = C::DV / 4;
-        constexpr int NW = (NB + 3) / 4;
-        uint32_t WA[NW], WB[NW], CA[4][NW], CB[4][NW], ma[NW], mb[NW];
-        lds_words<NW>(ca, WA);
-        lds_words<NW>(cb, WB);
-        uint32_t cna = 0, cnb = 0;
-#pragma unroll
-        for (int i = 0; i < NW; ++i) {
-            ma[i] = va ? (sent2(WA[i]) & low_bytes(NB)) : 0u;
-            mb[i] = vb ? (sent2(WB[i]) & low_bytes(NB)) : 0u;
-            cna += __popc(ma[i]);
-            cnb += __popc(mb[i]);
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                CA[k][i] = (WA[i] >> (2 * k)) & 0x03030303u;
-                CB[k][i] = (WB[i] >> (2 * k)) & 0x03030303u;
-            }
-        }
-        if (__ballot_sync(FULL, (cna | cnb) != 0u) != 0u) {
-            auto patch_a = [&](int i, int e4, uint32_t h) {  // element 16i + e4 of token A
-                const int e = 16 * i + e4;
-                const uint32_t off = esc_off(h, bp[e]);
-#pragma unroll
-                for (int c = 0; c < 4; ++c)
-                    if (c == (e & 3)) set_byte(CA[c][i], (e & 15) >> 2, off);
-                set_byte_of(SA, e >> 2, e & 3, esc_sm(h));
-            };
-            auto patch_b = [&](int i, int e4, uint32_t h) {
-                const int e = 16 * i + e4;
-                const uint32_t off = esc_off(h, bp[e]);
-#pragma unroll
-                for (int c = 0; c < 4; ++c)
-                    if (c == (e & 3)) set_byte(CB[c][i], (e & 15) >> 2, off);
-                set_byte_of(SB, e >> 2, e & 3, esc_sm(h));
-            };
-            uint32_t r_a, r_b;
-            if (rank_tokens(cna, cnb, es, lane, r_a, r_b)) {
-                if (cna != 0u) {
-                    const uint32_t h = esc_word(r_a, es, status);
-#pragma unroll
-                    for (int i = 0; i < NW; ++i)
-                        if (ma[i] != 0u) patch_a(i, (__ffs(ma[i]) - 1) >> 1, h);
-                }
-                if (cnb != 0u) {
-                    const uint32_t h = esc_word(r_b, es, status);
-#pragma unroll
-                    for (int i = 0; i < NW; ++i)
-                        if (mb[i] != 0u) patch_b(i, (__ffs(mb[i]) - 1) >> 1, h);
-                }
+            uint32_t cw;
+            if (MODE == 4) {
+                const int i = e >> 3, j = (e & 7) >> 1;
+                cw = (e & 1) ? prmt(HA[i], HB[i], sel_code(j)) : prmt(LA[i], LB[i], sel_code(j));
             } else {
-#pragma unroll
-                for (int i = 0; i < NW; ++i) {
-                    uint32_t mm = ma[i];
-                    while (mm != 0u) {
-                        const int e4 = (__ffs(mm) - 1) >> 1;
-                        mm &= mm - 1u;
-                        patch_a(i, e4, esc_word(r_a++, es, status));
-                    }
-                    mm = mb[i];
-                    while (mm != 0u) {
-                        const int e4 = (__ffs(mm) - 1) >> 1;
-                        mm &= mm - 1u;
-                        patch_b(i, e4, esc_word(r_b++, es, status));
-                    }
-                }
+                const int i = e >> 4, j = (e & 15) >> 2, k = e & 3;
+                cw = prmt(CA[k][i], CB[k][i], sel_code(j));
             }
-        }
-#pragma unroll
-        for (int e = 0; e < C::DV; ++e) {
-            const int i = e >> 4, j = (e & 15) >> 2, k = e & 3;
-            const uint32_t sg = prmt(SA[e >> 2], SB[e >> 2], sel_cross(e & 3));
-            const uint32_t cw = prmt(CA[k][i], CB[k][i], sel_code(j));
             o[e] = merge(sg, cw, b7[e]);
         }
     }
+};
+
+// Escapes of one V token half, through scratch: o[e] holds dim v0 + e of token A (low half) and
+// token B (high half), so element e of token A (B) sits at 16-bit position 2e (2e + 1).
+template <int D, int MODE>
+__device__ __forceinline__ void esc_v_half(uint32_t (&o)[Cfg<D>::DV], const VPair<D, MODE> &p,
+                                           uint8_t *scr, Esc &es, int *status, int lane) {
+    uint32_t *mine = reinterpret_cast<uint32_t *>(scr) + lane * Cfg<D>::DV;
+    __syncwarp();
+    regs_to(mine, o);
+    uint32_t ra, rb;
+    rank_tokens(p.ca, p.cb, es, lane, ra, rb);
+    uint16_t *h16 = reinterpret_cast<uint16_t *>(mine);
+#pragma unroll
+    for (int i = 0; i < VPair<D, MODE>::NW; ++i) {
+        uint32_t mm = p.ma[i];
+#pragma unroll 1
+        while (mm != 0u) {
+            const int e = VPair<D, MODE>::elem(i, __ffs(mm) - 1);
+            mm &= mm - 1u;
+            h16[2 * e] = uint16_t(esc_word(ra++, es, status));
+        }
+        mm = p.mb[i];
+#pragma unroll 1
+        while (mm != 0u) {
+            const int e = VPair<D, MODE>::elem(i, __ffs(mm) - 1);
+            mm &= mm - 1u;
+            h16[2 * e + 1] = uint16_t(esc_word(rb++, es, status));
+        }
+    }
+    regs_from(mine, o);
 }
 
 // ---- per-tile stages ----------------------------------------------------------------------------
 
-// Where the current tile's tensors sit in the ring slot (with the block's source alignment
+// Where the current sub-tile's tensors sit in the ring slot (with the block's source alignment
 // already applied), and the block's base exponents in its meta slot.
 struct TileView {
     const uint8_t *k_rows, *k_codes, *v_rows, *v_codes;
     const uint8_t *k_base, *v_base;  // this lane's first base byte
-    int rows;                        // valid tokens in the tile
+    uint8_t *k_scr, *v_scr;          // 16 D bytes of consumed sm rows (16-byte aligned), scratch
+    int rows;                        // valid tokens in the sub-tile
 };
 
 // S^T fragment of the tile: s0/s1 token g (queries 2t, 2t+1), s2/s3 token g + 8.
@@ -642,14 +524,29 @@ __device__ __forceinline__ void qk_tile(const TileView &tv, const uint32_t (&b7r
     const uint8_t *r0 = tv.k_rows + gi * RS + (MODE == 0 ? 2 * c0 : c0);
     const uint8_t *q0 = tv.k_codes + gi * CS + c0 * MODE / 8;
     s[0] = s[1] = s[2] = s[3] = 0.f;
+    if (MODE == 0) {
+        uint32_t ka0[C::NK], ka1[C::NK];
+        lds_words<C::NK>(r0, ka0);
+        lds_words<C::NK>(r0 + 8 * RS, ka1);
+#pragma unroll
+        for (int k = 0; k < C::KS; ++k)
+            mma_bf16(s[0], s[1], s[2], s[3], ka0[2 * k], ka1[2 * k], ka0[2 * k + 1], ka1[2 * k + 1],
+                     qb[k][0], qb[k][1]);
+        return;
+    }
     uint32_t b7[C::NK];
 #pragma unroll
     for (int p = 0; p < C::NK; ++p) b7[p] = b7r[p];
-    if (!C::B7REG && MODE != 0) load_b7k<D>(tv.k_base, b7);
+    if (!C::B7REG) load_b7k<D>(tv.k_base, b7);
     if (!C::SPLIT) {
         uint32_t ka0[C::NK], ka1[C::NK];
-        dec_k<D, MODE>(r0, q0, tv.k_base, b7, gi < tv.rows, es, status, ka0);
-        dec_k<D, MODE>(r0 + 8 * RS, q0 + 8 * CS, tv.k_base, b7, gi + 8 < tv.rows, es, status, ka1);
+        KRow<D, MODE> w0, w1;
+        w0.load(r0, q0, gi < tv.rows);
+        w1.load(r0 + 8 * RS, q0 + 8 * CS, gi + 8 < tv.rows);
+        w0.merge_into(b7, ka0);
+        w1.merge_into(b7, ka1);
+        if (__ballot_sync(FULL, w0.cnt != 0u) != 0u) esc_k_half<D, MODE>(ka0, w0, tv.k_scr, es, status, lane);
+        if (__ballot_sync(FULL, w1.cnt != 0u) != 0u) esc_k_half<D, MODE>(ka1, w1, tv.k_scr, es, status, lane);
 #pragma unroll
         for (int k = 0; k < C::KS; ++k)
             mma_bf16(s[0], s[1], s[2], s[3], ka0[2 * k], ka1[2 * k], ka0[2 * k + 1], ka1[2 * k + 1],
@@ -658,8 +555,10 @@ __device__ __forceinline__ void qk_tile(const TileView &tv, const uint32_t (&b7r
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
             uint32_t ka[C::NK];
-            dec_k<D, MODE>(r0 + 8 * h * RS, q0 + 8 * h * CS, tv.k_base, b7, gi + 8 * h < tv.rows, es,
-                           status, ka);
+            KRow<D, MODE> w;
+            w.load(r0 + 8 * h * RS, q0 + 8 * h * CS, gi + 8 * h < tv.rows);
+            w.merge_into(b7, ka);
+            if (__ballot_sync(FULL, w.cnt != 0u) != 0u) esc_k_half<D, MODE>(ka, w, tv.k_scr, es, status, lane);
 #pragma unroll
             for (int k = 0; k < C::KS; ++k) {
                 if (h == 0)
@@ -671,27 +570,22 @@ __device__ __forceinline__ void qk_tile(const TileView &tv, const uint32_t (&b7r
     }
 }
 
-// One V token half of this lane: tokens 2t + 8h (low halves) and 2t + 8h + 1 (high halves),
-// escapes patched, tokens past the tile's valid rows zeroed.
-template <int D, int MODE>
-__device__ __forceinline__ void v_half(const TileView &tv, const uint32_t (&b7)[Cfg<D>::DV],
-                                       int h, Esc &es, int *status, int lane,
-                                       uint32_t (&va)[Cfg<D>::DV]) {
-    using C = Cfg<D>;
-    const int gi = lane >> 2, tig = lane & 3;
-    constexpr int RS = MODE == 0 ? 2 * D : D;
-    constexpr int CS = D * MODE / 8;
-    const int v0 = gi * C::DV;
-    const int t = 2 * tig + 8 * h;
-    const uint8_t *r0 = tv.v_rows + t * RS + (MODE == 0 ? 2 * v0 : v0);
-    const uint8_t *q0 = tv.v_codes + t * CS + v0 * MODE / 8;
-    dec_v<D, MODE>(r0, r0 + RS, q0, q0 + CS, tv.v_base, b7, t < tv.rows, t + 1 < tv.rows, es, status,
-                   lane, va);
-    if (tv.rows < TT) {
-        const uint32_t keep = (t < tv.rows ? 0x0000FFFFu : 0u) | (t + 1 < tv.rows ? 0xFFFF0000u : 0u);
+// Raw V token pair (tokens 2t + 8h, 2t + 8h + 1) of this lane.
+template <int D>
+__device__ __forceinline__ void v_raw(const uint8_t *r0, int RS, uint32_t (&o)[Cfg<D>::DV]) {
+    uint32_t RA[Cfg<D>::DV / 2], RB[Cfg<D>::DV / 2];
+    lds_words<Cfg<D>::DV / 2>(r0, RA);
+    lds_words<Cfg<D>::DV / 2>(r0 + RS, RB);
 #pragma unroll
-        for (int e = 0; e < C::DV; ++e) va[e] &= keep;
-    }
+    for (int e = 0; e < Cfg<D>::DV; ++e) o[e] = prmt(RA[e >> 1], RB[e >> 1], (e & 1) ? 0x7632u : 0x5410u);
+}
+
+// Zero the halves of tokens past the sub-tile's valid rows (P is 0 there, V must be finite).
+template <int D>
+__device__ __forceinline__ void v_tail(int t, int rows, uint32_t (&va)[Cfg<D>::DV]) {
+    const uint32_t keep = (t < rows ? 0x0000FFFFu : 0u) | (t + 1 < rows ? 0xFFFF0000u : 0u);
+#pragma unroll
+    for (int e = 0; e < Cfg<D>::DV; ++e) va[e] &= keep;
 }
 
 // O^T += V^T P^T for the tile (P^T as B fragments: bh = bf16 part, bm = residual part).
@@ -700,14 +594,38 @@ __device__ __forceinline__ void pv_tile(const TileView &tv, const uint32_t (&b7r
                                         const uint32_t (&bh)[2], const uint32_t (&bm)[2], Esc &es,
                                         int *status, int lane, float (&acc)[Cfg<D>::KS][4]) {
     using C = Cfg<D>;
+    const int gi = lane >> 2, tig = lane & 3;
+    constexpr int RS = MODE == 0 ? 2 * D : D;
+    constexpr int CS = D * MODE / 8;
+    const int v0 = gi * C::DV;
+    const int t = 2 * tig;
+    const uint8_t *r0 = tv.v_rows + t * RS + (MODE == 0 ? 2 * v0 : v0);
+    const uint8_t *q0 = tv.v_codes + t * CS + v0 * MODE / 8;
     uint32_t b7[C::DV];
 #pragma unroll
     for (int e = 0; e < C::DV; ++e) b7[e] = b7r[e];
     if (!C::B7REG && MODE != 0) load_b7v<D>(tv.v_base, b7);
     if (!C::SPLIT) {
         uint32_t va0[C::DV], va1[C::DV];
-        v_half<D, MODE>(tv, b7, 0, es, status, lane, va0);
-        v_half<D, MODE>(tv, b7, 1, es, status, lane, va1);
+        if (MODE == 0) {
+            v_raw<D>(r0, RS, va0);
+            v_raw<D>(r0 + 8 * RS, RS, va1);
+        } else {
+            VPair<D, MODE> p0, p1;
+            p0.load(r0, r0 + RS, q0, q0 + CS, t < tv.rows, t + 1 < tv.rows);
+            p1.load(r0 + 8 * RS, r0 + 9 * RS, q0 + 8 * CS, q0 + 9 * CS, t + 8 < tv.rows,
+                    t + 9 < tv.rows);
+            p0.merge_into(b7, va0);
+            p1.merge_into(b7, va1);
+            if (__ballot_sync(FULL, (p0.ca | p0.cb) != 0u) != 0u)
+                esc_v_half<D, MODE>(va0, p0, tv.v_scr, es, status, lane);
+            if (__ballot_sync(FULL, (p1.ca | p1.cb) != 0u) != 0u)
+                esc_v_half<D, MODE>(va1, p1, tv.v_scr, es, status, lane);
+        }
+        if (tv.rows < TT) {
+            v_tail<D>(t, tv.rows, va0);
+            v_tail<D>(t + 8, tv.rows, va1);
+        }
 #pragma unroll
         for (int m = 0; m < C::KS; ++m) {
             mma_bf16(acc[m][0], acc[m][1], acc[m][2], acc[m][3], va0[2 * m], va0[2 * m + 1],
@@ -719,7 +637,17 @@ __device__ __forceinline__ void pv_tile(const TileView &tv, const uint32_t (&b7r
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
             uint32_t va[C::DV];
-            v_half<D, MODE>(tv, b7, h, es, status, lane, va);
+            if (MODE == 0) {
+                v_raw<D>(r0 + 8 * h * RS, RS, va);
+            } else {
+                VPair<D, MODE> p;
+                p.load(r0 + 8 * h * RS, r0 + (8 * h + 1) * RS, q0 + 8 * h * CS, q0 + (8 * h + 1) * CS,
+                       t + 8 * h < tv.rows, t + 8 * h + 1 < tv.rows);
+                p.merge_into(b7, va);
+                if (__ballot_sync(FULL, (p.ca | p.cb) != 0u) != 0u)
+                    esc_v_half<D, MODE>(va, p, tv.v_scr, es, status, lane);
+            }
+            if (tv.rows < TT) v_tail<D>(t + 8 * h, tv.rows, va);
 #pragma unroll
             for (int m = 0; m < C::KS; ++m) {
                 const uint32_t x0 = h == 0 ? va[2 * m] : 0u, x1 = h == 0 ? va[2 * m + 1] : 0u;
@@ -748,12 +676,13 @@ __device__ __forceinline__ void load_q(const uint16_t *q, int n_q, int stride,
 
 // ---- the worker -------------------------------------------------------------------------------
 
-// Walks the worker's flat blocks with one block of prefetch.
+// Walks the worker's flat blocks with one block of prefetch (flat indices fit 32 bits: the plan
+// refuses larger steps).
 struct Walker {
-    int64_t fb, fb1;
+    int fb, fb1;
     FlatBlock cur, nxt;
     int unit, nunit;
-    __device__ __forceinline__ void init(const AttnArgs &a, int64_t b0, int64_t b1) {
+    __device__ __forceinline__ void init(const AttnArgs &a, int b0, int b1) {
         fb = b0;
         fb1 = b1;
         cur = load_flat(a.flat, fb);
@@ -777,70 +706,82 @@ struct Walker {
     }
 };
 
+// Tokens per ring stage for a block: TSC when both tensors are coded, TT when either is raw.
+template <int D, bool BF16IN>
+__device__ __forceinline__ int stage_tokens(int km, int vm) {
+    return (BF16IN || km == 0 || vm == 0) ? TT : Cfg<D>::TSC;
+}
+
 // Copy side of the worker's ring.
 template <int D, bool BF16IN> struct Producer {
     using C = Cfg<D>;
     Walker w;
-    int tile = 0, stage = 0, bseq = 0, unit = -1;
-    const uint8_t *kb = nullptr, *vb = nullptr;
+    int tile = 0, stage = 0, bseq = 0;
+    const uint8_t *kr = nullptr, *vr = nullptr;  // row sections of the current block
+    int km = 0, vm = 0, st = TT;
 
-    __device__ __forceinline__ static void tensor(uint8_t *dst, const Sections &s, int mode, int tile, int rows,
-                                  int lane) {
-        const int t0 = tile * TT;
+    __device__ __forceinline__ static void tensor(uint8_t *dst, const uint8_t *rows, int mode,
+                                                  int n_tok, int t0, int n, int lane) {
         if (BF16IN || mode == 0) {
             copy_piece<TT * 2 * D + 16>(
-                dst, make_piece(s.rows + size_t(t0) * (2 * D), uint32_t(rows * 2 * D)), lane);
+                dst, make_piece(rows + size_t(t0) * (2 * D), uint32_t(n * 2 * D)), lane);
         } else {
-            copy_piece<TT * D + 16>(dst, make_piece(s.rows + size_t(t0) * D, uint32_t(rows * D)), lane);
-            copy_piece<TT * D / 2 + 16>(
+            copy_piece<C::TSC * D + 16>(dst, make_piece(rows + size_t(t0) * D, uint32_t(n * D)), lane);
+            const uint8_t *codes = rows + size_t(n_tok) * D;
+            copy_piece<C::TSC * D / 2 + 16>(
                 dst + C::CODE_OFF,
-                make_piece(s.codes + size_t(t0) * D * mode / 8, uint32_t(rows * D * mode / 8)), lane);
+                make_piece(codes + size_t(t0) * D * mode / 8, uint32_t(n * D * mode / 8)), lane);
         }
     }
-    __device__ __forceinline__ static void meta(uint8_t *base, uint8_t *escs, const Sections &s, int nesc, int lane) {
+    __device__ __forceinline__ static void meta(uint8_t *base, uint8_t *escs, const Sections &s,
+                                                int nesc, int lane) {
         copy_piece<D + 32>(base, make_piece(s.rows - D, D), lane);
         const Piece e = make_piece(s.esc, uint32_t(2 * nesc));
         if (esc_staged<D>(e, nesc)) copy_piece<C::ESCB>(escs, e, lane);
     }
 
-    // Issue tiles while a ring slot is free; a block start waits until the consumer is at most
+    // Issue stages while a ring slot is free; a block start waits until the consumer is at most
     // one block behind, so a meta slot is never overwritten while in use.
-    __device__ __forceinline__ void produce(const AttnArgs &a, uint8_t *ring, uint8_t *metas, int c_stage,
-                            int64_t c_fb, int lane) {
+    __device__ __forceinline__ void produce(const AttnArgs &a, uint8_t *ring, uint8_t *metas,
+                                            int c_stage, int c_fb, int lane) {
         while (w.fb < w.fb1 && stage - c_stage < C::NSTAGE) {
             if (tile == 0 && w.fb - c_fb >= 2) break;
             const FlatBlock &f = w.cur;
-            if (w.unit != unit) {
-                unit = w.unit;
-                kb = a.units[unit].k;
-                vb = a.units[unit].v;
+            if (tile == 0) {
+                km = BF16IN ? 0 : f.k_mode;
+                vm = BF16IN ? 0 : f.v_mode;
+                st = stage_tokens<D, BF16IN>(km, vm);
+                const Sections sk = sections<D, BF16IN>(a.units[w.unit].k, f.k_off, km, f.n_tok);
+                const Sections sv = sections<D, BF16IN>(a.units[w.unit].v, f.v_off, vm, f.n_tok);
+                kr = sk.rows;
+                vr = sv.rows;
+                if (!BF16IN) {
+                    uint8_t *ms = metas + (bseq & 1) * C::MSLOT;
+                    if (km != 0) meta(ms + C::M_K, ms + C::M_EK, sk, f.k_nesc, lane);
+                    if (vm != 0) meta(ms + C::M_V, ms + C::M_EV, sv, f.v_nesc, lane);
+                }
             }
-            const int rows = min(TT, int(f.valid) - tile * TT);
+            const int t0 = tile * st;
+            const int n = min(st, int(f.valid) - t0);
             uint8_t *slot = ring + (stage % C::NSTAGE) * C::SLOT;
-            const int km = BF16IN ? 0 : f.k_mode, vm = BF16IN ? 0 : f.v_mode;
-            const Sections sk = sections<D, BF16IN>(kb, f.k_off, km, f.n_tok);
-            const Sections sv = sections<D, BF16IN>(vb, f.v_off, vm, f.n_tok);
-            tensor(slot, sk, km, tile, rows, lane);
-            tensor(slot + C::TR, sv, vm, tile, rows, lane);
-            if (!BF16IN && tile == 0) {
-                uint8_t *ms = metas + (bseq & 1) * C::MSLOT;
-                if (km != 0) meta(ms + C::M_K, ms + C::M_EK, sk, f.k_nesc, lane);
-                if (vm != 0) meta(ms + C::M_V, ms + C::M_EV, sv, f.v_nesc, lane);
-            }
+            tensor(slot, kr, km, f.n_tok, t0, n, lane);
+            tensor(slot + C::TR, vr, vm, f.n_tok, t0, n, lane);
             cp_async_commit();
             ++stage;
-            if (++tile * TT >= int(f.valid)) {
+            if (t0 + st >= int(f.valid)) {
                 tile = 0;
                 ++bseq;
                 w.next(a);
+            } else {
+                ++tile;
             }
         }
     }
 };
 
 template <int D, bool BF16IN>
-__device__ __forceinline__ void worker(const AttnArgs &a, uint8_t *R, int wk, int64_t fb0,
-                                       int64_t fb1, int lane) {
+__device__ __forceinline__ void worker(const AttnArgs &a, uint8_t *R, int wk, int fb0, int fb1,
+                                       int lane) {
     using C = Cfg<D>;
     const int gi = lane >> 2, tig = lane & 3;
     uint8_t *ring = R;
@@ -849,12 +790,10 @@ __device__ __forceinline__ void worker(const AttnArgs &a, uint8_t *R, int wk, in
     pp.w.init(a, fb0, fb1);
     Walker cw;
     cw.init(a, fb0, fb1);
-    int tile = 0, stage = 0, bseq = 0, unit = -1;
-    int64_t seg_begin = fb0;
-    UnitDev cu{};
-    int kmode = 0, vmode = 0;
+    int tile = 0, stage = 0, bseq = 0;
+    int ubeg = 0, uend = 0, seg_begin = fb0;  // the current unit's flat block range
+    int kmode = 0, vmode = 0, st = TT;
     uint32_t kd = 0, vd = 0;  // source alignment of the block's row sections
-    const uint8_t *kbase = metas, *vbase = metas;
     Esc ek{0, 0, nullptr, nullptr}, ev{0, 0, nullptr, nullptr};
     uint32_t b7k[C::NK], b7v[C::DV];
 #pragma unroll
@@ -870,22 +809,20 @@ __device__ __forceinline__ void worker(const AttnArgs &a, uint8_t *R, int wk, in
         cp_async_wait(pp.stage - stage - 1);
         __syncwarp();
         const FlatBlock f = cw.cur;
+        const uint8_t *ms = metas + (bseq & 1) * C::MSLOT;
         if (tile == 0) {
-            if (cw.unit != unit) {
-                unit = cw.unit;
-                cu = a.units[unit];
-            }
+            const UnitDev *U = a.units + cw.unit;
+            ubeg = int(U->block_begin);
+            uend = ubeg + U->n_blocks;
             kmode = BF16IN ? 0 : f.k_mode;
             vmode = BF16IN ? 0 : f.v_mode;
-            const Sections sk = sections<D, BF16IN>(cu.k, f.k_off, kmode, f.n_tok);
-            const Sections sv = sections<D, BF16IN>(cu.v, f.v_off, vmode, f.n_tok);
+            st = stage_tokens<D, BF16IN>(kmode, vmode);
+            const Sections sk = sections<D, BF16IN>(U->k, f.k_off, kmode, f.n_tok);
+            const Sections sv = sections<D, BF16IN>(U->v, f.v_off, vmode, f.n_tok);
             kd = uint32_t(reinterpret_cast<uintptr_t>(sk.rows) & 15u);
             vd = uint32_t(reinterpret_cast<uintptr_t>(sv.rows) & 15u);
-            const uint8_t *ms = metas + (bseq & 1) * C::MSLOT;
-            kbase = ms + C::M_K + kd + tig * C::DK;
-            vbase = ms + C::M_V + vd + gi * C::DV;
             if (kmode != 0) {
-                if (C::B7REG) load_b7k<D>(kbase, b7k);
+                if (C::B7REG) load_b7k<D>(ms + C::M_K + kd + tig * C::DK, b7k);
                 const Piece e = make_piece(sk.esc, uint32_t(2 * f.k_nesc));
                 ek.run = 0;
                 ek.n = f.k_nesc;
@@ -893,7 +830,7 @@ __device__ __forceinline__ void worker(const AttnArgs &a, uint8_t *R, int wk, in
                 ek.sm = esc_staged<D>(e, f.k_nesc) ? ms + C::M_EK + e.data : nullptr;
             }
             if (vmode != 0) {
-                if (C::B7REG) load_b7v<D>(vbase, b7v);
+                if (C::B7REG) load_b7v<D>(ms + C::M_V + vd + gi * C::DV, b7v);
                 const Piece e = make_piece(sv.esc, uint32_t(2 * f.v_nesc));
                 ev.run = 0;
                 ev.n = f.v_nesc;
@@ -901,7 +838,7 @@ __device__ __forceinline__ void worker(const AttnArgs &a, uint8_t *R, int wk, in
                 ev.sm = esc_staged<D>(e, f.v_nesc) ? ms + C::M_EV + e.data : nullptr;
             }
             if (cw.fb == seg_begin) {
-                load_q<D>(cu.q, cu.n_q, cu.q_stride, qb, lane);
+                load_q<D>(U->q, U->n_q, U->q_stride, qb, lane);
                 m0 = m1 = -INFINITY;
                 l0 = l1 = 0.f;
 #pragma unroll
@@ -909,67 +846,75 @@ __device__ __forceinline__ void worker(const AttnArgs &a, uint8_t *R, int wk, in
             }
         }
         const uint8_t *slot = ring + (stage % C::NSTAGE) * C::SLOT;
-        TileView tv;
-        tv.rows = min(TT, int(f.valid) - tile * TT);
-        tv.k_rows = slot + kd;
-        tv.k_codes = slot + C::CODE_OFF + kd;
-        tv.v_rows = slot + C::TR + vd;
-        tv.v_codes = slot + C::TR + C::CODE_OFF + vd;
-        tv.k_base = kbase;
-        tv.v_base = vbase;
-        const bool last_tile = (tile + 1) * TT >= int(f.valid);
-        const int64_t ub = cu.block_begin + cu.n_blocks;
-        const bool seg_end = last_tile && (cw.fb + 1 == fb1 || cw.fb + 1 == ub);
+        const int t0 = tile * st;
+        const int rows_stage = min(st, int(f.valid) - t0);
+        const bool last_tile = t0 + st >= int(f.valid);
+        const bool seg_end = last_tile && (cw.fb + 1 == fb1 || cw.fb + 1 == uend);
 
-        // S^T = K Q^T
-        float s[4];
-        if (kmode == 4) qk_tile<D, 4>(tv, b7k, qb, ek, a.status, lane, s);
-        else if (kmode == 2) qk_tile<D, 2>(tv, b7k, qb, ek, a.status, lane, s);
-        else qk_tile<D, 0>(tv, b7k, qb, ek, a.status, lane, s);
-        if (gi >= tv.rows) s[0] = s[1] = -INFINITY;
-        if (gi + 8 >= tv.rows) s[2] = s[3] = -INFINITY;
+#pragma unroll 1
+        for (int sub = 0; sub < C::SUBS; ++sub) {
+            if (sub * TT >= rows_stage) break;
+            TileView tv;
+            tv.rows = min(TT, rows_stage - sub * TT);
+            tv.k_rows = slot + kd + sub * TT * (kmode == 0 ? 2 * D : D);
+            tv.k_codes = slot + C::CODE_OFF + kd + sub * TT * (D * kmode / 8);
+            tv.v_rows = slot + C::TR + vd + sub * TT * (vmode == 0 ? 2 * D : D);
+            tv.v_codes = slot + C::TR + C::CODE_OFF + vd + sub * TT * (D * vmode / 8);
+            tv.k_base = ms + C::M_K + kd + tig * C::DK;
+            tv.v_base = ms + C::M_V + vd + gi * C::DV;
+            tv.k_scr = C::SPLIT ? R + C::W_SCR : const_cast<uint8_t *>(slot) + sub * TT * D;
+            tv.v_scr = C::SPLIT ? R + C::W_SCR : const_cast<uint8_t *>(slot) + C::TR + sub * TT * D;
 
-        // online softmax over the tile's tokens; p = 2^(s log2e - m log2e)
-        float t0 = fmaxf(s[0], s[2]), t1 = fmaxf(s[1], s[3]);
+            // S^T = K Q^T
+            float s[4];
+            if (kmode == 4) qk_tile<D, 4>(tv, b7k, qb, ek, a.status, lane, s);
+            else if (kmode == 2) qk_tile<D, 2>(tv, b7k, qb, ek, a.status, lane, s);
+            else qk_tile<D, 0>(tv, b7k, qb, ek, a.status, lane, s);
+            if (gi >= tv.rows) s[0] = s[1] = -INFINITY;
+            if (gi + 8 >= tv.rows) s[2] = s[3] = -INFINITY;
+
+            // online softmax over the sub-tile's tokens; p = 2^(s log2e - m log2e)
+            float t0m = fmaxf(s[0], s[2]), t1m = fmaxf(s[1], s[3]);
 #pragma unroll
-        for (int o = 4; o < 32; o <<= 1) {
-            t0 = fmaxf(t0, __shfl_xor_sync(FULL, t0, o));
-            t1 = fmaxf(t1, __shfl_xor_sync(FULL, t1, o));
-        }
-        const float mn0 = fmaxf(m0, t0), mn1 = fmaxf(m1, t1);
-        const float ml0 = __fmul_rn(mn0, kLog2e), ml1 = __fmul_rn(mn1, kLog2e);
-        const float al0 = ex2(__fmaf_rn(m0, kLog2e, -ml0)), al1 = ex2(__fmaf_rn(m1, kLog2e, -ml1));
-        const float p0 = ex2(__fmaf_rn(s[0], kLog2e, -ml0)), p1 = ex2(__fmaf_rn(s[1], kLog2e, -ml1));
-        const float p2 = ex2(__fmaf_rn(s[2], kLog2e, -ml0)), p3 = ex2(__fmaf_rn(s[3], kLog2e, -ml1));
-        l0 = __fmaf_rn(l0, al0, __fadd_rn(p0, p2));
-        l1 = __fmaf_rn(l1, al1, __fadd_rn(p1, p3));
-        m0 = mn0;
-        m1 = mn1;
-
-        // P^T B fragments: bf16(p) and bf16(p - bf16(p))
-        uint32_t bh[2], bm[2];
-        {
-            const uint32_t h01 = pack_bf16x2(p1, p0), h23 = pack_bf16x2(p3, p2);
-            const float r0 = __fsub_rn(p0, bf16lo_to_f32(h01)), r1 = __fsub_rn(p1, bf16hi_to_f32(h01));
-            const float r2 = __fsub_rn(p2, bf16lo_to_f32(h23)), r3 = __fsub_rn(p3, bf16hi_to_f32(h23));
-            bh[0] = movm_t(h01);
-            bh[1] = movm_t(h23);
-            bm[0] = movm_t(pack_bf16x2(r1, r0));
-            bm[1] = movm_t(pack_bf16x2(r3, r2));
-        }
-        if (__any_sync(FULL, al0 != 1.0f || al1 != 1.0f)) {
-#pragma unroll
-            for (int m = 0; m < C::KS; ++m) {
-                acc[m][0] = __fmul_rn(acc[m][0], al0);
-                acc[m][1] = __fmul_rn(acc[m][1], al1);
-                acc[m][2] = __fmul_rn(acc[m][2], al0);
-                acc[m][3] = __fmul_rn(acc[m][3], al1);
+            for (int o = 4; o < 32; o <<= 1) {
+                t0m = fmaxf(t0m, __shfl_xor_sync(FULL, t0m, o));
+                t1m = fmaxf(t1m, __shfl_xor_sync(FULL, t1m, o));
             }
+            const float mn0 = fmaxf(m0, t0m), mn1 = fmaxf(m1, t1m);
+            const float ml0 = __fmul_rn(mn0, kLog2e), ml1 = __fmul_rn(mn1, kLog2e);
+            const float al0 = ex2(__fmaf_rn(m0, kLog2e, -ml0)), al1 = ex2(__fmaf_rn(m1, kLog2e, -ml1));
+            const float p0 = ex2(__fmaf_rn(s[0], kLog2e, -ml0)), p1 = ex2(__fmaf_rn(s[1], kLog2e, -ml1));
+            const float p2 = ex2(__fmaf_rn(s[2], kLog2e, -ml0)), p3 = ex2(__fmaf_rn(s[3], kLog2e, -ml1));
+            l0 = __fmaf_rn(l0, al0, __fadd_rn(p0, p2));
+            l1 = __fmaf_rn(l1, al1, __fadd_rn(p1, p3));
+            m0 = mn0;
+            m1 = mn1;
+
+            // P^T B fragments: bf16(p) and bf16(p - bf16(p))
+            uint32_t bh[2], bm[2];
+            {
+                const uint32_t h01 = pack_bf16x2(p1, p0), h23 = pack_bf16x2(p3, p2);
+                const float r0 = __fsub_rn(p0, bf16lo_to_f32(h01)), r1 = __fsub_rn(p1, bf16hi_to_f32(h01));
+                const float r2 = __fsub_rn(p2, bf16lo_to_f32(h23)), r3 = __fsub_rn(p3, bf16hi_to_f32(h23));
+                bh[0] = movm_t(h01);
+                bh[1] = movm_t(h23);
+                bm[0] = movm_t(pack_bf16x2(r1, r0));
+                bm[1] = movm_t(pack_bf16x2(r3, r2));
+            }
+            if (__any_sync(FULL, al0 != 1.0f || al1 != 1.0f)) {
+#pragma unroll
+                for (int m = 0; m < C::KS; ++m) {
+                    acc[m][0] = __fmul_rn(acc[m][0], al0);
+                    acc[m][1] = __fmul_rn(acc[m][1], al1);
+                    acc[m][2] = __fmul_rn(acc[m][2], al0);
+                    acc[m][3] = __fmul_rn(acc[m][3], al1);
+                }
+            }
+            // O^T += V^T P^T
+            if (vmode == 4) pv_tile<D, 4>(tv, b7v, bh, bm, ev, a.status, lane, acc);
+            else if (vmode == 2) pv_tile<D, 2>(tv, b7v, bh, bm, ev, a.status, lane, acc);
+            else pv_tile<D, 0>(tv, b7v, bh, bm, ev, a.status, lane, acc);
         }
-        // O^T += V^T P^T
-        if (vmode == 4) pv_tile<D, 4>(tv, b7v, bh, bm, ev, a.status, lane, acc);
-        else if (vmode == 2) pv_tile<D, 2>(tv, b7v, bh, bm, ev, a.status, lane, acc);
-        else pv_tile<D, 0>(tv, b7v, bh, bm, ev, a.status, lane, acc);
 
         if (seg_end) {
             float lt0 = l0, lt1 = l1;
@@ -980,17 +925,20 @@ __device__ __forceinline__ void worker(const AttnArgs &a, uint8_t *R, int wk, in
             }
             const int qa = 2 * tig, qc = 2 * tig + 1;
             const int d0 = gi * C::DV;
-            if (seg_begin == cu.block_begin && cw.fb + 1 == ub) {
+            if (seg_begin == ubeg && cw.fb + 1 == uend) {
+                const UnitDev *U = a.units + cw.unit;
+                const int n_q = U->n_q, stride = U->q_stride;
+                float *out = U->out;
                 const float inv0 = __frcp_rn(lt0), inv1 = __frcp_rn(lt1);
-                if (qa < cu.n_q) {
-                    float *o = cu.out + size_t(qa) * cu.q_stride + d0;
+                if (qa < n_q) {
+                    float *o = out + size_t(qa) * stride + d0;
 #pragma unroll
                     for (int m = 0; m < C::KS; ++m)
                         *reinterpret_cast<float2 *>(o + 2 * m) =
                             make_float2(__fmul_rn(acc[m][0], inv0), __fmul_rn(acc[m][2], inv0));
                 }
-                if (qc < cu.n_q) {
-                    float *o = cu.out + size_t(qc) * cu.q_stride + d0;
+                if (qc < n_q) {
+                    float *o = out + size_t(qc) * stride + d0;
 #pragma unroll
                     for (int m = 0; m < C::KS; ++m)
                         *reinterpret_cast<float2 *>(o + 2 * m) =
@@ -1035,7 +983,7 @@ __global__ void __launch_bounds__(32 * Cfg<D>::WARPS, 1) attn_kernel(const AttnA
     // consecutive workers on different SMs: neighbouring ranges often share a cost profile
     const int wk = warp * gridDim.x + blockIdx.x;
     if (wk >= a.n_workers) return;
-    const int64_t fb0 = a.range_begin[wk], fb1 = a.range_begin[wk + 1];
+    const int fb0 = int(a.range_begin[wk]), fb1 = int(a.range_begin[wk + 1]);
     if (fb0 >= fb1) return;
     worker<D, BF16IN>(a, smem + warp * C::WARP_BYTES, wk, fb0, fb1, lane);
 }
@@ -1114,7 +1062,10 @@ __global__ void __launch_bounds__(kCombineThreads) combine_kernel(const CombineA
 
 // Cost of one flat block for the worker split: 8 per attended token plus kEscCost per escape word
 // (a worker's time grows with its tokens and, on escape-dense blocks, with its escape words).
-constexpr uint32_t kEscCost = 2;
+#ifndef KVX_ESC_COST
+#define KVX_ESC_COST 4
+#endif
+constexpr uint32_t kEscCost = KVX_ESC_COST;
 __device__ __forceinline__ uint64_t block_cost(const FlatBlock &b) {
     return 8ull * b.valid + kEscCost * (uint64_t(b.k_nesc) + b.v_nesc);
 }
