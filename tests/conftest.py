@@ -35,6 +35,13 @@ def reference():
 
 
 @pytest.fixture(scope="session")
+def reference_or_none():
+    """The compiled reference library when oracle/_ref was built here, else None."""
+    import oracle as O
+    return O.reference()
+
+
+@pytest.fixture(scope="session")
 def kvx():
     import build
     build.build()
