@@ -315,6 +315,7 @@ int kvx_plan_create(const kvx_unit *units, int n_units, int n_q, int dim, int bl
             d.v = static_cast<const uint8_t *>(x.v);
             d.q = x.q + size_t(8) * g * dim;
             d.out = x.out + size_t(8) * g * dim;
+            d.lse = x.lse != nullptr ? x.lse + size_t(8) * g : nullptr;
             d.block_begin = total;
             d.n_blocks = nb;
             d.n_q = std::min(8, n_q - 8 * g);

@@ -929,7 +929,12 @@ __device__ __forceinline__ void worker(const AttnArgs &a, uint8_t *R, int wk, in
                 const UnitDev *U = a.units + cw.unit;
                 const int n_q = U->n_q, stride = U->q_stride;
                 float *out = U->out;
+                float *lse = U->lse;
                 const float inv0 = __frcp_rn(lt0), inv1 = __frcp_rn(lt1);
+                if (lse != nullptr && gi == 0) {
+                    if (qa < n_q) lse[qa] = m0 + logf(lt0);
+                    if (qc < n_q) lse[qc] = m1 + logf(lt1);
+                }
                 if (qa < n_q) {
                     float *o = out + size_t(qa) * stride + d0;
 #pragma unroll
@@ -1043,7 +1048,8 @@ __global__ void __launch_bounds__(kCombineThreads) combine_kernel(const CombineA
         if (tid < o) red[tid] = __fadd_rn(red[tid], red[tid + o]);
         __syncthreads();
     }
-    const float inv = __frcp_rn(red[0]);
+    const float lsum = red[0];
+    const float inv = __frcp_rn(lsum);
     __syncthreads();
     const int d = tid % D, sl = tid / D;
     float acc = 0.f;
@@ -1056,6 +1062,7 @@ __global__ void __launch_bounds__(kCombineThreads) combine_kernel(const CombineA
         for (int j = 1; j < S; ++j) v = __fadd_rn(v, red[j * D + d]);
         unit.out[size_t(g) * unit.q_stride + d] = __fmul_rn(v, inv);
     }
+    if (tid == 0 && unit.lse != nullptr) unit.lse[g] = M + logf(lsum);
 }
 
 // ---- worker ranges -----------------------------------------------------------------------------

@@ -30,7 +30,8 @@ struct UnitDev {
     int32_t n_blocks;
     int32_t n_q;          // <= 8 (larger query groups are split into several units)
     int32_t q_stride;     // elements between query rows of q / out
-    int32_t pad[3];
+    int32_t pad0;
+    float *lse;           // optional [n_q]: log-sum-exp of the scores per query
 };
 static_assert(sizeof(UnitDev) == 64, "UnitDev is 64 bytes");
 

@@ -73,7 +73,7 @@ class kvx_block(C.Structure):
 class kvx_unit(C.Structure):
     _fields_ = [("k", _vp), ("v", _vp), ("k_index", _vp), ("v_index", _vp), ("q", _vp),
                 ("out", _vp), ("k_bytes", C.c_uint64), ("v_bytes", C.c_uint64),
-                ("n_blocks", C.c_int32), ("seq", C.c_int32)]
+                ("n_blocks", C.c_int32), ("seq", C.c_int32), ("lse", _vp)]
 
 
 def _sig(name, res, args):
@@ -287,9 +287,9 @@ class Plan:
 
 
 def make_unit(k, v, q, out, *, k_index=None, v_index=None, k_bytes=0, v_bytes=0, n_blocks=0,
-              seq) -> kvx_unit:
+              seq, lse=None) -> kvx_unit:
     return kvx_unit(_addr(k), _addr(v), _addr(k_index), _addr(v_index), _addr(q), _addr(out),
-                    int(k_bytes), int(v_bytes), int(n_blocks), int(seq))
+                    int(k_bytes), int(v_bytes), int(n_blocks), int(seq), _addr(lse))
 
 
 def encode_batch_bounds(n_tensors, seq, head_dim, block_tokens=K_ENCODE_BLOCK):

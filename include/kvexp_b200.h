@@ -122,6 +122,8 @@ typedef struct kvx_unit {
     uint64_t v_bytes;
     int32_t n_blocks;  /* XKV blocks covering the first `seq` tokens */
     int32_t seq;       /* tokens attended */
+    float *lse;        /* optional [n_q] FP32: m + ln(l) of each query's softmax (the log of its
+                        * normaliser), for folding outputs of sequence shards; NULL = not written */
 } kvx_unit;
 
 typedef struct kvx_plan_s *kvx_plan;
