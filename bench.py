@@ -9,6 +9,11 @@ Default workload: BASELINE.json config[1] (24 layers x 2 KV heads x GQA 7 x head
 32768 tokens, block 128), synthetic seeded data.  With N > 1 (torchrun) every rank decodes its own
 full config[1] cache (weak scaling, no collective on the data path); time is the max over ranks.
 
+--config 3 holds one of 8 layer x KV head shards of config[3] per GPU (the whole config does not
+fit one GPU; N GPUs run N/8 of it, no collective).  --config 4 cuts config[4]'s 1M-token
+sequence into N block-aligned shards, one per GPU, and ends each step with one NCCL all-gather
+of (out, lse) and the rank-ordered fold kernel (strong scaling).
+
 Prints one JSON line (rank 0).  `--impl reference` times the unmodified reference library
 (compiled from its own sources into oracle/_ref) on this host's cores on the same workload.
 """
@@ -174,14 +179,14 @@ def cpu_reference_rate(qs, ks, vs, cfg, seconds, max_passes=50):
             break
     gbps = total * passes / el / 1e9
     return {"value": gbps, "unit": "GB/s", "cores": threads, "kind": kind,
-            "sample": f"{passes} full passes over all {n} units of {cfg.name} "
+            "sample": f"{passes} full passes over {n} units of {cfg.name} "
                       f"({total / 1e6:.1f} MB of XKV containers per pass), {what}, "
                       f"{el:.1f} s wall"}, el / passes
 
 
-def host_workload(cfg, seed):
+def host_workload(cfg, seed, n_units=None):
     """Host-side inputs for the reference arm: numpy synthetic data encoded by the reference's
-    own encoder (no GPU code)."""
+    own encoder (no GPU code), for the first n_units units (default all)."""
     import numpy as np
     import oracle as O
     import synth as S
@@ -189,7 +194,7 @@ def host_workload(cfg, seed):
     ref = O.reference()
     enc = ref.encode if ref is not None else O.oracle().encode
     qs, ks, vs = [], [], []
-    for u in range(cfg.units):
+    for u in range(cfg.units if n_units is None else n_units):
         kp = W.k_profile_of(cfg, u)
         k = S.synth_bf16(seed, S.stream_id(u, 0), cfg.seq, cfg.dim, kp, W.rate_of(kp))
         v = S.synth_bf16(seed, S.stream_id(u, 1), cfg.seq, cfg.dim, cfg.v_profile,
@@ -206,11 +211,10 @@ def run_reference(args, rank, world):
         return
     import workloads as W
     cfg = W.CONFIGS[args.config]
-    if cfg.units * cfg.seq * cfg.dim * 4 > 64 << 30:
-        print(json.dumps({"impl": "reference", "unavailable":
-                          f"{cfg.name} does not fit host memory for the CPU reference"}))
-        return
-    qs, ks, vs = host_workload(cfg, 0x12345678)
+    # a workload too large for host memory is timed on its first units (the metric is per byte)
+    per_unit = 4 * cfg.seq * cfg.dim
+    n_units = cfg.units if cfg.units * per_unit <= 8 << 30 else max(1, (4 << 30) // per_unit)
+    qs, ks, vs = host_workload(cfg, 0x12345678, n_units)
     import numpy as np
     import oracle as O
     ref = O.reference()
@@ -242,15 +246,51 @@ def run_reference(args, rank, world):
         "higher_is_better": True, "scaling": "weak",
         "vs_baseline": gbps / PUBLISHED_GBPS, "dtype": "bf16", "data": "synthetic",
         "config": {"workload": cfg.name, "units": n, "compressed_bytes_per_step": total,
-                   "backend": bname, "threads": threads},
+                   "units_of_workload": cfg.units, "backend": bname, "threads": threads},
         "cpu_baseline": {"value": gbps, "unit": "GB/s", "cores": threads, "kind": "reference",
-                         "sample": f"{steps} model_heads passes over {n} units, {bname}"},
+                         "sample": f"{steps} model_heads passes over {n} of {cfg.units} units, "
+                                   f"{bname}"},
         "e2e": {"value": gbps, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
 
 # ---- GPU arm ----------------------------------------------------------------------------------------
+
+GPU_SLOTS = 8          # config[3] is cut into 8 unit shards, one per GPU of an 8-GPU box
+SAMPLE_BYTES = 1 << 30  # host sample (CPU baseline, end-to-end) for workloads above this size
+
+
+def rank_share(cfg, rank, world):
+    """This rank's part of the workload: (config to build, unit ids or None, seed, description).
+
+    replica  -- every GPU decodes its own full cache (weak scaling, no collective);
+    units    -- GPU r holds unit shard r of GPU_SLOTS (weak scaling: N GPUs run N/8 of the
+                config; no collective);
+    sequence -- GPU r holds blocks [r*B/N, (r+1)*B/N) of every KV head (strong scaling); one
+                NCCL all-gather of (out, lse) and a rank-ordered fold end the step.
+    """
+    import dataclasses
+    import seqsplit
+    base = 0x12345678
+    if cfg.shard == "units":
+        if world > GPU_SLOTS:
+            raise SystemExit(f"{cfg.name} is sharded over at most {GPU_SLOTS} GPUs")
+        per = cfg.units // GPU_SLOTS
+        ids = list(range(rank * per, (rank + 1) * per))
+        return cfg, ids, base, (f"layer x KV head shards: GPU r holds units [r*{per}, (r+1)*{per}) "
+                                f"of {cfg.units} (one of {GPU_SLOTS} shards, 4 layers each); "
+                                "no collective")
+    if cfg.shard == "sequence":
+        nb = (cfg.seq + cfg.block - 1) // cfg.block
+        b0, b1 = seqsplit.shard_blocks(nb, world, rank)
+        sub = dataclasses.replace(cfg, seq=min(b1 * cfg.block, cfg.seq) - b0 * cfg.block)
+        how = (f"sequence split: GPU r holds blocks [r*{nb}/N, (r+1)*{nb}/N) of every KV head"
+               + ("; one NCCL all-gather of (out, lse) per step, then the rank-ordered fold "
+                  "kernel (kvx_fold_shards)" if world > 1 else " (N=1: the whole sequence)"))
+        return sub, None, base + 7919 * rank, how
+    return cfg, None, base + 7919 * rank, f"dp{world}: an independent cache per GPU, no collective"
+
 
 def run_kvx(args, rank, world, local):
     import numpy as np
@@ -263,16 +303,30 @@ def run_kvx(args, rank, world, local):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
     import kvexp_b200 as kvx
+    import seqsplit
     import workloads as W
-    cfg = W.CONFIGS[args.config]
-    seed = 0x12345678 + 7919 * rank
-    cache = W.build_cache(cfg, seed=seed)
-    replica = W.build_cache(cfg, seed=seed)  # second copy: consecutive steps read other buffers
-    caches = [cache, replica]
-    plans = [kvx.Plan(c.kvx_units(), cfg.group, cfg.dim, cfg.block) for c in caches]
+    full = W.CONFIGS[args.config]
+    cfg, unit_ids, seed, parallelism = rank_share(full, rank, world)
+    n_units = cfg.units if unit_ids is None else len(unit_ids)
+    cache = W.build_cache(cfg, unit_ids=unit_ids, seed=seed)
+    caches = [cache]
+    if cache.compressed_bytes < SAMPLE_BYTES:
+        # second copy: consecutive steps read other buffers, so no step finds the last one's
+        # blobs in L2
+        caches.append(W.build_cache(cfg, unit_ids=unit_ids, seed=seed))
+    exch = None
+    if cfg.shard == "sequence" and world > 1:
+        exch = seqsplit.ShardExchange(n_units * cfg.group, cfg.dim)
+        outs = exch.out_view().view(n_units, cfg.group, cfg.dim)
+        lses = exch.lse_view().view(n_units, cfg.group)
+        plans = [kvx.Plan(c.kvx_units(out=outs, lse=lses), cfg.group, cfg.dim, cfg.block)
+                 for c in caches]
+    else:
+        plans = [kvx.Plan(c.kvx_units(), cfg.group, cfg.dim, cfg.block) for c in caches]
     comp = cache.compressed_bytes
-    q_bytes = cfg.units * cfg.group * cfg.dim * 2
-    o_bytes = cfg.units * cfg.group * cfg.dim * 4
+    tight = 4 * cfg.seq * cfg.dim * n_units
+    q_bytes = n_units * cfg.group * cfg.dim * 2
+    o_bytes = n_units * cfg.group * cfg.dim * 4
     algo_bytes = comp + q_bytes + o_bytes
     stream = torch.cuda.current_stream()
     h = stream.cuda_stream
@@ -282,10 +336,21 @@ def run_kvx(args, rank, world, local):
     probe_gbs = kvx.hbm_read_probe(probe_buf, reps=5)
     del probe_buf
 
+    def step(i, evs=None):
+        p = plans[i % len(plans)]
+        if evs is not None:
+            evs[0].record(stream)
+        p.run_part(0, h)
+        if evs is not None:
+            evs[1].record(stream)
+        p.run_part(1, h)
+        if exch is not None:
+            exch.step(h)
+
     for i in range(max(3, args.warmup)):
-        plans[i % 2].run(h)
-    plans[0].check()
-    plans[1].check()
+        step(i)
+    for p in plans:
+        p.check()
     torch.cuda.synchronize()
     if dist:
         dist.barrier()
@@ -299,11 +364,7 @@ def run_kvx(args, rank, world, local):
     torch.cuda.synchronize()
     start.record(stream)
     for i in range(K):
-        p = plans[i % 2]
-        evs[i][0].record(stream)
-        p.run_part(0, h)
-        evs[i][1].record(stream)
-        p.run_part(1, h)
+        step(i, evs[i])
     end.record(stream)
     end.synchronize()
     torch.cuda.synchronize()
@@ -314,22 +375,35 @@ def run_kvx(args, rank, world, local):
     kern_ms = statistics.fmean(a.elapsed_time(b) for a, b in evs)
     for p in plans:
         p.check()
+    comp_all = comp * world
     if dist:
         t = torch.tensor([elapsed_ms, kern_ms], dtype=torch.float64, device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         elapsed_ms, kern_ms = float(t[0]), float(t[1])
+        c = torch.tensor([comp, tight], dtype=torch.float64, device="cuda")
+        dist.all_reduce(c, op=dist.ReduceOp.SUM)
+        comp_all, tight_all = float(c[0]), float(c[1])
+    else:
+        tight_all = tight
     ms_step = elapsed_ms / K
-    value = comp * world * K / (elapsed_ms * 1e-3) / 1e9
+    value = comp_all * K / (elapsed_ms * 1e-3) / 1e9
+
+    # the host sample: every unit when the workload is small, else the first units up to about
+    # SAMPLE_BYTES of containers
+    sample = list(range(n_units))
+    if comp > SAMPLE_BYTES:
+        per_unit = comp / n_units
+        sample = list(range(max(1, min(n_units, int(SAMPLE_BYTES // per_unit)))))
 
     # end to end through the reference-facing C ABI with pinned host buffers
     e2e = None
-    if not args.no_e2e:
-        qs, ks, vs = cache.host_blobs()
+    if not args.no_e2e and exch is None:
+        qs, ks, vs = cache.host_blobs(sample)
         pk = [torch.from_numpy(x).pin_memory() for x in ks]
         pv = [torch.from_numpy(x).pin_memory() for x in vs]
         pq = [torch.from_numpy(x.view(np.int16)).pin_memory() for x in qs]
         po = [torch.zeros((cfg.group, cfg.dim), dtype=torch.float32).pin_memory()
-              for _ in range(cfg.units)]
+              for _ in sample]
         call = lambda: kvx.attention_decode_units(
             0, pq, pk, [x.numel() for x in pk], pv, [x.numel() for x in pv], po, cfg.group,
             cfg.dim, cfg.seq)
@@ -341,19 +415,22 @@ def run_kvx(args, rank, world, local):
             call()
             ts.append(time.perf_counter() - t0)
         e2e_s = sum(ts) / len(ts)
+        s_bytes = sum(x.numel() for x in pk) + sum(x.numel() for x in pv)
         if dist:
             t = torch.tensor([e2e_s], dtype=torch.float64, device="cuda")
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             e2e_s = float(t[0])
-        e2e = {"value": comp * world / e2e_s / 1e9, "unit": "GB/s",
-               "h2d_bytes_per_step": comp + q_bytes, "d2h_bytes_per_step": o_bytes,
+        e2e = {"value": s_bytes * world / e2e_s / 1e9, "unit": "GB/s",
+               "h2d_bytes_per_step": s_bytes + len(sample) * cfg.group * cfg.dim * 2,
+               "d2h_bytes_per_step": len(sample) * cfg.group * cfg.dim * 4,
                "ms_per_step": e2e_s * 1e3, "steps": args.e2e_steps,
+               "units_per_gpu": len(sample),
                "path": "kvx_attention_decode_units (C ABI) with pinned host blobs, one call "
                        "per step: H2D of every blob and query, header walks, decode attention, "
                        "D2H of outputs"}
         # the outputs of the host path must equal the device-resident plan's outputs
         got = np.stack([o.numpy() for o in po])
-        want = cache.out.cpu().numpy()
+        want = cache.out[: len(sample)].cpu().numpy()
         if not np.array_equal(got.view(np.uint32), want.view(np.uint32)):
             rel = np.max(np.abs(got - want) / np.maximum(np.abs(want), 1e-3))
             e2e["check"] = f"host-path outputs differ from the device plan (max rel {rel:.2e})"
@@ -362,9 +439,12 @@ def run_kvx(args, rank, world, local):
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        qs, ks, vs = cache.host_blobs()
+        qs, ks, vs = cache.host_blobs(sample)
         cpu, _ = cpu_reference_rate(qs, ks, vs, cfg, args.cpu_seconds)
 
+    launches = K * plans[0].launches + (K if exch is not None else 0)
+    for p in plans:
+        p.close()
     if dist:
         dist.barrier()
         dist.destroy_process_group()
@@ -376,17 +456,20 @@ def run_kvx(args, rank, world, local):
     line = {
         "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": K,
         "warmup": max(3, args.warmup), "ms_per_step": ms_step, "us_per_step": ms_step * 1e3,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": value / PUBLISHED_GBPS,
+        "higher_is_better": True,
+        "scaling": "strong" if cfg.shard == "sequence" else "weak",
+        "vs_baseline": value / PUBLISHED_GBPS,
         "dtype": "bf16", "data": "synthetic (seeded generator; BASELINE.json distributions)",
         "config": {
-            "workload": cfg.name, "units_per_gpu": cfg.units, "block_tokens": cfg.block,
-            "compressed_bytes_per_gpu_step": comp, "tight_bytes_per_gpu_step": cfg.tight_bytes,
-            "container_ratio": comp / cfg.tight_bytes,
-            "parallelism": f"dp{world}: an independent cache per GPU, no collective",
-            "l2": "inputs larger than L2 (container > 126 MB) and two cache copies alternate "
-                  "between steps",
+            "workload": full.name, "units_per_gpu": n_units, "seq_per_gpu": cfg.seq,
+            "block_tokens": cfg.block, "compressed_bytes_per_gpu_step": comp,
+            "tight_bytes_per_gpu_step": tight,
+            "container_ratio": comp / tight,
+            "parallelism": parallelism,
+            "l2": ("inputs larger than L2 (container > 126 MB)"
+                   + ("; two cache copies alternate between steps" if len(caches) > 1 else "")),
         },
-        "tight_equiv_gbps": cfg.tight_bytes * world * K / (elapsed_ms * 1e-3) / 1e9,
+        "tight_equiv_gbps": tight_all * K / (elapsed_ms * 1e-3) / 1e9,
         "pct_of_hbm_peak": 100.0 * (value / world) / peak,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "traffic": traffic,
@@ -396,10 +479,15 @@ def run_kvx(args, rank, world, local):
                      "device_read_probe_gbs": probe_gbs},
         "cpu_baseline": cpu,
         "e2e": e2e,
-        "gpu_launches": K * plans[0].launches,
+        "gpu_launches": launches,
         "clocks": clocks,
         "impl": "kvexp_b200",
     }
+    if exch is not None:
+        line["exchange"] = {"collective": "NCCL all_gather_into_tensor", "bytes_per_rank":
+                            exch.bytes_per_rank, "fold": "kvx_fold_shards, rank order"}
+        line["e2e_note"] = ("no end-to-end line for the sequence split: the host-buffer entry "
+                            "points return no lse to fold")
     print(json.dumps(line), flush=True)
 
 

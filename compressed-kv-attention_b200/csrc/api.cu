@@ -48,6 +48,8 @@ const char *detail_message(int code, int detail) {
     case DERR_TIMEOUT: return "a bounded device wait timed out";
     case DERR_INDEX_CAP: return "xkv block index capacity exceeded";
     case DERR_RANGE: return "xkv block index entry outside its blob";
+    case DERR_ESC_CAP:
+        return "kvx_attention_decode_noalloc: the blobs' escape positions exceed the fixed scratch";
     default: return "device error";
     }
 }
@@ -221,7 +223,7 @@ struct kvx_plan_s {
     cudaStream_t s = nullptr;
     UnitDev *units = nullptr;
     FlatBlock *flat = nullptr;
-    int32_t *flat_unit = nullptr;
+    uint16_t *esc = nullptr;  // escape records of the step's coded blocks
     int64_t *range_begin = nullptr;
     float *partials = nullptr;
     int32_t *split_units = nullptr;
@@ -292,7 +294,7 @@ int kvx_plan_create(const kvx_unit *units, int n_units, int n_q, int dim, int bl
     const int groups = (n_q + 7) / 8;
     std::vector<kvx_unit> vu;
     std::vector<UnitDev> ud;
-    std::vector<int64_t> begin;
+    std::vector<int64_t> begin, src;
     int64_t total = 0;
     vu.reserve(size_t(n_units) * groups);
     for (int u = 0; u < n_units; ++u) {
@@ -321,6 +323,8 @@ int kvx_plan_create(const kvx_unit *units, int n_units, int n_q, int dim, int bl
             d.n_q = std::min(8, n_q - 8 * g);
             d.q_stride = dim;
             ud.push_back(d);
+            // query groups of one unit share its K/V blocks and their escape records
+            src.push_back(g == 0 ? total : begin[begin.size() - size_t(g)]);
             begin.push_back(total);
             total += nb;
         }
@@ -338,26 +342,42 @@ int kvx_plan_create(const kvx_unit *units, int n_units, int n_q, int dim, int bl
     p->grid = (p->n_workers + per_cta - 1) / per_cta;
     std::vector<int64_t> tb(size_t(p->n_workers) + 1);
     kvx_unit *dvu = nullptr;
-    int64_t *dbegin = nullptr;
+    int64_t *dbegin = nullptr, *dsrc = nullptr;
+    unsigned long long *desc_total = nullptr;
     cudaError_t e = cudaSuccess;
     if ((e = plan_alloc(p, &p->units, ud.size())) != cudaSuccess ||
         (e = plan_alloc(p, &p->flat, size_t(total))) != cudaSuccess ||
-        (e = plan_alloc(p, &p->flat_unit, size_t(total))) != cudaSuccess ||
         (e = plan_alloc(p, &p->range_begin, tb.size())) != cudaSuccess ||
         (e = plan_alloc(p, &p->partials, size_t(p->n_workers) * 2 * partial_stride(dim))) != cudaSuccess ||
         (e = plan_alloc(p, &p->split_units, ud.size())) != cudaSuccess ||
         (e = plan_alloc(p, &p->status, 2)) != cudaSuccess ||
         (e = plan_alloc(p, &dvu, vu.size())) != cudaSuccess ||
-        (e = plan_alloc(p, &dbegin, begin.size())) != cudaSuccess) {
+        (e = plan_alloc(p, &dbegin, begin.size())) != cudaSuccess ||
+        (e = plan_alloc(p, &dsrc, src.size())) != cudaSuccess ||
+        (e = plan_alloc(p, &desc_total, 1)) != cudaSuccess) {
         delete p;
         return fail(KVX_ERR_CUDA, std::string("kvx_plan_create: ") + cudaGetErrorString(e));
     }
     cudaMemcpy(p->units, ud.data(), ud.size() * sizeof(UnitDev), cudaMemcpyHostToDevice);
     cudaMemcpy(dvu, vu.data(), vu.size() * sizeof(kvx_unit), cudaMemcpyHostToDevice);
     cudaMemcpy(dbegin, begin.data(), begin.size() * sizeof(int64_t), cudaMemcpyHostToDevice);
+    cudaMemcpy(dsrc, src.data(), src.size() * sizeof(int64_t), cudaMemcpyHostToDevice);
     cudaMemset(p->status, 0, 2 * sizeof(int));
-    e = launch_build_flat(dvu, dbegin, p->n_units, dim, block_tokens, bf16, p->flat, p->flat_unit,
+    e = launch_build_flat(dvu, dbegin, dsrc, p->n_units, dim, block_tokens, bf16, p->flat,
                           p->status, nullptr);
+    // escape records: offsets, then (with the array sized) the records
+    unsigned long long esc_total = 0;
+    if (e == cudaSuccess && !bf16)
+        e = launch_esc_layout(p->flat, total, desc_total, ~0ull, p->status, nullptr);
+    if (e == cudaSuccess && !bf16)
+        e = cudaMemcpy(&esc_total, desc_total, sizeof esc_total, cudaMemcpyDeviceToHost);
+    if (e == cudaSuccess && esc_total > 0xFFFFFFFFull) {
+        delete p;
+        return fail(KVX_ERR_UNSUPPORTED, "kvx_plan_create: more than 2^32 escape record entries");
+    }
+    if (e == cudaSuccess) e = plan_alloc(p, &p->esc, size_t(esc_total));
+    if (e == cudaSuccess && esc_total > 0)
+        e = launch_esc_fill(p->units, p->flat, total, dim, p->esc, esc_total, p->status, nullptr);
     if (e == cudaSuccess) e = cudaDeviceSynchronize();
     if (e != cudaSuccess) {
         delete p;
@@ -425,7 +445,7 @@ int kvx_plan_run_part(kvx_plan p, int part, void *stream) {
     AttnArgs a{};
     a.units = p->units;
     a.flat = p->flat;
-    a.flat_unit = p->flat_unit;
+    a.esc = p->esc;
     a.range_begin = p->range_begin;
     a.partials = p->partials;
     a.status = p->status;
@@ -972,6 +992,18 @@ extern "C" int kvx_hbm_read_probe(const void *buf, size_t bytes, int reps, doubl
     return KVX_OK;
 }
 
+// ---- fold of sequence shards ---------------------------------------------------------------
+
+extern "C" int kvx_fold_shards(const float *parts, int n_parts, int n_rows, int dim, float *out,
+                               float *lse_out, void *stream) {
+    if (parts == nullptr || out == nullptr || n_parts <= 0 || n_rows <= 0 || dim <= 0 ||
+        dim > kMaxHeadDim)
+        return fail(KVX_ERR_INVALID_ARGUMENT, "kvx_fold_shards: bad argument");
+    KVX_CUDA(launch_fold(parts, n_parts, n_rows, dim, out, lse_out,
+                         static_cast<cudaStream_t>(stream)));
+    return KVX_OK;
+}
+
 // ---- decode attention without allocation ---------------------------------------------------
 //
 // kvx_attention_decode_noalloc is for callers that must not allocate GPU memory once they are
@@ -983,7 +1015,8 @@ extern "C" int kvx_hbm_read_probe(const void *buf, size_t bytes, int reps, doubl
 
 namespace kvx {
 namespace {
-constexpr size_t kNoAllocScratchBytes = size_t(8) << 20;  // 8 MiB per device
+constexpr size_t kNoAllocScratchBytes = size_t(16) << 20;  // 16 MiB per device
+constexpr size_t kNoAllocEscEntries = size_t(3) << 20;      // escape record entries (6 MiB)
 constexpr int kNoAllocMaxBlocks = 8192;                   // XKV blocks per tensor
 constexpr int kNoAllocMaxQueries = 64;                    // queries per call (8 groups of 8)
 constexpr int kNoAllocMaxWorkers = 4096;
@@ -1055,7 +1088,8 @@ extern "C" int kvx_attention_decode_noalloc(const uint16_t *q, const uint8_t *k_
     cudaStream_t s = static_cast<cudaStream_t>(stream);
 
     // Scratch layout (256-byte aligned pieces): status | units | unit descriptors | block
-    // begins | split units | flat blocks | flat units | worker ranges | partial states.
+    // begins | record sources | split units | flat blocks | worker ranges | record size |
+    // escape records | partial states.
     const int groups = (n_q + 7) / 8;
     const int64_t total = int64_t(groups) * n_blocks;
     size_t off = 0;
@@ -1068,12 +1102,14 @@ extern "C" int kvx_attention_decode_noalloc(const uint16_t *q, const uint8_t *k_
     UnitDev *d_units = reinterpret_cast<UnitDev *>(take(kNoAllocMaxQueries / 8 * sizeof(UnitDev)));
     kvx_unit *d_vu = reinterpret_cast<kvx_unit *>(take(kNoAllocMaxQueries / 8 * sizeof(kvx_unit)));
     int64_t *d_begin = reinterpret_cast<int64_t *>(take(kNoAllocMaxQueries / 8 * sizeof(int64_t)));
+    int64_t *d_src = reinterpret_cast<int64_t *>(take(kNoAllocMaxQueries / 8 * sizeof(int64_t)));
     int32_t *d_split = reinterpret_cast<int32_t *>(take(kNoAllocMaxQueries / 8 * sizeof(int32_t)));
     FlatBlock *d_flat = reinterpret_cast<FlatBlock *>(
         take(size_t(kNoAllocMaxQueries / 8) * kNoAllocMaxBlocks * sizeof(FlatBlock)));
-    int32_t *d_flat_unit = reinterpret_cast<int32_t *>(
-        take(size_t(kNoAllocMaxQueries / 8) * kNoAllocMaxBlocks * sizeof(int32_t)));
     int64_t *d_range = reinterpret_cast<int64_t *>(take((kNoAllocMaxWorkers + 1) * sizeof(int64_t)));
+    unsigned long long *d_esc_total =
+        reinterpret_cast<unsigned long long *>(take(sizeof(unsigned long long)));
+    uint16_t *d_esc = reinterpret_cast<uint16_t *>(take(kNoAllocEscEntries * sizeof(uint16_t)));
     float *d_partials = reinterpret_cast<float *>(base + off);
     const size_t per_worker = 2 * size_t(partial_stride(dim)) * sizeof(float);
     const int64_t fit = int64_t((kNoAllocScratchBytes - off) / per_worker);
@@ -1085,6 +1121,8 @@ extern "C" int kvx_attention_decode_noalloc(const uint16_t *q, const uint8_t *k_
     std::vector<kvx_unit> vu(static_cast<size_t>(groups));
     std::vector<UnitDev> ud(static_cast<size_t>(groups));
     std::vector<int64_t> begin(static_cast<size_t>(groups));
+    // every query group reads the same K/V blocks: their escape records are built once
+    const std::vector<int64_t> srcs(static_cast<size_t>(groups), 0);
     for (int g = 0; g < groups; ++g) {
         kvx_unit &x = vu[size_t(g)];
         x.k = k_xkv;
@@ -1126,16 +1164,19 @@ extern "C" int kvx_attention_decode_noalloc(const uint16_t *q, const uint8_t *k_
     KVX_CUDA(cudaMemcpyAsync(d_units, ud.data(), ud.size() * sizeof(UnitDev), cudaMemcpyHostToDevice, s));
     KVX_CUDA(cudaMemcpyAsync(d_vu, vu.data(), vu.size() * sizeof(kvx_unit), cudaMemcpyHostToDevice, s));
     KVX_CUDA(cudaMemcpyAsync(d_begin, begin.data(), begin.size() * sizeof(int64_t), cudaMemcpyHostToDevice, s));
+    KVX_CUDA(cudaMemcpyAsync(d_src, srcs.data(), srcs.size() * sizeof(int64_t), cudaMemcpyHostToDevice, s));
     KVX_CUDA(cudaMemcpyAsync(d_range, tb.data(), tb.size() * sizeof(int64_t), cudaMemcpyHostToDevice, s));
     if (!split.empty())
         KVX_CUDA(cudaMemcpyAsync(d_split, split.data(), split.size() * sizeof(int32_t),
                                  cudaMemcpyHostToDevice, s));
-    KVX_CUDA(launch_build_flat(d_vu, d_begin, groups, dim, kDefaultBlock, false, d_flat, d_flat_unit,
+    KVX_CUDA(launch_build_flat(d_vu, d_begin, d_src, groups, dim, kDefaultBlock, false, d_flat,
                                status, s));
+    KVX_CUDA(launch_esc_layout(d_flat, total, d_esc_total, kNoAllocEscEntries, status, s));
+    KVX_CUDA(launch_esc_fill(d_units, d_flat, total, dim, d_esc, kNoAllocEscEntries, status, s));
     AttnArgs a{};
     a.units = d_units;
     a.flat = d_flat;
-    a.flat_unit = d_flat_unit;
+    a.esc = d_esc;
     a.range_begin = d_range;
     a.partials = d_partials;
     a.status = status;

@@ -5,22 +5,29 @@
 // for the GPU:
 //
 //  * The step's (unit, block) pairs are flattened; each worker warp owns a contiguous range and
-//    streams the compressed 16-token tiles of K and V (sign/mantissa rows and packed exponent
-//    residuals, or raw BF16 rows) through its own shared-memory ring with cp.async, one cp.async
-//    group per tile.  A block's base exponents and escape words ride along with its first tile.
-//    Only the compressed bytes cross HBM, and no warp ever waits on another warp.
+//    streams stages of TS tokens of K and V through its own shared-memory ring with cp.async, one
+//    cp.async group per stage: sign/mantissa rows, packed exponent residuals, and the stage's
+//    escape words with their element positions -- or raw BF16 rows.  A block's base exponents ride
+//    along with its first stage.  Only the compressed bytes cross HBM (plus, for a coded block
+//    with escapes, its escape record: 2 bytes per escape word and a 32-byte count header, built
+//    once per plan), and no warp ever waits on another warp.
 //  * K rows are rebuilt straight into mma.sync A fragments: lane (g, t) rebuilds tokens g and g+8,
 //    head dims [t D/4, (t+1) D/4).  The MMA's k index runs over the head dims in that permuted
 //    order and the query B fragments use the same order, so S = K Q^T (tokens x queries, fp32
-//    accumulate) needs no shared-memory staging of a BF16 tile.
-//  * The online softmax runs on the S fragments: lane (g, t) holds queries 2t and 2t+1, which are
-//    also the output columns it accumulates, so the rescale factors never leave the lane.
+//    accumulate) needs no BF16 tile in shared memory.  A pair of elements costs four instructions:
+//    two byte permutes (sign/mantissa bytes; exponent residuals), one multiply-add that adds the
+//    residual to the base exponent, and one bit-select.  A block's sections start 0 or 2 bytes
+//    past a 4-byte boundary of the ring (every size and offset in an XKV blob is even); the
+//    permutes take that shift in their selectors.
+//  * The online softmax runs on the S fragments of a whole stage: lane (g, t) holds queries 2t and
+//    2t+1, which are also the output columns it accumulates, so the rescale factors never leave
+//    the lane.
 //  * V rows are rebuilt into A fragments of V^T: lane (g, t) rebuilds tokens 2t, 2t+1, 2t+8, 2t+9,
 //    head dims [g D/8, (g+1) D/8).  O^T += V^T P^T with P^T split into a bf16 part and a bf16
 //    residual part (two MMAs), so P enters with 16 significant bits.
-//  * Exponent escapes are patched in the staged words before the rebuild, in the container's scan
-//    order (token-major); the lane order of both fragment layouts gives each sentinel its rank with
-//    a few warp ballots.
+//  * Exponent escapes: a row half whose tokens hold escape words goes to scratch, each escape word
+//    is stored over its element (one 16-bit store, at the position the block's escape record
+//    gives) and the half is read back.  Halves without escapes skip all of it.
 //  * Unit segments that span several workers leave (m, l, acc) partial states that combine_kernel
 //    folds in worker order with merge_state semantics (src/softmax.hpp:16-30), then finalizes like
 //    finalize_state (src/softmax.hpp:32-41: reciprocal, then multiply).
@@ -29,14 +36,14 @@
 // blocks and worker ranges it produces bit-identical outputs to the XKV variant, because both
 // rebuild identical BF16 fragments and run identical arithmetic afterwards.  (Ranges are one block
 // per worker whenever the step has no more blocks than workers; beyond that they are balanced by
-// cost, and escape words count towards an XKV block's cost.)
+// cost.)
 #include "attention.cuh"
 
 namespace kvx {
 namespace {
 
 constexpr uint32_t FULL = 0xFFFFFFFFu;
-constexpr int TT = 16;  // tokens per tile (one m16 block of the QK MMA)
+constexpr int TT = 16;  // tokens per MMA tile (one m16 block of the QK MMA)
 constexpr float kLog2e = 1.4426950408889634f;
 
 // 2^x by the SFU (ex2.approx.f32, subnormal results kept).
@@ -50,9 +57,6 @@ __host__ __device__ constexpr int round16(int x) { return (x + 15) & ~15; }
 __host__ __device__ constexpr int cmin(int a, int b) { return a < b ? a : b; }
 __host__ __device__ constexpr int cmax(int a, int b) { return a > b ? a : b; }
 
-#ifndef KVX_NSTAGE64
-#define KVX_NSTAGE64 2
-#endif
 #ifndef KVX_MAXWARPS
 #define KVX_MAXWARPS 12
 #endif
@@ -62,45 +66,33 @@ template <int D> struct Cfg {
     static constexpr int NK = D / 8;        // K fragment registers per row (dim pairs)
     static constexpr int DV = D / 8;        // head dims per lane in a V token (= V registers)
     static constexpr int KS = D / 16;       // k-steps of QK = M-tiles of PV
-    static constexpr bool SPLIT = D > 128;  // rebuild row halves one at a time (register budget)
-    static constexpr bool B7REG = D <= 128; // keep the block's base exponents in registers
-    static constexpr int ESC_CAP = 1536;    // escape bytes staged per block and tensor
-    // A ring stage holds TSC tokens of a coded block or TT tokens of a raw one (raw rows take
-    // two bytes per element, coded ones 1.25-1.5), for K and V.
-    static constexpr int TSC = D <= 128 ? 2 * TT : TT;
-    static constexpr int SUBS = TSC / TT;         // 16-token sub-tiles per stage at most
-    static constexpr int TR = round16(cmax(TSC * D * 3 / 2 + 48, TT * 2 * D + 32));  // one tensor
-    static constexpr int CODE_OFF = TSC * D + 16;  // residual-code rows inside a coded tensor stage
-    static constexpr int SLOT = 2 * TR;            // K stage | V stage
-    static constexpr int NSTAGE = D <= 32 ? 3 : D == 64 ? KVX_NSTAGE64 : 2;
+    static constexpr bool SPLIT = D > 128;  // rebuild and multiply row halves one at a time
+    static constexpr int TS = D <= 64 ? 32 : 16;  // tokens per ring stage
+    static constexpr int SUBS = TS / TT;          // MMA tiles per stage
+    // One tensor's stage: sign/mantissa rows | residual codes | escape words | their positions,
+    // or TS raw BF16 rows -- both fit 2 TS D bytes (escapes beyond ESC_CAP stay in HBM).
+    static constexpr int ESC_CAP = TS * D / 8;
+    static constexpr int CODE_OFF = TS * D + 16;
+    static constexpr int EV_OFF = CODE_OFF + TS * D / 2 + 16;
+    static constexpr int EP_OFF = EV_OFF + 2 * ESC_CAP + 16;
+    static constexpr int TR = round16(cmax(EP_OFF + 2 * ESC_CAP + 16, TS * 2 * D + 16));
+    static constexpr int SLOT = 2 * TR;  // K stage | V stage
+    static constexpr int NSTAGE = D <= 32 ? 3 : 2;
     static_assert(NSTAGE >= 2 && NSTAGE <= 4, "stage waits cover at most 3 younger groups");
     static constexpr int BASE = round16(D + 32);  // one block's base exponents (+ alignment slack)
-    static constexpr int ESCB = ESC_CAP + 32;
-    static constexpr int M_K = 0, M_V = BASE, M_EK = 2 * BASE, M_EV = 2 * BASE + ESCB;
-    static constexpr int MSLOT = 2 * BASE + 2 * ESCB;
-    // Escape scratch: the consumed sm rows of the sub-tile, except when the row halves are rebuilt
-    // one at a time (then the second half's rows are still unread): a region of its own.
-    static constexpr int SCR = SPLIT ? TT * D : 0;
+    // Per-block meta slot: K base | V base | the block's FlatBlock | its escape count headers.
+    static constexpr int M_FB = 2 * BASE;
+    static constexpr int M_EM = M_FB + 32;
+    static constexpr int MSLOT = M_EM + 64;
+    static constexpr int SCR = 16 * D;            // escape scratch: one row half of fragments
     static constexpr int W_META = NSTAGE * SLOT;  // per-warp region: ring | meta x2 | scratch
     static constexpr int W_SCR = W_META + 2 * MSLOT;
     static constexpr int WARP_BYTES = (W_SCR + SCR + 127) & ~127;
-    static constexpr int WARPS = cmin(KVX_MAXWARPS, 232448 / WARP_BYTES);
+    // Register budget 65536 / (32 WARPS): 12 warps leave 168 per thread, 10 leave 204.
+    static constexpr int MAXW = D <= 32 ? 16 : D <= 64 ? KVX_MAXWARPS : 10;
+    static constexpr int WARPS = cmin(MAXW, 232448 / WARP_BYTES);
     static_assert(WARPS >= 1, "worker does not fit in shared memory");
 };
-
-__device__ __forceinline__ FlatBlock load_flat(const FlatBlock *f, int64_t i) {
-    const uint4 r = __ldg(reinterpret_cast<const uint4 *>(f) + i);
-    FlatBlock b;
-    b.k_off = r.x;
-    b.v_off = r.y;
-    b.k_nesc = uint16_t(r.z & 0xFFFF);
-    b.v_nesc = uint16_t(r.z >> 16);
-    b.k_mode = uint8_t(r.w & 0xFF);
-    b.v_mode = uint8_t((r.w >> 8) & 0xFF);
-    b.n_tok = uint8_t((r.w >> 16) & 0xFF);
-    b.valid = uint8_t(r.w >> 24);
-    return b;
-}
 
 // ---- copies ------------------------------------------------------------------------------------
 
@@ -173,380 +165,372 @@ __device__ __forceinline__ Sections sections(const uint8_t *blob, uint32_t off, 
     return s;
 }
 
-// Whether a block's escape words fit its meta slot (producer and consumer agree on this).
-template <int D> __device__ __forceinline__ bool esc_staged(const Piece &e, int nesc) {
-    return nesc > 0 && e.alloc <= uint32_t(Cfg<D>::ESCB);
+// ---- escape records ----------------------------------------------------------------------------
+
+// Lane l < 16 holds entry l of the block's K count header, lane 16 + l entry l of V's (0 without
+// a record): e(i) = escape words of tokens [0, 16 i).
+__device__ __forceinline__ uint32_t load_em(const uint16_t *esc, const FlatBlock &f, int lane) {
+    const bool v = lane >= 16;
+    const int mode = v ? f.v_mode : f.k_mode;
+    const int n = v ? f.v_nesc : f.k_nesc;
+    const uint32_t rec = v ? f.v_rec : f.k_rec;
+    return (mode != 0 && n != 0) ? uint32_t(__ldg(esc + rec + (lane & 15))) : 0u;
+}
+// e(i) of tensor T (0 K, 1 V), i = 0..16; every lane of the warp calls it.
+__device__ __forceinline__ int esc_at(uint32_t em, int T, int i) {
+    const uint32_t v = __shfl_sync(FULL, em, (T << 4) + ((i + 15) & 15));
+    return i == 0 ? 0 : int(v);
+}
+
+// e(i) of tensor T from a meta slot's copy of the headers.
+__device__ __forceinline__ int esc_ms(const uint8_t *em, int T, int i) {
+    return i == 0 ? 0 : int(*reinterpret_cast<const uint16_t *>(em + 2 * (16 * T + i - 1)));
+}
+
+// Byte offset inside a 16-byte line of escape word i of a coded block (the blob is 16-byte
+// aligned) and of its position in the escape records (16-byte aligned allocation).
+template <int D>
+__device__ __forceinline__ uint32_t esc_word_line(uint32_t off, int n_tok, int mode, int i) {
+    return (off + uint32_t(kHeaderBytes + D) + uint32_t(n_tok * D) + uint32_t(n_tok * D * mode / 8) +
+            2u * uint32_t(i)) & 15u;
+}
+__device__ __forceinline__ uint32_t esc_pos_line(uint32_t rec, int i) {
+    return (2u * (rec + uint32_t(kEscRecHead) + uint32_t(i))) & 15u;
 }
 
 // ---- decode helpers ----------------------------------------------------------------------------
 
-// NW 32-bit words of shared memory starting at any byte address (byte 0 in bits 0-7 of w[0]).
-// The aligned pointer is derived from p by pointer arithmetic (not through an integer), so the
-// compiler keeps these as 32-bit shared-memory loads.
-template <int NW> __device__ __forceinline__ void lds_words(const uint8_t *p, uint32_t (&w)[NW]) {
-    const uint32_t mis = uint32_t(reinterpret_cast<uintptr_t>(p)) & 3u;
-    const uint32_t *q = reinterpret_cast<const uint32_t *>(p - mis);
-    const uint32_t sh = mis * 8u;
-    uint32_t x[NW + 1];
-#pragma unroll
-    for (int i = 0; i <= NW; ++i) x[i] = q[i];
-#pragma unroll
-    for (int i = 0; i < NW; ++i) w[i] = __funnelshift_r(x[i], x[i + 1], sh);
+__host__ __device__ constexpr uint32_t rep2(uint32_t b) {  // bytes b, b, b+1, b+1
+    return b | (b << 4) | ((b + 1) << 8) | ((b + 1) << 12);
 }
-
-__host__ __device__ constexpr uint32_t sel_pair(int j) {  // bytes j, j+1 of A with sign bytes
-    return uint32_t(j) | (uint32_t(j | 8) << 4) | (uint32_t(j + 1) << 8) | (uint32_t((j + 1) | 8) << 12);
+__host__ __device__ constexpr uint32_t shift4(uint32_t o) {  // bytes o .. o+3
+    return o | ((o + 1) << 4) | ((o + 2) << 8) | ((o + 3) << 12);
 }
-__host__ __device__ constexpr uint32_t sel_cross(int b) {  // byte b of A and of B with sign bytes
-    return uint32_t(b) | (uint32_t(b | 8) << 4) | (uint32_t(4 + b) << 8) | (uint32_t((4 + b) | 8) << 12);
-}
-__host__ __device__ constexpr uint32_t sel_code(int j) {  // byte j of A -> bits 0-7, of B -> 16-23
+__host__ __device__ constexpr uint32_t sel_code(int j) {  // byte j of A -> bytes 0, 1; of B -> 2, 3
     return uint32_t(j) | (uint32_t(j) << 4) | (uint32_t(4 + j) << 8) | (uint32_t(4 + j) << 12);
 }
-__host__ __device__ constexpr uint32_t low_bytes(int nb) {
-    return nb >= 4 ? 0xFFFFFFFFu : (1u << (8 * nb)) - 1u;
+__host__ __device__ constexpr uint32_t sel_cross(int b) {  // byte b of A -> 0, 1; of B -> 2, 3
+    return uint32_t(b) | (uint32_t(b) << 4) | (uint32_t(4 + b) << 8) | (uint32_t(4 + b) << 12);
 }
 
-// Two BF16 values from a sign-replicated sm pair and a code pair: exponent offsets in bytes 0 and
-// 2 of cw (bytes 1 and 3 hold other offsets and are masked off).  Offsets are 8-bit wide because
-// an escaped element carries its full offset (exponent - base) mod 256 there.  Exponent = base +
-// offset modulo 256 like bf16_from_delta's uint8 sum (include/kvexp/bf16.hpp:35-37 of the
-// reference): the carry out of bit 14 is masked away.
+// Two BF16 values from sign/mantissa bytes (byte 0 and 1 of each half hold the element's byte:
+// bits 0-6 give the mantissa, bit 15 the sign) and exponent residuals in bytes 0 and 2 of cw.
+// Exponent = base + residual modulo 256 like bf16_from_delta's uint8 sum (reference
+// include/kvexp/bf16.hpp:35-37).  Bytes 1 and 3 of cw may hold other residuals (< 16): times 128
+// they land in bits 15-18 of each half, which the select drops, and no carry reaches bit 23.
 __device__ __forceinline__ uint32_t merge(uint32_t sg, uint32_t cw, uint32_t b7) {
-    const uint32_t e = (cw & 0x00FF00FFu) * 128u + b7;
-    return (sg & 0x807F807Fu) | (e & 0x7F807F80u);
+    return (sg & 0x807F807Fu) | ((cw * 128u + b7) & 0x7F807F80u);
 }
 
-__device__ __forceinline__ uint32_t sent4(uint32_t x) {  // nibble == 15 -> bit 4k
-    uint32_t t = x & (x >> 1);
-    t &= t >> 2;
-    return t & 0x11111111u;
-}
-__device__ __forceinline__ uint32_t sent2(uint32_t x) {  // 2-bit code == 3 -> bit 2k
-    return x & (x >> 1) & 0x55555555u;
+// How this lane reads one tensor of the current block from a ring stage.  Row sections start
+// m = 0 or 2 bytes past a 4-byte boundary; the lane's columns add a multiple of 4 to the sign/
+// mantissa and raw rows, and any byte count to the residual rows.
+struct Lay {
+    uint32_t p0, p1;  // sign/mantissa bytes of element pairs 2q and 2q+1 from words q, q+1
+    uint32_t w;       // one realigned word from two loaded ones (sign/mantissa, raw rows)
+    uint32_t cs;      // one realigned word of residual codes
+    int rows;         // byte offset of the lane's row window in the stage (4-aligned)
+    int codes;        // byte offset of the lane's residual window in the stage (4-aligned)
+};
+// rd / cd: data offsets of the block's row and code pieces; col: the lane's first head dim.
+template <int D>
+__device__ __forceinline__ Lay make_lay(uint32_t rd, uint32_t cd, int mode, int col, bool bf16) {
+    Lay l;
+    const uint32_t m = rd & 3u;
+    l.p0 = rep2(m);
+    l.p1 = rep2(m + 2);
+    l.w = shift4(m);
+    const int rcol = (bf16 || mode == 0) ? 2 * col : col;
+    l.rows = int(rd & ~3u) + rcol;
+    const uint32_t cb = (cd & 3u) + uint32_t(col * (mode == 0 ? 0 : mode) / 8);
+    l.cs = shift4(cb & 3u);
+    l.codes = Cfg<D>::CODE_OFF + int(cd & ~3u) + int(cb & ~3u);
+    return l;
 }
 
-// b7 of a K register (dims d, d+1): base[d] << 7 | base[d+1] << 23; of a V register (one dim,
-// two tokens): base[d] << 7 | base[d] << 23.
+// b7 of a K register (dims d, d+1): base[d] << 7 | base[d+1] << 23.  `base` points at the
+// block's staged base exponents (data offset applied), the lane's first dim c0.
 template <int D>
 __device__ __forceinline__ void load_b7k(const uint8_t *base, uint32_t (&b7)[Cfg<D>::NK]) {
-    uint32_t B[Cfg<D>::DK / 4];
-    lds_words<Cfg<D>::DK / 4>(base, B);
+    constexpr int NB = Cfg<D>::DK / 4;
+    const uint32_t m = uint32_t(reinterpret_cast<uintptr_t>(base)) & 3u;
+    const uint32_t *q = reinterpret_cast<const uint32_t *>(base - m);
+    uint32_t B[NB + 1];
 #pragma unroll
-    for (int p = 0; p < Cfg<D>::NK; ++p) {
-        const int j = 2 * (p & 1);
-        b7[p] = prmt(B[p >> 1], 0u, uint32_t(j) | (4u << 4) | (uint32_t(j + 1) << 8) | (4u << 12)) << 7;
-    }
+    for (int i = 0; i <= NB; ++i) B[i] = q[i];
+    const uint32_t s0 = rep2(m), s1 = rep2(m + 2);
+#pragma unroll
+    for (int p = 0; p < Cfg<D>::NK; ++p)
+        b7[p] = (prmt(B[p >> 1], B[(p >> 1) + 1], (p & 1) ? s1 : s0) & 0x00FF00FFu) << 7;
 }
+// b7 of a V register (one dim, two tokens): base[d] << 7 | base[d] << 23.
 template <int D>
 __device__ __forceinline__ void load_b7v(const uint8_t *base, uint32_t (&b7)[Cfg<D>::DV]) {
-    uint32_t B[Cfg<D>::DV / 4];
-    lds_words<Cfg<D>::DV / 4>(base, B);
+    constexpr int NB = Cfg<D>::DV / 4;
+    const uint32_t m = uint32_t(reinterpret_cast<uintptr_t>(base)) & 3u;
+    const uint32_t *q = reinterpret_cast<const uint32_t *>(base - m);
+    uint32_t B[NB + 1];
+#pragma unroll
+    for (int i = 0; i <= NB; ++i) B[i] = q[i];
+    const uint32_t sw = shift4(m);
 #pragma unroll
     for (int e = 0; e < Cfg<D>::DV; ++e) {
-        const int j = e & 3;
-        b7[e] = prmt(B[e >> 2], 0u, uint32_t(j) | (4u << 4) | (uint32_t(j) << 8) | (4u << 12)) << 7;
+        const uint32_t w = prmt(B[e >> 2], B[(e >> 2) + 1], sw);
+        b7[e] = (prmt(w, 0u, uint32_t(e & 3) * 0x1111u) & 0x00FF00FFu) << 7;
     }
+}
+
+// ---- row rebuild -------------------------------------------------------------------------------
+
+// One K row of this lane (token r of the stage, dims c0 .. c0 + DK - 1).  MODE 4 / 2: coded,
+// 0: raw BF16 rows.
+template <int D, int MODE>
+__device__ __forceinline__ void k_row(const uint8_t *stage, const Lay &ly, int r,
+                                      const uint32_t (&b7)[Cfg<D>::NK], uint32_t (&o)[Cfg<D>::NK]) {
+    using C = Cfg<D>;
+    if constexpr (MODE == 0) {
+        const uint32_t *q = reinterpret_cast<const uint32_t *>(stage + ly.rows + r * (2 * D));
+        uint32_t W[C::NK + 1];
+#pragma unroll
+        for (int i = 0; i <= C::NK; ++i) W[i] = q[i];
+#pragma unroll
+        for (int p = 0; p < C::NK; ++p) o[p] = prmt(W[p], W[p + 1], ly.w);
+    } else {
+        constexpr int NS = C::DK / 4;
+        const uint32_t *qs = reinterpret_cast<const uint32_t *>(stage + ly.rows + r * D);
+        uint32_t W[NS + 1];
+#pragma unroll
+        for (int i = 0; i <= NS; ++i) W[i] = qs[i];
+        const uint32_t *qc = reinterpret_cast<const uint32_t *>(stage + ly.codes + r * (D * MODE / 8));
+        if constexpr (MODE == 4) {
+            constexpr int NC = C::DK / 8;  // words of 8 residuals
+            uint32_t X[NC + 1], lo[NC], hi[NC];
+#pragma unroll
+            for (int i = 0; i <= NC; ++i) X[i] = qc[i];
+#pragma unroll
+            for (int k = 0; k < NC; ++k) {
+                const uint32_t x = prmt(X[k], X[k + 1], ly.cs);
+                lo[k] = x & 0x0F0F0F0Fu;
+                hi[k] = (x >> 4) & 0x0F0F0F0Fu;
+            }
+#pragma unroll
+            for (int p = 0; p < C::NK; ++p)
+                o[p] = merge(prmt(W[p >> 1], W[(p >> 1) + 1], (p & 1) ? ly.p1 : ly.p0),
+                             prmt(lo[p >> 2], hi[p >> 2], sel_code(p & 3)), b7[p]);
+        } else {
+            constexpr int NC = (C::DK + 15) / 16;  // words of 16 residuals
+            uint32_t X[NC + 1], el[NC], eh[NC], ol[NC], oh[NC];
+#pragma unroll
+            for (int i = 0; i <= NC; ++i) X[i] = qc[i];
+#pragma unroll
+            for (int k = 0; k < NC; ++k) {
+                const uint32_t x = prmt(X[k], X[k + 1], ly.cs);
+                const uint32_t ev = x & 0x33333333u, od = (x >> 2) & 0x33333333u;
+                el[k] = ev & 0x0F0F0F0Fu;  // even elements of pairs 0, 2, 4, 6
+                eh[k] = (ev >> 4) & 0x0F0F0F0Fu;
+                ol[k] = od & 0x0F0F0F0Fu;
+                oh[k] = (od >> 4) & 0x0F0F0F0Fu;
+            }
+#pragma unroll
+            for (int p = 0; p < C::NK; ++p) {
+                const int k = p >> 3, j = (p & 7) >> 1;
+                const uint32_t cw = (p & 1) ? prmt(eh[k], oh[k], sel_code(j)) : prmt(el[k], ol[k], sel_code(j));
+                o[p] = merge(prmt(W[p >> 1], W[(p >> 1) + 1], (p & 1) ? ly.p1 : ly.p0), cw, b7[p]);
+            }
+        }
+    }
+}
+
+// Two V tokens of this lane (token a of the stage -> low halves, a + 1 -> high halves; dims
+// v0 .. v0 + DV - 1).
+template <int D, int MODE>
+__device__ __forceinline__ void v_pair(const uint8_t *stage, const Lay &ly, int a,
+                                       const uint32_t (&b7)[Cfg<D>::DV], uint32_t (&o)[Cfg<D>::DV]) {
+    using C = Cfg<D>;
+    if constexpr (MODE == 0) {
+        constexpr int NW = C::DV / 2;
+        const uint32_t *qa = reinterpret_cast<const uint32_t *>(stage + ly.rows + a * (2 * D));
+        const uint32_t *qb = qa + D / 2;
+        uint32_t A[NW + 1], B[NW + 1];
+#pragma unroll
+        for (int i = 0; i <= NW; ++i) {
+            A[i] = qa[i];
+            B[i] = qb[i];
+        }
+#pragma unroll
+        for (int e = 0; e < C::DV; ++e) {
+            const uint32_t x = prmt(A[e >> 1], A[(e >> 1) + 1], ly.w);
+            const uint32_t y = prmt(B[e >> 1], B[(e >> 1) + 1], ly.w);
+            o[e] = prmt(x, y, (e & 1) ? 0x7632u : 0x5410u);
+        }
+    } else {
+        constexpr int NS = C::DV / 4;
+        const uint32_t *sa = reinterpret_cast<const uint32_t *>(stage + ly.rows + a * D);
+        const uint32_t *sb = sa + D / 4;
+        uint32_t A[NS + 1], B[NS + 1], SA[NS], SB[NS];
+#pragma unroll
+        for (int i = 0; i <= NS; ++i) {
+            A[i] = sa[i];
+            B[i] = sb[i];
+        }
+#pragma unroll
+        for (int k = 0; k < NS; ++k) {
+            SA[k] = prmt(A[k], A[k + 1], ly.w);
+            SB[k] = prmt(B[k], B[k + 1], ly.w);
+        }
+        constexpr int CR = D * MODE / 8;  // residual bytes per row
+        const uint32_t *ca = reinterpret_cast<const uint32_t *>(stage + ly.codes + a * CR);
+        const uint32_t *cb = reinterpret_cast<const uint32_t *>(stage + ly.codes + (a + 1) * CR);
+        if constexpr (MODE == 4) {
+            constexpr int NC = (C::DV + 7) / 8;
+            uint32_t XA[NC + 1], XB[NC + 1], la[NC], ha[NC], lb[NC], hb[NC];
+#pragma unroll
+            for (int i = 0; i <= NC; ++i) {
+                XA[i] = ca[i];
+                XB[i] = cb[i];
+            }
+#pragma unroll
+            for (int k = 0; k < NC; ++k) {
+                const uint32_t x = prmt(XA[k], XA[k + 1], ly.cs), y = prmt(XB[k], XB[k + 1], ly.cs);
+                la[k] = x & 0x0F0F0F0Fu;
+                ha[k] = (x >> 4) & 0x0F0F0F0Fu;
+                lb[k] = y & 0x0F0F0F0Fu;
+                hb[k] = (y >> 4) & 0x0F0F0F0Fu;
+            }
+#pragma unroll
+            for (int e = 0; e < C::DV; ++e) {
+                const int k = e >> 3, j = (e & 7) >> 1;
+                const uint32_t cw = (e & 1) ? prmt(ha[k], hb[k], sel_code(j)) : prmt(la[k], lb[k], sel_code(j));
+                o[e] = merge(prmt(SA[e >> 2], SB[e >> 2], sel_cross(e & 3)), cw, b7[e]);
+            }
+        } else {
+            constexpr int NC = (C::DV + 15) / 16;
+            uint32_t XA[NC + 1], XB[NC + 1], ca4[4][NC], cb4[4][NC];
+#pragma unroll
+            for (int i = 0; i <= NC; ++i) {
+                XA[i] = ca[i];
+                XB[i] = cb[i];
+            }
+#pragma unroll
+            for (int k = 0; k < NC; ++k) {
+                const uint32_t x = prmt(XA[k], XA[k + 1], ly.cs), y = prmt(XB[k], XB[k + 1], ly.cs);
+#pragma unroll
+                for (int s = 0; s < 4; ++s) {
+                    ca4[s][k] = (x >> (2 * s)) & 0x03030303u;
+                    cb4[s][k] = (y >> (2 * s)) & 0x03030303u;
+                }
+            }
+#pragma unroll
+            for (int e = 0; e < C::DV; ++e) {
+                const int k = e >> 4, s = e & 3, j = (e & 15) >> 2;
+                o[e] = merge(prmt(SA[e >> 2], SB[e >> 2], sel_cross(e & 3)),
+                             prmt(ca4[s][k], cb4[s][k], sel_code(j)), b7[e]);
+            }
+        }
+    }
+}
+
+// Zero the halves of tokens past the tile's valid rows (P is 0 there, V must be finite).
+template <int D>
+__device__ __forceinline__ void v_tail(int t, int rows, uint32_t (&va)[Cfg<D>::DV]) {
+    const uint32_t keep = (t < rows ? 0x0000FFFFu : 0u) | (t + 1 < rows ? 0xFFFF0000u : 0u);
+#pragma unroll
+    for (int e = 0; e < Cfg<D>::DV; ++e) va[e] &= keep;
 }
 
 // ---- escapes -----------------------------------------------------------------------------------
-//
-// A sentinel element takes the next escape word of its block in scan order (token-major).  The
-// rows are rebuilt first (a sentinel comes out with a wrong exponent).  When a row half holds a
-// sentinel, every lane writes its fragment registers to scratch in shared memory (the half's
-// sign/mantissa rows, already consumed), lanes write their escape words over the sentinel
-// elements in place, and every lane reads its registers back.  Ranks come from warp ballots.
 
-struct Esc {
-    uint32_t run;               // escapes consumed so far in this block
-    uint32_t n;                 // escape words in this block
-    const uint8_t *sm;          // staged escape words (shared memory), or nullptr
-    const unsigned short *gm;   // escape words in global memory
+// The escape words of one tensor of a stage: word i of the block is val[i - off], its element
+// position pos[i - off] (shared memory when the stage staged them, else the block's words in HBM
+// with off = 0).
+struct StageEsc {
+    const uint16_t *val;
+    const uint16_t *pos;
+    int off;
 };
 
-__device__ __forceinline__ uint32_t esc_word(uint32_t r, const Esc &es, int *status) {
-    if (r >= es.n) {
-        report(status, KVX_ERR_RUNTIME, DERR_ESC_OVERRUN);
-        return 0u;
-    }
-    return es.sm != nullptr ? uint32_t(*reinterpret_cast<const uint16_t *>(es.sm + 2 * r))
-                            : uint32_t(__ldg(es.gm + r));
-}
-
-// First escape rank of this lane when the scan order is the lane order (K rows): exclusive
-// prefix of the per-lane sentinel counts, bit by bit (one step when no lane holds two).
-__device__ __forceinline__ uint32_t rank_lanes(uint32_t cnt, Esc &es) {
-    const uint32_t lt = lanemask_lt();
-    const int bits = 32 - __clz(__reduce_max_sync(FULL, cnt));
-    uint32_t pre = 0, tot = 0;
-#pragma unroll 1
-    for (int b = 0; b < bits; ++b) {
-        const uint32_t B = __ballot_sync(FULL, (cnt >> b) & 1u);
-        pre += uint32_t(__popc(B & lt)) << b;
-        tot += uint32_t(__popc(B)) << b;
-    }
-    const uint32_t r = es.run + pre;
-    es.run += tot;
-    return r;
-}
-
-// First escape ranks of tokens A and B of a V token half.  Lane 4g + t holds tokens 2t (A) and
-// 2t+1 (B) of the half, dims [g D/8, (g+1) D/8); the scan order inside the half is
-// (t, A/B, g, element).
-__device__ __forceinline__ void rank_tokens(uint32_t ca, uint32_t cb, Esc &es, int lane,
-                                            uint32_t &ra, uint32_t &rb) {
-    const uint32_t lt = lanemask_lt();
-    const int tig = lane & 3;
-    const uint32_t G = 0x11111111u << tig;                // lanes with this t
-    const uint32_t L = 0x11111111u * ((1u << tig) - 1u);  // lanes with a smaller t
-    const int bits = 32 - __clz(__reduce_max_sync(FULL, ca > cb ? ca : cb));
-    uint32_t sl = 0, sag = 0, saglt = 0, sbglt = 0, tot = 0;
-#pragma unroll 1
-    for (int b = 0; b < bits; ++b) {
-        const uint32_t BA = __ballot_sync(FULL, (ca >> b) & 1u);
-        const uint32_t BB = __ballot_sync(FULL, (cb >> b) & 1u);
-        sl += uint32_t(__popc(BA & L) + __popc(BB & L)) << b;
-        sag += uint32_t(__popc(BA & G)) << b;
-        saglt += uint32_t(__popc(BA & G & lt)) << b;
-        sbglt += uint32_t(__popc(BB & G & lt)) << b;
-        tot += uint32_t(__popc(BA) + __popc(BB)) << b;
-    }
-    ra = es.run + sl + saglt;
-    rb = es.run + sl + sag + sbglt;
-    es.run += tot;
-}
-
-template <int N>
-__device__ __forceinline__ void regs_to(uint32_t *p, const uint32_t (&o)[N]) {
+// A row half of N fragment registers per lane goes to scratch as N / 4 chunks of 512 bytes, chunk
+// k holding lane l's registers 4k .. 4k+3 at byte 16 l (16-byte stores without bank conflicts).
+template <int N> __device__ __forceinline__ void regs_to(uint8_t *scr, const uint32_t (&o)[N], int lane) {
 #pragma unroll
-    for (int i = 0; i < N; i += 4)
-        *reinterpret_cast<uint4 *>(p + i) = make_uint4(o[i], o[i + 1], o[i + 2], o[i + 3]);
+    for (int k = 0; k < N / 4; ++k)
+        *reinterpret_cast<uint4 *>(scr + 512 * k + 16 * lane) =
+            make_uint4(o[4 * k], o[4 * k + 1], o[4 * k + 2], o[4 * k + 3]);
 }
-template <int N> __device__ __forceinline__ void regs_from(const uint32_t *p, uint32_t (&o)[N]) {
+template <int N> __device__ __forceinline__ void regs_from(const uint8_t *scr, uint32_t (&o)[N], int lane) {
 #pragma unroll
-    for (int i = 0; i < N; i += 4) {
-        const uint4 v = *reinterpret_cast<const uint4 *>(p + i);
-        o[i] = v.x;
-        o[i + 1] = v.y;
-        o[i + 2] = v.z;
-        o[i + 3] = v.w;
+    for (int k = 0; k < N / 4; ++k) {
+        const uint4 v = *reinterpret_cast<const uint4 *>(scr + 512 * k + 16 * lane);
+        o[4 * k] = v.x;
+        o[4 * k + 1] = v.y;
+        o[4 * k + 2] = v.z;
+        o[4 * k + 3] = v.w;
     }
 }
+__device__ __forceinline__ uint32_t scr_addr(int owner, int p, int half) {
+    return uint32_t(512 * (p >> 2) + 16 * owner + 4 * (p & 3) + 2 * half);
+}
 
-// ---- decode ------------------------------------------------------------------------------------
-//
-// A K row (one token, this lane's DK dims) or a V token pair (two tokens, this lane's DV dims) is
-// loaded into staged words (sign/mantissa bytes, one exponent code byte per element) and merged
-// into BF16 pairs; the sentinel masks are kept for the escape walk.
-
-// One K row of this lane (dims c0 .. c0 + DK - 1 of one token).
-template <int D, int MODE> struct KRow {
+// Scratch byte of element (token r of the 16-token tile, dim c) in its row half's layout.
+template <int D, bool K> __device__ __forceinline__ uint32_t esc_slot(int r, int c) {
     using C = Cfg<D>;
-    static constexpr int NS = C::DK / 4;                                    // sm words
-    static constexpr int NW = MODE == 2 ? cmax(1, C::DK / 16) : C::DK / 8;  // code words
-    uint32_t S[NS], L[NW], H[NW], Cd[4][NW], mk[NW];
-    uint32_t cnt;
-
-    __device__ __forceinline__ void load(const uint8_t *rp, const uint8_t *cp, bool valid) {
-        lds_words<NS>(rp, S);
-        uint32_t N[NW];
-        lds_words<NW>(cp, N);
-        cnt = 0;
-#pragma unroll
-        for (int i = 0; i < NW; ++i) {
-            if (MODE == 4) {
-                L[i] = N[i] & 0x0F0F0F0Fu;
-                H[i] = (N[i] >> 4) & 0x0F0F0F0Fu;
-                mk[i] = valid ? sent4(N[i]) : 0u;
-            } else {
-#pragma unroll
-                for (int k = 0; k < 4; ++k) Cd[k][i] = (N[i] >> (2 * k)) & 0x03030303u;
-                mk[i] = valid ? (sent2(N[i]) & low_bytes(C::DK / 4)) : 0u;
-            }
-            cnt += __popc(mk[i]);
-        }
+    if (K) {  // lane (r & 7, c / DK) register (c % DK) / 2, half c & 1
+        const int q = c % C::DK;
+        return scr_addr(4 * (r & 7) + c / C::DK, q >> 1, q & 1);
     }
-    // element index of mask bit b of word i
-    __device__ __forceinline__ static int elem(int i, int b) {
-        return MODE == 4 ? 8 * i + (b >> 2) : 16 * i + (b >> 1);
-    }
-    __device__ __forceinline__ void merge_into(const uint32_t (&b7)[C::NK], uint32_t (&o)[C::NK]) const {
-#pragma unroll
-        for (int p = 0; p < C::NK; ++p) {
-            const uint32_t sg = prmt(S[p >> 1], 0u, sel_pair(2 * (p & 1)));
-            uint32_t cw;
-            if (MODE == 4) {
-                cw = prmt(L[p >> 2], H[p >> 2], sel_code(p & 3));
-            } else {
-                const int e = 2 * p, i = e >> 4, j = (e & 15) >> 2, k = e & 3;
-                cw = prmt(Cd[k][i], Cd[k + 1][i], sel_code(j));
-            }
-            o[p] = merge(sg, cw, b7[p]);
-        }
-    }
-};
-
-// Escapes of one K row half (rows 0-7 or 8-15; scan order (row, dim) = (lane, element)), through
-// scratch: o holds dims c0 + 2p (low half) and c0 + 2p + 1 (high half), so element e sits at
-// 16-bit position e of the lane's words.  Called by the whole warp when some lane's row has one.
-template <int D, int MODE>
-__device__ __forceinline__ void esc_k_half(uint32_t (&o)[Cfg<D>::NK], const KRow<D, MODE> &w,
-                                           uint8_t *scr, Esc &es, int *status, int lane) {
-    uint32_t *mine = reinterpret_cast<uint32_t *>(scr) + lane * Cfg<D>::NK;
-    __syncwarp();  // every lane has read the rows this scratch overlays
-    regs_to(mine, o);
-    uint32_t r = rank_lanes(w.cnt, es);
-    uint16_t *h16 = reinterpret_cast<uint16_t *>(mine);
-#pragma unroll
-    for (int i = 0; i < KRow<D, MODE>::NW; ++i) {
-        uint32_t mm = w.mk[i];
-#pragma unroll 1
-        while (mm != 0u) {
-            const int e = KRow<D, MODE>::elem(i, __ffs(mm) - 1);
-            mm &= mm - 1u;
-            h16[e] = uint16_t(esc_word(r++, es, status));
-        }
-    }
-    regs_from(mine, o);
+    // V: lane (c / DV, (r & 7) / 2) register c % DV, half r & 1
+    return scr_addr(4 * (c / C::DV) + ((r & 7) >> 1), c % C::DV, r & 1);
 }
 
-// Two V tokens (A -> low halves, B -> high halves; dims v0 .. v0 + DV - 1).
-template <int D, int MODE> struct VPair {
-    using C = Cfg<D>;
-    static constexpr int NS = C::DV / 4;
-    static constexpr int NB = MODE == 2 ? C::DV / 4 : C::DV / 2;  // code bytes per token
-    static constexpr int NW = (NB + 3) / 4;
-    uint32_t SA[NS], SB[NS], LA[NW], HA[NW], LB[NW], HB[NW], CA[4][NW], CB[4][NW], ma[NW], mb[NW];
-    uint32_t ca, cb;
+// Which row halves of the tile (tokens t0 .. t0+15 of the block) hold escapes [i0, i1): bit h.
+template <int D>
+__device__ __forceinline__ uint32_t esc_halves(const StageEsc &se, int i0, int i1, int t0, int lane) {
+    uint32_t f = 0;
+    for (int i = i0 + lane; i < i1; i += 32) {
+        const int r = int(se.pos[i - se.off]) / D - t0;
+        f |= 1u << ((r >> 3) & 1);
+    }
+    return __reduce_or_sync(FULL, f);
+}
 
-    __device__ __forceinline__ void load(const uint8_t *ra, const uint8_t *rb, const uint8_t *pa,
-                                         const uint8_t *pb, bool va, bool vb) {
-        lds_words<NS>(ra, SA);
-        lds_words<NS>(rb, SB);
-        uint32_t WA[NW], WB[NW];
-        lds_words<NW>(pa, WA);
-        lds_words<NW>(pb, WB);
-        ca = cb = 0;
-#pragma unroll
-        for (int i = 0; i < NW; ++i) {
-            if (MODE == 4) {
-                LA[i] = WA[i] & 0x0F0F0F0Fu;
-                HA[i] = (WA[i] >> 4) & 0x0F0F0F0Fu;
-                LB[i] = WB[i] & 0x0F0F0F0Fu;
-                HB[i] = (WB[i] >> 4) & 0x0F0F0F0Fu;
-                ma[i] = va ? (sent4(WA[i]) & low_bytes(NB)) : 0u;
-                mb[i] = vb ? (sent4(WB[i]) & low_bytes(NB)) : 0u;
-            } else {
-#pragma unroll
-                for (int k = 0; k < 4; ++k) {
-                    CA[k][i] = (WA[i] >> (2 * k)) & 0x03030303u;
-                    CB[k][i] = (WB[i] >> (2 * k)) & 0x03030303u;
-                }
-                ma[i] = va ? (sent2(WA[i]) & low_bytes(NB)) : 0u;
-                mb[i] = vb ? (sent2(WB[i]) & low_bytes(NB)) : 0u;
-            }
-            ca += __popc(ma[i]);
-            cb += __popc(mb[i]);
-        }
-    }
-    __device__ __forceinline__ static int elem(int i, int b) {
-        return MODE == 4 ? 8 * i + (b >> 2) : 16 * i + (b >> 1);
-    }
-    __device__ __forceinline__ void merge_into(const uint32_t (&b7)[C::DV], uint32_t (&o)[C::DV]) const {
-#pragma unroll
-        for (int e = 0; e < C::DV; ++e) {
-            const uint32_t sg = prmt(SA[e >> 2], SB[e >> 2], sel_cross(e & 3));
-            uint32_t cw;
-            if (MODE == 4) {
-                const int i = e >> 3, j = (e & 7) >> 1;
-                cw = (e & 1) ? prmt(HA[i], HB[i], sel_code(j)) : prmt(LA[i], LB[i], sel_code(j));
-            } else {
-                const int i = e >> 4, j = (e & 15) >> 2, k = e & 3;
-                cw = prmt(CA[k][i], CB[k][i], sel_code(j));
-            }
-            o[e] = merge(sg, cw, b7[e]);
-        }
-    }
-};
-
-// Escapes of one V token half, through scratch: o[e] holds dim v0 + e of token A (low half) and
-// token B (high half), so element e of token A (B) sits at 16-bit position 2e (2e + 1).
-template <int D, int MODE>
-__device__ __forceinline__ void esc_v_half(uint32_t (&o)[Cfg<D>::DV], const VPair<D, MODE> &p,
-                                           uint8_t *scr, Esc &es, int *status, int lane) {
-    uint32_t *mine = reinterpret_cast<uint32_t *>(scr) + lane * Cfg<D>::DV;
+// Store escapes [i0, i1) of row half h over their elements: the half's registers round-trip
+// through scratch.
+template <int D, bool K, int N>
+__device__ __forceinline__ void esc_patch(uint32_t (&o)[N], uint8_t *scr, const StageEsc &se, int i0,
+                                          int i1, int t0, int h, int lane) {
     __syncwarp();
-    regs_to(mine, o);
-    uint32_t ra, rb;
-    rank_tokens(p.ca, p.cb, es, lane, ra, rb);
-    uint16_t *h16 = reinterpret_cast<uint16_t *>(mine);
-#pragma unroll
-    for (int i = 0; i < VPair<D, MODE>::NW; ++i) {
-        uint32_t mm = p.ma[i];
-#pragma unroll 1
-        while (mm != 0u) {
-            const int e = VPair<D, MODE>::elem(i, __ffs(mm) - 1);
-            mm &= mm - 1u;
-            h16[2 * e] = uint16_t(esc_word(ra++, es, status));
-        }
-        mm = p.mb[i];
-#pragma unroll 1
-        while (mm != 0u) {
-            const int e = VPair<D, MODE>::elem(i, __ffs(mm) - 1);
-            mm &= mm - 1u;
-            h16[2 * e + 1] = uint16_t(esc_word(rb++, es, status));
-        }
+    regs_to(scr, o, lane);
+    __syncwarp();
+    for (int i = i0 + lane; i < i1; i += 32) {
+        const int pos = int(se.pos[i - se.off]);
+        const int r = pos / D - t0, c = pos % D;
+        if ((r >> 3) == h) *reinterpret_cast<uint16_t *>(scr + esc_slot<D, K>(r, c)) = se.val[i - se.off];
     }
-    regs_from(mine, o);
+    __syncwarp();
+    regs_from(scr, o, lane);
 }
 
 // ---- per-tile stages ----------------------------------------------------------------------------
 
-// Where the current sub-tile's tensors sit in the ring slot (with the block's source alignment
-// already applied), and the block's base exponents in its meta slot.
-struct TileView {
-    const uint8_t *k_rows, *k_codes, *v_rows, *v_codes;
-    const uint8_t *k_base, *v_base;  // this lane's first base byte
-    uint8_t *k_scr, *v_scr;          // 16 D bytes of consumed sm rows (16-byte aligned), scratch
-    int rows;                        // valid tokens in the sub-tile
-};
-
-// S^T fragment of the tile: s0/s1 token g (queries 2t, 2t+1), s2/s3 token g + 8.
+// S^T fragment of a 16-token tile (tile row r0 of the stage): s0/s1 token g (queries 2t, 2t+1),
+// s2/s3 token g + 8.
 template <int D, int MODE>
-__device__ __forceinline__ void qk_tile(const TileView &tv, const uint32_t (&b7r)[Cfg<D>::NK],
-                                        const uint32_t (&qb)[Cfg<D>::KS][2], Esc &es, int *status,
-                                        int lane, float (&s)[4]) {
+__device__ __forceinline__ void qk_tile(const uint8_t *stage, const Lay &ly, int r0,
+                                        const uint32_t (&b7)[Cfg<D>::NK],
+                                        const uint32_t (&qb)[Cfg<D>::KS][2], const StageEsc &se,
+                                        int i0, int i1, int tb, uint8_t *scr, int lane, float (&s)[4]) {
     using C = Cfg<D>;
-    const int gi = lane >> 2, tig = lane & 3;
-    constexpr int RS = MODE == 0 ? 2 * D : D;  // row stride of the row section
-    constexpr int CS = D * MODE / 8;           // row stride of the code section
-    const int c0 = tig * C::DK;
-    const uint8_t *r0 = tv.k_rows + gi * RS + (MODE == 0 ? 2 * c0 : c0);
-    const uint8_t *q0 = tv.k_codes + gi * CS + c0 * MODE / 8;
+    const int gi = lane >> 2;
     s[0] = s[1] = s[2] = s[3] = 0.f;
-    if (MODE == 0) {
-        uint32_t ka0[C::NK], ka1[C::NK];
-        lds_words<C::NK>(r0, ka0);
-        lds_words<C::NK>(r0 + 8 * RS, ka1);
-#pragma unroll
-        for (int k = 0; k < C::KS; ++k)
-            mma_bf16(s[0], s[1], s[2], s[3], ka0[2 * k], ka1[2 * k], ka0[2 * k + 1], ka1[2 * k + 1],
-                     qb[k][0], qb[k][1]);
-        return;
-    }
-    uint32_t b7[C::NK];
-#pragma unroll
-    for (int p = 0; p < C::NK; ++p) b7[p] = b7r[p];
-    if (!C::B7REG) load_b7k<D>(tv.k_base, b7);
+    const uint32_t halves = (MODE != 0 && i1 > i0) ? esc_halves<D>(se, i0, i1, tb, lane) : 0u;
     if (!C::SPLIT) {
         uint32_t ka0[C::NK], ka1[C::NK];
-        KRow<D, MODE> w0, w1;
-        w0.load(r0, q0, gi < tv.rows);
-        w1.load(r0 + 8 * RS, q0 + 8 * CS, gi + 8 < tv.rows);
-        w0.merge_into(b7, ka0);
-        w1.merge_into(b7, ka1);
-        if (__ballot_sync(FULL, w0.cnt != 0u) != 0u) esc_k_half<D, MODE>(ka0, w0, tv.k_scr, es, status, lane);
-        if (__ballot_sync(FULL, w1.cnt != 0u) != 0u) esc_k_half<D, MODE>(ka1, w1, tv.k_scr, es, status, lane);
+        k_row<D, MODE>(stage, ly, r0 + gi, b7, ka0);
+        k_row<D, MODE>(stage, ly, r0 + gi + 8, b7, ka1);
+        if (MODE != 0) {
+            if (halves & 1u) esc_patch<D, true>(ka0, scr, se, i0, i1, tb, 0, lane);
+            if (halves & 2u) esc_patch<D, true>(ka1, scr, se, i0, i1, tb, 1, lane);
+        }
 #pragma unroll
         for (int k = 0; k < C::KS; ++k)
             mma_bf16(s[0], s[1], s[2], s[3], ka0[2 * k], ka1[2 * k], ka0[2 * k + 1], ka1[2 * k + 1],
@@ -555,10 +539,8 @@ __device__ __forceinline__ void qk_tile(const TileView &tv, const uint32_t (&b7r
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
             uint32_t ka[C::NK];
-            KRow<D, MODE> w;
-            w.load(r0 + 8 * h * RS, q0 + 8 * h * CS, gi + 8 * h < tv.rows);
-            w.merge_into(b7, ka);
-            if (__ballot_sync(FULL, w.cnt != 0u) != 0u) esc_k_half<D, MODE>(ka, w, tv.k_scr, es, status, lane);
+            k_row<D, MODE>(stage, ly, r0 + gi + 8 * h, b7, ka);
+            if (MODE != 0 && (halves >> h & 1u)) esc_patch<D, true>(ka, scr, se, i0, i1, tb, h, lane);
 #pragma unroll
             for (int k = 0; k < C::KS; ++k) {
                 if (h == 0)
@@ -570,61 +552,26 @@ __device__ __forceinline__ void qk_tile(const TileView &tv, const uint32_t (&b7r
     }
 }
 
-// Raw V token pair (tokens 2t + 8h, 2t + 8h + 1) of this lane.
-template <int D>
-__device__ __forceinline__ void v_raw(const uint8_t *r0, int RS, uint32_t (&o)[Cfg<D>::DV]) {
-    uint32_t RA[Cfg<D>::DV / 2], RB[Cfg<D>::DV / 2];
-    lds_words<Cfg<D>::DV / 2>(r0, RA);
-    lds_words<Cfg<D>::DV / 2>(r0 + RS, RB);
-#pragma unroll
-    for (int e = 0; e < Cfg<D>::DV; ++e) o[e] = prmt(RA[e >> 1], RB[e >> 1], (e & 1) ? 0x7632u : 0x5410u);
-}
-
-// Zero the halves of tokens past the sub-tile's valid rows (P is 0 there, V must be finite).
-template <int D>
-__device__ __forceinline__ void v_tail(int t, int rows, uint32_t (&va)[Cfg<D>::DV]) {
-    const uint32_t keep = (t < rows ? 0x0000FFFFu : 0u) | (t + 1 < rows ? 0xFFFF0000u : 0u);
-#pragma unroll
-    for (int e = 0; e < Cfg<D>::DV; ++e) va[e] &= keep;
-}
-
-// O^T += V^T P^T for the tile (P^T as B fragments: bh = bf16 part, bm = residual part).
+// O^T += V^T P^T for a 16-token tile (P^T as B fragments: bh = bf16 part, bm = residual part).
 template <int D, int MODE>
-__device__ __forceinline__ void pv_tile(const TileView &tv, const uint32_t (&b7r)[Cfg<D>::DV],
-                                        const uint32_t (&bh)[2], const uint32_t (&bm)[2], Esc &es,
-                                        int *status, int lane, float (&acc)[Cfg<D>::KS][4]) {
+__device__ __forceinline__ void pv_tile(const uint8_t *stage, const Lay &ly, int r0, int rows,
+                                        const uint32_t (&b7)[Cfg<D>::DV], const uint32_t (&bh)[2],
+                                        const uint32_t (&bm)[2], const StageEsc &se, int i0, int i1,
+                                        int tb, uint8_t *scr, int lane, float (&acc)[Cfg<D>::KS][4]) {
     using C = Cfg<D>;
-    const int gi = lane >> 2, tig = lane & 3;
-    constexpr int RS = MODE == 0 ? 2 * D : D;
-    constexpr int CS = D * MODE / 8;
-    const int v0 = gi * C::DV;
-    const int t = 2 * tig;
-    const uint8_t *r0 = tv.v_rows + t * RS + (MODE == 0 ? 2 * v0 : v0);
-    const uint8_t *q0 = tv.v_codes + t * CS + v0 * MODE / 8;
-    uint32_t b7[C::DV];
-#pragma unroll
-    for (int e = 0; e < C::DV; ++e) b7[e] = b7r[e];
-    if (!C::B7REG && MODE != 0) load_b7v<D>(tv.v_base, b7);
+    const int t = 2 * (lane & 3);
+    const uint32_t halves = (MODE != 0 && i1 > i0) ? esc_halves<D>(se, i0, i1, tb, lane) : 0u;
     if (!C::SPLIT) {
         uint32_t va0[C::DV], va1[C::DV];
-        if (MODE == 0) {
-            v_raw<D>(r0, RS, va0);
-            v_raw<D>(r0 + 8 * RS, RS, va1);
-        } else {
-            VPair<D, MODE> p0, p1;
-            p0.load(r0, r0 + RS, q0, q0 + CS, t < tv.rows, t + 1 < tv.rows);
-            p1.load(r0 + 8 * RS, r0 + 9 * RS, q0 + 8 * CS, q0 + 9 * CS, t + 8 < tv.rows,
-                    t + 9 < tv.rows);
-            p0.merge_into(b7, va0);
-            p1.merge_into(b7, va1);
-            if (__ballot_sync(FULL, (p0.ca | p0.cb) != 0u) != 0u)
-                esc_v_half<D, MODE>(va0, p0, tv.v_scr, es, status, lane);
-            if (__ballot_sync(FULL, (p1.ca | p1.cb) != 0u) != 0u)
-                esc_v_half<D, MODE>(va1, p1, tv.v_scr, es, status, lane);
+        v_pair<D, MODE>(stage, ly, r0 + t, b7, va0);
+        v_pair<D, MODE>(stage, ly, r0 + t + 8, b7, va1);
+        if (MODE != 0) {
+            if (halves & 1u) esc_patch<D, false>(va0, scr, se, i0, i1, tb, 0, lane);
+            if (halves & 2u) esc_patch<D, false>(va1, scr, se, i0, i1, tb, 1, lane);
         }
-        if (tv.rows < TT) {
-            v_tail<D>(t, tv.rows, va0);
-            v_tail<D>(t + 8, tv.rows, va1);
+        if (rows < TT) {
+            v_tail<D>(t, rows, va0);
+            v_tail<D>(t + 8, rows, va1);
         }
 #pragma unroll
         for (int m = 0; m < C::KS; ++m) {
@@ -637,17 +584,9 @@ __device__ __forceinline__ void pv_tile(const TileView &tv, const uint32_t (&b7r
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
             uint32_t va[C::DV];
-            if (MODE == 0) {
-                v_raw<D>(r0 + 8 * h * RS, RS, va);
-            } else {
-                VPair<D, MODE> p;
-                p.load(r0 + 8 * h * RS, r0 + (8 * h + 1) * RS, q0 + 8 * h * CS, q0 + (8 * h + 1) * CS,
-                       t + 8 * h < tv.rows, t + 8 * h + 1 < tv.rows);
-                p.merge_into(b7, va);
-                if (__ballot_sync(FULL, (p.ca | p.cb) != 0u) != 0u)
-                    esc_v_half<D, MODE>(va, p, tv.v_scr, es, status, lane);
-            }
-            if (tv.rows < TT) v_tail<D>(t + 8 * h, tv.rows, va);
+            v_pair<D, MODE>(stage, ly, r0 + t + 8 * h, b7, va);
+            if (MODE != 0 && (halves >> h & 1u)) esc_patch<D, false>(va, scr, se, i0, i1, tb, h, lane);
+            if (rows < TT) v_tail<D>(t + 8 * h, rows, va);
 #pragma unroll
             for (int m = 0; m < C::KS; ++m) {
                 const uint32_t x0 = h == 0 ? va[2 * m] : 0u, x1 = h == 0 ? va[2 * m + 1] : 0u;
@@ -677,67 +616,60 @@ __device__ __forceinline__ void load_q(const uint16_t *q, int n_q, int stride,
 // ---- the worker -------------------------------------------------------------------------------
 
 // Walks the worker's flat blocks with one block of prefetch (flat indices fit 32 bits: the plan
-// refuses larger steps).
+// refuses larger steps), together with this lane's entry of each block's escape count headers.
 struct Walker {
     int fb, fb1;
     FlatBlock cur, nxt;
-    int unit, nunit;
-    __device__ __forceinline__ void init(const AttnArgs &a, int b0, int b1) {
+    uint32_t em, emn;
+    __device__ __forceinline__ void init(const AttnArgs &a, int b0, int b1, int lane) {
         fb = b0;
         fb1 = b1;
         cur = load_flat(a.flat, fb);
-        unit = __ldg(a.flat_unit + fb);
-        nunit = unit;
+        em = load_em(a.esc, cur, lane);
         if (fb + 1 < fb1) {
             nxt = load_flat(a.flat, fb + 1);
-            nunit = __ldg(a.flat_unit + fb + 1);
+            emn = load_em(a.esc, nxt, lane);
         }
     }
-    __device__ __forceinline__ void next(const AttnArgs &a) {
+    __device__ __forceinline__ void next(const AttnArgs &a, int lane) {
         ++fb;
         if (fb < fb1) {
             cur = nxt;
-            unit = nunit;
+            em = emn;
             if (fb + 1 < fb1) {
                 nxt = load_flat(a.flat, fb + 1);
-                nunit = __ldg(a.flat_unit + fb + 1);
+                emn = load_em(a.esc, nxt, lane);
             }
         }
     }
 };
 
-// Tokens per ring stage for a block: TSC when both tensors are coded, TT when either is raw.
-template <int D, bool BF16IN>
-__device__ __forceinline__ int stage_tokens(int km, int vm) {
-    return (BF16IN || km == 0 || vm == 0) ? TT : Cfg<D>::TSC;
-}
-
-// Copy side of the worker's ring.
+// Copy side of the worker's ring.  At a block's first stage it also leaves the block's FlatBlock
+// and escape count headers in the block's meta slot for the consumer side.
 template <int D, bool BF16IN> struct Producer {
     using C = Cfg<D>;
     Walker w;
     int tile = 0, stage = 0, bseq = 0;
-    const uint8_t *kr = nullptr, *vr = nullptr;  // row sections of the current block
-    int km = 0, vm = 0, st = TT;
+    const uint8_t *kb = nullptr, *vb = nullptr;  // the current unit's K and V blobs
 
-    __device__ __forceinline__ static void tensor(uint8_t *dst, const uint8_t *rows, int mode,
-                                                  int n_tok, int t0, int n, int lane) {
+    __device__ __forceinline__ static void tensor(uint8_t *dst, const Sections &s, const uint16_t *pos,
+                                                  int mode, int t0, int n, int e0, int e1, int lane) {
         if (BF16IN || mode == 0) {
-            copy_piece<TT * 2 * D + 16>(
-                dst, make_piece(rows + size_t(t0) * (2 * D), uint32_t(n * 2 * D)), lane);
+            copy_piece<C::TS * 2 * D + 16>(
+                dst, make_piece(s.rows + size_t(t0) * (2 * D), uint32_t(n * 2 * D)), lane);
         } else {
-            copy_piece<C::TSC * D + 16>(dst, make_piece(rows + size_t(t0) * D, uint32_t(n * D)), lane);
-            const uint8_t *codes = rows + size_t(n_tok) * D;
-            copy_piece<C::TSC * D / 2 + 16>(
+            copy_piece<C::TS * D + 16>(dst, make_piece(s.rows + size_t(t0) * D, uint32_t(n * D)), lane);
+            copy_piece<C::TS * D / 2 + 16>(
                 dst + C::CODE_OFF,
-                make_piece(codes + size_t(t0) * D * mode / 8, uint32_t(n * D * mode / 8)), lane);
+                make_piece(s.codes + size_t(t0) * D * mode / 8, uint32_t(n * D * mode / 8)), lane);
+            const int cnt = e1 - e0;
+            if (cnt > 0 && cnt <= C::ESC_CAP) {
+                copy_piece<2 * C::ESC_CAP + 16>(dst + C::EV_OFF, make_piece(s.esc + 2 * e0, uint32_t(2 * cnt)), lane);
+                copy_piece<2 * C::ESC_CAP + 16>(
+                    dst + C::EP_OFF, make_piece(reinterpret_cast<const uint8_t *>(pos + e0), uint32_t(2 * cnt)),
+                    lane);
+            }
         }
-    }
-    __device__ __forceinline__ static void meta(uint8_t *base, uint8_t *escs, const Sections &s,
-                                                int nesc, int lane) {
-        copy_piece<D + 32>(base, make_piece(s.rows - D, D), lane);
-        const Piece e = make_piece(s.esc, uint32_t(2 * nesc));
-        if (esc_staged<D>(e, nesc)) copy_piece<C::ESCB>(escs, e, lane);
     }
 
     // Issue stages while a ring slot is free; a block start waits until the consumer is at most
@@ -747,37 +679,65 @@ template <int D, bool BF16IN> struct Producer {
         while (w.fb < w.fb1 && stage - c_stage < C::NSTAGE) {
             if (tile == 0 && w.fb - c_fb >= 2) break;
             const FlatBlock &f = w.cur;
+            const int km = BF16IN ? 0 : f.k_mode, vm = BF16IN ? 0 : f.v_mode;
             if (tile == 0) {
-                km = BF16IN ? 0 : f.k_mode;
-                vm = BF16IN ? 0 : f.v_mode;
-                st = stage_tokens<D, BF16IN>(km, vm);
-                const Sections sk = sections<D, BF16IN>(a.units[w.unit].k, f.k_off, km, f.n_tok);
-                const Sections sv = sections<D, BF16IN>(a.units[w.unit].v, f.v_off, vm, f.n_tok);
-                kr = sk.rows;
-                vr = sv.rows;
+                const UnitDev *U = a.units + f.unit;
+                kb = U->k;
+                vb = U->v;
+                uint8_t *ms = metas + (bseq & 1) * C::MSLOT;
+                if (lane == 0) {
+                    const uint4 *src = reinterpret_cast<const uint4 *>(&f);
+                    reinterpret_cast<uint4 *>(ms + C::M_FB)[0] = src[0];
+                    reinterpret_cast<uint4 *>(ms + C::M_FB)[1] = src[1];
+                }
+                reinterpret_cast<uint16_t *>(ms + C::M_EM)[lane] = uint16_t(w.em);
                 if (!BF16IN) {
-                    uint8_t *ms = metas + (bseq & 1) * C::MSLOT;
-                    if (km != 0) meta(ms + C::M_K, ms + C::M_EK, sk, f.k_nesc, lane);
-                    if (vm != 0) meta(ms + C::M_V, ms + C::M_EV, sv, f.v_nesc, lane);
+                    if (km != 0) copy_piece<D + 32>(ms, make_piece(kb + f.k_off + kHeaderBytes, D), lane);
+                    if (vm != 0) copy_piece<D + 32>(ms + C::BASE, make_piece(vb + f.v_off + kHeaderBytes, D), lane);
                 }
             }
-            const int t0 = tile * st;
-            const int n = min(st, int(f.valid) - t0);
+            const int t0 = tile * C::TS;
+            const int n = min(C::TS, int(f.valid) - t0);
+            const int ia = t0 >> 4, ib = min(16, (t0 + C::TS) >> 4);
             uint8_t *slot = ring + (stage % C::NSTAGE) * C::SLOT;
-            tensor(slot, kr, km, f.n_tok, t0, n, lane);
-            tensor(slot + C::TR, vr, vm, f.n_tok, t0, n, lane);
+            tensor(slot, sections<D, BF16IN>(kb, f.k_off, km, f.n_tok), a.esc + f.k_rec + kEscRecHead,
+                   km, t0, n, esc_at(w.em, 0, ia), esc_at(w.em, 0, ib), lane);
+            tensor(slot + C::TR, sections<D, BF16IN>(vb, f.v_off, vm, f.n_tok),
+                   a.esc + f.v_rec + kEscRecHead, vm, t0, n, esc_at(w.em, 1, ia), esc_at(w.em, 1, ib), lane);
             cp_async_commit();
             ++stage;
-            if (t0 + st >= int(f.valid)) {
+            if (t0 + C::TS >= int(f.valid)) {
                 tile = 0;
                 ++bseq;
-                w.next(a);
+                w.next(a, lane);
             } else {
                 ++tile;
             }
         }
     }
 };
+
+// The escape words of tensor T (0 K, 1 V) of the block's stage holding escapes [e0, e1):
+// the producer's staged copies when they fit, else the block's words in HBM.
+template <int D>
+__device__ __forceinline__ StageEsc stage_esc(const AttnArgs &a, const FlatBlock &f, int T,
+                                              const uint8_t *tstage, int e0, int e1) {
+    using C = Cfg<D>;
+    const uint32_t off = T ? f.v_off : f.k_off, rec = T ? f.v_rec : f.k_rec;
+    const int mode = T ? f.v_mode : f.k_mode;
+    StageEsc se;
+    if (e1 - e0 <= C::ESC_CAP) {
+        se.val = reinterpret_cast<const uint16_t *>(tstage + C::EV_OFF + esc_word_line<D>(off, f.n_tok, mode, e0));
+        se.pos = reinterpret_cast<const uint16_t *>(tstage + C::EP_OFF + esc_pos_line(rec, e0));
+        se.off = e0;
+    } else {
+        const UnitDev *U = a.units + f.unit;
+        se.val = reinterpret_cast<const uint16_t *>(sections<D, false>(T ? U->v : U->k, off, mode, f.n_tok).esc);
+        se.pos = a.esc + rec + kEscRecHead;
+        se.off = 0;
+    }
+    return se;
+}
 
 template <int D, bool BF16IN>
 __device__ __forceinline__ void worker(const AttnArgs &a, uint8_t *R, int wk, int fb0, int fb1,
@@ -786,15 +746,12 @@ __device__ __forceinline__ void worker(const AttnArgs &a, uint8_t *R, int wk, in
     const int gi = lane >> 2, tig = lane & 3;
     uint8_t *ring = R;
     uint8_t *metas = R + C::W_META;
+    uint8_t *scr = R + C::W_SCR;
     Producer<D, BF16IN> pp;
-    pp.w.init(a, fb0, fb1);
-    Walker cw;
-    cw.init(a, fb0, fb1);
-    int tile = 0, stage = 0, bseq = 0;
+    pp.w.init(a, fb0, fb1, lane);
+    int fb = fb0, tile = 0, stage = 0, bseq = 0;
     int ubeg = 0, uend = 0, seg_begin = fb0;  // the current unit's flat block range
-    int kmode = 0, vmode = 0, st = TT;
-    uint32_t kd = 0, vd = 0;  // source alignment of the block's row sections
-    Esc ek{0, 0, nullptr, nullptr}, ev{0, 0, nullptr, nullptr};
+    Lay lk{}, lv{};
     uint32_t b7k[C::NK], b7v[C::DV];
 #pragma unroll
     for (int p = 0; p < C::NK; ++p) b7k[p] = 0u;
@@ -804,40 +761,29 @@ __device__ __forceinline__ void worker(const AttnArgs &a, uint8_t *R, int wk, in
     float acc[C::KS][4];
     float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
 
-    while (cw.fb < fb1) {
-        pp.produce(a, ring, metas, stage, cw.fb, lane);
+    while (fb < fb1) {
+        pp.produce(a, ring, metas, stage, fb, lane);
         cp_async_wait(pp.stage - stage - 1);
         __syncwarp();
-        const FlatBlock f = cw.cur;
         const uint8_t *ms = metas + (bseq & 1) * C::MSLOT;
+        const FlatBlock f = *reinterpret_cast<const FlatBlock *>(ms + C::M_FB);
+        const uint8_t *em = ms + C::M_EM;
+        const int kmode = BF16IN ? 0 : f.k_mode, vmode = BF16IN ? 0 : f.v_mode;
         if (tile == 0) {
-            const UnitDev *U = a.units + cw.unit;
+            const UnitDev *U = a.units + f.unit;
             ubeg = int(U->block_begin);
             uend = ubeg + U->n_blocks;
-            kmode = BF16IN ? 0 : f.k_mode;
-            vmode = BF16IN ? 0 : f.v_mode;
-            st = stage_tokens<D, BF16IN>(kmode, vmode);
             const Sections sk = sections<D, BF16IN>(U->k, f.k_off, kmode, f.n_tok);
             const Sections sv = sections<D, BF16IN>(U->v, f.v_off, vmode, f.n_tok);
-            kd = uint32_t(reinterpret_cast<uintptr_t>(sk.rows) & 15u);
-            vd = uint32_t(reinterpret_cast<uintptr_t>(sv.rows) & 15u);
-            if (kmode != 0) {
-                if (C::B7REG) load_b7k<D>(ms + C::M_K + kd + tig * C::DK, b7k);
-                const Piece e = make_piece(sk.esc, uint32_t(2 * f.k_nesc));
-                ek.run = 0;
-                ek.n = f.k_nesc;
-                ek.gm = reinterpret_cast<const unsigned short *>(sk.esc);
-                ek.sm = esc_staged<D>(e, f.k_nesc) ? ms + C::M_EK + e.data : nullptr;
-            }
-            if (vmode != 0) {
-                if (C::B7REG) load_b7v<D>(ms + C::M_V + vd + gi * C::DV, b7v);
-                const Piece e = make_piece(sv.esc, uint32_t(2 * f.v_nesc));
-                ev.run = 0;
-                ev.n = f.v_nesc;
-                ev.gm = reinterpret_cast<const unsigned short *>(sv.esc);
-                ev.sm = esc_staged<D>(e, f.v_nesc) ? ms + C::M_EV + e.data : nullptr;
-            }
-            if (cw.fb == seg_begin) {
+            const uint32_t kd = uint32_t(reinterpret_cast<uintptr_t>(sk.rows) & 15u);
+            const uint32_t vd = uint32_t(reinterpret_cast<uintptr_t>(sv.rows) & 15u);
+            const uint32_t kc = kmode ? uint32_t(reinterpret_cast<uintptr_t>(sk.codes) & 15u) : 0u;
+            const uint32_t vc = vmode ? uint32_t(reinterpret_cast<uintptr_t>(sv.codes) & 15u) : 0u;
+            lk = make_lay<D>(kd, kc, kmode, tig * C::DK, BF16IN);
+            lv = make_lay<D>(vd, vc, vmode, gi * C::DV, BF16IN);
+            if (kmode != 0) load_b7k<D>(ms + kd + tig * C::DK, b7k);
+            if (vmode != 0) load_b7v<D>(ms + C::BASE + vd + gi * C::DV, b7v);
+            if (fb == seg_begin) {
                 load_q<D>(U->q, U->n_q, U->q_stride, qb, lane);
                 m0 = m1 = -INFINITY;
                 l0 = l1 = 0.f;
@@ -845,75 +791,95 @@ __device__ __forceinline__ void worker(const AttnArgs &a, uint8_t *R, int wk, in
                 for (int m = 0; m < C::KS; ++m) acc[m][0] = acc[m][1] = acc[m][2] = acc[m][3] = 0.f;
             }
         }
-        const uint8_t *slot = ring + (stage % C::NSTAGE) * C::SLOT;
-        const int t0 = tile * st;
-        const int rows_stage = min(st, int(f.valid) - t0);
-        const bool last_tile = t0 + st >= int(f.valid);
-        const bool seg_end = last_tile && (cw.fb + 1 == fb1 || cw.fb + 1 == uend);
+        uint8_t *slot = ring + (stage % C::NSTAGE) * C::SLOT;
+        const int t0 = tile * C::TS;
+        const int rows = min(C::TS, int(f.valid) - t0);
+        const bool last_tile = t0 + C::TS >= int(f.valid);
+        const bool seg_end = last_tile && (fb + 1 == fb1 || fb + 1 == uend);
+        const int ia = t0 >> 4, ib = min(16, (t0 + C::TS) >> 4);
 
-#pragma unroll 1
-        for (int sub = 0; sub < C::SUBS; ++sub) {
-            if (sub * TT >= rows_stage) break;
-            TileView tv;
-            tv.rows = min(TT, rows_stage - sub * TT);
-            tv.k_rows = slot + kd + sub * TT * (kmode == 0 ? 2 * D : D);
-            tv.k_codes = slot + C::CODE_OFF + kd + sub * TT * (D * kmode / 8);
-            tv.v_rows = slot + C::TR + vd + sub * TT * (vmode == 0 ? 2 * D : D);
-            tv.v_codes = slot + C::TR + C::CODE_OFF + vd + sub * TT * (D * vmode / 8);
-            tv.k_base = ms + C::M_K + kd + tig * C::DK;
-            tv.v_base = ms + C::M_V + vd + gi * C::DV;
-            tv.k_scr = C::SPLIT ? R + C::W_SCR : const_cast<uint8_t *>(slot) + sub * TT * D;
-            tv.v_scr = C::SPLIT ? R + C::W_SCR : const_cast<uint8_t *>(slot) + C::TR + sub * TT * D;
-
-            // S^T = K Q^T
-            float s[4];
-            if (kmode == 4) qk_tile<D, 4>(tv, b7k, qb, ek, a.status, lane, s);
-            else if (kmode == 2) qk_tile<D, 2>(tv, b7k, qb, ek, a.status, lane, s);
-            else qk_tile<D, 0>(tv, b7k, qb, ek, a.status, lane, s);
-            if (gi >= tv.rows) s[0] = s[1] = -INFINITY;
-            if (gi + 8 >= tv.rows) s[2] = s[3] = -INFINITY;
-
-            // online softmax over the sub-tile's tokens; p = 2^(s log2e - m log2e)
-            float t0m = fmaxf(s[0], s[2]), t1m = fmaxf(s[1], s[3]);
+        // S^T = K Q^T for every tile of the stage
+        float s[C::SUBS][4];
+        {
+            const StageEsc se = stage_esc<D>(a, f, 0, slot, esc_ms(em, 0, ia), esc_ms(em, 0, ib));
 #pragma unroll
-            for (int o = 4; o < 32; o <<= 1) {
-                t0m = fmaxf(t0m, __shfl_xor_sync(FULL, t0m, o));
-                t1m = fmaxf(t1m, __shfl_xor_sync(FULL, t1m, o));
-            }
-            const float mn0 = fmaxf(m0, t0m), mn1 = fmaxf(m1, t1m);
-            const float ml0 = __fmul_rn(mn0, kLog2e), ml1 = __fmul_rn(mn1, kLog2e);
-            const float al0 = ex2(__fmaf_rn(m0, kLog2e, -ml0)), al1 = ex2(__fmaf_rn(m1, kLog2e, -ml1));
-            const float p0 = ex2(__fmaf_rn(s[0], kLog2e, -ml0)), p1 = ex2(__fmaf_rn(s[1], kLog2e, -ml1));
-            const float p2 = ex2(__fmaf_rn(s[2], kLog2e, -ml0)), p3 = ex2(__fmaf_rn(s[3], kLog2e, -ml1));
-            l0 = __fmaf_rn(l0, al0, __fadd_rn(p0, p2));
-            l1 = __fmaf_rn(l1, al1, __fadd_rn(p1, p3));
-            m0 = mn0;
-            m1 = mn1;
-
-            // P^T B fragments: bf16(p) and bf16(p - bf16(p))
-            uint32_t bh[2], bm[2];
-            {
-                const uint32_t h01 = pack_bf16x2(p1, p0), h23 = pack_bf16x2(p3, p2);
-                const float r0 = __fsub_rn(p0, bf16lo_to_f32(h01)), r1 = __fsub_rn(p1, bf16hi_to_f32(h01));
-                const float r2 = __fsub_rn(p2, bf16lo_to_f32(h23)), r3 = __fsub_rn(p3, bf16hi_to_f32(h23));
-                bh[0] = movm_t(h01);
-                bh[1] = movm_t(h23);
-                bm[0] = movm_t(pack_bf16x2(r1, r0));
-                bm[1] = movm_t(pack_bf16x2(r3, r2));
-            }
-            if (__any_sync(FULL, al0 != 1.0f || al1 != 1.0f)) {
-#pragma unroll
-                for (int m = 0; m < C::KS; ++m) {
-                    acc[m][0] = __fmul_rn(acc[m][0], al0);
-                    acc[m][1] = __fmul_rn(acc[m][1], al1);
-                    acc[m][2] = __fmul_rn(acc[m][2], al0);
-                    acc[m][3] = __fmul_rn(acc[m][3], al1);
+            for (int sub = 0; sub < C::SUBS; ++sub) {
+                if (sub * TT < rows) {
+                    const int i0 = esc_ms(em, 0, ia + sub), i1 = esc_ms(em, 0, ia + sub + 1);
+                    const int tb = t0 + sub * TT;
+                    if (kmode == 4) qk_tile<D, 4>(slot, lk, sub * TT, b7k, qb, se, i0, i1, tb, scr, lane, s[sub]);
+                    else if (kmode == 2) qk_tile<D, 2>(slot, lk, sub * TT, b7k, qb, se, i0, i1, tb, scr, lane, s[sub]);
+                    else qk_tile<D, 0>(slot, lk, sub * TT, b7k, qb, se, i0, i1, tb, scr, lane, s[sub]);
+                    const int rr = rows - sub * TT;
+                    if (gi >= rr) s[sub][0] = s[sub][1] = -INFINITY;
+                    if (gi + 8 >= rr) s[sub][2] = s[sub][3] = -INFINITY;
+                } else {
+                    s[sub][0] = s[sub][1] = s[sub][2] = s[sub][3] = -INFINITY;
                 }
             }
-            // O^T += V^T P^T
-            if (vmode == 4) pv_tile<D, 4>(tv, b7v, bh, bm, ev, a.status, lane, acc);
-            else if (vmode == 2) pv_tile<D, 2>(tv, b7v, bh, bm, ev, a.status, lane, acc);
-            else pv_tile<D, 0>(tv, b7v, bh, bm, ev, a.status, lane, acc);
+        }
+
+        // online softmax over the stage's tokens; p = 2^(s log2e - m log2e)
+        float t0m = fmaxf(s[0][0], s[0][2]), t1m = fmaxf(s[0][1], s[0][3]);
+#pragma unroll
+        for (int sub = 1; sub < C::SUBS; ++sub) {
+            t0m = fmaxf(t0m, fmaxf(s[sub][0], s[sub][2]));
+            t1m = fmaxf(t1m, fmaxf(s[sub][1], s[sub][3]));
+        }
+#pragma unroll
+        for (int o = 4; o < 32; o <<= 1) {
+            t0m = fmaxf(t0m, __shfl_xor_sync(FULL, t0m, o));
+            t1m = fmaxf(t1m, __shfl_xor_sync(FULL, t1m, o));
+        }
+        const float mn0 = fmaxf(m0, t0m), mn1 = fmaxf(m1, t1m);
+        const float ml0 = __fmul_rn(mn0, kLog2e), ml1 = __fmul_rn(mn1, kLog2e);
+        const float al0 = ex2(__fmaf_rn(m0, kLog2e, -ml0)), al1 = ex2(__fmaf_rn(m1, kLog2e, -ml1));
+        float ps0 = 0.f, ps1 = 0.f;
+        uint32_t bh[C::SUBS][2], bm[C::SUBS][2];
+#pragma unroll
+        for (int sub = 0; sub < C::SUBS; ++sub) {
+            const float p0 = ex2(__fmaf_rn(s[sub][0], kLog2e, -ml0)), p1 = ex2(__fmaf_rn(s[sub][1], kLog2e, -ml1));
+            const float p2 = ex2(__fmaf_rn(s[sub][2], kLog2e, -ml0)), p3 = ex2(__fmaf_rn(s[sub][3], kLog2e, -ml1));
+            ps0 = __fadd_rn(ps0, __fadd_rn(p0, p2));
+            ps1 = __fadd_rn(ps1, __fadd_rn(p1, p3));
+            // P^T B fragments: bf16(p) and bf16(p - bf16(p))
+            const uint32_t h01 = pack_bf16x2(p1, p0), h23 = pack_bf16x2(p3, p2);
+            const float r0 = __fsub_rn(p0, bf16lo_to_f32(h01)), r1 = __fsub_rn(p1, bf16hi_to_f32(h01));
+            const float r2 = __fsub_rn(p2, bf16lo_to_f32(h23)), r3 = __fsub_rn(p3, bf16hi_to_f32(h23));
+            bh[sub][0] = movm_t(h01);
+            bh[sub][1] = movm_t(h23);
+            bm[sub][0] = movm_t(pack_bf16x2(r1, r0));
+            bm[sub][1] = movm_t(pack_bf16x2(r3, r2));
+        }
+        l0 = __fmaf_rn(l0, al0, ps0);
+        l1 = __fmaf_rn(l1, al1, ps1);
+        m0 = mn0;
+        m1 = mn1;
+        if (__any_sync(FULL, al0 != 1.0f || al1 != 1.0f)) {
+#pragma unroll
+            for (int m = 0; m < C::KS; ++m) {
+                acc[m][0] = __fmul_rn(acc[m][0], al0);
+                acc[m][1] = __fmul_rn(acc[m][1], al1);
+                acc[m][2] = __fmul_rn(acc[m][2], al0);
+                acc[m][3] = __fmul_rn(acc[m][3], al1);
+            }
+        }
+
+        // O^T += V^T P^T for every tile of the stage
+        {
+            const uint8_t *vstage = slot + C::TR;
+            const StageEsc se = stage_esc<D>(a, f, 1, vstage, esc_ms(em, 1, ia), esc_ms(em, 1, ib));
+#pragma unroll
+            for (int sub = 0; sub < C::SUBS; ++sub) {
+                if (sub * TT < rows) {
+                    const int i0 = esc_ms(em, 1, ia + sub), i1 = esc_ms(em, 1, ia + sub + 1);
+                    const int tb = t0 + sub * TT;
+                    const int rr = min(TT, rows - sub * TT);
+                    if (vmode == 4) pv_tile<D, 4>(vstage, lv, sub * TT, rr, b7v, bh[sub], bm[sub], se, i0, i1, tb, scr, lane, acc);
+                    else if (vmode == 2) pv_tile<D, 2>(vstage, lv, sub * TT, rr, b7v, bh[sub], bm[sub], se, i0, i1, tb, scr, lane, acc);
+                    else pv_tile<D, 0>(vstage, lv, sub * TT, rr, b7v, bh[sub], bm[sub], se, i0, i1, tb, scr, lane, acc);
+                }
+            }
         }
 
         if (seg_end) {
@@ -925,8 +891,8 @@ __device__ __forceinline__ void worker(const AttnArgs &a, uint8_t *R, int wk, in
             }
             const int qa = 2 * tig, qc = 2 * tig + 1;
             const int d0 = gi * C::DV;
-            if (seg_begin == ubeg && cw.fb + 1 == uend) {
-                const UnitDev *U = a.units + cw.unit;
+            if (seg_begin == ubeg && fb + 1 == uend) {
+                const UnitDev *U = a.units + f.unit;
                 const int n_q = U->n_q, stride = U->q_stride;
                 float *out = U->out;
                 float *lse = U->lse;
@@ -972,8 +938,8 @@ __device__ __forceinline__ void worker(const AttnArgs &a, uint8_t *R, int wk, in
         if (last_tile) {
             tile = 0;
             ++bseq;
-            if (seg_end) seg_begin = cw.fb + 1;
-            cw.next(a);
+            if (seg_end) seg_begin = fb + 1;
+            ++fb;
         } else {
             ++tile;
         }
@@ -1063,6 +1029,37 @@ __global__ void __launch_bounds__(kCombineThreads) combine_kernel(const CombineA
         unit.out[size_t(g) * unit.q_stride + d] = __fmul_rn(v, inv);
     }
     if (tid == 0 && unit.lse != nullptr) unit.lse[g] = M + logf(lsum);
+}
+
+// ---- fold of sequence shards --------------------------------------------------------------------
+
+// Rank-ordered fold of the normalised outputs of sequence shards: per row (unit, query),
+// M = max_r lse_r, w_r = exp(lse_r - M), out = (sum_r w_r o_r) * (1 / sum_r w_r).  This is the
+// reference's thread fold (src/dispatch.cpp:98-103 with merge_state, src/softmax.hpp:16-30, and
+// finalize_state, :32-41) carried over to outputs that are already normalised, where l_r is
+// exp(lse_r - m_r).  Part r sits at parts + r * (n_rows * dim + n_rows): outputs [n_rows, dim],
+// then lse [n_rows].  A part whose lse is -inf (an empty shard) is skipped, whatever its outputs
+// hold.  One CTA per row; every thread folds the parts in rank order.
+__global__ void fold_kernel(const float *__restrict__ parts, int n_parts, int n_rows, int dim,
+                            float *__restrict__ out, float *__restrict__ lse_out) {
+    const int row = blockIdx.x;
+    const size_t stride = size_t(n_rows) * dim + n_rows;
+    const float *lse = parts + size_t(n_rows) * dim + row;
+    float M = -INFINITY;
+    for (int r = 0; r < n_parts; ++r) M = fmaxf(M, lse[r * stride]);
+    float den = 0.f;
+    for (int r = 0; r < n_parts; ++r) den = __fadd_rn(den, expf(lse[r * stride] - M));
+    const float inv = __frcp_rn(den);
+    for (int d = threadIdx.x; d < dim; d += blockDim.x) {
+        float acc = 0.f;
+        for (int r = 0; r < n_parts; ++r) {
+            const float l = lse[r * stride];
+            if (l == -INFINITY) continue;
+            acc = __fmaf_rn(expf(l - M), parts[r * stride + size_t(row) * dim + d], acc);
+        }
+        out[size_t(row) * dim + d] = __fmul_rn(acc, inv);
+    }
+    if (threadIdx.x == 0 && lse_out != nullptr) lse_out[row] = M + logf(den);
 }
 
 // ---- worker ranges -----------------------------------------------------------------------------
@@ -1176,6 +1173,12 @@ cudaError_t launch_attention(int dim, bool bf16_input, const AttnArgs &a, int gr
 cudaError_t launch_split(const FlatBlock *flat, int64_t n_blocks, int n_workers, int64_t *range_begin,
                          cudaStream_t s) {
     split_kernel<<<1, 1024, 0, s>>>(flat, n_blocks, n_workers, range_begin);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_fold(const float *parts, int n_parts, int n_rows, int dim, float *out,
+                        float *lse_out, cudaStream_t s) {
+    fold_kernel<<<n_rows, dim < 256 ? dim : 256, 0, s>>>(parts, n_parts, n_rows, dim, out, lse_out);
     return cudaGetLastError();
 }
 

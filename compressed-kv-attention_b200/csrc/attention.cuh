@@ -6,19 +6,52 @@
 namespace kvx {
 
 // One flat block of a batched step: the K and V index entries of the same token range.
-// `tok0` is the block's first token (used by the BF16 kernel, whose "blocks" are tiles of
-// block_tokens rows of a plain [seq, dim] array).
+// For the BF16 kernel, whose "blocks" are tiles of block_tokens rows of a plain [seq, dim] array,
+// k_off / v_off hold the tile's first token.
 struct FlatBlock {
     uint32_t k_off;   // XKV: header offset in the K blob.  BF16: first token.
     uint32_t v_off;   // XKV: header offset in the V blob.  BF16: first token.
+    uint32_t k_rec;   // escape record of the K block in the step's record array (u16 units)
+    uint32_t v_rec;
     uint16_t k_nesc;  // escape words
     uint16_t v_nesc;
     uint8_t k_mode;   // 0 raw, 2, 4
     uint8_t v_mode;
     uint8_t n_tok;    // tokens in the encoded block (layout)
     uint8_t valid;    // tokens attended (< n_tok only for the last block of a unit)
+    int32_t unit;     // device unit the block belongs to
+    int32_t src;      // flat block whose escape records this one shares (itself unless it is the
+                      // same K/V block seen by another query group of the same unit)
 };
-static_assert(sizeof(FlatBlock) == 16, "FlatBlock is 16 bytes");
+static_assert(sizeof(FlatBlock) == 32, "FlatBlock is 32 bytes");
+
+// Escape record of one coded block with escape words (u16 array):
+//   [0, 16)           e[i - 1] = escape words of tokens [0, 16 i), i = 1..16 (clamped to the
+//                     block), so the escapes of tokens [16 a, 16 b) are [e(a), e(b)), e(0) = 0;
+//   [16, 16 + n_esc)  the element index (token * dim + channel) of every escape, in the
+//                     container's scan order -- the sentinel the escape word replaces.
+// Built once per plan from the blob's residual codes; raw blocks and blocks without escapes
+// have none.
+constexpr int kEscRecHead = 16;
+
+__device__ __forceinline__ FlatBlock load_flat(const FlatBlock *f, int64_t i) {
+    const uint4 a = __ldg(reinterpret_cast<const uint4 *>(f + i));
+    const uint4 b = __ldg(reinterpret_cast<const uint4 *>(f + i) + 1);
+    FlatBlock r;
+    r.k_off = a.x;
+    r.v_off = a.y;
+    r.k_rec = a.z;
+    r.v_rec = a.w;
+    r.k_nesc = uint16_t(b.x & 0xFFFF);
+    r.v_nesc = uint16_t(b.x >> 16);
+    r.k_mode = uint8_t(b.y & 0xFF);
+    r.v_mode = uint8_t((b.y >> 8) & 0xFF);
+    r.n_tok = uint8_t((b.y >> 16) & 0xFF);
+    r.valid = uint8_t(b.y >> 24);
+    r.unit = int32_t(b.z);
+    r.src = int32_t(b.w);
+    return r;
+}
 
 // Device copy of one unit.
 struct UnitDev {
@@ -38,7 +71,7 @@ static_assert(sizeof(UnitDev) == 64, "UnitDev is 64 bytes");
 struct AttnArgs {
     const UnitDev *units;
     const FlatBlock *flat;      // [n_blocks]
-    const int32_t *flat_unit;   // [n_blocks] unit of each flat block
+    const uint16_t *esc;        // escape records (FlatBlock::k_rec / v_rec index it)
     const int64_t *range_begin; // [n_workers + 1] flat-block range of each worker warp
     float *partials;            // [n_workers][2][8 + 8 + 8 * dim]
     int *status;                // [2] first error (code, detail)
@@ -69,6 +102,16 @@ __host__ __device__ inline int worker_of_block(const int64_t *range_begin, int n
 // Launchers (attention.cu).  Return cudaError_t of the launch.
 cudaError_t launch_attention(int dim, bool bf16_input, const AttnArgs &a, int grid, cudaStream_t s);
 cudaError_t launch_combine(int dim, const CombineArgs &a, int n_split, cudaStream_t s);
+cudaError_t launch_fold(const float *parts, int n_parts, int n_rows, int dim, float *out,
+                        float *lse_out, cudaStream_t s);
+// Escape records: sizes and offsets (single CTA; *total receives the record array length in u16,
+// blocks whose src is another block take that block's offsets, and a record that would end past
+// `cap` entries reports DERR_ESC_CAP), then the records themselves (the fill reports
+// DERR_ESC_OVERRUN for a block with more sentinels than escape words).
+cudaError_t launch_esc_layout(FlatBlock *flat, int64_t n_blocks, unsigned long long *total,
+                              unsigned long long cap, int *status, cudaStream_t s);
+cudaError_t launch_esc_fill(const UnitDev *units, const FlatBlock *flat, int64_t n_blocks, int dim,
+                            uint16_t *esc, unsigned long long cap, int *status, cudaStream_t s);
 // Cost-balanced worker ranges over the flat block list: range_begin[0..n_workers].
 cudaError_t launch_split(const FlatBlock *flat, int64_t n_blocks, int n_workers, int64_t *range_begin,
                          cudaStream_t s);

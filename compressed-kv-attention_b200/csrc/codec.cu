@@ -84,12 +84,13 @@ __global__ void index_walk_kernel(const uint8_t *blob, uint64_t bytes, int dim, 
     *n_tokens = tok;
 }
 
-__global__ void build_flat_kernel(const kvx_unit *units, const int64_t *block_begin, int dim,
-                                  int bt, bool bf16, FlatBlock *flat, int32_t *flat_unit,
-                                  int *status) {
+__global__ void build_flat_kernel(const kvx_unit *units, const int64_t *block_begin,
+                                  const int64_t *src_begin, int dim, int bt, bool bf16,
+                                  FlatBlock *flat, int *status) {
     const int u = blockIdx.x;
     const kvx_unit U = units[u];
     const int64_t b0 = block_begin[u];
+    const int64_t s0 = src_begin != nullptr ? src_begin[u] : b0;
     __shared__ int last_valid;
     if (threadIdx.x == 0) {
         if (bf16) {
@@ -123,8 +124,10 @@ __global__ void build_flat_kernel(const kvx_unit *units, const int64_t *block_be
             const bool km = ke.mode == 0 || ke.mode == 2 || ke.mode == 4;
             const bool vm = ve.mode == 0 || ve.mode == 2 || ve.mode == 4;
             if (!km || !vm) report(status, KVX_ERR_RUNTIME, DERR_MODE);
+            // Every block of a well-formed blob starts at an even offset (all sizes are even);
+            // the kernels rely on it.
             if (uint64_t(ke.offset) + block_bytes(ke, dim) > U.k_bytes ||
-                uint64_t(ve.offset) + block_bytes(ve, dim) > U.v_bytes)
+                uint64_t(ve.offset) + block_bytes(ve, dim) > U.v_bytes || ((ke.offset | ve.offset) & 1u))
                 report(status, KVX_ERR_RUNTIME, DERR_RANGE);
             f.k_off = ke.offset;
             f.v_off = ve.offset;
@@ -135,8 +138,10 @@ __global__ void build_flat_kernel(const kvx_unit *units, const int64_t *block_be
             f.n_tok = ke.n_tokens;
             f.valid = uint8_t(j + 1 == U.n_blocks ? last_valid : ke.n_tokens);
         }
+        f.k_rec = f.v_rec = 0;
+        f.unit = u;
+        f.src = int32_t(s0 + j);
         flat[b0 + j] = f;
-        flat_unit[b0 + j] = u;
     }
 }
 
@@ -477,6 +482,143 @@ __global__ void read_probe_kernel(const uint4 *buf, size_t n16, uint32_t *sink) 
     if (acc == 0x9E3779B9u) sink[0] = acc;  // keeps the loads alive
 }
 
+// ---- escape records --------------------------------------------------------------------------
+//
+// For every coded block with escape words, the element index of each escape (the position of the
+// sentinel residual it replaces, in scan order) and the escape counts of its 16-token groups; see
+// kEscRecHead.  The attention kernels read these instead of searching for sentinels.
+
+__device__ __forceinline__ uint32_t esc_rec_size(int mode, int nesc) {
+    return (mode != 0 && nesc > 0) ? uint32_t(kEscRecHead + nesc) : 0u;
+}
+
+// One CTA: record offsets in flat order (K then V of each block), blocks that share another
+// block's records get size 0 here and its offsets in esc_dup_kernel.
+__global__ void __launch_bounds__(1024) esc_layout_kernel(FlatBlock *flat, int64_t n,
+                                                          unsigned long long *total,
+                                                          unsigned long long cap, int *status) {
+    __shared__ unsigned long long part[1024];
+    const int t = threadIdx.x, T = blockDim.x;
+    const int64_t chunk = (n + T - 1) / T;
+    const int64_t lo = min(n, t * chunk), hi = min(n, lo + chunk);
+    auto size = [&](const FlatBlock &f, int64_t b) -> unsigned long long {
+        if (int64_t(f.src) != b) return 0ull;
+        return esc_rec_size(f.k_mode, f.k_nesc) + esc_rec_size(f.v_mode, f.v_nesc);
+    };
+    unsigned long long sum = 0;
+    for (int64_t b = lo; b < hi; ++b) sum += size(flat[b], b);
+    part[t] = sum;
+    __syncthreads();
+    for (int o = 1; o < T; o <<= 1) {  // inclusive scan
+        const unsigned long long v = t >= o ? part[t - o] : 0ull;
+        __syncthreads();
+        part[t] += v;
+        __syncthreads();
+    }
+    // A record that would end past `cap` gets offset 0 (every read of it stays inside an array of
+    // at least kEscRecHead + 65535 entries) and the step reports DERR_ESC_CAP.
+    unsigned long long c = part[t] - sum;
+    bool over = false;
+    for (int64_t b = lo; b < hi; ++b) {
+        FlatBlock &f = flat[b];
+        if (int64_t(f.src) != b) continue;
+        const uint32_t ks = esc_rec_size(f.k_mode, f.k_nesc), vs = esc_rec_size(f.v_mode, f.v_nesc);
+        over |= c + ks + vs > cap;
+        f.k_rec = c + ks > cap ? 0u : uint32_t(c);
+        f.v_rec = c + ks + vs > cap ? 0u : uint32_t(c + ks);
+        c += ks + vs;
+    }
+    if (over) report(status, KVX_ERR_INVALID_ARGUMENT, DERR_ESC_CAP);
+    if (t == T - 1) *total = part[T - 1];
+}
+
+__global__ void esc_dup_kernel(FlatBlock *flat, int64_t n) {
+    const int64_t b = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (b >= n) return;
+    const int64_t s = flat[b].src;
+    if (s != b) {
+        flat[b].k_rec = flat[s].k_rec;
+        flat[b].v_rec = flat[s].v_rec;
+    }
+}
+
+// One warp per (block, tensor): scan the residual codes for sentinels (all ones) in scan order,
+// write their element indices and the 16-token group counts.
+__global__ void esc_fill_kernel(const UnitDev *units, const FlatBlock *flat, int64_t n, int dim,
+                                uint16_t *esc, unsigned long long cap, int *status) {
+    const int64_t w = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (w >= 2 * n) return;
+    const int64_t b = w >> 1;
+    const int T = int(w & 1);
+    const FlatBlock f = flat[b];
+    if (int64_t(f.src) != b) return;
+    const int mode = T ? f.v_mode : f.k_mode;
+    const int nesc = T ? f.v_nesc : f.k_nesc;
+    if (mode == 0 || nesc == 0) return;
+    const unsigned long long rec = T ? f.v_rec : f.k_rec;
+    if (rec + kEscRecHead + unsigned(nesc) > cap) return;  // reported by esc_layout_kernel
+    const UnitDev &U = units[f.unit];
+    const uint8_t *blob = T ? U.v : U.k;
+    const uint32_t off = T ? f.v_off : f.k_off;
+    const int n_tok = f.n_tok;
+    const uint8_t *codes = blob + off + kHeaderBytes + dim + size_t(n_tok) * dim;
+    const uint32_t len = uint32_t(exp_payload_bytes(n_tok, dim, mode));
+    const uint32_t lead = uint32_t(reinterpret_cast<uintptr_t>(codes) & 3u);
+    const uint32_t *words = reinterpret_cast<const uint32_t *>(codes - lead);
+    const uint32_t nwords = (lead + len + 3) / 4;
+    const int per_byte = 8 / mode;  // residuals per code byte
+    uint16_t *pos = esc + rec + kEscRecHead;
+    int run = 0;
+    for (uint32_t w0 = 0; w0 < nwords; w0 += 32) {
+        const uint32_t wi = w0 + uint32_t(lane);
+        const uint32_t x = wi < nwords ? __ldg(words + wi) : 0u;
+        uint32_t mask = 0;  // bit k: residual k of this word (k = byte * per_byte + slot) is a sentinel
+#pragma unroll
+        for (int bb = 0; bb < 4; ++bb) {
+            const int64_t j = int64_t(wi) * 4 + bb - lead;  // code byte index in the section
+            if (j < 0 || j >= int64_t(len)) continue;
+            const uint32_t by = (x >> (8 * bb)) & 0xFFu;
+            if (mode == 4) {
+                if ((by & 0xFu) == 0xFu) mask |= 1u << (2 * bb);
+                if ((by >> 4) == 0xFu) mask |= 1u << (2 * bb + 1);
+            } else {
+#pragma unroll
+                for (int k = 0; k < 4; ++k)
+                    if (((by >> (2 * k)) & 3u) == 3u) mask |= 1u << (4 * bb + k);
+            }
+        }
+        const int cnt = __popc(mask);
+        int incl = cnt;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int v = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+            if (lane >= o) incl += v;
+        }
+        int idx = run + incl - cnt;
+        const int64_t e0 = (int64_t(wi) * 4 - lead) * per_byte;  // residual index of bit 0
+        while (mask != 0u) {
+            const int bit = __ffs(mask) - 1;
+            mask &= mask - 1u;
+            if (idx < nesc) pos[idx] = uint16_t(e0 + bit);
+            ++idx;
+        }
+        run += __shfl_sync(0xFFFFFFFFu, incl, 31);
+    }
+    if (run > nesc && lane == 0) report(status, KVX_ERR_RUNTIME, DERR_ESC_OVERRUN);
+    __syncwarp();
+    if (lane < 16) {
+        const int m = min(run, nesc);
+        const uint32_t limit = uint32_t(16 * (lane + 1)) * uint32_t(dim);
+        int lo = 0, hi = m;  // first position >= limit
+        while (lo < hi) {
+            const int mid = (lo + hi) >> 1;
+            if (uint32_t(pos[mid]) < limit) lo = mid + 1; else hi = mid;
+        }
+        esc[rec + lane] = uint16_t(lo);
+    }
+}
+
 }  // namespace
 
 cudaError_t launch_index_walk(const uint8_t *blob, uint64_t bytes, int dim, kvx_block *index,
@@ -487,12 +629,12 @@ cudaError_t launch_index_walk(const uint8_t *blob, uint64_t bytes, int dim, kvx_
     return cudaGetLastError();
 }
 
-cudaError_t launch_build_flat(const kvx_unit *units, const int64_t *block_begin, int n_units,
-                              int dim, int block_tokens, bool bf16, FlatBlock *flat,
-                              int32_t *flat_unit, int *status, cudaStream_t s) {
+cudaError_t launch_build_flat(const kvx_unit *units, const int64_t *block_begin,
+                              const int64_t *src_begin, int n_units, int dim, int block_tokens,
+                              bool bf16, FlatBlock *flat, int *status, cudaStream_t s) {
     if (n_units <= 0) return cudaSuccess;
-    build_flat_kernel<<<n_units, 256, 0, s>>>(units, block_begin, dim, block_tokens, bf16, flat,
-                                              flat_unit, status);
+    build_flat_kernel<<<n_units, 256, 0, s>>>(units, block_begin, src_begin, dim, block_tokens,
+                                              bf16, flat, status);
     return cudaGetLastError();
 }
 
@@ -547,6 +689,29 @@ cudaError_t launch_synth(uint16_t *out, int seq, int dim, uint64_t seed, uint64_
 cudaError_t launch_read_probe(const uint4 *buf, size_t n16, uint32_t *sink, int grid,
                               cudaStream_t s) {
     read_probe_kernel<<<grid, 512, 0, s>>>(buf, n16, sink);
+    return cudaGetLastError();
+}
+
+}  // namespace kvx
+
+namespace kvx {
+
+cudaError_t launch_esc_layout(FlatBlock *flat, int64_t n_blocks, unsigned long long *total,
+                              unsigned long long cap, int *status, cudaStream_t s) {
+    if (n_blocks <= 0) return cudaMemsetAsync(total, 0, sizeof *total, s);
+    esc_layout_kernel<<<1, 1024, 0, s>>>(flat, n_blocks, total, cap, status);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    esc_dup_kernel<<<unsigned((n_blocks + 255) / 256), 256, 0, s>>>(flat, n_blocks);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_esc_fill(const UnitDev *units, const FlatBlock *flat, int64_t n_blocks, int dim,
+                            uint16_t *esc, unsigned long long cap, int *status, cudaStream_t s) {
+    if (n_blocks <= 0) return cudaSuccess;
+    const int64_t warps = 2 * n_blocks;
+    esc_fill_kernel<<<unsigned((warps + 7) / 8), 256, 0, s>>>(units, flat, n_blocks, dim, esc, cap,
+                                                             status);
     return cudaGetLastError();
 }
 

@@ -18,10 +18,12 @@ cudaError_t launch_index_walk(const uint8_t *blob, uint64_t bytes, int dim, kvx_
                               uint32_t *tok_start, int cap, int *counts /*[2] blocks, tokens lo*/,
                               long long *n_tokens, int *status, cudaStream_t s);
 
-// Flatten units into FlatBlock entries (validates entries against blob sizes and seq).
-cudaError_t launch_build_flat(const kvx_unit *units, const int64_t *block_begin, int n_units,
-                              int dim, int block_tokens, bool bf16, FlatBlock *flat,
-                              int32_t *flat_unit, int *status, cudaStream_t s);
+// Flatten units into FlatBlock entries (validates entries against blob sizes and seq).  Unit u's
+// blocks start at flat index block_begin[u]; src_begin[u] (NULL: block_begin) is the flat index
+// of the first block of the unit whose K/V blocks -- and escape records -- they are.
+cudaError_t launch_build_flat(const kvx_unit *units, const int64_t *block_begin,
+                              const int64_t *src_begin, int n_units, int dim, int block_tokens,
+                              bool bf16, FlatBlock *flat, int *status, cudaStream_t s);
 
 // Decode blocks [0, n_blocks) of a blob into [seq, dim] BF16 (out rows beyond seq untouched).
 cudaError_t launch_decode(const uint8_t *blob, const kvx_block *index, const uint32_t *tok_start,

@@ -31,6 +31,7 @@ enum DeviceError : int {
     DERR_TIMEOUT = 9,       // bounded mbarrier wait expired
     DERR_INDEX_CAP = 10,    // more blocks than the index capacity
     DERR_RANGE = 11,        // an index entry points outside its blob
+    DERR_ESC_CAP = 12,      // escape records do not fit the fixed scratch
 };
 
 __host__ __device__ inline int exp_payload_bytes(int n_tokens, int dim, int bits) {

@@ -117,6 +117,7 @@ _synth = _sig("kvx_synth_bf16", C.c_int,
 _probe = _sig("kvx_hbm_read_probe", C.c_int, [_vp, _sz, C.c_int, C.POINTER(C.c_double)])
 _noalloc = _sig("kvx_attention_decode_noalloc", C.c_int,
                 [_vp, _vp, _sz, _vp, _vp, _sz, _vp, C.c_int, _vp, C.c_int, C.c_int, C.c_int, _vp])
+_fold = _sig("kvx_fold_shards", C.c_int, [_vp, C.c_int, C.c_int, C.c_int, _vp, _vp, _vp])
 
 # Every symbol the C header declares, for load/export checks.
 EXPORTED = [
@@ -124,7 +125,7 @@ EXPORTED = [
     "kvx_attention_decode_units", "kvx_encode_bound", "kvx_encode_bf16", "kvx_decode_bf16",
     "kvx_xkv_index", "kvx_plan_create", "kvx_plan_run", "kvx_plan_run_part", "kvx_plan_check", "kvx_plan_launches",
     "kvx_plan_destroy", "kvx_encode_batch_bounds", "kvx_encode_batch", "kvx_cache_append",
-    "kvx_synth_bf16", "kvx_hbm_read_probe", "kvx_attention_decode_noalloc",
+    "kvx_synth_bf16", "kvx_hbm_read_probe", "kvx_attention_decode_noalloc", "kvx_fold_shards",
 ]
 
 
@@ -245,6 +246,13 @@ def attention_decode_noalloc(q, k_xkv, k_bytes, k_index, v_xkv, v_bytes, v_index
     _check(_noalloc(_addr(q), _addr(k_xkv), int(k_bytes), _addr(k_index), _addr(v_xkv),
                     int(v_bytes), _addr(v_index), int(n_blocks), _addr(out), int(n_q), int(dim),
                     int(seq), _addr(stream)))
+
+
+def fold_shards(parts, n_parts, n_rows, dim, out, lse_out=None, stream=None):
+    """Rank-ordered fold of sequence-shard results on the GPU (kvx_fold_shards): parts holds
+    n_parts blocks of [n_rows * dim outputs, n_rows lse] FP32; asynchronous on `stream`."""
+    _check(_fold(_addr(parts), int(n_parts), int(n_rows), int(dim), _addr(out), _addr(lse_out),
+                 stream))
 
 
 class Plan:

@@ -8,7 +8,10 @@ query, its normalised output o_r and the log of its softmax normaliser lse_r = m
     M = max_r lse_r,  w_r = exp(lse_r - M),  o = sum_r w_r o_r / sum_r w_r
 
 in rank order.  The exchange is one all-gather of (o, lse): U x G x (D + 1) floats per rank,
-33 KB for config[4] -- the only collective on the data path.
+33 KB for config[4] -- the only collective on the data path.  On the GPU, ShardExchange lays
+each rank's outputs and lse out in one buffer so that the exchange is a single NCCL all-gather,
+and folds the gathered parts with one kernel (kvx_fold_shards); fold() is the same arithmetic in
+torch, for CPU ranks and as the check.
 """
 from __future__ import annotations
 
@@ -43,3 +46,44 @@ def gather_fold(out, lse, group=None):
     dist.all_gather(outs, out.contiguous(), group=group)
     dist.all_gather(lses, lse.contiguous(), group=group)
     return fold(torch.stack(outs), torch.stack(lses))
+
+
+class ShardExchange:
+    """The exchange step of a sequence split on the GPU.
+
+    `pack` holds this rank's results as kvx_fold_shards expects them: outputs [rows, dim] then
+    lse [rows], rows = units x queries; point the plan's kvx_unit.out / .lse at `out_view()` /
+    `lse_view()`.  step() all-gathers every rank's pack over NCCL (one collective, on the current
+    stream) and folds the parts in rank order into `out` [rows, dim] and `lse` [rows].
+    """
+
+    def __init__(self, rows: int, dim: int, group=None, device="cuda"):
+        import torch
+        import torch.distributed as dist
+        self.rows, self.dim, self.group = rows, dim, group
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        n = rows * dim + rows
+        self.pack = torch.zeros(n, dtype=torch.float32, device=device)
+        self.gathered = torch.zeros(self.world * n, dtype=torch.float32, device=device)
+        self.out = torch.zeros((rows, dim), dtype=torch.float32, device=device)
+        self.lse = torch.zeros(rows, dtype=torch.float32, device=device)
+
+    def out_view(self):
+        return self.pack[: self.rows * self.dim].view(self.rows, self.dim)
+
+    def lse_view(self):
+        return self.pack[self.rows * self.dim:]
+
+    @property
+    def bytes_per_rank(self) -> int:
+        return self.pack.numel() * 4
+
+    def step(self, stream=None):
+        import torch.distributed as dist
+        import kvexp_b200 as kvx
+        if self.world > 1:
+            dist.all_gather_into_tensor(self.gathered, self.pack, group=self.group)
+            parts = self.gathered
+        else:
+            parts = self.pack
+        kvx.fold_shards(parts, self.world, self.rows, self.dim, self.out, self.lse, stream)

@@ -28,6 +28,10 @@ class Config:
     v_profile: int = S.PROFILE_V
     layer0_k_profile: int | None = None
     block: int = 128
+    # How N GPUs share the workload: "replica" (each GPU its own full cache), "units" (the
+    # (layer, KV head, sequence) units split over 8 GPU slots) or "sequence" (every KV head's
+    # sequence cut into block-aligned shards, folded by log-sum-exp).
+    shard: str = "replica"
 
     @property
     def units(self) -> int:
@@ -45,9 +49,9 @@ CONFIGS = {
     2: Config("config[2]: config[1] shape at S32731 (91-token tail block)", 24, 2, 7, 64, 32731,
               layer0_k_profile=S.PROFILE_NARROW),
     3: Config("config[3]: 32L x 8KV x GQA4 x D128 x 64 seqs x S32768 (Llama-3-8B shape)", 32, 8,
-              4, 128, 32768, seqs=64),
+              4, 128, 32768, seqs=64, shard="units"),
     4: Config("config[4]: 1L x 8KV x GQA4 x D256 x S1048576", 1, 8, 4, 256, 1 << 20,
-              k_profile=S.PROFILE_WIDE_K, v_profile=S.PROFILE_WIDE_V),
+              k_profile=S.PROFILE_WIDE_K, v_profile=S.PROFILE_WIDE_V, shard="sequence"),
 }
 
 
@@ -79,8 +83,11 @@ class DeviceCache:
     def compressed_bytes(self) -> int:
         return int(sum(b for _, _, b in self.k) + sum(b for _, _, b in self.v))
 
-    def kvx_units(self):
+    def kvx_units(self, out=None, lse=None):
+        """kvx_unit descriptors of every unit; outputs go to self.out unless `out` ([U, G, D]
+        FP32) is given; `lse` ([U, G] FP32) optionally receives each query's log-sum-exp."""
         import kvexp_b200 as kvx
+        out = self.out if out is None else out
         units = []
         for i in range(len(self.unit_ids)):
             ka, ko, kb = self.k[i]
@@ -89,8 +96,8 @@ class DeviceCache:
             vidx = self._index_of(va, i, 1)
             units.append(kvx.kvx_unit(
                 self.arenas[ka].data_ptr() + ko, self.arenas[va].data_ptr() + vo,
-                kidx, vidx, self.q[i].data_ptr(), self.out[i].data_ptr(), kb, vb,
-                self.nb_per, self.cfg.seq))
+                kidx, vidx, self.q[i].data_ptr(), out[i].data_ptr(), kb, vb,
+                self.nb_per, self.cfg.seq, None if lse is None else lse[i].data_ptr()))
         return units
 
     def _index_of(self, arena_idx, i, kind):
@@ -99,12 +106,15 @@ class DeviceCache:
         base = self.indexes[arena_idx].data_ptr()
         return base + (2 * local + kind) * self.nb_per * 8
 
-    def host_blobs(self):
-        """Host copies (numpy) of every unit's K and V blobs, and the queries."""
-        host = [a.cpu().numpy() for a in self.arenas]
-        ks = [host[a][o:o + b].copy() for a, o, b in self.k]
-        vs = [host[a][o:o + b].copy() for a, o, b in self.v]
-        qs = [self.q[i].cpu().numpy().view(np.uint16).copy() for i in range(len(self.unit_ids))]
+    def host_blobs(self, units=None):
+        """Host copies (numpy) of the K and V blobs and queries of `units` (local positions;
+        default all)."""
+        units = range(len(self.unit_ids)) if units is None else units
+        ks = [self.arenas[self.k[i][0]][self.k[i][1]:self.k[i][1] + self.k[i][2]].cpu().numpy()
+              for i in units]
+        vs = [self.arenas[self.v[i][0]][self.v[i][1]:self.v[i][1] + self.v[i][2]].cpu().numpy()
+              for i in units]
+        qs = [self.q[i].cpu().numpy().view(np.uint16).copy() for i in units]
         return qs, ks, vs
 
 

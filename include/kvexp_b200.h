@@ -162,6 +162,19 @@ KVX_API int kvx_cache_append(const uint16_t *kv_new, int n_new, int head_dim, in
                      uint8_t *blob, size_t at, size_t capacity, kvx_block *index,
                      size_t *bytes_written, int *blocks_written, void *stream);
 
+/* Fold the results of a sequence split (one shard per rank, in rank order) into the result over
+ * the whole sequence.  Per row (unit, query): M = max_r lse_r, w_r = exp(lse_r - M),
+ * out = (sum_r w_r o_r) * (1 / sum_r w_r), summed in rank order -- the reference's fold of its
+ * thread ranges (src/dispatch.cpp:98-103: merge_state, src/softmax.hpp:16-30, then
+ * finalize_state, :32-41) applied to normalised shard outputs.  parts: device memory, n_parts
+ * consecutive parts of n_rows * dim + n_rows FP32 each: the shard's outputs [n_rows, dim] (the
+ * kvx_unit.out rows of its units, back to back) followed by their lse [n_rows] (kvx_unit.lse),
+ * which is what an all-gather of one such buffer per rank yields.  A part whose lse is -inf (an
+ * empty shard) contributes nothing.  out [n_rows, dim] FP32; lse_out [n_rows] (optional) gets the
+ * lse of the whole sequence.  Asynchronous on `stream`. */
+KVX_API int kvx_fold_shards(const float *parts, int n_parts, int n_rows, int dim, float *out,
+                            float *lse_out, void *stream);
+
 /* Decode attention that allocates no GPU memory.  No counterpart in the reference: it exists for
  * callers that cannot allocate while they run, such as serving engines that reserve the
  * device's memory for their KV-cache pool at start-up and treat a later cudaMalloc as a failure,

@@ -123,3 +123,91 @@ def test_sequence_split_fold_matches_whole(kvx, cuda, oracle, dim, n_q, seq, wor
     cpu = oracle.attention(q, kx=oracle.encode(k, 128), vx=oracle.encode(v, 128), seq=seq)
     assert_attention_close(folded, cpu, attn_scale(q, k, v), f"fold world={world}", seq=seq)
     assert_attention_close(whole.cpu().numpy(), cpu, attn_scale(q, k, v), "whole", seq=seq)
+
+
+@pytest.mark.parametrize("n_parts,rows,dim", [(1, 3, 64), (2, 32, 256), (8, 32, 256),
+                                              (5, 7, 40), (3, 200, 128)])
+def test_fold_kernel_matches_rank_order_fold(kvx, cuda, n_parts, rows, dim):
+    """kvx_fold_shards against seqsplit.fold (float64), with an empty shard (lse -inf, outputs
+    NaN) among the parts when there are three or more."""
+    import torch
+    gen = torch.Generator().manual_seed(1000 * n_parts + rows)
+    outs = torch.randn(n_parts, rows, dim, generator=gen).float()
+    lses = (torch.randn(n_parts, rows, generator=gen) * 20).float()
+    if n_parts >= 3:
+        lses[1] = float("-inf")
+        outs[1] = float("nan")
+    parts = torch.cat([outs.reshape(n_parts, -1), lses], dim=1).contiguous().cuda()
+    out = torch.full((rows, dim), float("nan"), device="cuda")
+    lse = torch.full((rows,), float("nan"), device="cuda")
+    kvx.fold_shards(parts, n_parts, rows, dim, out, lse)
+    torch.cuda.synchronize()
+    clean = torch.where(torch.isnan(outs), torch.zeros_like(outs), outs).double()
+    want = seqsplit.fold(clean, lses.double())
+    scale = clean.abs().amax()
+    assert torch.max(torch.abs(out.cpu().double() - want)) <= 2e-6 * scale
+    m = lses.double().amax(0)
+    want_lse = m + torch.log(torch.exp(lses.double() - m).sum(0))
+    assert torch.allclose(lse.cpu().double(), want_lse, rtol=1e-6, atol=1e-5)
+
+
+def _nccl_rank(rank, world, port, rows, dim, result):
+    import datetime
+    import os
+
+    import torch
+    import torch.distributed as dist
+    torch.cuda.set_device(rank)
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    try:
+        gen = torch.Generator().manual_seed(77 + rank)
+        exch = seqsplit.ShardExchange(rows, dim)
+        exch.out_view().copy_(torch.randn(rows, dim, generator=gen))
+        exch.lse_view().copy_(torch.randn(rows, generator=gen) * 10)
+        exch.step()
+        torch.cuda.synchronize()
+        result[rank] = (exch.out.cpu().numpy(), exch.lse.cpu().numpy())
+    finally:
+        dist.destroy_process_group()
+
+
+def test_shard_exchange_over_nccl(cuda):
+    """Two ranks on two GPUs: one NCCL all-gather + the fold kernel give every rank the fold of
+    both ranks' parts.  Runs only where the box has two GPUs."""
+    import socket
+
+    import torch
+    import torch.multiprocessing as mp
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    world, rows, dim = 2, 32, 256
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    result = mp.Manager().dict()
+    ctx = mp.get_context("spawn")
+    procs = [ctx.Process(target=_nccl_rank, args=(r, world, port, rows, dim, result))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(180)
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+        assert p.exitcode == 0
+    outs, lses = [], []
+    for r in range(world):
+        gen = torch.Generator().manual_seed(77 + r)
+        outs.append(torch.randn(rows, dim, generator=gen).double())
+        lses.append((torch.randn(rows, generator=gen) * 10).float().double())
+    want = seqsplit.fold(torch.stack(outs).float().double(), torch.stack(lses))
+    for r in range(world):
+        got = torch.from_numpy(result[r][0]).double()
+        assert torch.max(torch.abs(got - want)) <= 2e-6 * want.abs().amax()
+    assert np.array_equal(result[0][0], result[1][0])
