@@ -5,38 +5,36 @@
 // for the GPU:
 //
 //  * The step's (unit, block) pairs are flattened; each worker warp owns a contiguous range and
-//    streams stages of TS tokens of K and V through its own shared-memory ring with cp.async, one
-//    cp.async group per stage: sign/mantissa rows, packed exponent residuals, and the stage's
-//    escape words with their element positions -- or raw BF16 rows.  A block's base exponents ride
-//    along with its first stage.  Only the compressed bytes cross HBM (plus, for a coded block
-//    with escapes, its escape record: 2 bytes per escape word and a 32-byte count header, built
-//    once per plan), and no warp ever waits on another warp.
-//  * K rows are rebuilt straight into mma.sync A fragments: lane (g, t) rebuilds tokens g and g+8,
-//    head dims [t D/4, (t+1) D/4).  The MMA's k index runs over the head dims in that permuted
-//    order and the query B fragments use the same order, so S = K Q^T (tokens x queries, fp32
-//    accumulate) needs no BF16 tile in shared memory.  A pair of elements costs four instructions:
-//    two byte permutes (sign/mantissa bytes; exponent residuals), one multiply-add that adds the
-//    residual to the base exponent, and one bit-select.  A block's sections start 0 or 2 bytes
-//    past a 4-byte boundary of the ring (every size and offset in an XKV blob is even); the
-//    permutes take that shift in their selectors.
-//  * The online softmax runs on the S fragments of a whole stage: lane (g, t) holds queries 2t and
-//    2t+1, which are also the output columns it accumulates, so the rescale factors never leave
-//    the lane.
-//  * V rows are rebuilt into A fragments of V^T: lane (g, t) rebuilds tokens 2t, 2t+1, 2t+8, 2t+9,
-//    head dims [g D/8, (g+1) D/8).  O^T += V^T P^T with P^T split into a bf16 part and a bf16
-//    residual part (two MMAs), so P enters with 16 significant bits.
-//  * Exponent escapes: a row half whose tokens hold escape words goes to scratch, each escape word
-//    is stored over its element (one 16-bit store, at the position the block's escape record
-//    gives) and the half is read back.  Halves without escapes skip all of it.
+//    streams stages of TS tokens of K and V through its own shared-memory ring: sign/mantissa
+//    rows, packed exponent residuals, and the stage's escape words with their tile slots -- or raw
+//    BF16 rows.  The pieces arrive as 1-D bulk copies of the TMA engine, issued in parallel by
+//    ten lanes and completing on the ring slot's mbarrier.  A block's base exponents ride along
+//    with its first stage.  Only the compressed bytes cross HBM (plus, for a coded block with
+//    escapes, its escape record: 2 bytes per escape word and a 32-byte count header, built once
+//    per plan), and no warp ever waits on another warp.
+//  * Each lane rebuilds 8-element chunks of a stage's rows into BF16 words and stores them, 16
+//    bytes at a time, into the warp's tile: TS rows of D BF16 values with 16-byte chunks swizzled
+//    so that neither those stores nor the ldmatrix reads of the MMA conflict on shared-memory
+//    banks.  A pair of elements costs four instructions: two byte permutes (sign/mantissa bytes;
+//    exponent residuals), one multiply-add that adds the residual to the base exponent, and one
+//    bit-select.  A block's sections start 0 or 2 bytes past a 4-byte boundary of the ring (every
+//    size and offset in an XKV blob is even); the permutes take that shift in their selectors.
+//  * Escape words are stored over their elements of the tile: one 16-bit store each, at the slot
+//    the block's escape record gives.
+//  * S = K Q^T runs on the tensor cores (mma.sync m16n8k16, tokens x queries, fp32 accumulate)
+//    with K fragments from ldmatrix; the online softmax runs on the S fragments of a whole stage:
+//    lane (g, t) holds queries 2t and 2t+1, which are also the output columns it accumulates, so
+//    the rescale factors never leave the lane.  O^T += V^T P^T reads V^T with ldmatrix.trans; P^T
+//    enters split into a bf16 part and a bf16 residual part (two MMAs), with 16 significant bits.
 //  * Unit segments that span several workers leave (m, l, acc) partial states that combine_kernel
 //    folds in worker order with merge_state semantics (src/softmax.hpp:16-30), then finalizes like
 //    finalize_state (src/softmax.hpp:32-41: reciprocal, then multiply).
 //
-// The BF16-input variant (BF16IN) is the same template reading [seq, dim] BF16 rows; for the same
-// blocks and worker ranges it produces bit-identical outputs to the XKV variant, because both
-// rebuild identical BF16 fragments and run identical arithmetic afterwards.  (Ranges are one block
-// per worker whenever the step has no more blocks than workers; beyond that they are balanced by
-// cost.)
+// The BF16-input variant (BF16IN) is the same template reading [seq, dim] BF16 rows into the same
+// tile; for the same blocks and worker ranges it produces bit-identical outputs to the XKV variant,
+// because the tensor cores see identical BF16 tiles and everything after them is the same code.
+// (Ranges are one block per worker whenever the step has no more blocks than workers; beyond
+// that they are balanced by cost.)
 #include "attention.cuh"
 
 namespace kvx {
@@ -62,15 +60,13 @@ __host__ __device__ constexpr int cmax(int a, int b) { return a > b ? a : b; }
 #endif
 
 template <int D> struct Cfg {
-    static constexpr int DK = D / 4;        // head dims per lane in a K row
-    static constexpr int NK = D / 8;        // K fragment registers per row (dim pairs)
-    static constexpr int DV = D / 8;        // head dims per lane in a V token (= V registers)
-    static constexpr int KS = D / 16;       // k-steps of QK = M-tiles of PV
-    static constexpr bool SPLIT = D > 128;  // rebuild and multiply row halves one at a time
+    static constexpr int KS = D / 16;             // k-steps of QK = M-tiles of PV
     static constexpr int TS = D <= 64 ? 32 : 16;  // tokens per ring stage
     static constexpr int SUBS = TS / TT;          // MMA tiles per stage
-    // One tensor's stage: sign/mantissa rows | residual codes | escape words | their positions,
-    // or TS raw BF16 rows -- both fit 2 TS D bytes (escapes beyond ESC_CAP stay in HBM).
+    static constexpr int C8 = D / 8;              // 8-element chunks per row
+    static constexpr int NIT = TS * C8 / 32;      // chunk steps of a lane per stage and tensor
+    // One tensor's stage: sign/mantissa rows | residual codes | escape words | their slots, or
+    // TS raw BF16 rows -- both fit 2 TS D bytes (escapes beyond ESC_CAP stay in HBM).
     static constexpr int ESC_CAP = TS * D / 8;
     static constexpr int CODE_OFF = TS * D + 16;
     static constexpr int EV_OFF = CODE_OFF + TS * D / 2 + 16;
@@ -78,20 +74,21 @@ template <int D> struct Cfg {
     static constexpr int TR = round16(cmax(EP_OFF + 2 * ESC_CAP + 16, TS * 2 * D + 16));
     static constexpr int SLOT = 2 * TR;  // K stage | V stage
     static constexpr int NSTAGE = D <= 32 ? 3 : 2;
-    static_assert(NSTAGE >= 2 && NSTAGE <= 4, "stage waits cover at most 3 younger groups");
     static constexpr int BASE = round16(D + 32);  // one block's base exponents (+ alignment slack)
     // Per-block meta slot: K base | V base | the block's FlatBlock | its escape count headers.
     static constexpr int M_FB = 2 * BASE;
     static constexpr int M_EM = M_FB + 32;
     static constexpr int MSLOT = M_EM + 64;
-    static constexpr int SCR = 16 * D;            // escape scratch: one row half of fragments
-    static constexpr int W_META = NSTAGE * SLOT;  // per-warp region: ring | meta x2 | scratch
-    static constexpr int W_SCR = W_META + 2 * MSLOT;
-    static constexpr int WARP_BYTES = (W_SCR + SCR + 127) & ~127;
-    // Register budget 65536 / (32 WARPS): 12 warps leave 168 per thread, 10 leave 204.
-    static constexpr int MAXW = D <= 32 ? 16 : D <= 64 ? KVX_MAXWARPS : 10;
+    static constexpr int XB = TS * 2 * D;  // the BF16 tile of one tensor's stage
+    // per-warp region: ring | meta x2 | tile | one mbarrier per ring slot
+    static constexpr int W_META = NSTAGE * SLOT;
+    static constexpr int W_XB = W_META + 2 * MSLOT;
+    static constexpr int W_BAR = W_XB + XB;
+    static constexpr int WARP_BYTES = (W_BAR + 8 * NSTAGE + 127) & ~127;
+    static constexpr int MAXW = D <= 32 ? 16 : KVX_MAXWARPS;
     static constexpr int WARPS = cmin(MAXW, 232448 / WARP_BYTES);
     static_assert(WARPS >= 1, "worker does not fit in shared memory");
+    static_assert(32 % C8 == 0 && NIT >= 1, "a warp step covers whole rows");
 };
 
 // ---- copies ------------------------------------------------------------------------------------
@@ -109,37 +106,12 @@ __device__ __forceinline__ Piece make_piece(const uint8_t *p, uint32_t len) {
     return Piece{reinterpret_cast<const uint8_t *>(lo), uint32_t(hi - lo), uint32_t(a - lo)};
 }
 
-// No "memory" clobber: a clobber would pin every address-taken local in memory around each copy.
-// Ordering against this warp's own shared-memory reads comes from __syncwarp() before a slot is
-// refilled and from the clobber on cp_async_wait() before it is read.
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src));
-}
-// One cp.async group per ring stage; a consumer waits until at most `younger` groups issued after
-// the stage it needs are still in flight.  These waits end by themselves: they wait for this
-// thread's own copies only.
-__device__ __forceinline__ void cp_async_commit() {
-    asm volatile("cp.async.commit_group;" ::: "memory");
-}
-__device__ __forceinline__ void cp_async_wait(int younger) {
-    switch (younger) {
-    case 0: asm volatile("cp.async.wait_group 0;" ::: "memory"); break;
-    case 1: asm volatile("cp.async.wait_group 1;" ::: "memory"); break;
-    case 2: asm volatile("cp.async.wait_group 2;" ::: "memory"); break;
-    default: asm volatile("cp.async.wait_group 3;" ::: "memory"); break;
-    }
-}
-// The warp copies one piece of at most MAXB bytes: lane l moves 16-byte chunks l, l + 32, ...
-template <int MAXB>
-__device__ __forceinline__ void copy_piece(uint8_t *dst, const Piece p, int lane) {
-    constexpr int MAXC = (MAXB / 16 + 31) / 32;
-    const uint32_t n = p.alloc >> 4;
-    const uint32_t d = smem_u32(dst) + 16u * uint32_t(lane);
-    const uint8_t *src = p.src + 16 * lane;
-#pragma unroll
-    for (int k = 0; k < MAXC; ++k)
-        if (uint32_t(lane + 32 * k) < n) cp_async16(d + 512u * k, src + 512 * k);
-}
+// Stages arrive through the TMA engine: one 1-D bulk copy per piece (16-byte aligned source,
+// destination and size), each completing its byte count on the ring slot's mbarrier; the
+// consumer waits on the barrier's phase for that use of the slot.
+
+// Longest a warp waits for one stage before it reports DERR_TIMEOUT and stops (microseconds).
+constexpr uint32_t kStageWaitUs = 1000000;
 
 // Section pointers of one tensor of one block.
 struct Sections {
@@ -209,11 +181,8 @@ __host__ __device__ constexpr uint32_t shift4(uint32_t o) {  // bytes o .. o+3
 __host__ __device__ constexpr uint32_t sel_code(int j) {  // byte j of A -> bytes 0, 1; of B -> 2, 3
     return uint32_t(j) | (uint32_t(j) << 4) | (uint32_t(4 + j) << 8) | (uint32_t(4 + j) << 12);
 }
-__host__ __device__ constexpr uint32_t sel_cross(int b) {  // byte b of A -> 0, 1; of B -> 2, 3
-    return uint32_t(b) | (uint32_t(b) << 4) | (uint32_t(4 + b) << 8) | (uint32_t(4 + b) << 12);
-}
 
-// Two BF16 values from sign/mantissa bytes (byte 0 and 1 of each half hold the element's byte:
+// Two BF16 values from sign/mantissa bytes (bytes 0 and 1 of each half hold the element's byte:
 // bits 0-6 give the mantissa, bit 15 the sign) and exponent residuals in bytes 0 and 2 of cw.
 // Exponent = base + residual modulo 256 like bf16_from_delta's uint8 sum (reference
 // include/kvexp/bf16.hpp:35-37).  Bytes 1 and 3 of cw may hold other residuals (< 16): times 128
@@ -222,394 +191,184 @@ __device__ __forceinline__ uint32_t merge(uint32_t sg, uint32_t cw, uint32_t b7)
     return (sg & 0x807F807Fu) | ((cw * 128u + b7) & 0x7F807F80u);
 }
 
-// How this lane reads one tensor of the current block from a ring stage.  Row sections start
-// m = 0 or 2 bytes past a 4-byte boundary; the lane's columns add a multiple of 4 to the sign/
-// mantissa and raw rows, and any byte count to the residual rows.
+// How this lane reads one tensor of the current block from a ring stage: the 8-element chunk c8
+// (head dims 8 c8 .. 8 c8 + 7) of rows t0 + RPI k.  Row sections start m = 0 or 2 bytes past a
+// 4-byte boundary of the ring; the chunk adds a multiple of 4 to the sign/mantissa and raw rows,
+// and 4 (4-bit) or 2 (2-bit) bytes per chunk to the residual rows.
 struct Lay {
     uint32_t p0, p1;  // sign/mantissa bytes of element pairs 2q and 2q+1 from words q, q+1
-    uint32_t w;       // one realigned word from two loaded ones (sign/mantissa, raw rows)
+    uint32_t w;       // one realigned word from two loaded ones (raw rows)
     uint32_t cs;      // one realigned word of residual codes
-    int rows;         // byte offset of the lane's row window in the stage (4-aligned)
-    int codes;        // byte offset of the lane's residual window in the stage (4-aligned)
+    uint32_t rows;    // byte offset of the lane's row window in the stage (4-aligned)
+    uint32_t codes;   // byte offset of the lane's residual window in the stage (4-aligned)
 };
-// rd / cd: data offsets of the block's row and code pieces; col: the lane's first head dim.
+// rd / cd: data offsets of the block's row and code pieces.
 template <int D>
-__device__ __forceinline__ Lay make_lay(uint32_t rd, uint32_t cd, int mode, int col, bool bf16) {
+__device__ __forceinline__ Lay make_lay(uint32_t rd, uint32_t cd, int mode, int c8, bool bf16) {
     Lay l;
     const uint32_t m = rd & 3u;
     l.p0 = rep2(m);
     l.p1 = rep2(m + 2);
     l.w = shift4(m);
-    const int rcol = (bf16 || mode == 0) ? 2 * col : col;
-    l.rows = int(rd & ~3u) + rcol;
-    const uint32_t cb = (cd & 3u) + uint32_t(col * (mode == 0 ? 0 : mode) / 8);
+    l.rows = (rd & ~3u) + uint32_t((bf16 || mode == 0) ? 16 * c8 : 8 * c8);
+    const uint32_t cb = (cd & 3u) + uint32_t(c8 * (mode == 0 ? 0 : mode));
     l.cs = shift4(cb & 3u);
-    l.codes = Cfg<D>::CODE_OFF + int(cd & ~3u) + int(cb & ~3u);
+    l.codes = uint32_t(Cfg<D>::CODE_OFF) + (cd & ~3u) + (cb & ~3u);
     return l;
 }
 
-// b7 of a K register (dims d, d+1): base[d] << 7 | base[d+1] << 23.  `base` points at the
-// block's staged base exponents (data offset applied), the lane's first dim c0.
-template <int D>
-__device__ __forceinline__ void load_b7k(const uint8_t *base, uint32_t (&b7)[Cfg<D>::NK]) {
-    constexpr int NB = Cfg<D>::DK / 4;
-    const uint32_t m = uint32_t(reinterpret_cast<uintptr_t>(base)) & 3u;
-    const uint32_t *q = reinterpret_cast<const uint32_t *>(base - m);
-    uint32_t B[NB + 1];
-#pragma unroll
-    for (int i = 0; i <= NB; ++i) B[i] = q[i];
+// b7 of the lane's four dim pairs (c, c+1): base[c] << 7 | base[c+1] << 23.  `base` is the
+// shared address of base[8 c8].
+__device__ __forceinline__ void load_b7(uint32_t base, uint32_t (&b7)[4]) {
+    const uint32_t m = base & 3u, q = base - m;
+    const uint32_t B0 = lds_u32(q), B1 = lds_u32(q + 4u), B2 = lds_u32(q + 8u);
     const uint32_t s0 = rep2(m), s1 = rep2(m + 2);
-#pragma unroll
-    for (int p = 0; p < Cfg<D>::NK; ++p)
-        b7[p] = (prmt(B[p >> 1], B[(p >> 1) + 1], (p & 1) ? s1 : s0) & 0x00FF00FFu) << 7;
-}
-// b7 of a V register (one dim, two tokens): base[d] << 7 | base[d] << 23.
-template <int D>
-__device__ __forceinline__ void load_b7v(const uint8_t *base, uint32_t (&b7)[Cfg<D>::DV]) {
-    constexpr int NB = Cfg<D>::DV / 4;
-    const uint32_t m = uint32_t(reinterpret_cast<uintptr_t>(base)) & 3u;
-    const uint32_t *q = reinterpret_cast<const uint32_t *>(base - m);
-    uint32_t B[NB + 1];
-#pragma unroll
-    for (int i = 0; i <= NB; ++i) B[i] = q[i];
-    const uint32_t sw = shift4(m);
-#pragma unroll
-    for (int e = 0; e < Cfg<D>::DV; ++e) {
-        const uint32_t w = prmt(B[e >> 2], B[(e >> 2) + 1], sw);
-        b7[e] = (prmt(w, 0u, uint32_t(e & 3) * 0x1111u) & 0x00FF00FFu) << 7;
-    }
+    b7[0] = (prmt(B0, B1, s0) & 0x00FF00FFu) << 7;
+    b7[1] = (prmt(B0, B1, s1) & 0x00FF00FFu) << 7;
+    b7[2] = (prmt(B1, B2, s0) & 0x00FF00FFu) << 7;
+    b7[3] = (prmt(B1, B2, s1) & 0x00FF00FFu) << 7;
 }
 
-// ---- row rebuild -------------------------------------------------------------------------------
+// Byte offset of 16-byte chunk c8 of tile row t: rows of 2 D bytes, chunks XOR-swizzled by the
+// row so that eight rows read at one chunk position (ldmatrix) and eight chunks of a row written
+// by eight lanes (decode) fall on distinct banks.
+template <int D> __device__ __forceinline__ uint32_t xb_off(int t, int c8) {
+    return uint32_t(t * (2 * D)) + (uint32_t(c8 ^ (D == 32 ? (t >> 1) & 3 : t & 7)) << 4);
+}
 
-// One K row of this lane (token r of the stage, dims c0 .. c0 + DK - 1).  MODE 4 / 2: coded,
-// 0: raw BF16 rows.
+// ---- stage decode ------------------------------------------------------------------------------
+
+// Rebuild this lane's chunks of one tensor's stage into the tile (MODE 4 / 2 coded, 0 raw BF16).
+// Rows at or past `zero_from` are stored as zeros (V: P is 0 there, V must be finite).
 template <int D, int MODE>
-__device__ __forceinline__ void k_row(const uint8_t *stage, const Lay &ly, int r,
-                                      const uint32_t (&b7)[Cfg<D>::NK], uint32_t (&o)[Cfg<D>::NK]) {
+__device__ __forceinline__ void decode_stage(uint32_t stage, uint32_t xb, const Lay &ly,
+                                             const uint32_t (&b7)[4], int lane, int zero_from) {
     using C = Cfg<D>;
-    if constexpr (MODE == 0) {
-        const uint32_t *q = reinterpret_cast<const uint32_t *>(stage + ly.rows + r * (2 * D));
-        uint32_t W[C::NK + 1];
-#pragma unroll
-        for (int i = 0; i <= C::NK; ++i) W[i] = q[i];
-#pragma unroll
-        for (int p = 0; p < C::NK; ++p) o[p] = prmt(W[p], W[p + 1], ly.w);
-    } else {
-        constexpr int NS = C::DK / 4;
-        const uint32_t *qs = reinterpret_cast<const uint32_t *>(stage + ly.rows + r * D);
-        uint32_t W[NS + 1];
-#pragma unroll
-        for (int i = 0; i <= NS; ++i) W[i] = qs[i];
-        const uint32_t *qc = reinterpret_cast<const uint32_t *>(stage + ly.codes + r * (D * MODE / 8));
-        if constexpr (MODE == 4) {
-            constexpr int NC = C::DK / 8;  // words of 8 residuals
-            uint32_t X[NC + 1], lo[NC], hi[NC];
-#pragma unroll
-            for (int i = 0; i <= NC; ++i) X[i] = qc[i];
-#pragma unroll
-            for (int k = 0; k < NC; ++k) {
-                const uint32_t x = prmt(X[k], X[k + 1], ly.cs);
-                lo[k] = x & 0x0F0F0F0Fu;
-                hi[k] = (x >> 4) & 0x0F0F0F0Fu;
-            }
-#pragma unroll
-            for (int p = 0; p < C::NK; ++p)
-                o[p] = merge(prmt(W[p >> 1], W[(p >> 1) + 1], (p & 1) ? ly.p1 : ly.p0),
-                             prmt(lo[p >> 2], hi[p >> 2], sel_code(p & 3)), b7[p]);
+    constexpr int RPI = 32 / C::C8;  // rows per chunk step
+    const int c8 = lane % C::C8, r0 = lane / C::C8;
+#pragma unroll 4
+    for (int k = 0; k < C::NIT; ++k) {
+        const int t = r0 + RPI * k;
+        uint32_t w0, w1, w2, w3;
+        if constexpr (MODE == 0) {
+            const uint32_t q = stage + ly.rows + uint32_t(t * (2 * D));
+            const uint32_t R0 = lds_u32(q), R1 = lds_u32(q + 4u), R2 = lds_u32(q + 8u),
+                           R3 = lds_u32(q + 12u), R4 = lds_u32(q + 16u);
+            w0 = prmt(R0, R1, ly.w);
+            w1 = prmt(R1, R2, ly.w);
+            w2 = prmt(R2, R3, ly.w);
+            w3 = prmt(R3, R4, ly.w);
         } else {
-            constexpr int NC = (C::DK + 15) / 16;  // words of 16 residuals
-            uint32_t X[NC + 1], el[NC], eh[NC], ol[NC], oh[NC];
-#pragma unroll
-            for (int i = 0; i <= NC; ++i) X[i] = qc[i];
-#pragma unroll
-            for (int k = 0; k < NC; ++k) {
-                const uint32_t x = prmt(X[k], X[k + 1], ly.cs);
-                const uint32_t ev = x & 0x33333333u, od = (x >> 2) & 0x33333333u;
-                el[k] = ev & 0x0F0F0F0Fu;  // even elements of pairs 0, 2, 4, 6
-                eh[k] = (ev >> 4) & 0x0F0F0F0Fu;
-                ol[k] = od & 0x0F0F0F0Fu;
-                oh[k] = (od >> 4) & 0x0F0F0F0Fu;
+            const uint32_t qs = stage + ly.rows + uint32_t(t * D);
+            const uint32_t W0 = lds_u32(qs), W1 = lds_u32(qs + 4u), W2 = lds_u32(qs + 8u);
+            const uint32_t qc = stage + ly.codes + uint32_t(t * (D * MODE / 8));
+            uint32_t c0, c1, c2, c3;
+            if constexpr (MODE == 4) {
+                const uint32_t x = prmt(lds_u32(qc), lds_u32(qc + 4u), ly.cs);
+                const uint32_t lo = x & 0x0F0F0F0Fu, hi = (x >> 4) & 0x0F0F0F0Fu;
+                c0 = prmt(lo, hi, sel_code(0));
+                c1 = prmt(lo, hi, sel_code(1));
+                c2 = prmt(lo, hi, sel_code(2));
+                c3 = prmt(lo, hi, sel_code(3));
+            } else {  // 8 residuals of 2 bits in the low 16 bits of x
+                const uint32_t x = prmt(lds_u32(qc), 0u, ly.cs);
+                const uint32_t ev = x & 0x3333u, od = (x >> 2) & 0x3333u;
+                const uint32_t el = ev & 0x0F0Fu, eh = (ev >> 4) & 0x0F0Fu;
+                const uint32_t ol = od & 0x0F0Fu, oh = (od >> 4) & 0x0F0Fu;
+                c0 = prmt(el, ol, sel_code(0));
+                c1 = prmt(eh, oh, sel_code(0));
+                c2 = prmt(el, ol, sel_code(1));
+                c3 = prmt(eh, oh, sel_code(1));
             }
-#pragma unroll
-            for (int p = 0; p < C::NK; ++p) {
-                const int k = p >> 3, j = (p & 7) >> 1;
-                const uint32_t cw = (p & 1) ? prmt(eh[k], oh[k], sel_code(j)) : prmt(el[k], ol[k], sel_code(j));
-                o[p] = merge(prmt(W[p >> 1], W[(p >> 1) + 1], (p & 1) ? ly.p1 : ly.p0), cw, b7[p]);
-            }
+            w0 = merge(prmt(W0, W1, ly.p0), c0, b7[0]);
+            w1 = merge(prmt(W0, W1, ly.p1), c1, b7[1]);
+            w2 = merge(prmt(W1, W2, ly.p0), c2, b7[2]);
+            w3 = merge(prmt(W1, W2, ly.p1), c3, b7[3]);
         }
+        if (t >= zero_from) w0 = w1 = w2 = w3 = 0u;
+        sts_v4(xb + xb_off<D>(t, c8), w0, w1, w2, w3);
     }
 }
 
-// Two V tokens of this lane (token a of the stage -> low halves, a + 1 -> high halves; dims
-// v0 .. v0 + DV - 1).
-template <int D, int MODE>
-__device__ __forceinline__ void v_pair(const uint8_t *stage, const Lay &ly, int a,
-                                       const uint32_t (&b7)[Cfg<D>::DV], uint32_t (&o)[Cfg<D>::DV]) {
-    using C = Cfg<D>;
-    if constexpr (MODE == 0) {
-        constexpr int NW = C::DV / 2;
-        const uint32_t *qa = reinterpret_cast<const uint32_t *>(stage + ly.rows + a * (2 * D));
-        const uint32_t *qb = qa + D / 2;
-        uint32_t A[NW + 1], B[NW + 1];
-#pragma unroll
-        for (int i = 0; i <= NW; ++i) {
-            A[i] = qa[i];
-            B[i] = qb[i];
-        }
-#pragma unroll
-        for (int e = 0; e < C::DV; ++e) {
-            const uint32_t x = prmt(A[e >> 1], A[(e >> 1) + 1], ly.w);
-            const uint32_t y = prmt(B[e >> 1], B[(e >> 1) + 1], ly.w);
-            o[e] = prmt(x, y, (e & 1) ? 0x7632u : 0x5410u);
-        }
-    } else {
-        constexpr int NS = C::DV / 4;
-        const uint32_t *sa = reinterpret_cast<const uint32_t *>(stage + ly.rows + a * D);
-        const uint32_t *sb = sa + D / 4;
-        uint32_t A[NS + 1], B[NS + 1], SA[NS], SB[NS];
-#pragma unroll
-        for (int i = 0; i <= NS; ++i) {
-            A[i] = sa[i];
-            B[i] = sb[i];
-        }
-#pragma unroll
-        for (int k = 0; k < NS; ++k) {
-            SA[k] = prmt(A[k], A[k + 1], ly.w);
-            SB[k] = prmt(B[k], B[k + 1], ly.w);
-        }
-        constexpr int CR = D * MODE / 8;  // residual bytes per row
-        const uint32_t *ca = reinterpret_cast<const uint32_t *>(stage + ly.codes + a * CR);
-        const uint32_t *cb = reinterpret_cast<const uint32_t *>(stage + ly.codes + (a + 1) * CR);
-        if constexpr (MODE == 4) {
-            constexpr int NC = (C::DV + 7) / 8;
-            uint32_t XA[NC + 1], XB[NC + 1], la[NC], ha[NC], lb[NC], hb[NC];
-#pragma unroll
-            for (int i = 0; i <= NC; ++i) {
-                XA[i] = ca[i];
-                XB[i] = cb[i];
-            }
-#pragma unroll
-            for (int k = 0; k < NC; ++k) {
-                const uint32_t x = prmt(XA[k], XA[k + 1], ly.cs), y = prmt(XB[k], XB[k + 1], ly.cs);
-                la[k] = x & 0x0F0F0F0Fu;
-                ha[k] = (x >> 4) & 0x0F0F0F0Fu;
-                lb[k] = y & 0x0F0F0F0Fu;
-                hb[k] = (y >> 4) & 0x0F0F0F0Fu;
-            }
-#pragma unroll
-            for (int e = 0; e < C::DV; ++e) {
-                const int k = e >> 3, j = (e & 7) >> 1;
-                const uint32_t cw = (e & 1) ? prmt(ha[k], hb[k], sel_code(j)) : prmt(la[k], lb[k], sel_code(j));
-                o[e] = merge(prmt(SA[e >> 2], SB[e >> 2], sel_cross(e & 3)), cw, b7[e]);
-            }
-        } else {
-            constexpr int NC = (C::DV + 15) / 16;
-            uint32_t XA[NC + 1], XB[NC + 1], ca4[4][NC], cb4[4][NC];
-#pragma unroll
-            for (int i = 0; i <= NC; ++i) {
-                XA[i] = ca[i];
-                XB[i] = cb[i];
-            }
-#pragma unroll
-            for (int k = 0; k < NC; ++k) {
-                const uint32_t x = prmt(XA[k], XA[k + 1], ly.cs), y = prmt(XB[k], XB[k + 1], ly.cs);
-#pragma unroll
-                for (int s = 0; s < 4; ++s) {
-                    ca4[s][k] = (x >> (2 * s)) & 0x03030303u;
-                    cb4[s][k] = (y >> (2 * s)) & 0x03030303u;
-                }
-            }
-#pragma unroll
-            for (int e = 0; e < C::DV; ++e) {
-                const int k = e >> 4, s = e & 3, j = (e & 15) >> 2;
-                o[e] = merge(prmt(SA[e >> 2], SB[e >> 2], sel_cross(e & 3)),
-                             prmt(ca4[s][k], cb4[s][k], sel_code(j)), b7[e]);
-            }
-        }
-    }
-}
-
-// Zero the halves of tokens past the tile's valid rows (P is 0 there, V must be finite).
-template <int D>
-__device__ __forceinline__ void v_tail(int t, int rows, uint32_t (&va)[Cfg<D>::DV]) {
-    const uint32_t keep = (t < rows ? 0x0000FFFFu : 0u) | (t + 1 < rows ? 0xFFFF0000u : 0u);
-#pragma unroll
-    for (int e = 0; e < Cfg<D>::DV; ++e) va[e] &= keep;
-}
-
-// ---- escapes -----------------------------------------------------------------------------------
-
-// The escape words of one tensor of a stage: word i of the block is val[i - off], its element
-// position pos[i - off] (shared memory when the stage staged them, else the block's words in HBM
-// with off = 0).
+// The escape words of one tensor of a stage.  Staged (val != 0): word i of the block is the u16
+// at shared address val + 2 (i - off), its slot in the 16-token tile (esc_scratch_slot) at
+// pos + 2 (i - off).  Otherwise the block's words and slots are read from HBM (gval / gpos).
 struct StageEsc {
-    const uint16_t *val;
-    const uint16_t *pos;
+    uint32_t val, pos;
     int off;
+    const uint16_t *gval, *gpos;
 };
 
-// A row half of N fragment registers per lane goes to scratch as N / 4 chunks of 512 bytes, chunk
-// k holding lane l's registers 4k .. 4k+3 at byte 16 l (16-byte stores without bank conflicts).
-template <int N> __device__ __forceinline__ void regs_to(uint8_t *scr, const uint32_t (&o)[N], int lane) {
-#pragma unroll
-    for (int k = 0; k < N / 4; ++k)
-        *reinterpret_cast<uint4 *>(scr + 512 * k + 16 * lane) =
-            make_uint4(o[4 * k], o[4 * k + 1], o[4 * k + 2], o[4 * k + 3]);
-}
-template <int N> __device__ __forceinline__ void regs_from(const uint8_t *scr, uint32_t (&o)[N], int lane) {
-#pragma unroll
-    for (int k = 0; k < N / 4; ++k) {
-        const uint4 v = *reinterpret_cast<const uint4 *>(scr + 512 * k + 16 * lane);
-        o[4 * k] = v.x;
-        o[4 * k + 1] = v.y;
-        o[4 * k + 2] = v.z;
-        o[4 * k + 3] = v.w;
-    }
-}
-__device__ __forceinline__ uint32_t scr_addr(int owner, int p, int half) {
-    return uint32_t(512 * (p >> 2) + 16 * owner + 4 * (p & 3) + 2 * half);
-}
-
-// Scratch byte of element (token r of the 16-token tile, dim c) in its row half's layout.
-template <int D, bool K> __device__ __forceinline__ uint32_t esc_slot(int r, int c) {
-    using C = Cfg<D>;
-    if (K) {  // lane (r & 7, c / DK) register (c % DK) / 2, half c & 1
-        const int q = c % C::DK;
-        return scr_addr(4 * (r & 7) + c / C::DK, q >> 1, q & 1);
-    }
-    // V: lane (c / DV, (r & 7) / 2) register c % DV, half r & 1
-    return scr_addr(4 * (c / C::DV) + ((r & 7) >> 1), c % C::DV, r & 1);
-}
-
-// Which row halves of the tile (tokens t0 .. t0+15 of the block) hold escapes [i0, i1): bit h.
+// Store the stage's escape words over their elements of the tile: escapes [e0, e1) of the block,
+// those from em on in the stage's second tile; rows at or past `rows` keep their value.
 template <int D>
-__device__ __forceinline__ uint32_t esc_halves(const StageEsc &se, int i0, int i1, int t0, int lane) {
-    uint32_t f = 0;
-    for (int i = i0 + lane; i < i1; i += 32) {
-        const int r = int(se.pos[i - se.off]) / D - t0;
-        f |= 1u << ((r >> 3) & 1);
+__device__ __forceinline__ void esc_patch(uint32_t xb, const StageEsc &se, int e0, int em, int e1,
+                                          int rows, int lane) {
+    for (int i = e0 + lane; i < e1; i += 32) {
+        uint32_t slot, val;
+        if (se.val != 0u) {
+            slot = lds_u16(se.pos + 2u * uint32_t(i - se.off));
+            val = lds_u16(se.val + 2u * uint32_t(i - se.off));
+        } else {
+            slot = __ldg(se.gpos + i);
+            val = __ldg(se.gval + i);
+        }
+        const int second = i >= em;
+        if (TT * second + int(slot / (2 * D)) < rows)
+            sts_u16(xb + uint32_t(second * TT * 2 * D) + slot, val);
     }
-    return __reduce_or_sync(FULL, f);
 }
 
-// Store escapes [i0, i1) of row half h over their elements: the half's registers round-trip
-// through scratch.
-template <int D, bool K, int N>
-__device__ __forceinline__ void esc_patch(uint32_t (&o)[N], uint8_t *scr, const StageEsc &se, int i0,
-                                          int i1, int t0, int h, int lane) {
-    __syncwarp();
-    regs_to(scr, o, lane);
-    __syncwarp();
-    for (int i = i0 + lane; i < i1; i += 32) {
-        const int pos = int(se.pos[i - se.off]);
-        const int r = pos / D - t0, c = pos % D;
-        if ((r >> 3) == h) *reinterpret_cast<uint16_t *>(scr + esc_slot<D, K>(r, c)) = se.val[i - se.off];
-    }
-    __syncwarp();
-    regs_from(scr, o, lane);
-}
+// ---- tiles on the tensor cores ------------------------------------------------------------------
 
-// ---- per-tile stages ----------------------------------------------------------------------------
-
-// S^T fragment of a 16-token tile (tile row r0 of the stage): s0/s1 token g (queries 2t, 2t+1),
-// s2/s3 token g + 8.
-template <int D, int MODE>
-__device__ __forceinline__ void qk_tile(const uint8_t *stage, const Lay &ly, int r0,
-                                        const uint32_t (&b7)[Cfg<D>::NK],
-                                        const uint32_t (&qb)[Cfg<D>::KS][2], const StageEsc &se,
-                                        int i0, int i1, int tb, uint8_t *scr, int lane, float (&s)[4]) {
-    using C = Cfg<D>;
-    const int gi = lane >> 2;
+// S^T fragment of the 16-token tile at tile row r0: s0/s1 token g (queries 2t, 2t+1), s2/s3
+// token g + 8.  K A fragments by ldmatrix: lanes 8 i .. 8 i + 7 address matrix i (rows 0-7 / 8-15,
+// head dims 0-7 / 8-15 of the k-step).
+template <int D>
+__device__ __forceinline__ void qk_tile(uint32_t xb, int r0, const uint32_t (&qb)[Cfg<D>::KS][2],
+                                        int lane, float (&s)[4]) {
+    const int row = r0 + (lane & 7) + ((lane >> 3) & 1) * 8;
+    const uint32_t base = xb + uint32_t(row * (2 * D));
+    const int y = (lane >> 4) ^ (D == 32 ? (row >> 1) & 3 : row & 7);
     s[0] = s[1] = s[2] = s[3] = 0.f;
-    const uint32_t halves = (MODE != 0 && i1 > i0) ? esc_halves<D>(se, i0, i1, tb, lane) : 0u;
-    if (!C::SPLIT) {
-        uint32_t ka0[C::NK], ka1[C::NK];
-        k_row<D, MODE>(stage, ly, r0 + gi, b7, ka0);
-        k_row<D, MODE>(stage, ly, r0 + gi + 8, b7, ka1);
-        if (MODE != 0) {
-            if (halves & 1u) esc_patch<D, true>(ka0, scr, se, i0, i1, tb, 0, lane);
-            if (halves & 2u) esc_patch<D, true>(ka1, scr, se, i0, i1, tb, 1, lane);
-        }
 #pragma unroll
-        for (int k = 0; k < C::KS; ++k)
-            mma_bf16(s[0], s[1], s[2], s[3], ka0[2 * k], ka1[2 * k], ka0[2 * k + 1], ka1[2 * k + 1],
-                     qb[k][0], qb[k][1]);
-    } else {
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-            uint32_t ka[C::NK];
-            k_row<D, MODE>(stage, ly, r0 + gi + 8 * h, b7, ka);
-            if (MODE != 0 && (halves >> h & 1u)) esc_patch<D, true>(ka, scr, se, i0, i1, tb, h, lane);
-#pragma unroll
-            for (int k = 0; k < C::KS; ++k) {
-                if (h == 0)
-                    mma_bf16(s[0], s[1], s[2], s[3], ka[2 * k], 0u, ka[2 * k + 1], 0u, qb[k][0], qb[k][1]);
-                else
-                    mma_bf16(s[0], s[1], s[2], s[3], 0u, ka[2 * k], 0u, ka[2 * k + 1], qb[k][0], qb[k][1]);
-            }
-        }
+    for (int k = 0; k < Cfg<D>::KS; ++k) {
+        uint32_t a0, a1, a2, a3;
+        ldsm_x4(base + (uint32_t((2 * k) ^ y) << 4), a0, a1, a2, a3);
+        mma_bf16(s[0], s[1], s[2], s[3], a0, a1, a2, a3, qb[k][0], qb[k][1]);
     }
 }
 
-// O^T += V^T P^T for a 16-token tile (P^T as B fragments: bh = bf16 part, bm = residual part).
-template <int D, int MODE>
-__device__ __forceinline__ void pv_tile(const uint8_t *stage, const Lay &ly, int r0, int rows,
-                                        const uint32_t (&b7)[Cfg<D>::DV], const uint32_t (&bh)[2],
-                                        const uint32_t (&bm)[2], const StageEsc &se, int i0, int i1,
-                                        int tb, uint8_t *scr, int lane, float (&acc)[Cfg<D>::KS][4]) {
-    using C = Cfg<D>;
-    const int t = 2 * (lane & 3);
-    const uint32_t halves = (MODE != 0 && i1 > i0) ? esc_halves<D>(se, i0, i1, tb, lane) : 0u;
-    if (!C::SPLIT) {
-        uint32_t va0[C::DV], va1[C::DV];
-        v_pair<D, MODE>(stage, ly, r0 + t, b7, va0);
-        v_pair<D, MODE>(stage, ly, r0 + t + 8, b7, va1);
-        if (MODE != 0) {
-            if (halves & 1u) esc_patch<D, false>(va0, scr, se, i0, i1, tb, 0, lane);
-            if (halves & 2u) esc_patch<D, false>(va1, scr, se, i0, i1, tb, 1, lane);
-        }
-        if (rows < TT) {
-            v_tail<D>(t, rows, va0);
-            v_tail<D>(t + 8, rows, va1);
-        }
+// O^T += V^T P^T for the 16-token tile at tile row r0 (P^T as B fragments: bh = bf16 part, bm =
+// residual part).  V^T A fragments by ldmatrix.trans: matrix i covers tokens 0-7 / 8-15 (i / 2)
+// and head dims 0-7 / 8-15 (i % 2) of the m-tile.
+template <int D>
+__device__ __forceinline__ void pv_tile(uint32_t xb, int r0, const uint32_t (&bh)[2],
+                                        const uint32_t (&bm)[2], int lane,
+                                        float (&acc)[Cfg<D>::KS][4]) {
+    const int row = r0 + (lane & 7) + (lane >> 4) * 8;
+    const uint32_t base = xb + uint32_t(row * (2 * D));
+    const int y = ((lane >> 3) & 1) ^ (D == 32 ? (row >> 1) & 3 : row & 7);
 #pragma unroll
-        for (int m = 0; m < C::KS; ++m) {
-            mma_bf16(acc[m][0], acc[m][1], acc[m][2], acc[m][3], va0[2 * m], va0[2 * m + 1],
-                     va1[2 * m], va1[2 * m + 1], bh[0], bh[1]);
-            mma_bf16(acc[m][0], acc[m][1], acc[m][2], acc[m][3], va0[2 * m], va0[2 * m + 1],
-                     va1[2 * m], va1[2 * m + 1], bm[0], bm[1]);
-        }
-    } else {
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-            uint32_t va[C::DV];
-            v_pair<D, MODE>(stage, ly, r0 + t + 8 * h, b7, va);
-            if (MODE != 0 && (halves >> h & 1u)) esc_patch<D, false>(va, scr, se, i0, i1, tb, h, lane);
-            if (rows < TT) v_tail<D>(t + 8 * h, rows, va);
-#pragma unroll
-            for (int m = 0; m < C::KS; ++m) {
-                const uint32_t x0 = h == 0 ? va[2 * m] : 0u, x1 = h == 0 ? va[2 * m + 1] : 0u;
-                const uint32_t x2 = h == 0 ? 0u : va[2 * m], x3 = h == 0 ? 0u : va[2 * m + 1];
-                mma_bf16(acc[m][0], acc[m][1], acc[m][2], acc[m][3], x0, x1, x2, x3, bh[0], bh[1]);
-                mma_bf16(acc[m][0], acc[m][1], acc[m][2], acc[m][3], x0, x1, x2, x3, bm[0], bm[1]);
-            }
-        }
+    for (int m = 0; m < Cfg<D>::KS; ++m) {
+        uint32_t a0, a1, a2, a3;
+        ldsm_x4_t(base + (uint32_t((2 * m) ^ y) << 4), a0, a1, a2, a3);
+        mma_bf16(acc[m][0], acc[m][1], acc[m][2], acc[m][3], a0, a1, a2, a3, bh[0], bh[1]);
+        mma_bf16(acc[m][0], acc[m][1], acc[m][2], acc[m][3], a0, a1, a2, a3, bm[0], bm[1]);
     }
 }
 
-// Q B fragments: qb[k][0] = Q[g][t D/4 + 4k + {0,1}], qb[k][1] = Q[g][t D/4 + 4k + {2,3}] -- the
-// head-dim order of the K fragments.
+// Q B fragments: qb[k][0] = Q[g][16k + 2t + {0,1}], qb[k][1] = Q[g][16k + 8 + 2t + {0,1}].
 template <int D>
 __device__ __forceinline__ void load_q(const uint16_t *q, int n_q, int stride,
                                        uint32_t (&qb)[Cfg<D>::KS][2], int lane) {
     const int gi = lane >> 2, tig = lane & 3;
     const uint32_t *row =
-        reinterpret_cast<const uint32_t *>(q + size_t(gi < n_q ? gi : 0) * stride + tig * Cfg<D>::DK);
+        reinterpret_cast<const uint32_t *>(q + size_t(gi < n_q ? gi : 0) * stride + 2 * tig);
 #pragma unroll
     for (int k = 0; k < Cfg<D>::KS; ++k) {
-        qb[k][0] = gi < n_q ? __ldg(row + 2 * k) : 0u;
-        qb[k][1] = gi < n_q ? __ldg(row + 2 * k + 1) : 0u;
+        qb[k][0] = gi < n_q ? __ldg(row + 8 * k) : 0u;
+        qb[k][1] = gi < n_q ? __ldg(row + 8 * k + 4) : 0u;
     }
 }
 
@@ -652,59 +411,74 @@ template <int D, bool BF16IN> struct Producer {
     int tile = 0, stage = 0, bseq = 0;
     const uint8_t *kb = nullptr, *vb = nullptr;  // the current unit's K and V blobs
 
-    __device__ __forceinline__ static void tensor(uint8_t *dst, const Sections &s, const uint16_t *pos,
-                                                  int mode, int t0, int n, int e0, int e1, int lane) {
-        if (BF16IN || mode == 0) {
-            copy_piece<C::TS * 2 * D + 16>(
-                dst, make_piece(s.rows + size_t(t0) * (2 * D), uint32_t(n * 2 * D)), lane);
-        } else {
-            copy_piece<C::TS * D + 16>(dst, make_piece(s.rows + size_t(t0) * D, uint32_t(n * D)), lane);
-            copy_piece<C::TS * D / 2 + 16>(
-                dst + C::CODE_OFF,
-                make_piece(s.codes + size_t(t0) * D * mode / 8, uint32_t(n * D * mode / 8)), lane);
-            const int cnt = e1 - e0;
-            if (cnt > 0 && cnt <= C::ESC_CAP) {
-                copy_piece<2 * C::ESC_CAP + 16>(dst + C::EV_OFF, make_piece(s.esc + 2 * e0, uint32_t(2 * cnt)), lane);
-                copy_piece<2 * C::ESC_CAP + 16>(
-                    dst + C::EP_OFF, make_piece(reinterpret_cast<const uint8_t *>(pos + e0), uint32_t(2 * cnt)),
-                    lane);
-            }
-        }
-    }
-
     // Issue stages while a ring slot is free; a block start waits until the consumer is at most
-    // one block behind, so a meta slot is never overwritten while in use.
+    // one block behind, so a meta slot is never overwritten while in use.  The slot's previous
+    // stage was read by the whole warp before this call (__syncwarp at the end of every stage).
+    // The pieces of a stage go out in parallel: lane 4 T + j copies piece j of tensor T (rows,
+    // residual codes, escape words, their positions), lanes 8 and 9 a new block's K and V base
+    // exponents; lane 0 first tells the slot's barrier how many bytes to expect.
     __device__ __forceinline__ void produce(const AttnArgs &a, uint8_t *ring, uint8_t *metas,
-                                            int c_stage, int c_fb, int lane) {
+                                            uint8_t *bars, int c_stage, int c_fb, int lane) {
         while (w.fb < w.fb1 && stage - c_stage < C::NSTAGE) {
             if (tile == 0 && w.fb - c_fb >= 2) break;
             const FlatBlock &f = w.cur;
             const int km = BF16IN ? 0 : f.k_mode, vm = BF16IN ? 0 : f.v_mode;
+            const uint32_t bar = smem_u32(bars + 8 * (stage % C::NSTAGE));
+            uint8_t *ms = metas + (bseq & 1) * C::MSLOT;
             if (tile == 0) {
                 const UnitDev *U = a.units + f.unit;
                 kb = U->k;
                 vb = U->v;
-                uint8_t *ms = metas + (bseq & 1) * C::MSLOT;
                 if (lane == 0) {
                     const uint4 *src = reinterpret_cast<const uint4 *>(&f);
                     reinterpret_cast<uint4 *>(ms + C::M_FB)[0] = src[0];
                     reinterpret_cast<uint4 *>(ms + C::M_FB)[1] = src[1];
                 }
                 reinterpret_cast<uint16_t *>(ms + C::M_EM)[lane] = uint16_t(w.em);
-                if (!BF16IN) {
-                    if (km != 0) copy_piece<D + 32>(ms, make_piece(kb + f.k_off + kHeaderBytes, D), lane);
-                    if (vm != 0) copy_piece<D + 32>(ms + C::BASE, make_piece(vb + f.v_off + kHeaderBytes, D), lane);
-                }
             }
             const int t0 = tile * C::TS;
             const int n = min(C::TS, int(f.valid) - t0);
             const int ia = t0 >> 4, ib = min(16, (t0 + C::TS) >> 4);
-            uint8_t *slot = ring + (stage % C::NSTAGE) * C::SLOT;
-            tensor(slot, sections<D, BF16IN>(kb, f.k_off, km, f.n_tok), a.esc + f.k_rec + kEscRecHead,
-                   km, t0, n, esc_at(w.em, 0, ia), esc_at(w.em, 0, ib), lane);
-            tensor(slot + C::TR, sections<D, BF16IN>(vb, f.v_off, vm, f.n_tok),
-                   a.esc + f.v_rec + kEscRecHead, vm, t0, n, esc_at(w.em, 1, ia), esc_at(w.em, 1, ib), lane);
-            cp_async_commit();
+            const int T = (lane >> 2) & 1, j = lane & 3;
+            const int e0 = esc_at(w.em, T, ia), e1 = esc_at(w.em, T, ib);
+            const int mode = T ? vm : km;
+            const uint32_t off = T ? f.v_off : f.k_off;
+            const Sections sc = sections<D, BF16IN>(T ? vb : kb, off, mode, f.n_tok);
+            uint8_t *dst = ring + (stage % C::NSTAGE) * C::SLOT + T * C::TR;
+            const uint8_t *src = nullptr;
+            uint32_t len = 0;
+            if (lane < 8) {
+                if (BF16IN || mode == 0) {
+                    if (j == 0) {
+                        src = sc.rows + size_t(t0) * (2 * D);
+                        len = uint32_t(n * 2 * D);
+                    }
+                } else if (j == 0) {
+                    src = sc.rows + size_t(t0) * D;
+                    len = uint32_t(n * D);
+                } else if (j == 1) {
+                    src = sc.codes + size_t(t0) * D * mode / 8;
+                    len = uint32_t(n * D * mode / 8);
+                    dst += C::CODE_OFF;
+                } else if (e1 - e0 > 0 && e1 - e0 <= C::ESC_CAP) {
+                    src = j == 2 ? sc.esc + 2 * e0
+                                 : reinterpret_cast<const uint8_t *>(a.esc + (T ? f.v_rec : f.k_rec) +
+                                                                     kEscRecHead + e0);
+                    len = uint32_t(2 * (e1 - e0));
+                    dst += j == 2 ? C::EV_OFF : C::EP_OFF;
+                }
+            } else if (!BF16IN && tile == 0 && lane < 10 && (lane == 8 ? km : vm) != 0) {
+                src = (lane == 8 ? kb + f.k_off : vb + f.v_off) + kHeaderBytes;
+                len = D;
+                dst = ms + (lane - 8) * C::BASE;
+            }
+            const Piece p = make_piece(src, len);
+            const uint32_t bytes = len != 0 ? p.alloc : 0u;
+            const uint32_t total = __reduce_add_sync(FULL, bytes);
+            fence_proxy_async();
+            if (lane == 0) mbar_arrive_expect_tx(bar, total);
+            __syncwarp();
+            if (bytes != 0) bulk_g2s(smem_u32(dst), p.src, bytes, bar);
             ++stage;
             if (t0 + C::TS >= int(f.valid)) {
                 tile = 0;
@@ -721,49 +495,79 @@ template <int D, bool BF16IN> struct Producer {
 // the producer's staged copies when they fit, else the block's words in HBM.
 template <int D>
 __device__ __forceinline__ StageEsc stage_esc(const AttnArgs &a, const FlatBlock &f, int T,
-                                              const uint8_t *tstage, int e0, int e1) {
+                                              uint32_t tstage, int e0, int e1) {
     using C = Cfg<D>;
     const uint32_t off = T ? f.v_off : f.k_off, rec = T ? f.v_rec : f.k_rec;
     const int mode = T ? f.v_mode : f.k_mode;
     StageEsc se;
+    se.gval = se.gpos = nullptr;
     if (e1 - e0 <= C::ESC_CAP) {
-        se.val = reinterpret_cast<const uint16_t *>(tstage + C::EV_OFF + esc_word_line<D>(off, f.n_tok, mode, e0));
-        se.pos = reinterpret_cast<const uint16_t *>(tstage + C::EP_OFF + esc_pos_line(rec, e0));
+        se.val = tstage + C::EV_OFF + esc_word_line<D>(off, f.n_tok, mode, e0);
+        se.pos = tstage + C::EP_OFF + esc_pos_line(rec, e0);
         se.off = e0;
     } else {
         const UnitDev *U = a.units + f.unit;
-        se.val = reinterpret_cast<const uint16_t *>(sections<D, false>(T ? U->v : U->k, off, mode, f.n_tok).esc);
-        se.pos = a.esc + rec + kEscRecHead;
+        se.val = se.pos = 0u;
         se.off = 0;
+        se.gval = reinterpret_cast<const uint16_t *>(sections<D, false>(T ? U->v : U->k, off, mode, f.n_tok).esc);
+        se.gpos = a.esc + rec + kEscRecHead;
     }
     return se;
+}
+
+// One tensor of a stage into the tile, escapes included.
+template <int D>
+__device__ __forceinline__ void stage_tile(const AttnArgs &a, const FlatBlock &f, int T, int mode,
+                                           uint32_t tstage, uint32_t xb, const Lay &ly,
+                                           const uint32_t (&b7)[4], const uint8_t *em, int ia,
+                                           int ib, int rows, int zero_from, int lane) {
+    if (mode == 4) decode_stage<D, 4>(tstage, xb, ly, b7, lane, zero_from);
+    else if (mode == 2) decode_stage<D, 2>(tstage, xb, ly, b7, lane, zero_from);
+    else decode_stage<D, 0>(tstage, xb, ly, b7, lane, zero_from);
+    const int e0 = esc_ms(em, T, ia), e1 = esc_ms(em, T, ib);
+    if (e1 > e0) {
+        const StageEsc se = stage_esc<D>(a, f, T, tstage, e0, e1);
+        __syncwarp();  // the decoded words are in place before escapes overwrite some
+        esc_patch<D>(xb, se, e0, Cfg<D>::SUBS > 1 ? esc_ms(em, T, ia + 1) : e1, e1, rows, lane);
+    }
+    __syncwarp();
 }
 
 template <int D, bool BF16IN>
 __device__ __forceinline__ void worker(const AttnArgs &a, uint8_t *R, int wk, int fb0, int fb1,
                                        int lane) {
     using C = Cfg<D>;
-    const int gi = lane >> 2, tig = lane & 3;
+    const int gi = lane >> 2, tig = lane & 3, c8 = lane % C::C8;
     uint8_t *ring = R;
     uint8_t *metas = R + C::W_META;
-    uint8_t *scr = R + C::W_SCR;
+    const uint32_t xb = smem_u32(R + C::W_XB);
+    uint8_t *bars = R + C::W_BAR;
+    if (lane == 0) {
+#pragma unroll
+        for (int j = 0; j < C::NSTAGE; ++j) mbar_init(smem_u32(bars + 8 * j), 1);
+        fence_mbar_init();
+    }
+    __syncwarp();
     Producer<D, BF16IN> pp;
     pp.w.init(a, fb0, fb1, lane);
     int fb = fb0, tile = 0, stage = 0, bseq = 0;
     int ubeg = 0, uend = 0, seg_begin = fb0;  // the current unit's flat block range
     Lay lk{}, lv{};
-    uint32_t b7k[C::NK], b7v[C::DV];
-#pragma unroll
-    for (int p = 0; p < C::NK; ++p) b7k[p] = 0u;
-#pragma unroll
-    for (int e = 0; e < C::DV; ++e) b7v[e] = 0u;
+    uint32_t b7k[4] = {0u, 0u, 0u, 0u}, b7v[4] = {0u, 0u, 0u, 0u};
     uint32_t qb[C::KS][2];
     float acc[C::KS][4];
     float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
 
     while (fb < fb1) {
-        pp.produce(a, ring, metas, stage, fb, lane);
-        cp_async_wait(pp.stage - stage - 1);
+        pp.produce(a, ring, metas, bars, stage, fb, lane);
+        if (!mbar_wait_bounded(smem_u32(bars + 8 * (stage % C::NSTAGE)), (stage / C::NSTAGE) & 1,
+                               kStageWaitUs)) {
+            if (lane == 0) report(a.status, KVX_ERR_TIMEOUT, DERR_TIMEOUT);
+            // let the copies already issued land before this CTA's shared memory goes away
+            for (int q = stage + 1; q < pp.stage; ++q)
+                mbar_wait_bounded(smem_u32(bars + 8 * (q % C::NSTAGE)), (q / C::NSTAGE) & 1, kStageWaitUs);
+            return;
+        }
         __syncwarp();
         const uint8_t *ms = metas + (bseq & 1) * C::MSLOT;
         const FlatBlock f = *reinterpret_cast<const FlatBlock *>(ms + C::M_FB);
@@ -779,10 +583,10 @@ __device__ __forceinline__ void worker(const AttnArgs &a, uint8_t *R, int wk, in
             const uint32_t vd = uint32_t(reinterpret_cast<uintptr_t>(sv.rows) & 15u);
             const uint32_t kc = kmode ? uint32_t(reinterpret_cast<uintptr_t>(sk.codes) & 15u) : 0u;
             const uint32_t vc = vmode ? uint32_t(reinterpret_cast<uintptr_t>(sv.codes) & 15u) : 0u;
-            lk = make_lay<D>(kd, kc, kmode, tig * C::DK, BF16IN);
-            lv = make_lay<D>(vd, vc, vmode, gi * C::DV, BF16IN);
-            if (kmode != 0) load_b7k<D>(ms + kd + tig * C::DK, b7k);
-            if (vmode != 0) load_b7v<D>(ms + C::BASE + vd + gi * C::DV, b7v);
+            lk = make_lay<D>(kd, kc, kmode, c8, BF16IN);
+            lv = make_lay<D>(vd, vc, vmode, c8, BF16IN);
+            if (kmode != 0) load_b7(smem_u32(ms) + kd + 8 * c8, b7k);
+            if (vmode != 0) load_b7(smem_u32(ms) + C::BASE + vd + 8 * c8, b7v);
             if (fb == seg_begin) {
                 load_q<D>(U->q, U->n_q, U->q_stride, qb, lane);
                 m0 = m1 = -INFINITY;
@@ -791,7 +595,7 @@ __device__ __forceinline__ void worker(const AttnArgs &a, uint8_t *R, int wk, in
                 for (int m = 0; m < C::KS; ++m) acc[m][0] = acc[m][1] = acc[m][2] = acc[m][3] = 0.f;
             }
         }
-        uint8_t *slot = ring + (stage % C::NSTAGE) * C::SLOT;
+        const uint32_t kst = smem_u32(ring + (stage % C::NSTAGE) * C::SLOT), vst = kst + C::TR;
         const int t0 = tile * C::TS;
         const int rows = min(C::TS, int(f.valid) - t0);
         const bool last_tile = t0 + C::TS >= int(f.valid);
@@ -799,23 +603,17 @@ __device__ __forceinline__ void worker(const AttnArgs &a, uint8_t *R, int wk, in
         const int ia = t0 >> 4, ib = min(16, (t0 + C::TS) >> 4);
 
         // S^T = K Q^T for every tile of the stage
+        stage_tile<D>(a, f, 0, kmode, kst, xb, lk, b7k, em, ia, ib, rows, C::TS, lane);
         float s[C::SUBS][4];
-        {
-            const StageEsc se = stage_esc<D>(a, f, 0, slot, esc_ms(em, 0, ia), esc_ms(em, 0, ib));
 #pragma unroll
-            for (int sub = 0; sub < C::SUBS; ++sub) {
-                if (sub * TT < rows) {
-                    const int i0 = esc_ms(em, 0, ia + sub), i1 = esc_ms(em, 0, ia + sub + 1);
-                    const int tb = t0 + sub * TT;
-                    if (kmode == 4) qk_tile<D, 4>(slot, lk, sub * TT, b7k, qb, se, i0, i1, tb, scr, lane, s[sub]);
-                    else if (kmode == 2) qk_tile<D, 2>(slot, lk, sub * TT, b7k, qb, se, i0, i1, tb, scr, lane, s[sub]);
-                    else qk_tile<D, 0>(slot, lk, sub * TT, b7k, qb, se, i0, i1, tb, scr, lane, s[sub]);
-                    const int rr = rows - sub * TT;
-                    if (gi >= rr) s[sub][0] = s[sub][1] = -INFINITY;
-                    if (gi + 8 >= rr) s[sub][2] = s[sub][3] = -INFINITY;
-                } else {
-                    s[sub][0] = s[sub][1] = s[sub][2] = s[sub][3] = -INFINITY;
-                }
+        for (int sub = 0; sub < C::SUBS; ++sub) {
+            if (sub * TT < rows) {
+                qk_tile<D>(xb, sub * TT, qb, lane, s[sub]);
+                const int rr = rows - sub * TT;
+                if (gi >= rr) s[sub][0] = s[sub][1] = -INFINITY;
+                if (gi + 8 >= rr) s[sub][2] = s[sub][3] = -INFINITY;
+            } else {
+                s[sub][0] = s[sub][1] = s[sub][2] = s[sub][3] = -INFINITY;
             }
         }
 
@@ -865,22 +663,13 @@ __device__ __forceinline__ void worker(const AttnArgs &a, uint8_t *R, int wk, in
             }
         }
 
-        // O^T += V^T P^T for every tile of the stage
-        {
-            const uint8_t *vstage = slot + C::TR;
-            const StageEsc se = stage_esc<D>(a, f, 1, vstage, esc_ms(em, 1, ia), esc_ms(em, 1, ib));
+        // O^T += V^T P^T for every tile of the stage (the tile's K reads are done: stage_tile
+        // ends with __syncwarp, and the K tiles were read before the softmax)
+        __syncwarp();
+        stage_tile<D>(a, f, 1, vmode, vst, xb, lv, b7v, em, ia, ib, rows, rows, lane);
 #pragma unroll
-            for (int sub = 0; sub < C::SUBS; ++sub) {
-                if (sub * TT < rows) {
-                    const int i0 = esc_ms(em, 1, ia + sub), i1 = esc_ms(em, 1, ia + sub + 1);
-                    const int tb = t0 + sub * TT;
-                    const int rr = min(TT, rows - sub * TT);
-                    if (vmode == 4) pv_tile<D, 4>(vstage, lv, sub * TT, rr, b7v, bh[sub], bm[sub], se, i0, i1, tb, scr, lane, acc);
-                    else if (vmode == 2) pv_tile<D, 2>(vstage, lv, sub * TT, rr, b7v, bh[sub], bm[sub], se, i0, i1, tb, scr, lane, acc);
-                    else pv_tile<D, 0>(vstage, lv, sub * TT, rr, b7v, bh[sub], bm[sub], se, i0, i1, tb, scr, lane, acc);
-                }
-            }
-        }
+        for (int sub = 0; sub < C::SUBS; ++sub)
+            if (sub * TT < rows) pv_tile<D>(xb, sub * TT, bh[sub], bm[sub], lane, acc);
 
         if (seg_end) {
             float lt0 = l0, lt1 = l1;
@@ -890,7 +679,7 @@ __device__ __forceinline__ void worker(const AttnArgs &a, uint8_t *R, int wk, in
                 lt1 = __fadd_rn(lt1, __shfl_xor_sync(FULL, lt1, o));
             }
             const int qa = 2 * tig, qc = 2 * tig + 1;
-            const int d0 = gi * C::DV;
+            // acc[m][0 / 1]: dim 16 m + g of queries qa / qc; acc[m][2 / 3]: dim 16 m + g + 8
             if (seg_begin == ubeg && fb + 1 == uend) {
                 const UnitDev *U = a.units + f.unit;
                 const int n_q = U->n_q, stride = U->q_stride;
@@ -902,18 +691,20 @@ __device__ __forceinline__ void worker(const AttnArgs &a, uint8_t *R, int wk, in
                     if (qc < n_q) lse[qc] = m1 + logf(lt1);
                 }
                 if (qa < n_q) {
-                    float *o = out + size_t(qa) * stride + d0;
+                    float *o = out + size_t(qa) * stride + gi;
 #pragma unroll
-                    for (int m = 0; m < C::KS; ++m)
-                        *reinterpret_cast<float2 *>(o + 2 * m) =
-                            make_float2(__fmul_rn(acc[m][0], inv0), __fmul_rn(acc[m][2], inv0));
+                    for (int m = 0; m < C::KS; ++m) {
+                        o[16 * m] = __fmul_rn(acc[m][0], inv0);
+                        o[16 * m + 8] = __fmul_rn(acc[m][2], inv0);
+                    }
                 }
                 if (qc < n_q) {
-                    float *o = out + size_t(qc) * stride + d0;
+                    float *o = out + size_t(qc) * stride + gi;
 #pragma unroll
-                    for (int m = 0; m < C::KS; ++m)
-                        *reinterpret_cast<float2 *>(o + 2 * m) =
-                            make_float2(__fmul_rn(acc[m][1], inv1), __fmul_rn(acc[m][3], inv1));
+                    for (int m = 0; m < C::KS; ++m) {
+                        o[16 * m] = __fmul_rn(acc[m][1], inv1);
+                        o[16 * m + 8] = __fmul_rn(acc[m][3], inv1);
+                    }
                 }
             } else {
                 const int ps = (seg_begin == fb0) ? 0 : 1;
@@ -924,16 +715,18 @@ __device__ __forceinline__ void worker(const AttnArgs &a, uint8_t *R, int wk, in
                     part[8 + qa] = lt0;
                     part[8 + qc] = lt1;
                 }
-                float *oa = part + 16 + qa * D + d0;
-                float *oc = part + 16 + qc * D + d0;
+                float *oa = part + 16 + qa * D + gi;
+                float *oc = part + 16 + qc * D + gi;
 #pragma unroll
                 for (int m = 0; m < C::KS; ++m) {
-                    *reinterpret_cast<float2 *>(oa + 2 * m) = make_float2(acc[m][0], acc[m][2]);
-                    *reinterpret_cast<float2 *>(oc + 2 * m) = make_float2(acc[m][1], acc[m][3]);
+                    oa[16 * m] = acc[m][0];
+                    oa[16 * m + 8] = acc[m][2];
+                    oc[16 * m] = acc[m][1];
+                    oc[16 * m + 8] = acc[m][3];
                 }
             }
         }
-        __syncwarp();  // every lane is done with this ring slot before it is refilled
+        __syncwarp();  // every lane is done with this ring slot and the tile before they are reused
         ++stage;
         if (last_tile) {
             tile = 0;

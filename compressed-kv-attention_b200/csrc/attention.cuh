@@ -28,11 +28,22 @@ static_assert(sizeof(FlatBlock) == 32, "FlatBlock is 32 bytes");
 // Escape record of one coded block with escape words (u16 array):
 //   [0, 16)           e[i - 1] = escape words of tokens [0, 16 i), i = 1..16 (clamped to the
 //                     block), so the escapes of tokens [16 a, 16 b) are [e(a), e(b)), e(0) = 0;
-//   [16, 16 + n_esc)  the element index (token * dim + channel) of every escape, in the
-//                     container's scan order -- the sentinel the escape word replaces.
+//   [16, 16 + n_esc)  for every escape, in the container's scan order, where the attention kernel
+//                     stores it: the byte of the element it replaces in the kernel's BF16 tile
+//                     (esc_scratch_slot of its token within the 16-token tile and its channel).
 // Built once per plan from the blob's residual codes; raw blocks and blocks without escapes
 // have none.
 constexpr int kEscRecHead = 16;
+
+// Byte of element (token r of a 16-token tile, channel c) in the attention kernel's BF16 tile:
+// rows of 2 dim bytes, 16-byte chunks XOR-swizzled by the row (chunk c / 8 of row r sits at
+// chunk position (c / 8) ^ (r & 7), or ^ ((r / 2) & 3) for dim 32).  The same for K and V.
+__host__ __device__ inline uint32_t esc_scratch_slot(int dim, int T, int r, int c) {
+    (void)T;
+    const int c8 = c >> 3;
+    const int sw = dim == 32 ? (r >> 1) & 3 : r & 7;
+    return uint32_t(r * 2 * dim + ((c8 ^ sw) << 4) + 2 * (c & 7));
+}
 
 __device__ __forceinline__ FlatBlock load_flat(const FlatBlock *f, int64_t i) {
     const uint4 a = __ldg(reinterpret_cast<const uint4 *>(f + i));

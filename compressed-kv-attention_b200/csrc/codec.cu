@@ -607,15 +607,23 @@ __global__ void esc_fill_kernel(const UnitDev *units, const FlatBlock *flat, int
     }
     if (run > nesc && lane == 0) report(status, KVX_ERR_RUNTIME, DERR_ESC_OVERRUN);
     __syncwarp();
+    const int m = min(run, nesc);
+    int e = 0;
     if (lane < 16) {
-        const int m = min(run, nesc);
         const uint32_t limit = uint32_t(16 * (lane + 1)) * uint32_t(dim);
         int lo = 0, hi = m;  // first position >= limit
         while (lo < hi) {
             const int mid = (lo + hi) >> 1;
             if (uint32_t(pos[mid]) < limit) lo = mid + 1; else hi = mid;
         }
-        esc[rec + lane] = uint16_t(lo);
+        e = lo;
+    }
+    __syncwarp();
+    if (lane < 16) esc[rec + lane] = uint16_t(e);
+    // element index -> the escape's byte in the attention kernel's scratch
+    for (int i = lane; i < m; i += 32) {
+        const int el = pos[i];
+        pos[i] = uint16_t(esc_scratch_slot(dim, T, (el / dim) & 15, el % dim));
     }
 }
 
