@@ -58,10 +58,13 @@ __host__ __device__ constexpr int cmax(int a, int b) { return a > b ? a : b; }
 #ifndef KVX_MAXWARPS
 #define KVX_MAXWARPS 12
 #endif
+#ifndef KVX_TS64
+#define KVX_TS64 32
+#endif
 
 template <int D> struct Cfg {
     static constexpr int KS = D / 16;             // k-steps of QK = M-tiles of PV
-    static constexpr int TS = D <= 64 ? 32 : 16;  // tokens per ring stage
+    static constexpr int TS = D <= 64 ? KVX_TS64 : 16;  // tokens per ring stage
     static constexpr int SUBS = TS / TT;          // MMA tiles per stage
     static constexpr int C8 = D / 8;              // 8-element chunks per row
     static constexpr int NIT = TS * C8 / 32;      // chunk steps of a lane per stage and tensor
@@ -239,54 +242,68 @@ template <int D> __device__ __forceinline__ uint32_t xb_off(int t, int c8) {
 // ---- stage decode ------------------------------------------------------------------------------
 
 // Rebuild this lane's chunks of one tensor's stage into the tile (MODE 4 / 2 coded, 0 raw BF16).
-// Rows at or past `zero_from` are stored as zeros (V: P is 0 there, V must be finite).
+// Rows at or past `zero_from` are stored as zeros (V: P is 0 there, V must be finite).  The
+// shared-memory accesses are ordered as written, so the chunks go in groups of G: all loads of the
+// group, then the arithmetic, then the stores.
 template <int D, int MODE>
 __device__ __forceinline__ void decode_stage(uint32_t stage, uint32_t xb, const Lay &ly,
                                              const uint32_t (&b7)[4], int lane, int zero_from) {
     using C = Cfg<D>;
     constexpr int RPI = 32 / C::C8;  // rows per chunk step
+    constexpr int G = C::NIT < 4 ? C::NIT : 4;
+    constexpr int NW = MODE == 0 ? 5 : 3;  // row words per chunk
     const int c8 = lane % C::C8, r0 = lane / C::C8;
-#pragma unroll 4
-    for (int k = 0; k < C::NIT; ++k) {
-        const int t = r0 + RPI * k;
-        uint32_t w0, w1, w2, w3;
-        if constexpr (MODE == 0) {
-            const uint32_t q = stage + ly.rows + uint32_t(t * (2 * D));
-            const uint32_t R0 = lds_u32(q), R1 = lds_u32(q + 4u), R2 = lds_u32(q + 8u),
-                           R3 = lds_u32(q + 12u), R4 = lds_u32(q + 16u);
-            w0 = prmt(R0, R1, ly.w);
-            w1 = prmt(R1, R2, ly.w);
-            w2 = prmt(R2, R3, ly.w);
-            w3 = prmt(R3, R4, ly.w);
-        } else {
-            const uint32_t qs = stage + ly.rows + uint32_t(t * D);
-            const uint32_t W0 = lds_u32(qs), W1 = lds_u32(qs + 4u), W2 = lds_u32(qs + 8u);
-            const uint32_t qc = stage + ly.codes + uint32_t(t * (D * MODE / 8));
-            uint32_t c0, c1, c2, c3;
-            if constexpr (MODE == 4) {
-                const uint32_t x = prmt(lds_u32(qc), lds_u32(qc + 4u), ly.cs);
-                const uint32_t lo = x & 0x0F0F0F0Fu, hi = (x >> 4) & 0x0F0F0F0Fu;
-                c0 = prmt(lo, hi, sel_code(0));
-                c1 = prmt(lo, hi, sel_code(1));
-                c2 = prmt(lo, hi, sel_code(2));
-                c3 = prmt(lo, hi, sel_code(3));
-            } else {  // 8 residuals of 2 bits in the low 16 bits of x
-                const uint32_t x = prmt(lds_u32(qc), 0u, ly.cs);
-                const uint32_t ev = x & 0x3333u, od = (x >> 2) & 0x3333u;
-                const uint32_t el = ev & 0x0F0Fu, eh = (ev >> 4) & 0x0F0Fu;
-                const uint32_t ol = od & 0x0F0Fu, oh = (od >> 4) & 0x0F0Fu;
-                c0 = prmt(el, ol, sel_code(0));
-                c1 = prmt(eh, oh, sel_code(0));
-                c2 = prmt(el, ol, sel_code(1));
-                c3 = prmt(eh, oh, sel_code(1));
+#pragma unroll 1
+    for (int k0 = 0; k0 < C::NIT; k0 += G) {
+        uint32_t W[G][NW], X[G][2];
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+            const int t = r0 + RPI * (k0 + g);
+            const uint32_t q = stage + ly.rows + uint32_t(t * (MODE == 0 ? 2 * D : D));
+#pragma unroll
+            for (int i = 0; i < NW; ++i) W[g][i] = lds_u32(q + 4u * i);
+            if (MODE != 0) {
+                const uint32_t qc = stage + ly.codes + uint32_t(t * (D * (MODE == 0 ? 4 : MODE) / 8));
+                X[g][0] = lds_u32(qc);
+                if (MODE == 4) X[g][1] = lds_u32(qc + 4u);
             }
-            w0 = merge(prmt(W0, W1, ly.p0), c0, b7[0]);
-            w1 = merge(prmt(W0, W1, ly.p1), c1, b7[1]);
-            w2 = merge(prmt(W1, W2, ly.p0), c2, b7[2]);
-            w3 = merge(prmt(W1, W2, ly.p1), c3, b7[3]);
         }
-        if (t >= zero_from) w0 = w1 = w2 = w3 = 0u;
-        sts_v4(xb + xb_off<D>(t, c8), w0, w1, w2, w3);
+        uint32_t w[G][4];
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+            if constexpr (MODE == 0) {
+#pragma unroll
+                for (int i = 0; i < 4; ++i) w[g][i] = prmt(W[g][i], W[g][i + 1], ly.w);
+            } else {
+                uint32_t c0, c1, c2, c3;
+                if constexpr (MODE == 4) {
+                    const uint32_t x = prmt(X[g][0], X[g][1], ly.cs);
+                    const uint32_t lo = x & 0x0F0F0F0Fu, hi = (x >> 4) & 0x0F0F0F0Fu;
+                    c0 = prmt(lo, hi, sel_code(0));
+                    c1 = prmt(lo, hi, sel_code(1));
+                    c2 = prmt(lo, hi, sel_code(2));
+                    c3 = prmt(lo, hi, sel_code(3));
+                } else {  // 8 residuals of 2 bits in the low 16 bits of x
+                    const uint32_t x = prmt(X[g][0], 0u, ly.cs);
+                    const uint32_t ev = x & 0x3333u, od = (x >> 2) & 0x3333u;
+                    const uint32_t el = ev & 0x0F0Fu, eh = (ev >> 4) & 0x0F0Fu;
+                    const uint32_t ol = od & 0x0F0Fu, oh = (od >> 4) & 0x0F0Fu;
+                    c0 = prmt(el, ol, sel_code(0));
+                    c1 = prmt(eh, oh, sel_code(0));
+                    c2 = prmt(el, ol, sel_code(1));
+                    c3 = prmt(eh, oh, sel_code(1));
+                }
+                w[g][0] = merge(prmt(W[g][0], W[g][1], ly.p0), c0, b7[0]);
+                w[g][1] = merge(prmt(W[g][0], W[g][1], ly.p1), c1, b7[1]);
+                w[g][2] = merge(prmt(W[g][1], W[g][2], ly.p0), c2, b7[2]);
+                w[g][3] = merge(prmt(W[g][1], W[g][2], ly.p1), c3, b7[3]);
+            }
+            const int t = r0 + RPI * (k0 + g);
+            if (t >= zero_from) w[g][0] = w[g][1] = w[g][2] = w[g][3] = 0u;
+        }
+#pragma unroll
+        for (int g = 0; g < G; ++g)
+            sts_v4(xb + xb_off<D>(r0 + RPI * (k0 + g), c8), w[g][0], w[g][1], w[g][2], w[g][3]);
     }
 }
 
@@ -324,18 +341,31 @@ __device__ __forceinline__ void esc_patch(uint32_t xb, const StageEsc &se, int e
 // S^T fragment of the 16-token tile at tile row r0: s0/s1 token g (queries 2t, 2t+1), s2/s3
 // token g + 8.  K A fragments by ldmatrix: lanes 8 i .. 8 i + 7 address matrix i (rows 0-7 / 8-15,
 // head dims 0-7 / 8-15 of the k-step).
-template <int D>
-__device__ __forceinline__ void qk_tile(uint32_t xb, int r0, const uint32_t (&qb)[Cfg<D>::KS][2],
-                                        int lane, float (&s)[4]) {
-    const int row = r0 + (lane & 7) + ((lane >> 3) & 1) * 8;
+template <int D, int NT>
+__device__ __forceinline__ void qk_tiles(uint32_t xb, const uint32_t (&qb)[Cfg<D>::KS][2], int lane,
+                                         float (&s)[NT][4]) {
+    // the NT tiles' MMA chains interleave (independent accumulators); ldmatrix runs ahead
+    constexpr int KS = Cfg<D>::KS, G = KS < 2 ? KS : 2;
+    const int row = (lane & 7) + ((lane >> 3) & 1) * 8;
     const uint32_t base = xb + uint32_t(row * (2 * D));
     const int y = (lane >> 4) ^ (D == 32 ? (row >> 1) & 3 : row & 7);
-    s[0] = s[1] = s[2] = s[3] = 0.f;
 #pragma unroll
-    for (int k = 0; k < Cfg<D>::KS; ++k) {
-        uint32_t a0, a1, a2, a3;
-        ldsm_x4(base + (uint32_t((2 * k) ^ y) << 4), a0, a1, a2, a3);
-        mma_bf16(s[0], s[1], s[2], s[3], a0, a1, a2, a3, qb[k][0], qb[k][1]);
+    for (int t = 0; t < NT; ++t) s[t][0] = s[t][1] = s[t][2] = s[t][3] = 0.f;
+#pragma unroll
+    for (int k0 = 0; k0 < KS; k0 += G) {
+        uint32_t a[G][NT][4];
+#pragma unroll
+        for (int g = 0; g < G; ++g)
+#pragma unroll
+            for (int t = 0; t < NT; ++t)
+                ldsm_x4(base + uint32_t(t * TT * 2 * D) + (uint32_t((2 * (k0 + g)) ^ y) << 4),
+                        a[g][t][0], a[g][t][1], a[g][t][2], a[g][t][3]);
+#pragma unroll
+        for (int g = 0; g < G; ++g)
+#pragma unroll
+            for (int t = 0; t < NT; ++t)
+                mma_bf16(s[t][0], s[t][1], s[t][2], s[t][3], a[g][t][0], a[g][t][1], a[g][t][2],
+                         a[g][t][3], qb[k0 + g][0], qb[k0 + g][1]);
     }
 }
 
@@ -346,15 +376,26 @@ template <int D>
 __device__ __forceinline__ void pv_tile(uint32_t xb, int r0, const uint32_t (&bh)[2],
                                         const uint32_t (&bm)[2], int lane,
                                         float (&acc)[Cfg<D>::KS][4]) {
+    constexpr int KS = Cfg<D>::KS, G = KS < 4 ? KS : 4;
     const int row = r0 + (lane & 7) + (lane >> 4) * 8;
     const uint32_t base = xb + uint32_t(row * (2 * D));
     const int y = ((lane >> 3) & 1) ^ (D == 32 ? (row >> 1) & 3 : row & 7);
 #pragma unroll
-    for (int m = 0; m < Cfg<D>::KS; ++m) {
-        uint32_t a0, a1, a2, a3;
-        ldsm_x4_t(base + (uint32_t((2 * m) ^ y) << 4), a0, a1, a2, a3);
-        mma_bf16(acc[m][0], acc[m][1], acc[m][2], acc[m][3], a0, a1, a2, a3, bh[0], bh[1]);
-        mma_bf16(acc[m][0], acc[m][1], acc[m][2], acc[m][3], a0, a1, a2, a3, bm[0], bm[1]);
+    for (int m0 = 0; m0 < KS; m0 += G) {
+        uint32_t a[G][4];
+#pragma unroll
+        for (int g = 0; g < G; ++g)
+            ldsm_x4_t(base + (uint32_t((2 * (m0 + g)) ^ y) << 4), a[g][0], a[g][1], a[g][2], a[g][3]);
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+            float (&c)[4] = acc[m0 + g];
+            mma_bf16(c[0], c[1], c[2], c[3], a[g][0], a[g][1], a[g][2], a[g][3], bh[0], bh[1]);
+        }
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+            float (&c)[4] = acc[m0 + g];
+            mma_bf16(c[0], c[1], c[2], c[3], a[g][0], a[g][1], a[g][2], a[g][3], bm[0], bm[1]);
+        }
     }
 }
 
@@ -604,16 +645,15 @@ __device__ __forceinline__ void worker(const AttnArgs &a, uint8_t *R, int wk, in
 
         // S^T = K Q^T for every tile of the stage
         stage_tile<D>(a, f, 0, kmode, kst, xb, lk, b7k, em, ia, ib, rows, C::TS, lane);
+        // (a stage's rows past `rows` hold stale words: their scores are dropped below)
         float s[C::SUBS][4];
+        qk_tiles<D, C::SUBS>(xb, qb, lane, s);
+        if (rows < C::TS) {
 #pragma unroll
-        for (int sub = 0; sub < C::SUBS; ++sub) {
-            if (sub * TT < rows) {
-                qk_tile<D>(xb, sub * TT, qb, lane, s[sub]);
+            for (int sub = 0; sub < C::SUBS; ++sub) {
                 const int rr = rows - sub * TT;
                 if (gi >= rr) s[sub][0] = s[sub][1] = -INFINITY;
                 if (gi + 8 >= rr) s[sub][2] = s[sub][3] = -INFINITY;
-            } else {
-                s[sub][0] = s[sub][1] = s[sub][2] = s[sub][3] = -INFINITY;
             }
         }
 
