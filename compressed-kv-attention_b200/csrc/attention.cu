@@ -331,7 +331,8 @@ __device__ __forceinline__ void esc_patch(uint32_t xb, const StageEsc &se, int e
             val = __ldg(se.gval + i);
         }
         const int second = i >= em;
-        if (TT * second + int(slot / (2 * D)) < rows)
+        // slots are even bytes inside a 16-row tile (esc_scratch_slot); anything else is skipped
+        if (slot < uint32_t(TT * 2 * D) && (slot & 1u) == 0u && TT * second + int(slot / (2 * D)) < rows)
             sts_u16(xb + uint32_t(second * TT * 2 * D) + slot, val);
     }
 }
@@ -787,6 +788,8 @@ __global__ void __launch_bounds__(32 * Cfg<D>::WARPS, 1) attn_kernel(const AttnA
     // consecutive workers on different SMs: neighbouring ranges often share a cost profile
     const int wk = warp * gridDim.x + blockIdx.x;
     if (wk >= a.n_workers) return;
+    // a step whose preparation reported an error (its escape records are incomplete) runs no work
+    if (*reinterpret_cast<volatile const int *>(a.status) != 0) return;
     const int fb0 = int(a.range_begin[wk]), fb1 = int(a.range_begin[wk + 1]);
     if (fb0 >= fb1) return;
     worker<D, BF16IN>(a, smem + warp * C::WARP_BYTES, wk, fb0, fb1, lane);

@@ -549,6 +549,8 @@ __global__ void esc_fill_kernel(const UnitDev *units, const FlatBlock *flat, int
     const int64_t w = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
     if (w >= 2 * n) return;
+    // records past the capacity were not laid out (esc_layout_kernel reported it): write none
+    if (*reinterpret_cast<volatile const int *>(status) != 0) return;
     const int64_t b = w >> 1;
     const int T = int(w & 1);
     const FlatBlock f = flat[b];

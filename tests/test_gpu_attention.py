@@ -103,6 +103,27 @@ def test_narrow_two_bit_blocks(kvx, cuda, oracle):
     assert_attention_close(g_xkv, cpu, attn_scale(q, k, v), "2-bit", seq=2048)
 
 
+@pytest.mark.parametrize("dim,n_q,seq", [(64, 7, 1000), (128, 4, 600), (256, 4, 300), (32, 8, 700)])
+def test_escape_heavy_blocks(kvx, cuda, oracle, dim, n_q, seq):
+    """4-bit blocks with ~17 % escapes: more escape words per stage than the kernel stages in
+    shared memory (it then reads them from HBM), and tiles with more than 32 escapes."""
+    rng = np.random.default_rng(dim + seq)
+    e = 120 + rng.integers(0, 18, size=(seq, dim))  # 18 exponents: 15 fit the 4-bit window
+    m = rng.integers(0, 128, size=(seq, dim))
+    sg = rng.integers(0, 2, size=(seq, dim))
+    k = ((sg << 15) | (e << 7) | m).astype(np.uint16)
+    v = S.synth_bf16(5, 1, seq, dim, S.PROFILE_V)
+    q = soften(S.synth_bf16(5, 2, n_q, dim, S.PROFILE_Q), 6)
+    kx, modes = oracle.encode(k, 128, with_modes=True)
+    assert (modes == 4).all()
+    vx = oracle.encode(v, 128)
+    g_raw = _gpu(kvx, q, k, v, seq=seq)
+    g_xkv = _gpu(kvx, q, kx=kx, vx=vx, seq=seq)
+    assert np.array_equal(_bits(g_raw), _bits(g_xkv))
+    cpu = oracle.attention(q, kx=kx, vx=vx, seq=seq)
+    assert_attention_close(g_xkv, cpu, attn_scale(q, k, v), f"escape-heavy D{dim}", seq=seq)
+
+
 def test_raw_blocks(kvx, cuda, oracle):
     """Blocks the encoder stores raw (config[4] distribution), mixed with coded blocks."""
     q, k, v = _case(256, 4, 128 * 40, seed=5, k_profile=S.PROFILE_WIDE_K)

@@ -65,3 +65,24 @@ def test_noalloc_rejects_oversize(kvx, cuda):
         kvx.attention_decode_noalloc(q, z, 4096, z, z, 4096, z, 8193, out, 4, 64, 8193 * 128)
     with pytest.raises(ValueError, match="64 queries"):
         kvx.attention_decode_noalloc(q, z, 4096, z, z, 4096, z, 1, out, 65, 64, 128)
+
+
+def test_noalloc_rejects_escape_overflow(kvx, cuda, oracle):
+    """Blobs whose escape records do not fit the fixed scratch: the call fails with the
+    invalid-argument status and says so; the next ordinary call still works."""
+    torch = cuda
+    dim, n_q, seq = 128, 4, 192 * 1024  # ~3.5M escape words: over the 3M-entry records
+    rng = np.random.default_rng(9)
+    e = 120 + rng.integers(0, 18, size=(seq, dim))  # ~17 % escapes in 4-bit blocks
+    k = ((rng.integers(0, 2, size=(seq, dim)) << 15) | (e << 7) |
+         rng.integers(0, 128, size=(seq, dim))).astype(np.uint16)
+    v = S.synth_bf16(9, 1, seq, dim, S.PROFILE_V)
+    q = S.synth_bf16(9, 2, n_q, dim, S.PROFILE_Q)
+    kx, vx = oracle.encode(k, 128), oracle.encode(v, 128)
+    kd, kidx, nb = _device_index(kvx, torch, kx, dim)
+    vd, vidx, _ = _device_index(kvx, torch, vx, dim)
+    qd = torch.from_numpy(q.view(np.int16)).cuda()
+    out = torch.zeros((n_q, dim), dtype=torch.float32, device="cuda")
+    with pytest.raises(ValueError, match="escape positions exceed the fixed scratch"):
+        kvx.attention_decode_noalloc(qd, kd, kx.size, kidx, vd, vx.size, vidx, nb, out, n_q, dim, seq)
+    test_noalloc_matches_attention_decode(kvx, cuda, oracle, [(64, 7, 3000, 15)])
