@@ -226,7 +226,7 @@ struct kvx_plan_s {
     uint16_t *esc = nullptr;  // escape records of the step's coded blocks
     int64_t *range_begin = nullptr;
     float *partials = nullptr;
-    int32_t *split_units = nullptr;
+    int4 *split_units = nullptr;  // {unit, first worker, workers} of each split unit
     int *status = nullptr;
     std::vector<void *> owned;
     ~kvx_plan_s() {
@@ -399,16 +399,16 @@ int kvx_plan_create(const kvx_unit *units, int n_units, int n_q, int dim, int bl
             e = cudaMemcpy(tb.data(), p->range_begin, tb.size() * sizeof(int64_t),
                            cudaMemcpyDeviceToHost);
     }
-    std::vector<int32_t> split;
+    std::vector<int4> split;
     if (e == cudaSuccess) {
         for (int u = 0; u < p->n_units; ++u) {
             const int t0 = worker_of_block(tb.data(), p->n_workers, ud[size_t(u)].block_begin);
             const int t1 = worker_of_block(tb.data(), p->n_workers,
                                            ud[size_t(u)].block_begin + ud[size_t(u)].n_blocks - 1);
-            if (t0 != t1) split.push_back(u);
+            if (t0 != t1) split.push_back(make_int4(u, t0, t1 - t0 + 1, 0));
         }
         if (!split.empty())
-            e = cudaMemcpy(p->split_units, split.data(), split.size() * sizeof(int32_t),
+            e = cudaMemcpy(p->split_units, split.data(), split.size() * sizeof(int4),
                            cudaMemcpyHostToDevice);
     }
     if (e != cudaSuccess) {
@@ -433,7 +433,7 @@ int kvx_plan_run_part(kvx_plan p, int part, void *stream) {
         if (p->n_split > 0) {
             CombineArgs c{};
             c.units = p->units;
-            c.split_units = p->split_units;
+            c.split = p->split_units;
             c.range_begin = p->range_begin;
             c.partials = p->partials;
             c.n_workers = p->n_workers;
@@ -463,6 +463,8 @@ int kvx_plan_check(kvx_plan p) {
 }
 
 int kvx_plan_launches(kvx_plan p) { return p ? 1 + (p->n_split > 0 ? 1 : 0) : 0; }
+
+int kvx_plan_split_units(kvx_plan p) { return p ? p->n_split : 0; }
 
 void kvx_plan_destroy(kvx_plan p) { delete p; }
 
@@ -1103,7 +1105,7 @@ extern "C" int kvx_attention_decode_noalloc(const uint16_t *q, const uint8_t *k_
     kvx_unit *d_vu = reinterpret_cast<kvx_unit *>(take(kNoAllocMaxQueries / 8 * sizeof(kvx_unit)));
     int64_t *d_begin = reinterpret_cast<int64_t *>(take(kNoAllocMaxQueries / 8 * sizeof(int64_t)));
     int64_t *d_src = reinterpret_cast<int64_t *>(take(kNoAllocMaxQueries / 8 * sizeof(int64_t)));
-    int32_t *d_split = reinterpret_cast<int32_t *>(take(kNoAllocMaxQueries / 8 * sizeof(int32_t)));
+    int4 *d_split = reinterpret_cast<int4 *>(take(kNoAllocMaxQueries / 8 * sizeof(int4)));
     FlatBlock *d_flat = reinterpret_cast<FlatBlock *>(
         take(size_t(kNoAllocMaxQueries / 8) * kNoAllocMaxBlocks * sizeof(FlatBlock)));
     int64_t *d_range = reinterpret_cast<int64_t *>(take((kNoAllocMaxWorkers + 1) * sizeof(int64_t)));
@@ -1150,12 +1152,12 @@ extern "C" int kvx_attention_decode_noalloc(const uint16_t *q, const uint8_t *k_
     // Worker ranges: one block each when they fit, else an even split of the blocks.
     std::vector<int64_t> tb(static_cast<size_t>(n_workers) + 1);
     for (int t = 0; t <= n_workers; ++t) tb[size_t(t)] = int64_t(t) * total / n_workers;
-    std::vector<int32_t> split;
+    std::vector<int4> split;
     for (int g = 0; g < groups; ++g) {
         const int t0 = worker_of_block(tb.data(), n_workers, ud[size_t(g)].block_begin);
         const int t1 = worker_of_block(tb.data(), n_workers,
                                        ud[size_t(g)].block_begin + ud[size_t(g)].n_blocks - 1);
-        if (t0 != t1) split.push_back(g);
+        if (t0 != t1) split.push_back(make_int4(g, t0, t1 - t0 + 1, 0));
     }
 
     // Every call shares the scratch and finds the previous call's contents there: the status
@@ -1167,7 +1169,7 @@ extern "C" int kvx_attention_decode_noalloc(const uint16_t *q, const uint8_t *k_
     KVX_CUDA(cudaMemcpyAsync(d_src, srcs.data(), srcs.size() * sizeof(int64_t), cudaMemcpyHostToDevice, s));
     KVX_CUDA(cudaMemcpyAsync(d_range, tb.data(), tb.size() * sizeof(int64_t), cudaMemcpyHostToDevice, s));
     if (!split.empty())
-        KVX_CUDA(cudaMemcpyAsync(d_split, split.data(), split.size() * sizeof(int32_t),
+        KVX_CUDA(cudaMemcpyAsync(d_split, split.data(), split.size() * sizeof(int4),
                                  cudaMemcpyHostToDevice, s));
     KVX_CUDA(launch_build_flat(d_vu, d_begin, d_src, groups, dim, kDefaultBlock, false, d_flat,
                                status, s));
@@ -1186,7 +1188,7 @@ extern "C" int kvx_attention_decode_noalloc(const uint16_t *q, const uint8_t *k_
     if (!split.empty()) {
         CombineArgs c{};
         c.units = d_units;
-        c.split_units = d_split;
+        c.split = d_split;
         c.range_begin = d_range;
         c.partials = d_partials;
         c.n_workers = n_workers;

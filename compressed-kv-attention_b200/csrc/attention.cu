@@ -810,13 +810,12 @@ __global__ void __launch_bounds__(kCombineThreads) combine_kernel(const CombineA
     constexpr int S = kCombineThreads / D;  // segment slices summed in parallel
     __shared__ float e[kMaxSegments];
     __shared__ float red[kCombineThreads];
-    const int u = a.split_units[blockIdx.x];
+    const int4 sp = a.split[blockIdx.x];
     const int g = blockIdx.y;
-    const UnitDev unit = a.units[u];
+    const UnitDev unit = a.units[sp.x];
     if (g >= unit.n_q) return;
-    const int t0 = worker_of_block(a.range_begin, a.n_workers, unit.block_begin);
-    const int t1 = worker_of_block(a.range_begin, a.n_workers, unit.block_begin + unit.n_blocks - 1);
-    const int nt = min(t1 - t0 + 1, kMaxSegments);
+    const int t0 = sp.y;  // first worker of the unit and the number of workers (host-computed)
+    const int nt = min(sp.z, kMaxSegments);
     const int ps = partial_stride(D);
     auto part = [&](int i) {
         const int t = t0 + i;

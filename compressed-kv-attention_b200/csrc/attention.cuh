@@ -91,7 +91,8 @@ struct AttnArgs {
 
 struct CombineArgs {
     const UnitDev *units;
-    const int32_t *split_units;   // units whose blocks span several workers
+    const int4 *split;            // units whose blocks span several workers:
+                                  // {unit, first worker, number of workers, 0}
     const int64_t *range_begin;    // [n_workers + 1]
     const float *partials;
     int n_workers;

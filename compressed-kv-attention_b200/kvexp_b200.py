@@ -104,6 +104,7 @@ _plan_run = _sig("kvx_plan_run", C.c_int, [_vp, _vp])
 _plan_run_part = _sig("kvx_plan_run_part", C.c_int, [_vp, C.c_int, _vp])
 _plan_check = _sig("kvx_plan_check", C.c_int, [_vp])
 _plan_launches = _sig("kvx_plan_launches", C.c_int, [_vp])
+_plan_split = _sig("kvx_plan_split_units", C.c_int, [_vp])
 _plan_destroy = _sig("kvx_plan_destroy", None, [_vp])
 _enc_bounds = _sig("kvx_encode_batch_bounds", C.c_int,
                    [C.c_int, C.c_int, C.c_int, C.c_int, C.POINTER(_sz), C.POINTER(_sz)])
@@ -123,7 +124,7 @@ _fold = _sig("kvx_fold_shards", C.c_int, [_vp, C.c_int, C.c_int, C.c_int, _vp, _
 EXPORTED = [
     "kvx_last_error", "kvx_version", "kvx_device_info", "kvx_attention_decode",
     "kvx_attention_decode_units", "kvx_encode_bound", "kvx_encode_bf16", "kvx_decode_bf16",
-    "kvx_xkv_index", "kvx_plan_create", "kvx_plan_run", "kvx_plan_run_part", "kvx_plan_check", "kvx_plan_launches",
+    "kvx_xkv_index", "kvx_plan_create", "kvx_plan_run", "kvx_plan_run_part", "kvx_plan_check", "kvx_plan_launches", "kvx_plan_split_units",
     "kvx_plan_destroy", "kvx_encode_batch_bounds", "kvx_encode_batch", "kvx_cache_append",
     "kvx_synth_bf16", "kvx_hbm_read_probe", "kvx_attention_decode_noalloc", "kvx_fold_shards",
 ]
@@ -273,7 +274,7 @@ class Plan:
 
     @property
     def n_split(self) -> int:
-        return self.launches - 1
+        return int(_plan_split(self._h))
 
     def check(self):
         _check(_plan_check(self._h))
