@@ -405,7 +405,9 @@ int kvx_plan_create(const kvx_unit *units, int n_units, int n_q, int dim, int bl
             const int t0 = worker_of_block(tb.data(), p->n_workers, ud[size_t(u)].block_begin);
             const int t1 = worker_of_block(tb.data(), p->n_workers,
                                            ud[size_t(u)].block_begin + ud[size_t(u)].n_blocks - 1);
-            if (t0 != t1) split.push_back(make_int4(u, t0, t1 - t0 + 1, 0));
+            if (t0 != t1)
+                split.push_back(make_int4(u, t0, t1 - t0 + 1,
+                                          tb[size_t(t0)] < ud[size_t(u)].block_begin ? 1 : 0));
         }
         if (!split.empty())
             e = cudaMemcpy(p->split_units, split.data(), split.size() * sizeof(int4),
@@ -1157,7 +1159,8 @@ extern "C" int kvx_attention_decode_noalloc(const uint16_t *q, const uint8_t *k_
         const int t0 = worker_of_block(tb.data(), n_workers, ud[size_t(g)].block_begin);
         const int t1 = worker_of_block(tb.data(), n_workers,
                                        ud[size_t(g)].block_begin + ud[size_t(g)].n_blocks - 1);
-        if (t0 != t1) split.push_back(make_int4(g, t0, t1 - t0 + 1, 0));
+        if (t0 != t1)
+            split.push_back(make_int4(g, t0, t1 - t0 + 1, tb[size_t(t0)] < ud[size_t(g)].block_begin ? 1 : 0));
     }
 
     // Every call shares the scratch and finds the previous call's contents there: the status

@@ -817,10 +817,11 @@ __global__ void __launch_bounds__(kCombineThreads) combine_kernel(const CombineA
     const int t0 = sp.y;  // first worker of the unit and the number of workers (host-computed)
     const int nt = min(sp.z, kMaxSegments);
     const int ps = partial_stride(D);
+    // only the unit's first worker can hold it in its second partial slot (its range began in an
+    // earlier unit); the host worked that out (sp.w)
     auto part = [&](int i) {
         const int t = t0 + i;
-        const int slot = (a.range_begin[t] >= unit.block_begin) ? 0 : 1;
-        return a.partials + (size_t(t) * 2 + slot) * ps;
+        return a.partials + (size_t(t) * 2 + (i == 0 ? sp.w : 0)) * ps;
     };
     const int tid = threadIdx.x;
     float mx = -INFINITY;

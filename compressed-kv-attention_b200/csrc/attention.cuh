@@ -91,8 +91,8 @@ struct AttnArgs {
 
 struct CombineArgs {
     const UnitDev *units;
-    const int4 *split;            // units whose blocks span several workers:
-                                  // {unit, first worker, number of workers, 0}
+    const int4 *split;            // units whose blocks span several workers: {unit, first
+                                  // worker, number of workers, partial slot of the first}
     const int64_t *range_begin;    // [n_workers + 1]
     const float *partials;
     int n_workers;
