@@ -223,6 +223,7 @@ struct kvx_plan_s {
     cudaStream_t s = nullptr;
     UnitDev *units = nullptr;
     FlatBlock *flat = nullptr;
+    BlockDesc *desc = nullptr;  // per flat block, for the attention kernel
     uint16_t *esc = nullptr;  // escape records of the step's coded blocks
     int64_t *range_begin = nullptr;
     float *partials = nullptr;
@@ -347,6 +348,7 @@ int kvx_plan_create(const kvx_unit *units, int n_units, int n_q, int dim, int bl
     cudaError_t e = cudaSuccess;
     if ((e = plan_alloc(p, &p->units, ud.size())) != cudaSuccess ||
         (e = plan_alloc(p, &p->flat, size_t(total))) != cudaSuccess ||
+        (e = plan_alloc(p, &p->desc, size_t(total))) != cudaSuccess ||
         (e = plan_alloc(p, &p->range_begin, tb.size())) != cudaSuccess ||
         (e = plan_alloc(p, &p->partials, size_t(p->n_workers) * 2 * partial_stride(dim))) != cudaSuccess ||
         (e = plan_alloc(p, &p->split_units, ud.size())) != cudaSuccess ||
@@ -378,6 +380,7 @@ int kvx_plan_create(const kvx_unit *units, int n_units, int n_q, int dim, int bl
     if (e == cudaSuccess) e = plan_alloc(p, &p->esc, size_t(esc_total));
     if (e == cudaSuccess && esc_total > 0)
         e = launch_esc_fill(p->units, p->flat, total, dim, p->esc, esc_total, p->status, nullptr);
+    if (e == cudaSuccess) e = launch_block_desc(p->units, p->flat, p->esc, total, dim, bf16, p->desc, nullptr);
     if (e == cudaSuccess) e = cudaDeviceSynchronize();
     if (e != cudaSuccess) {
         delete p;
@@ -447,6 +450,7 @@ int kvx_plan_run_part(kvx_plan p, int part, void *stream) {
     AttnArgs a{};
     a.units = p->units;
     a.flat = p->flat;
+    a.desc = p->desc;
     a.esc = p->esc;
     a.range_begin = p->range_begin;
     a.partials = p->partials;
@@ -1014,12 +1018,12 @@ extern "C" int kvx_fold_shards(const float *parts, int n_parts, int n_rows, int 
 // running: serving engines that reserve the device's memory for their KV-cache pool at start-up
 // and treat any later cudaMalloc as a failure, and decode loops that cannot afford the
 // device-wide synchronisation that cudaFree implies.  All of its scratch (the flat block list,
-// worker ranges, partial softmax states and the error word) lives in the file-scope device array
+// block descriptors, worker ranges, partial softmax states and the error word) lives in the file-scope device array
 // below, which every device that loads this library holds until the process exits.
 
 namespace kvx {
 namespace {
-constexpr size_t kNoAllocScratchBytes = size_t(16) << 20;  // 16 MiB per device
+constexpr size_t kNoAllocScratchBytes = size_t(24) << 20;  // 24 MiB per device
 constexpr size_t kNoAllocEscEntries = size_t(3) << 20;      // escape record entries (6 MiB)
 constexpr int kNoAllocMaxBlocks = 8192;                   // XKV blocks per tensor
 constexpr int kNoAllocMaxQueries = 64;                    // queries per call (8 groups of 8)
@@ -1110,6 +1114,8 @@ extern "C" int kvx_attention_decode_noalloc(const uint16_t *q, const uint8_t *k_
     int4 *d_split = reinterpret_cast<int4 *>(take(kNoAllocMaxQueries / 8 * sizeof(int4)));
     FlatBlock *d_flat = reinterpret_cast<FlatBlock *>(
         take(size_t(kNoAllocMaxQueries / 8) * kNoAllocMaxBlocks * sizeof(FlatBlock)));
+    BlockDesc *d_desc = reinterpret_cast<BlockDesc *>(
+        take(size_t(kNoAllocMaxQueries / 8) * kNoAllocMaxBlocks * sizeof(BlockDesc)));
     int64_t *d_range = reinterpret_cast<int64_t *>(take((kNoAllocMaxWorkers + 1) * sizeof(int64_t)));
     unsigned long long *d_esc_total =
         reinterpret_cast<unsigned long long *>(take(sizeof(unsigned long long)));
@@ -1178,9 +1184,11 @@ extern "C" int kvx_attention_decode_noalloc(const uint16_t *q, const uint8_t *k_
                                status, s));
     KVX_CUDA(launch_esc_layout(d_flat, total, d_esc_total, kNoAllocEscEntries, status, s));
     KVX_CUDA(launch_esc_fill(d_units, d_flat, total, dim, d_esc, kNoAllocEscEntries, status, s));
+    KVX_CUDA(launch_block_desc(d_units, d_flat, d_esc, total, dim, false, d_desc, s));
     AttnArgs a{};
     a.units = d_units;
     a.flat = d_flat;
+    a.desc = d_desc;
     a.esc = d_esc;
     a.range_begin = d_range;
     a.partials = d_partials;

@@ -78,16 +78,17 @@ template <int D> struct Cfg {
     static constexpr int SLOT = 2 * TR;  // K stage | V stage
     static constexpr int NSTAGE = D <= 32 ? 3 : 2;
     static constexpr int BASE = round16(D + 32);  // one block's base exponents (+ alignment slack)
-    // Per-block meta slot: K base | V base | the block's FlatBlock | its escape count headers.
-    static constexpr int M_FB = 2 * BASE;
-    static constexpr int M_EM = M_FB + 32;
-    static constexpr int MSLOT = M_EM + 64;
-    static constexpr int XB = TS * 2 * D;  // the BF16 tile of one tensor's stage
-    // per-warp region: ring | meta x2 | tile | one mbarrier per ring slot
+    static constexpr int MSLOT = 2 * BASE;        // per-block meta slot: K base | V base
+    static constexpr int XB = TS * 2 * D;         // the BF16 tile of one tensor's stage
+    static constexpr int NDESC = 4;               // block descriptor ring
+    // per-warp region: ring | meta x2 | tile | descriptors | one mbarrier per ring slot and
+    // per descriptor
     static constexpr int W_META = NSTAGE * SLOT;
     static constexpr int W_XB = W_META + 2 * MSLOT;
-    static constexpr int W_BAR = W_XB + XB;
-    static constexpr int WARP_BYTES = (W_BAR + 8 * NSTAGE + 127) & ~127;
+    static constexpr int W_DESC = W_XB + XB;
+    static constexpr int W_BAR = W_DESC + NDESC * int(sizeof(BlockDesc));
+    static constexpr int W_DBAR = W_BAR + 8 * NSTAGE;
+    static constexpr int WARP_BYTES = (W_DBAR + 8 * NDESC + 127) & ~127;
     static constexpr int MAXW = D <= 32 ? 16 : KVX_MAXWARPS;
     static constexpr int WARPS = cmin(MAXW, 232448 / WARP_BYTES);
     static_assert(WARPS >= 1, "worker does not fit in shared memory");
@@ -123,17 +124,18 @@ struct Sections {
     const uint8_t *esc;    // coded: escape words
 };
 
+// blk: the block's header (BF16 input: its first row).
 template <int D, bool BF16IN>
-__device__ __forceinline__ Sections sections(const uint8_t *blob, uint32_t off, int mode, int n_tok) {
+__device__ __forceinline__ Sections sections(const uint8_t *blk, int mode, int n_tok) {
     Sections s;
     if (BF16IN) {
-        s.rows = blob + size_t(off) * (2 * D);
+        s.rows = blk;
         s.codes = s.esc = nullptr;
     } else if (mode == 0) {
-        s.rows = blob + off + kHeaderBytes;
+        s.rows = blk + kHeaderBytes;
         s.codes = s.esc = nullptr;
     } else {
-        s.rows = blob + off + kHeaderBytes + D;
+        s.rows = blk + kHeaderBytes + D;
         s.codes = s.rows + size_t(n_tok) * D;
         s.esc = s.codes + size_t(n_tok) * D * mode / 8;
     }
@@ -142,31 +144,22 @@ __device__ __forceinline__ Sections sections(const uint8_t *blob, uint32_t off, 
 
 // ---- escape records ----------------------------------------------------------------------------
 
-// Lane l < 16 holds entry l of the block's K count header, lane 16 + l entry l of V's (0 without
-// a record): e(i) = escape words of tokens [0, 16 i).
-__device__ __forceinline__ uint32_t load_em(const uint16_t *esc, const FlatBlock &f, int lane) {
-    const bool v = lane >= 16;
-    const int mode = v ? f.v_mode : f.k_mode;
-    const int n = v ? f.v_nesc : f.k_nesc;
-    const uint32_t rec = v ? f.v_rec : f.k_rec;
-    return (mode != 0 && n != 0) ? uint32_t(__ldg(esc + rec + (lane & 15))) : 0u;
-}
 // e(i) of tensor T (0 K, 1 V), i = 0..16; every lane of the warp calls it.
 __device__ __forceinline__ int esc_at(uint32_t em, int T, int i) {
     const uint32_t v = __shfl_sync(FULL, em, (T << 4) + ((i + 15) & 15));
     return i == 0 ? 0 : int(v);
 }
 
-// e(i) of tensor T from a meta slot's copy of the headers.
-__device__ __forceinline__ int esc_ms(const uint8_t *em, int T, int i) {
-    return i == 0 ? 0 : int(*reinterpret_cast<const uint16_t *>(em + 2 * (16 * T + i - 1)));
+// e(i) of tensor T from a block descriptor's headers.
+__device__ __forceinline__ int esc_ms(const BlockDesc &bd, int T, int i) {
+    return i == 0 ? 0 : int(bd.em[T][i - 1]);
 }
 
-// Byte offset inside a 16-byte line of escape word i of a coded block (the blob is 16-byte
-// aligned) and of its position in the escape records (16-byte aligned allocation).
+// Byte offset inside a 16-byte line of escape word i of a coded block (blk: its header's address)
+// and of its position in the escape records (16-byte aligned allocation).
 template <int D>
-__device__ __forceinline__ uint32_t esc_word_line(uint32_t off, int n_tok, int mode, int i) {
-    return (off + uint32_t(kHeaderBytes + D) + uint32_t(n_tok * D) + uint32_t(n_tok * D * mode / 8) +
+__device__ __forceinline__ uint32_t esc_word_line(uint64_t blk, int n_tok, int mode, int i) {
+    return (uint32_t(blk) + uint32_t(kHeaderBytes + D) + uint32_t(n_tok * D) + uint32_t(n_tok * D * mode / 8) +
             2u * uint32_t(i)) & 15u;
 }
 __device__ __forceinline__ uint32_t esc_pos_line(uint32_t rec, int i) {
@@ -241,69 +234,122 @@ template <int D> __device__ __forceinline__ uint32_t xb_off(int t, int c8) {
 
 // ---- stage decode ------------------------------------------------------------------------------
 
+// Tile addresses of this lane's chunks: chunk j of a stage (row r0 + RPI j, head dims 8 c8 ..
+// 8 c8 + 7) is stored at st[j % NB] + j RPI 2 D.  The swizzle of row t depends on t mod 8 (D 32:
+// on t / 2 mod 4), so NB bases cover every chunk; for D 256 (NB 8) the base is computed per chunk.
+template <int D> struct StoreMap {
+    static constexpr int RPI = 32 / Cfg<D>::C8;
+    static constexpr int NB = D == 32 ? 1 : 8 / RPI;
+    static constexpr int NR = NB <= 4 ? NB : 1;  // bases held in registers
+    uint32_t st[NR];
+    uint32_t row, c16;  // D 256: xb + r0 2 D and c8 << 4
+    __device__ __forceinline__ void init(uint32_t xb, int lane) {
+        const int c8 = lane % Cfg<D>::C8, r0 = lane / Cfg<D>::C8;
+        row = xb + uint32_t(r0 * (2 * D));
+        c16 = uint32_t(c8) << 4;
+#pragma unroll
+        for (int k = 0; k < NR; ++k) st[k] = xb + xb_off<D>(r0 + RPI * k, c8);
+    }
+    // j is a constant after unrolling
+    __device__ __forceinline__ uint32_t at(int j) const {
+        if constexpr (NB <= 4) return st[j % NB] + uint32_t((j / NB) * NB * RPI * 2 * D);
+        else return row + uint32_t(j * RPI * 2 * D) + (c16 ^ uint32_t((j & 7) << 4));
+    }
+};
+
+// Loads of chunk steps [K0, K0 + G) of one tensor's stage: row words W, residual code words X.
+template <int D, int MODE, int G, int K0>
+__device__ __forceinline__ void load_chunks(uint32_t qr, uint32_t qc, uint32_t (&W)[G][MODE == 0 ? 5 : 3],
+                                            uint32_t (&X)[G][2]) {
+    constexpr int RPI = 32 / Cfg<D>::C8;
+    constexpr int RB = MODE == 0 ? 2 * D : D;  // row bytes
+    constexpr int CB = D * MODE / 8;           // residual bytes per row
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+        const uint32_t q = qr + uint32_t((K0 + g) * RPI * RB);
+#pragma unroll
+        for (int i = 0; i < (MODE == 0 ? 5 : 3); ++i) W[g][i] = lds_u32(q + 4u * i);
+        if constexpr (MODE != 0) {
+            const uint32_t c = qc + uint32_t((K0 + g) * RPI * CB);
+            X[g][0] = lds_u32(c);
+            if constexpr (MODE == 4) X[g][1] = lds_u32(c + 4u);
+        }
+    }
+}
+
+// The four BF16 pair words of one chunk from its loaded words.
+template <int MODE>
+__device__ __forceinline__ void build_chunk(const Lay &ly, const uint32_t (&b7)[4],
+                                            const uint32_t (&W)[MODE == 0 ? 5 : 3], const uint32_t (&X)[2],
+                                            uint32_t (&w)[4]) {
+    if constexpr (MODE == 0) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) w[i] = prmt(W[i], W[i + 1], ly.w);
+    } else {
+        uint32_t c0, c1, c2, c3;
+        if constexpr (MODE == 4) {
+            const uint32_t x = prmt(X[0], X[1], ly.cs);
+            const uint32_t lo = x & 0x0F0F0F0Fu, hi = (x >> 4) & 0x0F0F0F0Fu;
+            c0 = prmt(lo, hi, sel_code(0));
+            c1 = prmt(lo, hi, sel_code(1));
+            c2 = prmt(lo, hi, sel_code(2));
+            c3 = prmt(lo, hi, sel_code(3));
+        } else {  // 8 residuals of 2 bits in the low 16 bits of x
+            const uint32_t x = prmt(X[0], 0u, ly.cs);
+            const uint32_t ev = x & 0x3333u, od = (x >> 2) & 0x3333u;
+            const uint32_t el = ev & 0x0F0Fu, eh = (ev >> 4) & 0x0F0Fu;
+            const uint32_t ol = od & 0x0F0Fu, oh = (od >> 4) & 0x0F0Fu;
+            c0 = prmt(el, ol, sel_code(0));
+            c1 = prmt(eh, oh, sel_code(0));
+            c2 = prmt(el, ol, sel_code(1));
+            c3 = prmt(eh, oh, sel_code(1));
+        }
+        w[0] = merge(prmt(W[0], W[1], ly.p0), c0, b7[0]);
+        w[1] = merge(prmt(W[0], W[1], ly.p1), c1, b7[1]);
+        w[2] = merge(prmt(W[1], W[2], ly.p0), c2, b7[2]);
+        w[3] = merge(prmt(W[1], W[2], ly.p1), c3, b7[3]);
+    }
+}
+
+// Chunk steps [K0, NIT) in groups of G: the loads of the next group are issued before the
+// current group's arithmetic and stores (the shared-memory accesses keep their written order).
+template <int D, int MODE, int G, int K0>
+__device__ __forceinline__ void decode_groups(uint32_t qr, uint32_t qc, const Lay &ly, const uint32_t (&b7)[4],
+                                              const StoreMap<D> &sm, uint32_t (&W)[G][MODE == 0 ? 5 : 3],
+                                              uint32_t (&X)[G][2]) {
+    constexpr int NIT = Cfg<D>::NIT;
+    uint32_t Wn[G][MODE == 0 ? 5 : 3], Xn[G][2];
+    if constexpr (K0 + G < NIT) load_chunks<D, MODE, G, K0 + G>(qr, qc, Wn, Xn);
+    uint32_t w[G][4];
+#pragma unroll
+    for (int g = 0; g < G; ++g) build_chunk<MODE>(ly, b7, W[g], X[g], w[g]);
+#pragma unroll
+    for (int g = 0; g < G; ++g) sts_v4(sm.at(K0 + g), w[g][0], w[g][1], w[g][2], w[g][3]);
+    if constexpr (K0 + G < NIT) decode_groups<D, MODE, G, K0 + G>(qr, qc, ly, b7, sm, Wn, Xn);
+}
+
 // Rebuild this lane's chunks of one tensor's stage into the tile (MODE 4 / 2 coded, 0 raw BF16).
-// Rows at or past `zero_from` are stored as zeros (V: P is 0 there, V must be finite).  The
-// shared-memory accesses are ordered as written, so the chunks go in groups of G: all loads of the
-// group, then the arithmetic, then the stores.
 template <int D, int MODE>
-__device__ __forceinline__ void decode_stage(uint32_t stage, uint32_t xb, const Lay &ly,
-                                             const uint32_t (&b7)[4], int lane, int zero_from) {
+__device__ __forceinline__ void decode_stage(uint32_t stage, const Lay &ly, const uint32_t (&b7)[4],
+                                             const StoreMap<D> &sm, int lane) {
     using C = Cfg<D>;
-    constexpr int RPI = 32 / C::C8;  // rows per chunk step
+    // chunk steps per group (two groups' loads are live at a time)
     constexpr int G = C::NIT < 4 ? C::NIT : 4;
-    constexpr int NW = MODE == 0 ? 5 : 3;  // row words per chunk
-    const int c8 = lane % C::C8, r0 = lane / C::C8;
-#pragma unroll 1
-    for (int k0 = 0; k0 < C::NIT; k0 += G) {
-        uint32_t W[G][NW], X[G][2];
-#pragma unroll
-        for (int g = 0; g < G; ++g) {
-            const int t = r0 + RPI * (k0 + g);
-            const uint32_t q = stage + ly.rows + uint32_t(t * (MODE == 0 ? 2 * D : D));
-#pragma unroll
-            for (int i = 0; i < NW; ++i) W[g][i] = lds_u32(q + 4u * i);
-            if (MODE != 0) {
-                const uint32_t qc = stage + ly.codes + uint32_t(t * (D * (MODE == 0 ? 4 : MODE) / 8));
-                X[g][0] = lds_u32(qc);
-                if (MODE == 4) X[g][1] = lds_u32(qc + 4u);
-            }
-        }
-        uint32_t w[G][4];
-#pragma unroll
-        for (int g = 0; g < G; ++g) {
-            if constexpr (MODE == 0) {
-#pragma unroll
-                for (int i = 0; i < 4; ++i) w[g][i] = prmt(W[g][i], W[g][i + 1], ly.w);
-            } else {
-                uint32_t c0, c1, c2, c3;
-                if constexpr (MODE == 4) {
-                    const uint32_t x = prmt(X[g][0], X[g][1], ly.cs);
-                    const uint32_t lo = x & 0x0F0F0F0Fu, hi = (x >> 4) & 0x0F0F0F0Fu;
-                    c0 = prmt(lo, hi, sel_code(0));
-                    c1 = prmt(lo, hi, sel_code(1));
-                    c2 = prmt(lo, hi, sel_code(2));
-                    c3 = prmt(lo, hi, sel_code(3));
-                } else {  // 8 residuals of 2 bits in the low 16 bits of x
-                    const uint32_t x = prmt(X[g][0], 0u, ly.cs);
-                    const uint32_t ev = x & 0x3333u, od = (x >> 2) & 0x3333u;
-                    const uint32_t el = ev & 0x0F0Fu, eh = (ev >> 4) & 0x0F0Fu;
-                    const uint32_t ol = od & 0x0F0Fu, oh = (od >> 4) & 0x0F0Fu;
-                    c0 = prmt(el, ol, sel_code(0));
-                    c1 = prmt(eh, oh, sel_code(0));
-                    c2 = prmt(el, ol, sel_code(1));
-                    c3 = prmt(eh, oh, sel_code(1));
-                }
-                w[g][0] = merge(prmt(W[g][0], W[g][1], ly.p0), c0, b7[0]);
-                w[g][1] = merge(prmt(W[g][0], W[g][1], ly.p1), c1, b7[1]);
-                w[g][2] = merge(prmt(W[g][1], W[g][2], ly.p0), c2, b7[2]);
-                w[g][3] = merge(prmt(W[g][1], W[g][2], ly.p1), c3, b7[3]);
-            }
-            const int t = r0 + RPI * (k0 + g);
-            if (t >= zero_from) w[g][0] = w[g][1] = w[g][2] = w[g][3] = 0u;
-        }
-#pragma unroll
-        for (int g = 0; g < G; ++g)
-            sts_v4(xb + xb_off<D>(r0 + RPI * (k0 + g), c8), w[g][0], w[g][1], w[g][2], w[g][3]);
+    const int r0 = lane / C::C8;
+    const uint32_t qr = stage + ly.rows + uint32_t(r0 * (MODE == 0 ? 2 * D : D));
+    const uint32_t qc = stage + ly.codes + uint32_t(r0 * (D * MODE / 8));
+    uint32_t W[G][MODE == 0 ? 5 : 3], X[G][2];
+    load_chunks<D, MODE, G, 0>(qr, qc, W, X);
+    decode_groups<D, MODE, G, 0>(qr, qc, ly, b7, sm, W, X);
+}
+
+// Zero this lane's chunks of tile rows at or past `from` (V rows past the block's valid tokens:
+// P is 0 there and V must be finite).
+template <int D, int J = 0>
+__device__ __forceinline__ void zero_rows(const StoreMap<D> &sm, int from, int lane) {
+    if constexpr (J < Cfg<D>::NIT) {
+        if (lane / Cfg<D>::C8 + J * StoreMap<D>::RPI >= from) sts_v4(sm.at(J), 0u, 0u, 0u, 0u);
+        zero_rows<D, J + 1>(sm, from, lane);
     }
 }
 
@@ -416,142 +462,154 @@ __device__ __forceinline__ void load_q(const uint16_t *q, int n_q, int stride,
 
 // ---- the worker -------------------------------------------------------------------------------
 
-// Walks the worker's flat blocks with one block of prefetch (flat indices fit 32 bits: the plan
-// refuses larger steps), together with this lane's entry of each block's escape count headers.
-struct Walker {
-    int fb, fb1;
-    FlatBlock cur, nxt;
-    uint32_t em, emn;
-    __device__ __forceinline__ void init(const AttnArgs &a, int b0, int b1, int lane) {
-        fb = b0;
-        fb1 = b1;
-        cur = load_flat(a.flat, fb);
-        em = load_em(a.esc, cur, lane);
-        if (fb + 1 < fb1) {
-            nxt = load_flat(a.flat, fb + 1);
-            emn = load_em(a.esc, nxt, lane);
-        }
-    }
-    __device__ __forceinline__ void next(const AttnArgs &a, int lane) {
-        ++fb;
-        if (fb < fb1) {
-            cur = nxt;
-            em = emn;
-            if (fb + 1 < fb1) {
-                nxt = load_flat(a.flat, fb + 1);
-                emn = load_em(a.esc, nxt, lane);
-            }
-        }
-    }
-};
+__device__ __forceinline__ const uint8_t *desc_ptr(uint64_t a) { return reinterpret_cast<const uint8_t *>(a); }
 
-// Copy side of the worker's ring.  At a block's first stage it also leaves the block's FlatBlock
-// and escape count headers in the block's meta slot for the consumer side.
+// Copy side of the worker's ring.  Block descriptors arrive in a ring of NDESC slots, fetched one
+// block ahead of their first stage (block fb0 + i uses slot i % NDESC); the producer reads a block's descriptor when
+// it issues the block's first stage, the consumer while it works on the block.
 template <int D, bool BF16IN> struct Producer {
     using C = Cfg<D>;
-    Walker w;
+    int fb, fb0, fb1;  // next block to start; the worker's range
+    int pf;            // next block whose descriptor is fetched
+    int dwait;         // next block whose descriptor is waited for
     int tile = 0, stage = 0, bseq = 0;
-    const uint8_t *kb = nullptr, *vb = nullptr;  // the current unit's K and V blobs
+    int valid = 0;     // tokens of the block being issued
+    uint32_t em = 0u;  // lane l: entry l % 16 of its K (l < 16) / V count header
+    // This lane's piece of every stage of the current block.  Lane 4 T + j (j < 4) copies piece j
+    // of tensor T: rows (j 0) and residual codes (j 1) are [src + t0 stride, + n stride) for the
+    // stage's tokens [t0, t0 + n); escape words (j 2) and their positions (j 3) are the stage's
+    // escapes [e0, e1) at src + 2 e0, when they fit the slot.  Lanes 8 and 9 copy the K and V base
+    // exponents (D bytes at src) with the block's first stage.  dst: offset in the ring slot or
+    // (base exponents) in the meta slot.
+    const uint8_t *src = nullptr;
+    uint32_t stride = 0, dst = 0;
+    int kind = 0;  // 0 none, 1 strided, 2 escapes, 3 base exponents
+
+    // Fetch descriptors up to the block after the next one to start (lane 0 issues).  A block
+    // starts when the consumer is at most one block behind, so the slot a fetch overwrites (its
+    // block four earlier) is no longer read.
+    __device__ __forceinline__ void fetch(const AttnArgs &a, uint8_t *R, int lane) {
+        while (pf < fb1 && pf <= fb + 1) {
+            const int i = (pf - fb0) % C::NDESC;
+            const uint32_t bar = smem_u32(R + C::W_DBAR + 8 * i);
+            if (lane == 0) {
+                mbar_arrive_expect_tx(bar, uint32_t(sizeof(BlockDesc)));
+                bulk_g2s(smem_u32(R + C::W_DESC + i * int(sizeof(BlockDesc))),
+                         reinterpret_cast<const uint8_t *>(a.desc + pf), uint32_t(sizeof(BlockDesc)), bar);
+            }
+            ++pf;
+        }
+    }
+
+    __device__ __forceinline__ bool start_block(const AttnArgs &a, uint8_t *R, int lane) {
+        const int i = (fb - fb0) % C::NDESC;
+        if (!mbar_wait_bounded(smem_u32(R + C::W_DBAR + 8 * i), ((fb - fb0) / C::NDESC) & 1, kStageWaitUs))
+            return false;
+        dwait = fb + 1;
+        const BlockDesc &bd = *reinterpret_cast<const BlockDesc *>(R + C::W_DESC + i * int(sizeof(BlockDesc)));
+        const int T = (lane >> 2) & 1, j = lane & 3;
+        const int km = BF16IN ? 0 : bd.k_mode, vm = BF16IN ? 0 : bd.v_mode;
+        const int mode = T ? vm : km;
+        const uint8_t *blk = desc_ptr(T ? bd.v : bd.k);
+        const Sections sc = sections<D, BF16IN>(blk, mode, bd.n_tok);
+        valid = bd.valid;
+        em = bd.em[lane >> 4][lane & 15];
+        src = nullptr;
+        stride = 0;
+        kind = 0;
+        dst = uint32_t(T * C::TR);
+        if (lane < 8) {
+            if (j == 0) {
+                src = sc.rows;
+                stride = (BF16IN || mode == 0) ? 2 * D : D;
+                kind = 1;
+            } else if (!BF16IN && mode != 0) {
+                if (j == 1) {
+                    src = sc.codes;
+                    stride = uint32_t(D * mode / 8);
+                    dst += C::CODE_OFF;
+                    kind = 1;
+                } else {
+                    src = j == 2 ? sc.esc
+                                 : reinterpret_cast<const uint8_t *>(a.esc + (T ? bd.v_rec : bd.k_rec) + kEscRecHead);
+                    dst += j == 2 ? C::EV_OFF : C::EP_OFF;
+                    kind = 2;
+                }
+            }
+        } else if (!BF16IN && lane < 10 && (lane == 8 ? km : vm) != 0) {
+            src = desc_ptr(lane == 8 ? bd.k : bd.v) + kHeaderBytes;
+            dst = uint32_t((lane - 8) * C::BASE);
+            kind = 3;
+        }
+        return true;
+    }
 
     // Issue stages while a ring slot is free; a block start waits until the consumer is at most
     // one block behind, so a meta slot is never overwritten while in use.  The slot's previous
     // stage was read by the whole warp before this call (__syncwarp at the end of every stage).
-    // The pieces of a stage go out in parallel: lane 4 T + j copies piece j of tensor T (rows,
-    // residual codes, escape words, their positions), lanes 8 and 9 a new block's K and V base
-    // exponents; lane 0 first tells the slot's barrier how many bytes to expect.
-    __device__ __forceinline__ void produce(const AttnArgs &a, uint8_t *ring, uint8_t *metas,
-                                            uint8_t *bars, int c_stage, int c_fb, int lane) {
-        while (w.fb < w.fb1 && stage - c_stage < C::NSTAGE) {
-            if (tile == 0 && w.fb - c_fb >= 2) break;
-            const FlatBlock &f = w.cur;
-            const int km = BF16IN ? 0 : f.k_mode, vm = BF16IN ? 0 : f.v_mode;
-            const uint32_t bar = smem_u32(bars + 8 * (stage % C::NSTAGE));
-            uint8_t *ms = metas + (bseq & 1) * C::MSLOT;
-            if (tile == 0) {
-                const UnitDev *U = a.units + f.unit;
-                kb = U->k;
-                vb = U->v;
-                if (lane == 0) {
-                    const uint4 *src = reinterpret_cast<const uint4 *>(&f);
-                    reinterpret_cast<uint4 *>(ms + C::M_FB)[0] = src[0];
-                    reinterpret_cast<uint4 *>(ms + C::M_FB)[1] = src[1];
-                }
-                reinterpret_cast<uint16_t *>(ms + C::M_EM)[lane] = uint16_t(w.em);
-            }
+    // The pieces of a stage go out in parallel, one bulk copy per lane; lane 0 first tells the
+    // slot's barrier how many bytes to expect.  False when a descriptor did not arrive in time.
+    __device__ __forceinline__ bool produce(const AttnArgs &a, uint8_t *R, int c_stage, int c_fb, int lane) {
+        while (fb < fb1 && stage - c_stage < C::NSTAGE) {
+            if (tile == 0 && fb - c_fb >= 2) break;
+            const int slot = stage % C::NSTAGE;
+            const uint32_t bar = smem_u32(R + C::W_BAR + 8 * slot);
+            const uint32_t ms = smem_u32(R + C::W_META + (bseq & 1) * C::MSLOT);
+            if (tile == 0 && !start_block(a, R, lane)) return false;
             const int t0 = tile * C::TS;
-            const int n = min(C::TS, int(f.valid) - t0);
-            const int ia = t0 >> 4, ib = min(16, (t0 + C::TS) >> 4);
-            const int T = (lane >> 2) & 1, j = lane & 3;
-            const int e0 = esc_at(w.em, T, ia), e1 = esc_at(w.em, T, ib);
-            const int mode = T ? vm : km;
-            const uint32_t off = T ? f.v_off : f.k_off;
-            const Sections sc = sections<D, BF16IN>(T ? vb : kb, off, mode, f.n_tok);
-            uint8_t *dst = ring + (stage % C::NSTAGE) * C::SLOT + T * C::TR;
-            const uint8_t *src = nullptr;
-            uint32_t len = 0;
-            if (lane < 8) {
-                if (BF16IN || mode == 0) {
-                    if (j == 0) {
-                        src = sc.rows + size_t(t0) * (2 * D);
-                        len = uint32_t(n * 2 * D);
-                    }
-                } else if (j == 0) {
-                    src = sc.rows + size_t(t0) * D;
-                    len = uint32_t(n * D);
-                } else if (j == 1) {
-                    src = sc.codes + size_t(t0) * D * mode / 8;
-                    len = uint32_t(n * D * mode / 8);
-                    dst += C::CODE_OFF;
-                } else if (e1 - e0 > 0 && e1 - e0 <= C::ESC_CAP) {
-                    src = j == 2 ? sc.esc + 2 * e0
-                                 : reinterpret_cast<const uint8_t *>(a.esc + (T ? f.v_rec : f.k_rec) +
-                                                                     kEscRecHead + e0);
-                    len = uint32_t(2 * (e1 - e0));
-                    dst += j == 2 ? C::EV_OFF : C::EP_OFF;
-                }
-            } else if (!BF16IN && tile == 0 && lane < 10 && (lane == 8 ? km : vm) != 0) {
-                src = (lane == 8 ? kb + f.k_off : vb + f.v_off) + kHeaderBytes;
-                len = D;
-                dst = ms + (lane - 8) * C::BASE;
+            const int n = min(C::TS, valid - t0);
+            const int T = (lane >> 2) & 1;
+            const int e0 = esc_at(em, T, t0 >> 4), e1 = esc_at(em, T, min(16, (t0 + C::TS) >> 4));
+            const uint8_t *p;
+            uint32_t len;
+            if (kind == 2) {
+                p = src + 2 * e0;
+                len = e1 - e0 <= C::ESC_CAP ? uint32_t(2 * (e1 - e0)) : 0u;
+            } else {
+                p = src + size_t(t0) * stride;
+                len = kind == 1 ? uint32_t(n) * stride : (kind == 3 && tile == 0 ? uint32_t(D) : 0u);
             }
-            const Piece p = make_piece(src, len);
-            const uint32_t bytes = len != 0 ? p.alloc : 0u;
+            const uint32_t d = kind == 3 ? ms + dst : smem_u32(R + slot * C::SLOT) + dst;
+            const Piece pc = make_piece(p, len);
+            const uint32_t bytes = len != 0 ? pc.alloc : 0u;
             const uint32_t total = __reduce_add_sync(FULL, bytes);
             fence_proxy_async();
             if (lane == 0) mbar_arrive_expect_tx(bar, total);
             __syncwarp();
-            if (bytes != 0) bulk_g2s(smem_u32(dst), p.src, bytes, bar);
+            if (bytes != 0) bulk_g2s(d, pc.src, bytes, bar);
             ++stage;
-            if (t0 + C::TS >= int(f.valid)) {
+            if (t0 + C::TS >= valid) {
                 tile = 0;
                 ++bseq;
-                w.next(a, lane);
+                ++fb;
+                fetch(a, R, lane);
             } else {
                 ++tile;
             }
         }
+        return true;
     }
 };
 
 // The escape words of tensor T (0 K, 1 V) of the block's stage holding escapes [e0, e1):
 // the producer's staged copies when they fit, else the block's words in HBM.
 template <int D>
-__device__ __forceinline__ StageEsc stage_esc(const AttnArgs &a, const FlatBlock &f, int T,
+__device__ __forceinline__ StageEsc stage_esc(const AttnArgs &a, const BlockDesc &bd, int T,
                                               uint32_t tstage, int e0, int e1) {
     using C = Cfg<D>;
-    const uint32_t off = T ? f.v_off : f.k_off, rec = T ? f.v_rec : f.k_rec;
-    const int mode = T ? f.v_mode : f.k_mode;
+    const uint64_t blk = T ? bd.v : bd.k;
+    const uint32_t rec = T ? bd.v_rec : bd.k_rec;
+    const int mode = T ? bd.v_mode : bd.k_mode;
     StageEsc se;
     se.gval = se.gpos = nullptr;
     if (e1 - e0 <= C::ESC_CAP) {
-        se.val = tstage + C::EV_OFF + esc_word_line<D>(off, f.n_tok, mode, e0);
+        se.val = tstage + C::EV_OFF + esc_word_line<D>(blk, bd.n_tok, mode, e0);
         se.pos = tstage + C::EP_OFF + esc_pos_line(rec, e0);
         se.off = e0;
     } else {
-        const UnitDev *U = a.units + f.unit;
         se.val = se.pos = 0u;
         se.off = 0;
-        se.gval = reinterpret_cast<const uint16_t *>(sections<D, false>(T ? U->v : U->k, off, mode, f.n_tok).esc);
+        se.gval = reinterpret_cast<const uint16_t *>(sections<D, false>(desc_ptr(blk), mode, bd.n_tok).esc);
         se.gpos = a.esc + rec + kEscRecHead;
     }
     return se;
@@ -559,18 +617,19 @@ __device__ __forceinline__ StageEsc stage_esc(const AttnArgs &a, const FlatBlock
 
 // One tensor of a stage into the tile, escapes included.
 template <int D>
-__device__ __forceinline__ void stage_tile(const AttnArgs &a, const FlatBlock &f, int T, int mode,
-                                           uint32_t tstage, uint32_t xb, const Lay &ly,
-                                           const uint32_t (&b7)[4], const uint8_t *em, int ia,
-                                           int ib, int rows, int zero_from, int lane) {
-    if (mode == 4) decode_stage<D, 4>(tstage, xb, ly, b7, lane, zero_from);
-    else if (mode == 2) decode_stage<D, 2>(tstage, xb, ly, b7, lane, zero_from);
-    else decode_stage<D, 0>(tstage, xb, ly, b7, lane, zero_from);
-    const int e0 = esc_ms(em, T, ia), e1 = esc_ms(em, T, ib);
+__device__ __forceinline__ void stage_tile(const AttnArgs &a, const BlockDesc &bd, int T, int mode,
+                                           uint32_t tstage, uint32_t xb, const StoreMap<D> &sm, const Lay &ly,
+                                           const uint32_t (&b7)[4], int ia, int ib, int rows,
+                                           int zero_from, int lane) {
+    if (mode == 4) decode_stage<D, 4>(tstage, ly, b7, sm, lane);
+    else if (mode == 2) decode_stage<D, 2>(tstage, ly, b7, sm, lane);
+    else decode_stage<D, 0>(tstage, ly, b7, sm, lane);
+    if (zero_from < Cfg<D>::TS) zero_rows<D>(sm, zero_from, lane);
+    const int e0 = esc_ms(bd, T, ia), e1 = esc_ms(bd, T, ib);
     if (e1 > e0) {
-        const StageEsc se = stage_esc<D>(a, f, T, tstage, e0, e1);
+        const StageEsc se = stage_esc<D>(a, bd, T, tstage, e0, e1);
         __syncwarp();  // the decoded words are in place before escapes overwrite some
-        esc_patch<D>(xb, se, e0, Cfg<D>::SUBS > 1 ? esc_ms(em, T, ia + 1) : e1, e1, rows, lane);
+        esc_patch<D>(xb, se, e0, Cfg<D>::SUBS > 1 ? esc_ms(bd, T, ia + 1) : e1, e1, rows, lane);
     }
     __syncwarp();
 }
@@ -584,16 +643,23 @@ __device__ __forceinline__ void worker(const AttnArgs &a, uint8_t *R, int wk, in
     uint8_t *metas = R + C::W_META;
     const uint32_t xb = smem_u32(R + C::W_XB);
     uint8_t *bars = R + C::W_BAR;
+    StoreMap<D> smap;
+    smap.init(xb, lane);
     if (lane == 0) {
 #pragma unroll
         for (int j = 0; j < C::NSTAGE; ++j) mbar_init(smem_u32(bars + 8 * j), 1);
+#pragma unroll
+        for (int j = 0; j < C::NDESC; ++j) mbar_init(smem_u32(R + C::W_DBAR + 8 * j), 1);
         fence_mbar_init();
     }
     __syncwarp();
     Producer<D, BF16IN> pp;
-    pp.w.init(a, fb0, fb1, lane);
+    pp.fb = pp.fb0 = pp.pf = pp.dwait = fb0;
+    pp.fb1 = fb1;
+    pp.fetch(a, R, lane);
     int fb = fb0, tile = 0, stage = 0, bseq = 0;
-    int ubeg = 0, uend = 0, seg_begin = fb0;  // the current unit's flat block range
+    int seg_begin = fb0;
+    uint32_t flags = 0u, whole = 0u;  // the block's flags; the segment began at its unit's start
     Lay lk{}, lv{};
     uint32_t b7k[4] = {0u, 0u, 0u, 0u}, b7v[4] = {0u, 0u, 0u, 0u};
     uint32_t qb[C::KS][2];
@@ -601,35 +667,35 @@ __device__ __forceinline__ void worker(const AttnArgs &a, uint8_t *R, int wk, in
     float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
 
     while (fb < fb1) {
-        pp.produce(a, ring, metas, bars, stage, fb, lane);
-        if (!mbar_wait_bounded(smem_u32(bars + 8 * (stage % C::NSTAGE)), (stage / C::NSTAGE) & 1,
+        if (!pp.produce(a, R, stage, fb, lane) ||
+            !mbar_wait_bounded(smem_u32(bars + 8 * (stage % C::NSTAGE)), (stage / C::NSTAGE) & 1,
                                kStageWaitUs)) {
             if (lane == 0) report(a.status, KVX_ERR_TIMEOUT, DERR_TIMEOUT);
             // let the copies already issued land before this CTA's shared memory goes away
-            for (int q = stage + 1; q < pp.stage; ++q)
+            for (int q = stage; q < pp.stage; ++q)
                 mbar_wait_bounded(smem_u32(bars + 8 * (q % C::NSTAGE)), (q / C::NSTAGE) & 1, kStageWaitUs);
+            for (int b = pp.dwait; b < pp.pf; ++b)
+                mbar_wait_bounded(smem_u32(R + C::W_DBAR + 8 * ((b - fb0) % C::NDESC)),
+                                  ((b - fb0) / C::NDESC) & 1, kStageWaitUs);
             return;
         }
         __syncwarp();
         const uint8_t *ms = metas + (bseq & 1) * C::MSLOT;
-        const FlatBlock f = *reinterpret_cast<const FlatBlock *>(ms + C::M_FB);
-        const uint8_t *em = ms + C::M_EM;
-        const int kmode = BF16IN ? 0 : f.k_mode, vmode = BF16IN ? 0 : f.v_mode;
+        const BlockDesc &bd =
+            *reinterpret_cast<const BlockDesc *>(R + C::W_DESC + ((fb - fb0) % C::NDESC) * int(sizeof(BlockDesc)));
+        const int kmode = BF16IN ? 0 : bd.k_mode, vmode = BF16IN ? 0 : bd.v_mode;
+        const int valid = bd.valid;
         if (tile == 0) {
-            const UnitDev *U = a.units + f.unit;
-            ubeg = int(U->block_begin);
-            uend = ubeg + U->n_blocks;
-            const Sections sk = sections<D, BF16IN>(U->k, f.k_off, kmode, f.n_tok);
-            const Sections sv = sections<D, BF16IN>(U->v, f.v_off, vmode, f.n_tok);
-            const uint32_t kd = uint32_t(reinterpret_cast<uintptr_t>(sk.rows) & 15u);
-            const uint32_t vd = uint32_t(reinterpret_cast<uintptr_t>(sv.rows) & 15u);
-            const uint32_t kc = kmode ? uint32_t(reinterpret_cast<uintptr_t>(sk.codes) & 15u) : 0u;
-            const uint32_t vc = vmode ? uint32_t(reinterpret_cast<uintptr_t>(sv.codes) & 15u) : 0u;
+            const uint32_t al = *reinterpret_cast<const uint32_t *>(bd.align);
+            flags = bd.flags;
+            const uint32_t kd = al & 15u, kc = (al >> 8) & 15u, vd = (al >> 16) & 15u, vc = (al >> 24) & 15u;
             lk = make_lay<D>(kd, kc, kmode, c8, BF16IN);
             lv = make_lay<D>(vd, vc, vmode, c8, BF16IN);
             if (kmode != 0) load_b7(smem_u32(ms) + kd + 8 * c8, b7k);
             if (vmode != 0) load_b7(smem_u32(ms) + C::BASE + vd + 8 * c8, b7v);
             if (fb == seg_begin) {
+                const UnitDev *U = a.units + bd.unit;
+                whole = flags & kDescFirst;
                 load_q<D>(U->q, U->n_q, U->q_stride, qb, lane);
                 m0 = m1 = -INFINITY;
                 l0 = l1 = 0.f;
@@ -639,13 +705,13 @@ __device__ __forceinline__ void worker(const AttnArgs &a, uint8_t *R, int wk, in
         }
         const uint32_t kst = smem_u32(ring + (stage % C::NSTAGE) * C::SLOT), vst = kst + C::TR;
         const int t0 = tile * C::TS;
-        const int rows = min(C::TS, int(f.valid) - t0);
-        const bool last_tile = t0 + C::TS >= int(f.valid);
-        const bool seg_end = last_tile && (fb + 1 == fb1 || fb + 1 == uend);
+        const int rows = min(C::TS, valid - t0);
+        const bool last_tile = t0 + C::TS >= valid;
+        const bool seg_end = last_tile && (fb + 1 == fb1 || (flags & kDescLast) != 0u);
         const int ia = t0 >> 4, ib = min(16, (t0 + C::TS) >> 4);
 
         // S^T = K Q^T for every tile of the stage
-        stage_tile<D>(a, f, 0, kmode, kst, xb, lk, b7k, em, ia, ib, rows, C::TS, lane);
+        stage_tile<D>(a, bd, 0, kmode, kst, xb, smap, lk, b7k, ia, ib, rows, C::TS, lane);
         // (a stage's rows past `rows` hold stale words: their scores are dropped below)
         float s[C::SUBS][4];
         qk_tiles<D, C::SUBS>(xb, qb, lane, s);
@@ -707,7 +773,7 @@ __device__ __forceinline__ void worker(const AttnArgs &a, uint8_t *R, int wk, in
         // O^T += V^T P^T for every tile of the stage (the tile's K reads are done: stage_tile
         // ends with __syncwarp, and the K tiles were read before the softmax)
         __syncwarp();
-        stage_tile<D>(a, f, 1, vmode, vst, xb, lv, b7v, em, ia, ib, rows, rows, lane);
+        stage_tile<D>(a, bd, 1, vmode, vst, xb, smap, lv, b7v, ia, ib, rows, rows, lane);
 #pragma unroll
         for (int sub = 0; sub < C::SUBS; ++sub)
             if (sub * TT < rows) pv_tile<D>(xb, sub * TT, bh[sub], bm[sub], lane, acc);
@@ -721,8 +787,8 @@ __device__ __forceinline__ void worker(const AttnArgs &a, uint8_t *R, int wk, in
             }
             const int qa = 2 * tig, qc = 2 * tig + 1;
             // acc[m][0 / 1]: dim 16 m + g of queries qa / qc; acc[m][2 / 3]: dim 16 m + g + 8
-            if (seg_begin == ubeg && fb + 1 == uend) {
-                const UnitDev *U = a.units + f.unit;
+            if (whole != 0u && (flags & kDescLast) != 0u) {
+                const UnitDev *U = a.units + bd.unit;
                 const int n_q = U->n_q, stride = U->q_stride;
                 float *out = U->out;
                 float *lse = U->lse;
@@ -958,6 +1024,43 @@ template <int D> void configure(bool bf16) {
     done[bf16] = true;
 }
 
+// ---- block descriptors ---------------------------------------------------------------------------
+
+__global__ void block_desc_kernel(const UnitDev *units, const FlatBlock *flat, const uint16_t *esc, int64_t n,
+                                  int dim, bool bf16, BlockDesc *desc) {
+    const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const FlatBlock f = flat[i];
+    const UnitDev &U = units[f.unit];
+    BlockDesc d = {};
+    d.k_rec = f.k_rec;
+    d.v_rec = f.v_rec;
+    d.k_nesc = f.k_nesc;
+    d.v_nesc = f.v_nesc;
+    d.k_mode = bf16 ? 0 : f.k_mode;
+    d.v_mode = bf16 ? 0 : f.v_mode;
+    d.n_tok = f.n_tok;
+    d.valid = f.valid;
+    d.unit = f.unit;
+    d.flags = uint8_t((i == U.block_begin ? kDescFirst : 0) | (i + 1 == U.block_begin + U.n_blocks ? kDescLast : 0));
+    for (int T = 0; T < 2; ++T) {
+        const uint8_t *blob = T ? U.v : U.k;
+        const uint32_t off = T ? f.v_off : f.k_off;
+        const int mode = T ? d.v_mode : d.k_mode;
+        const uint8_t *blk = bf16 ? blob + size_t(off) * 2 * dim : blob + off;
+        const uint8_t *rows = bf16 ? blk : blk + kHeaderBytes + (mode != 0 ? dim : 0);
+        const uint8_t *codes = rows + size_t(f.n_tok) * dim;
+        (T ? d.v : d.k) = reinterpret_cast<uint64_t>(blk);
+        d.align[2 * T] = uint8_t(reinterpret_cast<uintptr_t>(rows) & 15u);
+        d.align[2 * T + 1] = mode != 0 ? uint8_t(reinterpret_cast<uintptr_t>(codes) & 15u) : uint8_t(0);
+        const int nesc = T ? f.v_nesc : f.k_nesc;
+        const uint32_t rec = T ? f.v_rec : f.k_rec;
+        if (mode != 0 && nesc != 0)
+            for (int j = 0; j < 16; ++j) d.em[T][j] = esc[rec + j];
+    }
+    desc[i] = d;
+}
+
 template <int D>
 cudaError_t launch_d(bool bf16, const AttnArgs &a, int grid, cudaStream_t s) {
     configure<D>(bf16);
@@ -1028,6 +1131,13 @@ cudaError_t launch_combine(int dim, const CombineArgs &a, int n_split, cudaStrea
     case 256: combine_kernel<256><<<grid, kCombineThreads, 0, s>>>(a); break;
     default: return cudaErrorInvalidValue;
     }
+    return cudaGetLastError();
+}
+
+cudaError_t launch_block_desc(const UnitDev *units, const FlatBlock *flat, const uint16_t *esc, int64_t n,
+                              int dim, bool bf16, BlockDesc *desc, cudaStream_t s) {
+    if (n <= 0) return cudaSuccess;
+    block_desc_kernel<<<unsigned((n + 255) / 256), 256, 0, s>>>(units, flat, esc, n, dim, bf16, desc);
     return cudaGetLastError();
 }
 

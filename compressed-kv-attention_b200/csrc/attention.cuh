@@ -1,6 +1,8 @@
 // attention.cuh -- declarations shared by the attention kernels and the host plan code.
 #pragma once
 
+#include <cstddef>
+
 #include "common.cuh"
 
 namespace kvx {
@@ -79,9 +81,28 @@ struct UnitDev {
 };
 static_assert(sizeof(UnitDev) == 64, "UnitDev is 64 bytes");
 
+// Everything the attention kernel needs to stream one flat block, built once per plan (after
+// the escape records) and fetched by one 128-byte bulk copy, two blocks ahead of its use.
+struct BlockDesc {
+    uint64_t k, v;          // XKV: address of the K / V block header.  BF16: of the block's first row.
+    uint32_t k_rec, v_rec;  // FlatBlock::k_rec / v_rec
+    uint16_t k_nesc, v_nesc;
+    uint8_t k_mode, v_mode, n_tok, valid;
+    int32_t unit;
+    uint8_t align[4];       // K rows, K codes, V rows, V codes: offset of the section's first byte
+                            // in its 16-byte line (codes 0 for a raw block)
+    uint8_t flags;          // kDescFirst | kDescLast
+    uint8_t pad[23];
+    uint16_t em[2][16];     // K / V escape count headers, e(i) at [i - 1] (zeros without a record)
+};
+static_assert(sizeof(BlockDesc) == 128 && offsetof(BlockDesc, align) == 36 && offsetof(BlockDesc, em) == 64,
+              "BlockDesc layout");
+constexpr uint8_t kDescFirst = 1, kDescLast = 2;  // the first / last block of its unit
+
 struct AttnArgs {
     const UnitDev *units;
     const FlatBlock *flat;      // [n_blocks]
+    const BlockDesc *desc;      // [n_blocks]
     const uint16_t *esc;        // escape records (FlatBlock::k_rec / v_rec index it)
     const int64_t *range_begin; // [n_workers + 1] flat-block range of each worker warp
     float *partials;            // [n_workers][2][8 + 8 + 8 * dim]
@@ -114,6 +135,9 @@ __host__ __device__ inline int worker_of_block(const int64_t *range_begin, int n
 // Launchers (attention.cu).  Return cudaError_t of the launch.
 cudaError_t launch_attention(int dim, bool bf16_input, const AttnArgs &a, int grid, cudaStream_t s);
 cudaError_t launch_combine(int dim, const CombineArgs &a, int n_split, cudaStream_t s);
+// Block descriptors of a step from its flat blocks, units and escape records.
+cudaError_t launch_block_desc(const UnitDev *units, const FlatBlock *flat, const uint16_t *esc, int64_t n,
+                              int dim, bool bf16, BlockDesc *desc, cudaStream_t s);
 cudaError_t launch_fold(const float *parts, int n_parts, int n_rows, int dim, float *out,
                         float *lse_out, cudaStream_t s);
 // Escape records: sizes and offsets (single CTA; *total receives the record array length in u16,

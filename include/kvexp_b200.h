@@ -187,7 +187,7 @@ KVX_API int kvx_fold_shards(const float *parts, int n_parts, int n_rows, int dim
  * kvx_attention_decode for one KV head (within FP32 rounding), with every buffer in device
  * memory: q [n_q, dim] BF16, the K/V XKV blobs (16-byte aligned) with their block indexes
  * (n_blocks entries each, from kvx_xkv_index or the GPU encoder), out [n_q, dim] FP32.  Its
- * scratch is one fixed 16 MiB array in the library's device image, held by every device that
+ * scratch is one fixed 24 MiB array in the library's device image, held by every device that
  * loads the library until the process exits; limits: n_blocks <= 8192, n_q <= 64, and the
  * blobs' escape words plus 16 per coded block that has any at most 3 Mi (about 1 in 6 elements
  * of 8192 blocks of 128 x 128) -- larger calls fail with KVX_ERR_INVALID_ARGUMENT (the escape
