@@ -58,13 +58,9 @@ __host__ __device__ constexpr int cmax(int a, int b) { return a > b ? a : b; }
 #ifndef KVX_MAXWARPS
 #define KVX_MAXWARPS 12
 #endif
-#ifndef KVX_TS64
-#define KVX_TS64 32
-#endif
-
 template <int D> struct Cfg {
     static constexpr int KS = D / 16;             // k-steps of QK = M-tiles of PV
-    static constexpr int TS = D <= 64 ? KVX_TS64 : 16;  // tokens per ring stage
+    static constexpr int TS = stage_tokens(D);    // tokens per ring stage
     static constexpr int SUBS = TS / TT;          // MMA tiles per stage
     static constexpr int C8 = D / 8;              // 8-element chunks per row
     static constexpr int NIT = TS * C8 / 32;      // chunk steps of a lane per stage and tensor
@@ -353,33 +349,26 @@ __device__ __forceinline__ void zero_rows(const StoreMap<D> &sm, int from, int l
     }
 }
 
-// The escape words of one tensor of a stage.  Staged (val != 0): word i of the block is the u16
-// at shared address val + 2 (i - off), its slot in the 16-token tile (esc_scratch_slot) at
-// pos + 2 (i - off).  Otherwise the block's words and slots are read from HBM (gval / gpos).
-struct StageEsc {
-    uint32_t val, pos;
-    int off;
-    const uint16_t *gval, *gpos;
-};
-
-// Store the stage's escape words over their elements of the tile: escapes [e0, e1) of the block,
-// those from em on in the stage's second tile; rows at or past `rows` keep their value.
+// Store escape words [e0, e1) of a block over their elements of the stage's tile: word i is the
+// u16 at vals + 2 i, its tile byte (esc_scratch_slot of its token in the stage) at slots + 2 i --
+// shared addresses of the staged copies, or (HBM variant) the block's words and record in global
+// memory.  Slots at or past the stage's valid rows (lim bytes) are skipped; slots are even.
 template <int D>
-__device__ __forceinline__ void esc_patch(uint32_t xb, const StageEsc &se, int e0, int em, int e1,
-                                          int rows, int lane) {
+__device__ __forceinline__ void esc_patch(uint32_t xb, uint32_t vals, uint32_t slots, int e0, int e1,
+                                          uint32_t lim, int lane) {
     for (int i = e0 + lane; i < e1; i += 32) {
-        uint32_t slot, val;
-        if (se.val != 0u) {
-            slot = lds_u16(se.pos + 2u * uint32_t(i - se.off));
-            val = lds_u16(se.val + 2u * uint32_t(i - se.off));
-        } else {
-            slot = __ldg(se.gpos + i);
-            val = __ldg(se.gval + i);
-        }
-        const int second = i >= em;
-        // slots are even bytes inside a 16-row tile (esc_scratch_slot); anything else is skipped
-        if (slot < uint32_t(TT * 2 * D) && (slot & 1u) == 0u && TT * second + int(slot / (2 * D)) < rows)
-            sts_u16(xb + uint32_t(second * TT * 2 * D) + slot, val);
+        const uint32_t slot = lds_u16(slots + 2u * uint32_t(i));
+        const uint32_t val = lds_u16(vals + 2u * uint32_t(i));
+        if (slot < lim) sts_u16(xb + (slot & ~1u), val);
+    }
+}
+template <int D>
+__device__ __noinline__ void esc_patch_hbm(uint32_t xb, const uint16_t *vals, const uint16_t *slots, int e0,
+                                           int e1, uint32_t lim, int lane) {
+    for (int i = e0 + lane; i < e1; i += 32) {
+        const uint32_t slot = __ldg(slots + i);
+        const uint32_t val = __ldg(vals + i);
+        if (slot < lim) sts_u16(xb + (slot & ~1u), val);
     }
 }
 
@@ -591,30 +580,6 @@ template <int D, bool BF16IN> struct Producer {
     }
 };
 
-// The escape words of tensor T (0 K, 1 V) of the block's stage holding escapes [e0, e1):
-// the producer's staged copies when they fit, else the block's words in HBM.
-template <int D>
-__device__ __forceinline__ StageEsc stage_esc(const AttnArgs &a, const BlockDesc &bd, int T,
-                                              uint32_t tstage, int e0, int e1) {
-    using C = Cfg<D>;
-    const uint64_t blk = T ? bd.v : bd.k;
-    const uint32_t rec = T ? bd.v_rec : bd.k_rec;
-    const int mode = T ? bd.v_mode : bd.k_mode;
-    StageEsc se;
-    se.gval = se.gpos = nullptr;
-    if (e1 - e0 <= C::ESC_CAP) {
-        se.val = tstage + C::EV_OFF + esc_word_line<D>(blk, bd.n_tok, mode, e0);
-        se.pos = tstage + C::EP_OFF + esc_pos_line(rec, e0);
-        se.off = e0;
-    } else {
-        se.val = se.pos = 0u;
-        se.off = 0;
-        se.gval = reinterpret_cast<const uint16_t *>(sections<D, false>(desc_ptr(blk), mode, bd.n_tok).esc);
-        se.gpos = a.esc + rec + kEscRecHead;
-    }
-    return se;
-}
-
 // One tensor of a stage into the tile, escapes included.
 template <int D>
 __device__ __forceinline__ void stage_tile(const AttnArgs &a, const BlockDesc &bd, int T, int mode,
@@ -627,9 +592,19 @@ __device__ __forceinline__ void stage_tile(const AttnArgs &a, const BlockDesc &b
     if (zero_from < Cfg<D>::TS) zero_rows<D>(sm, zero_from, lane);
     const int e0 = esc_ms(bd, T, ia), e1 = esc_ms(bd, T, ib);
     if (e1 > e0) {
-        const StageEsc se = stage_esc<D>(a, bd, T, tstage, e0, e1);
+        using C = Cfg<D>;
+        const uint64_t blk = T ? bd.v : bd.k;
+        const uint32_t rec = T ? bd.v_rec : bd.k_rec;
+        const uint32_t lim = uint32_t(rows) * (2 * D);
         __syncwarp();  // the decoded words are in place before escapes overwrite some
-        esc_patch<D>(xb, se, e0, Cfg<D>::SUBS > 1 ? esc_ms(bd, T, ia + 1) : e1, e1, rows, lane);
+        if (e1 - e0 <= C::ESC_CAP) {  // staged by the producer
+            const uint32_t vals = tstage + C::EV_OFF + esc_word_line<D>(blk, bd.n_tok, mode, e0) - 2u * uint32_t(e0);
+            const uint32_t slots = tstage + C::EP_OFF + esc_pos_line(rec, e0) - 2u * uint32_t(e0);
+            esc_patch<D>(xb, vals, slots, e0, e1, lim, lane);
+        } else {
+            const uint16_t *vals = reinterpret_cast<const uint16_t *>(sections<D, false>(desc_ptr(blk), mode, bd.n_tok).esc);
+            esc_patch_hbm<D>(xb, vals, a.esc + rec + kEscRecHead, e0, e1, lim, lane);
+        }
     }
     __syncwarp();
 }

@@ -32,14 +32,20 @@ static_assert(sizeof(FlatBlock) == 32, "FlatBlock is 32 bytes");
 //                     block), so the escapes of tokens [16 a, 16 b) are [e(a), e(b)), e(0) = 0;
 //   [16, 16 + n_esc)  for every escape, in the container's scan order, where the attention kernel
 //                     stores it: the byte of the element it replaces in the kernel's BF16 tile
-//                     (esc_scratch_slot of its token within the 16-token tile and its channel).
+//                     (esc_scratch_slot of its token within the kernel's stage and its channel).
 // Built once per plan from the blob's residual codes; raw blocks and blocks without escapes
 // have none.
 constexpr int kEscRecHead = 16;
 
-// Byte of element (token r of a 16-token tile, channel c) in the attention kernel's BF16 tile:
-// rows of 2 dim bytes, 16-byte chunks XOR-swizzled by the row (chunk c / 8 of row r sits at
-// chunk position (c / 8) ^ (r & 7), or ^ ((r / 2) & 3) for dim 32).  The same for K and V.
+#ifndef KVX_TS64
+#define KVX_TS64 32
+#endif
+// Tokens per stage of the attention kernel (a multiple of 16).
+__host__ __device__ constexpr int stage_tokens(int dim) { return dim <= 64 ? KVX_TS64 : 16; }
+
+// Byte of element (token r of a stage, channel c) in the attention kernel's BF16 tile of the
+// stage: rows of 2 dim bytes, 16-byte chunks XOR-swizzled by the row (chunk c / 8 of row r sits
+// at chunk position (c / 8) ^ (r & 7), or ^ ((r / 2) & 3) for dim 32).  The same for K and V.
 __host__ __device__ inline uint32_t esc_scratch_slot(int dim, int T, int r, int c) {
     (void)T;
     const int c8 = c >> 3;

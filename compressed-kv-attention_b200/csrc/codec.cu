@@ -625,7 +625,7 @@ __global__ void esc_fill_kernel(const UnitDev *units, const FlatBlock *flat, int
     // element index -> the escape's byte in the attention kernel's scratch
     for (int i = lane; i < m; i += 32) {
         const int el = pos[i];
-        pos[i] = uint16_t(esc_scratch_slot(dim, T, (el / dim) & 15, el % dim));
+        pos[i] = uint16_t(esc_scratch_slot(dim, T, (el / dim) % stage_tokens(dim), el % dim));
     }
 }
 
