@@ -224,7 +224,7 @@ struct kvx_plan_s {
     UnitDev *units = nullptr;
     FlatBlock *flat = nullptr;
     BlockDesc *desc = nullptr;  // per flat block, for the attention kernel
-    uint16_t *esc = nullptr;  // escape records of the step's coded blocks
+    uint32_t *esc = nullptr;  // escape records of the step's coded blocks
     int64_t *range_begin = nullptr;
     float *partials = nullptr;
     int4 *split_units = nullptr;  // {unit, first worker, workers} of each split unit
@@ -1023,8 +1023,8 @@ extern "C" int kvx_fold_shards(const float *parts, int n_parts, int n_rows, int 
 
 namespace kvx {
 namespace {
-constexpr size_t kNoAllocScratchBytes = size_t(24) << 20;  // 24 MiB per device
-constexpr size_t kNoAllocEscEntries = size_t(3) << 20;      // escape record entries (6 MiB)
+constexpr size_t kNoAllocScratchBytes = size_t(30) << 20;  // 30 MiB per device
+constexpr size_t kNoAllocEscEntries = size_t(3) << 20;      // escape record entries (12 MiB)
 constexpr int kNoAllocMaxBlocks = 8192;                   // XKV blocks per tensor
 constexpr int kNoAllocMaxQueries = 64;                    // queries per call (8 groups of 8)
 constexpr int kNoAllocMaxWorkers = 4096;
@@ -1119,7 +1119,7 @@ extern "C" int kvx_attention_decode_noalloc(const uint16_t *q, const uint8_t *k_
     int64_t *d_range = reinterpret_cast<int64_t *>(take((kNoAllocMaxWorkers + 1) * sizeof(int64_t)));
     unsigned long long *d_esc_total =
         reinterpret_cast<unsigned long long *>(take(sizeof(unsigned long long)));
-    uint16_t *d_esc = reinterpret_cast<uint16_t *>(take(kNoAllocEscEntries * sizeof(uint16_t)));
+    uint32_t *d_esc = reinterpret_cast<uint32_t *>(take(kNoAllocEscEntries * sizeof(uint32_t)));
     float *d_partials = reinterpret_cast<float *>(base + off);
     const size_t per_worker = 2 * size_t(partial_stride(dim)) * sizeof(float);
     const int64_t fit = int64_t((kNoAllocScratchBytes - off) / per_worker);

@@ -64,13 +64,12 @@ template <int D> struct Cfg {
     static constexpr int SUBS = TS / TT;          // MMA tiles per stage
     static constexpr int C8 = D / 8;              // 8-element chunks per row
     static constexpr int NIT = TS * C8 / 32;      // chunk steps of a lane per stage and tensor
-    // One tensor's stage: sign/mantissa rows | residual codes | escape words | their slots, or
-    // TS raw BF16 rows -- both fit 2 TS D bytes (escapes beyond ESC_CAP stay in HBM).
+    // One tensor's stage: sign/mantissa rows | residual codes | escape record entries, or TS raw
+    // BF16 rows -- both fit 2 TS D bytes (escapes beyond ESC_CAP stay in HBM).
     static constexpr int ESC_CAP = TS * D / 8;
     static constexpr int CODE_OFF = TS * D + 16;
-    static constexpr int EV_OFF = CODE_OFF + TS * D / 2 + 16;
-    static constexpr int EP_OFF = EV_OFF + 2 * ESC_CAP + 16;
-    static constexpr int TR = round16(cmax(EP_OFF + 2 * ESC_CAP + 16, TS * 2 * D + 16));
+    static constexpr int EE_OFF = CODE_OFF + TS * D / 2 + 16;
+    static constexpr int TR = round16(cmax(EE_OFF + 4 * ESC_CAP + 16, TS * 2 * D + 16));
     static constexpr int SLOT = 2 * TR;  // K stage | V stage
     static constexpr int NSTAGE = D <= 32 ? 3 : 2;
     static constexpr int BASE = round16(D + 32);  // one block's base exponents (+ alignment slack)
@@ -151,15 +150,10 @@ __device__ __forceinline__ int esc_ms(const BlockDesc &bd, int T, int i) {
     return i == 0 ? 0 : int(bd.em[T][i - 1]);
 }
 
-// Byte offset inside a 16-byte line of escape word i of a coded block (blk: its header's address)
-// and of its position in the escape records (16-byte aligned allocation).
-template <int D>
-__device__ __forceinline__ uint32_t esc_word_line(uint64_t blk, int n_tok, int mode, int i) {
-    return (uint32_t(blk) + uint32_t(kHeaderBytes + D) + uint32_t(n_tok * D) + uint32_t(n_tok * D * mode / 8) +
-            2u * uint32_t(i)) & 15u;
-}
-__device__ __forceinline__ uint32_t esc_pos_line(uint32_t rec, int i) {
-    return (2u * (rec + uint32_t(kEscRecHead) + uint32_t(i))) & 15u;
+// Byte offset inside a 16-byte line of entry i of the escape record at `rec` (the record array is
+// 16-byte aligned).
+__device__ __forceinline__ uint32_t esc_rec_line(uint32_t rec, int i) {
+    return (4u * (rec + uint32_t(kEscRecHead) + uint32_t(i))) & 15u;
 }
 
 // ---- decode helpers ----------------------------------------------------------------------------
@@ -349,26 +343,23 @@ __device__ __forceinline__ void zero_rows(const StoreMap<D> &sm, int from, int l
     }
 }
 
-// Store escape words [e0, e1) of a block over their elements of the stage's tile: word i is the
-// u16 at vals + 2 i, its tile byte (esc_scratch_slot of its token in the stage) at slots + 2 i --
-// shared addresses of the staged copies, or (HBM variant) the block's words and record in global
-// memory.  Slots at or past the stage's valid rows (lim bytes) are skipped; slots are even.
+// Store escapes [e0, e1) of a block over their elements of the stage's tile: record entry i (tile
+// byte | escape word << 16) is the u32 at ents + 4 i -- a shared address of the staged copy, or
+// (HBM variant) the record in global memory.  Slots at or past the stage's valid rows (lim bytes)
+// are skipped; slots are even.
 template <int D>
-__device__ __forceinline__ void esc_patch(uint32_t xb, uint32_t vals, uint32_t slots, int e0, int e1,
-                                          uint32_t lim, int lane) {
+__device__ __forceinline__ void esc_patch(uint32_t xb, uint32_t ents, int e0, int e1, uint32_t lim, int lane) {
     for (int i = e0 + lane; i < e1; i += 32) {
-        const uint32_t slot = lds_u16(slots + 2u * uint32_t(i));
-        const uint32_t val = lds_u16(vals + 2u * uint32_t(i));
-        if (slot < lim) sts_u16(xb + (slot & ~1u), val);
+        const uint32_t e = lds_u32(ents + 4u * uint32_t(i));
+        if ((e & 0xFFFFu) < lim) sts_u16(xb + (e & 0xFFFEu), e >> 16);
     }
 }
 template <int D>
-__device__ __noinline__ void esc_patch_hbm(uint32_t xb, const uint16_t *vals, const uint16_t *slots, int e0,
-                                           int e1, uint32_t lim, int lane) {
+__device__ __noinline__ void esc_patch_hbm(uint32_t xb, const uint32_t *ents, int e0, int e1, uint32_t lim,
+                                           int lane) {
     for (int i = e0 + lane; i < e1; i += 32) {
-        const uint32_t slot = __ldg(slots + i);
-        const uint32_t val = __ldg(vals + i);
-        if (slot < lim) sts_u16(xb + (slot & ~1u), val);
+        const uint32_t e = __ldg(ents + i);
+        if ((e & 0xFFFFu) < lim) sts_u16(xb + (e & 0xFFFEu), e >> 16);
     }
 }
 
@@ -466,8 +457,8 @@ template <int D, bool BF16IN> struct Producer {
     uint32_t em = 0u;  // lane l: entry l % 16 of its K (l < 16) / V count header
     // This lane's piece of every stage of the current block.  Lane 4 T + j (j < 4) copies piece j
     // of tensor T: rows (j 0) and residual codes (j 1) are [src + t0 stride, + n stride) for the
-    // stage's tokens [t0, t0 + n); escape words (j 2) and their positions (j 3) are the stage's
-    // escapes [e0, e1) at src + 2 e0, when they fit the slot.  Lanes 8 and 9 copy the K and V base
+    // stage's tokens [t0, t0 + n); the escape record entries (j 2) of the stage's escapes
+    // [e0, e1) are at src + 4 e0, copied when they fit the slot.  Lanes 8 and 9 copy the K and V base
     // exponents (D bytes at src) with the block's first stage.  dst: offset in the ring slot or
     // (base exponents) in the meta slot.
     const uint8_t *src = nullptr;
@@ -518,10 +509,9 @@ template <int D, bool BF16IN> struct Producer {
                     stride = uint32_t(D * mode / 8);
                     dst += C::CODE_OFF;
                     kind = 1;
-                } else {
-                    src = j == 2 ? sc.esc
-                                 : reinterpret_cast<const uint8_t *>(a.esc + (T ? bd.v_rec : bd.k_rec) + kEscRecHead);
-                    dst += j == 2 ? C::EV_OFF : C::EP_OFF;
+                } else if (j == 2) {
+                    src = reinterpret_cast<const uint8_t *>(a.esc + (T ? bd.v_rec : bd.k_rec) + kEscRecHead);
+                    dst += C::EE_OFF;
                     kind = 2;
                 }
             }
@@ -552,8 +542,8 @@ template <int D, bool BF16IN> struct Producer {
             const uint8_t *p;
             uint32_t len;
             if (kind == 2) {
-                p = src + 2 * e0;
-                len = e1 - e0 <= C::ESC_CAP ? uint32_t(2 * (e1 - e0)) : 0u;
+                p = src + 4 * e0;
+                len = e1 - e0 <= C::ESC_CAP ? uint32_t(4 * (e1 - e0)) : 0u;
             } else {
                 p = src + size_t(t0) * stride;
                 len = kind == 1 ? uint32_t(n) * stride : (kind == 3 && tile == 0 ? uint32_t(D) : 0u);
@@ -593,18 +583,13 @@ __device__ __forceinline__ void stage_tile(const AttnArgs &a, const BlockDesc &b
     const int e0 = esc_ms(bd, T, ia), e1 = esc_ms(bd, T, ib);
     if (e1 > e0) {
         using C = Cfg<D>;
-        const uint64_t blk = T ? bd.v : bd.k;
         const uint32_t rec = T ? bd.v_rec : bd.k_rec;
         const uint32_t lim = uint32_t(rows) * (2 * D);
         __syncwarp();  // the decoded words are in place before escapes overwrite some
-        if (e1 - e0 <= C::ESC_CAP) {  // staged by the producer
-            const uint32_t vals = tstage + C::EV_OFF + esc_word_line<D>(blk, bd.n_tok, mode, e0) - 2u * uint32_t(e0);
-            const uint32_t slots = tstage + C::EP_OFF + esc_pos_line(rec, e0) - 2u * uint32_t(e0);
-            esc_patch<D>(xb, vals, slots, e0, e1, lim, lane);
-        } else {
-            const uint16_t *vals = reinterpret_cast<const uint16_t *>(sections<D, false>(desc_ptr(blk), mode, bd.n_tok).esc);
-            esc_patch_hbm<D>(xb, vals, a.esc + rec + kEscRecHead, e0, e1, lim, lane);
-        }
+        if (e1 - e0 <= C::ESC_CAP)  // staged by the producer
+            esc_patch<D>(xb, tstage + C::EE_OFF + esc_rec_line(rec, e0) - 4u * uint32_t(e0), e0, e1, lim, lane);
+        else
+            esc_patch_hbm<D>(xb, a.esc + rec + kEscRecHead, e0, e1, lim, lane);
     }
     __syncwarp();
 }
@@ -699,21 +684,29 @@ __device__ __forceinline__ void worker(const AttnArgs &a, uint8_t *R, int wk, in
             }
         }
 
-        // online softmax over the stage's tokens; p = 2^(s log2e - m log2e)
+        // online softmax over the stage's tokens; p = 2^(s log2e - m log2e).  The warp-wide
+        // maximum is only taken when some score exceeds the running one; otherwise m stays and
+        // the accumulators are not rescaled (alpha is exactly 1).
         float t0m = fmaxf(s[0][0], s[0][2]), t1m = fmaxf(s[0][1], s[0][3]);
 #pragma unroll
         for (int sub = 1; sub < C::SUBS; ++sub) {
             t0m = fmaxf(t0m, fmaxf(s[sub][0], s[sub][2]));
             t1m = fmaxf(t1m, fmaxf(s[sub][1], s[sub][3]));
         }
+        const bool grow = __any_sync(FULL, t0m > m0 || t1m > m1);
+        float mn0 = m0, mn1 = m1, al0 = 1.0f, al1 = 1.0f;
+        if (grow) {
 #pragma unroll
-        for (int o = 4; o < 32; o <<= 1) {
-            t0m = fmaxf(t0m, __shfl_xor_sync(FULL, t0m, o));
-            t1m = fmaxf(t1m, __shfl_xor_sync(FULL, t1m, o));
+            for (int o = 4; o < 32; o <<= 1) {
+                t0m = fmaxf(t0m, __shfl_xor_sync(FULL, t0m, o));
+                t1m = fmaxf(t1m, __shfl_xor_sync(FULL, t1m, o));
+            }
+            mn0 = fmaxf(m0, t0m);
+            mn1 = fmaxf(m1, t1m);
+            al0 = ex2(__fmaf_rn(m0, kLog2e, -__fmul_rn(mn0, kLog2e)));
+            al1 = ex2(__fmaf_rn(m1, kLog2e, -__fmul_rn(mn1, kLog2e)));
         }
-        const float mn0 = fmaxf(m0, t0m), mn1 = fmaxf(m1, t1m);
         const float ml0 = __fmul_rn(mn0, kLog2e), ml1 = __fmul_rn(mn1, kLog2e);
-        const float al0 = ex2(__fmaf_rn(m0, kLog2e, -ml0)), al1 = ex2(__fmaf_rn(m1, kLog2e, -ml1));
         float ps0 = 0.f, ps1 = 0.f;
         uint32_t bh[C::SUBS][2], bm[C::SUBS][2];
 #pragma unroll
@@ -735,7 +728,7 @@ __device__ __forceinline__ void worker(const AttnArgs &a, uint8_t *R, int wk, in
         l1 = __fmaf_rn(l1, al1, ps1);
         m0 = mn0;
         m1 = mn1;
-        if (__any_sync(FULL, al0 != 1.0f || al1 != 1.0f)) {
+        if (grow) {
 #pragma unroll
             for (int m = 0; m < C::KS; ++m) {
                 acc[m][0] = __fmul_rn(acc[m][0], al0);
@@ -1001,7 +994,7 @@ template <int D> void configure(bool bf16) {
 
 // ---- block descriptors ---------------------------------------------------------------------------
 
-__global__ void block_desc_kernel(const UnitDev *units, const FlatBlock *flat, const uint16_t *esc, int64_t n,
+__global__ void block_desc_kernel(const UnitDev *units, const FlatBlock *flat, const uint32_t *esc, int64_t n,
                                   int dim, bool bf16, BlockDesc *desc) {
     const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
     if (i >= n) return;
@@ -1031,7 +1024,7 @@ __global__ void block_desc_kernel(const UnitDev *units, const FlatBlock *flat, c
         const int nesc = T ? f.v_nesc : f.k_nesc;
         const uint32_t rec = T ? f.v_rec : f.k_rec;
         if (mode != 0 && nesc != 0)
-            for (int j = 0; j < 16; ++j) d.em[T][j] = esc[rec + j];
+            for (int j = 0; j < 16; ++j) d.em[T][j] = uint16_t(esc[rec + j]);
     }
     desc[i] = d;
 }
@@ -1109,7 +1102,7 @@ cudaError_t launch_combine(int dim, const CombineArgs &a, int n_split, cudaStrea
     return cudaGetLastError();
 }
 
-cudaError_t launch_block_desc(const UnitDev *units, const FlatBlock *flat, const uint16_t *esc, int64_t n,
+cudaError_t launch_block_desc(const UnitDev *units, const FlatBlock *flat, const uint32_t *esc, int64_t n,
                               int dim, bool bf16, BlockDesc *desc, cudaStream_t s) {
     if (n <= 0) return cudaSuccess;
     block_desc_kernel<<<unsigned((n + 255) / 256), 256, 0, s>>>(units, flat, esc, n, dim, bf16, desc);

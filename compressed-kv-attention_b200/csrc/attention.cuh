@@ -13,7 +13,7 @@ namespace kvx {
 struct FlatBlock {
     uint32_t k_off;   // XKV: header offset in the K blob.  BF16: first token.
     uint32_t v_off;   // XKV: header offset in the V blob.  BF16: first token.
-    uint32_t k_rec;   // escape record of the K block in the step's record array (u16 units)
+    uint32_t k_rec;   // escape record of the K block in the step's record array (u32 units)
     uint32_t v_rec;
     uint16_t k_nesc;  // escape words
     uint16_t v_nesc;
@@ -27,14 +27,15 @@ struct FlatBlock {
 };
 static_assert(sizeof(FlatBlock) == 32, "FlatBlock is 32 bytes");
 
-// Escape record of one coded block with escape words (u16 array):
+// Escape record of one coded block with escape words (u32 array):
 //   [0, 16)           e[i - 1] = escape words of tokens [0, 16 i), i = 1..16 (clamped to the
 //                     block), so the escapes of tokens [16 a, 16 b) are [e(a), e(b)), e(0) = 0;
-//   [16, 16 + n_esc)  for every escape, in the container's scan order, where the attention kernel
-//                     stores it: the byte of the element it replaces in the kernel's BF16 tile
-//                     (esc_scratch_slot of its token within the kernel's stage and its channel).
-// Built once per plan from the blob's residual codes; raw blocks and blocks without escapes
-// have none.
+//   [16, 16 + n_esc)  for every escape, in the container's scan order: the byte of the element it
+//                     replaces in the attention kernel's BF16 tile (esc_scratch_slot of its token
+//                     within the kernel's stage and its channel) in bits 0-15, the escape word
+//                     (the element's BF16 value) in bits 16-31.
+// Built once per plan from the blob's residual codes and escape words; raw blocks and blocks
+// without escapes have none.
 constexpr int kEscRecHead = 16;
 
 #ifndef KVX_TS64
@@ -109,7 +110,7 @@ struct AttnArgs {
     const UnitDev *units;
     const FlatBlock *flat;      // [n_blocks]
     const BlockDesc *desc;      // [n_blocks]
-    const uint16_t *esc;        // escape records (FlatBlock::k_rec / v_rec index it)
+    const uint32_t *esc;        // escape records (FlatBlock::k_rec / v_rec index it)
     const int64_t *range_begin; // [n_workers + 1] flat-block range of each worker warp
     float *partials;            // [n_workers][2][8 + 8 + 8 * dim]
     int *status;                // [2] first error (code, detail)
@@ -142,7 +143,7 @@ __host__ __device__ inline int worker_of_block(const int64_t *range_begin, int n
 cudaError_t launch_attention(int dim, bool bf16_input, const AttnArgs &a, int grid, cudaStream_t s);
 cudaError_t launch_combine(int dim, const CombineArgs &a, int n_split, cudaStream_t s);
 // Block descriptors of a step from its flat blocks, units and escape records.
-cudaError_t launch_block_desc(const UnitDev *units, const FlatBlock *flat, const uint16_t *esc, int64_t n,
+cudaError_t launch_block_desc(const UnitDev *units, const FlatBlock *flat, const uint32_t *esc, int64_t n,
                               int dim, bool bf16, BlockDesc *desc, cudaStream_t s);
 cudaError_t launch_fold(const float *parts, int n_parts, int n_rows, int dim, float *out,
                         float *lse_out, cudaStream_t s);
@@ -153,7 +154,7 @@ cudaError_t launch_fold(const float *parts, int n_parts, int n_rows, int dim, fl
 cudaError_t launch_esc_layout(FlatBlock *flat, int64_t n_blocks, unsigned long long *total,
                               unsigned long long cap, int *status, cudaStream_t s);
 cudaError_t launch_esc_fill(const UnitDev *units, const FlatBlock *flat, int64_t n_blocks, int dim,
-                            uint16_t *esc, unsigned long long cap, int *status, cudaStream_t s);
+                            uint32_t *esc, unsigned long long cap, int *status, cudaStream_t s);
 // Cost-balanced worker ranges over the flat block list: range_begin[0..n_workers].
 cudaError_t launch_split(const FlatBlock *flat, int64_t n_blocks, int n_workers, int64_t *range_begin,
                          cudaStream_t s);

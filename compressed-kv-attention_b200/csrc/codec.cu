@@ -545,7 +545,7 @@ __global__ void esc_dup_kernel(FlatBlock *flat, int64_t n) {
 // One warp per (block, tensor): scan the residual codes for sentinels (all ones) in scan order,
 // write their element indices and the 16-token group counts.
 __global__ void esc_fill_kernel(const UnitDev *units, const FlatBlock *flat, int64_t n, int dim,
-                                uint16_t *esc, unsigned long long cap, int *status) {
+                                uint32_t *esc, unsigned long long cap, int *status) {
     const int64_t w = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
     if (w >= 2 * n) return;
@@ -570,7 +570,7 @@ __global__ void esc_fill_kernel(const UnitDev *units, const FlatBlock *flat, int
     const uint32_t *words = reinterpret_cast<const uint32_t *>(codes - lead);
     const uint32_t nwords = (lead + len + 3) / 4;
     const int per_byte = 8 / mode;  // residuals per code byte
-    uint16_t *pos = esc + rec + kEscRecHead;
+    uint32_t *pos = esc + rec + kEscRecHead;
     int run = 0;
     for (uint32_t w0 = 0; w0 < nwords; w0 += 32) {
         const uint32_t wi = w0 + uint32_t(lane);
@@ -602,7 +602,7 @@ __global__ void esc_fill_kernel(const UnitDev *units, const FlatBlock *flat, int
         while (mask != 0u) {
             const int bit = __ffs(mask) - 1;
             mask &= mask - 1u;
-            if (idx < nesc) pos[idx] = uint16_t(e0 + bit);
+            if (idx < nesc) pos[idx] = uint32_t(e0 + bit);
             ++idx;
         }
         run += __shfl_sync(0xFFFFFFFFu, incl, 31);
@@ -616,16 +616,19 @@ __global__ void esc_fill_kernel(const UnitDev *units, const FlatBlock *flat, int
         int lo = 0, hi = m;  // first position >= limit
         while (lo < hi) {
             const int mid = (lo + hi) >> 1;
-            if (uint32_t(pos[mid]) < limit) lo = mid + 1; else hi = mid;
+            if (pos[mid] < limit) lo = mid + 1; else hi = mid;
         }
         e = lo;
     }
     __syncwarp();
-    if (lane < 16) esc[rec + lane] = uint16_t(e);
-    // element index -> the escape's byte in the attention kernel's scratch
+    if (lane < 16) esc[rec + lane] = uint32_t(e);
+    // element index -> the escape's byte in the attention kernel's tile and its word
+    const uint8_t *words16 = codes + len;  // escape words, 2-byte aligned
     for (int i = lane; i < m; i += 32) {
-        const int el = pos[i];
-        pos[i] = uint16_t(esc_scratch_slot(dim, T, (el / dim) % stage_tokens(dim), el % dim));
+        const uint32_t el = pos[i];
+        const uint32_t word = uint32_t(words16[2 * i]) | (uint32_t(words16[2 * i + 1]) << 8);
+        pos[i] = esc_scratch_slot(dim, T, int(el / uint32_t(dim)) % stage_tokens(dim), int(el % uint32_t(dim))) |
+                 (word << 16);
     }
 }
 
@@ -717,7 +720,7 @@ cudaError_t launch_esc_layout(FlatBlock *flat, int64_t n_blocks, unsigned long l
 }
 
 cudaError_t launch_esc_fill(const UnitDev *units, const FlatBlock *flat, int64_t n_blocks, int dim,
-                            uint16_t *esc, unsigned long long cap, int *status, cudaStream_t s) {
+                            uint32_t *esc, unsigned long long cap, int *status, cudaStream_t s) {
     if (n_blocks <= 0) return cudaSuccess;
     const int64_t warps = 2 * n_blocks;
     esc_fill_kernel<<<unsigned((warps + 7) / 8), 256, 0, s>>>(units, flat, n_blocks, dim, esc, cap,
