@@ -173,8 +173,12 @@ __host__ __device__ constexpr uint32_t sel_code(int j) {  // byte j of A -> byte
 // Exponent = base + residual modulo 256 like bf16_from_delta's uint8 sum (reference
 // include/kvexp/bf16.hpp:35-37).  Bytes 1 and 3 of cw may hold other residuals (< 16): times 128
 // they land in bits 15-18 of each half, which the select drops, and no carry reaches bit 23.
+// The select is written as one LOP3 (mask 0x807F807F picks sg, its complement the sum).
 __device__ __forceinline__ uint32_t merge(uint32_t sg, uint32_t cw, uint32_t b7) {
-    return (sg & 0x807F807Fu) | ((cw * 128u + b7) & 0x7F807F80u);
+    uint32_t t, w;
+    asm("mad.lo.u32 %0, %1, 128, %2;" : "=r"(t) : "r"(cw), "r"(b7));
+    asm("lop3.b32 %0, %1, %2, 0x807F807F, 0xE4;" : "=r"(w) : "r"(sg), "r"(t));
+    return w;
 }
 
 // How this lane reads one tensor of the current block from a ring stage: the 8-element chunk c8
