@@ -44,10 +44,11 @@ constexpr uint32_t FULL = 0xFFFFFFFFu;
 constexpr int TT = 16;  // tokens per MMA tile (one m16 block of the QK MMA)
 constexpr float kLog2e = 1.4426950408889634f;
 
-// 2^x by the SFU (ex2.approx.f32, subnormal results kept).
+// 2^x by the SFU (ex2.approx.ftz.f32: one instruction; results below 2^-126, softmax weights
+// under 1e-38 of the largest, flush to zero).
 __device__ __forceinline__ float ex2(float x) {
     float y;
-    asm("ex2.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
     return y;
 }
 
@@ -938,14 +939,14 @@ __global__ void fold_kernel(const float *__restrict__ parts, int n_parts, int n_
 
 // ---- worker ranges -----------------------------------------------------------------------------
 
-// Cost of one flat block for the worker split: 8 per attended token plus kEscCost per escape word
-// (a worker's time grows with its tokens and, on escape-dense blocks, with its escape words).
-#ifndef KVX_ESC_COST
-#define KVX_ESC_COST 4
-#endif
-constexpr uint32_t kEscCost = KVX_ESC_COST;
+// Cost of one flat block for the worker split, per attended token and tensor: 4 with 4-bit
+// residuals, 5 with 2-bit ones (more unpacking), 2 for raw rows; plus 1 per escape word, which
+// costs a lane one staged load and one store.  (Weighting escapes near a token's cost, as an
+// earlier model did, starved the workers that hold escape-dense blocks and left the others
+// about 10 % more work than a balanced split.)
+__device__ __forceinline__ uint64_t mode_cost(int mode) { return mode == 4 ? 4u : (mode == 2 ? 5u : 2u); }
 __device__ __forceinline__ uint64_t block_cost(const FlatBlock &b) {
-    return 8ull * b.valid + kEscCost * (uint64_t(b.k_nesc) + b.v_nesc);
+    return uint64_t(b.valid) * (mode_cost(b.k_mode) + mode_cost(b.v_mode)) + uint64_t(b.k_nesc) + b.v_nesc;
 }
 
 // One CTA: range_begin[w] = first block whose cost prefix reaches w * total / n_workers.
