@@ -71,19 +71,20 @@ template <int D> struct Cfg {
     static constexpr int CODE_OFF = TS * D + 16;
     static constexpr int EE_OFF = CODE_OFF + TS * D / 2 + 16;
     static constexpr int TR = round16(cmax(EE_OFF + 4 * ESC_CAP + 16, TS * 2 * D + 16));
-    static constexpr int SLOT = 2 * TR;  // K stage | V stage
-    static constexpr int NSTAGE = D <= 32 ? 3 : 2;
+    // Ring of tensor-stages: K of stage s, V of stage s, K of stage s + 1, ...  A slot is free
+    // again once its tensor is in the tile, so three slots keep one stage of copies in flight.
+    static constexpr int NSLOT = 3;
     static constexpr int BASE = round16(D + 32);  // one block's base exponents (+ alignment slack)
     static constexpr int MSLOT = 2 * BASE;        // per-block meta slot: K base | V base
     static constexpr int XB = TS * 2 * D;         // the BF16 tile of one tensor's stage
     static constexpr int NDESC = 4;               // block descriptor ring
     // per-warp region: ring | meta x2 | tile | descriptors | one mbarrier per ring slot and
     // per descriptor
-    static constexpr int W_META = NSTAGE * SLOT;
+    static constexpr int W_META = NSLOT * TR;
     static constexpr int W_XB = W_META + 2 * MSLOT;
     static constexpr int W_DESC = W_XB + XB;
     static constexpr int W_BAR = W_DESC + NDESC * int(sizeof(BlockDesc));
-    static constexpr int W_DBAR = W_BAR + 8 * NSTAGE;
+    static constexpr int W_DBAR = W_BAR + 8 * NSLOT;
     static constexpr int WARP_BYTES = (W_DBAR + 8 * NDESC + 127) & ~127;
     static constexpr int MAXW = D <= 32 ? 16 : KVX_MAXWARPS;
     static constexpr int WARPS = cmin(MAXW, 232448 / WARP_BYTES);
@@ -457,7 +458,7 @@ template <int D, bool BF16IN> struct Producer {
     int fb, fb0, fb1;  // next block to start; the worker's range
     int pf;            // next block whose descriptor is fetched
     int dwait;         // next block whose descriptor is waited for
-    int tile = 0, stage = 0, bseq = 0;
+    int tile = 0, q = 0, bseq = 0;  // q: tensor-stages issued (2 per stage, K first)
     int valid = 0;     // tokens of the block being issued
     uint32_t em = 0u;  // lane l: entry l % 16 of its K (l < 16) / V count header
     // This lane's piece of every stage of the current block.  Lane 4 T + j (j < 4) copies piece j
@@ -502,7 +503,7 @@ template <int D, bool BF16IN> struct Producer {
         src = nullptr;
         stride = 0;
         kind = 0;
-        dst = uint32_t(T * C::TR);
+        dst = 0u;
         if (lane < 8) {
             if (j == 0) {
                 src = sc.rows;
@@ -528,22 +529,28 @@ template <int D, bool BF16IN> struct Producer {
         return true;
     }
 
-    // Issue stages while a ring slot is free; a block start waits until the consumer is at most
-    // one block behind, so a meta slot is never overwritten while in use.  The slot's previous
-    // stage was read by the whole warp before this call (__syncwarp at the end of every stage).
-    // The pieces of a stage go out in parallel, one bulk copy per lane; lane 0 first tells the
-    // slot's barrier how many bytes to expect.  False when a descriptor did not arrive in time.
-    __device__ __forceinline__ bool produce(const AttnArgs &a, uint8_t *R, int c_stage, int c_fb, int lane) {
-        while (fb < fb1 && stage - c_stage < C::NSTAGE) {
-            if (tile == 0 && fb - c_fb >= 2) break;
-            const int slot = stage % C::NSTAGE;
+    // Issue tensor-stages while a ring slot is free (the consumer is done with every one before
+    // c_q); a block start waits until the consumer is at most one block behind, so a meta slot is
+    // never overwritten while in use.  A slot's previous tensor was read by the whole warp before
+    // this call (__syncwarp after every tensor's decode).  The pieces of a tensor-stage go out in
+    // parallel, one bulk copy per lane (lanes 4 T .. 4 T + 2, and 8 and 9 with a block's first K);
+    // lane 0 first tells the slot's barrier how many bytes to expect.  False when a descriptor
+    // did not arrive in time.
+    __device__ __forceinline__ bool produce(const AttnArgs &a, uint8_t *R, int c_q, int c_fb, int lane) {
+        while (fb < fb1 && q - c_q < C::NSLOT) {
+            const int T = q & 1;
+            if (T == 0 && tile == 0) {
+                if (fb - c_fb >= 2) break;
+                if (!start_block(a, R, lane)) return false;
+            }
+            const int slot = q % C::NSLOT;
             const uint32_t bar = smem_u32(R + C::W_BAR + 8 * slot);
             const uint32_t ms = smem_u32(R + C::W_META + (bseq & 1) * C::MSLOT);
-            if (tile == 0 && !start_block(a, R, lane)) return false;
             const int t0 = tile * C::TS;
             const int n = min(C::TS, valid - t0);
-            const int T = (lane >> 2) & 1;
-            const int e0 = esc_at(em, T, t0 >> 4), e1 = esc_at(em, T, min(16, (t0 + C::TS) >> 4));
+            const int LT = (lane >> 2) & 1;  // the tensor of lanes 0-7's pieces
+            const int e0 = esc_at(em, LT, t0 >> 4), e1 = esc_at(em, LT, min(16, (t0 + C::TS) >> 4));
+            const bool now = lane < 8 ? LT == T : (T == 0 && tile == 0);
             const uint8_t *p;
             uint32_t len;
             if (kind == 2) {
@@ -551,9 +558,10 @@ template <int D, bool BF16IN> struct Producer {
                 len = e1 - e0 <= C::ESC_CAP ? uint32_t(4 * (e1 - e0)) : 0u;
             } else {
                 p = src + size_t(t0) * stride;
-                len = kind == 1 ? uint32_t(n) * stride : (kind == 3 && tile == 0 ? uint32_t(D) : 0u);
+                len = kind == 1 ? uint32_t(n) * stride : (kind == 3 ? uint32_t(D) : 0u);
             }
-            const uint32_t d = kind == 3 ? ms + dst : smem_u32(R + slot * C::SLOT) + dst;
+            if (!now) len = 0u;
+            const uint32_t d = kind == 3 ? ms + dst : smem_u32(R + slot * C::TR) + dst;
             const Piece pc = make_piece(p, len);
             const uint32_t bytes = len != 0 ? pc.alloc : 0u;
             const uint32_t total = __reduce_add_sync(FULL, bytes);
@@ -561,14 +569,16 @@ template <int D, bool BF16IN> struct Producer {
             if (lane == 0) mbar_arrive_expect_tx(bar, total);
             __syncwarp();
             if (bytes != 0) bulk_g2s(d, pc.src, bytes, bar);
-            ++stage;
-            if (t0 + C::TS >= valid) {
-                tile = 0;
-                ++bseq;
-                ++fb;
-                fetch(a, R, lane);
-            } else {
-                ++tile;
+            ++q;
+            if (T == 1) {
+                if (t0 + C::TS >= valid) {
+                    tile = 0;
+                    ++bseq;
+                    ++fb;
+                    fetch(a, R, lane);
+                } else {
+                    ++tile;
+                }
             }
         }
         return true;
@@ -612,7 +622,7 @@ __device__ __forceinline__ void worker(const AttnArgs &a, uint8_t *R, int wk, in
     smap.init(xb, lane);
     if (lane == 0) {
 #pragma unroll
-        for (int j = 0; j < C::NSTAGE; ++j) mbar_init(smem_u32(bars + 8 * j), 1);
+        for (int j = 0; j < C::NSLOT; ++j) mbar_init(smem_u32(bars + 8 * j), 1);
 #pragma unroll
         for (int j = 0; j < C::NDESC; ++j) mbar_init(smem_u32(R + C::W_DBAR + 8 * j), 1);
         fence_mbar_init();
@@ -622,7 +632,7 @@ __device__ __forceinline__ void worker(const AttnArgs &a, uint8_t *R, int wk, in
     pp.fb = pp.fb0 = pp.pf = pp.dwait = fb0;
     pp.fb1 = fb1;
     pp.fetch(a, R, lane);
-    int fb = fb0, tile = 0, stage = 0, bseq = 0;
+    int fb = fb0, tile = 0, cq = 0, bseq = 0;  // cq: the next tensor-stage to consume
     int seg_begin = fb0;
     uint32_t flags = 0u, whole = 0u;  // the block's flags; the segment began at its unit's start
     Lay lk{}, lv{};
@@ -631,17 +641,22 @@ __device__ __forceinline__ void worker(const AttnArgs &a, uint8_t *R, int wk, in
     float acc[C::KS][4];
     float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
 
+    // Tensor-stage q's slot barrier and its phase for that use.
+    auto slot_bar = [&](int q) { return smem_u32(bars + 8 * (q % C::NSLOT)); };
+    auto slot_par = [&](int q) { return uint32_t((q / C::NSLOT) & 1); };
+    // After a timeout: report it and let the copies already issued land before this CTA's
+    // shared memory goes away.
+    auto fail = [&]() {
+        if (lane == 0) report(a.status, KVX_ERR_TIMEOUT, DERR_TIMEOUT);
+        for (int q = cq; q < pp.q; ++q) mbar_wait_bounded(slot_bar(q), slot_par(q), kStageWaitUs);
+        for (int b = pp.dwait; b < pp.pf; ++b)
+            mbar_wait_bounded(smem_u32(R + C::W_DBAR + 8 * ((b - fb0) % C::NDESC)),
+                              ((b - fb0) / C::NDESC) & 1, kStageWaitUs);
+    };
+
     while (fb < fb1) {
-        if (!pp.produce(a, R, stage, fb, lane) ||
-            !mbar_wait_bounded(smem_u32(bars + 8 * (stage % C::NSTAGE)), (stage / C::NSTAGE) & 1,
-                               kStageWaitUs)) {
-            if (lane == 0) report(a.status, KVX_ERR_TIMEOUT, DERR_TIMEOUT);
-            // let the copies already issued land before this CTA's shared memory goes away
-            for (int q = stage; q < pp.stage; ++q)
-                mbar_wait_bounded(smem_u32(bars + 8 * (q % C::NSTAGE)), (q / C::NSTAGE) & 1, kStageWaitUs);
-            for (int b = pp.dwait; b < pp.pf; ++b)
-                mbar_wait_bounded(smem_u32(R + C::W_DBAR + 8 * ((b - fb0) % C::NDESC)),
-                                  ((b - fb0) / C::NDESC) & 1, kStageWaitUs);
+        if (!pp.produce(a, R, cq, fb, lane) || !mbar_wait_bounded(slot_bar(cq), slot_par(cq), kStageWaitUs)) {
+            fail();
             return;
         }
         __syncwarp();
@@ -668,7 +683,8 @@ __device__ __forceinline__ void worker(const AttnArgs &a, uint8_t *R, int wk, in
                 for (int m = 0; m < C::KS; ++m) acc[m][0] = acc[m][1] = acc[m][2] = acc[m][3] = 0.f;
             }
         }
-        const uint32_t kst = smem_u32(ring + (stage % C::NSTAGE) * C::SLOT), vst = kst + C::TR;
+        const uint32_t kst = smem_u32(ring + (cq % C::NSLOT) * C::TR);
+        const uint32_t vst = smem_u32(ring + ((cq + 1) % C::NSLOT) * C::TR);
         const int t0 = tile * C::TS;
         const int rows = min(C::TS, valid - t0);
         const bool last_tile = t0 + C::TS >= valid;
@@ -677,6 +693,11 @@ __device__ __forceinline__ void worker(const AttnArgs &a, uint8_t *R, int wk, in
 
         // S^T = K Q^T for every tile of the stage
         stage_tile<D>(a, bd, 0, kmode, kst, xb, smap, lk, b7k, ia, ib, rows, C::TS, lane);
+        ++cq;  // K's slot is free: the next copies can go out while the tensor cores work
+        if (!pp.produce(a, R, cq, fb, lane)) {
+            fail();
+            return;
+        }
         // (a stage's rows past `rows` hold stale words: their scores are dropped below)
         float s[C::SUBS][4];
         qk_tiles<D, C::SUBS>(xb, qb, lane, s);
@@ -745,8 +766,13 @@ __device__ __forceinline__ void worker(const AttnArgs &a, uint8_t *R, int wk, in
 
         // O^T += V^T P^T for every tile of the stage (the tile's K reads are done: stage_tile
         // ends with __syncwarp, and the K tiles were read before the softmax)
+        if (!mbar_wait_bounded(slot_bar(cq), slot_par(cq), kStageWaitUs)) {
+            fail();
+            return;
+        }
         __syncwarp();
         stage_tile<D>(a, bd, 1, vmode, vst, xb, smap, lv, b7v, ia, ib, rows, rows, lane);
+        ++cq;
 #pragma unroll
         for (int sub = 0; sub < C::SUBS; ++sub)
             if (sub * TT < rows) pv_tile<D>(xb, sub * TT, bh[sub], bm[sub], lane, acc);
@@ -807,7 +833,6 @@ __device__ __forceinline__ void worker(const AttnArgs &a, uint8_t *R, int wk, in
             }
         }
         __syncwarp();  // every lane is done with this ring slot and the tile before they are reused
-        ++stage;
         if (last_tile) {
             tile = 0;
             ++bseq;
