@@ -53,6 +53,10 @@ __device__ __forceinline__ float ex2(float x) {
 }
 
 __host__ __device__ constexpr int round16(int x) { return (x + 15) & ~15; }
+
+// One verdict for the whole warp on a condition its lanes may see differently (a bounded wait that
+// times out in some lanes just as the phase completes for others).
+__device__ __forceinline__ bool uni(bool c) { return __all_sync(0xFFFFFFFFu, c); }
 __host__ __device__ constexpr int cmin(int a, int b) { return a < b ? a : b; }
 __host__ __device__ constexpr int cmax(int a, int b) { return a > b ? a : b; }
 
@@ -489,7 +493,7 @@ template <int D, bool BF16IN> struct Producer {
 
     __device__ __forceinline__ bool start_block(const AttnArgs &a, uint8_t *R, int lane) {
         const int i = (fb - fb0) % C::NDESC;
-        if (!mbar_wait_bounded(smem_u32(R + C::W_DBAR + 8 * i), ((fb - fb0) / C::NDESC) & 1, kStageWaitUs))
+        if (!uni(mbar_wait_bounded(smem_u32(R + C::W_DBAR + 8 * i), ((fb - fb0) / C::NDESC) & 1, kStageWaitUs)))
             return false;
         dwait = fb + 1;
         const BlockDesc &bd = *reinterpret_cast<const BlockDesc *>(R + C::W_DESC + i * int(sizeof(BlockDesc)));
@@ -655,7 +659,7 @@ __device__ __forceinline__ void worker(const AttnArgs &a, uint8_t *R, int wk, in
     };
 
     while (fb < fb1) {
-        if (!pp.produce(a, R, cq, fb, lane) || !mbar_wait_bounded(slot_bar(cq), slot_par(cq), kStageWaitUs)) {
+        if (!pp.produce(a, R, cq, fb, lane) || !uni(mbar_wait_bounded(slot_bar(cq), slot_par(cq), kStageWaitUs))) {
             fail();
             return;
         }
@@ -766,7 +770,7 @@ __device__ __forceinline__ void worker(const AttnArgs &a, uint8_t *R, int wk, in
 
         // O^T += V^T P^T for every tile of the stage (the tile's K reads are done: stage_tile
         // ends with __syncwarp, and the K tiles were read before the softmax)
-        if (!mbar_wait_bounded(slot_bar(cq), slot_par(cq), kStageWaitUs)) {
+        if (!uni(mbar_wait_bounded(slot_bar(cq), slot_par(cq), kStageWaitUs))) {
             fail();
             return;
         }
