@@ -72,6 +72,23 @@ struct DevBuf {
     template <class T> T *as() const { return static_cast<T *>(p); }
 };
 
+struct EventGuard {
+    cudaEvent_t e = nullptr;
+    ~EventGuard() {
+        if (e) cudaEventDestroy(e);
+    }
+};
+
+// Drains two streams when it goes out of scope: buffers declared before it outlive every kernel
+// and copy that either stream may still run, on every return path.
+struct DrainGuard {
+    cudaStream_t a, b;
+    ~DrainGuard() {
+        cudaStreamSynchronize(a);
+        cudaStreamSynchronize(b);
+    }
+};
+
 bool is_device_ptr(const void *p) {
     if (p == nullptr) return false;
     cudaPointerAttributes a{};
@@ -82,12 +99,41 @@ bool is_device_ptr(const void *p) {
     return a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged;
 }
 
+constexpr int kMaxDevices = 64;
+
 int check_device() {
     int dev = 0;
     KVX_CUDA(cudaGetDevice(&dev));
     int major = 0;
     KVX_CUDA(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev));
     if (major != 10) return fail(KVX_ERR_RUNTIME, "kvexp_b200 needs an sm_100 (B200) device");
+    // The host-buffer entry points take their per-call arenas from the device's default memory
+    // pool; let the pool keep up to 1 GiB between calls instead of returning it to the driver at
+    // every synchronisation (re-mapping a few hundred MB each call costs milliseconds).
+    static std::once_flag pool_once[kMaxDevices];
+    if (dev >= 0 && dev < kMaxDevices)
+        std::call_once(pool_once[dev], [dev] {
+            cudaMemPool_t pool;
+            if (cudaDeviceGetDefaultMemPool(&pool, dev) == cudaSuccess) {
+                uint64_t keep = uint64_t(1) << 30;
+                cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep);
+            }
+            cudaGetLastError();
+        });
+    return KVX_OK;
+}
+
+// A non-blocking stream per device for host -> device copies of the host-buffer entry points, so
+// that work on the legacy stream (plan creation) does not wait for them.
+int copy_stream(cudaStream_t *out) {
+    static std::mutex mu;
+    static cudaStream_t streams[kMaxDevices] = {};
+    int dev = 0;
+    KVX_CUDA(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= kMaxDevices) return fail(KVX_ERR_RUNTIME, "kvexp_b200: device index out of range");
+    std::lock_guard<std::mutex> lock(mu);
+    if (streams[dev] == nullptr) KVX_CUDA(cudaStreamCreateWithFlags(&streams[dev], cudaStreamNonBlocking));
+    *out = streams[dev];
     return KVX_OK;
 }
 
@@ -229,9 +275,16 @@ struct kvx_plan_s {
     float *partials = nullptr;
     int4 *split_units = nullptr;  // {unit, first worker, workers} of each split unit
     int *status = nullptr;
+    // Internal plans of the host-buffer entry points take their arrays from the device's memory
+    // pool (stream-ordered on the legacy stream) and are destroyed only after that stream has
+    // drained; plans made by kvx_plan_create use cudaMalloc / cudaFree.
+    bool pooled = false;
     std::vector<void *> owned;
     ~kvx_plan_s() {
-        for (void *p : owned) cudaFree(p);
+        for (void *p : owned) {
+            if (pooled) cudaFreeAsync(p, nullptr);
+            else cudaFree(p);
+        }
     }
 };
 
@@ -239,13 +292,19 @@ namespace {
 
 template <class T> cudaError_t plan_alloc(kvx_plan_s *p, T **dst, size_t n) {
     void *q = nullptr;
-    cudaError_t e = cudaMalloc(&q, n ? n * sizeof(T) : 16);
+    cudaError_t e = p->pooled ? cudaMallocAsync(&q, n ? n * sizeof(T) : 16, nullptr)
+                              : cudaMalloc(&q, n ? n * sizeof(T) : 16);
     if (e == cudaSuccess) {
         p->owned.push_back(q);
         *dst = static_cast<T *>(q);
     }
     return e;
 }
+
+struct PlanGuard {
+    kvx_plan_s *p;
+    ~PlanGuard() { delete p; }
+};
 
 int read_status(int *dev_status, bool reset) {
     int st[2] = {0, 0};
@@ -281,8 +340,14 @@ int kvx_device_info(int *sm_major, int *sm_minor, int *sms, size_t *hbm_bytes) {
     return KVX_OK;
 }
 
-int kvx_plan_create(const kvx_unit *units, int n_units, int n_q, int dim, int block_tokens,
-                    kvx_plan *out) {
+// Plan creation.  `pooled`: the plan's arrays come from the device's memory pool (internal
+// plans).  `blobs_ready`: when given, the blob contents may still be in flight on another stream;
+// everything that reads only the block indexes (flat list, escape record sizes, worker split) is
+// done at once, and the escape records and block descriptors, which read the blobs, are enqueued
+// on the legacy stream behind the event, without waiting on the host; their errors then surface
+// at kvx_plan_check after the run.
+static int plan_create_impl(const kvx_unit *units, int n_units, int n_q, int dim, int block_tokens,
+                            kvx_plan *out, bool pooled, cudaEvent_t blobs_ready) {
     if (out == nullptr || units == nullptr || n_units <= 0 || n_q <= 0 || block_tokens <= 0 ||
         block_tokens > 255)
         return fail(KVX_ERR_INVALID_ARGUMENT, "kvx_plan_create: bad argument");
@@ -333,6 +398,7 @@ int kvx_plan_create(const kvx_unit *units, int n_units, int n_q, int dim, int bl
     if (total > int64_t(0x7FFFFFFF))
         return fail(KVX_ERR_UNSUPPORTED, "kvx_plan_create: more than 2^31 - 1 blocks in one step");
     auto *p = new kvx_plan_s();
+    p->pooled = pooled;
     p->dim = dim;
     p->bf16 = bf16;
     p->n_units = int(vu.size());
@@ -378,17 +444,9 @@ int kvx_plan_create(const kvx_unit *units, int n_units, int n_q, int dim, int bl
         return fail(KVX_ERR_UNSUPPORTED, "kvx_plan_create: more than 2^32 escape record entries");
     }
     if (e == cudaSuccess) e = plan_alloc(p, &p->esc, size_t(esc_total));
-    if (e == cudaSuccess && esc_total > 0)
-        e = launch_esc_fill(p->units, p->flat, total, dim, p->esc, esc_total, p->status, nullptr);
-    if (e == cudaSuccess) e = launch_block_desc(p->units, p->flat, p->esc, total, dim, bf16, p->desc, nullptr);
-    if (e == cudaSuccess) e = cudaDeviceSynchronize();
     if (e != cudaSuccess) {
         delete p;
         return fail(KVX_ERR_CUDA, std::string("kvx_plan_create: ") + cudaGetErrorString(e));
-    }
-    if (int rc = read_status(p->status, true)) {
-        delete p;
-        return rc;
     }
     // Worker ranges of about equal cost (tokens and escape words), then the units whose blocks
     // span several workers (they need the combine pass).
@@ -421,9 +479,35 @@ int kvx_plan_create(const kvx_unit *units, int n_units, int n_q, int dim, int bl
         return fail(KVX_ERR_CUDA, std::string("kvx_plan_create: ") + cudaGetErrorString(e));
     }
     p->n_split = int(split.size());
+    // errors of the flat list and the record layout (the copies above waited for those kernels)
+    if (int rc = read_status(p->status, true)) {
+        delete p;
+        return rc;
+    }
+    // escape records and block descriptors read the blobs
+    if (blobs_ready != nullptr) e = cudaStreamWaitEvent(nullptr, blobs_ready, 0);
+    if (e == cudaSuccess && esc_total > 0)
+        e = launch_esc_fill(p->units, p->flat, total, dim, p->esc, esc_total, p->status, nullptr);
+    if (e == cudaSuccess) e = launch_block_desc(p->units, p->flat, p->esc, total, dim, bf16, p->desc, nullptr);
+    if (e == cudaSuccess && blobs_ready == nullptr) e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) {
+        delete p;
+        return fail(KVX_ERR_CUDA, std::string("kvx_plan_create: ") + cudaGetErrorString(e));
+    }
+    if (blobs_ready == nullptr) {
+        if (int rc = read_status(p->status, true)) {
+            delete p;
+            return rc;
+        }
+    }
     *out = p;
     g_err.clear();
     return KVX_OK;
+}
+
+int kvx_plan_create(const kvx_unit *units, int n_units, int n_q, int dim, int block_tokens,
+                    kvx_plan *out) {
+    return plan_create_impl(units, n_units, n_q, dim, block_tokens, out, false, nullptr);
 }
 
 int kvx_plan_run(kvx_plan p, void *stream) {
@@ -647,7 +731,10 @@ extern "C" int kvx_attention_decode_units(int backend, int n_units, const uint16
             return rc;
     if (int rc = check_device()) return rc;
     cudaStream_t s = nullptr;
-    // one device arena for every host blob and query, copied with one transfer per buffer
+    // One device arena for every host blob and query, copied with one transfer per buffer on the
+    // copy stream; the host walks the headers and builds the plan while the copies run.
+    cudaStream_t sc = nullptr;
+    if (int rc = copy_stream(&sc)) return rc;
     std::vector<size_t> koff(static_cast<size_t>(n_units)), voff(static_cast<size_t>(n_units)), qoff(static_cast<size_t>(n_units));
     size_t arena = 0;
     auto place = [&](size_t bytes) {
@@ -664,18 +751,22 @@ extern "C" int kvx_attention_decode_units(int backend, int n_units, const uint16
     const size_t out_at = arena;
     arena += size_t(n_units) * out_bytes;
     DevBuf ar;
-    KVX_CUDA(ar.alloc(arena, s));
+    KVX_CUDA(ar.alloc(arena, sc));
+    DrainGuard drain{s, sc};
     uint8_t *A = ar.as<uint8_t>();
     std::vector<HostIndex> kidx(static_cast<size_t>(n_units)), vidx(static_cast<size_t>(n_units));
     for (int u = 0; u < n_units; ++u) {
         if (koff[size_t(u)] != SIZE_MAX)
-            KVX_CUDA(cudaMemcpyAsync(A + koff[size_t(u)], k_xkv[u], k_bytes[u], cudaMemcpyHostToDevice, s));
+            KVX_CUDA(cudaMemcpyAsync(A + koff[size_t(u)], k_xkv[u], k_bytes[u], cudaMemcpyHostToDevice, sc));
         if (voff[size_t(u)] != SIZE_MAX)
-            KVX_CUDA(cudaMemcpyAsync(A + voff[size_t(u)], v_xkv[u], v_bytes[u], cudaMemcpyHostToDevice, s));
+            KVX_CUDA(cudaMemcpyAsync(A + voff[size_t(u)], v_xkv[u], v_bytes[u], cudaMemcpyHostToDevice, sc));
         if (qoff[size_t(u)] != SIZE_MAX)
             KVX_CUDA(cudaMemcpyAsync(A + qoff[size_t(u)], q[u], size_t(n_q) * dim * 2,
-                                     cudaMemcpyHostToDevice, s));
+                                     cudaMemcpyHostToDevice, sc));
     }
+    EventGuard copied;
+    KVX_CUDA(cudaEventCreateWithFlags(&copied.e, cudaEventDisableTiming));
+    KVX_CUDA(cudaEventRecord(copied.e, sc));
     // header walks of the host blobs overlap the transfers
     std::vector<DevBlob> dk(static_cast<size_t>(n_units)), dv(static_cast<size_t>(n_units));
     std::vector<kvx_unit> units(static_cast<size_t>(n_units));
@@ -734,13 +825,22 @@ extern "C" int kvx_attention_decode_units(int backend, int n_units, const uint16
         x.n_blocks = int(kidx[size_t(u)].blocks.size());
         x.seq = seq;
     }
-    if (int rc = run_units(units, n_q, dim, 128, s)) return rc;
-    for (int u = 0; u < n_units; ++u)
+    // Plan (its blob readers wait for the copies), run and the output copies, all on the legacy
+    // stream; one synchronisation at the end, then the plan's status.
+    kvx_plan plan = nullptr;
+    if (int rc = plan_create_impl(units.data(), n_units, n_q, dim, 128, &plan, true, copied.e))
+        return rc;
+    PlanGuard pg{plan};
+    int rc = kvx_plan_run(plan, s);
+    for (int u = 0; rc == KVX_OK && u < n_units; ++u)
         KVX_CUDA(cudaMemcpyAsync(out[u], A + out_at + size_t(u) * out_bytes, out_bytes,
                                  is_device_ptr(out[u]) ? cudaMemcpyDeviceToDevice
                                                        : cudaMemcpyDeviceToHost,
                                  s));
     KVX_CUDA(cudaStreamSynchronize(s));
+    KVX_CUDA(cudaStreamSynchronize(sc));
+    if (rc == KVX_OK) rc = kvx_plan_check(plan);
+    if (rc != KVX_OK) return rc;
     g_err.clear();
     return KVX_OK;
 }

@@ -73,7 +73,10 @@ KVX_API int kvx_attention_decode(int backend, const uint16_t *q, const uint16_t 
 /* Batched form of the reference's per-head loop (src/bench.cpp:711-728 `model_heads`): n_units
  * independent attention_decode calls over XKV blobs, all with the same n_q, dim, seq, run as one
  * GPU job.  Pointer arrays live in host memory; the pointers they hold may be host or device.
- * With host buffers the library streams blobs to the GPU and overlaps copies with compute. */
+ * With host buffers the blobs go to the GPU on a library-owned non-blocking stream while the host
+ * walks their headers and builds the step's plan; the call returns when the outputs are back.
+ * Its device buffers come from the device's default CUDA memory pool, whose release threshold
+ * the library raises to 1 GiB (the pool then keeps up to 1 GiB between calls). */
 KVX_API int kvx_attention_decode_units(int backend, int n_units, const uint16_t *const *q,
                                const uint8_t *const *k_xkv, const size_t *k_bytes,
                                const uint8_t *const *v_xkv, const size_t *v_bytes,
