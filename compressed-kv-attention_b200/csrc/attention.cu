@@ -852,6 +852,9 @@ template <int D, bool BF16IN>
 __global__ void __launch_bounds__(32 * Cfg<D>::WARPS, 1) attn_kernel(const AttnArgs a) {
     using C = Cfg<D>;
     extern __shared__ __align__(128) uint8_t smem[];
+    // A combine pass launched behind this grid (programmatic dependent launch) may start placing
+    // its CTAs as soon as SMs free up; it waits for this grid's completion before reading.
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     // consecutive workers on different SMs: neighbouring ranges often share a cost profile
     const int wk = warp * gridDim.x + blockIdx.x;
@@ -876,8 +879,13 @@ constexpr int kMaxSegments = 4096;
 template <int D>
 __global__ void __launch_bounds__(kCombineThreads) combine_kernel(const CombineArgs a) {
     constexpr int S = kCombineThreads / D;  // segment slices summed in parallel
+    constexpr int PRE = 8;                  // accumulator values a thread loads up front
     __shared__ float e[kMaxSegments];
+    __shared__ float lw[kMaxSegments];
     __shared__ float red[kCombineThreads];
+    // launched as a dependent of the attention grid: its partial states are complete and visible
+    // after this wait (a no-op for an ordinary launch)
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     const int4 sp = a.split[blockIdx.x];
     const int g = blockIdx.y;
     const UnitDev unit = a.units[sp.x];
@@ -892,10 +900,21 @@ __global__ void __launch_bounds__(kCombineThreads) combine_kernel(const CombineA
         return a.partials + (size_t(t) * 2 + (i == 0 ? sp.w : 0)) * ps;
     };
     const int tid = threadIdx.x;
+    const int d = tid % D, sl = tid / D;
+    // every load that does not depend on M goes out first: (m, l) of the segments and the first
+    // PRE accumulator values of this thread's slice
+    float pre[PRE];
+#pragma unroll
+    for (int k = 0; k < PRE; ++k) {
+        const int i = sl + k * S;
+        pre[k] = (sl < S && i < nt) ? __ldg(part(i) + 16 + g * D + d) : 0.f;
+    }
     float mx = -INFINITY;
     for (int i = tid; i < nt; i += kCombineThreads) {
-        const float m = part(i)[g];
+        const float *pi = part(i);
+        const float m = __ldg(pi + g);
         e[i] = m;
+        lw[i] = __ldg(pi + 8 + g);
         mx = fmaxf(mx, m);
     }
     red[tid] = mx;
@@ -910,7 +929,7 @@ __global__ void __launch_bounds__(kCombineThreads) combine_kernel(const CombineA
     for (int i = tid; i < nt; i += kCombineThreads) {
         const float w = expf(e[i] - M);
         e[i] = w;
-        ls = __fmaf_rn(part(i)[8 + g], w, ls);
+        ls = __fmaf_rn(lw[i], w, ls);
     }
     red[tid] = ls;
     __syncthreads();
@@ -921,10 +940,14 @@ __global__ void __launch_bounds__(kCombineThreads) combine_kernel(const CombineA
     const float lsum = red[0];
     const float inv = __frcp_rn(lsum);
     __syncthreads();
-    const int d = tid % D, sl = tid / D;
     float acc = 0.f;
-    if (sl < S)
-        for (int i = sl; i < nt; i += S) acc = __fmaf_rn(part(i)[16 + g * D + d], e[i], acc);
+    if (sl < S) {
+#pragma unroll
+        for (int k = 0; k < PRE; ++k)
+            if (sl + k * S < nt) acc = __fmaf_rn(pre[k], e[sl + k * S], acc);
+#pragma unroll 8
+        for (int i = sl + PRE * S; i < nt; i += S) acc = __fmaf_rn(__ldg(part(i) + 16 + g * D + d), e[i], acc);
+    }
     red[tid] = acc;
     __syncthreads();
     if (sl == 0) {
@@ -1125,15 +1148,25 @@ cudaError_t launch_fold(const float *parts, int n_parts, int n_rows, int dim, fl
 
 cudaError_t launch_combine(int dim, const CombineArgs &a, int n_split, cudaStream_t s) {
     if (n_split <= 0) return cudaSuccess;
-    const dim3 grid(n_split, 8);  // (split unit, query); units hold at most 8 queries
+    // (split unit, query); units hold at most 8 queries.  Programmatic dependent launch: the grid
+    // may be set up while the attention grid before it drains (the kernel waits for it).
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(n_split, 8);
+    cfg.blockDim = dim3(kCombineThreads);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
     switch (dim) {
-    case 32: combine_kernel<32><<<grid, kCombineThreads, 0, s>>>(a); break;
-    case 64: combine_kernel<64><<<grid, kCombineThreads, 0, s>>>(a); break;
-    case 128: combine_kernel<128><<<grid, kCombineThreads, 0, s>>>(a); break;
-    case 256: combine_kernel<256><<<grid, kCombineThreads, 0, s>>>(a); break;
+    case 32: return cudaLaunchKernelEx(&cfg, combine_kernel<32>, a);
+    case 64: return cudaLaunchKernelEx(&cfg, combine_kernel<64>, a);
+    case 128: return cudaLaunchKernelEx(&cfg, combine_kernel<128>, a);
+    case 256: return cudaLaunchKernelEx(&cfg, combine_kernel<256>, a);
     default: return cudaErrorInvalidValue;
     }
-    return cudaGetLastError();
 }
 
 cudaError_t launch_block_desc(const UnitDev *units, const FlatBlock *flat, const uint32_t *esc, int64_t n,
