@@ -184,6 +184,29 @@ def test_units_batch_matches_single(kvx, cuda, oracle):
         assert np.max(np.abs(a - b) / scale) < 1e-4
 
 
+def test_units_batch_error_then_recovery(kvx, cuda, oracle):
+    """With host buffers the blobs are still being copied when a header walk fails: the call
+    reports the reference's error, and the next call (same buffers, fixed) is unaffected."""
+    dim, n_q, seq = 64, 7, 700
+    qs, kxs, vxs, singles = [], [], [], []
+    for u in range(4):
+        q, k, v = _case(dim, n_q, seq, seed=300 + u)
+        kx, vx = oracle.encode(k, 128), oracle.encode(v, 128)
+        qs.append(q); kxs.append(kx); vxs.append(vx)
+        singles.append(_gpu(kvx, q, kx=kx, vx=vx, seq=seq))
+    outs = [np.zeros((n_q, dim), dtype=np.float32) for _ in range(4)]
+    bad = list(kxs)
+    bad[2] = kxs[2][:-3]
+    with pytest.raises(RuntimeError, match="truncated"):
+        kvx.attention_decode_units(0, qs, bad, [x.size for x in bad], vxs, [x.size for x in vxs],
+                                   outs, n_q, dim, seq)
+    kvx.attention_decode_units(0, qs, kxs, [x.size for x in kxs], vxs, [x.size for x in vxs], outs,
+                               n_q, dim, seq)
+    for a, b in zip(outs, singles):
+        scale = np.maximum(np.abs(b), 1e-3)
+        assert np.max(np.abs(a - b) / scale) < 1e-4
+
+
 def test_errors_mirror_reference(kvx, cuda, oracle):
     q, k, v = _case(64, 7, 300)
     kx = oracle.encode(k, 128)
