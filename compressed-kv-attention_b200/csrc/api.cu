@@ -279,6 +279,7 @@ struct kvx_plan_s {
     // pool (stream-ordered on the legacy stream) and are destroyed only after that stream has
     // drained; plans made by kvx_plan_create use cudaMalloc / cudaFree.
     bool pooled = false;
+    unsigned long long esc_total = 0;  // escape record entries (u32)
     std::vector<void *> owned;
     ~kvx_plan_s() {
         for (void *p : owned) {
@@ -346,8 +347,23 @@ int kvx_device_info(int *sm_major, int *sm_minor, int *sms, size_t *hbm_bytes) {
 // done at once, and the escape records and block descriptors, which read the blobs, are enqueued
 // on the legacy stream behind the event, without waiting on the host; their errors then surface
 // at kvx_plan_check after the run.
+// The plan work that reads the blobs: escape records, then block descriptors (legacy stream,
+// behind `blobs_ready` when given).
+static cudaError_t plan_blob_work(kvx_plan_s *p, cudaEvent_t blobs_ready) {
+    cudaError_t e = cudaSuccess;
+    if (blobs_ready != nullptr) e = cudaStreamWaitEvent(nullptr, blobs_ready, 0);
+    if (e == cudaSuccess && p->esc_total > 0)
+        e = launch_esc_fill(p->units, p->flat, p->n_blocks, p->dim, p->esc, p->esc_total, p->status, nullptr);
+    if (e == cudaSuccess)
+        e = launch_block_desc(p->units, p->flat, p->esc, p->n_blocks, p->dim, p->bf16, p->desc, nullptr);
+    return e;
+}
+
+// `defer_blob_work`: return once the blob-independent part is done; the caller enqueues
+// plan_blob_work later (so that preparing several plans never waits on a copy).
 static int plan_create_impl(const kvx_unit *units, int n_units, int n_q, int dim, int block_tokens,
-                            kvx_plan *out, bool pooled, cudaEvent_t blobs_ready) {
+                            kvx_plan *out, bool pooled, cudaEvent_t blobs_ready,
+                            bool defer_blob_work = false) {
     if (out == nullptr || units == nullptr || n_units <= 0 || n_q <= 0 || block_tokens <= 0 ||
         block_tokens > 255)
         return fail(KVX_ERR_INVALID_ARGUMENT, "kvx_plan_create: bad argument");
@@ -484,11 +500,14 @@ static int plan_create_impl(const kvx_unit *units, int n_units, int n_q, int dim
         delete p;
         return rc;
     }
+    p->esc_total = esc_total;
+    if (defer_blob_work) {
+        *out = p;
+        g_err.clear();
+        return KVX_OK;
+    }
     // escape records and block descriptors read the blobs
-    if (blobs_ready != nullptr) e = cudaStreamWaitEvent(nullptr, blobs_ready, 0);
-    if (e == cudaSuccess && esc_total > 0)
-        e = launch_esc_fill(p->units, p->flat, total, dim, p->esc, esc_total, p->status, nullptr);
-    if (e == cudaSuccess) e = launch_block_desc(p->units, p->flat, p->esc, total, dim, bf16, p->desc, nullptr);
+    e = plan_blob_work(p, blobs_ready);
     if (e == cudaSuccess && blobs_ready == nullptr) e = cudaDeviceSynchronize();
     if (e != cudaSuccess) {
         delete p;
@@ -732,7 +751,9 @@ extern "C" int kvx_attention_decode_units(int backend, int n_units, const uint16
     if (int rc = check_device()) return rc;
     cudaStream_t s = nullptr;
     // One device arena for every host blob and query, copied with one transfer per buffer on the
-    // copy stream; the host walks the headers and builds the plan while the copies run.
+    // copy stream; the host walks the headers and builds the plans while the copies run.  With 8
+    // or more units the call runs as two chunks of units, each with its own plan behind its own
+    // copies, so the first chunk's records and kernels overlap the second chunk's copies.
     cudaStream_t sc = nullptr;
     if (int rc = copy_stream(&sc)) return rc;
     std::vector<size_t> koff(static_cast<size_t>(n_units)), voff(static_cast<size_t>(n_units)), qoff(static_cast<size_t>(n_units));
@@ -755,18 +776,22 @@ extern "C" int kvx_attention_decode_units(int backend, int n_units, const uint16
     DrainGuard drain{s, sc};
     uint8_t *A = ar.as<uint8_t>();
     std::vector<HostIndex> kidx(static_cast<size_t>(n_units)), vidx(static_cast<size_t>(n_units));
-    for (int u = 0; u < n_units; ++u) {
-        if (koff[size_t(u)] != SIZE_MAX)
-            KVX_CUDA(cudaMemcpyAsync(A + koff[size_t(u)], k_xkv[u], k_bytes[u], cudaMemcpyHostToDevice, sc));
-        if (voff[size_t(u)] != SIZE_MAX)
-            KVX_CUDA(cudaMemcpyAsync(A + voff[size_t(u)], v_xkv[u], v_bytes[u], cudaMemcpyHostToDevice, sc));
-        if (qoff[size_t(u)] != SIZE_MAX)
-            KVX_CUDA(cudaMemcpyAsync(A + qoff[size_t(u)], q[u], size_t(n_q) * dim * 2,
-                                     cudaMemcpyHostToDevice, sc));
+    const int nchunk = n_units >= 8 ? 2 : 1;
+    auto chunk_begin = [&](int c) { return int(int64_t(c) * n_units / nchunk); };
+    EventGuard copied[2];
+    for (int c = 0; c < nchunk; ++c) {
+        for (int u = chunk_begin(c); u < chunk_begin(c + 1); ++u) {
+            if (koff[size_t(u)] != SIZE_MAX)
+                KVX_CUDA(cudaMemcpyAsync(A + koff[size_t(u)], k_xkv[u], k_bytes[u], cudaMemcpyHostToDevice, sc));
+            if (voff[size_t(u)] != SIZE_MAX)
+                KVX_CUDA(cudaMemcpyAsync(A + voff[size_t(u)], v_xkv[u], v_bytes[u], cudaMemcpyHostToDevice, sc));
+            if (qoff[size_t(u)] != SIZE_MAX)
+                KVX_CUDA(cudaMemcpyAsync(A + qoff[size_t(u)], q[u], size_t(n_q) * dim * 2,
+                                         cudaMemcpyHostToDevice, sc));
+        }
+        KVX_CUDA(cudaEventCreateWithFlags(&copied[c].e, cudaEventDisableTiming));
+        KVX_CUDA(cudaEventRecord(copied[c].e, sc));
     }
-    EventGuard copied;
-    KVX_CUDA(cudaEventCreateWithFlags(&copied.e, cudaEventDisableTiming));
-    KVX_CUDA(cudaEventRecord(copied.e, sc));
     // header walks of the host blobs overlap the transfers
     std::vector<DevBlob> dk(static_cast<size_t>(n_units)), dv(static_cast<size_t>(n_units));
     std::vector<kvx_unit> units(static_cast<size_t>(n_units));
@@ -825,21 +850,30 @@ extern "C" int kvx_attention_decode_units(int backend, int n_units, const uint16
         x.n_blocks = int(kidx[size_t(u)].blocks.size());
         x.seq = seq;
     }
-    // Plan (its blob readers wait for the copies), run and the output copies, all on the legacy
-    // stream; one synchronisation at the end, then the plan's status.
-    kvx_plan plan = nullptr;
-    if (int rc = plan_create_impl(units.data(), n_units, n_q, dim, 128, &plan, true, copied.e))
-        return rc;
-    PlanGuard pg{plan};
-    int rc = kvx_plan_run(plan, s);
-    for (int u = 0; rc == KVX_OK && u < n_units; ++u)
-        KVX_CUDA(cudaMemcpyAsync(out[u], A + out_at + size_t(u) * out_bytes, out_bytes,
-                                 is_device_ptr(out[u]) ? cudaMemcpyDeviceToDevice
-                                                       : cudaMemcpyDeviceToHost,
-                                 s));
+    // Plans first (their host-side steps wait only for blob-independent work), then per chunk:
+    // the blob readers behind its copies, the run and its output copies, all on the legacy
+    // stream; one synchronisation at the end, then the plans' status.
+    PlanGuard pg[2] = {{nullptr}, {nullptr}};
+    for (int c = 0; c < nchunk; ++c) {
+        const int u0 = chunk_begin(c);
+        if (int rc = plan_create_impl(units.data() + u0, chunk_begin(c + 1) - u0, n_q, dim, 128, &pg[c].p,
+                                      true, nullptr, true))
+            return rc;
+    }
+    int rc = KVX_OK;
+    for (int c = 0; c < nchunk && rc == KVX_OK; ++c) {
+        const cudaError_t e = plan_blob_work(pg[c].p, copied[c].e);
+        if (e != cudaSuccess) return fail(KVX_ERR_CUDA, std::string("attention_decode: ") + cudaGetErrorString(e));
+        rc = kvx_plan_run(pg[c].p, s);
+        for (int u = chunk_begin(c); rc == KVX_OK && u < chunk_begin(c + 1); ++u)
+            KVX_CUDA(cudaMemcpyAsync(out[u], A + out_at + size_t(u) * out_bytes, out_bytes,
+                                     is_device_ptr(out[u]) ? cudaMemcpyDeviceToDevice
+                                                           : cudaMemcpyDeviceToHost,
+                                     s));
+    }
     KVX_CUDA(cudaStreamSynchronize(s));
     KVX_CUDA(cudaStreamSynchronize(sc));
-    if (rc == KVX_OK) rc = kvx_plan_check(plan);
+    for (int c = 0; c < nchunk && rc == KVX_OK; ++c) rc = kvx_plan_check(pg[c].p);
     if (rc != KVX_OK) return rc;
     g_err.clear();
     return KVX_OK;
