@@ -981,6 +981,38 @@ extern "C" int kvx_encode_bf16(const uint16_t *kv, int seq_len, int head_dim, in
     return KVX_OK;
 }
 
+extern "C" int kvx_exponent_stats(const uint16_t *kv, int seq_len, int head_dim, int block_tokens,
+                                  int *best, float *entropy) {
+    if (kv == nullptr || best == nullptr || entropy == nullptr || seq_len <= 0 || head_dim <= 0 ||
+        block_tokens <= 0)
+        return fail(KVX_ERR_INVALID_ARGUMENT, "exponent_stats: bad argument");
+    if (int rc = check_device()) return rc;
+    cudaStream_t s = nullptr;
+    const size_t nb = size_t((seq_len + block_tokens - 1) / block_tokens);
+    const size_t best_bytes = 3 * nb * size_t(head_dim) * sizeof(int);
+    const size_t ent_bytes = nb * size_t(head_dim) * sizeof(float);
+    DevBuf kb, bb, eb;
+    const void *kp = nullptr;
+    if (int rc = to_device(kv, size_t(seq_len) * head_dim * 2, kb, kp, s)) return rc;
+    const bool best_dev = is_device_ptr(best), ent_dev = is_device_ptr(entropy);
+    int *bp = best;
+    float *ep = entropy;
+    if (!best_dev) {
+        KVX_CUDA(bb.alloc(best_bytes, s));
+        bp = bb.as<int>();
+    }
+    if (!ent_dev) {
+        KVX_CUDA(eb.alloc(ent_bytes, s));
+        ep = eb.as<float>();
+    }
+    KVX_CUDA(launch_exp_stats(static_cast<const uint16_t *>(kp), seq_len, head_dim, block_tokens, bp, ep, s));
+    if (!best_dev) KVX_CUDA(cudaMemcpyAsync(best, bp, best_bytes, cudaMemcpyDeviceToHost, s));
+    if (!ent_dev) KVX_CUDA(cudaMemcpyAsync(entropy, ep, ent_bytes, cudaMemcpyDeviceToHost, s));
+    KVX_CUDA(cudaStreamSynchronize(s));
+    g_err.clear();
+    return KVX_OK;
+}
+
 extern "C" int kvx_decode_bf16(const uint8_t *blob, size_t bytes, int seq_len, int head_dim,
                                uint16_t *out) {
     if (blob == nullptr || out == nullptr || seq_len <= 0 || head_dim <= 0)

@@ -632,7 +632,67 @@ __global__ void esc_fill_kernel(const UnitDev *units, const FlatBlock *flat, int
     }
 }
 
+// ---- exponent statistics (the reference's size / entropy analyser) ---------------------------
+//
+// One CTA per (block of `bt` tokens, 32 head dims): a 256-bin histogram of the BF16 exponents of
+// each dim, then per dim the Shannon entropy of the histogram (bits) and, for code widths of
+// 3, 7 and 15 exponents (2-, 3- and 4-bit residuals minus the sentinel), the largest count in
+// any window of that many consecutive exponents -- what python/analyze_exponents.py computes
+// per block (`policy_size`, :117-156; `block_conditional_entropy`, :57-72).
+constexpr int kStatDims = 32;
+
+__global__ void __launch_bounds__(256) exp_stats_kernel(const uint16_t *kv, int seq, int dim, int bt,
+                                                        int *best, float *entropy) {
+    __shared__ uint32_t hist[kStatDims][256];
+    const int blk = blockIdx.x, d0 = blockIdx.y * kStatDims;
+    const int t0 = blk * bt, n = min(bt, seq - t0);
+    const int nd = min(kStatDims, dim - d0);
+    for (int i = threadIdx.x; i < kStatDims * 256; i += blockDim.x) (&hist[0][0])[i] = 0u;
+    __syncthreads();
+    for (int i = threadIdx.x; i < n * nd; i += blockDim.x) {
+        const int t = i / nd, d = i % nd;
+        const uint32_t x = kv[size_t(t0 + t) * dim + d0 + d];
+        atomicAdd(&hist[d][(x >> 7) & 0xFFu], 1u);
+    }
+    __syncthreads();
+    const int d = threadIdx.x;
+    if (d >= nd) return;
+    const uint32_t *h = hist[d];
+    float ent = 0.f;
+    uint32_t w3 = 0, w7 = 0, w15 = 0, b3 = 0, b7 = 0, b15 = 0;
+    for (int e = 0; e < 256; ++e) {
+        const uint32_t c = h[e];
+        if (c) {
+            const float p = float(c) / float(n);
+            ent -= p * log2f(p);
+        }
+        w3 += c;
+        w7 += c;
+        w15 += c;
+        if (e >= 3) w3 -= h[e - 3];
+        if (e >= 7) w7 -= h[e - 7];
+        if (e >= 15) w15 -= h[e - 15];
+        if (e >= 2) b3 = max(b3, w3);
+        if (e >= 6) b7 = max(b7, w7);
+        if (e >= 14) b15 = max(b15, w15);
+    }
+    const size_t nb = gridDim.x;
+    const size_t at = size_t(blk) * dim + d0 + d;
+    best[at] = int(b3);
+    best[nb * dim + at] = int(b7);
+    best[2 * nb * dim + at] = int(b15);
+    entropy[at] = ent;
+}
+
 }  // namespace
+
+cudaError_t launch_exp_stats(const uint16_t *kv, int seq, int dim, int bt, int *best, float *entropy,
+                             cudaStream_t s) {
+    const int nb = (seq + bt - 1) / bt;
+    exp_stats_kernel<<<dim3(nb, (dim + kStatDims - 1) / kStatDims), 256, 0, s>>>(kv, seq, dim, bt, best,
+                                                                              entropy);
+    return cudaGetLastError();
+}
 
 cudaError_t launch_index_walk(const uint8_t *blob, uint64_t bytes, int dim, kvx_block *index,
                               uint32_t *tok_start, int cap, int *counts, long long *n_tokens,

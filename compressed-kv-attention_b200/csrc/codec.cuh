@@ -14,6 +14,10 @@ struct EncBlock {
 };
 
 // Index walk of one device blob (single thread; validates like parse_block).
+// Exponent statistics per (block, dim): best[w][block][dim] for code widths 3, 7, 15 and
+// entropy[block][dim] (see exp_stats_kernel).
+cudaError_t launch_exp_stats(const uint16_t *kv, int seq, int dim, int bt, int *best, float *entropy,
+                             cudaStream_t s);
 cudaError_t launch_index_walk(const uint8_t *blob, uint64_t bytes, int dim, kvx_block *index,
                               uint32_t *tok_start, int cap, int *counts /*[2] blocks, tokens lo*/,
                               long long *n_tokens, int *status, cudaStream_t s);

@@ -119,6 +119,7 @@ _probe = _sig("kvx_hbm_read_probe", C.c_int, [_vp, _sz, C.c_int, C.POINTER(C.c_d
 _noalloc = _sig("kvx_attention_decode_noalloc", C.c_int,
                 [_vp, _vp, _sz, _vp, _vp, _sz, _vp, C.c_int, _vp, C.c_int, C.c_int, C.c_int, _vp])
 _fold = _sig("kvx_fold_shards", C.c_int, [_vp, C.c_int, C.c_int, C.c_int, _vp, _vp, _vp])
+_expstats = _sig("kvx_exponent_stats", C.c_int, [_vp, C.c_int, C.c_int, C.c_int, _vp, _vp])
 
 # Every symbol the C header declares, for load/export checks.
 EXPORTED = [
@@ -127,6 +128,7 @@ EXPORTED = [
     "kvx_xkv_index", "kvx_plan_create", "kvx_plan_run", "kvx_plan_run_part", "kvx_plan_check", "kvx_plan_launches", "kvx_plan_split_units",
     "kvx_plan_destroy", "kvx_encode_batch_bounds", "kvx_encode_batch", "kvx_cache_append",
     "kvx_synth_bf16", "kvx_hbm_read_probe", "kvx_attention_decode_noalloc", "kvx_fold_shards",
+    "kvx_exponent_stats",
 ]
 
 
@@ -341,3 +343,50 @@ def hbm_read_probe(buf, nbytes=None, reps=10) -> float:
     _check(_probe(_addr(buf), int(nbytes if nbytes is not None else _nbytes(buf)), int(reps),
                   C.byref(g)))
     return g.value
+
+
+def exponent_stats(kv, seq_len, head_dim, block_tokens=K_ENCODE_BLOCK):
+    """kvx_exponent_stats on a [seq_len, head_dim] BF16 tensor (host numpy or a device tensor):
+    returns (best [3, n_blocks, head_dim] int32 for windows of 3 / 7 / 15 exponents,
+    entropy [n_blocks, head_dim] float32)."""
+    nb = (int(seq_len) + int(block_tokens) - 1) // int(block_tokens)
+    best = np.zeros((3, nb, int(head_dim)), dtype=np.int32)
+    ent = np.zeros((nb, int(head_dim)), dtype=np.float32)
+    _check(_expstats(_addr(kv), int(seq_len), int(head_dim), int(block_tokens), best.ctypes.data,
+                     ent.ctypes.data))
+    return best, ent
+
+
+def exponent_report(kv, seq_len, head_dim, block_tokens=K_ENCODE_BLOCK, bit_widths=(2, 3, 4)):
+    """The reference analyser's per-tensor report from the GPU statistics: the size policy
+    (python/analyze_exponents.py:117-156 `policy_size`: per block the smallest of the raw
+    container and each residual width, ties to raw, then fewer escapes, then narrower codes) and
+    the mean entropy of the exponent in each (full block, dim) (`block_conditional_entropy`,
+    :57-72; nan when there is no full block)."""
+    seq, dim, bt = int(seq_len), int(head_dim), int(block_tokens)
+    best, ent = exponent_stats(kv, seq, dim, bt)
+    col = {2: 0, 3: 1, 4: 2}
+    total = 0
+    esc_total = 0
+    coded = 0
+    modes = {}
+    for b in range(best.shape[1]):
+        n = min(bt, seq - b * bt)
+        options = [(0, 8 + 2 * n * dim, 0)]
+        for bits in bit_widths:
+            n_esc = n * dim - int(best[col[bits], b].sum())
+            options.append((bits, 8 + dim + n * dim + (n * dim * bits + 7) // 8 + 2 * n_esc, n_esc))
+        mode, size, n_esc = min(options, key=lambda t: (t[1], 0 if t[0] == 0 else 1, t[2], t[0]))
+        total += size
+        esc_total += n_esc
+        modes[mode] = modes.get(mode, 0) + 1
+        if mode != 0:
+            coded += n * dim
+    full = seq // bt
+    tight = 2 * seq * dim
+    return {
+        "container_bytes": total, "tight_bytes": tight, "ratio": total / tight,
+        "escape_rate": esc_total / (seq * dim), "coded_element_fraction": coded / (seq * dim),
+        "mode_blocks": {str(k): v for k, v in sorted(modes.items())},
+        "block_conditional_entropy": float(ent[:full].astype(np.float64).mean()) if full else float("nan"),
+    }

@@ -89,6 +89,17 @@ KVX_API size_t kvx_encode_bound(int seq_len, int head_dim, int block_tokens);
 KVX_API int kvx_encode_bf16(const uint16_t *kv, int seq_len, int head_dim, int block_tokens,
                     uint8_t *out, size_t out_capacity, size_t *out_bytes);
 
+/* The statistics behind the reference's exponent analyser (python/analyze_exponents.py:57-72
+ * `block_conditional_entropy`, :117-156 `policy_size`), on the GPU.  For every block of
+ * block_tokens tokens of a [seq_len, head_dim] BF16 tensor (the last block may be shorter) and
+ * every head dim: best[w][block][dim] = the largest number of the block's exponents that fall in
+ * any window of 3, 7 or 15 consecutive exponents (w = 0, 1, 2: 2-, 3- and 4-bit residual codes),
+ * entropy[block][dim] = Shannon entropy (bits) of the block's exponents.  kv, best and entropy
+ * may be host or device memory; best holds 3 * n_blocks * head_dim ints, entropy
+ * n_blocks * head_dim floats. */
+KVX_API int kvx_exponent_stats(const uint16_t *kv, int seq_len, int head_dim, int block_tokens,
+                               int *best, float *entropy);
+
 /* Replaces kvexp::decode_bf16 (include/kvexp/codec.hpp:48, src/codec.cpp:166-174). */
 KVX_API int kvx_decode_bf16(const uint8_t *blob, size_t bytes, int seq_len, int head_dim,
                     uint16_t *out);
@@ -190,7 +201,7 @@ KVX_API int kvx_fold_shards(const float *parts, int n_parts, int n_rows, int dim
  * kvx_attention_decode for one KV head (within FP32 rounding), with every buffer in device
  * memory: q [n_q, dim] BF16, the K/V XKV blobs (16-byte aligned) with their block indexes
  * (n_blocks entries each, from kvx_xkv_index or the GPU encoder), out [n_q, dim] FP32.  Its
- * scratch is one fixed 24 MiB array in the library's device image, held by every device that
+ * scratch is one fixed 30 MiB array in the library's device image, held by every device that
  * loads the library until the process exits; limits: n_blocks <= 8192, n_q <= 64, and the
  * blobs' escape words plus 16 per coded block that has any at most 3 Mi (about 1 in 6 elements
  * of 8192 blocks of 128 x 128) -- larger calls fail with KVX_ERR_INVALID_ARGUMENT (the escape
