@@ -50,6 +50,9 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=8)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--units", type=int, default=0,
+                    help="only the first N units of this GPU's share (small cases for profilers; "
+                         "not a bench line of the config)")
     return ap.parse_args()
 
 
@@ -307,6 +310,9 @@ def run_kvx(args, rank, world, local):
     import workloads as W
     full = W.CONFIGS[args.config]
     cfg, unit_ids, seed, parallelism = rank_share(full, rank, world)
+    if args.units > 0:
+        unit_ids = list(unit_ids if unit_ids is not None else range(cfg.units))[: args.units]
+        parallelism += f"; only the first {len(unit_ids)} units (--units, a profiling case)"
     n_units = cfg.units if unit_ids is None else len(unit_ids)
     cache = W.build_cache(cfg, unit_ids=unit_ids, seed=seed)
     caches = [cache]
