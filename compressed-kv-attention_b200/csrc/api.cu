@@ -123,6 +123,19 @@ int check_device() {
     return KVX_OK;
 }
 
+// A pinned host buffer per device for the outputs of the host-buffer entry points: one
+// device -> host copy per chunk of units instead of one per unit; held (locked) by one call at a
+// time, grown when a call needs more.
+struct PinnedStage {
+    std::mutex mu;
+    void *p = nullptr;
+    size_t bytes = 0;
+};
+PinnedStage &pinned_stage(int dev) {
+    static PinnedStage stages[kMaxDevices];
+    return stages[dev];
+}
+
 // A non-blocking stream per device for host -> device copies of the host-buffer entry points, so
 // that work on the legacy stream (plan creation) does not wait for them.
 int copy_stream(cudaStream_t *out) {
@@ -860,12 +873,36 @@ extern "C" int kvx_attention_decode_units(int backend, int n_units, const uint16
                                       true, nullptr, true))
             return rc;
     }
+    // Outputs in host memory come back through the device's pinned staging buffer, one copy per
+    // chunk (the outputs sit together in the arena); outputs in device memory are copied one by one.
+    bool all_host = true;
+    for (int u = 0; u < n_units && all_host; ++u) all_host = !is_device_ptr(out[u]);
+    int dev = 0;
+    KVX_CUDA(cudaGetDevice(&dev));
+    PinnedStage *ps = all_host && dev >= 0 && dev < kMaxDevices ? &pinned_stage(dev) : nullptr;
+    std::unique_lock<std::mutex> stage_lock;
+    const size_t out_total = size_t(n_units) * out_bytes;
+    if (ps != nullptr) {
+        stage_lock = std::unique_lock<std::mutex>(ps->mu);
+        if (ps->bytes < out_total) {
+            if (ps->p != nullptr) cudaFreeHost(ps->p);
+            ps->p = nullptr;
+            ps->bytes = 0;
+            KVX_CUDA(cudaHostAlloc(&ps->p, out_total, cudaHostAllocDefault));
+            ps->bytes = out_total;
+        }
+    }
     int rc = KVX_OK;
     for (int c = 0; c < nchunk && rc == KVX_OK; ++c) {
         const cudaError_t e = plan_blob_work(pg[c].p, copied[c].e);
         if (e != cudaSuccess) return fail(KVX_ERR_CUDA, std::string("attention_decode: ") + cudaGetErrorString(e));
         rc = kvx_plan_run(pg[c].p, s);
-        for (int u = chunk_begin(c); rc == KVX_OK && u < chunk_begin(c + 1); ++u)
+        const int u0 = chunk_begin(c), u1 = chunk_begin(c + 1);
+        if (rc == KVX_OK && ps != nullptr)
+            KVX_CUDA(cudaMemcpyAsync(static_cast<uint8_t *>(ps->p) + size_t(u0) * out_bytes,
+                                     A + out_at + size_t(u0) * out_bytes, size_t(u1 - u0) * out_bytes,
+                                     cudaMemcpyDeviceToHost, s));
+        for (int u = u0; rc == KVX_OK && ps == nullptr && u < u1; ++u)
             KVX_CUDA(cudaMemcpyAsync(out[u], A + out_at + size_t(u) * out_bytes, out_bytes,
                                      is_device_ptr(out[u]) ? cudaMemcpyDeviceToDevice
                                                            : cudaMemcpyDeviceToHost,
@@ -875,6 +912,9 @@ extern "C" int kvx_attention_decode_units(int backend, int n_units, const uint16
     KVX_CUDA(cudaStreamSynchronize(sc));
     for (int c = 0; c < nchunk && rc == KVX_OK; ++c) rc = kvx_plan_check(pg[c].p);
     if (rc != KVX_OK) return rc;
+    if (ps != nullptr)
+        for (int u = 0; u < n_units; ++u)
+            std::memcpy(out[u], static_cast<const uint8_t *>(ps->p) + size_t(u) * out_bytes, out_bytes);
     g_err.clear();
     return KVX_OK;
 }

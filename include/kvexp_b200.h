@@ -76,7 +76,9 @@ KVX_API int kvx_attention_decode(int backend, const uint16_t *q, const uint16_t 
  * With host buffers the blobs go to the GPU on a library-owned non-blocking stream while the host
  * walks their headers and builds the step's plan; the call returns when the outputs are back.
  * Its device buffers come from the device's default CUDA memory pool, whose release threshold
- * the library raises to 1 GiB (the pool then keeps up to 1 GiB between calls). */
+ * the library raises to 1 GiB (the pool then keeps up to 1 GiB between calls).  Outputs in host
+ * memory come back through a pinned host buffer the library keeps per device (the size of the
+ * largest call's outputs). */
 KVX_API int kvx_attention_decode_units(int backend, int n_units, const uint16_t *const *q,
                                const uint8_t *const *k_xkv, const size_t *k_bytes,
                                const uint8_t *const *v_xkv, const size_t *v_bytes,
