@@ -286,7 +286,7 @@ struct kvx_plan_s {
     uint32_t *esc = nullptr;  // escape records of the step's coded blocks
     int64_t *range_begin = nullptr;
     float *partials = nullptr;
-    int4 *split_units = nullptr;  // {unit, first worker, workers} of each split unit
+    SplitUnit *split_units = nullptr;  // the units whose blocks span several workers
     int *status = nullptr;
     // Internal plans of the host-buffer entry points take their arrays from the device's memory
     // pool (stream-ordered on the legacy stream) and are destroyed only after that stream has
@@ -313,6 +313,18 @@ template <class T> cudaError_t plan_alloc(kvx_plan_s *p, T **dst, size_t n) {
         *dst = static_cast<T *>(q);
     }
     return e;
+}
+
+SplitUnit make_split(const UnitDev &d, int t0, int t1, int first_slot) {
+    SplitUnit x{};
+    x.out = d.out;
+    x.lse = d.lse;
+    x.first_worker = t0;
+    x.n_workers = t1 - t0 + 1;
+    x.first_slot = first_slot;
+    x.n_q = d.n_q;
+    x.q_stride = d.q_stride;
+    return x;
 }
 
 struct PlanGuard {
@@ -489,18 +501,18 @@ static int plan_create_impl(const kvx_unit *units, int n_units, int n_q, int dim
             e = cudaMemcpy(tb.data(), p->range_begin, tb.size() * sizeof(int64_t),
                            cudaMemcpyDeviceToHost);
     }
-    std::vector<int4> split;
+    std::vector<SplitUnit> split;
     if (e == cudaSuccess) {
         for (int u = 0; u < p->n_units; ++u) {
             const int t0 = worker_of_block(tb.data(), p->n_workers, ud[size_t(u)].block_begin);
             const int t1 = worker_of_block(tb.data(), p->n_workers,
                                            ud[size_t(u)].block_begin + ud[size_t(u)].n_blocks - 1);
             if (t0 != t1)
-                split.push_back(make_int4(u, t0, t1 - t0 + 1,
-                                          tb[size_t(t0)] < ud[size_t(u)].block_begin ? 1 : 0));
+                split.push_back(make_split(ud[size_t(u)], t0, t1,
+                                           tb[size_t(t0)] < ud[size_t(u)].block_begin ? 1 : 0));
         }
         if (!split.empty())
-            e = cudaMemcpy(p->split_units, split.data(), split.size() * sizeof(int4),
+            e = cudaMemcpy(p->split_units, split.data(), split.size() * sizeof(SplitUnit),
                            cudaMemcpyHostToDevice);
     }
     if (e != cudaSuccess) {
@@ -1317,7 +1329,7 @@ extern "C" int kvx_attention_decode_noalloc(const uint16_t *q, const uint8_t *k_
     kvx_unit *d_vu = reinterpret_cast<kvx_unit *>(take(kNoAllocMaxQueries / 8 * sizeof(kvx_unit)));
     int64_t *d_begin = reinterpret_cast<int64_t *>(take(kNoAllocMaxQueries / 8 * sizeof(int64_t)));
     int64_t *d_src = reinterpret_cast<int64_t *>(take(kNoAllocMaxQueries / 8 * sizeof(int64_t)));
-    int4 *d_split = reinterpret_cast<int4 *>(take(kNoAllocMaxQueries / 8 * sizeof(int4)));
+    SplitUnit *d_split = reinterpret_cast<SplitUnit *>(take(kNoAllocMaxQueries / 8 * sizeof(SplitUnit)));
     FlatBlock *d_flat = reinterpret_cast<FlatBlock *>(
         take(size_t(kNoAllocMaxQueries / 8) * kNoAllocMaxBlocks * sizeof(FlatBlock)));
     BlockDesc *d_desc = reinterpret_cast<BlockDesc *>(
@@ -1366,13 +1378,13 @@ extern "C" int kvx_attention_decode_noalloc(const uint16_t *q, const uint8_t *k_
     // Worker ranges: one block each when they fit, else an even split of the blocks.
     std::vector<int64_t> tb(static_cast<size_t>(n_workers) + 1);
     for (int t = 0; t <= n_workers; ++t) tb[size_t(t)] = int64_t(t) * total / n_workers;
-    std::vector<int4> split;
+    std::vector<SplitUnit> split;
     for (int g = 0; g < groups; ++g) {
         const int t0 = worker_of_block(tb.data(), n_workers, ud[size_t(g)].block_begin);
         const int t1 = worker_of_block(tb.data(), n_workers,
                                        ud[size_t(g)].block_begin + ud[size_t(g)].n_blocks - 1);
         if (t0 != t1)
-            split.push_back(make_int4(g, t0, t1 - t0 + 1, tb[size_t(t0)] < ud[size_t(g)].block_begin ? 1 : 0));
+            split.push_back(make_split(ud[size_t(g)], t0, t1, tb[size_t(t0)] < ud[size_t(g)].block_begin ? 1 : 0));
     }
 
     // Every call shares the scratch and finds the previous call's contents there: the status
@@ -1384,7 +1396,7 @@ extern "C" int kvx_attention_decode_noalloc(const uint16_t *q, const uint8_t *k_
     KVX_CUDA(cudaMemcpyAsync(d_src, srcs.data(), srcs.size() * sizeof(int64_t), cudaMemcpyHostToDevice, s));
     KVX_CUDA(cudaMemcpyAsync(d_range, tb.data(), tb.size() * sizeof(int64_t), cudaMemcpyHostToDevice, s));
     if (!split.empty())
-        KVX_CUDA(cudaMemcpyAsync(d_split, split.data(), split.size() * sizeof(int4),
+        KVX_CUDA(cudaMemcpyAsync(d_split, split.data(), split.size() * sizeof(SplitUnit),
                                  cudaMemcpyHostToDevice, s));
     KVX_CUDA(launch_build_flat(d_vu, d_begin, d_src, groups, dim, kDefaultBlock, false, d_flat,
                                status, s));

@@ -886,18 +886,17 @@ __global__ void __launch_bounds__(kCombineThreads) combine_kernel(const CombineA
     // launched as a dependent of the attention grid: its partial states are complete and visible
     // after this wait (a no-op for an ordinary launch)
     asm volatile("griddepcontrol.wait;" ::: "memory");
-    const int4 sp = a.split[blockIdx.x];
+    const SplitUnit sp = a.split[blockIdx.x];
     const int g = blockIdx.y;
-    const UnitDev unit = a.units[sp.x];
-    if (g >= unit.n_q) return;
-    const int t0 = sp.y;  // first worker of the unit and the number of workers (host-computed)
-    const int nt = min(sp.z, kMaxSegments);
+    if (g >= sp.n_q) return;
+    const int t0 = sp.first_worker;  // first worker of the unit and the number of workers
+    const int nt = min(sp.n_workers, kMaxSegments);
     const int ps = partial_stride(D);
     // only the unit's first worker can hold it in its second partial slot (its range began in an
-    // earlier unit); the host worked that out (sp.w)
+    // earlier unit); the host worked that out
     auto part = [&](int i) {
         const int t = t0 + i;
-        return a.partials + (size_t(t) * 2 + (i == 0 ? sp.w : 0)) * ps;
+        return a.partials + (size_t(t) * 2 + (i == 0 ? sp.first_slot : 0)) * ps;
     };
     const int tid = threadIdx.x;
     const int d = tid % D, sl = tid / D;
@@ -953,9 +952,9 @@ __global__ void __launch_bounds__(kCombineThreads) combine_kernel(const CombineA
     if (sl == 0) {
         float v = red[d];
         for (int j = 1; j < S; ++j) v = __fadd_rn(v, red[j * D + d]);
-        unit.out[size_t(g) * unit.q_stride + d] = __fmul_rn(v, inv);
+        sp.out[size_t(g) * sp.q_stride + d] = __fmul_rn(v, inv);
     }
-    if (tid == 0 && unit.lse != nullptr) unit.lse[g] = M + logf(lsum);
+    if (tid == 0 && sp.lse != nullptr) sp.lse[g] = M + logf(lsum);
 }
 
 // ---- fold of sequence shards --------------------------------------------------------------------

@@ -117,10 +117,20 @@ struct AttnArgs {
     int n_workers;
 };
 
+// A unit whose blocks span several workers, as the combine pass needs it (host-built, so the
+// kernel's first load is all it needs): where its outputs go, its queries, its first worker, how
+// many workers hold its segments, and the partial slot of the first (1 when that worker's range
+// began in an earlier unit).
+struct SplitUnit {
+    float *out;
+    float *lse;
+    int32_t first_worker, n_workers, first_slot, n_q, q_stride, pad;
+};
+static_assert(sizeof(SplitUnit) == 40, "SplitUnit is 40 bytes");
+
 struct CombineArgs {
     const UnitDev *units;
-    const int4 *split;            // units whose blocks span several workers: {unit, first
-                                  // worker, number of workers, partial slot of the first}
+    const SplitUnit *split;       // the units whose blocks span several workers
     const int64_t *range_begin;    // [n_workers + 1]
     const float *partials;
     int n_workers;
