@@ -852,6 +852,10 @@ template <int D, bool BF16IN>
 __global__ void __launch_bounds__(32 * Cfg<D>::WARPS, 1) attn_kernel(const AttnArgs a) {
     using C = Cfg<D>;
     extern __shared__ __align__(128) uint8_t smem[];
+    // Launched as a programmatic dependent of the kernel before it in the stream (the previous
+    // step's combine pass, or the plan's descriptor build): nothing is read before that grid has
+    // completed and its writes are visible.  Only the launch itself overlaps it.
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     // A combine pass launched behind this grid (programmatic dependent launch) may start placing
     // its CTAs as soon as SMs free up; it waits for this grid's completion before reading.
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
@@ -886,6 +890,8 @@ __global__ void __launch_bounds__(kCombineThreads) combine_kernel(const CombineA
     // launched as a dependent of the attention grid: its partial states are complete and visible
     // after this wait (a no-op for an ordinary launch)
     asm volatile("griddepcontrol.wait;" ::: "memory");
+    // the next step's attention grid may be set up while this one runs (it waits for it)
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const SplitUnit sp = a.split[blockIdx.x];
     const int g = blockIdx.y;
     if (g >= sp.n_q) return;
@@ -1088,13 +1094,20 @@ __global__ void block_desc_kernel(const UnitDev *units, const FlatBlock *flat, c
 template <int D>
 cudaError_t launch_d(bool bf16, const AttnArgs &a, int grid, cudaStream_t s) {
     configure<D>(bf16);
-    const int threads = 32 * Cfg<D>::WARPS;
-    const size_t sm = size_t(Cfg<D>::WARP_BYTES) * Cfg<D>::WARPS;
-    if (bf16)
-        attn_kernel<D, true><<<grid, threads, sm, s>>>(a);
-    else
-        attn_kernel<D, false><<<grid, threads, sm, s>>>(a);
-    return cudaGetLastError();
+    // programmatic dependent launch: the grid may be set up while the kernel before it in the
+    // stream drains (the kernel waits for that grid before it reads anything)
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(32 * Cfg<D>::WARPS);
+    cfg.dynamicSmemBytes = size_t(Cfg<D>::WARP_BYTES) * Cfg<D>::WARPS;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (bf16) return cudaLaunchKernelEx(&cfg, attn_kernel<D, true>, a);
+    return cudaLaunchKernelEx(&cfg, attn_kernel<D, false>, a);
 }
 
 }  // namespace
