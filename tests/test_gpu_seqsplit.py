@@ -211,3 +211,42 @@ def test_shard_exchange_over_nccl(cuda):
         got = torch.from_numpy(result[r][0]).double()
         assert torch.max(torch.abs(got - want)) <= 2e-6 * want.abs().amax()
     assert np.array_equal(result[0][0], result[1][0])
+
+
+def test_stream_order_with_dependent_launches(kvx, cuda, oracle):
+    """The attention and combine kernels are launched as programmatic dependents of the kernel
+    before them; each waits for it before reading.  A kernel that rewrites the queries between two
+    runs on the same stream, with no synchronisation, must be seen by the second run, and the
+    first run's outputs must be complete before the copy that follows it."""
+    import torch
+    dim, n_q, seq = 64, 7, 6000
+    q1, k, v = _case(dim, n_q, seq, 41, 6)
+    q2, _, _ = _case(dim, n_q, seq, 42, 6)
+    blobs = _Blobs(kvx, oracle, k, v, dim)
+    tq1 = torch.from_numpy(q1.view(np.int16)).cuda()
+    tq2 = torch.from_numpy(q2.view(np.int16)).cuda()
+    q = tq1.clone()
+    out = torch.zeros((n_q, dim), dtype=torch.float32, device="cuda")
+    plan = kvx.Plan([blobs.unit(kvx, q, out, None)], n_q, dim)
+    assert plan.n_split > 0  # the combine pass runs too
+    h = torch.cuda.current_stream().cuda_stream
+    refs = []
+    for tq in (tq1, tq2):  # each query set alone, synchronised
+        q.copy_(tq)
+        torch.cuda.synchronize()
+        plan.run(h)
+        torch.cuda.synchronize()
+        refs.append(out.clone())
+    q.copy_(tq1)
+    torch.cuda.synchronize()
+    plan.run(h)
+    o1 = out.clone()
+    torch.add(tq2, 0, out=q)  # a kernel, right before the next attention launch
+    plan.run(h)
+    o2 = out.clone()
+    plan.check()
+    torch.cuda.synchronize()
+    plan.close()
+    assert torch.equal(o1.view(torch.int32), refs[0].view(torch.int32))
+    assert torch.equal(o2.view(torch.int32), refs[1].view(torch.int32))
+    assert not torch.equal(refs[0], refs[1])
