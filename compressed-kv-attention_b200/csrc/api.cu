@@ -1246,6 +1246,23 @@ constexpr size_t kNoAllocEscEntries = size_t(3) << 20;      // escape record ent
 constexpr int kNoAllocMaxBlocks = 8192;                   // XKV blocks per tensor
 constexpr int kNoAllocMaxQueries = 64;                    // queries per call (8 groups of 8)
 constexpr int kNoAllocMaxWorkers = 4096;
+constexpr int kNoAllocMaxGroups = kNoAllocMaxQueries / 8;  // query groups of <= 8
+
+constexpr size_t up256c(size_t x) { return (x + 255) & ~size_t(255); }
+// Bytes of the fixed part of the scratch layout (everything before the partial states), in the
+// order kvx_attention_decode_noalloc carves it.
+constexpr size_t kNoAllocFixedBytes =
+    up256c(2 * sizeof(int)) + up256c(kNoAllocMaxGroups * sizeof(UnitDev)) +
+    up256c(kNoAllocMaxGroups * sizeof(kvx_unit)) + up256c(kNoAllocMaxGroups * sizeof(int64_t)) +
+    up256c(kNoAllocMaxGroups * sizeof(int64_t)) + up256c(kNoAllocMaxGroups * sizeof(SplitUnit)) +
+    up256c(size_t(kNoAllocMaxGroups) * kNoAllocMaxBlocks * sizeof(FlatBlock)) +
+    up256c(size_t(kNoAllocMaxGroups) * kNoAllocMaxBlocks * sizeof(BlockDesc)) +
+    up256c((kNoAllocMaxWorkers + 1) * sizeof(int64_t)) + up256c(sizeof(unsigned long long)) +
+    up256c(kNoAllocEscEntries * sizeof(uint32_t));
+// The partial states of one worker at the widest head dim (two slots of m, l and acc).
+constexpr size_t kNoAllocWorkerBytes256 = 2 * size_t(16 + 8 * kMaxHeadDim) * sizeof(float);
+static_assert(kNoAllocFixedBytes + 148 * kNoAllocWorkerBytes256 <= kNoAllocScratchBytes,
+              "the fixed scratch must leave room for one worker per SM at head_dim 256");
 }  // namespace
 }  // namespace kvx
 
@@ -1338,6 +1355,8 @@ extern "C" int kvx_attention_decode_noalloc(const uint16_t *q, const uint8_t *k_
     unsigned long long *d_esc_total =
         reinterpret_cast<unsigned long long *>(take(sizeof(unsigned long long)));
     uint32_t *d_esc = reinterpret_cast<uint32_t *>(take(kNoAllocEscEntries * sizeof(uint32_t)));
+    if (off != kNoAllocFixedBytes)
+        return fail(KVX_ERR_RUNTIME, std::string(fn) + "scratch layout out of step with its size");
     float *d_partials = reinterpret_cast<float *>(base + off);
     const size_t per_worker = 2 * size_t(partial_stride(dim)) * sizeof(float);
     const int64_t fit = int64_t((kNoAllocScratchBytes - off) / per_worker);

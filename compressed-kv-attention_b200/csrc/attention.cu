@@ -406,12 +406,14 @@ __device__ __forceinline__ void qk_tiles(uint32_t xb, const uint32_t (&qb)[Cfg<D
     }
 }
 
-// O^T += V^T P^T for the 16-token tile at tile row r0 (P^T as B fragments: bh = bf16 part, bm =
-// residual part).  V^T A fragments by ldmatrix.trans: matrix i covers tokens 0-7 / 8-15 (i / 2)
-// and head dims 0-7 / 8-15 (i % 2) of the m-tile.
+// O^T += V^T P^T for the 16-token tile at tile row r0 (P^T as B fragments: bh = bf16(p),
+// bm = bf16(p - bh), bl = bf16(p - bh - bm): three bf16 terms carry p's 24 significant bits, so the
+// tensor cores see the fp32 softmax weight exactly).  V^T A fragments by ldmatrix.trans: matrix i
+// covers tokens 0-7 / 8-15 (i / 2) and head dims 0-7 / 8-15 (i % 2) of the m-tile.  The three
+// MMAs accumulate the smallest term first.
 template <int D>
 __device__ __forceinline__ void pv_tile(uint32_t xb, int r0, const uint32_t (&bh)[2],
-                                        const uint32_t (&bm)[2], int lane,
+                                        const uint32_t (&bm)[2], const uint32_t (&bl)[2], int lane,
                                         float (&acc)[Cfg<D>::KS][4]) {
     constexpr int KS = Cfg<D>::KS, G = KS < 4 ? KS : 4;
     const int row = r0 + (lane & 7) + (lane >> 4) * 8;
@@ -426,12 +428,17 @@ __device__ __forceinline__ void pv_tile(uint32_t xb, int r0, const uint32_t (&bh
 #pragma unroll
         for (int g = 0; g < G; ++g) {
             float (&c)[4] = acc[m0 + g];
-            mma_bf16(c[0], c[1], c[2], c[3], a[g][0], a[g][1], a[g][2], a[g][3], bh[0], bh[1]);
+            mma_bf16(c[0], c[1], c[2], c[3], a[g][0], a[g][1], a[g][2], a[g][3], bl[0], bl[1]);
         }
 #pragma unroll
         for (int g = 0; g < G; ++g) {
             float (&c)[4] = acc[m0 + g];
             mma_bf16(c[0], c[1], c[2], c[3], a[g][0], a[g][1], a[g][2], a[g][3], bm[0], bm[1]);
+        }
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+            float (&c)[4] = acc[m0 + g];
+            mma_bf16(c[0], c[1], c[2], c[3], a[g][0], a[g][1], a[g][2], a[g][3], bh[0], bh[1]);
         }
     }
 }
@@ -738,21 +745,27 @@ __device__ __forceinline__ void worker(const AttnArgs &a, uint8_t *R, int wk, in
         }
         const float ml0 = __fmul_rn(mn0, kLog2e), ml1 = __fmul_rn(mn1, kLog2e);
         float ps0 = 0.f, ps1 = 0.f;
-        uint32_t bh[C::SUBS][2], bm[C::SUBS][2];
+        uint32_t bh[C::SUBS][2], bm[C::SUBS][2], bl[C::SUBS][2];
 #pragma unroll
         for (int sub = 0; sub < C::SUBS; ++sub) {
             const float p0 = ex2(__fmaf_rn(s[sub][0], kLog2e, -ml0)), p1 = ex2(__fmaf_rn(s[sub][1], kLog2e, -ml1));
             const float p2 = ex2(__fmaf_rn(s[sub][2], kLog2e, -ml0)), p3 = ex2(__fmaf_rn(s[sub][3], kLog2e, -ml1));
             ps0 = __fadd_rn(ps0, __fadd_rn(p0, p2));
             ps1 = __fadd_rn(ps1, __fadd_rn(p1, p3));
-            // P^T B fragments: bf16(p) and bf16(p - bf16(p))
+            // P^T B fragments: p = h + m + l exactly, h = bf16(p), m = bf16(p - h),
+            // l = bf16(p - h - m) (each difference is exact in fp32; 3 x 8 significant bits)
             const uint32_t h01 = pack_bf16x2(p1, p0), h23 = pack_bf16x2(p3, p2);
             const float r0 = __fsub_rn(p0, bf16lo_to_f32(h01)), r1 = __fsub_rn(p1, bf16hi_to_f32(h01));
             const float r2 = __fsub_rn(p2, bf16lo_to_f32(h23)), r3 = __fsub_rn(p3, bf16hi_to_f32(h23));
+            const uint32_t m01 = pack_bf16x2(r1, r0), m23 = pack_bf16x2(r3, r2);
+            const float u0 = __fsub_rn(r0, bf16lo_to_f32(m01)), u1 = __fsub_rn(r1, bf16hi_to_f32(m01));
+            const float u2 = __fsub_rn(r2, bf16lo_to_f32(m23)), u3 = __fsub_rn(r3, bf16hi_to_f32(m23));
             bh[sub][0] = movm_t(h01);
             bh[sub][1] = movm_t(h23);
-            bm[sub][0] = movm_t(pack_bf16x2(r1, r0));
-            bm[sub][1] = movm_t(pack_bf16x2(r3, r2));
+            bm[sub][0] = movm_t(m01);
+            bm[sub][1] = movm_t(m23);
+            bl[sub][0] = movm_t(pack_bf16x2(u1, u0));
+            bl[sub][1] = movm_t(pack_bf16x2(u3, u2));
         }
         l0 = __fmaf_rn(l0, al0, ps0);
         l1 = __fmaf_rn(l1, al1, ps1);
@@ -779,7 +792,7 @@ __device__ __forceinline__ void worker(const AttnArgs &a, uint8_t *R, int wk, in
         ++cq;
 #pragma unroll
         for (int sub = 0; sub < C::SUBS; ++sub)
-            if (sub * TT < rows) pv_tile<D>(xb, sub * TT, bh[sub], bm[sub], lane, acc);
+            if (sub * TT < rows) pv_tile<D>(xb, sub * TT, bh[sub], bm[sub], bl[sub], lane, acc);
 
         if (seg_end) {
             float lt0 = l0, lt1 = l1;

@@ -1,8 +1,8 @@
 """Seeded synthetic KV inputs for the benchmark configurations (numpy, host side).
 
-The same generator exists as a CUDA kernel (csrc/synth.cu, entry point kvx_synth_bf16); both
-use only integer arithmetic plus IEEE round-to-nearest float32 multiplies, so host and device
-produce bit-identical BF16 tensors.  This stands in for the reference's real Qwen2.5-0.5B dump
+The same generator exists as a CUDA kernel (synth_kernel in csrc/codec.cu, entry point
+kvx_synth_bf16); both use only integer arithmetic plus IEEE round-to-nearest float32 multiplies,
+so host and device produce bit-identical BF16 tensors.  This stands in for the reference's real Qwen2.5-0.5B dump
 (KVD1 files written by python/dump_kv.py), which is not available offline.
 
 Element value for tensor `stream`, token t, channel c (index i = t * dim + c):

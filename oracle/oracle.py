@@ -36,7 +36,15 @@ class OracleError(Exception):
         self.code = code
 
 
-def build(ref_root: str = "/root/reference") -> None:
+def default_ref_root() -> str:
+    """The reference checkout: $KVX_REFERENCE_ROOT, else a `reference` directory beside the
+    repository."""
+    return os.environ.get("KVX_REFERENCE_ROOT",
+                          os.path.join(os.path.dirname(os.path.dirname(HERE)), "reference"))
+
+
+def build(ref_root: str | None = None) -> None:
+    ref_root = ref_root or default_ref_root()
     subprocess.run(["make", "-s", "-C", HERE, "all"], check=True)
     if os.path.isdir(ref_root):
         subprocess.run(["make", "-s", "-C", HERE, "ref", f"REF_ROOT={ref_root}"], check=True)

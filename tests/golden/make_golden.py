@@ -49,6 +49,7 @@ def main():
         sys.exit("oracle/_ref/libkvexp_ref.so is missing: run `make -C oracle ref` first")
     out = {"generator": "tests/golden/make_golden.py", "reference": "kvexp built from its sources",
            "cases": {}}
+    exact = elems = 0
     for name, c in CASES.items():
         q, k, v = inputs(c)
         kx = ref.encode(k, c["block"])
@@ -68,8 +69,14 @@ def main():
             o = ref.attention(q, kx=kx, vx=vx, seq=c["seq"], backend=backend, threads=threads,
                               split=c["block"])
             e["out_" + tag] = b64(o.astype(np.float32))
+        o1 = np.frombuffer(base64.b64decode(e["out_scalar_t1"]), dtype=np.uint32)
+        exact += int(np.count_nonzero((o1 & 0xFFFF) == 0))
+        elems += o1.size
         out["cases"][name] = e
         print(name, e["k_bytes"], e["v_bytes"], e["k_modes"], e["v_modes"])
+    # share of output elements that are exact BF16 values (a one-hot softmax copies a V row)
+    out["exact_bf16_fraction"] = exact / elems
+    print(f"exact-BF16 output elements: {exact} of {elems} ({100 * exact / elems:.2f} %)")
     with open(os.path.join(HERE, "golden.json"), "w") as f:
         json.dump(out, f, indent=1, sort_keys=True)
 
