@@ -276,17 +276,17 @@ struct kvx_plan_s {
     bool bf16 = false;
     int n_units = 0;      // device units (query groups of <= 8)
     int64_t n_blocks = 0;
-    int n_workers = 0;
-    int grid = 0;
-    int n_split = 0;
+    int n_ranges = 0;     // CTA ranges of the attention grid (one CTA each)
+    int64_t n_rows = 0;   // partial-state rows (one per unit segment of a CTA range)
     cudaStream_t s = nullptr;
     UnitDev *units = nullptr;
     FlatBlock *flat = nullptr;
     BlockDesc *desc = nullptr;  // per flat block, for the attention kernel
     uint32_t *esc = nullptr;  // escape records of the step's coded blocks
     int64_t *range_begin = nullptr;
+    int32_t *seg_base = nullptr;
     float *partials = nullptr;
-    SplitUnit *split_units = nullptr;  // the units whose blocks span several workers
+    SplitUnit *split_units = nullptr;  // every unit, as the combine pass sees it
     int *status = nullptr;
     // Internal plans of the host-buffer entry points take their arrays from the device's memory
     // pool (stream-ordered on the legacy stream) and are destroyed only after that stream has
@@ -315,16 +315,33 @@ template <class T> cudaError_t plan_alloc(kvx_plan_s *p, T **dst, size_t n) {
     return e;
 }
 
-SplitUnit make_split(const UnitDev &d, int t0, int t1, int first_slot) {
-    SplitUnit x{};
-    x.out = d.out;
-    x.lse = d.lse;
-    x.first_worker = t0;
-    x.n_workers = t1 - t0 + 1;
-    x.first_slot = first_slot;
-    x.n_q = d.n_q;
-    x.q_stride = d.q_stride;
-    return x;
+// The partial-state rows of a step from its CTA ranges: seg_base per CTA and, per unit, the
+// combine pass's view (its run of states: one per consumer warp of each of its rows).
+int64_t plan_segments(const std::vector<int64_t> &tb, int n_ranges, const std::vector<UnitDev> &ud,
+                      int dim, std::vector<int32_t> &seg_base, std::vector<SplitUnit> &split) {
+    const size_t n = ud.size();
+    std::vector<int64_t> ub(n);
+    std::vector<int32_t> nb(n), first(n), rows(n);
+    for (size_t u = 0; u < n; ++u) {
+        ub[u] = ud[u].block_begin;
+        nb[u] = ud[u].n_blocks;
+    }
+    seg_base.assign(size_t(n_ranges), 0);
+    const int64_t total = segment_rows(tb.data(), n_ranges, ub.data(), nb.data(), int(n),
+                                       seg_base.data(), first.data(), rows.data());
+    const int nw = attention_consumer_warps(dim);
+    split.resize(n);
+    for (size_t u = 0; u < n; ++u) {
+        SplitUnit &x = split[u];
+        x = SplitUnit{};
+        x.out = ud[u].out;
+        x.lse = ud[u].lse;
+        x.first_state = first[u] * nw;
+        x.n_states = rows[u] * nw;
+        x.n_q = ud[u].n_q;
+        x.q_stride = ud[u].q_stride;
+    }
+    return total;
 }
 
 struct PlanGuard {
@@ -385,10 +402,13 @@ static cudaError_t plan_blob_work(kvx_plan_s *p, cudaEvent_t blobs_ready) {
 }
 
 // `defer_blob_work`: return once the blob-independent part is done; the caller enqueues
-// plan_blob_work later (so that preparing several plans never waits on a copy).
+// plan_blob_work later (so that preparing several plans never waits on a copy).  `by_tokens`: cut
+// the CTA ranges by token counts alone (an XKV plan and a BF16 plan over the same tokens then get
+// the same ranges, and bit-identical outputs); otherwise by decode cost (residual width, raw rows,
+// escape words).
 static int plan_create_impl(const kvx_unit *units, int n_units, int n_q, int dim, int block_tokens,
                             kvx_plan *out, bool pooled, cudaEvent_t blobs_ready,
-                            bool defer_blob_work = false) {
+                            bool defer_blob_work = false, bool by_tokens = false) {
     if (out == nullptr || units == nullptr || n_units <= 0 || n_q <= 0 || block_tokens <= 0 ||
         block_tokens > 255)
         return fail(KVX_ERR_INVALID_ARGUMENT, "kvx_plan_create: bad argument");
@@ -398,6 +418,7 @@ static int plan_create_impl(const kvx_unit *units, int n_units, int n_q, int dim
         return fail(KVX_ERR_UNSUPPORTED,
                     "kvexp_b200: head_dim must be 32, 64, 128 or 256 for the GPU kernels");
     const bool bf16 = units[0].k_index == nullptr;
+    if (bf16) by_tokens = true;
     const int groups = (n_q + 7) / 8;
     std::vector<kvx_unit> vu;
     std::vector<UnitDev> ud;
@@ -444,11 +465,9 @@ static int plan_create_impl(const kvx_unit *units, int n_units, int n_q, int dim
     p->bf16 = bf16;
     p->n_units = int(vu.size());
     p->n_blocks = total;
-    const int per_cta = attention_workers_per_cta(dim);
-    const int max_workers = sm_count() * per_cta;
-    p->n_workers = int(std::min<int64_t>(max_workers, total));
-    p->grid = (p->n_workers + per_cta - 1) / per_cta;
-    std::vector<int64_t> tb(size_t(p->n_workers) + 1);
+    // one CTA per SM, each with a cost-balanced range of flat blocks
+    p->n_ranges = int(std::min<int64_t>(sm_count(), total));
+    std::vector<int64_t> tb(size_t(p->n_ranges) + 1);
     kvx_unit *dvu = nullptr;
     int64_t *dbegin = nullptr, *dsrc = nullptr;
     unsigned long long *desc_total = nullptr;
@@ -457,7 +476,7 @@ static int plan_create_impl(const kvx_unit *units, int n_units, int n_q, int dim
         (e = plan_alloc(p, &p->flat, size_t(total))) != cudaSuccess ||
         (e = plan_alloc(p, &p->desc, size_t(total))) != cudaSuccess ||
         (e = plan_alloc(p, &p->range_begin, tb.size())) != cudaSuccess ||
-        (e = plan_alloc(p, &p->partials, size_t(p->n_workers) * 2 * partial_stride(dim))) != cudaSuccess ||
+        (e = plan_alloc(p, &p->seg_base, size_t(p->n_ranges))) != cudaSuccess ||
         (e = plan_alloc(p, &p->split_units, ud.size())) != cudaSuccess ||
         (e = plan_alloc(p, &p->status, 2)) != cudaSuccess ||
         (e = plan_alloc(p, &dvu, vu.size())) != cudaSuccess ||
@@ -484,42 +503,40 @@ static int plan_create_impl(const kvx_unit *units, int n_units, int n_q, int dim
         delete p;
         return fail(KVX_ERR_UNSUPPORTED, "kvx_plan_create: more than 2^32 escape record entries");
     }
-    if (e == cudaSuccess) e = plan_alloc(p, &p->esc, size_t(esc_total));
+    // (+4 entries: the kernel's 16-byte aligned bulk copies may read up to 12 bytes past the end)
+    if (e == cudaSuccess) e = plan_alloc(p, &p->esc, size_t(esc_total) + 4);
     if (e != cudaSuccess) {
         delete p;
         return fail(KVX_ERR_CUDA, std::string("kvx_plan_create: ") + cudaGetErrorString(e));
     }
-    // Worker ranges of about equal cost (tokens and escape words), then the units whose blocks
-    // span several workers (they need the combine pass).
-    // With no more blocks than workers every block is its own range, whatever the costs.
-    if (total <= max_workers) {
-        for (int t = 0; t <= p->n_workers; ++t) tb[size_t(t)] = t;
+    // CTA ranges of about equal cost; with no more blocks than CTAs every block is its own range.
+    if (total <= p->n_ranges) {
+        for (int t = 0; t <= p->n_ranges; ++t) tb[size_t(t)] = t;
         e = cudaMemcpy(p->range_begin, tb.data(), tb.size() * sizeof(int64_t), cudaMemcpyHostToDevice);
     } else {
-        e = launch_split(p->flat, total, p->n_workers, p->range_begin, nullptr);
+        e = launch_split(p->flat, total, p->n_ranges, by_tokens, p->range_begin, nullptr);
         if (e == cudaSuccess)
             e = cudaMemcpy(tb.data(), p->range_begin, tb.size() * sizeof(int64_t),
                            cudaMemcpyDeviceToHost);
     }
+    // the partial-state rows of every unit segment of every range, and the combine's unit list
+    std::vector<int32_t> seg_base;
     std::vector<SplitUnit> split;
     if (e == cudaSuccess) {
-        for (int u = 0; u < p->n_units; ++u) {
-            const int t0 = worker_of_block(tb.data(), p->n_workers, ud[size_t(u)].block_begin);
-            const int t1 = worker_of_block(tb.data(), p->n_workers,
-                                           ud[size_t(u)].block_begin + ud[size_t(u)].n_blocks - 1);
-            if (t0 != t1)
-                split.push_back(make_split(ud[size_t(u)], t0, t1,
-                                           tb[size_t(t0)] < ud[size_t(u)].block_begin ? 1 : 0));
-        }
-        if (!split.empty())
-            e = cudaMemcpy(p->split_units, split.data(), split.size() * sizeof(SplitUnit),
-                           cudaMemcpyHostToDevice);
+        p->n_rows = plan_segments(tb, p->n_ranges, ud, dim, seg_base, split);
+        e = cudaMemcpy(p->seg_base, seg_base.data(), seg_base.size() * sizeof(int32_t),
+                       cudaMemcpyHostToDevice);
     }
+    if (e == cudaSuccess)
+        e = cudaMemcpy(p->split_units, split.data(), split.size() * sizeof(SplitUnit),
+                       cudaMemcpyHostToDevice);
+    if (e == cudaSuccess)
+        e = plan_alloc(p, &p->partials,
+                       size_t(p->n_rows) * attention_consumer_warps(dim) * partial_stride(dim));
     if (e != cudaSuccess) {
         delete p;
         return fail(KVX_ERR_CUDA, std::string("kvx_plan_create: ") + cudaGetErrorString(e));
     }
-    p->n_split = int(split.size());
     // errors of the flat list and the record layout (the copies above waited for those kernels)
     if (int rc = read_status(p->status, true)) {
         delete p;
@@ -563,15 +580,10 @@ int kvx_plan_run_part(kvx_plan p, int part, void *stream) {
     if (p == nullptr) return fail(KVX_ERR_INVALID_ARGUMENT, "kvx_plan_run: null plan");
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     if (part == 1) {
-        if (p->n_split > 0) {
-            CombineArgs c{};
-            c.units = p->units;
-            c.split = p->split_units;
-            c.range_begin = p->range_begin;
-            c.partials = p->partials;
-            c.n_workers = p->n_workers;
-            KVX_CUDA(launch_combine(p->dim, c, p->n_split, s));
-        }
+        CombineArgs c{};
+        c.split = p->split_units;
+        c.partials = p->partials;
+        KVX_CUDA(launch_combine(p->dim, c, p->n_units, s));
         return KVX_OK;
     }
     if (part != 0) return fail(KVX_ERR_INVALID_ARGUMENT, "kvx_plan_run_part: part is 0 or 1");
@@ -581,10 +593,11 @@ int kvx_plan_run_part(kvx_plan p, int part, void *stream) {
     a.desc = p->desc;
     a.esc = p->esc;
     a.range_begin = p->range_begin;
+    a.seg_base = p->seg_base;
     a.partials = p->partials;
     a.status = p->status;
-    a.n_workers = p->n_workers;
-    KVX_CUDA(launch_attention(p->dim, p->bf16, a, p->grid, s));
+    a.n_ranges = p->n_ranges;
+    KVX_CUDA(launch_attention(p->dim, p->bf16, a, p->n_ranges, s));
     return KVX_OK;
 }
 
@@ -596,9 +609,9 @@ int kvx_plan_check(kvx_plan p) {
     return KVX_OK;
 }
 
-int kvx_plan_launches(kvx_plan p) { return p ? 1 + (p->n_split > 0 ? 1 : 0) : 0; }
+int kvx_plan_launches(kvx_plan p) { return p ? 2 : 0; }
 
-int kvx_plan_split_units(kvx_plan p) { return p ? p->n_split : 0; }
+int kvx_plan_split_units(kvx_plan p) { return p ? p->n_units : 0; }
 
 void kvx_plan_destroy(kvx_plan p) { delete p; }
 
@@ -696,7 +709,8 @@ int to_device(const void *src, size_t bytes, DevBuf &buf, const void *&dptr, cud
 int run_units(std::vector<kvx_unit> &units, int n_q, int dim, int block_tokens, cudaStream_t s) {
     KVX_CUDA(cudaStreamSynchronize(s));
     kvx_plan plan = nullptr;
-    if (int rc = kvx_plan_create(units.data(), int(units.size()), n_q, dim, block_tokens, &plan))
+    if (int rc = plan_create_impl(units.data(), int(units.size()), n_q, dim, block_tokens, &plan,
+                                  false, nullptr, false, true))
         return rc;
     int rc = kvx_plan_run(plan, s);
     if (rc == KVX_OK) rc = kvx_plan_check(plan);
@@ -1245,7 +1259,7 @@ constexpr size_t kNoAllocScratchBytes = size_t(30) << 20;  // 30 MiB per device
 constexpr size_t kNoAllocEscEntries = size_t(3) << 20;      // escape record entries (12 MiB)
 constexpr int kNoAllocMaxBlocks = 8192;                   // XKV blocks per tensor
 constexpr int kNoAllocMaxQueries = 64;                    // queries per call (8 groups of 8)
-constexpr int kNoAllocMaxWorkers = 4096;
+constexpr int kNoAllocMaxRanges = 1024;                   // CTA ranges of the attention grid
 constexpr int kNoAllocMaxGroups = kNoAllocMaxQueries / 8;  // query groups of <= 8
 
 constexpr size_t up256c(size_t x) { return (x + 255) & ~size_t(255); }
@@ -1257,12 +1271,16 @@ constexpr size_t kNoAllocFixedBytes =
     up256c(kNoAllocMaxGroups * sizeof(int64_t)) + up256c(kNoAllocMaxGroups * sizeof(SplitUnit)) +
     up256c(size_t(kNoAllocMaxGroups) * kNoAllocMaxBlocks * sizeof(FlatBlock)) +
     up256c(size_t(kNoAllocMaxGroups) * kNoAllocMaxBlocks * sizeof(BlockDesc)) +
-    up256c((kNoAllocMaxWorkers + 1) * sizeof(int64_t)) + up256c(sizeof(unsigned long long)) +
-    up256c(kNoAllocEscEntries * sizeof(uint32_t));
-// The partial states of one worker at the widest head dim (two slots of m, l and acc).
-constexpr size_t kNoAllocWorkerBytes256 = 2 * size_t(16 + 8 * kMaxHeadDim) * sizeof(float);
-static_assert(kNoAllocFixedBytes + 148 * kNoAllocWorkerBytes256 <= kNoAllocScratchBytes,
-              "the fixed scratch must leave room for one worker per SM at head_dim 256");
+    up256c((kNoAllocMaxRanges + 1) * sizeof(int64_t)) + up256c(kNoAllocMaxRanges * sizeof(int32_t)) +
+    up256c(sizeof(unsigned long long)) + up256c((kNoAllocEscEntries + 4) * sizeof(uint32_t));
+// One partial-state row (every consumer warp's m, l and acc) at its largest, over the head dims.
+constexpr size_t noalloc_row_bytes(int dim) {
+    return size_t(attention_consumer_warps(dim)) * size_t(16 + 8 * dim) * sizeof(float);
+}
+constexpr size_t kNoAllocMaxRowBytes =
+    noalloc_row_bytes(128) > noalloc_row_bytes(256) ? noalloc_row_bytes(128) : noalloc_row_bytes(256);
+static_assert(kNoAllocFixedBytes + (64 + kNoAllocMaxGroups) * kNoAllocMaxRowBytes <= kNoAllocScratchBytes,
+              "the fixed scratch must leave room for the partial states of at least 64 CTAs");
 }  // namespace
 }  // namespace kvx
 
@@ -1331,8 +1349,8 @@ extern "C" int kvx_attention_decode_noalloc(const uint16_t *q, const uint8_t *k_
     cudaStream_t s = static_cast<cudaStream_t>(stream);
 
     // Scratch layout (256-byte aligned pieces): status | units | unit descriptors | block
-    // begins | record sources | split units | flat blocks | worker ranges | record size |
-    // escape records | partial states.
+    // begins | record sources | split units | flat blocks | block descriptors | CTA ranges | row
+    // bases | record size | escape records | partial states.
     const int groups = (n_q + 7) / 8;
     const int64_t total = int64_t(groups) * n_blocks;
     size_t off = 0;
@@ -1342,27 +1360,28 @@ extern "C" int kvx_attention_decode_noalloc(const uint16_t *q, const uint8_t *k_
         return base + o;
     };
     int *status = reinterpret_cast<int *>(take(2 * sizeof(int)));
-    UnitDev *d_units = reinterpret_cast<UnitDev *>(take(kNoAllocMaxQueries / 8 * sizeof(UnitDev)));
-    kvx_unit *d_vu = reinterpret_cast<kvx_unit *>(take(kNoAllocMaxQueries / 8 * sizeof(kvx_unit)));
-    int64_t *d_begin = reinterpret_cast<int64_t *>(take(kNoAllocMaxQueries / 8 * sizeof(int64_t)));
-    int64_t *d_src = reinterpret_cast<int64_t *>(take(kNoAllocMaxQueries / 8 * sizeof(int64_t)));
-    SplitUnit *d_split = reinterpret_cast<SplitUnit *>(take(kNoAllocMaxQueries / 8 * sizeof(SplitUnit)));
+    UnitDev *d_units = reinterpret_cast<UnitDev *>(take(kNoAllocMaxGroups * sizeof(UnitDev)));
+    kvx_unit *d_vu = reinterpret_cast<kvx_unit *>(take(kNoAllocMaxGroups * sizeof(kvx_unit)));
+    int64_t *d_begin = reinterpret_cast<int64_t *>(take(kNoAllocMaxGroups * sizeof(int64_t)));
+    int64_t *d_src = reinterpret_cast<int64_t *>(take(kNoAllocMaxGroups * sizeof(int64_t)));
+    SplitUnit *d_split = reinterpret_cast<SplitUnit *>(take(kNoAllocMaxGroups * sizeof(SplitUnit)));
     FlatBlock *d_flat = reinterpret_cast<FlatBlock *>(
-        take(size_t(kNoAllocMaxQueries / 8) * kNoAllocMaxBlocks * sizeof(FlatBlock)));
+        take(size_t(kNoAllocMaxGroups) * kNoAllocMaxBlocks * sizeof(FlatBlock)));
     BlockDesc *d_desc = reinterpret_cast<BlockDesc *>(
-        take(size_t(kNoAllocMaxQueries / 8) * kNoAllocMaxBlocks * sizeof(BlockDesc)));
-    int64_t *d_range = reinterpret_cast<int64_t *>(take((kNoAllocMaxWorkers + 1) * sizeof(int64_t)));
+        take(size_t(kNoAllocMaxGroups) * kNoAllocMaxBlocks * sizeof(BlockDesc)));
+    int64_t *d_range = reinterpret_cast<int64_t *>(take((kNoAllocMaxRanges + 1) * sizeof(int64_t)));
+    int32_t *d_seg = reinterpret_cast<int32_t *>(take(kNoAllocMaxRanges * sizeof(int32_t)));
     unsigned long long *d_esc_total =
         reinterpret_cast<unsigned long long *>(take(sizeof(unsigned long long)));
-    uint32_t *d_esc = reinterpret_cast<uint32_t *>(take(kNoAllocEscEntries * sizeof(uint32_t)));
+    uint32_t *d_esc = reinterpret_cast<uint32_t *>(take((kNoAllocEscEntries + 4) * sizeof(uint32_t)));
     if (off != kNoAllocFixedBytes)
         return fail(KVX_ERR_RUNTIME, std::string(fn) + "scratch layout out of step with its size");
     float *d_partials = reinterpret_cast<float *>(base + off);
-    const size_t per_worker = 2 * size_t(partial_stride(dim)) * sizeof(float);
-    const int64_t fit = int64_t((kNoAllocScratchBytes - off) / per_worker);
-    const int per_cta = attention_workers_per_cta(dim);
-    const int n_workers = int(std::min<int64_t>(
-        std::min<int64_t>(total, int64_t(sm_count()) * per_cta), std::min<int64_t>(fit, kNoAllocMaxWorkers)));
+    // A range holds at most one more unit segment than it crosses unit starts, so the rows are at
+    // most n_ranges + groups - 1: cap the ranges so that they fit the rest of the scratch.
+    const int64_t fit_rows = int64_t((kNoAllocScratchBytes - off) / noalloc_row_bytes(dim));
+    const int n_ranges = int(std::max<int64_t>(1, std::min<int64_t>(
+        std::min<int64_t>(total, sm_count()), std::min<int64_t>(fit_rows - groups + 1, kNoAllocMaxRanges))));
 
     // Host-side descriptors (plain stack / vector memory, copied into the scratch).
     std::vector<kvx_unit> vu(static_cast<size_t>(groups));
@@ -1394,17 +1413,14 @@ extern "C" int kvx_attention_decode_noalloc(const uint16_t *q, const uint8_t *k_
         d.q_stride = dim;
         begin[size_t(g)] = d.block_begin;
     }
-    // Worker ranges: one block each when they fit, else an even split of the blocks.
-    std::vector<int64_t> tb(static_cast<size_t>(n_workers) + 1);
-    for (int t = 0; t <= n_workers; ++t) tb[size_t(t)] = int64_t(t) * total / n_workers;
+    // CTA ranges: one block each when they fit, else an even split of the blocks; then the
+    // partial-state rows of every unit segment and the combine's unit list.
+    std::vector<int64_t> tb(static_cast<size_t>(n_ranges) + 1);
+    for (int t = 0; t <= n_ranges; ++t) tb[size_t(t)] = int64_t(t) * total / n_ranges;
+    std::vector<int32_t> seg_base;
     std::vector<SplitUnit> split;
-    for (int g = 0; g < groups; ++g) {
-        const int t0 = worker_of_block(tb.data(), n_workers, ud[size_t(g)].block_begin);
-        const int t1 = worker_of_block(tb.data(), n_workers,
-                                       ud[size_t(g)].block_begin + ud[size_t(g)].n_blocks - 1);
-        if (t0 != t1)
-            split.push_back(make_split(ud[size_t(g)], t0, t1, tb[size_t(t0)] < ud[size_t(g)].block_begin ? 1 : 0));
-    }
+    const int64_t rows = plan_segments(tb, n_ranges, ud, dim, seg_base, split);
+    if (rows > fit_rows) return fail(KVX_ERR_RUNTIME, std::string(fn) + "partial states exceed the scratch");
 
     // Every call shares the scratch and finds the previous call's contents there: the status
     // word is cleared here; everything else is fully written before it is read.
@@ -1414,9 +1430,9 @@ extern "C" int kvx_attention_decode_noalloc(const uint16_t *q, const uint8_t *k_
     KVX_CUDA(cudaMemcpyAsync(d_begin, begin.data(), begin.size() * sizeof(int64_t), cudaMemcpyHostToDevice, s));
     KVX_CUDA(cudaMemcpyAsync(d_src, srcs.data(), srcs.size() * sizeof(int64_t), cudaMemcpyHostToDevice, s));
     KVX_CUDA(cudaMemcpyAsync(d_range, tb.data(), tb.size() * sizeof(int64_t), cudaMemcpyHostToDevice, s));
-    if (!split.empty())
-        KVX_CUDA(cudaMemcpyAsync(d_split, split.data(), split.size() * sizeof(SplitUnit),
-                                 cudaMemcpyHostToDevice, s));
+    KVX_CUDA(cudaMemcpyAsync(d_seg, seg_base.data(), seg_base.size() * sizeof(int32_t), cudaMemcpyHostToDevice, s));
+    KVX_CUDA(cudaMemcpyAsync(d_split, split.data(), split.size() * sizeof(SplitUnit),
+                             cudaMemcpyHostToDevice, s));
     KVX_CUDA(launch_build_flat(d_vu, d_begin, d_src, groups, dim, kDefaultBlock, false, d_flat,
                                status, s));
     KVX_CUDA(launch_esc_layout(d_flat, total, d_esc_total, kNoAllocEscEntries, status, s));
@@ -1428,20 +1444,15 @@ extern "C" int kvx_attention_decode_noalloc(const uint16_t *q, const uint8_t *k_
     a.desc = d_desc;
     a.esc = d_esc;
     a.range_begin = d_range;
+    a.seg_base = d_seg;
     a.partials = d_partials;
     a.status = status;
-    a.n_workers = n_workers;
-    const int grid = (n_workers + per_cta - 1) / per_cta;
-    KVX_CUDA(launch_attention(dim, false, a, grid, s));
-    if (!split.empty()) {
-        CombineArgs c{};
-        c.units = d_units;
-        c.split = d_split;
-        c.range_begin = d_range;
-        c.partials = d_partials;
-        c.n_workers = n_workers;
-        KVX_CUDA(launch_combine(dim, c, int(split.size()), s));
-    }
+    a.n_ranges = n_ranges;
+    KVX_CUDA(launch_attention(dim, false, a, n_ranges, s));
+    CombineArgs c{};
+    c.split = d_split;
+    c.partials = d_partials;
+    KVX_CUDA(launch_combine(dim, c, groups, s));
     // The host descriptors above are pageable stack/vector memory: wait for the stream before
     // they go out of scope, then report device-side errors like kvx_attention_decode.
     KVX_CUDA(cudaStreamSynchronize(s));

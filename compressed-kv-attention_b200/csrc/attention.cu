@@ -4,44 +4,45 @@
 // src/attention_{scalar,avx2,avx512}.cpp and the online softmax of src/softmax.hpp), restructured
 // for the GPU:
 //
-//  * The step's (unit, block) pairs are flattened; each worker warp owns a contiguous range and
-//    streams stages of TS tokens of K and V through its own shared-memory ring: sign/mantissa
-//    rows, packed exponent residuals, and the stage's escape words with their tile slots -- or raw
-//    BF16 rows.  The pieces arrive as 1-D bulk copies of the TMA engine, issued in parallel by
-//    ten lanes and completing on the ring slot's mbarrier.  A block's base exponents ride along
-//    with its first stage.  Only the compressed bytes cross HBM (plus, for a coded block with
-//    escapes, its escape record: 2 bytes per escape word and a 32-byte count header, built once
-//    per plan), and no warp ever waits on another warp.
-//  * Each lane rebuilds 8-element chunks of a stage's rows into BF16 words and stores them, 16
-//    bytes at a time, into the warp's tile: TS rows of D BF16 values with 16-byte chunks swizzled
-//    so that neither those stores nor the ldmatrix reads of the MMA conflict on shared-memory
-//    banks.  A pair of elements costs four instructions: two byte permutes (sign/mantissa bytes;
-//    exponent residuals), one multiply-add that adds the residual to the base exponent, and one
-//    bit-select.  A block's sections start 0 or 2 bytes past a 4-byte boundary of the ring (every
-//    size and offset in an XKV blob is even); the permutes take that shift in their selectors.
-//  * Escape words are stored over their elements of the tile: one 16-bit store each, at the slot
-//    the block's escape record gives.
-//  * S = K Q^T runs on the tensor cores (mma.sync m16n8k16, tokens x queries, fp32 accumulate)
-//    with K fragments from ldmatrix; the online softmax runs on the S fragments of a whole stage:
-//    lane (g, t) holds queries 2t and 2t+1, which are also the output columns it accumulates, so
-//    the rescale factors never leave the lane.  O^T += V^T P^T reads V^T with ldmatrix.trans; P^T
-//    enters split into a bf16 part and a bf16 residual part (two MMAs), with 16 significant bits.
-//  * Unit segments that span several workers leave (m, l, acc) partial states that combine_kernel
-//    folds in worker order with merge_state semantics (src/softmax.hpp:16-30), then finalizes like
-//    finalize_state (src/softmax.hpp:32-41: reciprocal, then multiply).
+//  * The step's (unit, block) pairs are flattened and cut into one cost-balanced range per CTA
+//    (one CTA per SM).  A CTA streams its blocks through a shared-memory ring of stages; a stage
+//    is up to TSB tokens of one block: the block's descriptor, and per tensor its base exponents,
+//    sign/mantissa rows, packed residual codes and the escape-record entries of those tokens (or
+//    raw BF16 rows).  One producer warp issues the stage as a handful of 1-D bulk copies of the
+//    TMA engine that complete on the slot's "full" mbarrier; only the compressed bytes cross HBM
+//    (plus, for a coded block with escapes, its escape record: 4 bytes per escape word and a
+//    64-byte count header, built once per plan).
+//  * The consumer warps (15, or 7 at D = 256) share every stage: the stage's 16-token tiles go round-robin
+//    over them (tile j of the CTA to warp j mod NW), each warp keeping its own online-softmax
+//    state.  A warp rebuilds its tile's K rows into BF16 words in its private tile (16 rows of D
+//    BF16 values, 16-byte chunks swizzled so that neither the decode stores nor the ldmatrix
+//    reads conflict on banks): per pair of elements two byte permutes, one multiply-add that adds
+//    the residual to the base exponent, and one bit-select.  Escape words are stored over their
+//    elements, one 16-bit store each, at the tile byte the escape record gives.
+//  * S = K Q^T on the tensor cores (mma.sync m16n8k16, tokens x queries, fp32 accumulate), the
+//    online softmax on the S fragment (lane (g, t) holds queries 2t and 2t+1, which are also the
+//    output columns it accumulates), then the tile's V rows replace K in the tile and
+//    O^T += V^T P^T reads V^T with ldmatrix.trans; P^T enters as three bf16 terms (all 24 bits of
+//    the fp32 weight).  Each warp arrives on the slot's "empty" mbarrier once it has read the
+//    stage, which frees the slot for the producer when every consumer warp has.
+//  * At the end of each unit segment of the CTA's range every consumer warp writes its (m, l,
+//    acc) state; combine_kernel folds a unit's states with merge_state semantics
+//    (src/softmax.hpp:16-30) and finalizes like finalize_state (src/softmax.hpp:32-41:
+//    reciprocal, then multiply).
 //
 // The BF16-input variant (BF16IN) is the same template reading [seq, dim] BF16 rows into the same
-// tile; for the same blocks and worker ranges it produces bit-identical outputs to the XKV variant,
+// tile; for the same blocks and CTA ranges it produces bit-identical outputs to the XKV variant,
 // because the tensor cores see identical BF16 tiles and everything after them is the same code.
-// (Ranges are one block per worker whenever the step has no more blocks than workers; beyond
-// that they are balanced by cost.)
+// (The drop-in single-head entry point cuts both inputs into CTA ranges by token counts alone, so
+// the ranges always agree there.)
+
 #include "attention.cuh"
 
 namespace kvx {
 namespace {
 
 constexpr uint32_t FULL = 0xFFFFFFFFu;
-constexpr int TT = 16;  // tokens per MMA tile (one m16 block of the QK MMA)
+constexpr int TT = kTileTokens;  // tokens per MMA tile (one m16 block of the QK MMA)
 constexpr float kLog2e = 1.4426950408889634f;
 
 // 2^x by the SFU (ex2.approx.ftz.f32: one instruction; results below 2^-126, softmax weights
@@ -58,42 +59,39 @@ __host__ __device__ constexpr int round16(int x) { return (x + 15) & ~15; }
 // times out in some lanes just as the phase completes for others).
 __device__ __forceinline__ bool uni(bool c) { return __all_sync(0xFFFFFFFFu, c); }
 __host__ __device__ constexpr int cmin(int a, int b) { return a < b ? a : b; }
-__host__ __device__ constexpr int cmax(int a, int b) { return a > b ? a : b; }
 
-#ifndef KVX_MAXWARPS
-#define KVX_MAXWARPS 12
-#endif
+
 template <int D> struct Cfg {
     static constexpr int KS = D / 16;             // k-steps of QK = M-tiles of PV
-    static constexpr int TS = stage_tokens(D);    // tokens per ring stage
-    static constexpr int SUBS = TS / TT;          // MMA tiles per stage
     static constexpr int C8 = D / 8;              // 8-element chunks per row
-    static constexpr int NIT = TS * C8 / 32;      // chunk steps of a lane per stage and tensor
-    // One tensor's stage: sign/mantissa rows | residual codes | escape record entries, or TS raw
-    // BF16 rows -- both fit 2 TS D bytes (escapes beyond ESC_CAP stay in HBM).
-    static constexpr int ESC_CAP = TS * D / 8;
-    static constexpr int CODE_OFF = TS * D + 16;
-    static constexpr int EE_OFF = CODE_OFF + TS * D / 2 + 16;
-    static constexpr int TR = round16(cmax(EE_OFF + 4 * ESC_CAP + 16, TS * 2 * D + 16));
-    // Ring of tensor-stages: K of stage s, V of stage s, K of stage s + 1, ...  A slot is free
-    // again once its tensor is in the tile, so three slots keep one stage of copies in flight.
-    static constexpr int NSLOT = 3;
-    static constexpr int BASE = round16(D + 32);  // one block's base exponents (+ alignment slack)
-    static constexpr int MSLOT = 2 * BASE;        // per-block meta slot: K base | V base
-    static constexpr int XB = TS * 2 * D;         // the BF16 tile of one tensor's stage
-    static constexpr int NDESC = 4;               // block descriptor ring
-    // per-warp region: ring | meta x2 | tile | descriptors | one mbarrier per ring slot and
-    // per descriptor
-    static constexpr int W_META = NSLOT * TR;
-    static constexpr int W_XB = W_META + 2 * MSLOT;
-    static constexpr int W_DESC = W_XB + XB;
-    static constexpr int W_BAR = W_DESC + NDESC * int(sizeof(BlockDesc));
-    static constexpr int W_DBAR = W_BAR + 8 * NSLOT;
-    static constexpr int WARP_BYTES = (W_DBAR + 8 * NDESC + 127) & ~127;
-    static constexpr int MAXW = D <= 32 ? 16 : KVX_MAXWARPS;
-    static constexpr int WARPS = cmin(MAXW, 232448 / WARP_BYTES);
-    static_assert(WARPS >= 1, "worker does not fit in shared memory");
+    static constexpr int NIT = TT * C8 / 32;      // chunk steps of a lane per tile and tensor
+    static constexpr int TSB = cmin(128, 8192 / D);  // tokens per ring stage
+    static constexpr int TPS = TSB / TT;          // tiles per stage
+    static constexpr int NW = attention_consumer_warps(D);  // consumer warps
+    static constexpr int NSLOT = 4;               // ring slots
+    // Escape-record entries of one tensor that a stage stages (12.5 % of its elements); a stage
+    // with more leaves them in HBM, where the consumers read them.
+    static constexpr int ESC_CAP = TSB * D / 8;
+    // One tensor's region of a slot: rows at 0 (raw: 2 D bytes per token; coded: D bytes, then the
+    // residual codes at CODE_OFF), base exponents at B_OFF, escape entries at E_OFF.  Every piece
+    // lands 0-15 bytes past its 16-byte aligned start.
+    static constexpr int R_BYTES = 2 * TSB * D + 32;
+    static constexpr int CODE_OFF = TSB * D + 16;
+    static constexpr int B_OFF = R_BYTES;
+    static constexpr int E_OFF = B_OFF + round16(D + 32);
+    static constexpr int T_BYTES = round16(E_OFF + 4 * ESC_CAP + 32);
+    // A slot: the block descriptor (128 bytes), then the K and V regions.
+    static constexpr int S_T = 128;
+    static constexpr int SLOT = S_T + 2 * T_BYTES;
+    static constexpr int TILE = TT * 2 * D;       // one consumer warp's BF16 tile
+    static constexpr int O_TILE = NSLOT * SLOT;
+    static constexpr int O_BAR = O_TILE + NW * TILE;  // full[NSLOT], then empty[NSLOT]
+    static constexpr int SMEM = O_BAR + 16 * NSLOT;
+    static constexpr int THREADS = 32 * (NW + 1);
+    static_assert(SMEM + 16 <= 232448, "stage ring and tiles exceed shared memory");
+    static_assert(NW >= TPS, "a consumer warp takes at most one tile of a stage");
     static_assert(32 % C8 == 0 && NIT >= 1, "a warp step covers whole rows");
+    static_assert((TSB * D) % 4096 == 0, "stage offsets keep every section's 16-byte alignment");
 };
 
 // ---- copies ------------------------------------------------------------------------------------
@@ -118,38 +116,9 @@ __device__ __forceinline__ Piece make_piece(const uint8_t *p, uint32_t len) {
 // Longest a warp waits for one stage before it reports DERR_TIMEOUT and stops (microseconds).
 constexpr uint32_t kStageWaitUs = 1000000;
 
-// Section pointers of one tensor of one block.
-struct Sections {
-    const uint8_t *rows;   // coded: sign/mantissa rows; raw / BF16: BF16 rows
-    const uint8_t *codes;  // coded: packed residual codes
-    const uint8_t *esc;    // coded: escape words
-};
-
-// blk: the block's header (BF16 input: its first row).
-template <int D, bool BF16IN>
-__device__ __forceinline__ Sections sections(const uint8_t *blk, int mode, int n_tok) {
-    Sections s;
-    if (BF16IN) {
-        s.rows = blk;
-        s.codes = s.esc = nullptr;
-    } else if (mode == 0) {
-        s.rows = blk + kHeaderBytes;
-        s.codes = s.esc = nullptr;
-    } else {
-        s.rows = blk + kHeaderBytes + D;
-        s.codes = s.rows + size_t(n_tok) * D;
-        s.esc = s.codes + size_t(n_tok) * D * mode / 8;
-    }
-    return s;
-}
 
 // ---- escape records ----------------------------------------------------------------------------
 
-// e(i) of tensor T (0 K, 1 V), i = 0..16; every lane of the warp calls it.
-__device__ __forceinline__ int esc_at(uint32_t em, int T, int i) {
-    const uint32_t v = __shfl_sync(FULL, em, (T << 4) + ((i + 15) & 15));
-    return i == 0 ? 0 : int(v);
-}
 
 // e(i) of tensor T from a block descriptor's headers.
 __device__ __forceinline__ int esc_ms(const BlockDesc &bd, int T, int i) {
@@ -160,6 +129,11 @@ __device__ __forceinline__ int esc_ms(const BlockDesc &bd, int T, int i) {
 // 16-byte aligned).
 __device__ __forceinline__ uint32_t esc_rec_line(uint32_t rec, int i) {
     return (4u * (rec + uint32_t(kEscRecHead) + uint32_t(i))) & 15u;
+}
+
+// e(i) of tensor T from a block descriptor in global memory (the producer's copy).
+__device__ __forceinline__ int esc_gd(const BlockDesc *gd, int T, int i) {
+    return i == 0 ? 0 : int(__ldg(&gd->em[T][i - 1]));
 }
 
 // ---- decode helpers ----------------------------------------------------------------------------
@@ -328,16 +302,18 @@ __device__ __forceinline__ void decode_groups(uint32_t qr, uint32_t qc, const La
     if constexpr (K0 + G < NIT) decode_groups<D, MODE, G, K0 + G>(qr, qc, ly, b7, sm, Wn, Xn);
 }
 
-// Rebuild this lane's chunks of one tensor's stage into the tile (MODE 4 / 2 coded, 0 raw BF16).
+// Rebuild this lane's chunks of one tensor's 16-token tile into the warp's BF16 tile (MODE 4 / 2
+// coded, 0 raw BF16).  rb / cb: the tile's rows / residual codes are at rb + ly.rows and
+// cb + ly.codes (plus the lane's row).
 template <int D, int MODE>
-__device__ __forceinline__ void decode_stage(uint32_t stage, const Lay &ly, const uint32_t (&b7)[4],
-                                             const StoreMap<D> &sm, int lane) {
+__device__ __forceinline__ void decode_tile(uint32_t rb, uint32_t cb, const Lay &ly, const uint32_t (&b7)[4],
+                                            const StoreMap<D> &sm, int lane) {
     using C = Cfg<D>;
     // chunk steps per group (two groups' loads are live at a time)
     constexpr int G = C::NIT < 4 ? C::NIT : 4;
     const int r0 = lane / C::C8;
-    const uint32_t qr = stage + ly.rows + uint32_t(r0 * (MODE == 0 ? 2 * D : D));
-    const uint32_t qc = stage + ly.codes + uint32_t(r0 * (D * MODE / 8));
+    const uint32_t qr = rb + ly.rows + uint32_t(r0 * (MODE == 0 ? 2 * D : D));
+    const uint32_t qc = cb + ly.codes + uint32_t(r0 * (D * MODE / 8));
     uint32_t W[G][MODE == 0 ? 5 : 3], X[G][2];
     load_chunks<D, MODE, G, 0>(qr, qc, W, X);
     decode_groups<D, MODE, G, 0>(qr, qc, ly, b7, sm, W, X);
@@ -457,414 +433,386 @@ __device__ __forceinline__ void load_q(const uint16_t *q, int n_q, int stride,
     }
 }
 
-// ---- the worker -------------------------------------------------------------------------------
+// ---- the CTA: one producer warp, NW consumer warps -------------------------------------------
 
-__device__ __forceinline__ const uint8_t *desc_ptr(uint64_t a) { return reinterpret_cast<const uint8_t *>(a); }
+__device__ __forceinline__ const uint8_t *gptr(uint64_t a) { return reinterpret_cast<const uint8_t *>(a); }
 
-// Copy side of the worker's ring.  Block descriptors arrive in a ring of NDESC slots, fetched one
-// block ahead of their first stage (block fb0 + i uses slot i % NDESC); the producer reads a block's descriptor when
-// it issues the block's first stage, the consumer while it works on the block.
-template <int D, bool BF16IN> struct Producer {
-    using C = Cfg<D>;
-    int fb, fb0, fb1;  // next block to start; the worker's range
-    int pf;            // next block whose descriptor is fetched
-    int dwait;         // next block whose descriptor is waited for
-    int tile = 0, q = 0, bseq = 0;  // q: tensor-stages issued (2 per stage, K first)
-    int valid = 0;     // tokens of the block being issued
-    uint32_t em = 0u;  // lane l: entry l % 16 of its K (l < 16) / V count header
-    // This lane's piece of every stage of the current block.  Lane 4 T + j (j < 4) copies piece j
-    // of tensor T: rows (j 0) and residual codes (j 1) are [src + t0 stride, + n stride) for the
-    // stage's tokens [t0, t0 + n); the escape record entries (j 2) of the stage's escapes
-    // [e0, e1) are at src + 4 e0, copied when they fit the slot.  Lanes 8 and 9 copy the K and V base
-    // exponents (D bytes at src) with the block's first stage.  dst: offset in the ring slot or
-    // (base exponents) in the meta slot.
-    const uint8_t *src = nullptr;
-    uint32_t stride = 0, dst = 0;
-    int kind = 0;  // 0 none, 1 strided, 2 escapes, 3 base exponents
+// Shared-memory address of ring barrier `i` (full: i < NSLOT; empty: NSLOT + i).
+template <int D> __device__ __forceinline__ uint32_t ring_bar(uint32_t sb, int i) {
+    return sb + uint32_t(Cfg<D>::O_BAR + 8 * i);
+}
 
-    // Fetch descriptors up to the block after the next one to start (lane 0 issues).  A block
-    // starts when the consumer is at most one block behind, so the slot a fetch overwrites (its
-    // block four earlier) is no longer read.
-    __device__ __forceinline__ void fetch(const AttnArgs &a, uint8_t *R, int lane) {
-        while (pf < fb1 && pf <= fb + 1) {
-            const int i = (pf - fb0) % C::NDESC;
-            const uint32_t bar = smem_u32(R + C::W_DBAR + 8 * i);
-            if (lane == 0) {
-                mbar_arrive_expect_tx(bar, uint32_t(sizeof(BlockDesc)));
-                bulk_g2s(smem_u32(R + C::W_DESC + i * int(sizeof(BlockDesc))),
-                         reinterpret_cast<const uint8_t *>(a.desc + pf), uint32_t(sizeof(BlockDesc)), bar);
-            }
-            ++pf;
-        }
-    }
+// One bulk copy of [src, src + len) into the shared region at `dst`: the 16-byte aligned superset
+// lands at dst (the wanted bytes start (src & 15) bytes in).  Returns the bytes copied.
+__device__ __forceinline__ uint32_t stage_piece(uint32_t dst, const uint8_t *src, uint32_t len,
+                                                uint32_t bar) {
+    if (len == 0u) return 0u;
+    const Piece p = make_piece(src, len);
+    bulk_g2s(dst, p.src, p.alloc, bar);
+    return p.alloc;
+}
 
-    __device__ __forceinline__ bool start_block(const AttnArgs &a, uint8_t *R, int lane) {
-        const int i = (fb - fb0) % C::NDESC;
-        if (!uni(mbar_wait_bounded(smem_u32(R + C::W_DBAR + 8 * i), ((fb - fb0) / C::NDESC) & 1, kStageWaitUs)))
-            return false;
-        dwait = fb + 1;
-        const BlockDesc &bd = *reinterpret_cast<const BlockDesc *>(R + C::W_DESC + i * int(sizeof(BlockDesc)));
-        const int T = (lane >> 2) & 1, j = lane & 3;
-        const int km = BF16IN ? 0 : bd.k_mode, vm = BF16IN ? 0 : bd.v_mode;
-        const int mode = T ? vm : km;
-        const uint8_t *blk = desc_ptr(T ? bd.v : bd.k);
-        const Sections sc = sections<D, BF16IN>(blk, mode, bd.n_tok);
-        valid = bd.valid;
-        em = bd.em[lane >> 4][lane & 15];
-        src = nullptr;
-        stride = 0;
-        kind = 0;
-        dst = 0u;
-        if (lane < 8) {
-            if (j == 0) {
-                src = sc.rows;
-                stride = (BF16IN || mode == 0) ? 2 * D : D;
-                kind = 1;
-            } else if (!BF16IN && mode != 0) {
-                if (j == 1) {
-                    src = sc.codes;
-                    stride = uint32_t(D * mode / 8);
-                    dst += C::CODE_OFF;
-                    kind = 1;
-                } else if (j == 2) {
-                    src = reinterpret_cast<const uint8_t *>(a.esc + (T ? bd.v_rec : bd.k_rec) + kEscRecHead);
-                    dst += C::EE_OFF;
-                    kind = 2;
-                }
-            }
-        } else if (!BF16IN && lane < 10 && (lane == 8 ? km : vm) != 0) {
-            src = desc_ptr(lane == 8 ? bd.k : bd.v) + kHeaderBytes;
-            dst = uint32_t((lane - 8) * C::BASE);
-            kind = 3;
-        }
-        return true;
-    }
+// Bytes stage_piece copies for [src, src + len).
+__device__ __forceinline__ uint32_t piece_bytes(const uint8_t *src, uint32_t len) {
+    return len == 0u ? 0u : make_piece(src, len).alloc;
+}
 
-    // Issue tensor-stages while a ring slot is free (the consumer is done with every one before
-    // c_q); a block start waits until the consumer is at most one block behind, so a meta slot is
-    // never overwritten while in use.  A slot's previous tensor was read by the whole warp before
-    // this call (__syncwarp after every tensor's decode).  The pieces of a tensor-stage go out in
-    // parallel, one bulk copy per lane (lanes 4 T .. 4 T + 2, and 8 and 9 with a block's first K);
-    // lane 0 first tells the slot's barrier how many bytes to expect.  False when a descriptor
-    // did not arrive in time.
-    __device__ __forceinline__ bool produce(const AttnArgs &a, uint8_t *R, int c_q, int c_fb, int lane) {
-        while (fb < fb1 && q - c_q < C::NSLOT) {
-            const int T = q & 1;
-            if (T == 0 && tile == 0) {
-                if (fb - c_fb >= 2) break;
-                if (!start_block(a, R, lane)) return false;
-            }
-            const int slot = q % C::NSLOT;
-            const uint32_t bar = smem_u32(R + C::W_BAR + 8 * slot);
-            const uint32_t ms = smem_u32(R + C::W_META + (bseq & 1) * C::MSLOT);
-            const int t0 = tile * C::TS;
-            const int n = min(C::TS, valid - t0);
-            const int LT = (lane >> 2) & 1;  // the tensor of lanes 0-7's pieces
-            const int e0 = esc_at(em, LT, t0 >> 4), e1 = esc_at(em, LT, min(16, (t0 + C::TS) >> 4));
-            const bool now = lane < 8 ? LT == T : (T == 0 && tile == 0);
-            const uint8_t *p;
-            uint32_t len;
-            if (kind == 2) {
-                p = src + 4 * e0;
-                len = e1 - e0 <= C::ESC_CAP ? uint32_t(4 * (e1 - e0)) : 0u;
-            } else {
-                p = src + size_t(t0) * stride;
-                len = kind == 1 ? uint32_t(n) * stride : (kind == 3 ? uint32_t(D) : 0u);
-            }
-            if (!now) len = 0u;
-            const uint32_t d = kind == 3 ? ms + dst : smem_u32(R + slot * C::TR) + dst;
-            const Piece pc = make_piece(p, len);
-            const uint32_t bytes = len != 0 ? pc.alloc : 0u;
-            const uint32_t total = __reduce_add_sync(FULL, bytes);
-            fence_proxy_async();
-            if (lane == 0) mbar_arrive_expect_tx(bar, total);
-            __syncwarp();
-            if (bytes != 0) bulk_g2s(d, pc.src, bytes, bar);
-            ++q;
-            if (T == 1) {
-                if (t0 + C::TS >= valid) {
-                    tile = 0;
-                    ++bseq;
-                    ++fb;
-                    fetch(a, R, lane);
-                } else {
-                    ++tile;
-                }
-            }
-        }
-        return true;
-    }
+// The descriptor words the producer needs of one block: bytes 0-31 (K / V addresses, escape
+// record offsets and counts, modes, tokens) and, when a block takes several stages, the escape
+// count headers (bytes 64-127).
+template <bool MULTI> struct PDesc {
+    uint4 w0, w1;
+    uint4 e[MULTI ? 4 : 1];
 };
 
-// One tensor of a stage into the tile, escapes included.
+template <bool MULTI>
+__device__ __forceinline__ void pdesc_load(const BlockDesc *gd, PDesc<MULTI> &d) {
+    const uint4 *p = reinterpret_cast<const uint4 *>(gd);
+    d.w0 = __ldg(p);
+    d.w1 = __ldg(p + 1);
+    if constexpr (MULTI) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) d.e[i] = __ldg(p + 4 + i);
+    }
+}
+
+// Escape count e(i), i = 1..16, of tensor T from a prefetched descriptor (em[T][i - 1]).
+__device__ __forceinline__ int pdesc_esc(const uint4 (&e)[4], int T, int i) {
+    const int w = (i - 1) >> 1;  // u32 word of em[T] holding entry i - 1
+    const uint4 a = T ? e[2] : e[0], b = T ? e[3] : e[1];
+    uint32_t r = a.x;
+    r = w == 1 ? a.y : r;
+    r = w == 2 ? a.z : r;
+    r = w == 3 ? a.w : r;
+    r = w == 4 ? b.x : r;
+    r = w == 5 ? b.y : r;
+    r = w == 6 ? b.z : r;
+    r = w == 7 ? b.w : r;
+    return int((r >> (16 * ((i - 1) & 1))) & 0xFFFFu);
+}
+
+// The producer warp: for every stage of the CTA's blocks, wait until the slot is free, announce
+// the stage's byte count on the slot's full barrier, then issue its copies (lane 0).  Lane l holds
+// the descriptor of block base + l; the next 32 are loaded while the current 32 are issued, so
+// the issuing lane never waits on a global load.  On a timeout it reports DERR_TIMEOUT and waits
+// (bounded) for the copies it issued before it returns.
+template <int D, bool BF16IN>
+__device__ void producer(const AttnArgs &a, uint8_t *smem, int fb0, int fb1, int lane) {
+    using C = Cfg<D>;
+    constexpr bool MULTI = C::TSB < 128;  // a 128-token block takes several stages
+    const uint32_t sb = smem_u32(smem);
+    int gs = 0;  // stages issued
+    bool ok = true;
+    PDesc<MULTI> cur, nxt;
+    if (fb0 + lane < fb1) pdesc_load<MULTI>(a.desc + fb0 + lane, cur);
+    for (int base = fb0; base < fb1 && ok; base += 32) {
+        if (base + 32 + lane < fb1) pdesc_load<MULTI>(a.desc + base + 32 + lane, nxt);
+        const int nb = min(32, fb1 - base);
+        for (int j = 0; j < nb && ok; ++j) {
+            const BlockDesc *gd = a.desc + base + j;
+            const uint64_t kp = (uint64_t(__shfl_sync(FULL, cur.w0.y, j)) << 32) | __shfl_sync(FULL, cur.w0.x, j);
+            const uint64_t vp = (uint64_t(__shfl_sync(FULL, cur.w0.w, j)) << 32) | __shfl_sync(FULL, cur.w0.z, j);
+            const uint32_t krec = __shfl_sync(FULL, cur.w1.x, j), vrec = __shfl_sync(FULL, cur.w1.y, j);
+            const uint32_t nesc = __shfl_sync(FULL, cur.w1.z, j), mw = __shfl_sync(FULL, cur.w1.w, j);
+            const int km = BF16IN ? 0 : int(mw & 0xFFu), vm = BF16IN ? 0 : int((mw >> 8) & 0xFFu);
+            const int n_tok = int((mw >> 16) & 0xFFu), valid = int(mw >> 24);
+            // e(i) of tensor T of this block (uniform i)
+            auto esc_count = [&](int T, int i) -> int {
+                if (i == 0) return 0;
+                if constexpr (MULTI) {
+                    return __shfl_sync(FULL, pdesc_esc(cur.e, T, i), j);
+                } else {
+                    if (16 * i >= n_tok) return int(T ? nesc >> 16 : nesc & 0xFFFFu);
+                    return esc_gd(gd, T, i);  // blocks over 128 tokens: not prefetched
+                }
+            };
+            for (int t0 = 0; t0 < valid; t0 += C::TSB) {
+                const int slot = gs % C::NSLOT;
+                const uint32_t full = ring_bar<D>(sb, slot), empty = ring_bar<D>(sb, C::NSLOT + slot);
+                if (gs >= C::NSLOT &&
+                    !uni(mbar_wait_bounded(empty, uint32_t((gs / C::NSLOT - 1) & 1), kStageWaitUs))) {
+                    if (lane == 0) report(a.status, KVX_ERR_TIMEOUT, DERR_TIMEOUT);
+                    ok = false;
+                    break;
+                }
+                const int n = min(C::TSB, valid - t0);
+                int ea[2] = {0, 0}, eb[2] = {0, 0};
+                if (!BF16IN) {
+#pragma unroll
+                    for (int T = 0; T < 2; ++T) {
+                        ea[T] = esc_count(T, t0 >> 4);
+                        eb[T] = esc_count(T, min(16, (t0 + C::TSB) >> 4));
+                    }
+                }
+                if (lane == 0) {
+                    const uint32_t dslot = sb + uint32_t(slot * C::SLOT);
+                    // the pieces of this stage: [src, len, dst]
+                    const uint8_t *src[9];
+                    uint32_t len[9], dst[9];
+                    int np = 0;
+                    src[np] = reinterpret_cast<const uint8_t *>(gd), len[np] = uint32_t(sizeof(BlockDesc)), dst[np++] = dslot;
+#pragma unroll
+                    for (int T = 0; T < 2; ++T) {
+                        const uint8_t *blk = gptr(T ? vp : kp);
+                        const int mode = T ? vm : km;
+                        const uint32_t reg = dslot + uint32_t(C::S_T + T * C::T_BYTES);
+                        if (BF16IN) {
+                            src[np] = blk + size_t(t0) * 2 * D, len[np] = uint32_t(n * 2 * D), dst[np++] = reg;
+                        } else if (mode == 0) {
+                            src[np] = blk + kHeaderBytes + size_t(t0) * 2 * D, len[np] = uint32_t(n * 2 * D), dst[np++] = reg;
+                        } else {
+                            const uint8_t *rows = blk + kHeaderBytes + D;
+                            src[np] = blk + kHeaderBytes, len[np] = uint32_t(D), dst[np++] = reg + C::B_OFF;
+                            src[np] = rows + size_t(t0) * D, len[np] = uint32_t(n * D), dst[np++] = reg;
+                            src[np] = rows + size_t(n_tok) * D + size_t(t0) * D * mode / 8;
+                            len[np] = uint32_t(n * D * mode / 8), dst[np++] = reg + C::CODE_OFF;
+                            if (eb[T] > ea[T] && eb[T] - ea[T] <= C::ESC_CAP) {
+                                src[np] = reinterpret_cast<const uint8_t *>(a.esc + (T ? vrec : krec) + kEscRecHead + ea[T]);
+                                len[np] = uint32_t(4 * (eb[T] - ea[T])), dst[np++] = reg + C::E_OFF;
+                            }
+                        }
+                    }
+                    uint32_t total = 0;
+                    for (int i = 0; i < np; ++i) total += piece_bytes(src[i], len[i]);
+                    mbar_arrive_expect_tx(full, total);
+                    for (int i = 0; i < np; ++i) stage_piece(dst[i], src[i], len[i], full);
+                }
+                __syncwarp();
+                ++gs;
+            }
+        }
+        cur = nxt;
+    }
+    if (!ok && lane == 0) {
+        // let the copies already issued land before this CTA's shared memory goes away
+        for (int s = max(0, gs - C::NSLOT); s < gs; ++s)
+            mbar_wait_bounded(ring_bar<D>(sb, s % C::NSLOT), uint32_t((s / C::NSLOT) & 1), kStageWaitUs);
+    }
+}
+
+// One tensor of one tile into the warp's BF16 tile, escapes included.  reg: the tensor's region of
+// the slot; g16: the tile's 16-token group in the block; t0: the stage's first token in the block;
+// rows: valid rows of the tile; zero_from: rows at or past it are zeroed.
 template <int D>
-__device__ __forceinline__ void stage_tile(const AttnArgs &a, const BlockDesc &bd, int T, int mode,
-                                           uint32_t tstage, uint32_t xb, const StoreMap<D> &sm, const Lay &ly,
-                                           const uint32_t (&b7)[4], int ia, int ib, int rows,
-                                           int zero_from, int lane) {
-    if (mode == 4) decode_stage<D, 4>(tstage, ly, b7, sm, lane);
-    else if (mode == 2) decode_stage<D, 2>(tstage, ly, b7, sm, lane);
-    else decode_stage<D, 0>(tstage, ly, b7, sm, lane);
-    if (zero_from < Cfg<D>::TS) zero_rows<D>(sm, zero_from, lane);
-    const int e0 = esc_ms(bd, T, ia), e1 = esc_ms(bd, T, ib);
+__device__ __forceinline__ void tile_tensor(const AttnArgs &a, const BlockDesc &bd, int T, int mode,
+                                            uint32_t al, uint32_t reg, int tw, uint32_t xb,
+                                            const StoreMap<D> &sm, int g16, int t0, int rows,
+                                            int zero_from, bool bf16, int lane) {
+    using C = Cfg<D>;
+    const int c8 = lane % C::C8;
+    const uint32_t rd = al & 15u, cd = (al >> 8) & 15u;
+    const Lay ly = make_lay<D>(rd, cd, mode, c8, bf16);
+    const uint32_t rb = reg + uint32_t(TT * tw * (mode == 0 ? 2 * D : D));
+    const uint32_t cb = reg + uint32_t(TT * tw * (D * mode / 8));
+    if (mode != 0) {
+        uint32_t b7[4];
+        load_b7(reg + uint32_t(C::B_OFF) + rd + 8u * uint32_t(c8), b7);
+        if (mode == 4) decode_tile<D, 4>(rb, cb, ly, b7, sm, lane);
+        else decode_tile<D, 2>(rb, cb, ly, b7, sm, lane);
+    } else {
+        const uint32_t b7[4] = {0u, 0u, 0u, 0u};
+        decode_tile<D, 0>(rb, cb, ly, b7, sm, lane);
+    }
+    if (zero_from < TT) zero_rows<D>(sm, zero_from, lane);
+    const int e0 = esc_ms(bd, T, g16), e1 = esc_ms(bd, T, g16 + 1);
     if (e1 > e0) {
-        using C = Cfg<D>;
         const uint32_t rec = T ? bd.v_rec : bd.k_rec;
+        const int ea = esc_ms(bd, T, t0 >> 4), eb = esc_ms(bd, T, min(16, (t0 + C::TSB) >> 4));
         const uint32_t lim = uint32_t(rows) * (2 * D);
         __syncwarp();  // the decoded words are in place before escapes overwrite some
-        if (e1 - e0 <= C::ESC_CAP)  // staged by the producer
-            esc_patch<D>(xb, tstage + C::EE_OFF + esc_rec_line(rec, e0) - 4u * uint32_t(e0), e0, e1, lim, lane);
+        if (eb - ea <= C::ESC_CAP)  // staged by the producer
+            esc_patch<D>(xb, reg + uint32_t(C::E_OFF) + esc_rec_line(rec, ea) - 4u * uint32_t(ea), e0, e1, lim, lane);
         else
             esc_patch_hbm<D>(xb, a.esc + rec + kEscRecHead, e0, e1, lim, lane);
     }
     __syncwarp();
 }
 
-template <int D, bool BF16IN>
-__device__ __forceinline__ void worker(const AttnArgs &a, uint8_t *R, int wk, int fb0, int fb1,
-                                       int lane) {
-    using C = Cfg<D>;
-    const int gi = lane >> 2, tig = lane & 3, c8 = lane % C::C8;
-    uint8_t *ring = R;
-    uint8_t *metas = R + C::W_META;
-    const uint32_t xb = smem_u32(R + C::W_XB);
-    uint8_t *bars = R + C::W_BAR;
-    StoreMap<D> smap;
-    smap.init(xb, lane);
-    if (lane == 0) {
+// Per-warp online-softmax state: lane (g, t) holds queries 2t (m0, l0, acc[m][0 / 2]) and 2t + 1
+// (m1, l1, acc[m][1 / 3]); acc[m][0 / 1] is head dim 16 m + g, acc[m][2 / 3] head dim 16 m + g + 8.
+template <int D> struct SoftState {
+    float acc[Cfg<D>::KS][4];
+    float m0, m1, l0, l1;
+    __device__ __forceinline__ void reset() {
+        m0 = m1 = -INFINITY;
+        l0 = l1 = 0.f;
 #pragma unroll
-        for (int j = 0; j < C::NSLOT; ++j) mbar_init(smem_u32(bars + 8 * j), 1);
-#pragma unroll
-        for (int j = 0; j < C::NDESC; ++j) mbar_init(smem_u32(R + C::W_DBAR + 8 * j), 1);
-        fence_mbar_init();
+        for (int m = 0; m < Cfg<D>::KS; ++m) acc[m][0] = acc[m][1] = acc[m][2] = acc[m][3] = 0.f;
     }
-    __syncwarp();
-    Producer<D, BF16IN> pp;
-    pp.fb = pp.fb0 = pp.pf = pp.dwait = fb0;
-    pp.fb1 = fb1;
-    pp.fetch(a, R, lane);
-    int fb = fb0, tile = 0, cq = 0, bseq = 0;  // cq: the next tensor-stage to consume
-    int seg_begin = fb0;
-    uint32_t flags = 0u, whole = 0u;  // the block's flags; the segment began at its unit's start
-    Lay lk{}, lv{};
-    uint32_t b7k[4] = {0u, 0u, 0u, 0u}, b7v[4] = {0u, 0u, 0u, 0u};
+};
+
+// One 16-token tile of K and V: decode, S = K Q^T, online softmax, decode V, free the slot, O += P V.
+template <int D, bool BF16IN>
+__device__ __forceinline__ void tile_step(const AttnArgs &a, const BlockDesc &bd, uint32_t slot_addr,
+                                          uint32_t empty, uint32_t xb, const StoreMap<D> &sm, int tw,
+                                          int t0, int rows, const uint32_t (&qb)[Cfg<D>::KS][2],
+                                          SoftState<D> &st, int lane) {
+    using C = Cfg<D>;
+    const int gi = lane >> 2;
+    const uint32_t al = *reinterpret_cast<const uint32_t *>(bd.align);
+    const int km = BF16IN ? 0 : bd.k_mode, vm = BF16IN ? 0 : bd.v_mode;
+    const int g16 = (t0 >> 4) + tw;
+    const uint32_t kreg = slot_addr + uint32_t(C::S_T), vreg = kreg + uint32_t(C::T_BYTES);
+
+    // S^T = K Q^T (rows past `rows` hold stale words: their scores are dropped)
+    tile_tensor<D>(a, bd, 0, km, al & 0xFFFFu, kreg, tw, xb, sm, g16, t0, rows, TT, BF16IN, lane);
+    float s[1][4];
+    qk_tiles<D, 1>(xb, qb, lane, s);
+    if (rows < TT) {
+        if (gi >= rows) s[0][0] = s[0][1] = -INFINITY;
+        if (gi + 8 >= rows) s[0][2] = s[0][3] = -INFINITY;
+    }
+
+    // online softmax (src/softmax.hpp:8-14): p = 2^((s - m) log2e); the warp-wide maximum and the
+    // rescale of the accumulators only when some score exceeds the running maximum.  s - m is
+    // formed first, like the reference's expf(s - m), so that huge scores keep the largest weight
+    // at exactly 1.
+    float t0m = fmaxf(s[0][0], s[0][2]), t1m = fmaxf(s[0][1], s[0][3]);
+    const bool grow = __any_sync(FULL, t0m > st.m0 || t1m > st.m1);
+    float mn0 = st.m0, mn1 = st.m1, al0 = 1.0f, al1 = 1.0f;
+    if (grow) {
+#pragma unroll
+        for (int o = 4; o < 32; o <<= 1) {
+            t0m = fmaxf(t0m, __shfl_xor_sync(FULL, t0m, o));
+            t1m = fmaxf(t1m, __shfl_xor_sync(FULL, t1m, o));
+        }
+        mn0 = fmaxf(st.m0, t0m);
+        mn1 = fmaxf(st.m1, t1m);
+        al0 = ex2(__fmul_rn(__fsub_rn(st.m0, mn0), kLog2e));
+        al1 = ex2(__fmul_rn(__fsub_rn(st.m1, mn1), kLog2e));
+    }
+    const float p0 = ex2(__fmul_rn(__fsub_rn(s[0][0], mn0), kLog2e));
+    const float p1 = ex2(__fmul_rn(__fsub_rn(s[0][1], mn1), kLog2e));
+    const float p2 = ex2(__fmul_rn(__fsub_rn(s[0][2], mn0), kLog2e));
+    const float p3 = ex2(__fmul_rn(__fsub_rn(s[0][3], mn1), kLog2e));
+    // P^T B fragments: p = h + m + l exactly, h = bf16(p), m = bf16(p - h), l = bf16(p - h - m)
+    // (each difference is exact in fp32; 3 x 8 significant bits)
+    uint32_t bh[2], bm[2], bl[2];
+    {
+        const uint32_t h01 = pack_bf16x2(p1, p0), h23 = pack_bf16x2(p3, p2);
+        const float r0 = __fsub_rn(p0, bf16lo_to_f32(h01)), r1 = __fsub_rn(p1, bf16hi_to_f32(h01));
+        const float r2 = __fsub_rn(p2, bf16lo_to_f32(h23)), r3 = __fsub_rn(p3, bf16hi_to_f32(h23));
+        const uint32_t m01 = pack_bf16x2(r1, r0), m23 = pack_bf16x2(r3, r2);
+        const float u0 = __fsub_rn(r0, bf16lo_to_f32(m01)), u1 = __fsub_rn(r1, bf16hi_to_f32(m01));
+        const float u2 = __fsub_rn(r2, bf16lo_to_f32(m23)), u3 = __fsub_rn(r3, bf16hi_to_f32(m23));
+        bh[0] = movm_t(h01);
+        bh[1] = movm_t(h23);
+        bm[0] = movm_t(m01);
+        bm[1] = movm_t(m23);
+        bl[0] = movm_t(pack_bf16x2(u1, u0));
+        bl[1] = movm_t(pack_bf16x2(u3, u2));
+    }
+    st.l0 = __fmaf_rn(st.l0, al0, __fadd_rn(p0, p2));
+    st.l1 = __fmaf_rn(st.l1, al1, __fadd_rn(p1, p3));
+    st.m0 = mn0;
+    st.m1 = mn1;
+    if (grow) {
+#pragma unroll
+        for (int m = 0; m < C::KS; ++m) {
+            st.acc[m][0] = __fmul_rn(st.acc[m][0], al0);
+            st.acc[m][1] = __fmul_rn(st.acc[m][1], al1);
+            st.acc[m][2] = __fmul_rn(st.acc[m][2], al0);
+            st.acc[m][3] = __fmul_rn(st.acc[m][3], al1);
+        }
+    }
+
+    // V replaces K in the tile (K was read by the MMAs above: ldmatrix is warp-synchronous);
+    // rows past `rows` are zeroed (P is 0 there and V must be finite)
+    tile_tensor<D>(a, bd, 1, vm, al >> 16, vreg, tw, xb, sm, g16, t0, rows, rows, BF16IN, lane);
+    if (lane == 0) mbar_arrive(empty);  // this warp has read everything it needs from the slot
+    pv_tile<D>(xb, 0, bh, bm, bl, lane, st.acc);
+    __syncwarp();  // every lane is done with the tile before the next decode writes it
+}
+
+// The warp's state for one unit segment goes to partial state `idx` (m, l summed over the lanes
+// of each query, acc).
+template <int D>
+__device__ __forceinline__ void flush_state(const AttnArgs &a, size_t idx, const SoftState<D> &st, int lane) {
+    const int gi = lane >> 2, tig = lane & 3;
+    float lt0 = st.l0, lt1 = st.l1;
+#pragma unroll
+    for (int o = 4; o < 32; o <<= 1) {
+        lt0 = __fadd_rn(lt0, __shfl_xor_sync(FULL, lt0, o));
+        lt1 = __fadd_rn(lt1, __shfl_xor_sync(FULL, lt1, o));
+    }
+    float *part = a.partials + idx * size_t(partial_stride(D));
+    const int qa = 2 * tig, qc = 2 * tig + 1;
+    if (gi == 0) {
+        part[qa] = st.m0;
+        part[qc] = st.m1;
+        part[8 + qa] = lt0;
+        part[8 + qc] = lt1;
+    }
+    float *oa = part + 16 + qa * D + gi;
+    float *oc = part + 16 + qc * D + gi;
+#pragma unroll
+    for (int m = 0; m < Cfg<D>::KS; ++m) {
+        oa[16 * m] = st.acc[m][0];
+        oa[16 * m + 8] = st.acc[m][2];
+        oc[16 * m] = st.acc[m][1];
+        oc[16 * m + 8] = st.acc[m][3];
+    }
+}
+
+// A consumer warp: visits every stage of the CTA's range in order, takes the tiles dealt to it,
+// arrives once per stage on the slot's empty barrier, and writes its state at every segment end
+// (the unit's last block, or the end of the range).
+template <int D, bool BF16IN>
+__device__ void consumer(const AttnArgs &a, uint8_t *smem, int w, int lane, int fb0, int fb1, int row0) {
+    using C = Cfg<D>;
+    const uint32_t sb = smem_u32(smem);
+    const uint32_t xb = sb + uint32_t(C::O_TILE + w * C::TILE);
+    StoreMap<D> sm;
+    sm.init(xb, lane);
     uint32_t qb[C::KS][2];
-    float acc[C::KS][4];
-    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
-
-    // Tensor-stage q's slot barrier and its phase for that use.
-    auto slot_bar = [&](int q) { return smem_u32(bars + 8 * (q % C::NSLOT)); };
-    auto slot_par = [&](int q) { return uint32_t((q / C::NSLOT) & 1); };
-    // After a timeout: report it and let the copies already issued land before this CTA's
-    // shared memory goes away.
-    auto fail = [&]() {
-        if (lane == 0) report(a.status, KVX_ERR_TIMEOUT, DERR_TIMEOUT);
-        for (int q = cq; q < pp.q; ++q) mbar_wait_bounded(slot_bar(q), slot_par(q), kStageWaitUs);
-        for (int b = pp.dwait; b < pp.pf; ++b)
-            mbar_wait_bounded(smem_u32(R + C::W_DBAR + 8 * ((b - fb0) % C::NDESC)),
-                              ((b - fb0) / C::NDESC) & 1, kStageWaitUs);
-    };
-
-    while (fb < fb1) {
-        if (!pp.produce(a, R, cq, fb, lane) || !uni(mbar_wait_bounded(slot_bar(cq), slot_par(cq), kStageWaitUs))) {
-            fail();
-            return;
-        }
-        __syncwarp();
-        const uint8_t *ms = metas + (bseq & 1) * C::MSLOT;
-        const BlockDesc &bd =
-            *reinterpret_cast<const BlockDesc *>(R + C::W_DESC + ((fb - fb0) % C::NDESC) * int(sizeof(BlockDesc)));
-        const int kmode = BF16IN ? 0 : bd.k_mode, vmode = BF16IN ? 0 : bd.v_mode;
-        const int valid = bd.valid;
-        if (tile == 0) {
-            const uint32_t al = *reinterpret_cast<const uint32_t *>(bd.align);
-            flags = bd.flags;
-            const uint32_t kd = al & 15u, kc = (al >> 8) & 15u, vd = (al >> 16) & 15u, vc = (al >> 24) & 15u;
-            lk = make_lay<D>(kd, kc, kmode, c8, BF16IN);
-            lv = make_lay<D>(vd, vc, vmode, c8, BF16IN);
-            if (kmode != 0) load_b7(smem_u32(ms) + kd + 8 * c8, b7k);
-            if (vmode != 0) load_b7(smem_u32(ms) + C::BASE + vd + 8 * c8, b7v);
-            if (fb == seg_begin) {
+    SoftState<D> st;
+    st.reset();
+    int row = row0;
+    int gs = 0;   // stages consumed
+    int tw = w;   // this warp's tile in stage gs: (w - gs TPS) mod NW (none when >= TPS)
+    for (int b = fb0; b < fb1; ++b) {
+        for (int t0 = 0;; t0 += C::TSB) {
+            const int slot = gs % C::NSLOT;
+            const uint32_t full = ring_bar<D>(sb, slot), empty = ring_bar<D>(sb, C::NSLOT + slot);
+            if (!uni(mbar_wait_bounded(full, uint32_t((gs / C::NSLOT) & 1), kStageWaitUs))) {
+                if (lane == 0) report(a.status, KVX_ERR_TIMEOUT, DERR_TIMEOUT);
+                return;
+            }
+            const uint8_t *sp = smem + slot * C::SLOT;
+            const BlockDesc &bd = *reinterpret_cast<const BlockDesc *>(sp);
+            const int valid = bd.valid;
+            const uint32_t flags = bd.flags;
+            if (t0 == 0 && (b == fb0 || (flags & kDescFirst) != 0u)) {
                 const UnitDev *U = a.units + bd.unit;
-                whole = flags & kDescFirst;
                 load_q<D>(U->q, U->n_q, U->q_stride, qb, lane);
-                m0 = m1 = -INFINITY;
-                l0 = l1 = 0.f;
-#pragma unroll
-                for (int m = 0; m < C::KS; ++m) acc[m][0] = acc[m][1] = acc[m][2] = acc[m][3] = 0.f;
+                st.reset();
             }
-        }
-        const uint32_t kst = smem_u32(ring + (cq % C::NSLOT) * C::TR);
-        const uint32_t vst = smem_u32(ring + ((cq + 1) % C::NSLOT) * C::TR);
-        const int t0 = tile * C::TS;
-        const int rows = min(C::TS, valid - t0);
-        const bool last_tile = t0 + C::TS >= valid;
-        const bool seg_end = last_tile && (fb + 1 == fb1 || (flags & kDescLast) != 0u);
-        const int ia = t0 >> 4, ib = min(16, (t0 + C::TS) >> 4);
-
-        // S^T = K Q^T for every tile of the stage
-        stage_tile<D>(a, bd, 0, kmode, kst, xb, smap, lk, b7k, ia, ib, rows, C::TS, lane);
-        ++cq;  // K's slot is free: the next copies can go out while the tensor cores work
-        if (!pp.produce(a, R, cq, fb, lane)) {
-            fail();
-            return;
-        }
-        // (a stage's rows past `rows` hold stale words: their scores are dropped below)
-        float s[C::SUBS][4];
-        qk_tiles<D, C::SUBS>(xb, qb, lane, s);
-        if (rows < C::TS) {
-#pragma unroll
-            for (int sub = 0; sub < C::SUBS; ++sub) {
-                const int rr = rows - sub * TT;
-                if (gi >= rr) s[sub][0] = s[sub][1] = -INFINITY;
-                if (gi + 8 >= rr) s[sub][2] = s[sub][3] = -INFINITY;
-            }
-        }
-
-        // online softmax over the stage's tokens; p = 2^(s log2e - m log2e).  The warp-wide
-        // maximum is only taken when some score exceeds the running one; otherwise m stays and
-        // the accumulators are not rescaled (alpha is exactly 1).
-        float t0m = fmaxf(s[0][0], s[0][2]), t1m = fmaxf(s[0][1], s[0][3]);
-#pragma unroll
-        for (int sub = 1; sub < C::SUBS; ++sub) {
-            t0m = fmaxf(t0m, fmaxf(s[sub][0], s[sub][2]));
-            t1m = fmaxf(t1m, fmaxf(s[sub][1], s[sub][3]));
-        }
-        const bool grow = __any_sync(FULL, t0m > m0 || t1m > m1);
-        float mn0 = m0, mn1 = m1, al0 = 1.0f, al1 = 1.0f;
-        if (grow) {
-#pragma unroll
-            for (int o = 4; o < 32; o <<= 1) {
-                t0m = fmaxf(t0m, __shfl_xor_sync(FULL, t0m, o));
-                t1m = fmaxf(t1m, __shfl_xor_sync(FULL, t1m, o));
-            }
-            mn0 = fmaxf(m0, t0m);
-            mn1 = fmaxf(m1, t1m);
-            al0 = ex2(__fmaf_rn(m0, kLog2e, -__fmul_rn(mn0, kLog2e)));
-            al1 = ex2(__fmaf_rn(m1, kLog2e, -__fmul_rn(mn1, kLog2e)));
-        }
-        const float ml0 = __fmul_rn(mn0, kLog2e), ml1 = __fmul_rn(mn1, kLog2e);
-        float ps0 = 0.f, ps1 = 0.f;
-        uint32_t bh[C::SUBS][2], bm[C::SUBS][2], bl[C::SUBS][2];
-#pragma unroll
-        for (int sub = 0; sub < C::SUBS; ++sub) {
-            const float p0 = ex2(__fmaf_rn(s[sub][0], kLog2e, -ml0)), p1 = ex2(__fmaf_rn(s[sub][1], kLog2e, -ml1));
-            const float p2 = ex2(__fmaf_rn(s[sub][2], kLog2e, -ml0)), p3 = ex2(__fmaf_rn(s[sub][3], kLog2e, -ml1));
-            ps0 = __fadd_rn(ps0, __fadd_rn(p0, p2));
-            ps1 = __fadd_rn(ps1, __fadd_rn(p1, p3));
-            // P^T B fragments: p = h + m + l exactly, h = bf16(p), m = bf16(p - h),
-            // l = bf16(p - h - m) (each difference is exact in fp32; 3 x 8 significant bits)
-            const uint32_t h01 = pack_bf16x2(p1, p0), h23 = pack_bf16x2(p3, p2);
-            const float r0 = __fsub_rn(p0, bf16lo_to_f32(h01)), r1 = __fsub_rn(p1, bf16hi_to_f32(h01));
-            const float r2 = __fsub_rn(p2, bf16lo_to_f32(h23)), r3 = __fsub_rn(p3, bf16hi_to_f32(h23));
-            const uint32_t m01 = pack_bf16x2(r1, r0), m23 = pack_bf16x2(r3, r2);
-            const float u0 = __fsub_rn(r0, bf16lo_to_f32(m01)), u1 = __fsub_rn(r1, bf16hi_to_f32(m01));
-            const float u2 = __fsub_rn(r2, bf16lo_to_f32(m23)), u3 = __fsub_rn(r3, bf16hi_to_f32(m23));
-            bh[sub][0] = movm_t(h01);
-            bh[sub][1] = movm_t(h23);
-            bm[sub][0] = movm_t(m01);
-            bm[sub][1] = movm_t(m23);
-            bl[sub][0] = movm_t(pack_bf16x2(u1, u0));
-            bl[sub][1] = movm_t(pack_bf16x2(u3, u2));
-        }
-        l0 = __fmaf_rn(l0, al0, ps0);
-        l1 = __fmaf_rn(l1, al1, ps1);
-        m0 = mn0;
-        m1 = mn1;
-        if (grow) {
-#pragma unroll
-            for (int m = 0; m < C::KS; ++m) {
-                acc[m][0] = __fmul_rn(acc[m][0], al0);
-                acc[m][1] = __fmul_rn(acc[m][1], al1);
-                acc[m][2] = __fmul_rn(acc[m][2], al0);
-                acc[m][3] = __fmul_rn(acc[m][3], al1);
-            }
-        }
-
-        // O^T += V^T P^T for every tile of the stage (the tile's K reads are done: stage_tile
-        // ends with __syncwarp, and the K tiles were read before the softmax)
-        if (!uni(mbar_wait_bounded(slot_bar(cq), slot_par(cq), kStageWaitUs))) {
-            fail();
-            return;
-        }
-        __syncwarp();
-        stage_tile<D>(a, bd, 1, vmode, vst, xb, smap, lv, b7v, ia, ib, rows, rows, lane);
-        ++cq;
-#pragma unroll
-        for (int sub = 0; sub < C::SUBS; ++sub)
-            if (sub * TT < rows) pv_tile<D>(xb, sub * TT, bh[sub], bm[sub], bl[sub], lane, acc);
-
-        if (seg_end) {
-            float lt0 = l0, lt1 = l1;
-#pragma unroll
-            for (int o = 4; o < 32; o <<= 1) {
-                lt0 = __fadd_rn(lt0, __shfl_xor_sync(FULL, lt0, o));
-                lt1 = __fadd_rn(lt1, __shfl_xor_sync(FULL, lt1, o));
-            }
-            const int qa = 2 * tig, qc = 2 * tig + 1;
-            // acc[m][0 / 1]: dim 16 m + g of queries qa / qc; acc[m][2 / 3]: dim 16 m + g + 8
-            if (whole != 0u && (flags & kDescLast) != 0u) {
-                const UnitDev *U = a.units + bd.unit;
-                const int n_q = U->n_q, stride = U->q_stride;
-                float *out = U->out;
-                float *lse = U->lse;
-                const float inv0 = __frcp_rn(lt0), inv1 = __frcp_rn(lt1);
-                if (lse != nullptr && gi == 0) {
-                    if (qa < n_q) lse[qa] = m0 + logf(lt0);
-                    if (qc < n_q) lse[qc] = m1 + logf(lt1);
-                }
-                if (qa < n_q) {
-                    float *o = out + size_t(qa) * stride + gi;
-#pragma unroll
-                    for (int m = 0; m < C::KS; ++m) {
-                        o[16 * m] = __fmul_rn(acc[m][0], inv0);
-                        o[16 * m + 8] = __fmul_rn(acc[m][2], inv0);
-                    }
-                }
-                if (qc < n_q) {
-                    float *o = out + size_t(qc) * stride + gi;
-#pragma unroll
-                    for (int m = 0; m < C::KS; ++m) {
-                        o[16 * m] = __fmul_rn(acc[m][1], inv1);
-                        o[16 * m + 8] = __fmul_rn(acc[m][3], inv1);
-                    }
-                }
+            const bool last = t0 + C::TSB >= valid;
+            const bool seg_end = last && ((flags & kDescLast) != 0u || b + 1 == fb1);
+            const int rows = valid - t0 - TT * tw;
+            if (tw < C::TPS && rows > 0) {
+                tile_step<D, BF16IN>(a, bd, smem_u32(sp), empty, xb, sm, tw, t0, min(rows, TT), qb, st, lane);
             } else {
-                const int ps = (seg_begin == fb0) ? 0 : 1;
-                float *part = a.partials + (size_t(wk) * 2 + ps) * partial_stride(D);
-                if (gi == 0) {
-                    part[qa] = m0;
-                    part[qc] = m1;
-                    part[8 + qa] = lt0;
-                    part[8 + qc] = lt1;
-                }
-                float *oa = part + 16 + qa * D + gi;
-                float *oc = part + 16 + qc * D + gi;
-#pragma unroll
-                for (int m = 0; m < C::KS; ++m) {
-                    oa[16 * m] = acc[m][0];
-                    oa[16 * m + 8] = acc[m][2];
-                    oc[16 * m] = acc[m][1];
-                    oc[16 * m + 8] = acc[m][3];
-                }
+                __syncwarp();  // every lane has read the descriptor
+                if (lane == 0) mbar_arrive(empty);
             }
-        }
-        __syncwarp();  // every lane is done with this ring slot and the tile before they are reused
-        if (last_tile) {
-            tile = 0;
-            ++bseq;
-            if (seg_end) seg_begin = fb + 1;
-            ++fb;
-        } else {
-            ++tile;
+            if (seg_end) {
+                flush_state<D>(a, size_t(row) * C::NW + size_t(w), st, lane);
+                ++row;
+            }
+            ++gs;
+            tw -= C::TPS;
+            if (tw < 0) tw += C::NW;
+            if (last) break;
         }
     }
 }
 
 template <int D, bool BF16IN>
-__global__ void __launch_bounds__(32 * Cfg<D>::WARPS, 1) attn_kernel(const AttnArgs a) {
+__global__ void __launch_bounds__(Cfg<D>::THREADS, 1) attn_kernel(const AttnArgs a) {
     using C = Cfg<D>;
     extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ int skip;
     // Launched as a programmatic dependent of the kernel before it in the stream (the previous
     // step's combine pass, or the plan's descriptor build): nothing is read before that grid has
     // completed and its writes are visible.  Only the launch itself overlaps it.
@@ -872,30 +820,44 @@ __global__ void __launch_bounds__(32 * Cfg<D>::WARPS, 1) attn_kernel(const AttnA
     // A combine pass launched behind this grid (programmatic dependent launch) may start placing
     // its CTAs as soon as SMs free up; it waits for this grid's completion before reading.
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    // consecutive workers on different SMs: neighbouring ranges often share a cost profile
-    const int wk = warp * gridDim.x + blockIdx.x;
-    if (wk >= a.n_workers) return;
-    // a step whose preparation reported an error (its escape records are incomplete) runs no work
-    if (*reinterpret_cast<volatile const int *>(a.status) != 0) return;
-    const int fb0 = int(a.range_begin[wk]), fb1 = int(a.range_begin[wk + 1]);
+    const int c = blockIdx.x;
+    if (c >= a.n_ranges) return;
+    const int fb0 = int(a.range_begin[c]), fb1 = int(a.range_begin[c + 1]);
     if (fb0 >= fb1) return;
-    worker<D, BF16IN>(a, smem + warp * C::WARP_BYTES, wk, fb0, fb1, lane);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        const uint32_t sb = smem_u32(smem);
+        for (int j = 0; j < C::NSLOT; ++j) {
+            mbar_init(ring_bar<D>(sb, j), 1);               // full: the producer's arrive + bytes
+            mbar_init(ring_bar<D>(sb, C::NSLOT + j), C::NW);  // empty: one arrive per consumer warp
+        }
+        fence_mbar_init();
+        // a step whose preparation reported an error (its escape records are incomplete) runs no work
+        skip = *reinterpret_cast<volatile const int *>(a.status);
+    }
+    __syncthreads();
+    if (skip != 0) return;
+    if (warp == C::NW) {
+        producer<D, BF16IN>(a, smem, fb0, fb1, lane);
+        return;
+    }
+    consumer<D, BF16IN>(a, smem, warp, lane, fb0, fb1, a.seg_base[c]);
 }
 
 // ---- combine ------------------------------------------------------------------------------------
 
-// Combine the partial states of one query of a split unit: with M = max m_t over the unit's
-// segments, l = sum l_t e^(m_t - M) and acc = sum acc_t e^(m_t - M) (merge_state's arithmetic,
-// src/softmax.hpp:16-30, applied to all segments at once instead of a left fold), then
+// Combine the partial states of one query of a unit: with M = max m_t over the unit's states,
+// l = sum l_t e^(m_t - M) and acc = sum acc_t e^(m_t - M) (merge_state's arithmetic,
+// src/softmax.hpp:16-30, applied to all states at once instead of a left fold), then
 // out = acc * (1 / l) like finalize_state (src/softmax.hpp:32-41).  One CTA per (unit, query);
-// the sums run over fixed slices of the segments, so the result is deterministic.
+// the sums run over fixed slices of the states, so the result is deterministic.  A state of a
+// warp that saw none of the unit's tokens has m = -inf and l = 0 and adds nothing.
 constexpr int kCombineThreads = 256;
 constexpr int kMaxSegments = 4096;
 
 template <int D>
 __global__ void __launch_bounds__(kCombineThreads) combine_kernel(const CombineArgs a) {
-    constexpr int S = kCombineThreads / D;  // segment slices summed in parallel
+    constexpr int S = kCombineThreads / D;  // state slices summed in parallel
     constexpr int PRE = 8;                  // accumulator values a thread loads up front
     __shared__ float e[kMaxSegments];
     __shared__ float lw[kMaxSegments];
@@ -908,15 +870,9 @@ __global__ void __launch_bounds__(kCombineThreads) combine_kernel(const CombineA
     const SplitUnit sp = a.split[blockIdx.x];
     const int g = blockIdx.y;
     if (g >= sp.n_q) return;
-    const int t0 = sp.first_worker;  // first worker of the unit and the number of workers
-    const int nt = min(sp.n_workers, kMaxSegments);
+    const int nt = min(sp.n_states, kMaxSegments);
     const int ps = partial_stride(D);
-    // only the unit's first worker can hold it in its second partial slot (its range began in an
-    // earlier unit); the host worked that out
-    auto part = [&](int i) {
-        const int t = t0 + i;
-        return a.partials + (size_t(t) * 2 + (i == 0 ? sp.first_slot : 0)) * ps;
-    };
+    auto part = [&](int i) { return a.partials + (size_t(sp.first_state) + size_t(i)) * ps; };
     const int tid = threadIdx.x;
     const int d = tid % D, sl = tid / D;
     // every load that does not depend on M goes out first: (m, l) of the segments and the first
@@ -1015,19 +971,20 @@ __global__ void fold_kernel(const float *__restrict__ parts, int n_parts, int n_
 // earlier model did, starved the workers that hold escape-dense blocks and left the others
 // about 10 % more work than a balanced split.)
 __device__ __forceinline__ uint64_t mode_cost(int mode) { return mode == 4 ? 4u : (mode == 2 ? 5u : 2u); }
-__device__ __forceinline__ uint64_t block_cost(const FlatBlock &b) {
+__device__ __forceinline__ uint64_t block_cost(const FlatBlock &b, bool by_tokens) {
+    if (by_tokens) return uint64_t(b.valid);
     return uint64_t(b.valid) * (mode_cost(b.k_mode) + mode_cost(b.v_mode)) + uint64_t(b.k_nesc) + b.v_nesc;
 }
 
-// One CTA: range_begin[w] = first block whose cost prefix reaches w * total / n_workers.
+// One CTA: range_begin[w] = first block whose cost prefix reaches w * total / nw.
 __global__ void __launch_bounds__(1024) split_kernel(const FlatBlock *flat, int64_t n, int nw,
-                                                     int64_t *range_begin) {
+                                                     bool by_tokens, int64_t *range_begin) {
     __shared__ unsigned long long part[1024];
     const int t = threadIdx.x, T = blockDim.x;
     const int64_t chunk = (n + T - 1) / T;
     const int64_t lo = min(n, t * chunk), hi = min(n, lo + chunk);
     unsigned long long sum = 0;
-    for (int64_t b = lo; b < hi; ++b) sum += block_cost(load_flat(flat, b));
+    for (int64_t b = lo; b < hi; ++b) sum += block_cost(load_flat(flat, b), by_tokens);
     part[t] = sum;
     __syncthreads();
     for (int o = 1; o < T; o <<= 1) {  // inclusive scan
@@ -1046,7 +1003,7 @@ __global__ void __launch_bounds__(1024) split_kernel(const FlatBlock *flat, int6
     // worker w starts after the block whose cost interval (c, c + cost] holds w * total / nw
     int w = int(c * uint64_t(nw) / (total ? total : 1));
     for (int64_t b = lo; b < hi; ++b) {
-        const unsigned long long cn = c + block_cost(load_flat(flat, b));
+        const unsigned long long cn = c + block_cost(load_flat(flat, b), by_tokens);
         while (w < nw && uint64_t(w) * total / nw <= c) ++w;
         while (w < nw && uint64_t(w) * total / nw <= cn) range_begin[w++] = b + 1;
         c = cn;
@@ -1059,11 +1016,9 @@ template <int D> void configure(bool bf16) {
     static bool done[2] = {false, false};
     if (done[bf16]) return;
     if (bf16)
-        cudaFuncSetAttribute(attn_kernel<D, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             Cfg<D>::WARP_BYTES * Cfg<D>::WARPS);
+        cudaFuncSetAttribute(attn_kernel<D, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<D>::SMEM);
     else
-        cudaFuncSetAttribute(attn_kernel<D, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             Cfg<D>::WARP_BYTES * Cfg<D>::WARPS);
+        cudaFuncSetAttribute(attn_kernel<D, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<D>::SMEM);
     done[bf16] = true;
 }
 
@@ -1111,8 +1066,8 @@ cudaError_t launch_d(bool bf16, const AttnArgs &a, int grid, cudaStream_t s) {
     // stream drains (the kernel waits for that grid before it reads anything)
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
-    cfg.blockDim = dim3(32 * Cfg<D>::WARPS);
-    cfg.dynamicSmemBytes = size_t(Cfg<D>::WARP_BYTES) * Cfg<D>::WARPS;
+    cfg.blockDim = dim3(Cfg<D>::THREADS);
+    cfg.dynamicSmemBytes = size_t(Cfg<D>::SMEM);
     cfg.stream = s;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -1129,22 +1084,12 @@ bool attention_dim_supported(int dim) {
     return dim == 32 || dim == 64 || dim == 128 || dim == 256;
 }
 
-int attention_workers_per_cta(int dim) {
-    switch (dim) {
-    case 32: return Cfg<32>::WARPS;
-    case 64: return Cfg<64>::WARPS;
-    case 128: return Cfg<128>::WARPS;
-    case 256: return Cfg<256>::WARPS;
-    default: return 0;
-    }
-}
-
 size_t attention_smem_bytes(int dim) {
     switch (dim) {
-    case 32: return size_t(Cfg<32>::WARP_BYTES) * Cfg<32>::WARPS;
-    case 64: return size_t(Cfg<64>::WARP_BYTES) * Cfg<64>::WARPS;
-    case 128: return size_t(Cfg<128>::WARP_BYTES) * Cfg<128>::WARPS;
-    case 256: return size_t(Cfg<256>::WARP_BYTES) * Cfg<256>::WARPS;
+    case 32: return size_t(Cfg<32>::SMEM);
+    case 64: return size_t(Cfg<64>::SMEM);
+    case 128: return size_t(Cfg<128>::SMEM);
+    case 256: return size_t(Cfg<256>::SMEM);
     default: return 0;
     }
 }
@@ -1159,9 +1104,9 @@ cudaError_t launch_attention(int dim, bool bf16_input, const AttnArgs &a, int gr
     }
 }
 
-cudaError_t launch_split(const FlatBlock *flat, int64_t n_blocks, int n_workers, int64_t *range_begin,
-                         cudaStream_t s) {
-    split_kernel<<<1, 1024, 0, s>>>(flat, n_blocks, n_workers, range_begin);
+cudaError_t launch_split(const FlatBlock *flat, int64_t n_blocks, int n_ranges, bool by_tokens,
+                         int64_t *range_begin, cudaStream_t s) {
+    split_kernel<<<1, 1024, 0, s>>>(flat, n_blocks, n_ranges, by_tokens, range_begin);
     return cudaGetLastError();
 }
 

@@ -38,21 +38,23 @@ static_assert(sizeof(FlatBlock) == 32, "FlatBlock is 32 bytes");
 // without escapes have none.
 constexpr int kEscRecHead = 16;
 
-#ifndef KVX_TS64
-#define KVX_TS64 32
-#endif
-// Tokens per stage of the attention kernel (a multiple of 16).
-__host__ __device__ constexpr int stage_tokens(int dim) { return dim <= 64 ? KVX_TS64 : 16; }
+// Tokens of one MMA tile of the attention kernel: each consumer warp decodes 16-token tiles of
+// K and V into its BF16 tile and runs them through the tensor cores.
+constexpr int kTileTokens = 16;
 
-// Byte of element (token r of a stage, channel c) in the attention kernel's BF16 tile of the
-// stage: rows of 2 dim bytes, 16-byte chunks XOR-swizzled by the row (chunk c / 8 of row r sits
-// at chunk position (c / 8) ^ (r & 7), or ^ ((r / 2) & 3) for dim 32).  The same for K and V.
+// Byte of element (token r of a 16-token tile, channel c) in the attention kernel's BF16 tile:
+// rows of 2 dim bytes, 16-byte chunks XOR-swizzled by the row (chunk c / 8 of row r sits at chunk
+// position (c / 8) ^ (r & 7), or ^ ((r / 2) & 3) for dim 32).  The same for K and V.
 __host__ __device__ inline uint32_t esc_scratch_slot(int dim, int T, int r, int c) {
     (void)T;
     const int c8 = c >> 3;
     const int sw = dim == 32 ? (r >> 1) & 3 : r & 7;
     return uint32_t(r * 2 * dim + ((c8 ^ sw) << 4) + 2 * (c & 7));
 }
+
+// Consumer warps per CTA of the attention kernel (one CTA per SM; one more warp issues the copies,
+// so a CTA is 16 warps at 128 registers a thread, or 8 warps at 255 for dim 256).
+__host__ __device__ constexpr int attention_consumer_warps(int dim) { return dim >= 256 ? 7 : 15; }
 
 __device__ __forceinline__ FlatBlock load_flat(const FlatBlock *f, int64_t i) {
     const uint4 a = __ldg(reinterpret_cast<const uint4 *>(f + i));
@@ -111,42 +113,53 @@ struct AttnArgs {
     const FlatBlock *flat;      // [n_blocks]
     const BlockDesc *desc;      // [n_blocks]
     const uint32_t *esc;        // escape records (FlatBlock::k_rec / v_rec index it)
-    const int64_t *range_begin; // [n_workers + 1] flat-block range of each worker warp
-    float *partials;            // [n_workers][2][8 + 8 + 8 * dim]
+    const int64_t *range_begin; // [n_ranges + 1] flat-block range of each CTA
+    const int32_t *seg_base;    // [n_ranges] first partial-state row of each CTA
+    float *partials;            // [rows][consumer warps][partial_stride(dim)]
     int *status;                // [2] first error (code, detail)
-    int n_workers;
+    int n_ranges;
 };
 
-// A unit whose blocks span several workers, as the combine pass needs it (host-built, so the
-// kernel's first load is all it needs): where its outputs go, its queries, its first worker, how
-// many workers hold its segments, and the partial slot of the first (1 when that worker's range
-// began in an earlier unit).
+// A unit as the combine pass sees it (host-built, so the kernel's first load is all it needs):
+// where its outputs go and the contiguous run of partial states [first_state, first_state +
+// n_states) that its blocks left (one per consumer warp of every CTA that held some of them).
 struct SplitUnit {
     float *out;
     float *lse;
-    int32_t first_worker, n_workers, first_slot, n_q, q_stride, pad;
+    int32_t first_state, n_states, n_q, q_stride, pad0, pad1;
 };
 static_assert(sizeof(SplitUnit) == 40, "SplitUnit is 40 bytes");
 
 struct CombineArgs {
-    const UnitDev *units;
-    const SplitUnit *split;       // the units whose blocks span several workers
-    const int64_t *range_begin;    // [n_workers + 1]
+    const SplitUnit *split;
     const float *partials;
-    int n_workers;
 };
 
-// Partial-state stride (floats) for one (worker, slot): m[8], l[8], acc[8][dim].
+// Partial-state stride (floats) of one consumer warp's segment: m[8], l[8], acc[8][dim].
 __host__ __device__ inline int partial_stride(int dim) { return 16 + 8 * dim; }
 
-// Worker that owns flat block b: the last worker whose range starts at or before b.
-__host__ __device__ inline int worker_of_block(const int64_t *range_begin, int n_workers, int64_t b) {
-    int lo = 0, hi = n_workers - 1;
-    while (lo < hi) {
-        int mid = (lo + hi + 1) >> 1;
-        if (range_begin[mid] <= b) lo = mid; else hi = mid - 1;
+// Partial-state rows of a step: every CTA writes one row (all its consumer warps) per unit segment
+// in its block range, rows numbered CTA by CTA; a unit's rows are therefore contiguous.  From the
+// CTA ranges and the units' flat block ranges (in flat order): seg_base[c] = first row of CTA c,
+// and per unit its first row and row count.  Returns the number of rows.
+inline int64_t segment_rows(const int64_t *range_begin, int n_ranges, const int64_t *unit_begin,
+                            const int32_t *unit_blocks, int n_units, int32_t *seg_base,
+                            int32_t *unit_first_row, int32_t *unit_rows) {
+    int64_t row = 0;
+    int u = 0;
+    for (int i = 0; i < n_units; ++i) unit_rows[i] = 0;
+    for (int c = 0; c < n_ranges; ++c) {
+        seg_base[c] = int32_t(row);
+        int64_t b = range_begin[c];
+        const int64_t e = range_begin[c + 1];
+        while (b < e) {
+            while (u < n_units && unit_begin[u] + unit_blocks[u] <= b) ++u;
+            if (unit_rows[u]++ == 0) unit_first_row[u] = int32_t(row);
+            ++row;
+            b = unit_begin[u] + unit_blocks[u] < e ? unit_begin[u] + unit_blocks[u] : e;
+        }
     }
-    return lo;
+    return row;
 }
 
 // Launchers (attention.cu).  Return cudaError_t of the launch.
@@ -165,10 +178,11 @@ cudaError_t launch_esc_layout(FlatBlock *flat, int64_t n_blocks, unsigned long l
                               unsigned long long cap, int *status, cudaStream_t s);
 cudaError_t launch_esc_fill(const UnitDev *units, const FlatBlock *flat, int64_t n_blocks, int dim,
                             uint32_t *esc, unsigned long long cap, int *status, cudaStream_t s);
-// Cost-balanced worker ranges over the flat block list: range_begin[0..n_workers].
-cudaError_t launch_split(const FlatBlock *flat, int64_t n_blocks, int n_workers, int64_t *range_begin,
-                         cudaStream_t s);
-int attention_workers_per_cta(int dim);
+// Cost-balanced CTA ranges over the flat block list: range_begin[0..n_ranges].  by_tokens: every
+// attended token costs the same whatever the block's encoding (the split then depends only on
+// the token counts, so an XKV step and a BF16 step over the same tokens get the same ranges).
+cudaError_t launch_split(const FlatBlock *flat, int64_t n_blocks, int n_ranges, bool by_tokens,
+                         int64_t *range_begin, cudaStream_t s);
 size_t attention_smem_bytes(int dim);
 bool attention_dim_supported(int dim);
 

@@ -627,7 +627,7 @@ __global__ void esc_fill_kernel(const UnitDev *units, const FlatBlock *flat, int
     for (int i = lane; i < m; i += 32) {
         const uint32_t el = pos[i];
         const uint32_t word = uint32_t(words16[2 * i]) | (uint32_t(words16[2 * i + 1]) << 8);
-        pos[i] = esc_scratch_slot(dim, T, int(el / uint32_t(dim)) % stage_tokens(dim), int(el % uint32_t(dim))) |
+        pos[i] = esc_scratch_slot(dim, T, int(el / uint32_t(dim)) % kTileTokens, int(el % uint32_t(dim))) |
                  (word << 16);
     }
 }

@@ -204,16 +204,19 @@ def run_model_heads(kvx, m: ModelHeads, dim: int, how: str) -> np.ndarray:
 def model_heads(kvx, dump: Dump, qs: QSnap, seq: int, reps: int = 5) -> dict:
     """Run the scope at one length.  Per unit, the XKV and raw outputs agree bit for bit (the
     reference's check, src/bench.cpp:688-690); the batched call, whose split of the work over the
-    GPU differs, agrees within 1e-4 relative.  Returns best-of-`reps` timings."""
+    GPU differs, agrees per unit within 1e-4 of the unit's largest output magnitude (fp32 summation
+    order).  Returns best-of-`reps` timings."""
     m = prepare_model_heads(kvx, dump, qs, seq)
     raw = run_model_heads(kvx, m, dump.dim, "raw")
     comp = run_model_heads(kvx, m, dump.dim, "xkv")
     if not np.array_equal(raw.view(np.uint32), comp.view(np.uint32)):
         raise RuntimeError("bit mismatch on full model")
     bat = run_model_heads(kvx, m, dump.dim, "batched")
-    rel = float(np.max(np.abs(bat - comp) / np.maximum(np.abs(comp), 1e-3)))
+    mag = np.maximum(np.abs(comp).reshape(len(comp), -1).max(axis=1), 1e-30)
+    rel = float(np.max(np.abs(bat - comp).reshape(len(comp), -1).max(axis=1) / mag))
     if rel >= 1e-4:
-        raise RuntimeError(f"batched outputs differ from the per-unit ones (max rel {rel:.2e})")
+        raise RuntimeError(f"batched outputs differ from the per-unit ones (max {rel:.2e} of the "
+                           "unit's largest output)")
     t = {}
     for how in ("raw", "xkv", "batched"):
         ts = []

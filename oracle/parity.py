@@ -3,25 +3,34 @@
 TEST INFRASTRUCTURE ONLY: used by tests/, __graft_entry__.smoke() and bench.py's parity check,
 always as the checker of the GPU path, never on it.
 
-The tolerance (per output element):
+Both sides are measured against the exact result: softmax(q K^T) V in float64 over the same BF16
+inputs ("truth").  The reference's own FP32 error against it grows with the sequence (its
+sequential online softmax adds 32768 terms one at a time into fp32 running sums: about
+5e-4 of the output scale at 32K tokens with a flat softmax,
+tests/test_oracle.py::test_reference_error_grows_with_length), so a fixed tolerance around the
+reference's output either fails a correct GPU result or lets a wrong one through.  The checks
+per output element are therefore:
 
-    |gpu - ref| <= ATOL_REL * sqrt(max(1, seq / 64)) * scale + RTOL * |ref|
+    accuracy:  |gpu - truth| <= tol
+    parity:    |gpu - ref|   <= |ref - truth| + tol
+    tol = ATOL * scale + RTOL * |truth| + sqrt(D) * u * cond        (u = 2^-24)
 
-scale = the p-weighted mean |v| of the element's column (attn_scale), the natural size of an
-attention output.  The two sides differ in expf implementations (glibc on the CPU, the SFU's
-exp2 on the GPU), in accumulation order (the reference's sequential online softmax with 8-lane
-FMA chains, against tensor-core tiles and a split-K fold) -- the P weights themselves enter the
-GPU's tensor cores exactly (three bf16 terms carry all 24 bits of the fp32 weight).  The
-reference's own fp32 error against a float64 softmax grows with the sequence like sqrt(seq)
-(tests/test_oracle.py::test_reference_error_grows_with_length measures it), which is what the
-length factor covers.
+scale = the p-weighted mean |v| of the element's column (the natural size of an attention
+output).  cond = the p-weighted mean over tokens of S_t * (|v_t| + |truth|), S_t = sum_d |q_d k_td|:
+any fp32 evaluation of a score q . k_t is off by about sqrt(D) u S_t (the probabilistic bound of a
+D-term dot product), which moves the token's weight by that fraction -- large only when a few
+outlier elements make S_t large (unsoftened queries against K with 2^9 outliers).  (Parity
+follows from accuracy by the triangle inequality; it is checked anyway, against the reference's
+actual output.)  The GPU's own error is about 1e-6 of the scale at 32K tokens with softened
+queries: the P weights enter its tensor cores exactly (three bf16 terms carry all 24 bits of the
+fp32 weight) and each warp's running sums cover only its share of the tiles.
 """
 from __future__ import annotations
 
 import numpy as np
 
-ATOL_REL = 2e-5
-RTOL = 1e-4
+ATOL = 2e-5
+RTOL = 2e-5
 
 
 def bf16_to_f64(x):
@@ -39,39 +48,74 @@ def _softmax_weights(q, k, chunk=1 << 16):
     return np.exp(s)
 
 
-def attention_f64(q, k, v, chunk=1 << 16):
-    """Float64 softmax(q K^T) V over all tokens (no scaling), q [G,D], k/v [S,D] bf16 bits."""
+class Exact:
+    """The float64 result of one attention output block and what its tolerance needs."""
+
+    def __init__(self, truth, scale, cond, dim):
+        self.truth, self.scale, self.cond, self.dim = truth, scale, cond, dim
+
+    def __iter__(self):  # (truth, scale), for callers that only need those
+        return iter((self.truth, self.scale))
+
+
+def exact(q, k, v, chunk=1 << 16) -> Exact:
+    """softmax(q K^T) V in float64 over all tokens (no scaling), with its scale and cond (see the
+    module docstring); q [G, D], k / v [S, D] as bf16 bits."""
+    qf = bf16_to_f64(q)
+    qa = np.abs(qf)
     p = _softmax_weights(q, k, chunk)
-    acc = np.zeros((p.shape[0], v.shape[1]), dtype=np.float64)
+    g, d = p.shape[0], v.shape[1]
+    acc = np.zeros((g, d))
+    mag = np.zeros((g, d))
+    cv = np.zeros((g, d))
+    cs = np.zeros((g, 1))
     for t0 in range(0, v.shape[0], chunk):
-        acc += p[:, t0:t0 + chunk] @ bf16_to_f64(v[t0:t0 + chunk])
-    return acc / p.sum(axis=1, keepdims=True)
+        vf = bf16_to_f64(v[t0:t0 + chunk])
+        pc = p[:, t0:t0 + chunk]
+        ps = pc * (qa @ np.abs(bf16_to_f64(k[t0:t0 + chunk])).T)  # p_t S_t
+        acc += pc @ vf
+        mag += pc @ np.abs(vf)
+        cv += ps @ np.abs(vf)
+        cs += ps.sum(axis=1, keepdims=True)
+    den = p.sum(axis=1, keepdims=True)
+    truth = acc / den
+    return Exact(truth, mag / den, (cv + cs * np.abs(truth)) / den, d)
+
+
+def truth_and_scale(q, k, v, chunk=1 << 16) -> Exact:
+    return exact(q, k, v, chunk)
+
+
+def attention_f64(q, k, v, chunk=1 << 16):
+    return exact(q, k, v, chunk).truth
 
 
 def attn_scale(q, k, v, chunk=1 << 16):
-    """Per query and column: the p-weighted mean of |v| -- the natural scale of an output."""
-    p = _softmax_weights(q, k, chunk)
-    acc = np.zeros((p.shape[0], v.shape[1]), dtype=np.float64)
-    for t0 in range(0, v.shape[0], chunk):
-        acc += p[:, t0:t0 + chunk] @ np.abs(bf16_to_f64(v[t0:t0 + chunk]))
-    return acc / p.sum(axis=1, keepdims=True)
+    return exact(q, k, v, chunk).scale
 
 
-def tolerance(ref, scale, seq):
-    return ATOL_REL * np.sqrt(max(1.0, seq / 64.0)) * scale + RTOL * np.abs(ref)
+def tolerance(ex: Exact):
+    return (ATOL * ex.scale + RTOL * np.abs(ex.truth)
+            + np.sqrt(ex.dim) * 2.0 ** -24 * ex.cond)
 
 
-def err_over_tol(got, ref, scale, seq) -> float:
-    """max |got - ref| / tolerance: <= 1 passes.  Non-finite outputs count as infinite error."""
-    got = np.asarray(got, dtype=np.float64)
-    ref = np.asarray(ref, dtype=np.float64)
-    if not np.all(np.isfinite(got)):
-        return float("inf")
-    return float(np.max(np.abs(got - ref) / tolerance(ref, scale, seq)))
-
-
-def err_over_scale(got, ref, scale) -> float:
-    """max |got - ref| / scale (the error in units of the output's natural size)."""
-    got = np.asarray(got, dtype=np.float64)
-    ref = np.asarray(ref, dtype=np.float64)
-    return float(np.max(np.abs(got - ref) / np.maximum(scale, 1e-300)))
+def measure(gpu, ref, ex: Exact) -> dict:
+    """The parity figures of one output block: max over its elements of
+    |gpu - truth| / tol (accuracy, <= 1 passes), |gpu - ref| / (|ref - truth| + tol) (parity,
+    <= 1 passes), and the errors in units of the scale.  Non-finite GPU outputs count as infinite
+    error."""
+    g = np.asarray(gpu, dtype=np.float64)
+    r = np.asarray(ref, dtype=np.float64)
+    t = ex.truth
+    tol = tolerance(ex)
+    sc = np.maximum(ex.scale, 1e-300)
+    if not np.all(np.isfinite(g)):
+        inf = float("inf")
+        return {"accuracy": inf, "parity": inf, "gpu_err_over_scale": inf,
+                "ref_err_over_scale": float(np.max(np.abs(r - t) / sc))}
+    return {
+        "accuracy": float(np.max(np.abs(g - t) / tol)),
+        "parity": float(np.max(np.abs(g - r) / (np.abs(r - t) + tol))),
+        "gpu_err_over_scale": float(np.max(np.abs(g - t) / sc)),
+        "ref_err_over_scale": float(np.max(np.abs(r - t) / sc)),
+    }

@@ -1,7 +1,8 @@
 """Test data generators and numeric references (test infrastructure only)."""
 import numpy as np
 
-from parity import ATOL_REL, RTOL, attention_f64, attn_scale, bf16_to_f64, tolerance  # noqa: F401
+from parity import (ATOL, RTOL, attention_f64, attn_scale, bf16_to_f64, exact,  # noqa: F401
+                    measure, tolerance, truth_and_scale)
 
 
 class XorShift32:
@@ -36,19 +37,25 @@ def clustered(rng, n, base, spread):
     return out
 
 
-def assert_attention_close(gpu, cpu, scale, what="", seq=64):
-    """Per element |gpu - cpu| <= tolerance(cpu, scale, seq) (oracle/parity.py)."""
-    gpu = np.asarray(gpu, dtype=np.float64)
-    cpu = np.asarray(cpu, dtype=np.float64)
-    tol = tolerance(cpu, scale, seq)
-    err = np.abs(gpu - cpu)
-    bad = ~(err <= tol)
+def assert_attention_close(gpu, ref, q=None, k=None, v=None, what="", truth=None):
+    """The GPU output against the float64 truth and the reference's output (oracle/parity.py):
+    per element |gpu - truth| <= tol and |gpu - ref| <= |ref - truth| + tol.  `truth` = the
+    parity.Exact of the block when already computed, else computed from q, k, v (BF16 bits)."""
+    ex = truth if truth is not None else exact(q, k, v)
+    t, sc = ex.truth, ex.scale
+    g = np.asarray(gpu, dtype=np.float64)
+    r = np.asarray(ref, dtype=np.float64)
+    tol = tolerance(ex)
+    bad = ~(np.abs(g - t) <= tol) | ~(np.abs(g - r) <= np.abs(r - t) + tol)
     if bad.any():
-        i = np.argwhere(bad)[0]
+        i = tuple(np.argwhere(bad)[0])
+        with np.errstate(invalid="ignore"):
+            gerr = np.max(np.abs(g - t) / np.maximum(sc, 1e-300))
+            rerr = np.max(np.abs(r - t) / np.maximum(sc, 1e-300))
         raise AssertionError(
-            f"{what}: {bad.sum()} of {bad.size} elements out of tolerance; first {tuple(i)}: "
-            f"gpu={gpu[tuple(i)]!r} cpu={cpu[tuple(i)]!r} tol={tol[tuple(i)]!r} "
-            f"max err/scale={np.max(err / np.maximum(scale, 1e-30)):.3e}")
+            f"{what}: {bad.sum()} of {bad.size} elements out of tolerance; first {i}: "
+            f"gpu={g[i]!r} ref={r[i]!r} truth={t[i]!r} tol={tol[i]!r}; "
+            f"max |gpu-truth|/scale={gerr:.3e}, max |ref-truth|/scale={rerr:.3e}")
 
 
 def soften(q, shift=4):

@@ -9,7 +9,7 @@ import pytest
 
 import dumps
 import synth as S
-from helpers import assert_attention_close, attn_scale
+from helpers import assert_attention_close
 
 LAYERS, KV, NQ, DIM, SEQ = 2, 2, 4, 64, 640
 POS = [300, 640]
@@ -96,8 +96,7 @@ def test_model_heads_on_dump(tmp_path, kvx, cuda, oracle):
             qq = q[s.index(seq), ly, h * group:(h + 1) * group]
             kk, vv = k[ly, h, :seq], v[ly, h, :seq]
             cpu = oracle.attention(qq, k=kk, v=vv, seq=seq)
-            assert_attention_close(out[u], cpu, attn_scale(qq, kk, vv), f"dump unit {u} seq {seq}",
-                                   seq=seq)
+            assert_attention_close(out[u], cpu, qq, kk, vv, f"dump unit {u} seq {seq}")
 
 
 def test_cli(tmp_path, kvx, cuda, capsys):

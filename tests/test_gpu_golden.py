@@ -5,10 +5,11 @@ reference library (kvexp, compiled from its sources) through tests/golden/make_g
 softened queries so that the softmax spreads over many tokens.  Per case:
   * the GPU encoder writes the reference's bytes (same length and SHA-256), and the GPU decoder
     returns the input bits;
-  * GPU attention over the XKV blobs is bit-identical to the GPU's BF16-input kernel, and within
-    the FP32 tolerance of the reference's scalar output (1 thread), and of its 3-thread output
-    where the fixture has one (the GPU then runs the same call with n_threads=3, which the
-    reference's split rule must accept).
+  * GPU attention over the XKV blobs is bit-identical to the GPU's BF16-input kernel, within the
+    tight tolerance of the float64 truth, and within the reference's own error (plus that
+    tolerance) of the reference's scalar output (1 thread), of its AVX2 output, and of its
+    3-thread output where the fixture has one (the GPU then runs the same call with
+    n_threads=3, which the reference's split rule must accept).
 """
 import base64
 import hashlib
@@ -19,7 +20,7 @@ import numpy as np
 import pytest
 
 from golden_cases import CASES, inputs
-from helpers import assert_attention_close, attn_scale
+from helpers import assert_attention_close, truth_and_scale
 
 pytestmark = pytest.mark.gpu
 
@@ -59,19 +60,19 @@ def test_attention_matches_reference_fixture(kvx, cuda, name):
     seq, dim, n_q, block = c["seq"], c["dim"], c["n_q"], c["block"]
     kx = kvx.encode_bf16(k, seq, dim, block).bytes
     vx = kvx.encode_bf16(v, seq, dim, block).bytes
-    scale = attn_scale(q, k, v)
+    truth = truth_and_scale(q, k, v)
     got = _gpu(kvx, q, seq, kx=kx, vx=vx, split=block)
     raw = _gpu(kvx, q, seq, k=k, v=v, split=block)
     assert np.array_equal(got.view(np.uint32), raw.view(np.uint32)), "XKV and BF16 GPU outputs differ"
-    assert_attention_close(got, _golden_out(g, "scalar_t1", n_q, dim), scale,
-                           f"{name} vs reference scalar", seq=seq)
+    assert_attention_close(got, _golden_out(g, "scalar_t1", n_q, dim),
+                           what=f"{name} vs reference scalar", truth=truth)
     if "out_avx2_t1" in g:
-        assert_attention_close(got, _golden_out(g, "avx2_t1", n_q, dim), scale,
-                               f"{name} vs reference AVX2", seq=seq)
+        assert_attention_close(got, _golden_out(g, "avx2_t1", n_q, dim),
+                               what=f"{name} vs reference AVX2", truth=truth)
     if "out_scalar_t3" in g:
         got3 = _gpu(kvx, q, seq, kx=kx, vx=vx, threads=3, split=block)
-        assert_attention_close(got3, _golden_out(g, "scalar_t3", n_q, dim), scale,
-                               f"{name} vs reference scalar, 3 threads", seq=seq)
+        assert_attention_close(got3, _golden_out(g, "scalar_t3", n_q, dim),
+                               what=f"{name} vs reference scalar, 3 threads", truth=truth)
 
 
 def test_unsupported_dim_says_so(kvx, cuda):

@@ -11,7 +11,7 @@ import pytest
 
 import seqsplit
 import synth as S
-from helpers import assert_attention_close, attn_scale, bf16_to_f64, soften
+from helpers import assert_attention_close, bf16_to_f64, soften
 
 pytestmark = pytest.mark.gpu
 
@@ -121,8 +121,8 @@ def test_sequence_split_fold_matches_whole(kvx, cuda, oracle, dim, n_q, seq, wor
     _run(kvx, units, n_q, dim)
     folded = seqsplit.fold(outs, lses).cpu().numpy()
     cpu = oracle.attention(q, kx=oracle.encode(k, 128), vx=oracle.encode(v, 128), seq=seq)
-    assert_attention_close(folded, cpu, attn_scale(q, k, v), f"fold world={world}", seq=seq)
-    assert_attention_close(whole.cpu().numpy(), cpu, attn_scale(q, k, v), "whole", seq=seq)
+    assert_attention_close(folded, cpu, q, k, v, f"fold world={world}")
+    assert_attention_close(whole.cpu().numpy(), cpu, q, k, v, "whole")
 
 
 @pytest.mark.parametrize("n_parts,rows,dim", [(1, 3, 64), (2, 32, 256), (8, 32, 256),

@@ -173,3 +173,24 @@ def test_split_must_align_with_blocks(oracle):
     kx = oracle.encode(k, 128)
     with pytest.raises(O.OracleError, match="not aligned"):
         oracle.attention(q, kx=kx, vx=kx, seq=256, threads=2, split=96)
+
+
+def test_reference_error_grows_with_length(oracle):
+    """The reference's scalar kernel (which the oracle restates bit for bit) adds every token into
+    fp32 running sums in turn, so its own error against the float64 softmax grows with the
+    sequence: at 32K tokens with a flat softmax it is about 20 times the GPU tolerance
+    (oracle/parity.py).  This is why the GPU is checked against the float64 truth, and against the
+    reference within the reference's own error."""
+    import synth as S
+    from helpers import soften
+    from parity import ATOL, truth_and_scale
+    errs = []
+    for seq in (1024, 8192, 32768):
+        k = S.synth_bf16(31, 0, seq, 64, S.PROFILE_K)
+        v = S.synth_bf16(31, 1, seq, 64, S.PROFILE_V)
+        q = soften(S.synth_bf16(31, 2, 7, 64, S.PROFILE_Q), 8)
+        out = oracle.attention(q, kx=oracle.encode(k, 128), vx=oracle.encode(v, 128), seq=seq)
+        ex = truth_and_scale(q, k, v)
+        errs.append(float(np.max(np.abs(out - ex.truth) / ex.scale)))
+    assert errs[0] < errs[1] < errs[2], errs
+    assert errs[2] > 5 * ATOL, errs

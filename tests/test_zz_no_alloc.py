@@ -5,16 +5,16 @@ device's memory for their KV-cache pool at start-up, and decode loops that canno
 device-wide stall of cudaFree.  This entry point keeps all of its scratch in one fixed device
 array inside the library.  The tests check two calls in a row (the second finds the first call's
 scratch contents) against the ordinary entry point kvx_attention_decode and against the scalar
-oracle directly, within the same FP32 tolerance as the other attention tests, including calls
-with more blocks than the grid has workers (then the entry point splits the blocks evenly over
-its workers, and units span several of them).  The file is named so that pytest collects it
+oracle directly, with the same float64-anchored tolerance as the other attention tests,
+including calls with more blocks than the grid has CTAs (then the entry point splits the blocks
+evenly over its CTA ranges, and every range holds several).  The file is named so that pytest collects it
 last.
 """
 import numpy as np
 import pytest
 
 import synth as S
-from helpers import assert_attention_close, attn_scale, soften
+from helpers import assert_attention_close, soften, truth_and_scale
 
 pytestmark = pytest.mark.gpu
 
@@ -37,9 +37,9 @@ def _device_index(kvx, torch, blob, dim):
 @pytest.mark.parametrize("cases", [
     [(64, 7, 3000, 11), (64, 7, 3000, 12)],     # same shape twice, new data
     [(128, 12, 5000, 13), (64, 3, 700, 14)],    # shape changes between the calls
-    # more blocks than workers: 2048 blocks at D=64 (an even split over 148 x 12 workers), then
-    # 2 query groups x 600 blocks at D=256 (the partial states then cap the workers below one
-    # CTA of 6 per SM), and back
+    # more blocks than CTAs: 2048 blocks at D=64 (an even split over 148 ranges), then 2 query
+    # groups x 600 blocks at D=256 (the partial states then cap the ranges below one per SM), and
+    # back
     [(64, 7, 2048 * 128, 16), (256, 12, 600 * 128, 17), (64, 7, 2048 * 128 - 37, 18)],
 ])
 def test_noalloc_matches_attention_decode(kvx, cuda, oracle, cases):
@@ -59,11 +59,11 @@ def test_noalloc_matches_attention_decode(kvx, cuda, oracle, cases):
                                      seq)
         got = out.cpu().numpy()
         assert np.all(np.isfinite(got))
-        scale = attn_scale(q, k, v)
-        assert_attention_close(got, want, scale, f"noalloc vs attention_decode dim={dim} "
-                               f"n_q={n_q} seq={seq}", seq=seq)
-        assert_attention_close(got, oracle.attention(q, kx=kx, vx=vx, seq=seq), scale,
-                               f"noalloc vs oracle dim={dim} n_q={n_q} seq={seq}", seq=seq)
+        truth = truth_and_scale(q, k, v)
+        assert_attention_close(got, want, what=f"noalloc vs attention_decode dim={dim} "
+                               f"n_q={n_q} seq={seq}", truth=truth)
+        assert_attention_close(got, oracle.attention(q, kx=kx, vx=vx, seq=seq),
+                               what=f"noalloc vs oracle dim={dim} n_q={n_q} seq={seq}", truth=truth)
 
 
 def test_noalloc_rejects_oversize(kvx, cuda):
