@@ -283,6 +283,7 @@ struct kvx_plan_s {
     FlatBlock *flat = nullptr;
     BlockDesc *desc = nullptr;  // per flat block, for the attention kernel
     uint32_t *esc = nullptr;  // escape records of the step's coded blocks
+    uint32_t *b7 = nullptr;   // merge words of the step's coded blocks ([n_blocks][dim])
     int64_t *range_begin = nullptr;
     int32_t *seg_base = nullptr;
     float *partials = nullptr;
@@ -396,6 +397,7 @@ static cudaError_t plan_blob_work(kvx_plan_s *p, cudaEvent_t blobs_ready) {
     if (blobs_ready != nullptr) e = cudaStreamWaitEvent(nullptr, blobs_ready, 0);
     if (e == cudaSuccess && p->esc_total > 0)
         e = launch_esc_fill(p->units, p->flat, p->n_blocks, p->dim, p->esc, p->esc_total, p->status, nullptr);
+    if (e == cudaSuccess && !p->bf16) e = launch_b7(p->units, p->flat, p->n_blocks, p->dim, p->b7, nullptr);
     if (e == cudaSuccess)
         e = launch_block_desc(p->units, p->flat, p->esc, p->n_blocks, p->dim, p->bf16, p->desc, nullptr);
     return e;
@@ -475,6 +477,7 @@ static int plan_create_impl(const kvx_unit *units, int n_units, int n_q, int dim
     if ((e = plan_alloc(p, &p->units, ud.size())) != cudaSuccess ||
         (e = plan_alloc(p, &p->flat, size_t(total))) != cudaSuccess ||
         (e = plan_alloc(p, &p->desc, size_t(total))) != cudaSuccess ||
+        (e = plan_alloc(p, &p->b7, bf16 ? size_t(0) : size_t(total) * size_t(dim))) != cudaSuccess ||
         (e = plan_alloc(p, &p->range_begin, tb.size())) != cudaSuccess ||
         (e = plan_alloc(p, &p->seg_base, size_t(p->n_ranges))) != cudaSuccess ||
         (e = plan_alloc(p, &p->split_units, ud.size())) != cudaSuccess ||
@@ -592,6 +595,7 @@ int kvx_plan_run_part(kvx_plan p, int part, void *stream) {
     a.flat = p->flat;
     a.desc = p->desc;
     a.esc = p->esc;
+    a.b7 = p->b7;
     a.range_begin = p->range_begin;
     a.seg_base = p->seg_base;
     a.partials = p->partials;
@@ -1255,7 +1259,7 @@ extern "C" int kvx_fold_shards(const float *parts, int n_parts, int n_rows, int 
 
 namespace kvx {
 namespace {
-constexpr size_t kNoAllocScratchBytes = size_t(30) << 20;  // 30 MiB per device
+constexpr size_t kNoAllocScratchBytes = size_t(40) << 20;  // 40 MiB per device
 constexpr size_t kNoAllocEscEntries = size_t(3) << 20;      // escape record entries (12 MiB)
 constexpr int kNoAllocMaxBlocks = 8192;                   // XKV blocks per tensor
 constexpr int kNoAllocMaxQueries = 64;                    // queries per call (8 groups of 8)
@@ -1272,7 +1276,8 @@ constexpr size_t kNoAllocFixedBytes =
     up256c(size_t(kNoAllocMaxGroups) * kNoAllocMaxBlocks * sizeof(FlatBlock)) +
     up256c(size_t(kNoAllocMaxGroups) * kNoAllocMaxBlocks * sizeof(BlockDesc)) +
     up256c((kNoAllocMaxRanges + 1) * sizeof(int64_t)) + up256c(kNoAllocMaxRanges * sizeof(int32_t)) +
-    up256c(sizeof(unsigned long long)) + up256c((kNoAllocEscEntries + 4) * sizeof(uint32_t));
+    up256c(sizeof(unsigned long long)) + up256c((kNoAllocEscEntries + 4) * sizeof(uint32_t)) +
+    up256c(size_t(kNoAllocMaxBlocks) * kMaxHeadDim * sizeof(uint32_t));
 // One partial-state row (every consumer warp's m, l and acc) at its largest, over the head dims.
 constexpr size_t noalloc_row_bytes(int dim) {
     return size_t(attention_consumer_warps(dim)) * size_t(16 + 8 * dim) * sizeof(float);
@@ -1350,7 +1355,7 @@ extern "C" int kvx_attention_decode_noalloc(const uint16_t *q, const uint8_t *k_
 
     // Scratch layout (256-byte aligned pieces): status | units | unit descriptors | block
     // begins | record sources | split units | flat blocks | block descriptors | CTA ranges | row
-    // bases | record size | escape records | partial states.
+    // bases | record size | escape records | merge words | partial states.
     const int groups = (n_q + 7) / 8;
     const int64_t total = int64_t(groups) * n_blocks;
     size_t off = 0;
@@ -1374,6 +1379,8 @@ extern "C" int kvx_attention_decode_noalloc(const uint16_t *q, const uint8_t *k_
     unsigned long long *d_esc_total =
         reinterpret_cast<unsigned long long *>(take(sizeof(unsigned long long)));
     uint32_t *d_esc = reinterpret_cast<uint32_t *>(take((kNoAllocEscEntries + 4) * sizeof(uint32_t)));
+    // merge words: only the first query group's blocks have their own (the others share them)
+    uint32_t *d_b7 = reinterpret_cast<uint32_t *>(take(size_t(kNoAllocMaxBlocks) * kMaxHeadDim * sizeof(uint32_t)));
     if (off != kNoAllocFixedBytes)
         return fail(KVX_ERR_RUNTIME, std::string(fn) + "scratch layout out of step with its size");
     float *d_partials = reinterpret_cast<float *>(base + off);
@@ -1437,12 +1444,14 @@ extern "C" int kvx_attention_decode_noalloc(const uint16_t *q, const uint8_t *k_
                                status, s));
     KVX_CUDA(launch_esc_layout(d_flat, total, d_esc_total, kNoAllocEscEntries, status, s));
     KVX_CUDA(launch_esc_fill(d_units, d_flat, total, dim, d_esc, kNoAllocEscEntries, status, s));
+    KVX_CUDA(launch_b7(d_units, d_flat, total, dim, d_b7, s));
     KVX_CUDA(launch_block_desc(d_units, d_flat, d_esc, total, dim, false, d_desc, s));
     AttnArgs a{};
     a.units = d_units;
     a.flat = d_flat;
     a.desc = d_desc;
     a.esc = d_esc;
+    a.b7 = d_b7;
     a.range_begin = d_range;
     a.seg_base = d_seg;
     a.partials = d_partials;

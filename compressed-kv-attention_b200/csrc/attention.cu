@@ -73,15 +73,16 @@ template <int D> struct Cfg {
     // with more leaves them in HBM, where the consumers read them.
     static constexpr int ESC_CAP = TSB * D / 8;
     // One tensor's region of a slot: rows at 0 (raw: 2 D bytes per token; coded: D bytes, then the
-    // residual codes at CODE_OFF), base exponents at B_OFF, escape entries at E_OFF.  Every piece
-    // lands 0-15 bytes past its 16-byte aligned start.
+    // residual codes at CODE_OFF), escape entries at E_OFF.  Every piece lands 0-15 bytes past its
+    // 16-byte aligned start.
     static constexpr int R_BYTES = 2 * TSB * D + 32;
     static constexpr int CODE_OFF = TSB * D + 16;
-    static constexpr int B_OFF = R_BYTES;
-    static constexpr int E_OFF = B_OFF + round16(D + 32);
+    static constexpr int E_OFF = R_BYTES;
     static constexpr int T_BYTES = round16(E_OFF + 4 * ESC_CAP + 32);
-    // A slot: the block descriptor (128 bytes), then the K and V regions.
-    static constexpr int S_T = 128;
+    // A slot: the block descriptor (128 bytes), the block's merge words (K then V, 2 D bytes each),
+    // then the K and V regions.
+    static constexpr int S_B7 = 128;
+    static constexpr int S_T = S_B7 + 4 * D;
     static constexpr int SLOT = S_T + 2 * T_BYTES;
     static constexpr int TILE = TT * 2 * D;       // one consumer warp's BF16 tile
     static constexpr int O_TILE = NSLOT * SLOT;
@@ -175,28 +176,18 @@ struct Lay {
 // rd / cd: data offsets of the block's row and code pieces.
 template <int D>
 __device__ __forceinline__ Lay make_lay(uint32_t rd, uint32_t cd, int mode, int c8, bool bf16) {
+    // Every offset in a blob is even, so a section starts 0 or 2 bytes past a 4-byte boundary and
+    // each selector is one of two constants.
     Lay l;
-    const uint32_t m = rd & 3u;
-    l.p0 = rep2(m);
-    l.p1 = rep2(m + 2);
-    l.w = shift4(m);
+    const bool m2 = (rd & 2u) != 0u;
+    l.p0 = m2 ? rep2(2) : rep2(0);
+    l.p1 = m2 ? rep2(4) : rep2(2);
+    l.w = m2 ? shift4(2) : shift4(0);
     l.rows = (rd & ~3u) + uint32_t((bf16 || mode == 0) ? 16 * c8 : 8 * c8);
     const uint32_t cb = (cd & 3u) + uint32_t(c8 * (mode == 0 ? 0 : mode));
-    l.cs = shift4(cb & 3u);
+    l.cs = (cb & 2u) != 0u ? shift4(2) : shift4(0);
     l.codes = uint32_t(Cfg<D>::CODE_OFF) + (cd & ~3u) + (cb & ~3u);
     return l;
-}
-
-// b7 of the lane's four dim pairs (c, c+1): base[c] << 7 | base[c+1] << 23.  `base` is the
-// shared address of base[8 c8].
-__device__ __forceinline__ void load_b7(uint32_t base, uint32_t (&b7)[4]) {
-    const uint32_t m = base & 3u, q = base - m;
-    const uint32_t B0 = lds_u32(q), B1 = lds_u32(q + 4u), B2 = lds_u32(q + 8u);
-    const uint32_t s0 = rep2(m), s1 = rep2(m + 2);
-    b7[0] = (prmt(B0, B1, s0) & 0x00FF00FFu) << 7;
-    b7[1] = (prmt(B0, B1, s1) & 0x00FF00FFu) << 7;
-    b7[2] = (prmt(B1, B2, s0) & 0x00FF00FFu) << 7;
-    b7[3] = (prmt(B1, B2, s1) & 0x00FF00FFu) << 7;
 }
 
 // Byte offset of 16-byte chunk c8 of tile row t: rows of 2 D bytes, chunks XOR-swizzled by the
@@ -452,16 +443,11 @@ __device__ __forceinline__ uint32_t stage_piece(uint32_t dst, const uint8_t *src
     return p.alloc;
 }
 
-// Bytes stage_piece copies for [src, src + len).
-__device__ __forceinline__ uint32_t piece_bytes(const uint8_t *src, uint32_t len) {
-    return len == 0u ? 0u : make_piece(src, len).alloc;
-}
-
-// The descriptor words the producer needs of one block: bytes 0-31 (K / V addresses, escape
-// record offsets and counts, modes, tokens) and, when a block takes several stages, the escape
-// count headers (bytes 64-127).
+// The descriptor words the producer needs of one block: bytes 0-47 (K / V addresses, escape
+// record offsets and counts, modes, tokens, the block of its merge words) and, when a block takes
+// several stages, the escape count headers (bytes 64-127).
 template <bool MULTI> struct PDesc {
-    uint4 w0, w1;
+    uint4 w0, w1, w2;
     uint4 e[MULTI ? 4 : 1];
 };
 
@@ -470,6 +456,7 @@ __device__ __forceinline__ void pdesc_load(const BlockDesc *gd, PDesc<MULTI> &d)
     const uint4 *p = reinterpret_cast<const uint4 *>(gd);
     d.w0 = __ldg(p);
     d.w1 = __ldg(p + 1);
+    d.w2 = __ldg(p + 2);
     if constexpr (MULTI) {
 #pragma unroll
         for (int i = 0; i < 4; ++i) d.e[i] = __ldg(p + 4 + i);
@@ -491,8 +478,8 @@ __device__ __forceinline__ int pdesc_esc(const uint4 (&e)[4], int T, int i) {
     return int((r >> (16 * ((i - 1) & 1))) & 0xFFFFu);
 }
 
-// The producer warp: for every stage of the CTA's blocks, wait until the slot is free, announce
-// the stage's byte count on the slot's full barrier, then issue its copies (lane 0).  Lane l holds
+// The producer warp: for every stage of the CTA's blocks, wait until the slot is free, issue the
+// stage's copies and announce their byte count on the slot's full barrier (lane 0).  Lane l holds
 // the descriptor of block base + l; the next 32 are loaded while the current 32 are issued, so
 // the issuing lane never waits on a global load.  On a timeout it reports DERR_TIMEOUT and waits
 // (bounded) for the copies it issued before it returns.
@@ -514,6 +501,7 @@ __device__ void producer(const AttnArgs &a, uint8_t *smem, int fb0, int fb1, int
             const uint64_t vp = (uint64_t(__shfl_sync(FULL, cur.w0.w, j)) << 32) | __shfl_sync(FULL, cur.w0.z, j);
             const uint32_t krec = __shfl_sync(FULL, cur.w1.x, j), vrec = __shfl_sync(FULL, cur.w1.y, j);
             const uint32_t nesc = __shfl_sync(FULL, cur.w1.z, j), mw = __shfl_sync(FULL, cur.w1.w, j);
+            const int b7_block = int(__shfl_sync(FULL, cur.w2.w, j));
             const int km = BF16IN ? 0 : int(mw & 0xFFu), vm = BF16IN ? 0 : int((mw >> 8) & 0xFFu);
             const int n_tok = int((mw >> 16) & 0xFFu), valid = int(mw >> 24);
             // e(i) of tensor T of this block (uniform i)
@@ -545,37 +533,40 @@ __device__ void producer(const AttnArgs &a, uint8_t *smem, int fb0, int fb1, int
                     }
                 }
                 if (lane == 0) {
+                    // Each piece goes out as soon as it is known; the slot's barrier learns the
+                    // stage's byte count after them (its tx-count may run below zero meanwhile;
+                    // the phase cannot complete before this arrive).
                     const uint32_t dslot = sb + uint32_t(slot * C::SLOT);
-                    // the pieces of this stage: [src, len, dst]
-                    const uint8_t *src[9];
-                    uint32_t len[9], dst[9];
-                    int np = 0;
-                    src[np] = reinterpret_cast<const uint8_t *>(gd), len[np] = uint32_t(sizeof(BlockDesc)), dst[np++] = dslot;
+                    uint32_t total = stage_piece(dslot, reinterpret_cast<const uint8_t *>(gd),
+                                                 uint32_t(sizeof(BlockDesc)), full);
+                    if (!BF16IN && (km | vm) != 0)
+                        total += stage_piece(dslot + C::S_B7,
+                                             reinterpret_cast<const uint8_t *>(a.b7 + size_t(b7_block) * D),
+                                             uint32_t(4 * D), full);
 #pragma unroll
                     for (int T = 0; T < 2; ++T) {
                         const uint8_t *blk = gptr(T ? vp : kp);
                         const int mode = T ? vm : km;
                         const uint32_t reg = dslot + uint32_t(C::S_T + T * C::T_BYTES);
                         if (BF16IN) {
-                            src[np] = blk + size_t(t0) * 2 * D, len[np] = uint32_t(n * 2 * D), dst[np++] = reg;
+                            total += stage_piece(reg, blk + size_t(t0) * 2 * D, uint32_t(n * 2 * D), full);
                         } else if (mode == 0) {
-                            src[np] = blk + kHeaderBytes + size_t(t0) * 2 * D, len[np] = uint32_t(n * 2 * D), dst[np++] = reg;
+                            total += stage_piece(reg, blk + kHeaderBytes + size_t(t0) * 2 * D,
+                                                 uint32_t(n * 2 * D), full);
                         } else {
                             const uint8_t *rows = blk + kHeaderBytes + D;
-                            src[np] = blk + kHeaderBytes, len[np] = uint32_t(D), dst[np++] = reg + C::B_OFF;
-                            src[np] = rows + size_t(t0) * D, len[np] = uint32_t(n * D), dst[np++] = reg;
-                            src[np] = rows + size_t(n_tok) * D + size_t(t0) * D * mode / 8;
-                            len[np] = uint32_t(n * D * mode / 8), dst[np++] = reg + C::CODE_OFF;
-                            if (eb[T] > ea[T] && eb[T] - ea[T] <= C::ESC_CAP) {
-                                src[np] = reinterpret_cast<const uint8_t *>(a.esc + (T ? vrec : krec) + kEscRecHead + ea[T]);
-                                len[np] = uint32_t(4 * (eb[T] - ea[T])), dst[np++] = reg + C::E_OFF;
-                            }
+                            total += stage_piece(reg, rows + size_t(t0) * D, uint32_t(n * D), full);
+                            total += stage_piece(reg + C::CODE_OFF,
+                                                 rows + size_t(n_tok) * D + size_t(t0) * D * mode / 8,
+                                                 uint32_t(n * D * mode / 8), full);
+                            if (eb[T] > ea[T] && eb[T] - ea[T] <= C::ESC_CAP)
+                                total += stage_piece(reg + C::E_OFF,
+                                                     reinterpret_cast<const uint8_t *>(
+                                                         a.esc + (T ? vrec : krec) + kEscRecHead + ea[T]),
+                                                     uint32_t(4 * (eb[T] - ea[T])), full);
                         }
                     }
-                    uint32_t total = 0;
-                    for (int i = 0; i < np; ++i) total += piece_bytes(src[i], len[i]);
                     mbar_arrive_expect_tx(full, total);
-                    for (int i = 0; i < np; ++i) stage_piece(dst[i], src[i], len[i], full);
                 }
                 __syncwarp();
                 ++gs;
@@ -591,11 +582,12 @@ __device__ void producer(const AttnArgs &a, uint8_t *smem, int fb0, int fb1, int
 }
 
 // One tensor of one tile into the warp's BF16 tile, escapes included.  reg: the tensor's region of
-// the slot; g16: the tile's 16-token group in the block; t0: the stage's first token in the block;
-// rows: valid rows of the tile; zero_from: rows at or past it are zeroed.
+// the slot; b7s: the tensor's merge words in the slot; g16: the tile's 16-token group in the
+// block; t0: the stage's first token in the block; rows: valid rows of the tile; zero_from: rows
+// at or past it are zeroed.
 template <int D>
 __device__ __forceinline__ void tile_tensor(const AttnArgs &a, const BlockDesc &bd, int T, int mode,
-                                            uint32_t al, uint32_t reg, int tw, uint32_t xb,
+                                            uint32_t al, uint32_t reg, uint32_t b7s, int tw, uint32_t xb,
                                             const StoreMap<D> &sm, int g16, int t0, int rows,
                                             int zero_from, bool bf16, int lane) {
     using C = Cfg<D>;
@@ -606,7 +598,7 @@ __device__ __forceinline__ void tile_tensor(const AttnArgs &a, const BlockDesc &
     const uint32_t cb = reg + uint32_t(TT * tw * (D * mode / 8));
     if (mode != 0) {
         uint32_t b7[4];
-        load_b7(reg + uint32_t(C::B_OFF) + rd + 8u * uint32_t(c8), b7);
+        lds_v4(b7s + 16u * uint32_t(c8), b7[0], b7[1], b7[2], b7[3]);
         if (mode == 4) decode_tile<D, 4>(rb, cb, ly, b7, sm, lane);
         else decode_tile<D, 2>(rb, cb, ly, b7, sm, lane);
     } else {
@@ -655,7 +647,8 @@ __device__ __forceinline__ void tile_step(const AttnArgs &a, const BlockDesc &bd
     const uint32_t kreg = slot_addr + uint32_t(C::S_T), vreg = kreg + uint32_t(C::T_BYTES);
 
     // S^T = K Q^T (rows past `rows` hold stale words: their scores are dropped)
-    tile_tensor<D>(a, bd, 0, km, al & 0xFFFFu, kreg, tw, xb, sm, g16, t0, rows, TT, BF16IN, lane);
+    tile_tensor<D>(a, bd, 0, km, al & 0xFFFFu, kreg, slot_addr + uint32_t(C::S_B7), tw, xb, sm, g16, t0,
+                   rows, TT, BF16IN, lane);
     float s[1][4];
     qk_tiles<D, 1>(xb, qb, lane, s);
     if (rows < TT) {
@@ -718,7 +711,8 @@ __device__ __forceinline__ void tile_step(const AttnArgs &a, const BlockDesc &bd
 
     // V replaces K in the tile (K was read by the MMAs above: ldmatrix is warp-synchronous);
     // rows past `rows` are zeroed (P is 0 there and V must be finite)
-    tile_tensor<D>(a, bd, 1, vm, al >> 16, vreg, tw, xb, sm, g16, t0, rows, rows, BF16IN, lane);
+    tile_tensor<D>(a, bd, 1, vm, al >> 16, vreg, slot_addr + uint32_t(C::S_B7 + 2 * D), tw, xb, sm, g16,
+                   t0, rows, rows, BF16IN, lane);
     if (lane == 0) mbar_arrive(empty);  // this warp has read everything it needs from the slot
     pv_tile<D>(xb, 0, bh, bm, bl, lane, st.acc);
     __syncwarp();  // every lane is done with the tile before the next decode writes it
@@ -1041,6 +1035,7 @@ __global__ void block_desc_kernel(const UnitDev *units, const FlatBlock *flat, c
     d.valid = f.valid;
     d.unit = f.unit;
     d.flags = uint8_t((i == U.block_begin ? kDescFirst : 0) | (i + 1 == U.block_begin + U.n_blocks ? kDescLast : 0));
+    d.b7_block = f.src;
     for (int T = 0; T < 2; ++T) {
         const uint8_t *blob = T ? U.v : U.k;
         const uint32_t off = T ? f.v_off : f.k_off;
@@ -1057,6 +1052,26 @@ __global__ void block_desc_kernel(const UnitDev *units, const FlatBlock *flat, c
             for (int j = 0; j < 16; ++j) d.em[T][j] = uint16_t(esc[rec + j]);
     }
     desc[i] = d;
+}
+
+// One warp per flat block: the merge words of its coded K and V (zeros for a raw tensor).  Blocks
+// that share another block's K/V (src != itself) have none of their own.
+__global__ void b7_kernel(const UnitDev *units, const FlatBlock *flat, int64_t n, int dim, uint32_t *b7) {
+    const int64_t i = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (i >= n) return;
+    const FlatBlock f = flat[i];
+    if (int64_t(f.src) != i) return;
+    const UnitDev &U = units[f.unit];
+    for (int T = 0; T < 2; ++T) {
+        const int mode = T ? f.v_mode : f.k_mode;
+        const uint16_t *base = reinterpret_cast<const uint16_t *>((T ? U.v : U.k) + (T ? f.v_off : f.k_off) + kHeaderBytes);
+        uint32_t *w = b7 + size_t(i) * dim + size_t(T) * (dim / 2);
+        for (int j = lane; j < dim / 2; j += 32) {
+            const uint32_t x = mode != 0 ? uint32_t(__ldg(base + j)) : 0u;  // base[2j] | base[2j + 1] << 8
+            w[j] = ((x & 0xFFu) << 7) | ((x >> 8) << 23);
+        }
+    }
 }
 
 template <int D>
@@ -1137,6 +1152,13 @@ cudaError_t launch_combine(int dim, const CombineArgs &a, int n_split, cudaStrea
     case 256: return cudaLaunchKernelEx(&cfg, combine_kernel<256>, a);
     default: return cudaErrorInvalidValue;
     }
+}
+
+cudaError_t launch_b7(const UnitDev *units, const FlatBlock *flat, int64_t n_blocks, int dim,
+                      uint32_t *b7, cudaStream_t s) {
+    if (n_blocks <= 0) return cudaSuccess;
+    b7_kernel<<<unsigned((n_blocks + 7) / 8), 256, 0, s>>>(units, flat, n_blocks, dim, b7);
+    return cudaGetLastError();
 }
 
 cudaError_t launch_block_desc(const UnitDev *units, const FlatBlock *flat, const uint32_t *esc, int64_t n,

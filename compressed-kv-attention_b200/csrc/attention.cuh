@@ -52,9 +52,13 @@ __host__ __device__ inline uint32_t esc_scratch_slot(int dim, int T, int r, int 
     return uint32_t(r * 2 * dim + ((c8 ^ sw) << 4) + 2 * (c & 7));
 }
 
-// Consumer warps per CTA of the attention kernel (one CTA per SM; one more warp issues the copies,
-// so a CTA is 16 warps at 128 registers a thread, or 8 warps at 255 for dim 256).
-__host__ __device__ constexpr int attention_consumer_warps(int dim) { return dim >= 256 ? 7 : 15; }
+// Consumer warps per CTA of the attention kernel (one CTA per SM; one more warp issues the copies):
+// a CTA of 16 warps at 128 registers a thread for dim <= 64, 12 at 168 for dim 128, 8 at 255 for
+// dim 256.  A stage of 128 tokens (64 at dim 128, 32 at dim 256) is 8 (4, 2) tiles, dealt round
+// robin; each consumer warp takes at most one tile of a stage.
+__host__ __device__ constexpr int attention_consumer_warps(int dim) {
+    return dim >= 256 ? 7 : (dim >= 128 ? 11 : 15);
+}
 
 __device__ __forceinline__ FlatBlock load_flat(const FlatBlock *f, int64_t i) {
     const uint4 a = __ldg(reinterpret_cast<const uint4 *>(f + i));
@@ -101,10 +105,13 @@ struct BlockDesc {
     uint8_t align[4];       // K rows, K codes, V rows, V codes: offset of the section's first byte
                             // in its 16-byte line (codes 0 for a raw block)
     uint8_t flags;          // kDescFirst | kDescLast
-    uint8_t pad[23];
+    uint8_t pad0[3];
+    int32_t b7_block;       // flat block whose merge words (AttnArgs::b7) this block uses
+    uint8_t pad1[16];
     uint16_t em[2][16];     // K / V escape count headers, e(i) at [i - 1] (zeros without a record)
 };
-static_assert(sizeof(BlockDesc) == 128 && offsetof(BlockDesc, align) == 36 && offsetof(BlockDesc, em) == 64,
+static_assert(sizeof(BlockDesc) == 128 && offsetof(BlockDesc, align) == 36 &&
+                  offsetof(BlockDesc, b7_block) == 44 && offsetof(BlockDesc, em) == 64,
               "BlockDesc layout");
 constexpr uint8_t kDescFirst = 1, kDescLast = 2;  // the first / last block of its unit
 
@@ -113,6 +120,7 @@ struct AttnArgs {
     const FlatBlock *flat;      // [n_blocks]
     const BlockDesc *desc;      // [n_blocks]
     const uint32_t *esc;        // escape records (FlatBlock::k_rec / v_rec index it)
+    const uint32_t *b7;         // [n_blocks][dim] merge words of each coded block: K, then V
     const int64_t *range_begin; // [n_ranges + 1] flat-block range of each CTA
     const int32_t *seg_base;    // [n_ranges] first partial-state row of each CTA
     float *partials;            // [rows][consumer warps][partial_stride(dim)]
@@ -165,6 +173,12 @@ inline int64_t segment_rows(const int64_t *range_begin, int n_ranges, const int6
 // Launchers (attention.cu).  Return cudaError_t of the launch.
 cudaError_t launch_attention(int dim, bool bf16_input, const AttnArgs &a, int grid, cudaStream_t s);
 cudaError_t launch_combine(int dim, const CombineArgs &a, int n_split, cudaStream_t s);
+// Merge words of a step's coded blocks (blocks that share another block's K/V blocks -- a later
+// query group of the same unit -- use that block's): for block f and tensor T, word w of
+// b7 + f dim + T dim / 2 holds the base exponents of head dims 2w and 2w + 1 moved to where the
+// decode adds the residual codes (base[2w] << 7 | base[2w + 1] << 23).
+cudaError_t launch_b7(const UnitDev *units, const FlatBlock *flat, int64_t n_blocks, int dim,
+                      uint32_t *b7, cudaStream_t s);
 // Block descriptors of a step from its flat blocks, units and escape records.
 cudaError_t launch_block_desc(const UnitDev *units, const FlatBlock *flat, const uint32_t *esc, int64_t n,
                               int dim, bool bf16, BlockDesc *desc, cudaStream_t s);

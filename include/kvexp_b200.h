@@ -146,22 +146,24 @@ typedef struct kvx_plan_s *kvx_plan;
 
 /* Build a reusable launch plan for a fixed set of units (host array of n_units descriptors).
  * block_tokens is the encode block size (the tile split of the BF16 kernel).  The plan uploads
- * the descriptors, balances HBM bytes across the GPU and owns the scratch for split units. */
+ * the descriptors, cuts the step's blocks into one range of about equal decode cost per SM, and
+ * owns the scratch for the partial softmax states. */
 KVX_API int kvx_plan_create(const kvx_unit *units, int n_units, int n_q, int dim, int block_tokens,
                     kvx_plan *plan);
 /* Launch one decode step for every unit on `stream` (a cudaStream_t; NULL = default stream).
  * A plan's steps run one after another on a stream: a step that overlaps the plan's previous
  * one (another stream) races on the plan's scratch. */
 KVX_API int kvx_plan_run(kvx_plan plan, void *stream);
-/* Launch one part of a step: 0 = the fused decode-attention kernel, 1 = the combine kernel of
- * units split across workers (a no-op when no unit is split).  kvx_plan_run = part 0 then 1. */
+/* Launch one part of a step: 0 = the fused decode-attention kernel, 1 = the combine kernel that
+ * folds every unit's partial softmax states (one per consumer warp of every CTA that held some of
+ * its blocks) into its outputs.  kvx_plan_run = part 0 then 1. */
 KVX_API int kvx_plan_run_part(kvx_plan plan, int part, void *stream);
 /* Synchronise the plan's last run and report device-side errors (malformed blocks, timeouts). */
 KVX_API int kvx_plan_check(kvx_plan plan);
 /* Number of kernel launches one kvx_plan_run makes. */
 KVX_API int kvx_plan_launches(kvx_plan plan);
-/* Number of the plan's units (query groups of <= 8) whose blocks span several workers (the
- * combine kernel folds their partial softmax states in worker order). */
+/* Number of the plan's units (query groups of <= 8) that the combine kernel folds: all of them
+ * (each unit's tiles are spread over several consumer warps). */
 KVX_API int kvx_plan_split_units(kvx_plan plan);
 KVX_API void kvx_plan_destroy(kvx_plan plan);
 
@@ -203,7 +205,7 @@ KVX_API int kvx_fold_shards(const float *parts, int n_parts, int n_rows, int dim
  * kvx_attention_decode for one KV head (within FP32 rounding), with every buffer in device
  * memory: q [n_q, dim] BF16, the K/V XKV blobs (16-byte aligned) with their block indexes
  * (n_blocks entries each, from kvx_xkv_index or the GPU encoder), out [n_q, dim] FP32.  Its
- * scratch is one fixed 30 MiB array in the library's device image, held by every device that
+ * scratch is one fixed 40 MiB array in the library's device image, held by every device that
  * loads the library until the process exits; limits: n_blocks <= 8192, n_q <= 64, and the
  * blobs' escape words plus 16 per coded block that has any at most 3 Mi (about 1 in 6 elements
  * of 8192 blocks of 128 x 128) -- larger calls fail with KVX_ERR_INVALID_ARGUMENT (the escape
