@@ -258,11 +258,13 @@ int check_attention_args(int backend, const uint16_t *q, const uint16_t *k_raw,
                                                   ? "avx2 attention: bad shape"
                                                   : "scalar attention: bad shape");
     }
-    if (!attention_dim_supported(dim))
-        return fail(KVX_ERR_UNSUPPORTED,
-                    "kvexp_b200: head_dim must be 32, 64, 128 or 256 for the GPU kernels");
     return KVX_OK;
 }
+
+// The fused kernels' head dims: 32, 64, 128, 256.  The drop-in single-head call takes every
+// head_dim the reference's backends take (a multiple of 8, or of 32 for AVX-512, up to 256) and
+// runs the others zero-padded to the next of these.
+int padded_dim(int dim) { return dim <= 32 ? 32 : dim <= 64 ? 64 : dim <= 128 ? 128 : 256; }
 
 }  // namespace
 }  // namespace kvx
@@ -710,6 +712,76 @@ int to_device(const void *src, size_t bytes, DevBuf &buf, const void *&dptr, cud
     return KVX_OK;
 }
 
+int run_units(std::vector<kvx_unit> &units, int n_q, int dim, int block_tokens, cudaStream_t s);
+
+// kvx_attention_decode for a head_dim the fused kernels do not take: K and V as [seq, dim] BF16 on
+// the device (XKV blobs decoded by the GPU decoder), zero-padded with Q to the next fused width
+// and run through the BF16-input kernel in tiles of split_tokens rows.  Zero columns add exact
+// zeros to every score and only the first dim output columns are returned; raw and XKV inputs
+// reach the tensor cores as the same tiles, so their outputs are bit-identical (the reference's
+// invariant, include/kvexp/attention.hpp:48-50).
+int attention_decode_padded(const uint16_t *q, const uint16_t *k_raw, const uint16_t *v_raw,
+                            const uint8_t *k_xkv, size_t k_bytes, const uint8_t *v_xkv,
+                            size_t v_bytes, float *out, int n_q, int dim, int seq, int n_threads,
+                            int split_tokens) {
+    cudaStream_t s = nullptr;
+    const int dp = padded_dim(dim);
+    const bool xkv = k_xkv != nullptr;
+    DevBuf kv_dense[2], kv_pad[2], st, tok, qb, qp, ob;
+    const void *dense[2] = {nullptr, nullptr};
+    if (xkv) {
+        DevBlob kb, vb;
+        if (int rc = prepare_blob(k_xkv, k_bytes, dim, seq, kb, s)) return rc;
+        if (int rc = prepare_blob(v_xkv, v_bytes, dim, seq, vb, s)) return rc;
+        if (int rc = check_split(kb.tok_start, kb.tokens, seq, n_threads, split_tokens)) return rc;
+        if (int rc = check_split(vb.tok_start, vb.tokens, seq, n_threads, split_tokens)) return rc;
+        if (kb.n_blocks != vb.n_blocks)
+            return fail(KVX_ERR_RUNTIME, "xkv K and V blocks cover different token counts");
+        KVX_CUDA(st.alloc(2 * sizeof(int), s));
+        KVX_CUDA(cudaMemsetAsync(st.p, 0, 2 * sizeof(int), s));
+        DevBlob *blobs[2] = {&kb, &vb};
+        for (int t = 0; t < 2; ++t) {
+            DevBlob &b = *blobs[t];
+            std::vector<uint32_t> ts(b.tok_start.begin(), b.tok_start.begin() + b.n_blocks);
+            DevBuf tk;
+            KVX_CUDA(tk.alloc(std::max<size_t>(ts.size(), 1) * 4, s));
+            KVX_CUDA(cudaMemcpyAsync(tk.p, ts.data(), ts.size() * 4, cudaMemcpyHostToDevice, s));
+            KVX_CUDA(kv_dense[t].alloc(size_t(seq) * dim * 2, s));
+            KVX_CUDA(launch_decode(b.ptr, b.idx.as<kvx_block>(), tk.as<uint32_t>(), b.n_blocks, dim,
+                                   seq, kv_dense[t].as<uint16_t>(), st.as<int>(), s));
+            KVX_CUDA(cudaStreamSynchronize(s));  // ts and tk go out of scope
+            dense[t] = kv_dense[t].p;
+        }
+        if (int rc = read_status(st.as<int>(), false)) return rc;
+    } else {
+        if (int rc = to_device(k_raw, size_t(seq) * dim * 2, kv_dense[0], dense[0], s)) return rc;
+        if (int rc = to_device(v_raw, size_t(seq) * dim * 2, kv_dense[1], dense[1], s)) return rc;
+    }
+    for (int t = 0; t < 2; ++t) {
+        KVX_CUDA(kv_pad[t].alloc(size_t(seq) * dp * 2, s));
+        KVX_CUDA(launch_pad_rows(static_cast<const uint16_t *>(dense[t]), seq, dim, dp,
+                                 kv_pad[t].as<uint16_t>(), s));
+    }
+    const void *qd = nullptr;
+    if (int rc = to_device(q, size_t(n_q) * dim * 2, qb, qd, s)) return rc;
+    KVX_CUDA(qp.alloc(size_t(n_q) * dp * 2, s));
+    KVX_CUDA(launch_pad_rows(static_cast<const uint16_t *>(qd), n_q, dim, dp, qp.as<uint16_t>(), s));
+    KVX_CUDA(ob.alloc(size_t(n_q) * dp * 4, s));
+    kvx_unit u{};
+    u.k = kv_pad[0].p;
+    u.v = kv_pad[1].p;
+    u.q = qp.as<uint16_t>();
+    u.out = ob.as<float>();
+    u.seq = seq;
+    std::vector<kvx_unit> us{u};
+    if (int rc = run_units(us, n_q, dp, std::min(split_tokens, 255), s)) return rc;
+    // the first dim columns of each output row
+    KVX_CUDA(cudaMemcpy2D(out, size_t(dim) * 4, ob.p, size_t(dp) * 4, size_t(dim) * 4, size_t(n_q),
+                          is_device_ptr(out) ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost));
+    g_err.clear();
+    return KVX_OK;
+}
+
 int run_units(std::vector<kvx_unit> &units, int n_q, int dim, int block_tokens, cudaStream_t s) {
     KVX_CUDA(cudaStreamSynchronize(s));
     kvx_plan plan = nullptr;
@@ -732,6 +804,9 @@ extern "C" int kvx_attention_decode(int backend, const uint16_t *q, const uint16
                                       split_tokens))
         return rc;
     if (int rc = check_device()) return rc;
+    if (!attention_dim_supported(dim))
+        return attention_decode_padded(q, k_raw, v_raw, k_xkv, k_bytes, v_xkv, v_bytes, out, n_q,
+                                       dim, seq, n_threads, split_tokens);
     cudaStream_t s = nullptr;
     const bool xkv = k_xkv != nullptr;
     DevBlob kb, vb;
@@ -791,6 +866,9 @@ extern "C" int kvx_attention_decode_units(int backend, int n_units, const uint16
         if (int rc = check_attention_args(backend, q[u], nullptr, nullptr, k_xkv[u], v_xkv[u],
                                           out[u], n_q, dim, seq, split_tokens))
             return rc;
+    if (!attention_dim_supported(dim))
+        return fail(KVX_ERR_UNSUPPORTED,
+                    "kvexp_b200: head_dim must be 32, 64, 128 or 256 for the batched GPU kernels");
     if (int rc = check_device()) return rc;
     cudaStream_t s = nullptr;
     // One device arena for every host blob and query, copied with one transfer per buffer on the

@@ -373,9 +373,9 @@ __device__ __forceinline__ void qk_tiles(uint32_t xb, const uint32_t (&qb)[Cfg<D
     }
 }
 
-// O^T += V^T P^T for the 16-token tile at tile row r0 (P^T as B fragments: bh = bf16(p),
-// bm = bf16(p - bh), bl = bf16(p - bh - bm): three bf16 terms carry p's 24 significant bits, so the
-// tensor cores see the fp32 softmax weight exactly).  V^T A fragments by ldmatrix.trans: matrix i
+// O^T += V^T P^T for the 16-token tile at tile row r0 (P^T as B fragments: three bf16 terms
+// bh + bm + bl = p that carry p's 24 significant bits, so the tensor cores see the fp32 softmax
+// weight exactly).  V^T A fragments by ldmatrix.trans: matrix i
 // covers tokens 0-7 / 8-15 (i / 2) and head dims 0-7 / 8-15 (i % 2) of the m-tile.  The three
 // MMAs accumulate the smallest term first.
 template <int D>
@@ -678,22 +678,27 @@ __device__ __forceinline__ void tile_step(const AttnArgs &a, const BlockDesc &bd
     const float p1 = ex2(__fmul_rn(__fsub_rn(s[0][1], mn1), kLog2e));
     const float p2 = ex2(__fmul_rn(__fsub_rn(s[0][2], mn0), kLog2e));
     const float p3 = ex2(__fmul_rn(__fsub_rn(s[0][3], mn1), kLog2e));
-    // P^T B fragments: p = h + m + l exactly, h = bf16(p), m = bf16(p - h), l = bf16(p - h - m)
-    // (each difference is exact in fp32; 3 x 8 significant bits)
+    // P^T B fragments: p = h + m + l exactly, each term the upper 16 bits of what remains (h = p
+    // truncated to bf16, m = (p - h) truncated, l = p - h - m); the differences are exact in fp32
+    // and l has at most 8 significant bits, so the three bf16 terms carry all 24 bits of p.  Two
+    // weights pack into one B register with one byte permute.
     uint32_t bh[2], bm[2], bl[2];
     {
-        const uint32_t h01 = pack_bf16x2(p1, p0), h23 = pack_bf16x2(p3, p2);
-        const float r0 = __fsub_rn(p0, bf16lo_to_f32(h01)), r1 = __fsub_rn(p1, bf16hi_to_f32(h01));
-        const float r2 = __fsub_rn(p2, bf16lo_to_f32(h23)), r3 = __fsub_rn(p3, bf16hi_to_f32(h23));
-        const uint32_t m01 = pack_bf16x2(r1, r0), m23 = pack_bf16x2(r3, r2);
-        const float u0 = __fsub_rn(r0, bf16lo_to_f32(m01)), u1 = __fsub_rn(r1, bf16hi_to_f32(m01));
-        const float u2 = __fsub_rn(r2, bf16lo_to_f32(m23)), u3 = __fsub_rn(r3, bf16hi_to_f32(m23));
-        bh[0] = movm_t(h01);
-        bh[1] = movm_t(h23);
-        bm[0] = movm_t(m01);
-        bm[1] = movm_t(m23);
-        bl[0] = movm_t(pack_bf16x2(u1, u0));
-        bl[1] = movm_t(pack_bf16x2(u3, u2));
+        constexpr uint32_t HI = 0xFFFF0000u, PK = 0x7632u;  // PK: the upper halves of a and b
+        const uint32_t P0 = __float_as_uint(p0), P1 = __float_as_uint(p1);
+        const uint32_t P2 = __float_as_uint(p2), P3 = __float_as_uint(p3);
+        const float r0 = __fsub_rn(p0, __uint_as_float(P0 & HI)), r1 = __fsub_rn(p1, __uint_as_float(P1 & HI));
+        const float r2 = __fsub_rn(p2, __uint_as_float(P2 & HI)), r3 = __fsub_rn(p3, __uint_as_float(P3 & HI));
+        const uint32_t R0 = __float_as_uint(r0), R1 = __float_as_uint(r1);
+        const uint32_t R2 = __float_as_uint(r2), R3 = __float_as_uint(r3);
+        const float u0 = __fsub_rn(r0, __uint_as_float(R0 & HI)), u1 = __fsub_rn(r1, __uint_as_float(R1 & HI));
+        const float u2 = __fsub_rn(r2, __uint_as_float(R2 & HI)), u3 = __fsub_rn(r3, __uint_as_float(R3 & HI));
+        bh[0] = movm_t(prmt(P0, P1, PK));
+        bh[1] = movm_t(prmt(P2, P3, PK));
+        bm[0] = movm_t(prmt(R0, R1, PK));
+        bm[1] = movm_t(prmt(R2, R3, PK));
+        bl[0] = movm_t(prmt(__float_as_uint(u0), __float_as_uint(u1), PK));
+        bl[1] = movm_t(prmt(__float_as_uint(u2), __float_as_uint(u3), PK));
     }
     st.l0 = __fmaf_rn(st.l0, al0, __fadd_rn(p0, p2));
     st.l1 = __fmaf_rn(st.l1, al1, __fadd_rn(p1, p3));

@@ -759,6 +759,23 @@ cudaError_t launch_synth(uint16_t *out, int seq, int dim, uint64_t seed, uint64_
     return cudaGetLastError();
 }
 
+// [rows, dim] BF16 -> [rows, dp] BF16, columns dim .. dp-1 zero (dp >= dim).
+__global__ void pad_rows_kernel(const uint16_t *in, int64_t rows, int dim, int dp, uint16_t *out) {
+    const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= rows * dp) return;
+    const int64_t r = i / dp;
+    const int c = int(i - r * dp);
+    out[i] = c < dim ? in[r * dim + c] : uint16_t(0);
+}
+
+cudaError_t launch_pad_rows(const uint16_t *in, int64_t rows, int dim, int dp, uint16_t *out,
+                            cudaStream_t s) {
+    const int64_t n = rows * dp;
+    if (n <= 0) return cudaSuccess;
+    pad_rows_kernel<<<unsigned((n + 255) / 256), 256, 0, s>>>(in, rows, dim, dp, out);
+    return cudaGetLastError();
+}
+
 cudaError_t launch_read_probe(const uint4 *buf, size_t n16, uint32_t *sink, int grid,
                               cudaStream_t s) {
     read_probe_kernel<<<grid, 512, 0, s>>>(buf, n16, sink);

@@ -44,6 +44,10 @@ cudaError_t launch_encode_emit(const uint16_t *const *tensors, int n_tensors, in
                                const uint64_t *block_off, uint8_t *arena, kvx_block *index,
                                const uint64_t *blob_off, int *status, cudaStream_t s);
 
+// [rows, dim] BF16 -> [rows, dp] BF16 with zero columns past dim.
+cudaError_t launch_pad_rows(const uint16_t *in, int64_t rows, int dim, int dp, uint16_t *out,
+                            cudaStream_t s);
+
 cudaError_t launch_synth(uint16_t *out, int seq, int dim, uint64_t seed, uint64_t stream_id,
                          int profile, uint32_t rate, cudaStream_t s);
 cudaError_t launch_read_probe(const uint4 *buf, size_t n16, uint32_t *sink, int grid,

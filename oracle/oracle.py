@@ -48,6 +48,8 @@ def build(ref_root: str | None = None) -> None:
     subprocess.run(["make", "-s", "-C", HERE, "all"], check=True)
     if os.path.isdir(ref_root):
         subprocess.run(["make", "-s", "-C", HERE, "ref", f"REF_ROOT={ref_root}"], check=True)
+        # the reference's own test program over the GPU library (needs the library built first)
+        subprocess.run(["make", "-s", "-C", HERE, "shimtest", f"REF_ROOT={ref_root}"], check=True)
 
 
 def _ptr(a, t):

@@ -104,3 +104,18 @@ def test_encode_argument_errors_mirror_the_reference(kvx, oracle, seq, dim, bloc
         oracle.encode_raw_args(x.ctypes.data_as(O._u16p), seq, dim, block)
     assert r.value.code == 1
     assert str(e.value) == str(r.value)
+
+
+def test_shim_compiles_against_reference_headers():
+    """The drop-in shim (the reference's kvexp:: API over the C ABI) compiles against the
+    reference's own public headers, where a reference checkout is present."""
+    import subprocess
+    import oracle as O
+    ref = O.default_ref_root()
+    if not os.path.isdir(os.path.join(ref, "include", "kvexp")):
+        pytest.skip("no reference checkout on this host")
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    shim = os.path.join(root, "compressed-kv-attention_b200", "shim", "kvexp_gpu_shim.cpp")
+    subprocess.run(["g++", "-std=c++20", "-fsyntax-only", "-Wall", "-Werror",
+                    "-I" + os.path.join(ref, "include"), "-I" + os.path.join(root, "include"), shim],
+                   check=True)

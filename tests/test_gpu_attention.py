@@ -159,6 +159,25 @@ def test_raw_blocks(kvx, cuda, oracle):
     assert_attention_close(g_xkv, cpu, q, k, v, "raw blocks")
 
 
+@pytest.mark.parametrize("backend,dim,n_q,seq,block", [
+    (0, 8, 3, 200, 64), (1, 16, 1, 40, 16), (0, 24, 4, 333, 128), (1, 40, 7, 1000, 128),
+    (2, 96, 4, 700, 128), (0, 200, 2, 300, 128), (2, 160, 3, 129, 128),
+])
+def test_padded_head_dims(kvx, cuda, oracle, backend, dim, n_q, seq, block):
+    """Head dims the reference's backends take but the fused kernels do not (any multiple of 8,
+    of 32 for AVX-512): the drop-in call runs them zero-padded to the next fused width, raw and XKV
+    inputs bit-identical, within tolerance of the oracle."""
+    k = S.synth_bf16(9, 0, seq, dim, S.PROFILE_K)
+    v = S.synth_bf16(9, 1, seq, dim, S.PROFILE_V)
+    q = soften(S.synth_bf16(9, 2, n_q, dim, S.PROFILE_Q), 8)
+    kx, vx = oracle.encode(k, block), oracle.encode(v, block)
+    g_raw = _gpu(kvx, q, k, v, seq=seq, split=block, backend=backend)
+    g_xkv = _gpu(kvx, q, kx=kx, vx=vx, seq=seq, split=block, backend=backend)
+    assert np.array_equal(_bits(g_raw), _bits(g_xkv))
+    cpu = oracle.attention(q, kx=kx, vx=vx, seq=seq, split=block)
+    assert_attention_close(g_xkv, cpu, q, k, v, f"padded dim={dim}")
+
+
 def test_identity_token(kvx, cuda):
     """seq 1, q = k = 1.0: out == v exactly (tests/test_main.cpp:102-122, at dim 32)."""
     dim = 32
