@@ -8,8 +8,8 @@
 //    (one CTA per SM).  A CTA streams its blocks through a shared-memory ring of stages; a stage
 //    is up to TSB tokens of one block: the block's descriptor, and per tensor its base exponents,
 //    sign/mantissa rows, packed residual codes and the escape-record entries of those tokens (or
-//    raw BF16 rows).  One producer warp issues the stage as a handful of 1-D bulk copies of the
-//    TMA engine that complete on the slot's "full" mbarrier; only the compressed bytes cross HBM
+//    raw BF16 rows).  Two producer warps (alternate stages) issue a stage as a handful of 1-D bulk
+//    copies of the TMA engine, one per lane, that complete on the slot's "full" mbarrier; only the compressed bytes cross HBM
 //    (plus, for a coded block with escapes, its escape record: 4 bytes per escape word and a
 //    64-byte count header, built once per plan).
 //  * The consumer warps (15, or 7 at D = 256) share every stage: the stage's 16-token tiles go round-robin
@@ -88,7 +88,8 @@ template <int D> struct Cfg {
     static constexpr int O_TILE = NSLOT * SLOT;
     static constexpr int O_BAR = O_TILE + NW * TILE;  // full[NSLOT], then empty[NSLOT]
     static constexpr int SMEM = O_BAR + 16 * NSLOT;
-    static constexpr int THREADS = 32 * (NW + 1);
+    static constexpr int NP = 2;                  // producer warps (stages alternate between them)
+    static constexpr int THREADS = 32 * (NW + NP);
     static_assert(SMEM + 16 <= 232448, "stage ring and tiles exceed shared memory");
     static_assert(NW >= TPS, "a consumer warp takes at most one tile of a stage");
     static_assert(32 % C8 == 0 && NIT >= 1, "a warp step covers whole rows");
@@ -163,7 +164,8 @@ __device__ __forceinline__ uint32_t merge(uint32_t sg, uint32_t cw, uint32_t b7)
 }
 
 // How this lane reads one tensor of the current block from a ring stage: the 8-element chunk c8
-// (head dims 8 c8 .. 8 c8 + 7) of rows t0 + RPI k.  Row sections start m = 0 or 2 bytes past a
+// (head dims 8 c8 .. 8 c8 + 7) of rows t0 + RPI k.  The residual codes start in the 16-byte line at
+// code_base (the codes' own copy, or right behind the rows when rows and codes came as one).  Row sections start m = 0 or 2 bytes past a
 // 4-byte boundary of the ring; the chunk adds a multiple of 4 to the sign/mantissa and raw rows,
 // and 4 (4-bit) or 2 (2-bit) bytes per chunk to the residual rows.
 struct Lay {
@@ -175,7 +177,8 @@ struct Lay {
 };
 // rd / cd: data offsets of the block's row and code pieces.
 template <int D>
-__device__ __forceinline__ Lay make_lay(uint32_t rd, uint32_t cd, int mode, int c8, bool bf16) {
+__device__ __forceinline__ Lay make_lay(uint32_t rd, uint32_t cd, int mode, int c8, bool bf16,
+                                       uint32_t code_base) {
     // Every offset in a blob is even, so a section starts 0 or 2 bytes past a 4-byte boundary and
     // each selector is one of two constants.
     Lay l;
@@ -186,7 +189,7 @@ __device__ __forceinline__ Lay make_lay(uint32_t rd, uint32_t cd, int mode, int 
     l.rows = (rd & ~3u) + uint32_t((bf16 || mode == 0) ? 16 * c8 : 8 * c8);
     const uint32_t cb = (cd & 3u) + uint32_t(c8 * (mode == 0 ? 0 : mode));
     l.cs = (cb & 2u) != 0u ? shift4(2) : shift4(0);
-    l.codes = uint32_t(Cfg<D>::CODE_OFF) + (cd & ~3u) + (cb & ~3u);
+    l.codes = code_base + (cd & ~3u) + (cb & ~3u);
     return l;
 }
 
@@ -478,13 +481,14 @@ __device__ __forceinline__ int pdesc_esc(const uint4 (&e)[4], int T, int i) {
     return int((r >> (16 * ((i - 1) & 1))) & 0xFFFFu);
 }
 
-// The producer warp: for every stage of the CTA's blocks, wait until the slot is free, issue the
-// stage's copies and announce their byte count on the slot's full barrier (lane 0).  Lane l holds
+// A producer warp (one of NP; producer pw takes the stages gs with gs mod NP == pw): for each of
+// its stages of the CTA's blocks, wait until the slot is free, issue the stage's copies and
+// announce their byte count on the slot's full barrier (lane 0).  Lane l holds
 // the descriptor of block base + l; the next 32 are loaded while the current 32 are issued, so
 // the issuing lane never waits on a global load.  On a timeout it reports DERR_TIMEOUT and waits
 // (bounded) for the copies it issued before it returns.
 template <int D, bool BF16IN>
-__device__ void producer(const AttnArgs &a, uint8_t *smem, int fb0, int fb1, int lane) {
+__device__ void producer(const AttnArgs &a, uint8_t *smem, int fb0, int fb1, int pw, int lane) {
     using C = Cfg<D>;
     constexpr bool MULTI = C::TSB < 128;  // a 128-token block takes several stages
     const uint32_t sb = smem_u32(smem);
@@ -515,6 +519,10 @@ __device__ void producer(const AttnArgs &a, uint8_t *smem, int fb0, int fb1, int
                 }
             };
             for (int t0 = 0; t0 < valid; t0 += C::TSB) {
+                if (gs % C::NP != pw) {  // the other producer warp's stage
+                    ++gs;
+                    continue;
+                }
                 const int slot = gs % C::NSLOT;
                 const uint32_t full = ring_bar<D>(sb, slot), empty = ring_bar<D>(sb, C::NSLOT + slot);
                 if (gs >= C::NSLOT &&
@@ -532,42 +540,55 @@ __device__ void producer(const AttnArgs &a, uint8_t *smem, int fb0, int fb1, int
                         eb[T] = esc_count(T, min(16, (t0 + C::TSB) >> 4));
                     }
                 }
+                // The stage's pieces go out in parallel, one per lane: 0 the descriptor, 1 the merge
+                // words, 2 + 3 T the rows of tensor T (with its residual codes when the stage is the
+                // whole block: they follow the rows in the blob), 3 + 3 T its codes otherwise, 4 + 3 T
+                // its escape-record entries.  Lane 0 then tells the slot's barrier the byte count; the
+                // barrier's tx-count may run below zero until then, and the phase cannot complete
+                // before that arrive.
+                const bool whole = t0 == 0 && n == n_tok;
+                const uint32_t dslot = sb + uint32_t(slot * C::SLOT);
+                const uint8_t *src = nullptr;
+                uint32_t len = 0u, dst = 0u;
                 if (lane == 0) {
-                    // Each piece goes out as soon as it is known; the slot's barrier learns the
-                    // stage's byte count after them (its tx-count may run below zero meanwhile;
-                    // the phase cannot complete before this arrive).
-                    const uint32_t dslot = sb + uint32_t(slot * C::SLOT);
-                    uint32_t total = stage_piece(dslot, reinterpret_cast<const uint8_t *>(gd),
-                                                 uint32_t(sizeof(BlockDesc)), full);
-                    if (!BF16IN && (km | vm) != 0)
-                        total += stage_piece(dslot + C::S_B7,
-                                             reinterpret_cast<const uint8_t *>(a.b7 + size_t(b7_block) * D),
-                                             uint32_t(4 * D), full);
-#pragma unroll
-                    for (int T = 0; T < 2; ++T) {
-                        const uint8_t *blk = gptr(T ? vp : kp);
-                        const int mode = T ? vm : km;
-                        const uint32_t reg = dslot + uint32_t(C::S_T + T * C::T_BYTES);
+                    src = reinterpret_cast<const uint8_t *>(gd), len = uint32_t(sizeof(BlockDesc)), dst = dslot;
+                } else if (lane == 1) {
+                    if (!BF16IN && (km | vm) != 0) {
+                        src = reinterpret_cast<const uint8_t *>(a.b7 + size_t(b7_block) * D);
+                        len = uint32_t(4 * D), dst = dslot + C::S_B7;
+                    }
+                } else if (lane < 8) {
+                    const int T = (lane - 2) / 3, part = (lane - 2) % 3;
+                    const uint8_t *blk = gptr(T ? vp : kp);
+                    const int mode = T ? vm : km;
+                    const uint32_t reg = dslot + uint32_t(C::S_T + T * C::T_BYTES);
+                    if (part == 0) {
+                        dst = reg;
                         if (BF16IN) {
-                            total += stage_piece(reg, blk + size_t(t0) * 2 * D, uint32_t(n * 2 * D), full);
+                            src = blk + size_t(t0) * 2 * D, len = uint32_t(n * 2 * D);
                         } else if (mode == 0) {
-                            total += stage_piece(reg, blk + kHeaderBytes + size_t(t0) * 2 * D,
-                                                 uint32_t(n * 2 * D), full);
+                            src = blk + kHeaderBytes + size_t(t0) * 2 * D, len = uint32_t(n * 2 * D);
                         } else {
-                            const uint8_t *rows = blk + kHeaderBytes + D;
-                            total += stage_piece(reg, rows + size_t(t0) * D, uint32_t(n * D), full);
-                            total += stage_piece(reg + C::CODE_OFF,
-                                                 rows + size_t(n_tok) * D + size_t(t0) * D * mode / 8,
-                                                 uint32_t(n * D * mode / 8), full);
-                            if (eb[T] > ea[T] && eb[T] - ea[T] <= C::ESC_CAP)
-                                total += stage_piece(reg + C::E_OFF,
-                                                     reinterpret_cast<const uint8_t *>(
-                                                         a.esc + (T ? vrec : krec) + kEscRecHead + ea[T]),
-                                                     uint32_t(4 * (eb[T] - ea[T])), full);
+                            src = blk + kHeaderBytes + D + size_t(t0) * D;
+                            len = uint32_t(n * D + (whole ? n * D * mode / 8 : 0));
+                        }
+                    } else if (!BF16IN && mode != 0) {
+                        if (part == 1) {
+                            if (!whole) {
+                                src = blk + kHeaderBytes + D + size_t(n_tok) * D + size_t(t0) * D * mode / 8;
+                                len = uint32_t(n * D * mode / 8), dst = reg + C::CODE_OFF;
+                            }
+                        } else {
+                            const int e0 = T ? ea[1] : ea[0], e1 = T ? eb[1] : eb[0];
+                            if (e1 > e0 && e1 - e0 <= C::ESC_CAP) {
+                                src = reinterpret_cast<const uint8_t *>(a.esc + (T ? vrec : krec) + kEscRecHead + e0);
+                                len = uint32_t(4 * (e1 - e0)), dst = reg + C::E_OFF;
+                            }
                         }
                     }
-                    mbar_arrive_expect_tx(full, total);
                 }
+                const uint32_t total = __reduce_add_sync(FULL, stage_piece(dst, src, len, full));
+                if (lane == 0) mbar_arrive_expect_tx(full, total);
                 __syncwarp();
                 ++gs;
             }
@@ -577,7 +598,8 @@ __device__ void producer(const AttnArgs &a, uint8_t *smem, int fb0, int fb1, int
     if (!ok && lane == 0) {
         // let the copies already issued land before this CTA's shared memory goes away
         for (int s = max(0, gs - C::NSLOT); s < gs; ++s)
-            mbar_wait_bounded(ring_bar<D>(sb, s % C::NSLOT), uint32_t((s / C::NSLOT) & 1), kStageWaitUs);
+            if (s % C::NP == pw)
+                mbar_wait_bounded(ring_bar<D>(sb, s % C::NSLOT), uint32_t((s / C::NSLOT) & 1), kStageWaitUs);
     }
 }
 
@@ -593,7 +615,11 @@ __device__ __forceinline__ void tile_tensor(const AttnArgs &a, const BlockDesc &
     using C = Cfg<D>;
     const int c8 = lane % C::C8;
     const uint32_t rd = al & 15u, cd = (al >> 8) & 15u;
-    const Lay ly = make_lay<D>(rd, cd, mode, c8, bf16);
+    // a whole block in one stage came as one copy: the codes follow its n rows
+    const int n = min(C::TSB, int(bd.valid) - t0);
+    const bool whole = t0 == 0 && n == int(bd.n_tok);
+    const uint32_t code_base = whole ? ((rd + uint32_t(n * D)) & ~15u) : uint32_t(C::CODE_OFF);
+    const Lay ly = make_lay<D>(rd, cd, mode, c8, bf16, code_base);
     const uint32_t rb = reg + uint32_t(TT * tw * (mode == 0 ? 2 * D : D));
     const uint32_t cb = reg + uint32_t(TT * tw * (D * mode / 8));
     if (mode != 0) {
@@ -836,8 +862,8 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1) attn_kernel(const AttnArgs
     }
     __syncthreads();
     if (skip != 0) return;
-    if (warp == C::NW) {
-        producer<D, BF16IN>(a, smem, fb0, fb1, lane);
+    if (warp >= C::NW) {
+        producer<D, BF16IN>(a, smem, fb0, fb1, warp - C::NW, lane);
         return;
     }
     consumer<D, BF16IN>(a, smem, warp, lane, fb0, fb1, a.seg_base[c]);

@@ -52,12 +52,12 @@ __host__ __device__ inline uint32_t esc_scratch_slot(int dim, int T, int r, int 
     return uint32_t(r * 2 * dim + ((c8 ^ sw) << 4) + 2 * (c & 7));
 }
 
-// Consumer warps per CTA of the attention kernel (one CTA per SM; one more warp issues the copies):
-// a CTA of 16 warps at 128 registers a thread for dim <= 64, 12 at 168 for dim 128, 8 at 255 for
-// dim 256.  A stage of 128 tokens (64 at dim 128, 32 at dim 256) is 8 (4, 2) tiles, dealt round
-// robin; each consumer warp takes at most one tile of a stage.
+// Consumer warps per CTA of the attention kernel (one CTA per SM; two more warps issue the
+// copies): a CTA of 16 warps at 128 registers a thread for dim <= 64, 12 at 168 for dim 128, 8 at
+// 255 for dim 256.  A stage of 128 tokens (64 at dim 128, 32 at dim 256) is 8 (4, 2) tiles, dealt
+// round robin; each consumer warp takes at most one tile of a stage.
 __host__ __device__ constexpr int attention_consumer_warps(int dim) {
-    return dim >= 256 ? 7 : (dim >= 128 ? 11 : 15);
+    return dim >= 256 ? 6 : (dim >= 128 ? 10 : 14);
 }
 
 __device__ __forceinline__ FlatBlock load_flat(const FlatBlock *f, int64_t i) {

@@ -28,7 +28,8 @@ class Config:
     v_profile: int = S.PROFILE_V
     layer0_k_profile: int | None = None
     block: int = 128
-    # How N GPUs share the workload: "replica" (each GPU its own full cache), "units" (the
+    # How N GPUs share the workload: "split" (the (layer, KV head) units dealt out in contiguous
+    # runs, one per GPU: strong scaling), "replica" (each GPU its own full cache), "units" (the
     # (layer, KV head, sequence) units split over 8 GPU slots) or "sequence" (every KV head's
     # sequence cut into block-aligned shards, folded by log-sum-exp).
     shard: str = "replica"
@@ -45,9 +46,9 @@ class Config:
 CONFIGS = {
     0: Config("config[0]: 1L x 1KV x GQA7 x D64 x S8192", 1, 1, 7, 64, 8192),
     1: Config("config[1]: 24L x 2KV x GQA7 x D64 x S32768 (Qwen2.5-0.5B shape)", 24, 2, 7, 64,
-              32768, layer0_k_profile=S.PROFILE_NARROW),
+              32768, layer0_k_profile=S.PROFILE_NARROW, shard="split"),
     2: Config("config[2]: config[1] shape at S32731 (91-token tail block)", 24, 2, 7, 64, 32731,
-              layer0_k_profile=S.PROFILE_NARROW),
+              layer0_k_profile=S.PROFILE_NARROW, shard="split"),
     3: Config("config[3]: 32L x 8KV x GQA4 x D128 x 64 seqs x S32768 (Llama-3-8B shape)", 32, 8,
               4, 128, 32768, seqs=64, shard="units"),
     4: Config("config[4]: 1L x 8KV x GQA4 x D256 x S1048576", 1, 8, 4, 256, 1 << 20,

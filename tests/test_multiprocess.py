@@ -3,7 +3,8 @@
   * config[4]'s sequence split: two ranks attend over their block-aligned halves of a sequence
     (float64 numpy attention stands in for the GPU kernel), all-gather (out, lse) and fold; the
     result equals single-rank attention over the whole sequence;
-  * config[1]/[3]'s unit sharding: the ranks' unit sets are disjoint and cover every unit.
+  * bench.py's unit sharding of config[1]/[2] (strong) and config[3] (8 shards): the ranks' unit
+    sets are disjoint, and for config[1]/[2] cover every unit.
 """
 import os
 import socket
@@ -92,3 +93,34 @@ def test_fold_is_exact_for_one_rank_and_weights_by_normaliser():
     got = seqsplit.fold(o, lse)
     np.testing.assert_allclose(got.numpy(), [[2.5, 4.25]])  # (1*o0 + 3*o1) / 4
     np.testing.assert_allclose(seqsplit.fold(o[:1], lse[:1]).numpy(), o[0].numpy())
+
+
+@pytest.mark.parametrize("config,world", [(1, 1), (1, 2), (1, 3), (1, 8), (2, 8), (1, 48), (3, 8)])
+def test_unit_shards_cover_the_config(config, world):
+    """bench.py's unit sharding: config[1]/[2] split their (layer, KV head) units over the ranks
+    (contiguous runs, sizes within one, one seed: the ranks together hold exactly the config);
+    config[3] gives rank r shard r of 8.  Disjoint in every case."""
+    import sys
+    sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    import bench
+    import workloads as W
+    cfg = W.CONFIGS[config]
+    shares = [bench.rank_share(cfg, r, world) for r in range(world)]
+    ids = [s[1] for s in shares]
+    flat = [u for x in ids for u in x]
+    assert len(flat) == len(set(flat))
+    if cfg.shard == "split":
+        assert sorted(flat) == list(range(cfg.units))
+        assert max(map(len, ids)) - min(map(len, ids)) <= 1
+        assert len({s[2] for s in shares}) == 1
+    else:
+        assert len(flat) == world * (cfg.units // bench.GPU_SLOTS)
+
+
+def test_unit_split_refuses_more_ranks_than_units():
+    import sys
+    sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    import bench
+    import workloads as W
+    with pytest.raises(SystemExit):
+        bench.rank_share(W.CONFIGS[1], 48, 49)
