@@ -46,6 +46,9 @@ def parse():
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--config", type=int, default=1)
+    ap.add_argument("--seq", type=int, default=0,
+                    help="attend this many tokens instead of the config's (config[2]'s prefix "
+                         "sweep: 8192, 16384, 32731)")
     ap.add_argument("--impl", default="kvx", choices=["kvx", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
@@ -57,6 +60,16 @@ def parse():
                     help="only the first N units of this GPU's share (small cases for profilers; "
                          "not a bench line of the config)")
     return ap.parse_args()
+
+
+def config_of(args):
+    """BASELINE.json config[args.config], at args.seq tokens when given."""
+    import dataclasses
+    import workloads as W
+    cfg = W.CONFIGS[args.config]
+    if args.seq > 0:
+        cfg = dataclasses.replace(cfg, seq=args.seq, name=f"{cfg.name} at S{args.seq}")
+    return cfg
 
 
 def env_rank():
@@ -148,9 +161,32 @@ class ClockSampler:
 
 # ---- CPU reference timing ------------------------------------------------------------------------
 
-def cpu_reference_rate(qs, ks, vs, cfg, seconds, max_passes=50):
-    """Time the reference library's model_heads loop (oracle/_ref) on all usable host cores;
-    falls back to the C restatement (oracle/) when the reference was not built."""
+BACKEND_NAMES = {0: "scalar", 1: "AVX2", 2: "AVX-512 BF16"}
+
+
+def ref_backends(ref):
+    """The reference's backends this host runs, fastest first (AVX-512 BF16, AVX2, scalar)."""
+    import oracle as O
+    out = [b for b, ok in ((O.AVX512BF16, ref.avx512_bf16), (O.AVX2, ref.avx2)) if ok]
+    return out or [O.SCALAR]
+
+
+def make_ref_step(ref, be, qs, ks, vs, outs, cfg, threads, cores):
+    """One pass of the reference over the units: its model_heads scope (one OpenMP thread per
+    (layer, KV head) unit, src/bench.cpp:711-728), or for a single unit its head scope (one
+    attention_decode over every core, the sequence split at the 128-token blocks)."""
+    if len(qs) == 1:
+        def step():
+            outs[0][...] = ref.attention(qs[0], kx=ks[0], vx=vs[0], seq=cfg.seq, backend=be,
+                                         threads=cores, split=cfg.block)
+        return step
+    return lambda: ref.model_heads(be, qs, ks, vs, outs, cfg.group, cfg.dim, cfg.seq, threads)
+
+
+def cpu_reference_rate(qs, ks, vs, cfg, seconds, max_passes=50, backend=None):
+    """Time the reference library's model_heads loop (oracle/_ref) on all usable host cores with
+    `backend` (default: the fastest this host runs); falls back to the C restatement (oracle/)
+    when the reference was not built."""
     import numpy as np
     import oracle as O
     n = len(qs)
@@ -159,9 +195,11 @@ def cpu_reference_rate(qs, ks, vs, cfg, seconds, max_passes=50):
     threads = max(1, min(n, os.cpu_count() or 1))
     ref = O.reference()
     if ref is not None:
-        be = O.AVX512BF16 if ref.avx512_bf16 else (O.AVX2 if ref.avx2 else O.SCALAR)
-        bname = {O.AVX512BF16: "AVX-512 BF16", O.AVX2: "AVX2", O.SCALAR: "scalar"}[be]
-        run = lambda: ref.model_heads(be, qs, ks, vs, outs, cfg.group, cfg.dim, cfg.seq, threads)
+        be = backend if backend is not None else ref_backends(ref)[0]
+        bname = BACKEND_NAMES[be]
+        run = make_ref_step(ref, be, qs, ks, vs, outs, cfg, threads, os.cpu_count() or 1)
+        if n == 1:
+            threads = os.cpu_count() or 1
         kind = "reference"
         what = f"reference kvexp model_heads, {bname}, {threads} OpenMP threads"
     else:
@@ -215,8 +253,7 @@ def host_workload(cfg, seed, n_units=None):
 def run_reference(args, rank, world):
     if rank != 0:
         return
-    import workloads as W
-    cfg = W.CONFIGS[args.config]
+    cfg = config_of(args)
     # a workload too large for host memory is timed on its first units (the metric is per byte)
     per_unit = 4 * cfg.seq * cfg.dim
     n_units = cfg.units if cfg.units * per_unit <= 8 << 30 else max(1, (4 << 30) // per_unit)
@@ -229,30 +266,45 @@ def run_reference(args, rank, world):
         return
     n = len(qs)
     outs = [np.zeros((cfg.group, cfg.dim), dtype=np.float32) for _ in range(n)]
-    threads = max(1, min(n, os.cpu_count() or 1))
-    be = O.AVX512BF16 if ref.avx512_bf16 else (O.AVX2 if ref.avx2 else O.SCALAR)
-    bname = {O.AVX512BF16: "AVX-512 BF16", O.AVX2: "AVX2", O.SCALAR: "scalar"}[be]
+    cores = os.cpu_count() or 1
+    threads = cores if n == 1 else max(1, min(n, cores))
     total = sum(k.size for k in ks) + sum(v.size for v in vs)
-    step = lambda: ref.model_heads(be, qs, ks, vs, outs, cfg.group, cfg.dim, cfg.seq, threads)
-    # a step is one model_heads pass; keep the run within a few minutes
-    for _ in range(max(1, args.warmup)):
+
+
+    def timed(be, budget_s):
+        step = make_ref_step(ref, be, qs, ks, vs, outs, cfg, threads, cores)
+        # a step is one model_heads pass; keep the run within a few minutes
+        for _ in range(max(1, args.warmup)):
+            step()
+        t0 = time.perf_counter()
         step()
-    t0 = time.perf_counter()
-    step()
-    one = time.perf_counter() - t0
-    steps = max(1, min(args.steps, int(120.0 / max(one, 1e-6))))
-    t0 = time.perf_counter()
-    for _ in range(steps):
-        step()
-    el = time.perf_counter() - t0
+        one = time.perf_counter() - t0
+        steps = max(1, min(args.steps, int(budget_s / max(one, 1e-6))))
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            step()
+        el = time.perf_counter() - t0
+        return steps, el
+
+    backends = ref_backends(ref)
+    be = backends[0]
+    bname = BACKEND_NAMES[be]
+    steps, el = timed(be, 90.0)
     gbps = total * steps / el / 1e9
+    others = {}
+    for b in backends[1:]:
+        st2, el2 = timed(b, 45.0)
+        others[BACKEND_NAMES[b]] = {"value": total * st2 / el2 / 1e9, "unit": "GB/s",
+                                    "ms_per_step": el2 / st2 * 1e3, "steps": st2}
     line = {
         "metric": METRIC, "impl": "reference", "value": gbps, "unit": "GB/s", "n_gpus": world,
         "steps": steps, "warmup": max(1, args.warmup), "ms_per_step": el / steps * 1e3,
-        "higher_is_better": True, "scaling": "weak",
+        "higher_is_better": True,
+        "scaling": "strong" if cfg.shard in ("sequence", "split") else "weak",
         "vs_baseline": gbps / PUBLISHED_GBPS, "dtype": "bf16", "data": "synthetic",
         "config": {"workload": cfg.name, "units": n, "compressed_bytes_per_step": total,
                    "units_of_workload": cfg.units, "backend": bname, "threads": threads},
+        "other_backends": others,
         "cpu_baseline": {"value": gbps, "unit": "GB/s", "cores": threads, "kind": "reference",
                          "sample": f"{steps} model_heads passes over {n} of {cfg.units} units, "
                                    f"{bname}"},
@@ -372,7 +424,7 @@ def run_kvx(args, rank, world, local):
     import kvexp_b200 as kvx
     import seqsplit
     import workloads as W
-    full = W.CONFIGS[args.config]
+    full = config_of(args)
     cfg, unit_ids, seed, parallelism = rank_share(full, rank, world)
     if args.units > 0:
         unit_ids = list(unit_ids if unit_ids is not None else range(cfg.units))[: args.units]
@@ -540,7 +592,12 @@ def run_kvx(args, rank, world, local):
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        import oracle as O
         cpu, _ = cpu_reference_rate(qs, ks, vs, cfg, args.cpu_seconds)
+        ref = O.reference()
+        if ref is not None and ref.avx2 and ref.avx512_bf16:
+            avx2, _ = cpu_reference_rate(qs, ks, vs, cfg, args.cpu_seconds / 2, backend=O.AVX2)
+            cpu["avx2"] = {"value": avx2["value"], "unit": "GB/s", "sample": avx2["sample"]}
 
     launches = K * plans[0].launches + (K if exch is not None else 0)
     for p in plans:

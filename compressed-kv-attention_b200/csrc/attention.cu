@@ -68,7 +68,7 @@ template <int D> struct Cfg {
     static constexpr int TSB = cmin(128, 8192 / D);  // tokens per ring stage
     static constexpr int TPS = TSB / TT;          // tiles per stage
     static constexpr int NW = attention_consumer_warps(D);  // consumer warps
-    static constexpr int NSLOT = 4;               // ring slots
+    static constexpr int NSLOT = D >= 128 ? 3 : 4;  // ring slots
     // Escape-record entries of one tensor that a stage stages (12.5 % of its elements); a stage
     // with more leaves them in HBM, where the consumers read them.
     static constexpr int ESC_CAP = TSB * D / 8;
@@ -80,13 +80,16 @@ template <int D> struct Cfg {
     static constexpr int E_OFF = R_BYTES;
     static constexpr int T_BYTES = round16(E_OFF + 4 * ESC_CAP + 32);
     // A slot: the block descriptor (128 bytes), the block's merge words (K then V, 2 D bytes each),
-    // then the K and V regions.
+    // the stage's escape words, then the K and V regions.
     static constexpr int S_B7 = 128;
-    static constexpr int S_T = S_B7 + 4 * D;
+    // Two words the producer writes for the stage: per tensor, the shared address (bit 0 set) from
+    // which the stage's staged escape-record entry i is read at + 4 i, or 0 when they stay in HBM.
+    static constexpr int S_INFO = S_B7 + 4 * D;
+    static constexpr int S_T = S_INFO + 16;
     static constexpr int SLOT = S_T + 2 * T_BYTES;
-    static constexpr int TILE = TT * 2 * D;       // one consumer warp's BF16 tile
+    static constexpr int TILE = TT * 2 * D;       // one BF16 tile; a consumer warp has a K and a V tile
     static constexpr int O_TILE = NSLOT * SLOT;
-    static constexpr int O_BAR = O_TILE + NW * TILE;  // full[NSLOT], then empty[NSLOT]
+    static constexpr int O_BAR = O_TILE + NW * 2 * TILE;  // full[NSLOT], then empty[NSLOT]
     static constexpr int SMEM = O_BAR + 16 * NSLOT;
     static constexpr int NP = 2;                  // producer warps (stages alternate between them)
     static constexpr int THREADS = 32 * (NW + NP);
@@ -281,7 +284,7 @@ __device__ __forceinline__ void build_chunk(const Lay &ly, const uint32_t (&b7)[
 
 // Chunk steps [K0, NIT) in groups of G: the loads of the next group are issued before the
 // current group's arithmetic and stores (the shared-memory accesses keep their written order).
-template <int D, int MODE, int G, int K0>
+template <int D, int MODE, int G, int K0, int TO>
 __device__ __forceinline__ void decode_groups(uint32_t qr, uint32_t qc, const Lay &ly, const uint32_t (&b7)[4],
                                               const StoreMap<D> &sm, uint32_t (&W)[G][MODE == 0 ? 5 : 3],
                                               uint32_t (&X)[G][2]) {
@@ -292,14 +295,14 @@ __device__ __forceinline__ void decode_groups(uint32_t qr, uint32_t qc, const La
 #pragma unroll
     for (int g = 0; g < G; ++g) build_chunk<MODE>(ly, b7, W[g], X[g], w[g]);
 #pragma unroll
-    for (int g = 0; g < G; ++g) sts_v4(sm.at(K0 + g), w[g][0], w[g][1], w[g][2], w[g][3]);
-    if constexpr (K0 + G < NIT) decode_groups<D, MODE, G, K0 + G>(qr, qc, ly, b7, sm, Wn, Xn);
+    for (int g = 0; g < G; ++g) sts_v4(sm.at(K0 + g) + uint32_t(TO), w[g][0], w[g][1], w[g][2], w[g][3]);
+    if constexpr (K0 + G < NIT) decode_groups<D, MODE, G, K0 + G, TO>(qr, qc, ly, b7, sm, Wn, Xn);
 }
 
 // Rebuild this lane's chunks of one tensor's 16-token tile into the warp's BF16 tile (MODE 4 / 2
 // coded, 0 raw BF16).  rb / cb: the tile's rows / residual codes are at rb + ly.rows and
 // cb + ly.codes (plus the lane's row).
-template <int D, int MODE>
+template <int D, int MODE, int TO>
 __device__ __forceinline__ void decode_tile(uint32_t rb, uint32_t cb, const Lay &ly, const uint32_t (&b7)[4],
                                             const StoreMap<D> &sm, int lane) {
     using C = Cfg<D>;
@@ -310,16 +313,16 @@ __device__ __forceinline__ void decode_tile(uint32_t rb, uint32_t cb, const Lay 
     const uint32_t qc = cb + ly.codes + uint32_t(r0 * (D * MODE / 8));
     uint32_t W[G][MODE == 0 ? 5 : 3], X[G][2];
     load_chunks<D, MODE, G, 0>(qr, qc, W, X);
-    decode_groups<D, MODE, G, 0>(qr, qc, ly, b7, sm, W, X);
+    decode_groups<D, MODE, G, 0, TO>(qr, qc, ly, b7, sm, W, X);
 }
 
 // Zero this lane's chunks of tile rows at or past `from` (V rows past the block's valid tokens:
 // P is 0 there and V must be finite).
-template <int D, int J = 0>
+template <int D, int TO, int J = 0>
 __device__ __forceinline__ void zero_rows(const StoreMap<D> &sm, int from, int lane) {
     if constexpr (J < Cfg<D>::NIT) {
-        if (lane / Cfg<D>::C8 + J * StoreMap<D>::RPI >= from) sts_v4(sm.at(J), 0u, 0u, 0u, 0u);
-        zero_rows<D, J + 1>(sm, from, lane);
+        if (lane / Cfg<D>::C8 + J * StoreMap<D>::RPI >= from) sts_v4(sm.at(J) + uint32_t(TO), 0u, 0u, 0u, 0u);
+        zero_rows<D, TO, J + 1>(sm, from, lane);
     }
 }
 
@@ -588,7 +591,21 @@ __device__ void producer(const AttnArgs &a, uint8_t *smem, int fb0, int fb1, int
                     }
                 }
                 const uint32_t total = __reduce_add_sync(FULL, stage_piece(dst, src, len, full));
-                if (lane == 0) mbar_arrive_expect_tx(full, total);
+                if (lane == 0) {
+                    if (!BF16IN) {
+#pragma unroll
+                        for (int T = 0; T < 2; ++T) {
+                            const int e0 = T ? ea[1] : ea[0], e1 = T ? eb[1] : eb[0];
+                            const uint32_t rec = T ? vrec : krec;
+                            const uint32_t ents = dslot + uint32_t(C::S_T + T * C::T_BYTES + C::E_OFF) +
+                                                  esc_rec_line(rec, e0) - 4u * uint32_t(e0);
+                            sts_u32(dslot + uint32_t(C::S_INFO + 4 * T),
+                                    e1 > e0 && e1 - e0 <= C::ESC_CAP ? (ents | 1u) : 0u);
+                        }
+                    }
+                    // (the stores above are ordered before the arrive, which releases them)
+                    mbar_arrive_expect_tx(full, total);
+                }
                 __syncwarp();
                 ++gs;
             }
@@ -604,12 +621,13 @@ __device__ void producer(const AttnArgs &a, uint8_t *smem, int fb0, int fb1, int
 }
 
 // One tensor of one tile into the warp's BF16 tile, escapes included.  reg: the tensor's region of
-// the slot; b7s: the tensor's merge words in the slot; g16: the tile's 16-token group in the
-// block; t0: the stage's first token in the block; rows: valid rows of the tile; zero_from: rows
-// at or past it are zeroed.
-template <int D>
-__device__ __forceinline__ void tile_tensor(const AttnArgs &a, const BlockDesc &bd, int T, int mode,
-                                            uint32_t al, uint32_t reg, uint32_t b7s, int tw, uint32_t xb,
+// the slot; b7s: the tensor's merge words in the slot; info: the producer's escape word of the
+// tensor for this stage; g16: the tile's 16-token group in the block; t0: the stage's first token
+// in the block; rows: valid rows of the tile; zero_from: rows at or past it are zeroed.
+template <int D, int T>
+__device__ __forceinline__ void tile_tensor(const AttnArgs &a, const BlockDesc &bd, int mode,
+                                            uint32_t al, uint32_t reg, uint32_t b7s, uint32_t info, int tw,
+                                            uint32_t xb,
                                             const StoreMap<D> &sm, int g16, int t0, int rows,
                                             int zero_from, bool bf16, int lane) {
     using C = Cfg<D>;
@@ -622,26 +640,39 @@ __device__ __forceinline__ void tile_tensor(const AttnArgs &a, const BlockDesc &
     const Lay ly = make_lay<D>(rd, cd, mode, c8, bf16, code_base);
     const uint32_t rb = reg + uint32_t(TT * tw * (mode == 0 ? 2 * D : D));
     const uint32_t cb = reg + uint32_t(TT * tw * (D * mode / 8));
+    // The tile's escapes [e0, e1) are fetched before the decode, one entry per lane (a tile has
+    // more than 32 only in escape-dense blocks; those lanes take the rest after the first 32), so
+    // that only their stores follow the decode.
+    const int e0 = esc_ms(bd, T, g16), e1 = esc_ms(bd, T, g16 + 1);
+    uint32_t ents = 0u, ent = 0u;
+    if (e1 > e0) {
+        ents = lds_u32(info);  // the producer's word for this stage and tensor
+        if (e0 + lane < e1)
+            ent = (ents & 1u) ? lds_u32((ents & ~1u) + 4u * uint32_t(e0 + lane))
+                              : __ldg(a.esc + (T ? bd.v_rec : bd.k_rec) + kEscRecHead + e0 + lane);
+    }
     if (mode != 0) {
         uint32_t b7[4];
         lds_v4(b7s + 16u * uint32_t(c8), b7[0], b7[1], b7[2], b7[3]);
-        if (mode == 4) decode_tile<D, 4>(rb, cb, ly, b7, sm, lane);
-        else decode_tile<D, 2>(rb, cb, ly, b7, sm, lane);
+        if (mode == 4) decode_tile<D, 4, T * Cfg<D>::TILE>(rb, cb, ly, b7, sm, lane);
+        else decode_tile<D, 2, T * Cfg<D>::TILE>(rb, cb, ly, b7, sm, lane);
     } else {
         const uint32_t b7[4] = {0u, 0u, 0u, 0u};
-        decode_tile<D, 0>(rb, cb, ly, b7, sm, lane);
+        decode_tile<D, 0, T * Cfg<D>::TILE>(rb, cb, ly, b7, sm, lane);
     }
-    if (zero_from < TT) zero_rows<D>(sm, zero_from, lane);
-    const int e0 = esc_ms(bd, T, g16), e1 = esc_ms(bd, T, g16 + 1);
+    if (zero_from < TT) zero_rows<D, T * Cfg<D>::TILE>(sm, zero_from, lane);
     if (e1 > e0) {
-        const uint32_t rec = T ? bd.v_rec : bd.k_rec;
-        const int ea = esc_ms(bd, T, t0 >> 4), eb = esc_ms(bd, T, min(16, (t0 + C::TSB) >> 4));
+        // entry: the element's byte in the tile (bits 0-15, even) | its BF16 word << 16; slots at or
+        // past the tile's valid rows are skipped
         const uint32_t lim = uint32_t(rows) * (2 * D);
         __syncwarp();  // the decoded words are in place before escapes overwrite some
-        if (eb - ea <= C::ESC_CAP)  // staged by the producer
-            esc_patch<D>(xb, reg + uint32_t(C::E_OFF) + esc_rec_line(rec, ea) - 4u * uint32_t(ea), e0, e1, lim, lane);
-        else
-            esc_patch_hbm<D>(xb, a.esc + rec + kEscRecHead, e0, e1, lim, lane);
+        if (e0 + lane < e1 && (ent & 0xFFFFu) < lim) sts_u16(xb + (ent & 0xFFFEu), ent >> 16);
+        if (e1 - e0 > 32) {
+            if (ents & 1u)
+                esc_patch<D>(xb, ents & ~1u, e0 + 32, e1, lim, lane);
+            else
+                esc_patch_hbm<D>(xb, a.esc + (T ? bd.v_rec : bd.k_rec) + kEscRecHead, e0 + 32, e1, lim, lane);
+        }
     }
     __syncwarp();
 }
@@ -659,7 +690,8 @@ template <int D> struct SoftState {
     }
 };
 
-// One 16-token tile of K and V: decode, S = K Q^T, online softmax, decode V, free the slot, O += P V.
+// One 16-token tile of K and V: decode K into the warp's K tile, S = K Q^T on the tensor cores,
+// decode V into its V tile while those MMAs run, free the slot, online softmax, O += P V.
 template <int D, bool BF16IN>
 __device__ __forceinline__ void tile_step(const AttnArgs &a, const BlockDesc &bd, uint32_t slot_addr,
                                           uint32_t empty, uint32_t xb, const StoreMap<D> &sm, int tw,
@@ -673,10 +705,16 @@ __device__ __forceinline__ void tile_step(const AttnArgs &a, const BlockDesc &bd
     const uint32_t kreg = slot_addr + uint32_t(C::S_T), vreg = kreg + uint32_t(C::T_BYTES);
 
     // S^T = K Q^T (rows past `rows` hold stale words: their scores are dropped)
-    tile_tensor<D>(a, bd, 0, km, al & 0xFFFFu, kreg, slot_addr + uint32_t(C::S_B7), tw, xb, sm, g16, t0,
-                   rows, TT, BF16IN, lane);
+    tile_tensor<D, 0>(a, bd, km, al & 0xFFFFu, kreg, slot_addr + uint32_t(C::S_B7),
+                      slot_addr + uint32_t(C::S_INFO), tw, xb, sm, g16, t0, rows, TT, BF16IN, lane);
     float s[1][4];
     qk_tiles<D, 1>(xb, qb, lane, s);
+    // V into the V tile (rows past `rows` zeroed: P is 0 there and V must be finite) while the
+    // MMAs above run; then the warp has read everything it needs from the slot
+    tile_tensor<D, 1>(a, bd, vm, al >> 16, vreg, slot_addr + uint32_t(C::S_B7 + 2 * D),
+                      slot_addr + uint32_t(C::S_INFO + 4), tw, xb + uint32_t(C::TILE), sm, g16, t0, rows,
+                      rows, BF16IN, lane);
+    if (lane == 0) mbar_arrive(empty);
     if (rows < TT) {
         if (gi >= rows) s[0][0] = s[0][1] = -INFINITY;
         if (gi + 8 >= rows) s[0][2] = s[0][3] = -INFINITY;
@@ -740,12 +778,7 @@ __device__ __forceinline__ void tile_step(const AttnArgs &a, const BlockDesc &bd
         }
     }
 
-    // V replaces K in the tile (K was read by the MMAs above: ldmatrix is warp-synchronous);
-    // rows past `rows` are zeroed (P is 0 there and V must be finite)
-    tile_tensor<D>(a, bd, 1, vm, al >> 16, vreg, slot_addr + uint32_t(C::S_B7 + 2 * D), tw, xb, sm, g16,
-                   t0, rows, rows, BF16IN, lane);
-    if (lane == 0) mbar_arrive(empty);  // this warp has read everything it needs from the slot
-    pv_tile<D>(xb, 0, bh, bm, bl, lane, st.acc);
+    pv_tile<D>(xb + uint32_t(C::TILE), 0, bh, bm, bl, lane, st.acc);
     __syncwarp();  // every lane is done with the tile before the next decode writes it
 }
 
@@ -786,7 +819,7 @@ template <int D, bool BF16IN>
 __device__ void consumer(const AttnArgs &a, uint8_t *smem, int w, int lane, int fb0, int fb1, int row0) {
     using C = Cfg<D>;
     const uint32_t sb = smem_u32(smem);
-    const uint32_t xb = sb + uint32_t(C::O_TILE + w * C::TILE);
+    const uint32_t xb = sb + uint32_t(C::O_TILE + w * 2 * C::TILE);  // K tile; V tile behind it
     StoreMap<D> sm;
     sm.init(xb, lane);
     uint32_t qb[C::KS][2];
