@@ -280,6 +280,7 @@ struct kvx_plan_s {
     int64_t n_blocks = 0;
     int n_ranges = 0;     // CTA ranges of the attention grid (one CTA each)
     int64_t n_rows = 0;   // partial-state rows (one per unit segment of a CTA range)
+    bool one_stage = false;  // every block is one ring stage of the attention kernel
     cudaStream_t s = nullptr;
     UnitDev *units = nullptr;
     FlatBlock *flat = nullptr;
@@ -487,7 +488,7 @@ static int plan_create_impl(const kvx_unit *units, int n_units, int n_q, int dim
         (e = plan_alloc(p, &dvu, vu.size())) != cudaSuccess ||
         (e = plan_alloc(p, &dbegin, begin.size())) != cudaSuccess ||
         (e = plan_alloc(p, &dsrc, src.size())) != cudaSuccess ||
-        (e = plan_alloc(p, &desc_total, 1)) != cudaSuccess) {
+        (e = plan_alloc(p, &desc_total, 2)) != cudaSuccess) {
         delete p;
         return fail(KVX_ERR_CUDA, std::string("kvx_plan_create: ") + cudaGetErrorString(e));
     }
@@ -498,6 +499,14 @@ static int plan_create_impl(const kvx_unit *units, int n_units, int n_q, int dim
     cudaMemset(p->status, 0, 2 * sizeof(int));
     e = launch_build_flat(dvu, dbegin, dsrc, p->n_units, dim, block_tokens, bf16, p->flat,
                           p->status, nullptr);
+    // blocks of at most 128 attended tokens at dim <= 64 are one ring stage each (the attention
+    // kernel then takes its one-stage path)
+    int max_valid = 255;
+    if (e == cudaSuccess && dim <= 64)
+        e = launch_max_valid(p->flat, total, reinterpret_cast<int *>(desc_total + 1), nullptr);
+    if (e == cudaSuccess && dim <= 64)
+        e = cudaMemcpy(&max_valid, desc_total + 1, sizeof max_valid, cudaMemcpyDeviceToHost);
+    p->one_stage = dim <= 64 && max_valid <= 128;
     // escape records: offsets, then (with the array sized) the records
     unsigned long long esc_total = 0;
     if (e == cudaSuccess && !bf16)
@@ -538,6 +547,8 @@ static int plan_create_impl(const kvx_unit *units, int n_units, int n_q, int dim
     if (e == cudaSuccess)
         e = plan_alloc(p, &p->partials,
                        size_t(p->n_rows) * attention_consumer_warps(dim) * partial_stride(dim));
+    if (e == cudaSuccess)
+        e = launch_init_partials(p->partials, p->n_rows * attention_consumer_warps(dim), dim, nullptr);
     if (e != cudaSuccess) {
         delete p;
         return fail(KVX_ERR_CUDA, std::string("kvx_plan_create: ") + cudaGetErrorString(e));
@@ -603,6 +614,7 @@ int kvx_plan_run_part(kvx_plan p, int part, void *stream) {
     a.partials = p->partials;
     a.status = p->status;
     a.n_ranges = p->n_ranges;
+    a.one_stage = p->one_stage ? 1 : 0;
     KVX_CUDA(launch_attention(p->dim, p->bf16, a, p->n_ranges, s));
     return KVX_OK;
 }

@@ -68,7 +68,7 @@ template <int D> struct Cfg {
     static constexpr int TSB = cmin(128, 8192 / D);  // tokens per ring stage
     static constexpr int TPS = TSB / TT;          // tiles per stage
     static constexpr int NW = attention_consumer_warps(D);  // consumer warps
-    static constexpr int NSLOT = D >= 128 ? 3 : 4;  // ring slots
+    static constexpr int NSLOT = 4;               // ring slots
     // Escape-record entries of one tensor that a stage stages (12.5 % of its elements); a stage
     // with more leaves them in HBM, where the consumers read them.
     static constexpr int ESC_CAP = TSB * D / 8;
@@ -87,9 +87,9 @@ template <int D> struct Cfg {
     static constexpr int S_INFO = S_B7 + 4 * D;
     static constexpr int S_T = S_INFO + 16;
     static constexpr int SLOT = S_T + 2 * T_BYTES;
-    static constexpr int TILE = TT * 2 * D;       // one BF16 tile; a consumer warp has a K and a V tile
+    static constexpr int TILE = TT * 2 * D;       // one consumer warp's BF16 tile (K, then V)
     static constexpr int O_TILE = NSLOT * SLOT;
-    static constexpr int O_BAR = O_TILE + NW * 2 * TILE;  // full[NSLOT], then empty[NSLOT]
+    static constexpr int O_BAR = O_TILE + NW * TILE;  // full[NSLOT], then empty[NSLOT]
     static constexpr int SMEM = O_BAR + 16 * NSLOT;
     static constexpr int NP = 2;                  // producer warps (stages alternate between them)
     static constexpr int THREADS = 32 * (NW + NP);
@@ -654,13 +654,13 @@ __device__ __forceinline__ void tile_tensor(const AttnArgs &a, const BlockDesc &
     if (mode != 0) {
         uint32_t b7[4];
         lds_v4(b7s + 16u * uint32_t(c8), b7[0], b7[1], b7[2], b7[3]);
-        if (mode == 4) decode_tile<D, 4, T * Cfg<D>::TILE>(rb, cb, ly, b7, sm, lane);
-        else decode_tile<D, 2, T * Cfg<D>::TILE>(rb, cb, ly, b7, sm, lane);
+        if (mode == 4) decode_tile<D, 4, 0>(rb, cb, ly, b7, sm, lane);
+        else decode_tile<D, 2, 0>(rb, cb, ly, b7, sm, lane);
     } else {
         const uint32_t b7[4] = {0u, 0u, 0u, 0u};
-        decode_tile<D, 0, T * Cfg<D>::TILE>(rb, cb, ly, b7, sm, lane);
+        decode_tile<D, 0, 0>(rb, cb, ly, b7, sm, lane);
     }
-    if (zero_from < TT) zero_rows<D, T * Cfg<D>::TILE>(sm, zero_from, lane);
+    if (zero_from < TT) zero_rows<D, 0>(sm, zero_from, lane);
     if (e1 > e0) {
         // entry: the element's byte in the tile (bits 0-15, even) | its BF16 word << 16; slots at or
         // past the tile's valid rows are skipped
@@ -690,8 +690,8 @@ template <int D> struct SoftState {
     }
 };
 
-// One 16-token tile of K and V: decode K into the warp's K tile, S = K Q^T on the tensor cores,
-// decode V into its V tile while those MMAs run, free the slot, online softmax, O += P V.
+// One 16-token tile of K and V: decode K into the warp's tile, S = K Q^T on the tensor cores, online
+// softmax, decode V into the tile, free the slot, O += P V.
 template <int D, bool BF16IN>
 __device__ __forceinline__ void tile_step(const AttnArgs &a, const BlockDesc &bd, uint32_t slot_addr,
                                           uint32_t empty, uint32_t xb, const StoreMap<D> &sm, int tw,
@@ -709,12 +709,6 @@ __device__ __forceinline__ void tile_step(const AttnArgs &a, const BlockDesc &bd
                       slot_addr + uint32_t(C::S_INFO), tw, xb, sm, g16, t0, rows, TT, BF16IN, lane);
     float s[1][4];
     qk_tiles<D, 1>(xb, qb, lane, s);
-    // V into the V tile (rows past `rows` zeroed: P is 0 there and V must be finite) while the
-    // MMAs above run; then the warp has read everything it needs from the slot
-    tile_tensor<D, 1>(a, bd, vm, al >> 16, vreg, slot_addr + uint32_t(C::S_B7 + 2 * D),
-                      slot_addr + uint32_t(C::S_INFO + 4), tw, xb + uint32_t(C::TILE), sm, g16, t0, rows,
-                      rows, BF16IN, lane);
-    if (lane == 0) mbar_arrive(empty);
     if (rows < TT) {
         if (gi >= rows) s[0][0] = s[0][1] = -INFINITY;
         if (gi + 8 >= rows) s[0][2] = s[0][3] = -INFINITY;
@@ -778,7 +772,12 @@ __device__ __forceinline__ void tile_step(const AttnArgs &a, const BlockDesc &bd
         }
     }
 
-    pv_tile<D>(xb + uint32_t(C::TILE), 0, bh, bm, bl, lane, st.acc);
+    // V replaces K in the tile (the QK MMAs' ldmatrix reads are done: their results were used
+    // above); rows past `rows` are zeroed (P is 0 there and V must be finite)
+    tile_tensor<D, 1>(a, bd, vm, al >> 16, vreg, slot_addr + uint32_t(C::S_B7 + 2 * D),
+                      slot_addr + uint32_t(C::S_INFO + 4), tw, xb, sm, g16, t0, rows, rows, BF16IN, lane);
+    if (lane == 0) mbar_arrive(empty);  // this warp has read everything it needs from the slot
+    pv_tile<D>(xb, 0, bh, bm, bl, lane, st.acc);
     __syncwarp();  // every lane is done with the tile before the next decode writes it
 }
 
@@ -819,7 +818,7 @@ template <int D, bool BF16IN>
 __device__ void consumer(const AttnArgs &a, uint8_t *smem, int w, int lane, int fb0, int fb1, int row0) {
     using C = Cfg<D>;
     const uint32_t sb = smem_u32(smem);
-    const uint32_t xb = sb + uint32_t(C::O_TILE + w * 2 * C::TILE);  // K tile; V tile behind it
+    const uint32_t xb = sb + uint32_t(C::O_TILE + w * C::TILE);
     StoreMap<D> sm;
     sm.init(xb, lane);
     uint32_t qb[C::KS][2];
@@ -866,6 +865,55 @@ __device__ void consumer(const AttnArgs &a, uint8_t *smem, int w, int lane, int 
     }
 }
 
+// A consumer warp when every block of the plan is one stage (D <= 64, blocks of at most 128
+// tokens): stage s of the range is block fb0 + s, so the warp goes straight to the stages of its
+// tiles (tile j = w, w + NW, ... of the range; stage j / TPS, tile j mod TPS), waits only on those,
+// and arrives once per tile (the slot's empty barrier counts TPS arrivals).  Its state is written
+// when the unit of its next tile differs, and at the end of the range, to row
+// row0 + (unit - the range's first unit); rows a warp never reaches keep m = -inf, l = 0.
+template <int D, bool BF16IN>
+__device__ void consumer_one_stage(const AttnArgs &a, uint8_t *smem, int w, int lane, int fb0, int fb1,
+                                   int row0) {
+    using C = Cfg<D>;
+    const uint32_t sb = smem_u32(smem);
+    const uint32_t xb = sb + uint32_t(C::O_TILE + w * C::TILE);
+    StoreMap<D> sm;
+    sm.init(xb, lane);
+    uint32_t qb[C::KS][2];
+    SoftState<D> st;
+    st.reset();
+    const int unit0 = __ldg(&a.desc[fb0].unit);
+    int cur = -1;  // unit of the warp's state (-1: none yet)
+    const int tiles = (fb1 - fb0) * C::TPS;
+    for (int j = w; j < tiles; j += C::NW) {
+        const int gs = j / C::TPS, tw = j % C::TPS;
+        const int slot = gs % C::NSLOT;
+        const uint32_t full = ring_bar<D>(sb, slot), empty = ring_bar<D>(sb, C::NSLOT + slot);
+        if (!uni(mbar_wait_bounded(full, uint32_t((gs / C::NSLOT) & 1), kStageWaitUs))) {
+            if (lane == 0) report(a.status, KVX_ERR_TIMEOUT, DERR_TIMEOUT);
+            return;
+        }
+        const uint8_t *sp = smem + slot * C::SLOT;
+        const BlockDesc &bd = *reinterpret_cast<const BlockDesc *>(sp);
+        const int valid = bd.valid, unit = bd.unit;
+        if (unit != cur) {
+            if (cur >= 0) flush_state<D>(a, size_t(row0 + cur - unit0) * C::NW + size_t(w), st, lane);
+            const UnitDev *U = a.units + unit;
+            load_q<D>(U->q, U->n_q, U->q_stride, qb, lane);
+            st.reset();
+            cur = unit;
+        }
+        const int rows = valid - TT * tw;
+        if (rows > 0) {
+            tile_step<D, BF16IN>(a, bd, smem_u32(sp), empty, xb, sm, tw, 0, min(rows, TT), qb, st, lane);
+        } else {
+            __syncwarp();  // every lane has read the descriptor
+            if (lane == 0) mbar_arrive(empty);
+        }
+    }
+    if (cur >= 0) flush_state<D>(a, size_t(row0 + cur - unit0) * C::NW + size_t(w), st, lane);
+}
+
 template <int D, bool BF16IN>
 __global__ void __launch_bounds__(Cfg<D>::THREADS, 1) attn_kernel(const AttnArgs a) {
     using C = Cfg<D>;
@@ -883,11 +931,13 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1) attn_kernel(const AttnArgs
     const int fb0 = int(a.range_begin[c]), fb1 = int(a.range_begin[c + 1]);
     if (fb0 >= fb1) return;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const bool one_stage = C::TSB >= 128 && a.one_stage != 0;
     if (threadIdx.x == 0) {
         const uint32_t sb = smem_u32(smem);
         for (int j = 0; j < C::NSLOT; ++j) {
             mbar_init(ring_bar<D>(sb, j), 1);               // full: the producer's arrive + bytes
-            mbar_init(ring_bar<D>(sb, C::NSLOT + j), C::NW);  // empty: one arrive per consumer warp
+            // empty: one arrive per consumer warp, or per tile on the one-stage path
+            mbar_init(ring_bar<D>(sb, C::NSLOT + j), one_stage ? C::TPS : C::NW);
         }
         fence_mbar_init();
         // a step whose preparation reported an error (its escape records are incomplete) runs no work
@@ -899,7 +949,10 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1) attn_kernel(const AttnArgs
         producer<D, BF16IN>(a, smem, fb0, fb1, warp - C::NW, lane);
         return;
     }
-    consumer<D, BF16IN>(a, smem, warp, lane, fb0, fb1, a.seg_base[c]);
+    if (one_stage)
+        consumer_one_stage<D, BF16IN>(a, smem, warp, lane, fb0, fb1, a.seg_base[c]);
+    else
+        consumer<D, BF16IN>(a, smem, warp, lane, fb0, fb1, a.seg_base[c]);
 }
 
 // ---- combine ------------------------------------------------------------------------------------
@@ -909,7 +962,8 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1) attn_kernel(const AttnArgs
 // src/softmax.hpp:16-30, applied to all states at once instead of a left fold), then
 // out = acc * (1 / l) like finalize_state (src/softmax.hpp:32-41).  One CTA per (unit, query);
 // the sums run over fixed slices of the states, so the result is deterministic.  A state of a
-// warp that saw none of the unit's tokens has m = -inf and l = 0 and adds nothing.
+// warp that saw none of the unit's tokens has m = -inf and l = 0 (written so, or initialised so
+// by init_partials_kernel and never written) and adds nothing; its accumulators are not read.
 constexpr int kCombineThreads = 256;
 constexpr int kMaxSegments = 4096;
 
@@ -976,9 +1030,10 @@ __global__ void __launch_bounds__(kCombineThreads) combine_kernel(const CombineA
     if (sl < S) {
 #pragma unroll
         for (int k = 0; k < PRE; ++k)
-            if (sl + k * S < nt) acc = __fmaf_rn(pre[k], e[sl + k * S], acc);
+            if (sl + k * S < nt && e[sl + k * S] > 0.f) acc = __fmaf_rn(pre[k], e[sl + k * S], acc);
 #pragma unroll 8
-        for (int i = sl + PRE * S; i < nt; i += S) acc = __fmaf_rn(__ldg(part(i) + 16 + g * D + d), e[i], acc);
+        for (int i = sl + PRE * S; i < nt; i += S)
+            if (e[i] > 0.f) acc = __fmaf_rn(__ldg(part(i) + 16 + g * D + d), e[i], acc);
     }
     red[tid] = acc;
     __syncthreads();
@@ -1138,6 +1193,25 @@ __global__ void b7_kernel(const UnitDev *units, const FlatBlock *flat, int64_t n
     }
 }
 
+// m = -inf and l = 0 in every partial state (its first 16 floats), so that a state no warp writes
+// adds nothing in the combine pass.
+__global__ void init_partials_kernel(float *partials, int64_t n_states, int stride) {
+    const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= n_states * 16) return;
+    const int64_t st = i >> 4;
+    const int f = int(i & 15);
+    partials[st * stride + f] = f < 8 ? -INFINITY : 0.f;
+}
+
+// The largest number of attended tokens of any flat block (atomic max into *out, set to 0 first).
+__global__ void max_valid_kernel(const FlatBlock *flat, int64_t n, int *out) {
+    int m = 0;
+    for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += int64_t(gridDim.x) * blockDim.x)
+        m = max(m, int(load_flat(flat, i).valid));
+    m = __reduce_max_sync(FULL, m);
+    if ((threadIdx.x & 31) == 0) atomicMax(out, m);
+}
+
 template <int D>
 cudaError_t launch_d(bool bf16, const AttnArgs &a, int grid, cudaStream_t s) {
     configure<D>(bf16);
@@ -1186,6 +1260,22 @@ cudaError_t launch_attention(int dim, bool bf16_input, const AttnArgs &a, int gr
 cudaError_t launch_split(const FlatBlock *flat, int64_t n_blocks, int n_ranges, bool by_tokens,
                          int64_t *range_begin, cudaStream_t s) {
     split_kernel<<<1, 1024, 0, s>>>(flat, n_blocks, n_ranges, by_tokens, range_begin);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_init_partials(float *partials, int64_t n_states, int dim, cudaStream_t s) {
+    const int64_t n = n_states * 16;
+    if (n <= 0) return cudaSuccess;
+    init_partials_kernel<<<unsigned((n + 255) / 256), 256, 0, s>>>(partials, n_states, partial_stride(dim));
+    return cudaGetLastError();
+}
+
+cudaError_t launch_max_valid(const FlatBlock *flat, int64_t n_blocks, int *out, cudaStream_t s) {
+    if (n_blocks <= 0) return cudaSuccess;
+    cudaError_t e = cudaMemsetAsync(out, 0, sizeof(int), s);
+    if (e != cudaSuccess) return e;
+    const int64_t grid = (n_blocks + 255) / 256 < 1024 ? (n_blocks + 255) / 256 : 1024;
+    max_valid_kernel<<<unsigned(grid), 256, 0, s>>>(flat, n_blocks, out);
     return cudaGetLastError();
 }
 

@@ -126,6 +126,7 @@ struct AttnArgs {
     float *partials;            // [rows][consumer warps][partial_stride(dim)]
     int *status;                // [2] first error (code, detail)
     int n_ranges;
+    int one_stage;              // every block is one ring stage (dim <= 64, <= 128 tokens each)
 };
 
 // A unit as the combine pass sees it (host-built, so the kernel's first load is all it needs):
@@ -184,6 +185,10 @@ cudaError_t launch_block_desc(const UnitDev *units, const FlatBlock *flat, const
                               int dim, bool bf16, BlockDesc *desc, cudaStream_t s);
 cudaError_t launch_fold(const float *parts, int n_parts, int n_rows, int dim, float *out,
                         float *lse_out, cudaStream_t s);
+// m = -inf, l = 0 in n_states partial states (so that states no warp writes add nothing).
+cudaError_t launch_init_partials(float *partials, int64_t n_states, int dim, cudaStream_t s);
+// *out = the largest number of attended tokens of any flat block.
+cudaError_t launch_max_valid(const FlatBlock *flat, int64_t n_blocks, int *out, cudaStream_t s);
 // Escape records: sizes and offsets (single CTA; *total receives the record array length in u16,
 // blocks whose src is another block take that block's offsets, and a record that would end past
 // `cap` entries reports DERR_ESC_CAP), then the records themselves (the fill reports
