@@ -280,7 +280,7 @@ struct kvx_plan_s {
     int64_t n_blocks = 0;
     int n_ranges = 0;     // CTA ranges of the attention grid (one CTA each)
     int64_t n_rows = 0;   // partial-state rows (one per unit segment of a CTA range)
-    bool one_stage = false;  // every block is one ring stage of the attention kernel
+    int stages_per_block = 0;  // ring stages of every block in the attention kernel (0: by block)
     cudaStream_t s = nullptr;
     UnitDev *units = nullptr;
     FlatBlock *flat = nullptr;
@@ -499,14 +499,18 @@ static int plan_create_impl(const kvx_unit *units, int n_units, int n_q, int dim
     cudaMemset(p->status, 0, 2 * sizeof(int));
     e = launch_build_flat(dvu, dbegin, dsrc, p->n_units, dim, block_tokens, bf16, p->flat,
                           p->status, nullptr);
-    // blocks of at most 128 attended tokens at dim <= 64 are one ring stage each (the attention
-    // kernel then takes its one-stage path)
-    int max_valid = 255;
-    if (e == cudaSuccess && dim <= 64)
+    // every block takes the same number of ring stages in the attention kernel (enough for the
+    // longest block; shorter ones get empty stages), so a consumer warp goes straight to the stage
+    // of each of its tiles
+    int max_valid = 0;
+    if (e == cudaSuccess)
         e = launch_max_valid(p->flat, total, reinterpret_cast<int *>(desc_total + 1), nullptr);
-    if (e == cudaSuccess && dim <= 64)
+    if (e == cudaSuccess)
         e = cudaMemcpy(&max_valid, desc_total + 1, sizeof max_valid, cudaMemcpyDeviceToHost);
-    p->one_stage = dim <= 64 && max_valid <= 128;
+    {
+        const int tsb = attention_stage_tokens(dim);
+        p->stages_per_block = max_valid > 0 ? (max_valid + tsb - 1) / tsb : 0;
+    }
     // escape records: offsets, then (with the array sized) the records
     unsigned long long esc_total = 0;
     if (e == cudaSuccess && !bf16)
@@ -614,7 +618,7 @@ int kvx_plan_run_part(kvx_plan p, int part, void *stream) {
     a.partials = p->partials;
     a.status = p->status;
     a.n_ranges = p->n_ranges;
-    a.one_stage = p->one_stage ? 1 : 0;
+    a.stages_per_block = p->stages_per_block;
     KVX_CUDA(launch_attention(p->dim, p->bf16, a, p->n_ranges, s));
     return KVX_OK;
 }

@@ -58,14 +58,13 @@ __host__ __device__ constexpr int round16(int x) { return (x + 15) & ~15; }
 // One verdict for the whole warp on a condition its lanes may see differently (a bounded wait that
 // times out in some lanes just as the phase completes for others).
 __device__ __forceinline__ bool uni(bool c) { return __all_sync(0xFFFFFFFFu, c); }
-__host__ __device__ constexpr int cmin(int a, int b) { return a < b ? a : b; }
 
 
 template <int D> struct Cfg {
     static constexpr int KS = D / 16;             // k-steps of QK = M-tiles of PV
     static constexpr int C8 = D / 8;              // 8-element chunks per row
     static constexpr int NIT = TT * C8 / 32;      // chunk steps of a lane per tile and tensor
-    static constexpr int TSB = cmin(128, 8192 / D);  // tokens per ring stage
+    static constexpr int TSB = attention_stage_tokens(D);  // tokens per ring stage
     static constexpr int TPS = TSB / TT;          // tiles per stage
     static constexpr int NW = attention_consumer_warps(D);  // consumer warps
     static constexpr int NSLOT = 4;               // ring slots
@@ -521,7 +520,10 @@ __device__ void producer(const AttnArgs &a, uint8_t *smem, int fb0, int fb1, int
                     return esc_gd(gd, T, i);  // blocks over 128 tokens: not prefetched
                 }
             };
-            for (int t0 = 0; t0 < valid; t0 += C::TSB) {
+            // every block takes a.stages_per_block stages when that is set (the ones past its
+            // tokens carry only the descriptor)
+            const int t_end = a.stages_per_block > 0 ? a.stages_per_block * C::TSB : valid;
+            for (int t0 = 0; t0 < t_end; t0 += C::TSB) {
                 if (gs % C::NP != pw) {  // the other producer warp's stage
                     ++gs;
                     continue;
@@ -536,7 +538,7 @@ __device__ void producer(const AttnArgs &a, uint8_t *smem, int fb0, int fb1, int
                 }
                 const int n = min(C::TSB, valid - t0);
                 int ea[2] = {0, 0}, eb[2] = {0, 0};
-                if (!BF16IN) {
+                if (!BF16IN && n > 0) {
 #pragma unroll
                     for (int T = 0; T < 2; ++T) {
                         ea[T] = esc_count(T, t0 >> 4);
@@ -556,11 +558,11 @@ __device__ void producer(const AttnArgs &a, uint8_t *smem, int fb0, int fb1, int
                 if (lane == 0) {
                     src = reinterpret_cast<const uint8_t *>(gd), len = uint32_t(sizeof(BlockDesc)), dst = dslot;
                 } else if (lane == 1) {
-                    if (!BF16IN && (km | vm) != 0) {
+                    if (!BF16IN && (km | vm) != 0 && n > 0) {
                         src = reinterpret_cast<const uint8_t *>(a.b7 + size_t(b7_block) * D);
                         len = uint32_t(4 * D), dst = dslot + C::S_B7;
                     }
-                } else if (lane < 8) {
+                } else if (lane < 8 && n > 0) {
                     const int T = (lane - 2) / 3, part = (lane - 2) % 3;
                     const uint8_t *blk = gptr(T ? vp : kp);
                     const int mode = T ? vm : km;
@@ -865,15 +867,15 @@ __device__ void consumer(const AttnArgs &a, uint8_t *smem, int w, int lane, int 
     }
 }
 
-// A consumer warp when every block of the plan is one stage (D <= 64, blocks of at most 128
-// tokens): stage s of the range is block fb0 + s, so the warp goes straight to the stages of its
-// tiles (tile j = w, w + NW, ... of the range; stage j / TPS, tile j mod TPS), waits only on those,
-// and arrives once per tile (the slot's empty barrier counts TPS arrivals).  Its state is written
+// A consumer warp when every block takes the same number of stages (spb): stage s of the range is
+// stage s mod spb of block fb0 + s / spb, so the warp goes straight to the stages of its tiles
+// (tile j = w, w + NW, ... of the range; stage j / TPS, tile j mod TPS), waits only on those, and
+// arrives once per tile (the slot's empty barrier counts TPS arrivals).  Its state is written
 // when the unit of its next tile differs, and at the end of the range, to row
 // row0 + (unit - the range's first unit); rows a warp never reaches keep m = -inf, l = 0.
 template <int D, bool BF16IN>
-__device__ void consumer_one_stage(const AttnArgs &a, uint8_t *smem, int w, int lane, int fb0, int fb1,
-                                   int row0) {
+__device__ void consumer_by_tile(const AttnArgs &a, uint8_t *smem, int w, int lane, int fb0, int fb1,
+                                 int row0) {
     using C = Cfg<D>;
     const uint32_t sb = smem_u32(smem);
     const uint32_t xb = sb + uint32_t(C::O_TILE + w * C::TILE);
@@ -882,11 +884,13 @@ __device__ void consumer_one_stage(const AttnArgs &a, uint8_t *smem, int w, int 
     uint32_t qb[C::KS][2];
     SoftState<D> st;
     st.reset();
+    const int spb = a.stages_per_block;
     const int unit0 = __ldg(&a.desc[fb0].unit);
     int cur = -1;  // unit of the warp's state (-1: none yet)
-    const int tiles = (fb1 - fb0) * C::TPS;
+    const int tiles = (fb1 - fb0) * spb * C::TPS;
     for (int j = w; j < tiles; j += C::NW) {
         const int gs = j / C::TPS, tw = j % C::TPS;
+        const int t0 = (gs % spb) * C::TSB;
         const int slot = gs % C::NSLOT;
         const uint32_t full = ring_bar<D>(sb, slot), empty = ring_bar<D>(sb, C::NSLOT + slot);
         if (!uni(mbar_wait_bounded(full, uint32_t((gs / C::NSLOT) & 1), kStageWaitUs))) {
@@ -903,9 +907,9 @@ __device__ void consumer_one_stage(const AttnArgs &a, uint8_t *smem, int w, int 
             st.reset();
             cur = unit;
         }
-        const int rows = valid - TT * tw;
+        const int rows = valid - t0 - TT * tw;
         if (rows > 0) {
-            tile_step<D, BF16IN>(a, bd, smem_u32(sp), empty, xb, sm, tw, 0, min(rows, TT), qb, st, lane);
+            tile_step<D, BF16IN>(a, bd, smem_u32(sp), empty, xb, sm, tw, t0, min(rows, TT), qb, st, lane);
         } else {
             __syncwarp();  // every lane has read the descriptor
             if (lane == 0) mbar_arrive(empty);
@@ -931,13 +935,13 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1) attn_kernel(const AttnArgs
     const int fb0 = int(a.range_begin[c]), fb1 = int(a.range_begin[c + 1]);
     if (fb0 >= fb1) return;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const bool one_stage = C::TSB >= 128 && a.one_stage != 0;
+    const bool by_tile = a.stages_per_block > 0;
     if (threadIdx.x == 0) {
         const uint32_t sb = smem_u32(smem);
         for (int j = 0; j < C::NSLOT; ++j) {
             mbar_init(ring_bar<D>(sb, j), 1);               // full: the producer's arrive + bytes
-            // empty: one arrive per consumer warp, or per tile on the one-stage path
-            mbar_init(ring_bar<D>(sb, C::NSLOT + j), one_stage ? C::TPS : C::NW);
+            // empty: one arrive per consumer warp, or per tile when the warps go by tile
+            mbar_init(ring_bar<D>(sb, C::NSLOT + j), by_tile ? C::TPS : C::NW);
         }
         fence_mbar_init();
         // a step whose preparation reported an error (its escape records are incomplete) runs no work
@@ -949,8 +953,8 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1) attn_kernel(const AttnArgs
         producer<D, BF16IN>(a, smem, fb0, fb1, warp - C::NW, lane);
         return;
     }
-    if (one_stage)
-        consumer_one_stage<D, BF16IN>(a, smem, warp, lane, fb0, fb1, a.seg_base[c]);
+    if (by_tile)
+        consumer_by_tile<D, BF16IN>(a, smem, warp, lane, fb0, fb1, a.seg_base[c]);
     else
         consumer<D, BF16IN>(a, smem, warp, lane, fb0, fb1, a.seg_base[c]);
 }

@@ -55,9 +55,14 @@ __host__ __device__ inline uint32_t esc_scratch_slot(int dim, int T, int r, int 
 // Consumer warps per CTA of the attention kernel (one CTA per SM; two more warps issue the
 // copies): a CTA of 16 warps at 128 registers a thread for dim <= 64, 12 at 168 for dim 128, 8 at
 // 255 for dim 256.  A stage of 128 tokens (64 at dim 128, 32 at dim 256) is 8 (4, 2) tiles, dealt
-// round robin; each consumer warp takes at most one tile of a stage.
+// round robin.
 __host__ __device__ constexpr int attention_consumer_warps(int dim) {
     return dim >= 256 ? 6 : (dim >= 128 ? 10 : 14);
+}
+
+// Tokens per ring stage of the attention kernel: 8 KiB of BF16 per tensor (128 tokens at dim <= 64).
+__host__ __device__ constexpr int attention_stage_tokens(int dim) {
+    return 8192 / dim < 128 ? 8192 / dim : 128;
 }
 
 __device__ __forceinline__ FlatBlock load_flat(const FlatBlock *f, int64_t i) {
@@ -126,7 +131,8 @@ struct AttnArgs {
     float *partials;            // [rows][consumer warps][partial_stride(dim)]
     int *status;                // [2] first error (code, detail)
     int n_ranges;
-    int one_stage;              // every block is one ring stage (dim <= 64, <= 128 tokens each)
+    int stages_per_block;       // > 0: every block takes this many ring stages (empty ones past
+                                //      its tokens); 0: each block takes as many as its tokens need
 };
 
 // A unit as the combine pass sees it (host-built, so the kernel's first load is all it needs):
