@@ -83,7 +83,9 @@ template <int D> struct Cfg {
     static constexpr int S_B7 = 128;
     // Two words the producer writes for the stage: per tensor, the shared address (bit 0 set) from
     // which the stage's staged escape-record entry i is read at + 4 i, or 0 when they stay in HBM.
+    // Then the stage's index in the CTA's sequence of stages (its tag).
     static constexpr int S_INFO = S_B7 + 4 * D;
+    static constexpr int S_TAG = S_INFO + 8;
     static constexpr int S_T = S_INFO + 16;
     static constexpr int SLOT = S_T + 2 * T_BYTES;
     static constexpr int TILE = TT * 2 * D;       // one consumer warp's BF16 tile (K, then V)
@@ -325,24 +327,27 @@ __device__ __forceinline__ void zero_rows(const StoreMap<D> &sm, int from, int l
     }
 }
 
-// Store escapes [e0, e1) of a block over their elements of the stage's tile: record entry i (tile
-// byte | escape word << 16) is the u32 at ents + 4 i -- a shared address of the staged copy, or
-// (HBM variant) the record in global memory.  Slots at or past the stage's valid rows (lim bytes)
-// are skipped; slots are even.
-template <int D>
-__device__ __forceinline__ void esc_patch(uint32_t xb, uint32_t ents, int e0, int e1, uint32_t lim, int lane) {
-    for (int i = e0 + lane; i < e1; i += 32) {
-        const uint32_t e = lds_u32(ents + 4u * uint32_t(i));
-        if ((e & 0xFFFFu) < lim) sts_u16(xb + (e & 0xFFFEu), e >> 16);
-    }
+// Store escapes [e0, e1) of a block over their elements in the warp's NT tiles: record entry i
+// (byte in its 16-token tile | escape word << 16) is the u32 at ents + 4 i -- a shared address of
+// the staged copy, or (HBM variant) the record in global memory.  Entries from em on belong to the
+// second tile.  Slots at or past a tile's valid rows are skipped (rows counts from the first
+// tile's start); slots are even.
+__device__ __forceinline__ void esc_store(uint32_t xb, uint32_t e, int second, int rows, int tile_bytes,
+                                          int row_bytes) {
+    const int rt = rows - (second ? kTileTokens : 0);
+    if (rt > 0 && (e & 0xFFFFu) < uint32_t(rt) * uint32_t(row_bytes))
+        sts_u16(xb + (second ? uint32_t(tile_bytes) : 0u) + (e & 0xFFFEu), e >> 16);
 }
 template <int D>
-__device__ __noinline__ void esc_patch_hbm(uint32_t xb, const uint32_t *ents, int e0, int e1, uint32_t lim,
-                                           int lane) {
-    for (int i = e0 + lane; i < e1; i += 32) {
-        const uint32_t e = __ldg(ents + i);
-        if ((e & 0xFFFFu) < lim) sts_u16(xb + (e & 0xFFFEu), e >> 16);
-    }
+__device__ __forceinline__ void esc_patch(uint32_t xb, uint32_t ents, int e0, int e1, int em, int rows,
+                                          int lane) {
+    for (int i = e0 + lane; i < e1; i += 32)
+        esc_store(xb, lds_u32(ents + 4u * uint32_t(i)), i >= em, rows, Cfg<D>::TILE, 2 * D);
+}
+template <int D>
+__device__ __noinline__ void esc_patch_hbm(uint32_t xb, const uint32_t *ents, int e0, int e1, int em,
+                                           int rows, int lane) {
+    for (int i = e0 + lane; i < e1; i += 32) esc_store(xb, __ldg(ents + i), i >= em, rows, Cfg<D>::TILE, 2 * D);
 }
 
 // ---- tiles on the tensor cores ------------------------------------------------------------------
@@ -594,6 +599,7 @@ __device__ void producer(const AttnArgs &a, uint8_t *smem, int fb0, int fb1, int
                 }
                 const uint32_t total = __reduce_add_sync(FULL, stage_piece(dst, src, len, full));
                 if (lane == 0) {
+                    sts_u32(dslot + uint32_t(C::S_TAG), uint32_t(gs));
                     if (!BF16IN) {
 #pragma unroll
                         for (int T = 0; T < 2; ++T) {
@@ -815,7 +821,8 @@ __device__ __forceinline__ void flush_state(const AttnArgs &a, size_t idx, const
 
 // A consumer warp: visits every stage of the CTA's range in order, takes the tiles dealt to it,
 // arrives once per stage on the slot's empty barrier, and writes its state at every segment end
-// (the unit's last block, or the end of the range).
+// (the unit's last block, or the end of the range).  It has seen stage gs - 1 (and so gs - NSLOT)
+// land before it waits on stage gs, so the parity of the slot's full barrier identifies the stage.
 template <int D, bool BF16IN>
 __device__ void consumer(const AttnArgs &a, uint8_t *smem, int w, int lane, int fb0, int fb1, int row0) {
     using C = Cfg<D>;
@@ -867,6 +874,31 @@ __device__ void consumer(const AttnArgs &a, uint8_t *smem, int w, int lane, int 
     }
 }
 
+// Wait until stage gs of the CTA has landed in its slot.  The slot's full barrier alone cannot tell
+// stage gs from stage gs - NSLOT (the slot's previous use, copied by the other producer warp's
+// sequence of stages or still in flight): a warp that skips stages may start waiting before that
+// stage has landed, and the parity check would then pass one phase early.  So the warp also reads
+// the stage tag, which the producer writes before the arrive that completes the phase, and keeps
+// waiting until it is gs.  Once it is, the slot holds stage gs until this warp arrives on the
+// slot's empty barrier.  Returns false after kStageWaitUs (the decision is the warp's, uniform).
+template <int D>
+__device__ __forceinline__ bool wait_stage(uint32_t sb, int gs) {
+    using C = Cfg<D>;
+    const int slot = gs % C::NSLOT;
+    const uint32_t full = ring_bar<D>(sb, slot);
+    const uint32_t tag = sb + uint32_t(slot * C::SLOT + C::S_TAG);
+    const uint32_t par = uint32_t((gs / C::NSLOT) & 1);
+    uint64_t t0 = 0;
+    for (;;) {
+        const bool ok = mbar_try_wait(full, par) && lds_u32(tag) == uint32_t(gs);
+        if (__all_sync(FULL, ok)) return true;
+        const uint64_t now = global_ns();
+        if (t0 == 0) t0 = now;
+        const bool late = now - t0 > uint64_t(kStageWaitUs) * 1000ull;
+        if (__shfl_sync(FULL, late ? 1 : 0, 0) != 0) return false;
+    }
+}
+
 // A consumer warp when every block takes the same number of stages (spb): stage s of the range is
 // stage s mod spb of block fb0 + s / spb, so the warp goes straight to the stages of its tiles
 // (tile j = w, w + NW, ... of the range; stage j / TPS, tile j mod TPS), waits only on those, and
@@ -892,8 +924,8 @@ __device__ void consumer_by_tile(const AttnArgs &a, uint8_t *smem, int w, int la
         const int gs = j / C::TPS, tw = j % C::TPS;
         const int t0 = (gs % spb) * C::TSB;
         const int slot = gs % C::NSLOT;
-        const uint32_t full = ring_bar<D>(sb, slot), empty = ring_bar<D>(sb, C::NSLOT + slot);
-        if (!uni(mbar_wait_bounded(full, uint32_t((gs / C::NSLOT) & 1), kStageWaitUs))) {
+        const uint32_t empty = ring_bar<D>(sb, C::NSLOT + slot);
+        if (!wait_stage<D>(sb, gs)) {
             if (lane == 0) report(a.status, KVX_ERR_TIMEOUT, DERR_TIMEOUT);
             return;
         }
@@ -942,6 +974,8 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1) attn_kernel(const AttnArgs
             mbar_init(ring_bar<D>(sb, j), 1);               // full: the producer's arrive + bytes
             // empty: one arrive per consumer warp, or per tile when the warps go by tile
             mbar_init(ring_bar<D>(sb, C::NSLOT + j), by_tile ? C::TPS : C::NW);
+            // no stage yet (shared memory keeps whatever an earlier CTA left there)
+            sts_u32(sb + uint32_t(j * C::SLOT + C::S_TAG), 0xFFFFFFFFu);
         }
         fence_mbar_init();
         // a step whose preparation reported an error (its escape records are incomplete) runs no work

@@ -270,3 +270,48 @@ def test_errors_mirror_reference(kvx, cuda, oracle):
         _gpu(kvx, q, kx=kx, vx=vx, seq=301)
     with pytest.raises(RuntimeError, match="not aligned"):
         _gpu(kvx, q, kx=kx, vx=vx, seq=300, threads=3, split=64)
+
+
+@pytest.mark.parametrize("dim", [64, 128, 256])
+def test_plan_mostly_empty_stages(kvx, cuda, oracle, dim):
+    """One long unit among hundreds of 1-3 token units.  Every block of a plan takes the stages
+    of the longest one, so most stages here are empty and the consumer warps run far ahead of the
+    copies: each must still take exactly its own stage (the slot's stage tag, not only the parity
+    of its barrier), run after run."""
+    torch = cuda
+    n_q = 4
+    seqs = [1100] + [1 + (u % 3) for u in range(400)]
+    keep, units, refs, cases = [], [], [], []
+    out = torch.full((len(seqs), n_q, dim), float("nan"), device="cuda")
+    for u, seq in enumerate(seqs):
+        q, k, v = _case(dim, n_q, seq, seed=900 + u, soft=6)
+        kx, vx = oracle.encode(k, 128), oracle.encode(v, 128)
+        refs.append(oracle.attention(q, kx=kx, vx=vx, seq=seq))
+        cases.append((q, k, v))
+        dq = torch.from_numpy(q.view(np.int16)).cuda()
+        ent = []
+        for blob in (kx, vx):
+            d = torch.from_numpy(blob.view(np.int8)).cuda()
+            idx = torch.empty(((blob.size // 8) + 16) * 8, dtype=torch.uint8, device="cuda")
+            nb, nt = kvx.xkv_index(d, blob.size, dim, idx, idx.numel() // 8)
+            assert nt == seq
+            ent.append((d, idx, nb))
+        (dk, kidx, nb), (dv, vidx, _) = ent
+        keep += [dq, dk, kidx, dv, vidx]
+        units.append(kvx.make_unit(dk, dv, dq, out[u], k_index=kidx, v_index=vidx, k_bytes=kx.size,
+                                   v_bytes=vx.size, n_blocks=nb, seq=seq))
+    plan = kvx.Plan(units, n_q, dim, 128)
+    try:
+        first = None
+        for _ in range(20):
+            plan.run()
+            plan.check()
+            got = out.cpu().numpy()
+            if first is None:
+                first = got.copy()
+            else:
+                assert np.array_equal(_bits(first), _bits(got)), "runs differ"
+    finally:
+        plan.close()
+    for u, (g, r, (q, k, v)) in enumerate(zip(first, refs, cases)):
+        assert_attention_close(g, r, q, k, v, f"unit {u} seq={seqs[u]}")
