@@ -87,14 +87,17 @@ def hbm_peak():
         return FALLBACK_HBM_GBS, "of fallback (6.65 TB/s)"
 
 
-def ncu_traffic(config):
-    """DRAM bytes per launch of the attention kernel from the committed ncu summary, if any."""
+def ncu_traffic(config, n_units):
+    """DRAM bytes per launch of the attention kernel from the committed ncu summary, if any,
+    scaled from the captured launch's units to this launch's (the traffic of a unit is fixed)."""
     path = os.path.join(ROOT, "profiles", "ncu_traffic.json")
     try:
         with open(path) as f:
             d = json.load(f)
         e = d.get(str(config))
-        return None if e is None else float(e["dram_bytes_per_launch"])
+        if e is None:
+            return None
+        return float(e["dram_bytes_per_launch"]) * n_units / float(e["units"])
     except Exception:
         return None
 
@@ -609,7 +612,7 @@ def run_kvx(args, rank, world, local):
         return
     peak, peak_src = hbm_peak()
     achieved = algo_bytes / (kern_ms * 1e-3) / 1e9
-    traffic = ncu_traffic(args.config)
+    traffic = ncu_traffic(args.config, n_units)
     line = {
         "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": K,
         "warmup": max(3, args.warmup), "ms_per_step": ms_step, "us_per_step": ms_step * 1e3,

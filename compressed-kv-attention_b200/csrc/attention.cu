@@ -327,27 +327,24 @@ __device__ __forceinline__ void zero_rows(const StoreMap<D> &sm, int from, int l
     }
 }
 
-// Store escapes [e0, e1) of a block over their elements in the warp's NT tiles: record entry i
-// (byte in its 16-token tile | escape word << 16) is the u32 at ents + 4 i -- a shared address of
-// the staged copy, or (HBM variant) the record in global memory.  Entries from em on belong to the
-// second tile.  Slots at or past a tile's valid rows are skipped (rows counts from the first
-// tile's start); slots are even.
-__device__ __forceinline__ void esc_store(uint32_t xb, uint32_t e, int second, int rows, int tile_bytes,
-                                          int row_bytes) {
-    const int rt = rows - (second ? kTileTokens : 0);
-    if (rt > 0 && (e & 0xFFFFu) < uint32_t(rt) * uint32_t(row_bytes))
-        sts_u16(xb + (second ? uint32_t(tile_bytes) : 0u) + (e & 0xFFFEu), e >> 16);
+// Store escapes [e0, e1) of a block over their elements of the stage's tile: record entry i (tile
+// byte | escape word << 16) is the u32 at ents + 4 i -- a shared address of the staged copy, or
+// (HBM variant) the record in global memory.  Slots at or past the stage's valid rows (lim bytes)
+// are skipped; slots are even.
+template <int D>
+__device__ __forceinline__ void esc_patch(uint32_t xb, uint32_t ents, int e0, int e1, uint32_t lim, int lane) {
+    for (int i = e0 + lane; i < e1; i += 32) {
+        const uint32_t e = lds_u32(ents + 4u * uint32_t(i));
+        if ((e & 0xFFFFu) < lim) sts_u16(xb + (e & 0xFFFEu), e >> 16);
+    }
 }
 template <int D>
-__device__ __forceinline__ void esc_patch(uint32_t xb, uint32_t ents, int e0, int e1, int em, int rows,
-                                          int lane) {
-    for (int i = e0 + lane; i < e1; i += 32)
-        esc_store(xb, lds_u32(ents + 4u * uint32_t(i)), i >= em, rows, Cfg<D>::TILE, 2 * D);
-}
-template <int D>
-__device__ __noinline__ void esc_patch_hbm(uint32_t xb, const uint32_t *ents, int e0, int e1, int em,
-                                           int rows, int lane) {
-    for (int i = e0 + lane; i < e1; i += 32) esc_store(xb, __ldg(ents + i), i >= em, rows, Cfg<D>::TILE, 2 * D);
+__device__ __noinline__ void esc_patch_hbm(uint32_t xb, const uint32_t *ents, int e0, int e1, uint32_t lim,
+                                           int lane) {
+    for (int i = e0 + lane; i < e1; i += 32) {
+        const uint32_t e = __ldg(ents + i);
+        if ((e & 0xFFFFu) < lim) sts_u16(xb + (e & 0xFFFEu), e >> 16);
+    }
 }
 
 // ---- tiles on the tensor cores ------------------------------------------------------------------
@@ -875,11 +872,13 @@ __device__ void consumer(const AttnArgs &a, uint8_t *smem, int w, int lane, int 
 }
 
 // Wait until stage gs of the CTA has landed in its slot.  The slot's full barrier alone cannot tell
-// stage gs from stage gs - NSLOT (the slot's previous use, copied by the other producer warp's
-// sequence of stages or still in flight): a warp that skips stages may start waiting before that
-// stage has landed, and the parity check would then pass one phase early.  So the warp also reads
-// the stage tag, which the producer writes before the arrive that completes the phase, and keeps
-// waiting until it is gs.  Once it is, the slot holds stage gs until this warp arrives on the
+// stage gs from stage gs - 2 NSLOT: a warp that skips stages may start waiting while the slot's
+// previous stage (gs - NSLOT) is still in flight, and the parity test would then pass one phase
+// early.  So the warp first reads the stage tag, which the producer writes once the slot is free
+// for stage gs (stage gs - NSLOT landed and was released) and before the arrive that completes
+// stage gs's phase; only when the tag is gs does it test the barrier.  The tag is read with acquire
+// semantics, so the test after it sees at least the phase of stage gs - NSLOT completed, and then
+// passes only when stage gs has landed; the slot then holds stage gs until this warp arrives on the
 // slot's empty barrier.  Returns false after kStageWaitUs (the decision is the warp's, uniform).
 template <int D>
 __device__ __forceinline__ bool wait_stage(uint32_t sb, int gs) {
@@ -890,7 +889,7 @@ __device__ __forceinline__ bool wait_stage(uint32_t sb, int gs) {
     const uint32_t par = uint32_t((gs / C::NSLOT) & 1);
     uint64_t t0 = 0;
     for (;;) {
-        const bool ok = mbar_try_wait(full, par) && lds_u32(tag) == uint32_t(gs);
+        const bool ok = lds_acquire_u32(tag) == uint32_t(gs) && mbar_try_wait(full, par);
         if (__all_sync(FULL, ok)) return true;
         const uint64_t now = global_ns();
         if (t0 == 0) t0 = now;

@@ -160,6 +160,13 @@ __device__ inline uint32_t lds_u32(uint32_t a) {
     asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a));
     return v;
 }
+// Shared-memory load with acquire semantics at CTA scope: operations after it (an mbarrier test
+// included) observe at least what was visible to its writer when the loaded value was stored.
+__device__ inline uint32_t lds_acquire_u32(uint32_t a) {
+    uint32_t v;
+    asm volatile("ld.acquire.cta.shared::cta.u32 %0, [%1];" : "=r"(v) : "r"(a) : "memory");
+    return v;
+}
 __device__ inline uint32_t lds_u16(uint32_t a) {
     unsigned short v;
     asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(a));
