@@ -79,20 +79,26 @@ class Oracle(_Lib):
         L.ox_encode_bound.argtypes = [C.c_int, C.c_int, C.c_int]
         L.ox_encode_bf16.argtypes = [_u16p, C.c_int, C.c_int, C.c_int, _u8p, C.c_size_t,
                                      C.POINTER(C.c_size_t), _u8p]
+        L.ox_encode_bf16_modes.argtypes = [_u16p, C.c_int, C.c_int, C.c_int, C.c_int, _u8p,
+                                           C.c_size_t, C.POINTER(C.c_size_t), _u8p]
         L.ox_decode_bf16.argtypes = [_u8p, C.c_size_t, C.c_int, C.c_int, _u16p]
         L.ox_attention_decode.argtypes = [_u16p, _u16p, _u16p, _u8p, C.c_size_t, _u8p,
                                           C.c_size_t, _f32p, C.c_int, C.c_int, C.c_int, C.c_int,
                                           C.c_int]
 
-    def encode(self, kv: np.ndarray, block: int = 128, with_modes: bool = False):
+    def encode(self, kv: np.ndarray, block: int = 128, with_modes: bool = False,
+               code_bits=(2, 4)):
+        """Encode like kvexp::encode_bf16; code_bits=(2, 3, 4) also allows the 3-bit extension."""
         kv = np.ascontiguousarray(kv, dtype=np.uint16)
         seq, dim = kv.shape
         cap = max(1, self.lib.ox_encode_bound(seq, dim, block))
         out = np.zeros(cap, dtype=np.uint8)
         nb = C.c_size_t(0)
         modes = np.zeros(max(1, (seq + block - 1) // block), dtype=np.uint8)
-        self.check(self.lib.ox_encode_bf16(_ptr(kv, _u16p), seq, dim, block, _ptr(out, _u8p),
-                                           cap, C.byref(nb), _ptr(modes, _u8p)))
+        mask = sum(1 << b for b in set(code_bits))
+        self.check(self.lib.ox_encode_bf16_modes(_ptr(kv, _u16p), seq, dim, block, mask,
+                                                 _ptr(out, _u8p), cap, C.byref(nb),
+                                                 _ptr(modes, _u8p)))
         blob = out[: nb.value].copy()
         return (blob, modes) if with_modes else blob
 

@@ -5,6 +5,15 @@
  * Each function names the reference file:line it follows.  Compile with
  * -ffp-contract=off -fno-fast-math so every fmaf / expf / + / * rounds as in the
  * reference's scalar kernel (reference CMakeLists.txt:48).
+ *
+ * One extension has no reference code: the 3-bit residual mode (mode byte 3), which the
+ * reference measured and did not implement (README.md:35, :200).  Its size model is the one of
+ * python/analyze_exponents.py:101-103 (width 7 = 2^3 - 1 exponents per window, sentinel 7) and
+ * :129-138 (the same best-window search and tie rules as 2 and 4 bits); its layout is this
+ * library's: element i's code in bits [3 i, 3 i + 3) of the little-endian code bytes, the code
+ * section padded with one zero byte to an even length when 3 n dim / 8 is odd (so every section
+ * of a blob stays 2-byte aligned).  The reference's own encoder never writes it: 3-bit blocks are
+ * emitted only when the caller's mode mask asks for them.
  */
 #include "xkv_oracle.h"
 
@@ -42,7 +51,10 @@ static uint16_t bf16_from_delta(uint8_t base, uint8_t delta, uint8_t sm) {
     return (uint16_t)(((uint16_t)(sm & 0x80) << 8) | ((uint16_t)e << 7) | (uint16_t)(sm & 0x7F));
 }
 
-int ox_exp_payload_bytes(int n_tokens, int dim, int bits) { return (n_tokens * dim * bits + 7) / 8; }
+int ox_exp_payload_bytes(int n_tokens, int dim, int bits) {
+    if (bits == 3) return (n_tokens * dim * 3 + 15) / 16 * 2; /* extension: padded to even */
+    return (n_tokens * dim * bits + 7) / 8;
+}
 
 int ox_coded_block_bytes(int n_tokens, int dim, int bits, int n_escape) {
     return 8 + dim + n_tokens * dim + ox_exp_payload_bytes(n_tokens, dim, bits) + 2 * n_escape;
@@ -78,7 +90,8 @@ int ox_parse_block(const uint8_t *blob, size_t bytes, size_t offset, int dim, ox
         b->next = offset + 8 + nbytes;
         return OX_OK;
     }
-    if (b->mode != 2 && b->mode != 4) return fail(OX_RUNTIME, "unknown xkv block mode");
+    /* mode 3 (3-bit residuals) is this library's extension; the reference knows 2 and 4 */
+    if (b->mode != 2 && b->mode != 3 && b->mode != 4) return fail(OX_RUNTIME, "unknown xkv block mode");
     size_t sm_bytes = (size_t)b->n_tokens * (size_t)dim;
     size_t exp_bytes = (size_t)ox_exp_payload_bytes(b->n_tokens, dim, b->mode);
     size_t esc_bytes = (size_t)b->n_escape * 2u;
@@ -92,6 +105,12 @@ static int residual_code(const uint8_t *exp, int index, int bits) {
     if (bits == 4) {
         uint8_t byte = exp[index >> 1];
         return (index & 1) ? (byte >> 4) : (byte & 0x0F);
+    }
+    if (bits == 3) { /* extension: bits [3 index, 3 index + 3), little-endian */
+        const int bit = 3 * index, sh = bit & 7;
+        int v = exp[bit >> 3] >> sh;
+        if (sh > 5) v |= exp[(bit >> 3) + 1] << (8 - sh);
+        return v & 7;
     }
     uint8_t byte = exp[index >> 2];
     return (byte >> ((index & 3) * 2)) & 0x03;
@@ -248,6 +267,12 @@ static void put_u16(uint8_t *p, uint16_t v) {
 
 int ox_encode_bf16(const uint16_t *kv, int seq, int dim, int block_tokens, uint8_t *out,
                    size_t out_cap, size_t *out_bytes, uint8_t *modes) {
+    return ox_encode_bf16_modes(kv, seq, dim, block_tokens, OX_MODES_REFERENCE, out, out_cap,
+                                out_bytes, modes);
+}
+
+int ox_encode_bf16_modes(const uint16_t *kv, int seq, int dim, int block_tokens, int mode_mask,
+                         uint8_t *out, size_t out_cap, size_t *out_bytes, uint8_t *modes) {
     /* validation, codec.cpp:40-52 */
     if (kv == NULL || seq <= 0 || dim <= 0 || block_tokens <= 0)
         return fail(OX_INVALID_ARGUMENT, "encode_bf16: empty input");
@@ -258,6 +283,8 @@ int ox_encode_bf16(const uint16_t *kv, int seq, int dim, int block_tokens, uint8
         return fail(OX_INVALID_ARGUMENT, "encode_bf16: block_tokens must fit in a byte");
     if ((long long)block_tokens * dim > 65535)
         return fail(OX_INVALID_ARGUMENT, "encode_bf16: block escape count would not fit in u16");
+    if ((mode_mask & ~OX_MODES_ALL) != 0 || (mode_mask & OX_MODES_REFERENCE) != OX_MODES_REFERENCE)
+        return fail(OX_INVALID_ARGUMENT, "encode_bf16: mode mask must hold 2 and 4 bits, and may add 3");
 
     int *hist = (int *)malloc(sizeof(int) * (size_t)dim * 256u);
     uint8_t *base_exp = (uint8_t *)malloc((size_t)dim);
@@ -278,9 +305,11 @@ int ox_encode_bf16(const uint16_t *kv, int seq, int dim, int block_tokens, uint8
         for (int t = 0; t < n; ++t)
             for (int d = 0; d < dim; ++d) ++hist[(size_t)d * 256 + bf16_exponent(src[(size_t)t * dim + d])];
 
-        /* mode choice with tie rules, codec.cpp:75-103 */
+        /* mode choice with tie rules, codec.cpp:75-103 (candidates narrowest first, so a tie
+         * between coded modes keeps fewer escapes, then the narrower code) */
         int best_mode = 0, best_bytes = ox_raw_block_bytes(n, dim), best_esc = 0;
-        for (int bits = 2; bits <= 4; bits += 2) {
+        for (int bits = 2; bits <= 4; ++bits) {
+            if (!(mode_mask & (1 << bits))) continue;
             const int width = (1 << bits) - 1;
             int n_esc = 0;
             for (int d = 0; d < dim; ++d) {
@@ -346,6 +375,10 @@ int ox_encode_bf16(const uint16_t *kv, int seq, int dim, int block_tokens, uint8
                 if (bits == 4) {
                     if ((index & 1) == 0) packed[index >> 1] = (uint8_t)code;
                     else packed[index >> 1] |= (uint8_t)(code << 4);
+                } else if (bits == 3) { /* extension: bits [3 index, 3 index + 3) */
+                    const int bit = 3 * index, sh = bit & 7;
+                    packed[bit >> 3] |= (uint8_t)(code << sh);
+                    if (sh > 5) packed[(bit >> 3) + 1] |= (uint8_t)(code >> (8 - sh));
                 } else {
                     packed[index >> 2] |= (uint8_t)(code << ((index & 3) * 2));
                 }

@@ -53,6 +53,13 @@ int ox_encode_bf16(const uint16_t *kv, int seq, int dim, int block_tokens, uint8
                    size_t out_cap, size_t *out_bytes, uint8_t *modes);
 
 /* Decode an XKV container into [seq, dim] BF16 bits. */
+/* The same with a mask of allowed code widths (bit b: b-bit residuals): OX_MODES_REFERENCE is the
+ * reference encoder's {2, 4}; OX_MODES_ALL adds this library's 3-bit extension. */
+#define OX_MODES_REFERENCE ((1 << 2) | (1 << 4))
+#define OX_MODES_ALL ((1 << 2) | (1 << 3) | (1 << 4))
+int ox_encode_bf16_modes(const uint16_t *kv, int seq, int dim, int block_tokens, int mode_mask,
+                         uint8_t *out, size_t out_cap, size_t *out_bytes, uint8_t *modes);
+
 int ox_decode_bf16(const uint8_t *blob, size_t bytes, int seq, int dim, uint16_t *out);
 
 /* One parsed block header (include/kvexp/scan.hpp:12-22 BlockView, as offsets). */

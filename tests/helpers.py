@@ -37,6 +37,29 @@ def clustered(rng, n, base, spread):
     return out
 
 
+def mixed_modes(seq, dim, block, seed=7):
+    """BF16 bits whose blocks favour every mode of the {raw, 2, 3, 4}-bit policy in turn: block b
+    draws its exponents per channel from a window of 3, 7, 15 or 64 values (2-bit, 3-bit, 4-bit,
+    raw), with a few outliers and the special classes (+-0, subnormals, +-inf, NaN)."""
+    rng = np.random.default_rng(seed)
+    spreads = (3, 7, 15, 64)
+    x = np.empty((seq, dim), dtype=np.uint16)
+    for b0 in range(0, seq, block):
+        n = min(block, seq - b0)
+        spread = spreads[(b0 // block) % len(spreads)]
+        base = rng.integers(100, 130, size=dim)
+        e = base[None, :] + rng.integers(0, spread, size=(n, dim))
+        out = rng.random((n, dim)) < 0.01
+        e[out] = rng.integers(1, 255, size=int(out.sum()))
+        x[b0:b0 + n] = ((rng.integers(0, 2, size=(n, dim)) << 15) | ((e & 0xFF) << 7) |
+                        rng.integers(0, 128, size=(n, dim))).astype(np.uint16)
+    specials = np.array([0x0000, 0x8000, 0x0001, 0x807F, 0x7F80, 0xFF80, 0x7FC0, 0xFFC1],
+                        dtype=np.uint16)
+    flat = x.reshape(-1)
+    flat[::211] = specials[np.arange(flat[::211].size) % specials.size]
+    return x
+
+
 def assert_attention_close(gpu, ref, q=None, k=None, v=None, what="", truth=None):
     """The GPU output against the float64 truth and the reference's output (oracle/parity.py):
     per element |gpu - truth| <= tol and |gpu - ref| <= |ref - truth| + tol.  `truth` = the

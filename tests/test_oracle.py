@@ -162,7 +162,7 @@ def test_malformed_blob_errors(oracle):
     with pytest.raises(O.OracleError, match="ran out of blocks"):
         oracle.decode(blob[:_sizes(blob)[0][0]], 256, 64)
     bad = blob.copy()
-    bad[0] = 3  # mode byte of the first header
+    bad[0] = 5  # mode byte of the first header (3 is the library's 3-bit extension)
     with pytest.raises(O.OracleError, match="unknown xkv block mode"):
         oracle.decode(bad, 256, 64)
 
