@@ -56,6 +56,9 @@ def parse():
                     help="skip the check of the timed outputs against the reference")
     ap.add_argument("--e2e-steps", type=int, default=8)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--code-bits", default="24", choices=["24", "234"],
+                    help="residual widths of the GPU-encoded cache: the reference's {2, 4} "
+                         "(default), or with the library's 3-bit extension")
     ap.add_argument("--units", type=int, default=0,
                     help="only the first N units of this GPU's share (small cases for profilers; "
                          "not a bench line of the config)")
@@ -316,7 +319,7 @@ def run_reference(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
-def parity_check(qs, ks, vs, cfg, plan_out, e2e_out):
+def parity_check(qs, ks, vs, cfg, plan_out, e2e_out, three_bit=False):
     """Check GPU outputs of the timed units against the float64 truth and the reference
     library's scalar kernel (oracle/_ref, or the C restatement when the reference was not built)
     on the same blobs and queries (oracle/parity.py: |gpu - truth| <= tol, and
@@ -327,7 +330,8 @@ def parity_check(qs, ks, vs, cfg, plan_out, e2e_out):
     import oracle as O
     import parity as P
     n = len(qs)
-    ref = O.reference()
+    # the reference cannot read 3-bit blocks: the oracle's restatement (which can) checks those
+    ref = None if three_bit else O.reference()
     outs = [np.zeros((cfg.group, cfg.dim), dtype=np.float32) for _ in range(n)]
     threads = max(1, min(n, os.cpu_count() or 1))
     t0 = time.perf_counter()
@@ -433,14 +437,15 @@ def run_kvx(args, rank, world, local):
         unit_ids = list(unit_ids if unit_ids is not None else range(cfg.units))[: args.units]
         parallelism += f"; only the first {len(unit_ids)} units (--units, a profiling case)"
     n_units = cfg.units if unit_ids is None else len(unit_ids)
-    cache = W.build_cache(cfg, unit_ids=unit_ids, seed=seed)
+    code_bits = kvx.CODE_BITS_ALL if args.code_bits == "234" else kvx.CODE_BITS_REFERENCE
+    cache = W.build_cache(cfg, unit_ids=unit_ids, seed=seed, code_bits=code_bits)
     caches = [cache]
     # Copies of the cache rotate between steps, enough that a step's blobs were last read at
     # least 3 x L2 bytes earlier: no step finds its inputs in L2.
     n_copies = 1 if cache.compressed_bytes >= 3 * L2_BYTES else min(
         MAX_COPIES, max(2, -(-3 * L2_BYTES // cache.compressed_bytes)))
     while len(caches) < n_copies:
-        caches.append(W.build_cache(cfg, unit_ids=unit_ids, seed=seed))
+        caches.append(W.build_cache(cfg, unit_ids=unit_ids, seed=seed, code_bits=code_bits))
     exch = None
     if cfg.shard == "sequence" and world > 1:
         exch = seqsplit.ShardExchange(n_units * cfg.group, cfg.dim)
@@ -577,7 +582,7 @@ def run_kvx(args, rank, world, local):
     # parity: the timed outputs against the reference's scalar kernel on the same units
     parity = None
     if exch is None and not args.no_parity:
-        parity = parity_check(qs, ks, vs, cfg, plan_out, e2e_out)
+        parity = parity_check(qs, ks, vs, cfg, plan_out, e2e_out, three_bit=args.code_bits == "234")
         if dist:
             keys = [k for k in ("plan", "e2e") if k in parity]
             vals = [parity[k][f] for k in keys for f in ("accuracy", "parity", "gpu_err_over_scale")]
@@ -594,7 +599,7 @@ def run_kvx(args, rank, world, local):
             parity["ranks"] = f"every rank checked its own sample; worst over {world} ranks"
 
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and args.code_bits == "24":
         import oracle as O
         cpu, _ = cpu_reference_rate(qs, ks, vs, cfg, args.cpu_seconds)
         ref = O.reference()
@@ -625,6 +630,9 @@ def run_kvx(args, rank, world, local):
             "block_tokens": cfg.block, "compressed_bytes_per_gpu_step": comp,
             "tight_bytes_per_gpu_step": tight,
             "container_ratio": comp / tight,
+            "code_bits": ("{2, 4} (the reference's container)" if args.code_bits == "24" else
+                          "{2, 3, 4} (with the library's 3-bit extension; the reference cannot "
+                          "read these blobs, so no CPU baseline and parity against the oracle)"),
             "parallelism": parallelism,
             "l2": (f"{len(caches)} cache copies rotate between steps: a step's inputs were last "
                    f"read {(len(caches) - 1) * comp / 1e6:.0f} MB earlier (L2 126 MB)"

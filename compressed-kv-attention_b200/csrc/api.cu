@@ -182,7 +182,7 @@ int host_walk(const uint8_t *blob, size_t bytes, int dim, HostIndex &idx) {
         if (mode == 0) {
             need = size_t(nt) * dim * 2;
             if (rest < need) return fail(KVX_ERR_RUNTIME, "truncated raw xkv block");
-        } else if (mode != 2 && mode != 4) {
+        } else if (mode != 2 && mode != 3 && mode != 4) {  // 3: the library's 3-bit extension
             return fail(KVX_ERR_RUNTIME, "unknown xkv block mode");
         } else {
             need = size_t(dim) + size_t(nt) * dim + size_t(exp_payload_bytes(nt, dim, mode)) +
@@ -1061,6 +1061,14 @@ int check_encode_args(const void *kv, int seq_len, int head_dim, int block_token
     return KVX_OK;
 }
 
+int check_code_bits(int code_bits) {
+    if ((code_bits & ~KVX_CODE_BITS_ALL) != 0 ||
+        (code_bits & KVX_CODE_BITS_REFERENCE) != KVX_CODE_BITS_REFERENCE)
+        return fail(KVX_ERR_INVALID_ARGUMENT,
+                    "encode_bf16: mode mask must hold 2 and 4 bits, and may add 3");
+    return KVX_OK;
+}
+
 size_t blob_bound(int seq, int dim, int bt) {
     const size_t nb = (size_t(seq) + size_t(bt) - 1) / size_t(bt);
     return nb * 8u + 2u * size_t(seq) * size_t(dim);
@@ -1068,7 +1076,7 @@ size_t blob_bound(int seq, int dim, int bt) {
 
 // Encode n device tensors: analyze, lay out, emit.  Offsets are relative to `arena`.
 int encode_device(const uint16_t *const *dev_tensors_host, int n, int seq, int dim, int bt,
-                  uint8_t *arena, size_t cap, kvx_block *index, uint64_t *blob_off,
+                  int code_bits, uint8_t *arena, size_t cap, kvx_block *index, uint64_t *blob_off,
                   uint64_t *blob_bytes, cudaStream_t s) {
     const int nb_per = (seq + bt - 1) / bt;
     const size_t nb = size_t(n) * size_t(nb_per);
@@ -1081,7 +1089,8 @@ int encode_device(const uint16_t *const *dev_tensors_host, int n, int seq, int d
     KVX_CUDA(status.alloc(2 * sizeof(int), s));
     KVX_CUDA(cudaMemsetAsync(status.p, 0, 2 * sizeof(int), s));
     const uint16_t *const *dt = tens.as<const uint16_t *const>();
-    KVX_CUDA(launch_encode_analyze(dt, n, seq, dim, bt, blocks.as<EncBlock>(), bases.as<uint8_t>(), s));
+    KVX_CUDA(launch_encode_analyze(dt, n, seq, dim, bt, code_bits, blocks.as<EncBlock>(),
+                                   bases.as<uint8_t>(), s));
     std::vector<EncBlock> hb(nb);
     KVX_CUDA(cudaMemcpyAsync(hb.data(), blocks.p, nb * sizeof(EncBlock), cudaMemcpyDeviceToHost, s));
     KVX_CUDA(cudaStreamSynchronize(s));
@@ -1121,7 +1130,15 @@ extern "C" size_t kvx_encode_bound(int seq_len, int head_dim, int block_tokens) 
 
 extern "C" int kvx_encode_bf16(const uint16_t *kv, int seq_len, int head_dim, int block_tokens,
                                uint8_t *out, size_t out_capacity, size_t *out_bytes) {
+    return kvx_encode_bf16_bits(kv, seq_len, head_dim, block_tokens, KVX_CODE_BITS_REFERENCE, out,
+                                out_capacity, out_bytes);
+}
+
+extern "C" int kvx_encode_bf16_bits(const uint16_t *kv, int seq_len, int head_dim, int block_tokens,
+                                    int code_bits, uint8_t *out, size_t out_capacity,
+                                    size_t *out_bytes) {
     if (int rc = check_encode_args(kv, seq_len, head_dim, block_tokens)) return rc;
+    if (int rc = check_code_bits(code_bits)) return rc;
     if (out == nullptr) return fail(KVX_ERR_INVALID_ARGUMENT, "encode_bf16: null output");
     if (int rc = check_device()) return rc;
     cudaStream_t s = nullptr;
@@ -1134,8 +1151,8 @@ extern "C" int kvx_encode_bf16(const uint16_t *kv, int seq_len, int head_dim, in
     KVX_CUDA(index.alloc(size_t(nb) * sizeof(kvx_block), s));
     const uint16_t *tp = static_cast<const uint16_t *>(dsrc);
     uint64_t boff = 0, bbytes = 0;
-    if (int rc = encode_device(&tp, 1, seq_len, head_dim, block_tokens, arena.as<uint8_t>(), cap,
-                               index.as<kvx_block>(), &boff, &bbytes, s))
+    if (int rc = encode_device(&tp, 1, seq_len, head_dim, block_tokens, code_bits,
+                               arena.as<uint8_t>(), cap, index.as<kvx_block>(), &boff, &bbytes, s))
         return rc;
     if (bbytes > out_capacity) return fail(KVX_ERR_INVALID_ARGUMENT, "encode_bf16: output capacity too small");
     KVX_CUDA(cudaMemcpy(out, arena.as<uint8_t>() + boff, bbytes,
@@ -1246,14 +1263,24 @@ extern "C" int kvx_encode_batch(int n_tensors, const uint16_t *const *kv, int se
                                 int block_tokens, uint8_t *arena, size_t arena_capacity,
                                 kvx_block *index, uint64_t *blob_offset, uint64_t *blob_bytes,
                                 void *stream) {
+    return kvx_encode_batch_bits(n_tensors, kv, seq, head_dim, block_tokens, KVX_CODE_BITS_REFERENCE,
+                                 arena, arena_capacity, index, blob_offset, blob_bytes, stream);
+}
+
+extern "C" int kvx_encode_batch_bits(int n_tensors, const uint16_t *const *kv, int seq, int head_dim,
+                                     int block_tokens, int code_bits, uint8_t *arena,
+                                     size_t arena_capacity, kvx_block *index, uint64_t *blob_offset,
+                                     uint64_t *blob_bytes, void *stream) {
     if (n_tensors <= 0 || kv == nullptr || arena == nullptr || index == nullptr ||
         blob_offset == nullptr || blob_bytes == nullptr)
         return fail(KVX_ERR_INVALID_ARGUMENT, "encode_batch: bad argument");
     if (int rc = check_encode_args(kv[0], seq, head_dim, block_tokens)) return rc;
+    if (int rc = check_code_bits(code_bits)) return rc;
     if (reinterpret_cast<uintptr_t>(arena) & 15u)
         return fail(KVX_ERR_INVALID_ARGUMENT, "encode_batch: arena must be 16-byte aligned");
-    if (int rc = encode_device(kv, n_tensors, seq, head_dim, block_tokens, arena, arena_capacity,
-                               index, blob_offset, blob_bytes, static_cast<cudaStream_t>(stream)))
+    if (int rc = encode_device(kv, n_tensors, seq, head_dim, block_tokens, code_bits, arena,
+                               arena_capacity, index, blob_offset, blob_bytes,
+                               static_cast<cudaStream_t>(stream)))
         return rc;
     g_err.clear();
     return KVX_OK;
@@ -1262,7 +1289,16 @@ extern "C" int kvx_encode_batch(int n_tensors, const uint16_t *const *kv, int se
 extern "C" int kvx_cache_append(const uint16_t *kv_new, int n_new, int head_dim, int block_tokens,
                                 uint8_t *blob, size_t at, size_t capacity, kvx_block *index,
                                 size_t *bytes_written, int *blocks_written, void *stream) {
+    return kvx_cache_append_bits(kv_new, n_new, head_dim, block_tokens, KVX_CODE_BITS_REFERENCE, blob,
+                                 at, capacity, index, bytes_written, blocks_written, stream);
+}
+
+extern "C" int kvx_cache_append_bits(const uint16_t *kv_new, int n_new, int head_dim, int block_tokens,
+                                     int code_bits, uint8_t *blob, size_t at, size_t capacity,
+                                     kvx_block *index, size_t *bytes_written, int *blocks_written,
+                                     void *stream) {
     if (int rc = check_encode_args(kv_new, n_new, head_dim, block_tokens)) return rc;
+    if (int rc = check_code_bits(code_bits)) return rc;
     if (blob == nullptr || index == nullptr)
         return fail(KVX_ERR_INVALID_ARGUMENT, "cache_append: bad argument");
     cudaStream_t s = static_cast<cudaStream_t>(stream);
@@ -1271,8 +1307,8 @@ extern "C" int kvx_cache_append(const uint16_t *kv_new, int n_new, int head_dim,
     KVX_CUDA(tmp.alloc(cap, s));
     uint64_t boff = 0, bbytes = 0;
     const int nb = (n_new + block_tokens - 1) / block_tokens;
-    if (int rc = encode_device(&kv_new, 1, n_new, head_dim, block_tokens, tmp.as<uint8_t>(), cap,
-                               index, &boff, &bbytes, s))
+    if (int rc = encode_device(&kv_new, 1, n_new, head_dim, block_tokens, code_bits,
+                               tmp.as<uint8_t>(), cap, index, &boff, &bbytes, s))
         return rc;
     if (at + bbytes > capacity) return fail(KVX_ERR_INVALID_ARGUMENT, "cache_append: blob capacity too small");
     KVX_CUDA(cudaMemcpyAsync(blob + at, tmp.as<uint8_t>() + boff, bbytes, cudaMemcpyDeviceToDevice, s));

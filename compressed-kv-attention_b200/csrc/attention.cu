@@ -169,9 +169,10 @@ __device__ __forceinline__ uint32_t merge(uint32_t sg, uint32_t cw, uint32_t b7)
 
 // How this lane reads one tensor of the current block from a ring stage: the 8-element chunk c8
 // (head dims 8 c8 .. 8 c8 + 7) of rows t0 + RPI k.  The residual codes start in the 16-byte line at
-// code_base (the codes' own copy, or right behind the rows when rows and codes came as one).  Row sections start m = 0 or 2 bytes past a
-// 4-byte boundary of the ring; the chunk adds a multiple of 4 to the sign/mantissa and raw rows,
-// and 4 (4-bit) or 2 (2-bit) bytes per chunk to the residual rows.
+// code_base (the codes' own copy, or right behind the rows when rows and codes came as one).  Row
+// sections start m = 0 or 2 bytes past a 4-byte boundary of the ring; the chunk adds a multiple of
+// 4 to the sign/mantissa and raw rows, and 4 (4-bit), 3 (3-bit) or 2 (2-bit) bytes per chunk to
+// the residual rows.
 struct Lay {
     uint32_t p0, p1;  // sign/mantissa bytes of element pairs 2q and 2q+1 from words q, q+1
     uint32_t w;       // one realigned word from two loaded ones (raw rows)
@@ -192,7 +193,7 @@ __device__ __forceinline__ Lay make_lay(uint32_t rd, uint32_t cd, int mode, int 
     l.w = m2 ? shift4(2) : shift4(0);
     l.rows = (rd & ~3u) + uint32_t((bf16 || mode == 0) ? 16 * c8 : 8 * c8);
     const uint32_t cb = (cd & 3u) + uint32_t(c8 * (mode == 0 ? 0 : mode));
-    l.cs = (cb & 2u) != 0u ? shift4(2) : shift4(0);
+    l.cs = shift4(0) + (cb & 3u) * 0x1111u;  // bytes o .. o + 3, o = cb mod 4 (odd only for 3-bit)
     l.codes = code_base + (cd & ~3u) + (cb & ~3u);
     return l;
 }
@@ -244,7 +245,7 @@ __device__ __forceinline__ void load_chunks(uint32_t qr, uint32_t qc, uint32_t (
         if constexpr (MODE != 0) {
             const uint32_t c = qc + uint32_t((K0 + g) * RPI * CB);
             X[g][0] = lds_u32(c);
-            if constexpr (MODE == 4) X[g][1] = lds_u32(c + 4u);
+            if constexpr (MODE >= 3) X[g][1] = lds_u32(c + 4u);
         }
     }
 }
@@ -266,6 +267,15 @@ __device__ __forceinline__ void build_chunk(const Lay &ly, const uint32_t (&b7)[
             c1 = prmt(lo, hi, sel_code(1));
             c2 = prmt(lo, hi, sel_code(2));
             c3 = prmt(lo, hi, sel_code(3));
+        } else if constexpr (MODE == 3) {
+            // 8 residuals of 3 bits in bits 0-23 of x (the library's 3-bit extension): pair j is
+            // the 6 bits at 6 j; times 0x2001 puts its first residual at bit 0 and its second at
+            // bit 16, and the mask keeps those
+            const uint32_t x = prmt(X[0], X[1], ly.cs);
+            c0 = ((x & 0x3Fu) * 0x2001u) & 0x70007u;
+            c1 = (((x >> 6) & 0x3Fu) * 0x2001u) & 0x70007u;
+            c2 = (((x >> 12) & 0x3Fu) * 0x2001u) & 0x70007u;
+            c3 = (((x >> 18) & 0x3Fu) * 0x2001u) & 0x70007u;
         } else {  // 8 residuals of 2 bits in the low 16 bits of x
             const uint32_t x = prmt(X[0], 0u, ly.cs);
             const uint32_t ev = x & 0x3333u, od = (x >> 2) & 0x3333u;
@@ -300,7 +310,7 @@ __device__ __forceinline__ void decode_groups(uint32_t qr, uint32_t qc, const La
     if constexpr (K0 + G < NIT) decode_groups<D, MODE, G, K0 + G, TO>(qr, qc, ly, b7, sm, Wn, Xn);
 }
 
-// Rebuild this lane's chunks of one tensor's 16-token tile into the warp's BF16 tile (MODE 4 / 2
+// Rebuild this lane's chunks of one tensor's 16-token tile into the warp's BF16 tile (MODE 4 / 3 / 2
 // coded, 0 raw BF16).  rb / cb: the tile's rows / residual codes are at rb + ly.rows and
 // cb + ly.codes (plus the lane's row).
 template <int D, int MODE, int TO>
@@ -660,7 +670,8 @@ __device__ __forceinline__ void tile_tensor(const AttnArgs &a, const BlockDesc &
         uint32_t b7[4];
         lds_v4(b7s + 16u * uint32_t(c8), b7[0], b7[1], b7[2], b7[3]);
         if (mode == 4) decode_tile<D, 4, 0>(rb, cb, ly, b7, sm, lane);
-        else decode_tile<D, 2, 0>(rb, cb, ly, b7, sm, lane);
+        else if (mode == 2) decode_tile<D, 2, 0>(rb, cb, ly, b7, sm, lane);
+        else decode_tile<D, 3, 0>(rb, cb, ly, b7, sm, lane);
     } else {
         const uint32_t b7[4] = {0u, 0u, 0u, 0u};
         decode_tile<D, 0, 0>(rb, cb, ly, b7, sm, lane);
@@ -1116,11 +1127,11 @@ __global__ void fold_kernel(const float *__restrict__ parts, int n_parts, int n_
 // ---- worker ranges -----------------------------------------------------------------------------
 
 // Cost of one flat block for the worker split, per attended token and tensor: 4 with 4-bit
-// residuals, 5 with 2-bit ones (more unpacking), 2 for raw rows; plus 1 per escape word, which
+// residuals, 5 with 2- or 3-bit ones (more unpacking), 2 for raw rows; plus 1 per escape word, which
 // costs a lane one staged load and one store.  (Weighting escapes near a token's cost, as an
 // earlier model did, starved the workers that hold escape-dense blocks and left the others
 // about 10 % more work than a balanced split.)
-__device__ __forceinline__ uint64_t mode_cost(int mode) { return mode == 4 ? 4u : (mode == 2 ? 5u : 2u); }
+__device__ __forceinline__ uint64_t mode_cost(int mode) { return mode == 4 ? 4u : (mode == 0 ? 2u : 5u); }
 __device__ __forceinline__ uint64_t block_cost(const FlatBlock &b, bool by_tokens) {
     if (by_tokens) return uint64_t(b.valid);
     return uint64_t(b.valid) * (mode_cost(b.k_mode) + mode_cost(b.v_mode)) + uint64_t(b.k_nesc) + b.v_nesc;

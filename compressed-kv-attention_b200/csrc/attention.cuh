@@ -17,7 +17,7 @@ struct FlatBlock {
     uint32_t v_rec;
     uint16_t k_nesc;  // escape words
     uint16_t v_nesc;
-    uint8_t k_mode;   // 0 raw, 2, 4
+    uint8_t k_mode;   // 0 raw, 2, 3 (extension), 4
     uint8_t v_mode;
     uint8_t n_tok;    // tokens in the encoded block (layout)
     uint8_t valid;    // tokens attended (< n_tok only for the last block of a unit)

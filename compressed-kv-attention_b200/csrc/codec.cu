@@ -50,7 +50,7 @@ __global__ void index_walk_kernel(const uint8_t *blob, uint64_t bytes, int dim, 
                 report(status, KVX_ERR_RUNTIME, DERR_TRUNC_RAW);
                 break;
             }
-        } else if (mode != 2 && mode != 4) {
+        } else if (mode != 2 && mode != 3 && mode != 4) {
             report(status, KVX_ERR_RUNTIME, DERR_MODE);
             break;
         } else {
@@ -121,8 +121,8 @@ __global__ void build_flat_kernel(const kvx_unit *units, const int64_t *block_be
         } else {
             const kvx_block ke = U.k_index[j], ve = U.v_index[j];
             if (ke.n_tokens != ve.n_tokens) report(status, KVX_ERR_RUNTIME, DERR_KV_MISMATCH);
-            const bool km = ke.mode == 0 || ke.mode == 2 || ke.mode == 4;
-            const bool vm = ve.mode == 0 || ve.mode == 2 || ve.mode == 4;
+            const bool km = ke.mode == 0 || (ke.mode >= 2 && ke.mode <= 4);
+            const bool vm = ve.mode == 0 || (ve.mode >= 2 && ve.mode <= 4);
             if (!km || !vm) report(status, KVX_ERR_RUNTIME, DERR_MODE);
             // Every block of a well-formed blob starts at an even offset (all sizes are even);
             // the kernels rely on it.
@@ -159,6 +159,15 @@ __device__ __forceinline__ uint32_t warp_prefix(uint32_t cnt, uint32_t &total) {
     return pre;
 }
 
+// Residual i of a 3-bit code section: bits [3 i, 3 i + 3) of its little-endian bytes (the
+// library's 3-bit extension; the second byte is read only when the code reaches into it).
+__device__ __forceinline__ uint32_t code3(const uint8_t *ex, int i) {
+    const int bit = 3 * i, sh = bit & 7;
+    uint32_t v = uint32_t(ex[bit >> 3]) >> sh;
+    if (sh > 5) v |= uint32_t(ex[(bit >> 3) + 1]) << (8 - sh);
+    return v & 7u;
+}
+
 __global__ void decode_kernel(const uint8_t *blob, const kvx_block *index,
                               const uint32_t *tok_start, int n_blocks, int dim, int seq,
                               uint16_t *out, int *status) {
@@ -190,7 +199,7 @@ __global__ void decode_kernel(const uint8_t *blob, const kvx_block *index,
             uint32_t c = 0;
             if (i < nel) {
                 c = bits == 4 ? ((ex[i >> 1] >> ((i & 1) * 4)) & 0xF)
-                              : ((ex[i >> 2] >> ((i & 3) * 2)) & 0x3);
+                              : bits == 3 ? code3(ex, i) : ((ex[i >> 2] >> ((i & 3) * 2)) & 0x3);
                 cnt += c == uint32_t(sentinel);
             }
             code[k] = c;
@@ -224,10 +233,10 @@ __global__ void decode_kernel(const uint8_t *blob, const kvx_block *index,
 // ---- encoder ------------------------------------------------------------------------------------
 
 __global__ void enc_analyze_kernel(const uint16_t *const *tensors, int seq, int dim, int bt,
-                                   EncBlock *blocks, uint8_t *bases) {
+                                   int code_bits, EncBlock *blocks, uint8_t *bases) {
     extern __shared__ uint32_t hist[];  // dim * 128 words: two 16-bit bins per word
-    __shared__ uint8_t b3[kMaxHeadDim], b15[kMaxHeadDim];
-    __shared__ int red[2][32];
+    __shared__ uint8_t b3[kMaxHeadDim], b7[kMaxHeadDim], b15[kMaxHeadDim];
+    __shared__ int red[3][32];
     const int nb_per = (seq + bt - 1) / bt;
     const int gb = blockIdx.x;
     const int t = gb / nb_per, b = gb % nb_per;
@@ -241,20 +250,29 @@ __global__ void enc_analyze_kernel(const uint16_t *const *tensors, int seq, int 
         atomicAdd(&hist[d * 128 + (e >> 1)], 1u << (16 * (e & 1)));
     }
     __syncthreads();
-    int cov3 = 0, cov15 = 0;
+    int cov3 = 0, cov7 = 0, cov15 = 0;
     for (int d = threadIdx.x; d < dim; d += blockDim.x) {
         const uint32_t *h = hist + d * 128;
         auto bin = [&](int e) { return int((h[e >> 1] >> (16 * (e & 1))) & 0xFFFF); };
-        // sliding windows of width 3 and 15; strictly-greater keeps the smallest base
+        // sliding windows of width 3, 7 (the 3-bit extension) and 15; strictly-greater keeps the
+        // smallest base
         int c3 = bin(0) + bin(1) + bin(2), best3 = c3, bb3 = 0;
-        int c15 = 0;
+        int c7 = 0, c15 = 0;
+        for (int e = 0; e < 7; ++e) c7 += bin(e);
         for (int e = 0; e < 15; ++e) c15 += bin(e);
-        int best15 = c15, bb15 = 0;
+        int best7 = c7, bb7 = 0, best15 = c15, bb15 = 0;
         for (int base = 1; base <= 256 - 3; ++base) {
             c3 += bin(base + 2) - bin(base - 1);
             if (c3 > best3) {
                 best3 = c3;
                 bb3 = base;
+            }
+            if (base <= 256 - 7) {
+                c7 += bin(base + 6) - bin(base - 1);
+                if (c7 > best7) {
+                    best7 = c7;
+                    bb7 = base;
+                }
             }
             if (base <= 256 - 15) {
                 c15 += bin(base + 14) - bin(base - 1);
@@ -265,32 +283,40 @@ __global__ void enc_analyze_kernel(const uint16_t *const *tensors, int seq, int 
             }
         }
         b3[d] = uint8_t(bb3);
+        b7[d] = uint8_t(bb7);
         b15[d] = uint8_t(bb15);
         cov3 += best3;
+        cov7 += best7;
         cov15 += best15;
     }
     // block reduction of the covered counts
     for (int o = 16; o > 0; o >>= 1) {
         cov3 += __shfl_xor_sync(FULL, cov3, o);
+        cov7 += __shfl_xor_sync(FULL, cov7, o);
         cov15 += __shfl_xor_sync(FULL, cov15, o);
     }
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (lane == 0) {
         red[0][warp] = cov3;
-        red[1][warp] = cov15;
+        red[1][warp] = cov7;
+        red[2][warp] = cov15;
     }
     __syncthreads();
     if (threadIdx.x == 0) {
-        int s3 = 0, s15 = 0;
+        int s3 = 0, s7 = 0, s15 = 0;
         for (int i = 0; i < int(blockDim.x >> 5); ++i) {
             s3 += red[0][i];
-            s15 += red[1][i];
+            s7 += red[1][i];
+            s15 += red[2][i];
         }
-        const int esc[2] = {n * dim - s3, n * dim - s15};
-        // mode choice, src/codec.cpp:75-103
+        const int esc[3] = {n * dim - s3, n * dim - s7, n * dim - s15};
+        // mode choice, src/codec.cpp:75-103, over the allowed widths narrowest first (2, then the
+        // 3-bit extension when code_bits allows it, then 4): ties between coded modes keep fewer
+        // escapes, then the narrower code
         int best_mode = 0, best_bytes = raw_block_bytes(n, dim), best_esc = 0;
-        for (int k = 0; k < 2; ++k) {
-            const int bits = k == 0 ? 2 : 4;
+        for (int k = 0; k < 3; ++k) {
+            const int bits = k + 2;
+            if (!(code_bits & (1 << bits))) continue;
             const int c_bytes = coded_block_bytes(n, dim, bits, esc[k]);
             const bool better_size = c_bytes < best_bytes;
             const bool tie = c_bytes == best_bytes;
@@ -313,7 +339,7 @@ __global__ void enc_analyze_kernel(const uint16_t *const *tensors, int seq, int 
     __syncthreads();
     const int mode = red[0][0];
     for (int d = threadIdx.x; d < dim; d += blockDim.x)
-        bases[size_t(gb) * dim + d] = mode == 2 ? b3[d] : (mode == 4 ? b15[d] : 0);
+        bases[size_t(gb) * dim + d] = mode == 2 ? b3[d] : (mode == 3 ? b7[d] : (mode == 4 ? b15[d] : 0));
 }
 
 __global__ void enc_emit_kernel(const uint16_t *const *tensors, int seq, int dim, int bt,
@@ -368,15 +394,29 @@ __global__ void enc_emit_kernel(const uint16_t *const *tensors, int seq, int dim
     };
     for (int i = threadIdx.x; i < nel; i += blockDim.x)
         osm[i] = uint8_t(((src[i] >> 8) & 0x80) | (src[i] & 0x7F));
-    const int per = 8 / bits;  // elements per packed byte
     const int nbytes = exp_payload_bytes(n, dim, bits);
-    for (int j = threadIdx.x; j < nbytes; j += blockDim.x) {
-        uint32_t v = 0;
-        for (int k = 0; k < per; ++k) {
-            const int i = j * per + k;
-            if (i < nel) v |= uint32_t(code_of(i)) << (k * bits);
+    if (bits == 3) {
+        // byte j holds bits [8 j, 8 j + 8) of the little-endian stream of 3-bit codes: parts of
+        // elements floor(8 j / 3) .. floor((8 j + 7) / 3); the padding byte stays zero
+        for (int j = threadIdx.x; j < nbytes; j += blockDim.x) {
+            uint32_t v = 0;
+            for (int i = (8 * j) / 3; i <= (8 * j + 7) / 3 && i < nel; ++i) {
+                const int sh = 3 * i - 8 * j;
+                const uint32_t c = uint32_t(code_of(i));
+                v |= sh >= 0 ? c << sh : c >> -sh;
+            }
+            oex[j] = uint8_t(v);
         }
-        oex[j] = uint8_t(v);
+    } else {
+        const int per = 8 / bits;  // elements per packed byte
+        for (int j = threadIdx.x; j < nbytes; j += blockDim.x) {
+            uint32_t v = 0;
+            for (int k = 0; k < per; ++k) {
+                const int i = j * per + k;
+                if (i < nel) v |= uint32_t(code_of(i)) << (k * bits);
+            }
+            oex[j] = uint8_t(v);
+        }
     }
     // escapes in scan order
     __syncthreads();
@@ -569,10 +609,42 @@ __global__ void esc_fill_kernel(const UnitDev *units, const FlatBlock *flat, int
     const uint32_t lead = uint32_t(reinterpret_cast<uintptr_t>(codes) & 3u);
     const uint32_t *words = reinterpret_cast<const uint32_t *>(codes - lead);
     const uint32_t nwords = (lead + len + 3) / 4;
-    const int per_byte = 8 / mode;  // residuals per code byte
     uint32_t *pos = esc + rec + kEscRecHead;
     int run = 0;
-    for (uint32_t w0 = 0; w0 < nwords; w0 += 32) {
+    if (mode == 3) {
+        // 3-bit codes: lane l of a step takes the 8 residuals of group g (code bytes 3 g .. 3 g + 2)
+        const int nel = n_tok * dim;
+        const int ngroups = (nel + 7) / 8;
+        for (int g0 = 0; g0 < ngroups; g0 += 32) {
+            const int g = g0 + lane;
+            uint32_t mask = 0;
+            if (g < ngroups) {
+                const uint32_t x = uint32_t(__ldg(codes + 3 * g)) |
+                                   (3 * g + 1 < int(len) ? uint32_t(__ldg(codes + 3 * g + 1)) << 8 : 0u) |
+                                   (3 * g + 2 < int(len) ? uint32_t(__ldg(codes + 3 * g + 2)) << 16 : 0u);
+#pragma unroll
+                for (int k = 0; k < 8; ++k)
+                    if (8 * g + k < nel && ((x >> (3 * k)) & 7u) == 7u) mask |= 1u << k;
+            }
+            const int cnt = __popc(mask);
+            int incl = cnt;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int v = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+                if (lane >= o) incl += v;
+            }
+            int idx = run + incl - cnt;
+            while (mask != 0u) {
+                const int bit = __ffs(mask) - 1;
+                mask &= mask - 1u;
+                if (idx < nesc) pos[idx] = uint32_t(8 * g + bit);
+                ++idx;
+            }
+            run += __shfl_sync(0xFFFFFFFFu, incl, 31);
+        }
+    }
+    const int per_byte = 8 / mode;  // residuals per code byte (2- and 4-bit codes)
+    for (uint32_t w0 = 0; mode != 3 && w0 < nwords; w0 += 32) {
         const uint32_t wi = w0 + uint32_t(lane);
         const uint32_t x = wi < nwords ? __ldg(words + wi) : 0u;
         uint32_t mask = 0;  // bit k: residual k of this word (k = byte * per_byte + slot) is a sentinel
@@ -723,7 +795,7 @@ cudaError_t launch_decode(const uint8_t *blob, const kvx_block *index, const uin
 }
 
 cudaError_t launch_encode_analyze(const uint16_t *const *tensors, int n_tensors, int seq, int dim,
-                                  int block_tokens, EncBlock *blocks, uint8_t *bases,
+                                  int block_tokens, int code_bits, EncBlock *blocks, uint8_t *bases,
                                   cudaStream_t s) {
     const int nb = n_tensors * ((seq + block_tokens - 1) / block_tokens);
     if (nb <= 0) return cudaSuccess;
@@ -734,7 +806,7 @@ cudaError_t launch_encode_analyze(const uint16_t *const *tensors, int n_tensors,
                              int(kMaxHeadDim * 128 * 4));
         configured = true;
     }
-    enc_analyze_kernel<<<nb, 256, sm, s>>>(tensors, seq, dim, block_tokens, blocks, bases);
+    enc_analyze_kernel<<<nb, 256, sm, s>>>(tensors, seq, dim, block_tokens, code_bits, blocks, bases);
     return cudaGetLastError();
 }
 

@@ -35,8 +35,9 @@ cudaError_t launch_decode(const uint8_t *blob, const kvx_block *index, const uin
                           cudaStream_t s);
 
 // Encoder phase 1: one CTA per block of n_tensors tensors of [seq, dim] (device pointer table).
+// code_bits: the residual widths a block may take (bit b: b-bit codes; KVX_CODE_BITS_*).
 cudaError_t launch_encode_analyze(const uint16_t *const *tensors, int n_tensors, int seq, int dim,
-                                  int block_tokens, EncBlock *blocks, uint8_t *bases,
+                                  int block_tokens, int code_bits, EncBlock *blocks, uint8_t *bases,
                                   cudaStream_t s);
 // Encoder phase 3: emit blocks at byte offsets (per block, relative to `arena`).
 cudaError_t launch_encode_emit(const uint16_t *const *tensors, int n_tensors, int seq, int dim,

@@ -34,7 +34,11 @@ enum DeviceError : int {
     DERR_ESC_CAP = 12,      // escape records do not fit the fixed scratch
 };
 
+// Residual code bytes of a coded block: the reference's formula for 2 and 4 bits
+// (include/kvexp/bf16.hpp:39-41); the 3-bit extension rounds 3 n dim / 8 up to an even count so
+// that the escape words that follow stay 2-byte aligned.
 __host__ __device__ inline int exp_payload_bytes(int n_tokens, int dim, int bits) {
+    if (bits == 3) return (n_tokens * dim * 3 + 15) / 16 * 2;
     return (n_tokens * dim * bits + 7) / 8;
 }
 __host__ __device__ inline int coded_block_bytes(int n_tokens, int dim, int bits, int n_escape) {

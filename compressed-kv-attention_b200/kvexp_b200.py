@@ -95,6 +95,8 @@ _attention_units = _sig("kvx_attention_decode_units", C.c_int,
 _encode_bound = _sig("kvx_encode_bound", _sz, [C.c_int, C.c_int, C.c_int])
 _encode = _sig("kvx_encode_bf16", C.c_int,
                [_vp, C.c_int, C.c_int, C.c_int, _vp, _sz, C.POINTER(_sz)])
+_encode_bits = _sig("kvx_encode_bf16_bits", C.c_int,
+                    [_vp, C.c_int, C.c_int, C.c_int, C.c_int, _vp, _sz, C.POINTER(_sz)])
 _decode = _sig("kvx_decode_bf16", C.c_int, [_vp, _sz, C.c_int, C.c_int, _vp])
 _xkv_index = _sig("kvx_xkv_index", C.c_int,
                   [_vp, _sz, C.c_int, _vp, C.c_int, C.POINTER(C.c_int), C.POINTER(C.c_longlong)])
@@ -110,6 +112,12 @@ _enc_bounds = _sig("kvx_encode_batch_bounds", C.c_int,
                    [C.c_int, C.c_int, C.c_int, C.c_int, C.POINTER(_sz), C.POINTER(_sz)])
 _enc_batch = _sig("kvx_encode_batch", C.c_int,
                   [C.c_int, _vp, C.c_int, C.c_int, C.c_int, _vp, _sz, _vp, _vp, _vp, _vp])
+_enc_batch_bits = _sig("kvx_encode_batch_bits", C.c_int,
+                       [C.c_int, _vp, C.c_int, C.c_int, C.c_int, C.c_int, _vp, _sz, _vp, _vp,
+                        _vp, _vp])
+_append_bits = _sig("kvx_cache_append_bits", C.c_int,
+                    [_vp, C.c_int, C.c_int, C.c_int, C.c_int, _vp, _sz, _sz, _vp,
+                     C.POINTER(_sz), C.POINTER(C.c_int), _vp])
 _append = _sig("kvx_cache_append", C.c_int,
                [_vp, C.c_int, C.c_int, C.c_int, _vp, _sz, _sz, _vp, C.POINTER(_sz),
                 C.POINTER(C.c_int), _vp])
@@ -128,8 +136,13 @@ EXPORTED = [
     "kvx_xkv_index", "kvx_plan_create", "kvx_plan_run", "kvx_plan_run_part", "kvx_plan_check", "kvx_plan_launches", "kvx_plan_split_units",
     "kvx_plan_destroy", "kvx_encode_batch_bounds", "kvx_encode_batch", "kvx_cache_append",
     "kvx_synth_bf16", "kvx_hbm_read_probe", "kvx_attention_decode_noalloc", "kvx_fold_shards",
-    "kvx_exponent_stats",
+    "kvx_exponent_stats", "kvx_encode_bf16_bits", "kvx_encode_batch_bits", "kvx_cache_append_bits",
 ]
+
+# Residual code widths the encoder may use (include/kvexp_b200.h KVX_CODE_BITS_*): the reference's
+# {2, 4}, or with the library's 3-bit extension.
+CODE_BITS_REFERENCE = 0x14
+CODE_BITS_ALL = 0x1C
 
 
 def _check(rc: int) -> None:
@@ -218,13 +231,19 @@ def encode_bound(seq_len, head_dim, block_tokens=K_ENCODE_BLOCK) -> int:
     return int(_encode_bound(int(seq_len), int(head_dim), int(block_tokens)))
 
 
-def encode_bf16(kv, seq_len, head_dim, block_tokens=K_ENCODE_BLOCK) -> EncodedTensor:
-    """kvexp::encode_bf16 (include/kvexp/codec.hpp:45-46) on the GPU; byte-identical output."""
+def encode_bf16(kv, seq_len, head_dim, block_tokens=K_ENCODE_BLOCK,
+                code_bits=CODE_BITS_REFERENCE) -> EncodedTensor:
+    """kvexp::encode_bf16 (include/kvexp/codec.hpp:45-46) on the GPU; byte-identical output.
+    code_bits=CODE_BITS_ALL also allows 3-bit blocks (the library's extension)."""
     cap = max(16, encode_bound(seq_len, head_dim, block_tokens))
     out = np.zeros(cap, dtype=np.uint8)
     nb = _sz(0)
-    _check(_encode(_addr(kv), int(seq_len), int(head_dim), int(block_tokens), out.ctypes.data,
-                   cap, C.byref(nb)))
+    if code_bits == CODE_BITS_REFERENCE:
+        _check(_encode(_addr(kv), int(seq_len), int(head_dim), int(block_tokens), out.ctypes.data,
+                       cap, C.byref(nb)))
+    else:
+        _check(_encode_bits(_addr(kv), int(seq_len), int(head_dim), int(block_tokens),
+                            int(code_bits), out.ctypes.data, cap, C.byref(nb)))
     return EncodedTensor(out[: nb.value].copy(), seq_len, head_dim, block_tokens)
 
 
@@ -311,25 +330,35 @@ def encode_batch_bounds(n_tensors, seq, head_dim, block_tokens=K_ENCODE_BLOCK):
 
 
 def encode_batch(tensors, seq, head_dim, arena, index, block_tokens=K_ENCODE_BLOCK,
-                 stream=None):
+                 stream=None, code_bits=CODE_BITS_REFERENCE):
     """GPU-encode device tensors into `arena`; returns (blob_offsets, blob_bytes) numpy arrays."""
     n = len(tensors)
     ptrs = (C.c_void_p * n)(*[_addr(t) for t in tensors])
     off = np.zeros(n, dtype=np.uint64)
     nb = np.zeros(n, dtype=np.uint64)
-    _check(_enc_batch(n, C.cast(ptrs, _vp), int(seq), int(head_dim), int(block_tokens),
-                      _addr(arena), _nbytes(arena), _addr(index), off.ctypes.data,
-                      nb.ctypes.data, stream))
+    if code_bits == CODE_BITS_REFERENCE:
+        _check(_enc_batch(n, C.cast(ptrs, _vp), int(seq), int(head_dim), int(block_tokens),
+                          _addr(arena), _nbytes(arena), _addr(index), off.ctypes.data,
+                          nb.ctypes.data, stream))
+    else:
+        _check(_enc_batch_bits(n, C.cast(ptrs, _vp), int(seq), int(head_dim), int(block_tokens),
+                               int(code_bits), _addr(arena), _nbytes(arena), _addr(index),
+                               off.ctypes.data, nb.ctypes.data, stream))
     return off, nb
 
 
 def cache_append(kv_new, n_new, head_dim, blob, at, capacity, index,
-                 block_tokens=K_ENCODE_BLOCK, stream=None):
+                 block_tokens=K_ENCODE_BLOCK, stream=None, code_bits=CODE_BITS_REFERENCE):
     """Encode n_new tokens and append them at byte `at` of a device blob; returns
     (bytes_written, blocks_written)."""
     bw, kw = _sz(0), C.c_int(0)
-    _check(_append(_addr(kv_new), int(n_new), int(head_dim), int(block_tokens), _addr(blob),
-                   int(at), int(capacity), _addr(index), C.byref(bw), C.byref(kw), stream))
+    if code_bits == CODE_BITS_REFERENCE:
+        _check(_append(_addr(kv_new), int(n_new), int(head_dim), int(block_tokens), _addr(blob),
+                       int(at), int(capacity), _addr(index), C.byref(bw), C.byref(kw), stream))
+    else:
+        _check(_append_bits(_addr(kv_new), int(n_new), int(head_dim), int(block_tokens),
+                            int(code_bits), _addr(blob), int(at), int(capacity), _addr(index),
+                            C.byref(bw), C.byref(kw), stream))
     return bw.value, kw.value
 
 

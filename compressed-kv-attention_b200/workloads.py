@@ -125,8 +125,9 @@ def _torch():
 
 
 def build_cache(cfg: Config, unit_ids=None, seed: int = 0x12345678, device="cuda",
-                chunk_units: int | None = None) -> DeviceCache:
-    """Generate and GPU-encode the units `unit_ids` (default: all) of `cfg`."""
+                chunk_units: int | None = None, code_bits: int | None = None) -> DeviceCache:
+    """Generate and GPU-encode the units `unit_ids` (default: all) of `cfg`; code_bits selects
+    the residual widths (default the reference's {2, 4}; kvx.CODE_BITS_ALL adds 3-bit blocks)."""
     import kvexp_b200 as kvx
     torch = _torch()
     if unit_ids is None:
@@ -159,7 +160,9 @@ def build_cache(cfg: Config, unit_ids=None, seed: int = 0x12345678, device="cuda
         arena_bytes, entries = kvx.encode_batch_bounds(len(tens), cfg.seq, cfg.dim, cfg.block)
         arena = torch.empty(arena_bytes, dtype=torch.uint8, device=device)
         index = torch.empty(entries * 8, dtype=torch.uint8, device=device)
-        off, nbytes = kvx.encode_batch(tens, cfg.seq, cfg.dim, arena, index, cfg.block, stream)
+        off, nbytes = kvx.encode_batch(tens, cfg.seq, cfg.dim, arena, index, cfg.block, stream,
+                                       code_bits=kvx.CODE_BITS_REFERENCE if code_bits is None
+                                       else code_bits)
         del tens
         used = int(off[-1] + nbytes[-1] + 16 + 15) & ~15
         if used < arena_bytes // 2:  # compact large arenas

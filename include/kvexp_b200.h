@@ -91,6 +91,23 @@ KVX_API size_t kvx_encode_bound(int seq_len, int head_dim, int block_tokens);
 KVX_API int kvx_encode_bf16(const uint16_t *kv, int seq_len, int head_dim, int block_tokens,
                     uint8_t *out, size_t out_capacity, size_t *out_bytes);
 
+/* Residual code widths the encoder may choose per block, as a bit mask (bit b: b-bit codes).
+ * KVX_CODE_BITS_REFERENCE is the reference encoder's {2, 4} (what kvx_encode_bf16,
+ * kvx_encode_batch and kvx_cache_append use); KVX_CODE_BITS_ALL adds the 3-bit mode, this
+ * library's extension of the container, which the reference measured (README.md:35) and does not
+ * implement: mode byte 3, base window of 7 exponents with code 7 the escape sentinel, element i's
+ * code in bits [3 i, 3 i + 3) of the little-endian code bytes, the code section padded with a zero
+ * byte to an even length.  Blobs holding mode-3 blocks are read by every entry point of this
+ * library and rejected by the reference ("unknown xkv block mode").  The mode choice extends the
+ * reference's tie rules: smaller block, then raw, then fewer escapes, then the narrower code. */
+#define KVX_CODE_BITS_REFERENCE 0x14
+#define KVX_CODE_BITS_ALL 0x1C
+
+/* kvx_encode_bf16 with a code-width mask (KVX_CODE_BITS_REFERENCE gives the same bytes).  No
+ * counterpart in the reference (3-bit blocks are this library's extension). */
+KVX_API int kvx_encode_bf16_bits(const uint16_t *kv, int seq_len, int head_dim, int block_tokens,
+                         int code_bits, uint8_t *out, size_t out_capacity, size_t *out_bytes);
+
 /* The statistics behind the reference's exponent analyser (python/analyze_exponents.py:57-72
  * `block_conditional_entropy`, :117-156 `policy_size`), on the GPU.  For every block of
  * block_tokens tokens of a [seq_len, head_dim] BF16 tensor (the last block may be shorter) and
@@ -177,6 +194,11 @@ KVX_API int kvx_encode_batch(int n_tensors, const uint16_t *const *kv, int seq, 
                      int block_tokens, uint8_t *arena, size_t arena_capacity,
                      kvx_block *index, uint64_t *blob_offset, uint64_t *blob_bytes,
                      void *stream);
+/* kvx_encode_batch with a code-width mask (KVX_CODE_BITS_*). */
+KVX_API int kvx_encode_batch_bits(int n_tensors, const uint16_t *const *kv, int seq, int head_dim,
+                          int block_tokens, int code_bits, uint8_t *arena,
+                          size_t arena_capacity, kvx_block *index, uint64_t *blob_offset,
+                          uint64_t *blob_bytes, void *stream);
 
 /* Append tokens to a device-resident cache: encode [n_new, head_dim] BF16 (device) as whole
  * blocks starting at byte `at` of `blob` (capacity `capacity`), writing the new blocks' index
@@ -184,6 +206,11 @@ KVX_API int kvx_encode_batch(int n_tensors, const uint16_t *const *kv, int seq, 
 KVX_API int kvx_cache_append(const uint16_t *kv_new, int n_new, int head_dim, int block_tokens,
                      uint8_t *blob, size_t at, size_t capacity, kvx_block *index,
                      size_t *bytes_written, int *blocks_written, void *stream);
+/* kvx_cache_append with a code-width mask (KVX_CODE_BITS_*). */
+KVX_API int kvx_cache_append_bits(const uint16_t *kv_new, int n_new, int head_dim, int block_tokens,
+                          int code_bits, uint8_t *blob, size_t at, size_t capacity,
+                          kvx_block *index, size_t *bytes_written, int *blocks_written,
+                          void *stream);
 
 /* Fold the results of a sequence split (one shard per rank, in rank order) into the result over
  * the whole sequence.  Per row (unit, query): M = max_r lse_r, w_r = exp(lse_r - M),

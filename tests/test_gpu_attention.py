@@ -263,7 +263,7 @@ def test_errors_mirror_reference(kvx, cuda, oracle):
     with pytest.raises(RuntimeError, match="dimension or length mismatch"):
         _gpu(kvx, q, kx=bad, vx=vx, seq=300)
     bad = kx.copy()
-    bad[0] = 3  # mode
+    bad[0] = 5  # mode (3 is the 3-bit extension)
     with pytest.raises(RuntimeError, match="unknown xkv block mode"):
         _gpu(kvx, q, kx=bad, vx=vx, seq=300)
     with pytest.raises(RuntimeError, match="ran out of blocks"):
