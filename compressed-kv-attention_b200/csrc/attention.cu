@@ -66,6 +66,12 @@ template <int D> struct Cfg {
     static constexpr int NIT = TT * C8 / 32;      // chunk steps of a lane per tile and tensor
     static constexpr int TSB = attention_stage_tokens(D);  // tokens per ring stage
     static constexpr int TPS = TSB / TT;          // tiles per stage
+    // Tiles a consumer warp takes together (one visit of a stage): two at D <= 64, where the
+    // per-visit work (waits, descriptor fields, layout selectors, escape bounds, the softmax's
+    // vote) is then shared by 32 tokens and the two tiles' chains interleave; one above, where the
+    // registers are taken by the wider tiles.
+    static constexpr int NT = D <= 64 ? 2 : 1;
+    static constexpr int TPP = TPS / NT;          // tile groups (visits) per stage
     static constexpr int NW = attention_consumer_warps(D);  // consumer warps
     static constexpr int NSLOT = 4;               // ring slots
     // Escape-record entries of one tensor that a stage stages (12.5 % of its elements); a stage
@@ -88,14 +94,16 @@ template <int D> struct Cfg {
     static constexpr int S_TAG = S_INFO + 8;
     static constexpr int S_T = S_INFO + 16;
     static constexpr int SLOT = S_T + 2 * T_BYTES;
-    static constexpr int TILE = TT * 2 * D;       // one consumer warp's BF16 tile (K, then V)
+    static constexpr int TILE1 = TT * 2 * D;      // one 16-token BF16 tile
+    static constexpr int TILE = NT * TILE1;       // one consumer warp's NT tiles (K, then V)
     static constexpr int O_TILE = NSLOT * SLOT;
     static constexpr int O_BAR = O_TILE + NW * TILE;  // full[NSLOT], then empty[NSLOT]
     static constexpr int SMEM = O_BAR + 16 * NSLOT;
     static constexpr int NP = 2;                  // producer warps (stages alternate between them)
     static constexpr int THREADS = 32 * (NW + NP);
     static_assert(SMEM + 16 <= 232448, "stage ring and tiles exceed shared memory");
-    static_assert(NW >= TPS, "a consumer warp takes at most one tile of a stage");
+    static_assert(NW >= TPP, "a consumer warp takes at most one tile group of a stage");
+    static_assert(TPS % NT == 0, "a stage holds whole tile groups");
     static_assert(32 % C8 == 0 && NIT >= 1, "a warp step covers whole rows");
     static_assert((TSB * D) % 4096 == 0, "stage offsets keep every section's 16-byte alignment");
 };
@@ -293,13 +301,15 @@ __device__ __forceinline__ void build_chunk(const Lay &ly, const uint32_t (&b7)[
     }
 }
 
-// Chunk steps [K0, NIT) in groups of G: the loads of the next group are issued before the
-// current group's arithmetic and stores (the shared-memory accesses keep their written order).
+// Chunk steps [K0, NT NIT) in groups of G (the NT tiles' rows follow one another in the stage and
+// in the warp's tile buffer, so step k of tile t is step t NIT + k): the loads of the next group
+// are issued before the current group's arithmetic and stores (the shared-memory accesses keep
+// their written order).
 template <int D, int MODE, int G, int K0, int TO>
 __device__ __forceinline__ void decode_groups(uint32_t qr, uint32_t qc, const Lay &ly, const uint32_t (&b7)[4],
                                               const StoreMap<D> &sm, uint32_t (&W)[G][MODE == 0 ? 5 : 3],
                                               uint32_t (&X)[G][2]) {
-    constexpr int NIT = Cfg<D>::NIT;
+    constexpr int NIT = Cfg<D>::NT * Cfg<D>::NIT;
     uint32_t Wn[G][MODE == 0 ? 5 : 3], Xn[G][2];
     if constexpr (K0 + G < NIT) load_chunks<D, MODE, G, K0 + G>(qr, qc, Wn, Xn);
     uint32_t w[G][4];
@@ -310,9 +320,9 @@ __device__ __forceinline__ void decode_groups(uint32_t qr, uint32_t qc, const La
     if constexpr (K0 + G < NIT) decode_groups<D, MODE, G, K0 + G, TO>(qr, qc, ly, b7, sm, Wn, Xn);
 }
 
-// Rebuild this lane's chunks of one tensor's 16-token tile into the warp's BF16 tile (MODE 4 / 3 / 2
-// coded, 0 raw BF16).  rb / cb: the tile's rows / residual codes are at rb + ly.rows and
-// cb + ly.codes (plus the lane's row).
+// Rebuild this lane's chunks of one tensor's NT 16-token tiles into the warp's BF16 tiles (MODE
+// 4 / 3 / 2 coded, 0 raw BF16).  rb / cb: the first tile's rows / residual codes are at rb + ly.rows
+// and cb + ly.codes (plus the lane's row).
 template <int D, int MODE, int TO>
 __device__ __forceinline__ void decode_tile(uint32_t rb, uint32_t cb, const Lay &ly, const uint32_t (&b7)[4],
                                             const StoreMap<D> &sm, int lane) {
@@ -331,30 +341,34 @@ __device__ __forceinline__ void decode_tile(uint32_t rb, uint32_t cb, const Lay 
 // P is 0 there and V must be finite).
 template <int D, int TO, int J = 0>
 __device__ __forceinline__ void zero_rows(const StoreMap<D> &sm, int from, int lane) {
-    if constexpr (J < Cfg<D>::NIT) {
+    if constexpr (J < Cfg<D>::NT * Cfg<D>::NIT) {
         if (lane / Cfg<D>::C8 + J * StoreMap<D>::RPI >= from) sts_v4(sm.at(J) + uint32_t(TO), 0u, 0u, 0u, 0u);
         zero_rows<D, TO, J + 1>(sm, from, lane);
     }
 }
 
-// Store escapes [e0, e1) of a block over their elements of the stage's tile: record entry i (tile
-// byte | escape word << 16) is the u32 at ents + 4 i -- a shared address of the staged copy, or
-// (HBM variant) the record in global memory.  Slots at or past the stage's valid rows (lim bytes)
-// are skipped; slots are even.
-template <int D>
-__device__ __forceinline__ void esc_patch(uint32_t xb, uint32_t ents, int e0, int e1, uint32_t lim, int lane) {
-    for (int i = e0 + lane; i < e1; i += 32) {
-        const uint32_t e = lds_u32(ents + 4u * uint32_t(i));
-        if ((e & 0xFFFFu) < lim) sts_u16(xb + (e & 0xFFFEu), e >> 16);
-    }
+// Store escapes [e0, e1) of a block over their elements in the warp's NT tiles: record entry i
+// (byte of the element in its 16-token tile | escape word << 16) is the u32 at ents + 4 i -- a
+// shared address of the staged copy, or (HBM variant) the record in global memory.  Entries from
+// em on belong to the second tile.  Elements in rows at or past `rows` (counted from the first
+// tile's first row) are skipped; bytes are even.
+__device__ __forceinline__ void esc_store(uint32_t xb, uint32_t e, bool second, int rows, int tile_bytes,
+                                          int row_bytes) {
+    const int rt = rows - (second ? kTileTokens : 0);
+    if ((e & 0xFFFFu) < uint32_t(max(rt, 0)) * uint32_t(row_bytes))
+        sts_u16(xb + (second ? uint32_t(tile_bytes) : 0u) + (e & 0xFFFEu), e >> 16);
 }
 template <int D>
-__device__ __noinline__ void esc_patch_hbm(uint32_t xb, const uint32_t *ents, int e0, int e1, uint32_t lim,
-                                           int lane) {
-    for (int i = e0 + lane; i < e1; i += 32) {
-        const uint32_t e = __ldg(ents + i);
-        if ((e & 0xFFFFu) < lim) sts_u16(xb + (e & 0xFFFEu), e >> 16);
-    }
+__device__ __forceinline__ void esc_patch(uint32_t xb, uint32_t ents, int e0, int e1, int em, int rows,
+                                          int lane) {
+    for (int i = e0 + lane; i < e1; i += 32)
+        esc_store(xb, lds_u32(ents + 4u * uint32_t(i)), i >= em, rows, Cfg<D>::TILE1, 2 * D);
+}
+template <int D>
+__device__ __noinline__ void esc_patch_hbm(uint32_t xb, const uint32_t *ents, int e0, int e1, int em,
+                                           int rows, int lane) {
+    for (int i = e0 + lane; i < e1; i += 32)
+        esc_store(xb, __ldg(ents + i), i >= em, rows, Cfg<D>::TILE1, 2 * D);
 }
 
 // ---- tiles on the tensor cores ------------------------------------------------------------------
@@ -635,10 +649,11 @@ __device__ void producer(const AttnArgs &a, uint8_t *smem, int fb0, int fb1, int
     }
 }
 
-// One tensor of one tile into the warp's BF16 tile, escapes included.  reg: the tensor's region of
-// the slot; b7s: the tensor's merge words in the slot; info: the producer's escape word of the
-// tensor for this stage; g16: the tile's 16-token group in the block; t0: the stage's first token
-// in the block; rows: valid rows of the tile; zero_from: rows at or past it are zeroed.
+// One tensor of the warp's NT tiles (tiles tw .. tw + NT - 1 of the stage) into its BF16 tiles,
+// escapes included.  reg: the tensor's region of the slot; b7s: the tensor's merge words in the
+// slot; info: the producer's escape word of the tensor for this stage; g16: the first tile's
+// 16-token group in the block; t0: the stage's first token in the block; rows: valid rows from the
+// first tile's first row on; zero_from: rows at or past it are zeroed.
 template <int D, int T>
 __device__ __forceinline__ void tile_tensor(const AttnArgs &a, const BlockDesc &bd, int mode,
                                             uint32_t al, uint32_t reg, uint32_t b7s, uint32_t info, int tw,
@@ -655,10 +670,12 @@ __device__ __forceinline__ void tile_tensor(const AttnArgs &a, const BlockDesc &
     const Lay ly = make_lay<D>(rd, cd, mode, c8, bf16, code_base);
     const uint32_t rb = reg + uint32_t(TT * tw * (mode == 0 ? 2 * D : D));
     const uint32_t cb = reg + uint32_t(TT * tw * (D * mode / 8));
-    // The tile's escapes [e0, e1) are fetched before the decode, one entry per lane (a tile has
-    // more than 32 only in escape-dense blocks; those lanes take the rest after the first 32), so
-    // that only their stores follow the decode.
-    const int e0 = esc_ms(bd, T, g16), e1 = esc_ms(bd, T, g16 + 1);
+    // The tiles' escapes [e0, e1) are fetched before the decode, one entry per lane (more than 32
+    // occur only in escape-dense blocks; those lanes take the rest after the first 32), so that only
+    // their stores follow the decode.  Entries from em on are the second tile's.
+    constexpr int NT = C::NT;
+    const int e0 = esc_ms(bd, T, g16), e1 = esc_ms(bd, T, g16 + NT);
+    const int em = NT > 1 ? esc_ms(bd, T, g16 + 1) : e1;
     uint32_t ents = 0u, ent = 0u;
     if (e1 > e0) {
         ents = lds_u32(info);  // the producer's word for this stage and tensor
@@ -676,18 +693,18 @@ __device__ __forceinline__ void tile_tensor(const AttnArgs &a, const BlockDesc &
         const uint32_t b7[4] = {0u, 0u, 0u, 0u};
         decode_tile<D, 0, 0>(rb, cb, ly, b7, sm, lane);
     }
-    if (zero_from < TT) zero_rows<D, 0>(sm, zero_from, lane);
+    if (zero_from < NT * TT) zero_rows<D, 0>(sm, zero_from, lane);
     if (e1 > e0) {
-        // entry: the element's byte in the tile (bits 0-15, even) | its BF16 word << 16; slots at or
-        // past the tile's valid rows are skipped
-        const uint32_t lim = uint32_t(rows) * (2 * D);
+        // entry: the element's byte in its tile (bits 0-15, even) | its BF16 word << 16; elements
+        // in rows at or past `rows` are skipped
         __syncwarp();  // the decoded words are in place before escapes overwrite some
-        if (e0 + lane < e1 && (ent & 0xFFFFu) < lim) sts_u16(xb + (ent & 0xFFFEu), ent >> 16);
+        if (e0 + lane < e1) esc_store(xb, ent, e0 + lane >= em, rows, C::TILE1, 2 * D);
         if (e1 - e0 > 32) {
             if (ents & 1u)
-                esc_patch<D>(xb, ents & ~1u, e0 + 32, e1, lim, lane);
+                esc_patch<D>(xb, ents & ~1u, e0 + 32, e1, em, rows, lane);
             else
-                esc_patch_hbm<D>(xb, a.esc + (T ? bd.v_rec : bd.k_rec) + kEscRecHead, e0 + 32, e1, lim, lane);
+                esc_patch_hbm<D>(xb, a.esc + (T ? bd.v_rec : bd.k_rec) + kEscRecHead, e0 + 32, e1, em,
+                                 rows, lane);
         }
     }
     __syncwarp();
@@ -706,14 +723,17 @@ template <int D> struct SoftState {
     }
 };
 
-// One 16-token tile of K and V: decode K into the warp's tile, S = K Q^T on the tensor cores, online
-// softmax, decode V into the tile, free the slot, O += P V.
+// The warp's NT 16-token tiles of K and V (tiles tw .. tw + NT - 1 of the stage): decode K into
+// the warp's tiles, S = K Q^T on the tensor cores, decode V into the same tiles (the MMAs have their
+// K fragments and run meanwhile), free the slot, online softmax, O += P V.  rows: valid rows from
+// the first tile's first row (1 .. NT 16).
 template <int D, bool BF16IN>
 __device__ __forceinline__ void tile_step(const AttnArgs &a, const BlockDesc &bd, uint32_t slot_addr,
                                           uint32_t empty, uint32_t xb, const StoreMap<D> &sm, int tw,
                                           int t0, int rows, const uint32_t (&qb)[Cfg<D>::KS][2],
                                           SoftState<D> &st, int lane) {
     using C = Cfg<D>;
+    constexpr int NT = C::NT;
     const int gi = lane >> 2;
     const uint32_t al = *reinterpret_cast<const uint32_t *>(bd.align);
     const int km = BF16IN ? 0 : bd.k_mode, vm = BF16IN ? 0 : bd.v_mode;
@@ -722,12 +742,21 @@ __device__ __forceinline__ void tile_step(const AttnArgs &a, const BlockDesc &bd
 
     // S^T = K Q^T (rows past `rows` hold stale words: their scores are dropped)
     tile_tensor<D, 0>(a, bd, km, al & 0xFFFFu, kreg, slot_addr + uint32_t(C::S_B7),
-                      slot_addr + uint32_t(C::S_INFO), tw, xb, sm, g16, t0, rows, TT, BF16IN, lane);
-    float s[1][4];
-    qk_tiles<D, 1>(xb, qb, lane, s);
-    if (rows < TT) {
-        if (gi >= rows) s[0][0] = s[0][1] = -INFINITY;
-        if (gi + 8 >= rows) s[0][2] = s[0][3] = -INFINITY;
+                      slot_addr + uint32_t(C::S_INFO), tw, xb, sm, g16, t0, rows, NT * TT, BF16IN, lane);
+    float s[NT][4];
+    qk_tiles<D, NT>(xb, qb, lane, s);
+    // V replaces K in the tiles once every lane's K fragments are loaded (the MMAs above need only
+    // those registers); rows past `rows` are zeroed (P is 0 there and V must be finite)
+    __syncwarp();
+    tile_tensor<D, 1>(a, bd, vm, al >> 16, vreg, slot_addr + uint32_t(C::S_B7 + 2 * D),
+                      slot_addr + uint32_t(C::S_INFO + 4), tw, xb, sm, g16, t0, rows, rows, BF16IN, lane);
+    if (lane == 0) mbar_arrive(empty);  // this warp has read everything it needs from the slot
+#pragma unroll
+    for (int t = 0; t < NT; ++t) {
+        if (rows < TT * (t + 1)) {
+            if (gi >= rows - TT * t) s[t][0] = s[t][1] = -INFINITY;
+            if (gi + 8 >= rows - TT * t) s[t][2] = s[t][3] = -INFINITY;
+        }
     }
 
     // online softmax (src/softmax.hpp:8-14): p = 2^((s - m) log2e); the warp-wide maximum and the
@@ -735,6 +764,11 @@ __device__ __forceinline__ void tile_step(const AttnArgs &a, const BlockDesc &bd
     // formed first, like the reference's expf(s - m), so that huge scores keep the largest weight
     // at exactly 1.
     float t0m = fmaxf(s[0][0], s[0][2]), t1m = fmaxf(s[0][1], s[0][3]);
+#pragma unroll
+    for (int t = 1; t < NT; ++t) {
+        t0m = fmaxf(t0m, fmaxf(s[t][0], s[t][2]));
+        t1m = fmaxf(t1m, fmaxf(s[t][1], s[t][3]));
+    }
     const bool grow = __any_sync(FULL, t0m > st.m0 || t1m > st.m1);
     float mn0 = st.m0, mn1 = st.m1, al0 = 1.0f, al1 = 1.0f;
     if (grow) {
@@ -748,17 +782,19 @@ __device__ __forceinline__ void tile_step(const AttnArgs &a, const BlockDesc &bd
         al0 = ex2(__fmul_rn(__fsub_rn(st.m0, mn0), kLog2e));
         al1 = ex2(__fmul_rn(__fsub_rn(st.m1, mn1), kLog2e));
     }
-    const float p0 = ex2(__fmul_rn(__fsub_rn(s[0][0], mn0), kLog2e));
-    const float p1 = ex2(__fmul_rn(__fsub_rn(s[0][1], mn1), kLog2e));
-    const float p2 = ex2(__fmul_rn(__fsub_rn(s[0][2], mn0), kLog2e));
-    const float p3 = ex2(__fmul_rn(__fsub_rn(s[0][3], mn1), kLog2e));
-    // P^T B fragments: p = h + m + l exactly, each term the upper 16 bits of what remains (h = p
-    // truncated to bf16, m = (p - h) truncated, l = p - h - m); the differences are exact in fp32
-    // and l has at most 8 significant bits, so the three bf16 terms carry all 24 bits of p.  Two
-    // weights pack into one B register with one byte permute.
-    uint32_t bh[2], bm[2], bl[2];
-    {
+    // P^T B fragments per tile: p = h + m + l exactly, each term the upper 16 bits of what remains
+    // (h = p truncated to bf16, m = (p - h) truncated, l = p - h - m); the differences are exact in
+    // fp32 and l has at most 8 significant bits, so the three bf16 terms carry all 24 bits of p.
+    // Two weights pack into one B register with one byte permute.
+    uint32_t bh[NT][2], bm[NT][2], bl[NT][2];
+    float ps0 = 0.f, ps1 = 0.f;
+#pragma unroll
+    for (int t = 0; t < NT; ++t) {
         constexpr uint32_t HI = 0xFFFF0000u, PK = 0x7632u;  // PK: the upper halves of a and b
+        const float p0 = ex2(__fmul_rn(__fsub_rn(s[t][0], mn0), kLog2e));
+        const float p1 = ex2(__fmul_rn(__fsub_rn(s[t][1], mn1), kLog2e));
+        const float p2 = ex2(__fmul_rn(__fsub_rn(s[t][2], mn0), kLog2e));
+        const float p3 = ex2(__fmul_rn(__fsub_rn(s[t][3], mn1), kLog2e));
         const uint32_t P0 = __float_as_uint(p0), P1 = __float_as_uint(p1);
         const uint32_t P2 = __float_as_uint(p2), P3 = __float_as_uint(p3);
         const float r0 = __fsub_rn(p0, __uint_as_float(P0 & HI)), r1 = __fsub_rn(p1, __uint_as_float(P1 & HI));
@@ -767,15 +803,17 @@ __device__ __forceinline__ void tile_step(const AttnArgs &a, const BlockDesc &bd
         const uint32_t R2 = __float_as_uint(r2), R3 = __float_as_uint(r3);
         const float u0 = __fsub_rn(r0, __uint_as_float(R0 & HI)), u1 = __fsub_rn(r1, __uint_as_float(R1 & HI));
         const float u2 = __fsub_rn(r2, __uint_as_float(R2 & HI)), u3 = __fsub_rn(r3, __uint_as_float(R3 & HI));
-        bh[0] = movm_t(prmt(P0, P1, PK));
-        bh[1] = movm_t(prmt(P2, P3, PK));
-        bm[0] = movm_t(prmt(R0, R1, PK));
-        bm[1] = movm_t(prmt(R2, R3, PK));
-        bl[0] = movm_t(prmt(__float_as_uint(u0), __float_as_uint(u1), PK));
-        bl[1] = movm_t(prmt(__float_as_uint(u2), __float_as_uint(u3), PK));
+        bh[t][0] = movm_t(prmt(P0, P1, PK));
+        bh[t][1] = movm_t(prmt(P2, P3, PK));
+        bm[t][0] = movm_t(prmt(R0, R1, PK));
+        bm[t][1] = movm_t(prmt(R2, R3, PK));
+        bl[t][0] = movm_t(prmt(__float_as_uint(u0), __float_as_uint(u1), PK));
+        bl[t][1] = movm_t(prmt(__float_as_uint(u2), __float_as_uint(u3), PK));
+        ps0 = __fadd_rn(ps0, __fadd_rn(p0, p2));
+        ps1 = __fadd_rn(ps1, __fadd_rn(p1, p3));
     }
-    st.l0 = __fmaf_rn(st.l0, al0, __fadd_rn(p0, p2));
-    st.l1 = __fmaf_rn(st.l1, al1, __fadd_rn(p1, p3));
+    st.l0 = __fmaf_rn(st.l0, al0, ps0);
+    st.l1 = __fmaf_rn(st.l1, al1, ps1);
     st.m0 = mn0;
     st.m1 = mn1;
     if (grow) {
@@ -787,14 +825,9 @@ __device__ __forceinline__ void tile_step(const AttnArgs &a, const BlockDesc &bd
             st.acc[m][3] = __fmul_rn(st.acc[m][3], al1);
         }
     }
-
-    // V replaces K in the tile (the QK MMAs' ldmatrix reads are done: their results were used
-    // above); rows past `rows` are zeroed (P is 0 there and V must be finite)
-    tile_tensor<D, 1>(a, bd, vm, al >> 16, vreg, slot_addr + uint32_t(C::S_B7 + 2 * D),
-                      slot_addr + uint32_t(C::S_INFO + 4), tw, xb, sm, g16, t0, rows, rows, BF16IN, lane);
-    if (lane == 0) mbar_arrive(empty);  // this warp has read everything it needs from the slot
-    pv_tile<D>(xb, 0, bh, bm, bl, lane, st.acc);
-    __syncwarp();  // every lane is done with the tile before the next decode writes it
+#pragma unroll
+    for (int t = 0; t < NT; ++t) pv_tile<D>(xb, TT * t, bh[t], bm[t], bl[t], lane, st.acc);
+    __syncwarp();  // every lane is done with the tiles before the next decode writes them
 }
 
 // The warp's state for one unit segment goes to partial state `idx` (m, l summed over the lanes
@@ -827,7 +860,7 @@ __device__ __forceinline__ void flush_state(const AttnArgs &a, size_t idx, const
     }
 }
 
-// A consumer warp: visits every stage of the CTA's range in order, takes the tiles dealt to it,
+// A consumer warp: visits every stage of the CTA's range in order, takes the tile groups dealt to it,
 // arrives once per stage on the slot's empty barrier, and writes its state at every segment end
 // (the unit's last block, or the end of the range).  It has seen stage gs - 1 (and so gs - NSLOT)
 // land before it waits on stage gs, so the parity of the slot's full barrier identifies the stage.
@@ -843,7 +876,7 @@ __device__ void consumer(const AttnArgs &a, uint8_t *smem, int w, int lane, int 
     st.reset();
     int row = row0;
     int gs = 0;   // stages consumed
-    int tw = w;   // this warp's tile in stage gs: (w - gs TPS) mod NW (none when >= TPS)
+    int tp = w;   // this warp's tile group in stage gs: (w - gs TPP) mod NW (none when >= TPP)
     for (int b = fb0; b < fb1; ++b) {
         for (int t0 = 0;; t0 += C::TSB) {
             const int slot = gs % C::NSLOT;
@@ -863,9 +896,10 @@ __device__ void consumer(const AttnArgs &a, uint8_t *smem, int w, int lane, int 
             }
             const bool last = t0 + C::TSB >= valid;
             const bool seg_end = last && ((flags & kDescLast) != 0u || b + 1 == fb1);
-            const int rows = valid - t0 - TT * tw;
-            if (tw < C::TPS && rows > 0) {
-                tile_step<D, BF16IN>(a, bd, smem_u32(sp), empty, xb, sm, tw, t0, min(rows, TT), qb, st, lane);
+            const int rows = valid - t0 - TT * C::NT * tp;
+            if (tp < C::TPP && rows > 0) {
+                tile_step<D, BF16IN>(a, bd, smem_u32(sp), empty, xb, sm, C::NT * tp, t0,
+                                     min(rows, C::NT * TT), qb, st, lane);
             } else {
                 __syncwarp();  // every lane has read the descriptor
                 if (lane == 0) mbar_arrive(empty);
@@ -875,8 +909,8 @@ __device__ void consumer(const AttnArgs &a, uint8_t *smem, int w, int lane, int 
                 ++row;
             }
             ++gs;
-            tw -= C::TPS;
-            if (tw < 0) tw += C::NW;
+            tp -= C::TPP;
+            if (tp < 0) tp += C::NW;
             if (last) break;
         }
     }
@@ -910,9 +944,9 @@ __device__ __forceinline__ bool wait_stage(uint32_t sb, int gs) {
 }
 
 // A consumer warp when every block takes the same number of stages (spb): stage s of the range is
-// stage s mod spb of block fb0 + s / spb, so the warp goes straight to the stages of its tiles
-// (tile j = w, w + NW, ... of the range; stage j / TPS, tile j mod TPS), waits only on those, and
-// arrives once per tile (the slot's empty barrier counts TPS arrivals).  Its state is written
+// stage s mod spb of block fb0 + s / spb, so the warp goes straight to the stages of its tile
+// groups (group j = w, w + NW, ... of the range; stage j / TPP, tiles NT (j mod TPP) ..), waits
+// only on those, and arrives once per group (the slot's empty barrier counts TPP arrivals).  Its state is written
 // when the unit of its next tile differs, and at the end of the range, to row
 // row0 + (unit - the range's first unit); rows a warp never reaches keep m = -inf, l = 0.
 template <int D, bool BF16IN>
@@ -929,9 +963,9 @@ __device__ void consumer_by_tile(const AttnArgs &a, uint8_t *smem, int w, int la
     const int spb = a.stages_per_block;
     const int unit0 = __ldg(&a.desc[fb0].unit);
     int cur = -1;  // unit of the warp's state (-1: none yet)
-    const int tiles = (fb1 - fb0) * spb * C::TPS;
-    for (int j = w; j < tiles; j += C::NW) {
-        const int gs = j / C::TPS, tw = j % C::TPS;
+    const int groups = (fb1 - fb0) * spb * C::TPP;
+    for (int j = w; j < groups; j += C::NW) {
+        const int gs = j / C::TPP, tw = (j % C::TPP) * C::NT;
         const int t0 = (gs % spb) * C::TSB;
         const int slot = gs % C::NSLOT;
         const uint32_t empty = ring_bar<D>(sb, C::NSLOT + slot);
@@ -951,7 +985,8 @@ __device__ void consumer_by_tile(const AttnArgs &a, uint8_t *smem, int w, int la
         }
         const int rows = valid - t0 - TT * tw;
         if (rows > 0) {
-            tile_step<D, BF16IN>(a, bd, smem_u32(sp), empty, xb, sm, tw, t0, min(rows, TT), qb, st, lane);
+            tile_step<D, BF16IN>(a, bd, smem_u32(sp), empty, xb, sm, tw, t0, min(rows, C::NT * TT), qb, st,
+                                 lane);
         } else {
             __syncwarp();  // every lane has read the descriptor
             if (lane == 0) mbar_arrive(empty);
@@ -982,8 +1017,8 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1) attn_kernel(const AttnArgs
         const uint32_t sb = smem_u32(smem);
         for (int j = 0; j < C::NSLOT; ++j) {
             mbar_init(ring_bar<D>(sb, j), 1);               // full: the producer's arrive + bytes
-            // empty: one arrive per consumer warp, or per tile when the warps go by tile
-            mbar_init(ring_bar<D>(sb, C::NSLOT + j), by_tile ? C::TPS : C::NW);
+            // empty: one arrive per consumer warp, or per tile group when the warps go by tile
+            mbar_init(ring_bar<D>(sb, C::NSLOT + j), by_tile ? C::TPP : C::NW);
             // no stage yet (shared memory keeps whatever an earlier CTA left there)
             sts_u32(sb + uint32_t(j * C::SLOT + C::S_TAG), 0xFFFFFFFFu);
         }
