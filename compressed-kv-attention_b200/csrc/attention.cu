@@ -1086,29 +1086,32 @@ __global__ void __launch_bounds__(kCombineThreads) combine_kernel(const CombineA
         lw[i] = __ldg(pi + 8 + g);
         mx = fmaxf(mx, m);
     }
-    red[tid] = mx;
+    // maxima: within each warp by shuffles, then over the warps' results
+    constexpr int NWC = kCombineThreads / 32;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(FULL, mx, o));
+    if ((tid & 31) == 0) red[tid >> 5] = mx;
     __syncthreads();
-    for (int o = kCombineThreads / 2; o > 0; o >>= 1) {
-        if (tid < o) red[tid] = fmaxf(red[tid], red[tid + o]);
-        __syncthreads();
-    }
-    const float M = red[0];
-    __syncthreads();
+    float M = red[0];
+#pragma unroll
+    for (int w = 1; w < NWC; ++w) M = fmaxf(M, red[w]);
     float ls = 0.f;
     for (int i = tid; i < nt; i += kCombineThreads) {
         const float w = expf(e[i] - M);
         e[i] = w;
         ls = __fmaf_rn(lw[i], w, ls);
     }
-    red[tid] = ls;
+    // sum of the weighted l: within each warp by shuffles, then over the warps in warp order
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ls = __fadd_rn(ls, __shfl_xor_sync(FULL, ls, o));
+    __syncthreads();  // every thread has read the maxima from red
+    if ((tid & 31) == 0) red[tid >> 5] = ls;
     __syncthreads();
-    for (int o = kCombineThreads / 2; o > 0; o >>= 1) {
-        if (tid < o) red[tid] = __fadd_rn(red[tid], red[tid + o]);
-        __syncthreads();
-    }
-    const float lsum = red[0];
+    float lsum = red[0];
+#pragma unroll
+    for (int w = 1; w < NWC; ++w) lsum = __fadd_rn(lsum, red[w]);
     const float inv = __frcp_rn(lsum);
-    __syncthreads();
+    __syncthreads();  // every thread has read the sums from red
     float acc = 0.f;
     if (sl < S) {
 #pragma unroll
