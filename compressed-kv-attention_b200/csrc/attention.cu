@@ -104,6 +104,11 @@ template <int D> struct Cfg {
     static_assert(SMEM + 16 <= 232448, "stage ring and tiles exceed shared memory");
     static_assert(NW >= TPP, "a consumer warp takes at most one tile group of a stage");
     static_assert(TPS % NT == 0, "a stage holds whole tile groups");
+    // Every use of a slot comes from the same producer warp (stage gs goes to warp gs mod NP), so
+    // that warp has waited for the slot's previous use to be released before it waits for the
+    // current one: with slots shared between the producers, a producer could test the slot's empty
+    // barrier for a phase two uses back and pass one phase early.
+    static_assert(NSLOT % NP == 0, "each ring slot is served by one producer warp");
     static_assert(32 % C8 == 0 && NIT >= 1, "a warp step covers whole rows");
     static_assert((TSB * D) % 4096 == 0, "stage offsets keep every section's 16-byte alignment");
 };
