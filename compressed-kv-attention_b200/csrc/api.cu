@@ -281,10 +281,12 @@ struct kvx_plan_s {
     int n_ranges = 0;     // CTA ranges of the attention grid (one CTA each)
     int64_t n_rows = 0;   // partial-state rows (one per unit segment of a CTA range)
     int stages_per_block = 0;  // ring stages of every block in the attention kernel (0: by block)
+    bool compact = false;      // every block is coded: the attention kernel's compact ring
     cudaStream_t s = nullptr;
     UnitDev *units = nullptr;
     FlatBlock *flat = nullptr;
     BlockDesc *desc = nullptr;  // per flat block, for the attention kernel
+    uint4 *stages = nullptr;    // stage copy lists ([n_blocks][stages_per_block][kStageRecWords])
     uint32_t *esc = nullptr;  // escape records of the step's coded blocks
     uint32_t *b7 = nullptr;   // merge words of the step's coded blocks ([n_blocks][dim])
     int64_t *range_begin = nullptr;
@@ -403,6 +405,9 @@ static cudaError_t plan_blob_work(kvx_plan_s *p, cudaEvent_t blobs_ready) {
     if (e == cudaSuccess && !p->bf16) e = launch_b7(p->units, p->flat, p->n_blocks, p->dim, p->b7, nullptr);
     if (e == cudaSuccess)
         e = launch_block_desc(p->units, p->flat, p->esc, p->n_blocks, p->dim, p->bf16, p->desc, nullptr);
+    if (e == cudaSuccess && p->stages != nullptr)
+        e = launch_stage_table(p->dim, p->bf16, p->compact, p->desc, p->b7, p->esc, p->n_blocks,
+                               p->stages_per_block, p->stages, nullptr);
     return e;
 }
 
@@ -502,14 +507,15 @@ static int plan_create_impl(const kvx_unit *units, int n_units, int n_q, int dim
     // every block takes the same number of ring stages in the attention kernel (enough for the
     // longest block; shorter ones get empty stages), so a consumer warp goes straight to the stage
     // of each of its tiles
-    int max_valid = 0;
+    int max_valid[2] = {0, 0};  // longest block, any raw block
     if (e == cudaSuccess)
         e = launch_max_valid(p->flat, total, reinterpret_cast<int *>(desc_total + 1), nullptr);
     if (e == cudaSuccess)
-        e = cudaMemcpy(&max_valid, desc_total + 1, sizeof max_valid, cudaMemcpyDeviceToHost);
+        e = cudaMemcpy(max_valid, desc_total + 1, sizeof max_valid, cudaMemcpyDeviceToHost);
     {
         const int tsb = attention_stage_tokens(dim);
-        p->stages_per_block = max_valid > 0 ? (max_valid + tsb - 1) / tsb : 0;
+        p->stages_per_block = max_valid[0] > 0 ? (max_valid[0] + tsb - 1) / tsb : 0;
+        p->compact = !bf16 && max_valid[1] == 0;
     }
     // escape records: offsets, then (with the array sized) the records
     unsigned long long esc_total = 0;
@@ -523,6 +529,8 @@ static int plan_create_impl(const kvx_unit *units, int n_units, int n_q, int dim
     }
     // (+4 entries: the kernel's 16-byte aligned bulk copies may read up to 12 bytes past the end)
     if (e == cudaSuccess) e = plan_alloc(p, &p->esc, size_t(esc_total) + 4);
+    if (e == cudaSuccess && p->stages_per_block > 0)
+        e = plan_alloc(p, &p->stages, size_t(total) * size_t(p->stages_per_block) * kStageRecWords);
     if (e != cudaSuccess) {
         delete p;
         return fail(KVX_ERR_CUDA, std::string("kvx_plan_create: ") + cudaGetErrorString(e));
@@ -611,6 +619,7 @@ int kvx_plan_run_part(kvx_plan p, int part, void *stream) {
     a.units = p->units;
     a.flat = p->flat;
     a.desc = p->desc;
+    a.stages = p->stages;
     a.esc = p->esc;
     a.b7 = p->b7;
     a.range_begin = p->range_begin;
@@ -619,7 +628,7 @@ int kvx_plan_run_part(kvx_plan p, int part, void *stream) {
     a.status = p->status;
     a.n_ranges = p->n_ranges;
     a.stages_per_block = p->stages_per_block;
-    KVX_CUDA(launch_attention(p->dim, p->bf16, a, p->n_ranges, s));
+    KVX_CUDA(launch_attention(p->dim, p->bf16, p->compact, a, p->n_ranges, s));
     return KVX_OK;
 }
 
@@ -1587,7 +1596,7 @@ extern "C" int kvx_attention_decode_noalloc(const uint16_t *q, const uint8_t *k_
     a.partials = d_partials;
     a.status = status;
     a.n_ranges = n_ranges;
-    KVX_CUDA(launch_attention(dim, false, a, n_ranges, s));
+    KVX_CUDA(launch_attention(dim, false, false, a, n_ranges, s));
     CombineArgs c{};
     c.split = d_split;
     c.partials = d_partials;

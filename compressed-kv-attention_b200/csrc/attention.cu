@@ -60,7 +60,11 @@ __host__ __device__ constexpr int round16(int x) { return (x + 15) & ~15; }
 __device__ __forceinline__ bool uni(bool c) { return __all_sync(0xFFFFFFFFu, c); }
 
 
-template <int D> struct Cfg {
+// Kernel geometry of head dim D.  CP: the compact ring, for steps whose blocks are all coded (6 slots
+// sized for a coded stage: D bytes of sign/mantissa and at most D / 2 bytes of residual codes per
+// token); otherwise 4 slots that also take raw BF16 rows (2 D bytes per token).  Only the ring's
+// layout differs: the tiles, their order and the arithmetic are the same in both.
+template <int D, bool CP = false> struct Cfg {
     static constexpr int KS = D / 16;             // k-steps of QK = M-tiles of PV
     static constexpr int C8 = D / 8;              // 8-element chunks per row
     static constexpr int NIT = TT * C8 / 32;      // chunk steps of a lane per tile and tensor
@@ -73,14 +77,14 @@ template <int D> struct Cfg {
     static constexpr int NT = D <= 64 ? 2 : 1;
     static constexpr int TPP = TPS / NT;          // tile groups (visits) per stage
     static constexpr int NW = attention_consumer_warps(D);  // consumer warps
-    static constexpr int NSLOT = 4;               // ring slots
-    // Escape-record entries of one tensor that a stage stages (12.5 % of its elements); a stage
-    // with more leaves them in HBM, where the consumers read them.
-    static constexpr int ESC_CAP = TSB * D / 8;
+    static constexpr int NSLOT = CP ? 6 : 4;      // ring slots
+    // Escape-record entries of one tensor that a stage stages (12.5 % of its elements, or 256 in
+    // the compact ring); a stage with more leaves them in HBM, where the consumers read them.
+    static constexpr int ESC_CAP = CP ? 256 : TSB * D / 8;
     // One tensor's region of a slot: rows at 0 (raw: 2 D bytes per token; coded: D bytes, then the
     // residual codes at CODE_OFF), escape entries at E_OFF.  Every piece lands 0-15 bytes past its
     // 16-byte aligned start.
-    static constexpr int R_BYTES = 2 * TSB * D + 32;
+    static constexpr int R_BYTES = (CP ? TSB * D + TSB * D / 2 : 2 * TSB * D) + 32;
     static constexpr int CODE_OFF = TSB * D + 16;
     static constexpr int E_OFF = R_BYTES;
     static constexpr int T_BYTES = round16(E_OFF + 4 * ESC_CAP + 32);
@@ -99,7 +103,7 @@ template <int D> struct Cfg {
     static constexpr int O_TILE = NSLOT * SLOT;
     static constexpr int O_BAR = O_TILE + NW * TILE;  // full[NSLOT], then empty[NSLOT]
     static constexpr int SMEM = O_BAR + 16 * NSLOT;
-    static constexpr int NP = 2;                  // producer warps (stages alternate between them)
+    static constexpr int NP = 1;                  // producer warps (stages go round-robin over them)
     static constexpr int THREADS = 32 * (NW + NP);
     static_assert(SMEM + 16 <= 232448, "stage ring and tiles exceed shared memory");
     static_assert(NW >= TPP, "a consumer warp takes at most one tile group of a stage");
@@ -465,8 +469,8 @@ __device__ __forceinline__ void load_q(const uint16_t *q, int n_q, int stride,
 __device__ __forceinline__ const uint8_t *gptr(uint64_t a) { return reinterpret_cast<const uint8_t *>(a); }
 
 // Shared-memory address of ring barrier `i` (full: i < NSLOT; empty: NSLOT + i).
-template <int D> __device__ __forceinline__ uint32_t ring_bar(uint32_t sb, int i) {
-    return sb + uint32_t(Cfg<D>::O_BAR + 8 * i);
+template <int D, bool CP> __device__ __forceinline__ uint32_t ring_bar(uint32_t sb, int i) {
+    return sb + uint32_t(Cfg<D, CP>::O_BAR + 8 * i);
 }
 
 // One bulk copy of [src, src + len) into the shared region at `dst`: the 16-byte aligned superset
@@ -520,9 +524,9 @@ __device__ __forceinline__ int pdesc_esc(const uint4 (&e)[4], int T, int i) {
 // the descriptor of block base + l; the next 32 are loaded while the current 32 are issued, so
 // the issuing lane never waits on a global load.  On a timeout it reports DERR_TIMEOUT and waits
 // (bounded) for the copies it issued before it returns.
-template <int D, bool BF16IN>
+template <int D, bool CP, bool BF16IN>
 __device__ void producer(const AttnArgs &a, uint8_t *smem, int fb0, int fb1, int pw, int lane) {
-    using C = Cfg<D>;
+    using C = Cfg<D, CP>;
     constexpr bool MULTI = C::TSB < 128;  // a 128-token block takes several stages
     const uint32_t sb = smem_u32(smem);
     int gs = 0;  // stages issued
@@ -560,7 +564,7 @@ __device__ void producer(const AttnArgs &a, uint8_t *smem, int fb0, int fb1, int
                     continue;
                 }
                 const int slot = gs % C::NSLOT;
-                const uint32_t full = ring_bar<D>(sb, slot), empty = ring_bar<D>(sb, C::NSLOT + slot);
+                const uint32_t full = ring_bar<D, CP>(sb, slot), empty = ring_bar<D, CP>(sb, C::NSLOT + slot);
                 if (gs >= C::NSLOT &&
                     !uni(mbar_wait_bounded(empty, uint32_t((gs / C::NSLOT - 1) & 1), kStageWaitUs))) {
                     if (lane == 0) report(a.status, KVX_ERR_TIMEOUT, DERR_TIMEOUT);
@@ -650,7 +654,64 @@ __device__ void producer(const AttnArgs &a, uint8_t *smem, int fb0, int fb1, int
         // let the copies already issued land before this CTA's shared memory goes away
         for (int s = max(0, gs - C::NSLOT); s < gs; ++s)
             if (s % C::NP == pw)
-                mbar_wait_bounded(ring_bar<D>(sb, s % C::NSLOT), uint32_t((s / C::NSLOT) & 1), kStageWaitUs);
+                mbar_wait_bounded(ring_bar<D, CP>(sb, s % C::NSLOT), uint32_t((s / C::NSLOT) & 1), kStageWaitUs);
+    }
+}
+
+// A producer warp with the plan's stage copy lists (AttnArgs::stages): for each of its stages
+// (gs mod NP == pw), wait until the slot is free, then lanes 0-7 issue the stage's pieces as the
+// list gives them and lane 8 writes the stage's tag and escape-entry words and announces the
+// stage's bytes on the slot's full barrier.  Each lane keeps its word of the lists of its next PF
+// stages in registers, loaded PF stages ahead.  On a timeout it reports DERR_TIMEOUT and waits
+// (bounded) for the copies it issued before it returns.
+template <int D, bool CP, bool BF16IN>
+__device__ void producer_listed(const AttnArgs &a, uint8_t *smem, int fb0, int fb1, int pw, int lane) {
+    using C = Cfg<D, CP>;
+    constexpr int PF = 3;
+    const uint32_t sb = smem_u32(smem);
+    const int n_st = (fb1 - fb0) * a.stages_per_block;
+    const uint4 *rec = a.stages + size_t(fb0) * size_t(a.stages_per_block) * kStageRecWords + lane;
+    auto fetch = [&](int g) -> uint4 {
+        return lane < kStageRecWords && g < n_st ? __ldg(rec + size_t(g) * kStageRecWords) : make_uint4(0u, 0u, 0u, 0u);
+    };
+    uint4 r[PF];
+#pragma unroll
+    for (int k = 0; k < PF; ++k) r[k] = fetch(pw + k * C::NP);
+    int gs = pw;
+    bool ok = true;
+    for (; gs < n_st; gs += C::NP) {
+        const uint4 w = r[0];
+#pragma unroll
+        for (int k = 0; k + 1 < PF; ++k) r[k] = r[k + 1];
+        r[PF - 1] = fetch(gs + PF * C::NP);
+        const int slot = gs % C::NSLOT;
+        const uint32_t full = ring_bar<D, CP>(sb, slot), empty = ring_bar<D, CP>(sb, C::NSLOT + slot);
+        if (gs >= C::NSLOT &&
+            !uni(mbar_wait_bounded(empty, uint32_t((gs / C::NSLOT - 1) & 1), kStageWaitUs))) {
+            if (lane == 0) report(a.status, KVX_ERR_TIMEOUT, DERR_TIMEOUT);
+            ok = false;
+            break;
+        }
+        const uint32_t dslot = sb + uint32_t(slot * C::SLOT);
+        if (lane < 8 && w.z != 0u)
+            bulk_g2s(dslot + w.w, reinterpret_cast<const void *>((uint64_t(w.y) << 32) | w.x), w.z, full);
+        if (lane == 8) {
+            sts_u32(dslot + uint32_t(C::S_TAG), uint32_t(gs));
+            if (!BF16IN) {
+                sts_u32(dslot + uint32_t(C::S_INFO), (w.w & 1u) ? ((dslot + w.x) | 1u) : 0u);
+                sts_u32(dslot + uint32_t(C::S_INFO + 4), (w.w & 2u) ? ((dslot + w.y) | 1u) : 0u);
+            }
+            // (the stores above are ordered before the arrive, which releases them; copies that
+            // complete before it only run the barrier's tx-count below zero meanwhile)
+            mbar_arrive_expect_tx(full, w.z);
+        }
+        __syncwarp();
+    }
+    if (!ok && lane < 8) {
+        // let the copies already issued land before this CTA's shared memory goes away
+        for (int s = max(0, gs - C::NSLOT); s < gs; ++s)
+            if (s % C::NP == pw)
+                mbar_wait_bounded(ring_bar<D, CP>(sb, s % C::NSLOT), uint32_t((s / C::NSLOT) & 1), kStageWaitUs);
     }
 }
 
@@ -659,13 +720,13 @@ __device__ void producer(const AttnArgs &a, uint8_t *smem, int fb0, int fb1, int
 // slot; info: the producer's escape word of the tensor for this stage; g16: the first tile's
 // 16-token group in the block; t0: the stage's first token in the block; rows: valid rows from the
 // first tile's first row on; zero_from: rows at or past it are zeroed.
-template <int D, int T>
+template <int D, bool CP, int T>
 __device__ __forceinline__ void tile_tensor(const AttnArgs &a, const BlockDesc &bd, int mode,
                                             uint32_t al, uint32_t reg, uint32_t b7s, uint32_t info, int tw,
                                             uint32_t xb,
                                             const StoreMap<D> &sm, int g16, int t0, int rows,
                                             int zero_from, bool bf16, int lane) {
-    using C = Cfg<D>;
+    using C = Cfg<D, CP>;
     const int c8 = lane % C::C8;
     const uint32_t rd = al & 15u, cd = (al >> 8) & 15u;
     // a whole block in one stage came as one copy: the codes follow its n rows
@@ -732,12 +793,12 @@ template <int D> struct SoftState {
 // the warp's tiles, S = K Q^T on the tensor cores, decode V into the same tiles (the MMAs have their
 // K fragments and run meanwhile), free the slot, online softmax, O += P V.  rows: valid rows from
 // the first tile's first row (1 .. NT 16).
-template <int D, bool BF16IN>
+template <int D, bool CP, bool BF16IN>
 __device__ __forceinline__ void tile_step(const AttnArgs &a, const BlockDesc &bd, uint32_t slot_addr,
                                           uint32_t empty, uint32_t xb, const StoreMap<D> &sm, int tw,
                                           int t0, int rows, const uint32_t (&qb)[Cfg<D>::KS][2],
                                           SoftState<D> &st, int lane) {
-    using C = Cfg<D>;
+    using C = Cfg<D, CP>;
     constexpr int NT = C::NT;
     const int gi = lane >> 2;
     const uint32_t al = *reinterpret_cast<const uint32_t *>(bd.align);
@@ -746,14 +807,14 @@ __device__ __forceinline__ void tile_step(const AttnArgs &a, const BlockDesc &bd
     const uint32_t kreg = slot_addr + uint32_t(C::S_T), vreg = kreg + uint32_t(C::T_BYTES);
 
     // S^T = K Q^T (rows past `rows` hold stale words: their scores are dropped)
-    tile_tensor<D, 0>(a, bd, km, al & 0xFFFFu, kreg, slot_addr + uint32_t(C::S_B7),
+    tile_tensor<D, CP, 0>(a, bd, km, al & 0xFFFFu, kreg, slot_addr + uint32_t(C::S_B7),
                       slot_addr + uint32_t(C::S_INFO), tw, xb, sm, g16, t0, rows, NT * TT, BF16IN, lane);
     float s[NT][4];
     qk_tiles<D, NT>(xb, qb, lane, s);
     // V replaces K in the tiles once every lane's K fragments are loaded (the MMAs above need only
     // those registers); rows past `rows` are zeroed (P is 0 there and V must be finite)
     __syncwarp();
-    tile_tensor<D, 1>(a, bd, vm, al >> 16, vreg, slot_addr + uint32_t(C::S_B7 + 2 * D),
+    tile_tensor<D, CP, 1>(a, bd, vm, al >> 16, vreg, slot_addr + uint32_t(C::S_B7 + 2 * D),
                       slot_addr + uint32_t(C::S_INFO + 4), tw, xb, sm, g16, t0, rows, rows, BF16IN, lane);
     if (lane == 0) mbar_arrive(empty);  // this warp has read everything it needs from the slot
 #pragma unroll
@@ -869,9 +930,9 @@ __device__ __forceinline__ void flush_state(const AttnArgs &a, size_t idx, const
 // arrives once per stage on the slot's empty barrier, and writes its state at every segment end
 // (the unit's last block, or the end of the range).  It has seen stage gs - 1 (and so gs - NSLOT)
 // land before it waits on stage gs, so the parity of the slot's full barrier identifies the stage.
-template <int D, bool BF16IN>
+template <int D, bool CP, bool BF16IN>
 __device__ void consumer(const AttnArgs &a, uint8_t *smem, int w, int lane, int fb0, int fb1, int row0) {
-    using C = Cfg<D>;
+    using C = Cfg<D, CP>;
     const uint32_t sb = smem_u32(smem);
     const uint32_t xb = sb + uint32_t(C::O_TILE + w * C::TILE);
     StoreMap<D> sm;
@@ -885,7 +946,7 @@ __device__ void consumer(const AttnArgs &a, uint8_t *smem, int w, int lane, int 
     for (int b = fb0; b < fb1; ++b) {
         for (int t0 = 0;; t0 += C::TSB) {
             const int slot = gs % C::NSLOT;
-            const uint32_t full = ring_bar<D>(sb, slot), empty = ring_bar<D>(sb, C::NSLOT + slot);
+            const uint32_t full = ring_bar<D, CP>(sb, slot), empty = ring_bar<D, CP>(sb, C::NSLOT + slot);
             if (!uni(mbar_wait_bounded(full, uint32_t((gs / C::NSLOT) & 1), kStageWaitUs))) {
                 if (lane == 0) report(a.status, KVX_ERR_TIMEOUT, DERR_TIMEOUT);
                 return;
@@ -903,7 +964,7 @@ __device__ void consumer(const AttnArgs &a, uint8_t *smem, int w, int lane, int 
             const bool seg_end = last && ((flags & kDescLast) != 0u || b + 1 == fb1);
             const int rows = valid - t0 - TT * C::NT * tp;
             if (tp < C::TPP && rows > 0) {
-                tile_step<D, BF16IN>(a, bd, smem_u32(sp), empty, xb, sm, C::NT * tp, t0,
+                tile_step<D, CP, BF16IN>(a, bd, smem_u32(sp), empty, xb, sm, C::NT * tp, t0,
                                      min(rows, C::NT * TT), qb, st, lane);
             } else {
                 __syncwarp();  // every lane has read the descriptor
@@ -930,11 +991,11 @@ __device__ void consumer(const AttnArgs &a, uint8_t *smem, int w, int lane, int 
 // semantics, so the test after it sees at least the phase of stage gs - NSLOT completed, and then
 // passes only when stage gs has landed; the slot then holds stage gs until this warp arrives on the
 // slot's empty barrier.  Returns false after kStageWaitUs (the decision is the warp's, uniform).
-template <int D>
+template <int D, bool CP>
 __device__ __forceinline__ bool wait_stage(uint32_t sb, int gs) {
-    using C = Cfg<D>;
+    using C = Cfg<D, CP>;
     const int slot = gs % C::NSLOT;
-    const uint32_t full = ring_bar<D>(sb, slot);
+    const uint32_t full = ring_bar<D, CP>(sb, slot);
     const uint32_t tag = sb + uint32_t(slot * C::SLOT + C::S_TAG);
     const uint32_t par = uint32_t((gs / C::NSLOT) & 1);
     uint64_t t0 = 0;
@@ -954,10 +1015,10 @@ __device__ __forceinline__ bool wait_stage(uint32_t sb, int gs) {
 // only on those, and arrives once per group (the slot's empty barrier counts TPP arrivals).  Its state is written
 // when the unit of its next tile differs, and at the end of the range, to row
 // row0 + (unit - the range's first unit); rows a warp never reaches keep m = -inf, l = 0.
-template <int D, bool BF16IN>
+template <int D, bool CP, bool BF16IN>
 __device__ void consumer_by_tile(const AttnArgs &a, uint8_t *smem, int w, int lane, int fb0, int fb1,
                                  int row0) {
-    using C = Cfg<D>;
+    using C = Cfg<D, CP>;
     const uint32_t sb = smem_u32(smem);
     const uint32_t xb = sb + uint32_t(C::O_TILE + w * C::TILE);
     StoreMap<D> sm;
@@ -973,8 +1034,8 @@ __device__ void consumer_by_tile(const AttnArgs &a, uint8_t *smem, int w, int la
         const int gs = j / C::TPP, tw = (j % C::TPP) * C::NT;
         const int t0 = (gs % spb) * C::TSB;
         const int slot = gs % C::NSLOT;
-        const uint32_t empty = ring_bar<D>(sb, C::NSLOT + slot);
-        if (!wait_stage<D>(sb, gs)) {
+        const uint32_t empty = ring_bar<D, CP>(sb, C::NSLOT + slot);
+        if (!wait_stage<D, CP>(sb, gs)) {
             if (lane == 0) report(a.status, KVX_ERR_TIMEOUT, DERR_TIMEOUT);
             return;
         }
@@ -990,7 +1051,7 @@ __device__ void consumer_by_tile(const AttnArgs &a, uint8_t *smem, int w, int la
         }
         const int rows = valid - t0 - TT * tw;
         if (rows > 0) {
-            tile_step<D, BF16IN>(a, bd, smem_u32(sp), empty, xb, sm, tw, t0, min(rows, C::NT * TT), qb, st,
+            tile_step<D, CP, BF16IN>(a, bd, smem_u32(sp), empty, xb, sm, tw, t0, min(rows, C::NT * TT), qb, st,
                                  lane);
         } else {
             __syncwarp();  // every lane has read the descriptor
@@ -1000,9 +1061,9 @@ __device__ void consumer_by_tile(const AttnArgs &a, uint8_t *smem, int w, int la
     if (cur >= 0) flush_state<D>(a, size_t(row0 + cur - unit0) * C::NW + size_t(w), st, lane);
 }
 
-template <int D, bool BF16IN>
-__global__ void __launch_bounds__(Cfg<D>::THREADS, 1) attn_kernel(const AttnArgs a) {
-    using C = Cfg<D>;
+template <int D, bool CP, bool BF16IN>
+__global__ void __launch_bounds__(Cfg<D, CP>::THREADS, 1) attn_kernel(const AttnArgs a) {
+    using C = Cfg<D, CP>;
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ int skip;
     // Launched as a programmatic dependent of the kernel before it in the stream (the previous
@@ -1021,9 +1082,9 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1) attn_kernel(const AttnArgs
     if (threadIdx.x == 0) {
         const uint32_t sb = smem_u32(smem);
         for (int j = 0; j < C::NSLOT; ++j) {
-            mbar_init(ring_bar<D>(sb, j), 1);               // full: the producer's arrive + bytes
+            mbar_init(ring_bar<D, CP>(sb, j), 1);               // full: the producer's arrive + bytes
             // empty: one arrive per consumer warp, or per tile group when the warps go by tile
-            mbar_init(ring_bar<D>(sb, C::NSLOT + j), by_tile ? C::TPP : C::NW);
+            mbar_init(ring_bar<D, CP>(sb, C::NSLOT + j), by_tile ? C::TPP : C::NW);
             // no stage yet (shared memory keeps whatever an earlier CTA left there)
             sts_u32(sb + uint32_t(j * C::SLOT + C::S_TAG), 0xFFFFFFFFu);
         }
@@ -1034,13 +1095,16 @@ __global__ void __launch_bounds__(Cfg<D>::THREADS, 1) attn_kernel(const AttnArgs
     __syncthreads();
     if (skip != 0) return;
     if (warp >= C::NW) {
-        producer<D, BF16IN>(a, smem, fb0, fb1, warp - C::NW, lane);
+        if (a.stages != nullptr)
+            producer_listed<D, CP, BF16IN>(a, smem, fb0, fb1, warp - C::NW, lane);
+        else
+            producer<D, CP, BF16IN>(a, smem, fb0, fb1, warp - C::NW, lane);
         return;
     }
     if (by_tile)
-        consumer_by_tile<D, BF16IN>(a, smem, warp, lane, fb0, fb1, a.seg_base[c]);
+        consumer_by_tile<D, CP, BF16IN>(a, smem, warp, lane, fb0, fb1, a.seg_base[c]);
     else
-        consumer<D, BF16IN>(a, smem, warp, lane, fb0, fb1, a.seg_base[c]);
+        consumer<D, CP, BF16IN>(a, smem, warp, lane, fb0, fb1, a.seg_base[c]);
 }
 
 // ---- combine ------------------------------------------------------------------------------------
@@ -1216,14 +1280,88 @@ __global__ void __launch_bounds__(1024) split_kernel(const FlatBlock *flat, int6
         for (int w2 = 1; w2 < nw; ++w2) range_begin[w2] = n;
 }
 
-template <int D> void configure(bool bf16) {
-    static bool done[2] = {false, false};
-    if (done[bf16]) return;
+template <int D, bool CP, bool BF16IN> void configure() {
+    static bool done = false;
+    if (done) return;
+    cudaFuncSetAttribute(attn_kernel<D, CP, BF16IN>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<D, CP>::SMEM);
+    done = true;
+}
+
+// ---- stage copy lists ------------------------------------------------------------------------------
+
+// One thread per (flat block, stage): the stage's copy list (kStageRecWords words) from the block's
+// descriptor -- the pieces a producer warp issues for the stage, where they land in the slot, and
+// where the consumers find the staged escape-record entries.
+template <int D, bool CP, bool BF16IN>
+__global__ void stage_table_kernel(const BlockDesc *desc, const uint32_t *b7, const uint32_t *esc,
+                                   int64_t n_blocks, int spb, uint4 *table) {
+    using C = Cfg<D, CP>;
+    const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= n_blocks * spb) return;
+    const int64_t b = i / spb;
+    const int t0 = int(i % spb) * C::TSB;
+    const BlockDesc &d = desc[b];
+    const int km = BF16IN ? 0 : d.k_mode, vm = BF16IN ? 0 : d.v_mode;
+    const int n_tok = d.n_tok;
+    const int n = min(C::TSB, int(d.valid) - t0);
+    const bool whole = t0 == 0 && n == n_tok;
+    uint4 w[kStageRecWords];
+#pragma unroll
+    for (int k = 0; k < kStageRecWords; ++k) w[k] = make_uint4(0u, 0u, 0u, 0u);
+    uint32_t total = 0;
+    auto put = [&](int k, const void *src, uint32_t len, uint32_t dst) {
+        if (len == 0u) return;
+        const Piece p = make_piece(static_cast<const uint8_t *>(src), len);
+        const uint64_t a = reinterpret_cast<uint64_t>(p.src);
+        w[k] = make_uint4(uint32_t(a), uint32_t(a >> 32), p.alloc, dst);
+        total += p.alloc;
+    };
+    put(0, desc + b, uint32_t(sizeof(BlockDesc)), 0u);
+    if (!BF16IN && (km | vm) != 0 && n > 0) put(1, b7 + size_t(d.b7_block) * D, uint32_t(4 * D), uint32_t(C::S_B7));
+    int rel[2] = {0, 0};
+    uint32_t staged = 0;
+    for (int T = 0; T < 2 && n > 0; ++T) {
+        const uint8_t *blk = reinterpret_cast<const uint8_t *>(T ? d.v : d.k);
+        const int mode = T ? vm : km;
+        const uint32_t reg = uint32_t(C::S_T + T * C::T_BYTES);
+        if (BF16IN) {
+            put(2 + 3 * T, blk + size_t(t0) * 2 * D, uint32_t(n * 2 * D), reg);
+        } else if (mode == 0) {
+            put(2 + 3 * T, blk + kHeaderBytes + size_t(t0) * 2 * D, uint32_t(n * 2 * D), reg);
+        } else {
+            // rows, with the codes when the stage is the whole block (they follow the rows)
+            put(2 + 3 * T, blk + kHeaderBytes + D + size_t(t0) * D, uint32_t(n * D + (whole ? n * D * mode / 8 : 0)), reg);
+            if (!whole)
+                put(3 + 3 * T, blk + kHeaderBytes + D + size_t(n_tok) * D + size_t(t0) * D * mode / 8,
+                    uint32_t(n * D * mode / 8), reg + uint32_t(C::CODE_OFF));
+            const int e0 = esc_ms(d, T, t0 >> 4), e1 = esc_ms(d, T, min(16, (t0 + C::TSB) >> 4));
+            if (e1 > e0 && e1 - e0 <= C::ESC_CAP) {
+                const uint32_t r = T ? d.v_rec : d.k_rec;
+                put(4 + 3 * T, esc + r + kEscRecHead + e0, uint32_t(4 * (e1 - e0)), reg + uint32_t(C::E_OFF));
+                rel[T] = int(reg + uint32_t(C::E_OFF) + esc_rec_line(r, e0)) - 4 * e0;
+                staged |= 1u << T;
+            }
+        }
+    }
+    w[8] = make_uint4(uint32_t(rel[0]), uint32_t(rel[1]), total, staged);
+    uint4 *out = table + size_t(i) * kStageRecWords;
+#pragma unroll
+    for (int k = 0; k < kStageRecWords; ++k) out[k] = w[k];
+}
+
+template <int D>
+cudaError_t stage_table_d(bool bf16, bool compact, const BlockDesc *desc, const uint32_t *b7, const uint32_t *esc,
+                          int64_t n_blocks, int spb, uint4 *table, cudaStream_t s) {
+    const int64_t n = n_blocks * spb;
+    if (n <= 0) return cudaSuccess;
+    const unsigned grid = unsigned((n + 127) / 128);
     if (bf16)
-        cudaFuncSetAttribute(attn_kernel<D, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<D>::SMEM);
+        stage_table_kernel<D, false, true><<<grid, 128, 0, s>>>(desc, b7, esc, n_blocks, spb, table);
+    else if (compact)
+        stage_table_kernel<D, true, false><<<grid, 128, 0, s>>>(desc, b7, esc, n_blocks, spb, table);
     else
-        cudaFuncSetAttribute(attn_kernel<D, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<D>::SMEM);
-    done[bf16] = true;
+        stage_table_kernel<D, false, false><<<grid, 128, 0, s>>>(desc, b7, esc, n_blocks, spb, table);
+    return cudaGetLastError();
 }
 
 // ---- block descriptors ---------------------------------------------------------------------------
@@ -1294,32 +1432,46 @@ __global__ void init_partials_kernel(float *partials, int64_t n_states, int stri
     partials[st * stride + f] = f < 8 ? -INFINITY : 0.f;
 }
 
-// The largest number of attended tokens of any flat block (atomic max into *out, set to 0 first).
+// The largest number of attended tokens of any flat block (atomic max into out[0]) and whether any
+// block has a raw K or V (out[1] != 0); both set to 0 first.
 __global__ void max_valid_kernel(const FlatBlock *flat, int64_t n, int *out) {
-    int m = 0;
-    for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += int64_t(gridDim.x) * blockDim.x)
-        m = max(m, int(load_flat(flat, i).valid));
+    int m = 0, raw = 0;
+    for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += int64_t(gridDim.x) * blockDim.x) {
+        const FlatBlock f = load_flat(flat, i);
+        m = max(m, int(f.valid));
+        raw |= (f.k_mode == 0 || f.v_mode == 0) ? 1 : 0;
+    }
     m = __reduce_max_sync(FULL, m);
-    if ((threadIdx.x & 31) == 0) atomicMax(out, m);
+    raw = __reduce_or_sync(FULL, raw);
+    if ((threadIdx.x & 31) == 0) {
+        atomicMax(out, m);
+        if (raw) atomicOr(out + 1, 1);
+    }
 }
 
-template <int D>
-cudaError_t launch_d(bool bf16, const AttnArgs &a, int grid, cudaStream_t s) {
-    configure<D>(bf16);
+template <int D, bool CP, bool BF16IN>
+cudaError_t launch_d(const AttnArgs &a, int grid, cudaStream_t s) {
+    configure<D, CP, BF16IN>();
     // programmatic dependent launch: the grid may be set up while the kernel before it in the
     // stream drains (the kernel waits for that grid before it reads anything)
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
-    cfg.blockDim = dim3(Cfg<D>::THREADS);
-    cfg.dynamicSmemBytes = size_t(Cfg<D>::SMEM);
+    cfg.blockDim = dim3(Cfg<D, CP>::THREADS);
+    cfg.dynamicSmemBytes = size_t(Cfg<D, CP>::SMEM);
     cfg.stream = s;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    if (bf16) return cudaLaunchKernelEx(&cfg, attn_kernel<D, true>, a);
-    return cudaLaunchKernelEx(&cfg, attn_kernel<D, false>, a);
+    return cudaLaunchKernelEx(&cfg, attn_kernel<D, CP, BF16IN>, a);
+}
+
+template <int D>
+cudaError_t launch_dim(bool bf16, bool compact, const AttnArgs &a, int grid, cudaStream_t s) {
+    if (bf16) return launch_d<D, false, true>(a, grid, s);
+    if (compact) return launch_d<D, true, false>(a, grid, s);
+    return launch_d<D, false, false>(a, grid, s);
 }
 
 }  // namespace
@@ -1328,22 +1480,13 @@ bool attention_dim_supported(int dim) {
     return dim == 32 || dim == 64 || dim == 128 || dim == 256;
 }
 
-size_t attention_smem_bytes(int dim) {
+cudaError_t launch_attention(int dim, bool bf16_input, bool compact, const AttnArgs &a, int grid,
+                             cudaStream_t s) {
     switch (dim) {
-    case 32: return size_t(Cfg<32>::SMEM);
-    case 64: return size_t(Cfg<64>::SMEM);
-    case 128: return size_t(Cfg<128>::SMEM);
-    case 256: return size_t(Cfg<256>::SMEM);
-    default: return 0;
-    }
-}
-
-cudaError_t launch_attention(int dim, bool bf16_input, const AttnArgs &a, int grid, cudaStream_t s) {
-    switch (dim) {
-    case 32: return launch_d<32>(bf16_input, a, grid, s);
-    case 64: return launch_d<64>(bf16_input, a, grid, s);
-    case 128: return launch_d<128>(bf16_input, a, grid, s);
-    case 256: return launch_d<256>(bf16_input, a, grid, s);
+    case 32: return launch_dim<32>(bf16_input, compact, a, grid, s);
+    case 64: return launch_dim<64>(bf16_input, compact, a, grid, s);
+    case 128: return launch_dim<128>(bf16_input, compact, a, grid, s);
+    case 256: return launch_dim<256>(bf16_input, compact, a, grid, s);
     default: return cudaErrorInvalidValue;
     }
 }
@@ -1363,7 +1506,7 @@ cudaError_t launch_init_partials(float *partials, int64_t n_states, int dim, cud
 
 cudaError_t launch_max_valid(const FlatBlock *flat, int64_t n_blocks, int *out, cudaStream_t s) {
     if (n_blocks <= 0) return cudaSuccess;
-    cudaError_t e = cudaMemsetAsync(out, 0, sizeof(int), s);
+    cudaError_t e = cudaMemsetAsync(out, 0, 2 * sizeof(int), s);
     if (e != cudaSuccess) return e;
     const int64_t grid = (n_blocks + 255) / 256 < 1024 ? (n_blocks + 255) / 256 : 1024;
     max_valid_kernel<<<unsigned(grid), 256, 0, s>>>(flat, n_blocks, out);
@@ -1404,6 +1547,18 @@ cudaError_t launch_b7(const UnitDev *units, const FlatBlock *flat, int64_t n_blo
     if (n_blocks <= 0) return cudaSuccess;
     b7_kernel<<<unsigned((n_blocks + 7) / 8), 256, 0, s>>>(units, flat, n_blocks, dim, b7);
     return cudaGetLastError();
+}
+
+cudaError_t launch_stage_table(int dim, bool bf16, bool compact, const BlockDesc *desc, const uint32_t *b7,
+                               const uint32_t *esc, int64_t n_blocks, int stages_per_block,
+                               uint4 *table, cudaStream_t s) {
+    switch (dim) {
+    case 32: return stage_table_d<32>(bf16, compact, desc, b7, esc, n_blocks, stages_per_block, table, s);
+    case 64: return stage_table_d<64>(bf16, compact, desc, b7, esc, n_blocks, stages_per_block, table, s);
+    case 128: return stage_table_d<128>(bf16, compact, desc, b7, esc, n_blocks, stages_per_block, table, s);
+    case 256: return stage_table_d<256>(bf16, compact, desc, b7, esc, n_blocks, stages_per_block, table, s);
+    default: return cudaErrorInvalidValue;
+    }
 }
 
 cudaError_t launch_block_desc(const UnitDev *units, const FlatBlock *flat, const uint32_t *esc, int64_t n,

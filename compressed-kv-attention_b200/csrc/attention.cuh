@@ -52,12 +52,12 @@ __host__ __device__ inline uint32_t esc_scratch_slot(int dim, int T, int r, int 
     return uint32_t(r * 2 * dim + ((c8 ^ sw) << 4) + 2 * (c & 7));
 }
 
-// Consumer warps per CTA of the attention kernel (one CTA per SM; two more warps issue the
+// Consumer warps per CTA of the attention kernel (one CTA per SM; one more warp issues the
 // copies): a CTA of 16 warps at 128 registers a thread for dim <= 64, 12 at 168 for dim 128, 8 at
 // 255 for dim 256.  A stage of 128 tokens (64 at dim 128, 32 at dim 256) is 8 (4, 2) tiles, dealt
 // round robin.
 __host__ __device__ constexpr int attention_consumer_warps(int dim) {
-    return dim >= 256 ? 6 : (dim >= 128 ? 10 : 14);
+    return dim >= 256 ? 7 : (dim >= 128 ? 11 : 15);
 }
 
 // Tokens per ring stage of the attention kernel: 8 KiB of BF16 per tensor (128 tokens at dim <= 64).
@@ -120,10 +120,22 @@ static_assert(sizeof(BlockDesc) == 128 && offsetof(BlockDesc, align) == 36 &&
               "BlockDesc layout");
 constexpr uint8_t kDescFirst = 1, kDescLast = 2;  // the first / last block of its unit
 
+// Copy list of one ring stage of the attention kernel, built once per plan (launch_stage_table)
+// so that a producer warp only loads it and issues: kStageRecWords 16-byte words, word i read by
+// producer lane i.  Words 0-7 are the stage's pieces {source address (low, high), bytes copied
+// (a multiple of 16; 0: none), destination offset in the ring slot}: 0 the block descriptor, 1 the
+// merge words, 2 + 3 T / 3 + 3 T / 4 + 3 T tensor T's rows (with the codes when the stage is the
+// whole block), residual codes and escape-record entries.  Word 8: {K escape entries, V escape
+// entries (int32 offsets in the slot from which entry i is read at + 4 i), the stage's total
+// bytes, bit 0 / 1: the K / V entries are staged (else they stay in HBM)}.
+constexpr int kStageRecWords = 9;
+
 struct AttnArgs {
     const UnitDev *units;
     const FlatBlock *flat;      // [n_blocks]
     const BlockDesc *desc;      // [n_blocks]
+    const uint4 *stages;        // [n_blocks][stages_per_block][kStageRecWords] copy lists, or null
+                                // (the producer then works the pieces out from the descriptors)
     const uint32_t *esc;        // escape records (FlatBlock::k_rec / v_rec index it)
     const uint32_t *b7;         // [n_blocks][dim] merge words of each coded block: K, then V
     const int64_t *range_begin; // [n_ranges + 1] flat-block range of each CTA
@@ -178,7 +190,10 @@ inline int64_t segment_rows(const int64_t *range_begin, int n_ranges, const int6
 }
 
 // Launchers (attention.cu).  Return cudaError_t of the launch.
-cudaError_t launch_attention(int dim, bool bf16_input, const AttnArgs &a, int grid, cudaStream_t s);
+// compact: every block of the step is coded (the 6-slot ring sized for coded stages; raw rows do
+// not fit its slots).
+cudaError_t launch_attention(int dim, bool bf16_input, bool compact, const AttnArgs &a, int grid,
+                             cudaStream_t s);
 cudaError_t launch_combine(int dim, const CombineArgs &a, int n_split, cudaStream_t s);
 // Merge words of a step's coded blocks (blocks that share another block's K/V blocks -- a later
 // query group of the same unit -- use that block's): for block f and tensor T, word w of
@@ -189,11 +204,17 @@ cudaError_t launch_b7(const UnitDev *units, const FlatBlock *flat, int64_t n_blo
 // Block descriptors of a step from its flat blocks, units and escape records.
 cudaError_t launch_block_desc(const UnitDev *units, const FlatBlock *flat, const uint32_t *esc, int64_t n,
                               int dim, bool bf16, BlockDesc *desc, cudaStream_t s);
+// Stage copy lists of a step (stages_per_block stages of every flat block) from its block
+// descriptors, merge words and escape records.
+cudaError_t launch_stage_table(int dim, bool bf16, bool compact, const BlockDesc *desc, const uint32_t *b7,
+                               const uint32_t *esc, int64_t n_blocks, int stages_per_block,
+                               uint4 *table, cudaStream_t s);
 cudaError_t launch_fold(const float *parts, int n_parts, int n_rows, int dim, float *out,
                         float *lse_out, cudaStream_t s);
 // m = -inf, l = 0 in n_states partial states (so that states no warp writes add nothing).
 cudaError_t launch_init_partials(float *partials, int64_t n_states, int dim, cudaStream_t s);
-// *out = the largest number of attended tokens of any flat block.
+// out[0] = the largest number of attended tokens of any flat block; out[1] != 0 when some block
+// has a raw K or V.
 cudaError_t launch_max_valid(const FlatBlock *flat, int64_t n_blocks, int *out, cudaStream_t s);
 // Escape records: sizes and offsets (single CTA; *total receives the record array length in u16,
 // blocks whose src is another block take that block's offsets, and a record that would end past
@@ -208,7 +229,6 @@ cudaError_t launch_esc_fill(const UnitDev *units, const FlatBlock *flat, int64_t
 // the token counts, so an XKV step and a BF16 step over the same tokens get the same ranges).
 cudaError_t launch_split(const FlatBlock *flat, int64_t n_blocks, int n_ranges, bool by_tokens,
                          int64_t *range_begin, cudaStream_t s);
-size_t attention_smem_bytes(int dim);
 bool attention_dim_supported(int dim);
 
 }  // namespace kvx
