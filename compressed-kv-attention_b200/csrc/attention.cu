@@ -1309,12 +1309,14 @@ __global__ void stage_table_kernel(const BlockDesc *desc, const uint32_t *b7, co
 #pragma unroll
     for (int k = 0; k < kStageRecWords; ++k) w[k] = make_uint4(0u, 0u, 0u, 0u);
     uint32_t total = 0;
-    auto put = [&](int k, const void *src, uint32_t len, uint32_t dst) {
-        if (len == 0u) return;
+    // piece k: [src, src + len) to slot offset dst; returns the bytes copied
+    auto put = [&](int k, const void *src, uint32_t len, uint32_t dst) -> uint32_t {
+        if (len == 0u) return 0u;
         const Piece p = make_piece(static_cast<const uint8_t *>(src), len);
         const uint64_t a = reinterpret_cast<uint64_t>(p.src);
         w[k] = make_uint4(uint32_t(a), uint32_t(a >> 32), p.alloc, dst);
         total += p.alloc;
+        return p.alloc;
     };
     put(0, desc + b, uint32_t(sizeof(BlockDesc)), 0u);
     if (!BF16IN && (km | vm) != 0 && n > 0) put(1, b7 + size_t(d.b7_block) * D, uint32_t(4 * D), uint32_t(C::S_B7));
@@ -1329,17 +1331,27 @@ __global__ void stage_table_kernel(const BlockDesc *desc, const uint32_t *b7, co
         } else if (mode == 0) {
             put(2 + 3 * T, blk + kHeaderBytes + size_t(t0) * 2 * D, uint32_t(n * 2 * D), reg);
         } else {
-            // rows, with the codes when the stage is the whole block (they follow the rows)
-            put(2 + 3 * T, blk + kHeaderBytes + D + size_t(t0) * D, uint32_t(n * D + (whole ? n * D * mode / 8 : 0)), reg);
+            // rows, with the codes when the stage is the whole block (they follow the rows); `end`:
+            // the first free byte of the tensor's region after them (16-byte aligned)
+            uint32_t end = reg + put(2 + 3 * T, blk + kHeaderBytes + D + size_t(t0) * D,
+                                     uint32_t(n * D + (whole ? n * D * mode / 8 : 0)), reg);
             if (!whole)
-                put(3 + 3 * T, blk + kHeaderBytes + D + size_t(n_tok) * D + size_t(t0) * D * mode / 8,
-                    uint32_t(n * D * mode / 8), reg + uint32_t(C::CODE_OFF));
+                end = reg + uint32_t(C::CODE_OFF) +
+                      put(3 + 3 * T, blk + kHeaderBytes + D + size_t(n_tok) * D + size_t(t0) * D * mode / 8,
+                          uint32_t(n * D * mode / 8), reg + uint32_t(C::CODE_OFF));
+            // the escape-record entries go right behind, when they fit in the region (narrower codes
+            // leave more room: a 2-bit stage of the compact ring takes about three times the entries
+            // of a 4-bit one); otherwise the consumers read them from HBM
             const int e0 = esc_ms(d, T, t0 >> 4), e1 = esc_ms(d, T, min(16, (t0 + C::TSB) >> 4));
-            if (e1 > e0 && e1 - e0 <= C::ESC_CAP) {
+            if (e1 > e0) {
                 const uint32_t r = T ? d.v_rec : d.k_rec;
-                put(4 + 3 * T, esc + r + kEscRecHead + e0, uint32_t(4 * (e1 - e0)), reg + uint32_t(C::E_OFF));
-                rel[T] = int(reg + uint32_t(C::E_OFF) + esc_rec_line(r, e0)) - 4 * e0;
-                staged |= 1u << T;
+                const uint32_t *src = esc + r + kEscRecHead + e0;
+                const uint32_t len = uint32_t(4 * (e1 - e0));
+                if (end + make_piece(reinterpret_cast<const uint8_t *>(src), len).alloc <= reg + uint32_t(C::T_BYTES)) {
+                    put(4 + 3 * T, src, len, end);
+                    rel[T] = int(end + esc_rec_line(r, e0)) - 4 * e0;
+                    staged |= 1u << T;
+                }
             }
         }
     }
