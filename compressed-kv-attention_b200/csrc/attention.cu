@@ -715,23 +715,48 @@ __device__ void producer_listed(const AttnArgs &a, uint8_t *smem, int fb0, int f
     }
 }
 
+// The descriptor fields a consumer warp uses during one visit of a stage, read from the slot's
+// copy of the block descriptor by two 16-byte loads (bytes 16-47 of BlockDesc).
+struct VisitDesc {
+    uint32_t k_rec, v_rec, nesc;
+    uint32_t mw;      // k_mode | v_mode << 8 | n_tok << 16 | valid << 24
+    int32_t unit;
+    uint32_t align;   // BlockDesc::align as one word
+    uint32_t flags, b7_block;
+    __device__ __forceinline__ int k_mode() const { return int(mw & 0xFFu); }
+    __device__ __forceinline__ int v_mode() const { return int((mw >> 8) & 0xFFu); }
+    __device__ __forceinline__ int n_tok() const { return int((mw >> 16) & 0xFFu); }
+    __device__ __forceinline__ int valid() const { return int(mw >> 24); }
+};
+static_assert(offsetof(BlockDesc, k_rec) == 16 && offsetof(BlockDesc, k_mode) == 28 &&
+                  offsetof(BlockDesc, valid) == 31 && offsetof(BlockDesc, unit) == 32,
+              "VisitDesc mirrors bytes 16-47 of BlockDesc");
+__device__ __forceinline__ VisitDesc load_visit(uint32_t slot_addr) {
+    VisitDesc v;
+    uint32_t u;
+    lds_v4(slot_addr + 16u, v.k_rec, v.v_rec, v.nesc, v.mw);
+    lds_v4(slot_addr + 32u, u, v.align, v.flags, v.b7_block);
+    v.unit = int32_t(u);
+    return v;
+}
+
 // One tensor of the warp's NT tiles (tiles tw .. tw + NT - 1 of the stage) into its BF16 tiles,
 // escapes included.  reg: the tensor's region of the slot; b7s: the tensor's merge words in the
 // slot; info: the producer's escape word of the tensor for this stage; g16: the first tile's
 // 16-token group in the block; t0: the stage's first token in the block; rows: valid rows from the
 // first tile's first row on; zero_from: rows at or past it are zeroed.
 template <int D, bool CP, int T>
-__device__ __forceinline__ void tile_tensor(const AttnArgs &a, const BlockDesc &bd, int mode,
-                                            uint32_t al, uint32_t reg, uint32_t b7s, uint32_t info, int tw,
-                                            uint32_t xb,
+__device__ __forceinline__ void tile_tensor(const AttnArgs &a, const BlockDesc &bd, const VisitDesc &vd,
+                                            int mode, uint32_t al, uint32_t reg, uint32_t b7s, uint32_t info,
+                                            int tw, uint32_t xb,
                                             const StoreMap<D> &sm, int g16, int t0, int rows,
                                             int zero_from, bool bf16, int lane) {
     using C = Cfg<D, CP>;
     const int c8 = lane % C::C8;
     const uint32_t rd = al & 15u, cd = (al >> 8) & 15u;
     // a whole block in one stage came as one copy: the codes follow its n rows
-    const int n = min(C::TSB, int(bd.valid) - t0);
-    const bool whole = t0 == 0 && n == int(bd.n_tok);
+    const int n = min(C::TSB, vd.valid() - t0);
+    const bool whole = t0 == 0 && n == vd.n_tok();
     const uint32_t code_base = whole ? ((rd + uint32_t(n * D)) & ~15u) : uint32_t(C::CODE_OFF);
     const Lay ly = make_lay<D>(rd, cd, mode, c8, bf16, code_base);
     const uint32_t rb = reg + uint32_t(TT * tw * (mode == 0 ? 2 * D : D));
@@ -747,7 +772,7 @@ __device__ __forceinline__ void tile_tensor(const AttnArgs &a, const BlockDesc &
         ents = lds_u32(info);  // the producer's word for this stage and tensor
         if (e0 + lane < e1)
             ent = (ents & 1u) ? lds_u32((ents & ~1u) + 4u * uint32_t(e0 + lane))
-                              : __ldg(a.esc + (T ? bd.v_rec : bd.k_rec) + kEscRecHead + e0 + lane);
+                              : __ldg(a.esc + (T ? vd.v_rec : vd.k_rec) + kEscRecHead + e0 + lane);
     }
     if (mode != 0) {
         uint32_t b7[4];
@@ -769,7 +794,7 @@ __device__ __forceinline__ void tile_tensor(const AttnArgs &a, const BlockDesc &
             if (ents & 1u)
                 esc_patch<D>(xb, ents & ~1u, e0 + 32, e1, em, rows, lane);
             else
-                esc_patch_hbm<D>(xb, a.esc + (T ? bd.v_rec : bd.k_rec) + kEscRecHead, e0 + 32, e1, em,
+                esc_patch_hbm<D>(xb, a.esc + (T ? vd.v_rec : vd.k_rec) + kEscRecHead, e0 + 32, e1, em,
                                  rows, lane);
         }
     }
@@ -794,27 +819,28 @@ template <int D> struct SoftState {
 // K fragments and run meanwhile), free the slot, online softmax, O += P V.  rows: valid rows from
 // the first tile's first row (1 .. NT 16).
 template <int D, bool CP, bool BF16IN>
-__device__ __forceinline__ void tile_step(const AttnArgs &a, const BlockDesc &bd, uint32_t slot_addr,
+__device__ __forceinline__ void tile_step(const AttnArgs &a, const BlockDesc &bd, const VisitDesc &vd,
+                                          uint32_t slot_addr,
                                           uint32_t empty, uint32_t xb, const StoreMap<D> &sm, int tw,
                                           int t0, int rows, const uint32_t (&qb)[Cfg<D>::KS][2],
                                           SoftState<D> &st, int lane) {
     using C = Cfg<D, CP>;
     constexpr int NT = C::NT;
     const int gi = lane >> 2;
-    const uint32_t al = *reinterpret_cast<const uint32_t *>(bd.align);
-    const int km = BF16IN ? 0 : bd.k_mode, vm = BF16IN ? 0 : bd.v_mode;
+    const uint32_t al = vd.align;
+    const int km = BF16IN ? 0 : vd.k_mode(), vm = BF16IN ? 0 : vd.v_mode();
     const int g16 = (t0 >> 4) + tw;
     const uint32_t kreg = slot_addr + uint32_t(C::S_T), vreg = kreg + uint32_t(C::T_BYTES);
 
     // S^T = K Q^T (rows past `rows` hold stale words: their scores are dropped)
-    tile_tensor<D, CP, 0>(a, bd, km, al & 0xFFFFu, kreg, slot_addr + uint32_t(C::S_B7),
+    tile_tensor<D, CP, 0>(a, bd, vd, km, al & 0xFFFFu, kreg, slot_addr + uint32_t(C::S_B7),
                       slot_addr + uint32_t(C::S_INFO), tw, xb, sm, g16, t0, rows, NT * TT, BF16IN, lane);
     float s[NT][4];
     qk_tiles<D, NT>(xb, qb, lane, s);
     // V replaces K in the tiles once every lane's K fragments are loaded (the MMAs above need only
     // those registers); rows past `rows` are zeroed (P is 0 there and V must be finite)
     __syncwarp();
-    tile_tensor<D, CP, 1>(a, bd, vm, al >> 16, vreg, slot_addr + uint32_t(C::S_B7 + 2 * D),
+    tile_tensor<D, CP, 1>(a, bd, vd, vm, al >> 16, vreg, slot_addr + uint32_t(C::S_B7 + 2 * D),
                       slot_addr + uint32_t(C::S_INFO + 4), tw, xb, sm, g16, t0, rows, rows, BF16IN, lane);
     if (lane == 0) mbar_arrive(empty);  // this warp has read everything it needs from the slot
 #pragma unroll
@@ -953,10 +979,11 @@ __device__ void consumer(const AttnArgs &a, uint8_t *smem, int w, int lane, int 
             }
             const uint8_t *sp = smem + slot * C::SLOT;
             const BlockDesc &bd = *reinterpret_cast<const BlockDesc *>(sp);
-            const int valid = bd.valid;
-            const uint32_t flags = bd.flags;
+            const VisitDesc vd = load_visit(smem_u32(sp));
+            const int valid = vd.valid();
+            const uint32_t flags = vd.flags;
             if (t0 == 0 && (b == fb0 || (flags & kDescFirst) != 0u)) {
-                const UnitDev *U = a.units + bd.unit;
+                const UnitDev *U = a.units + vd.unit;
                 load_q<D>(U->q, U->n_q, U->q_stride, qb, lane);
                 st.reset();
             }
@@ -964,7 +991,7 @@ __device__ void consumer(const AttnArgs &a, uint8_t *smem, int w, int lane, int 
             const bool seg_end = last && ((flags & kDescLast) != 0u || b + 1 == fb1);
             const int rows = valid - t0 - TT * C::NT * tp;
             if (tp < C::TPP && rows > 0) {
-                tile_step<D, CP, BF16IN>(a, bd, smem_u32(sp), empty, xb, sm, C::NT * tp, t0,
+                tile_step<D, CP, BF16IN>(a, bd, vd, smem_u32(sp), empty, xb, sm, C::NT * tp, t0,
                                      min(rows, C::NT * TT), qb, st, lane);
             } else {
                 __syncwarp();  // every lane has read the descriptor
@@ -1027,12 +1054,14 @@ __device__ void consumer_by_tile(const AttnArgs &a, uint8_t *smem, int w, int la
     SoftState<D> st;
     st.reset();
     const int spb = a.stages_per_block;
+    // stage of a block: gs mod spb (a mask when spb is a power of two, as it is for 128-token blocks)
+    const int spb_mask = (spb & (spb - 1)) == 0 ? spb - 1 : -1;
     const int unit0 = __ldg(&a.desc[fb0].unit);
     int cur = -1;  // unit of the warp's state (-1: none yet)
     const int groups = (fb1 - fb0) * spb * C::TPP;
     for (int j = w; j < groups; j += C::NW) {
         const int gs = j / C::TPP, tw = (j % C::TPP) * C::NT;
-        const int t0 = (gs % spb) * C::TSB;
+        const int t0 = (spb_mask >= 0 ? (gs & spb_mask) : gs % spb) * C::TSB;
         const int slot = gs % C::NSLOT;
         const uint32_t empty = ring_bar<D, CP>(sb, C::NSLOT + slot);
         if (!wait_stage<D, CP>(sb, gs)) {
@@ -1041,7 +1070,8 @@ __device__ void consumer_by_tile(const AttnArgs &a, uint8_t *smem, int w, int la
         }
         const uint8_t *sp = smem + slot * C::SLOT;
         const BlockDesc &bd = *reinterpret_cast<const BlockDesc *>(sp);
-        const int valid = bd.valid, unit = bd.unit;
+        const VisitDesc vd = load_visit(smem_u32(sp));
+        const int valid = vd.valid(), unit = vd.unit;
         if (unit != cur) {
             if (cur >= 0) flush_state<D>(a, size_t(row0 + cur - unit0) * C::NW + size_t(w), st, lane);
             const UnitDev *U = a.units + unit;
@@ -1051,7 +1081,7 @@ __device__ void consumer_by_tile(const AttnArgs &a, uint8_t *smem, int w, int la
         }
         const int rows = valid - t0 - TT * tw;
         if (rows > 0) {
-            tile_step<D, CP, BF16IN>(a, bd, smem_u32(sp), empty, xb, sm, tw, t0, min(rows, C::NT * TT), qb, st,
+            tile_step<D, CP, BF16IN>(a, bd, vd, smem_u32(sp), empty, xb, sm, tw, t0, min(rows, C::NT * TT), qb, st,
                                  lane);
         } else {
             __syncwarp();  // every lane has read the descriptor
