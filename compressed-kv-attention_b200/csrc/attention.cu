@@ -93,9 +93,7 @@ template <int D, bool CP = false> struct Cfg {
     static constexpr int S_B7 = 128;
     // Two words the producer writes for the stage: per tensor, the shared address (bit 0 set) from
     // which the stage's staged escape-record entry i is read at + 4 i, or 0 when they stay in HBM.
-    // Then the stage's index in the CTA's sequence of stages (its tag).
     static constexpr int S_INFO = S_B7 + 4 * D;
-    static constexpr int S_TAG = S_INFO + 8;
     static constexpr int S_T = S_INFO + 16;
     static constexpr int SLOT = S_T + 2 * T_BYTES;
     static constexpr int TILE1 = TT * 2 * D;      // one 16-token BF16 tile
@@ -629,7 +627,6 @@ __device__ void producer(const AttnArgs &a, uint8_t *smem, int fb0, int fb1, int
                 }
                 const uint32_t total = __reduce_add_sync(FULL, stage_piece(dst, src, len, full));
                 if (lane == 0) {
-                    sts_u32(dslot + uint32_t(C::S_TAG), uint32_t(gs));
                     if (!BF16IN) {
 #pragma unroll
                         for (int T = 0; T < 2; ++T) {
@@ -660,7 +657,7 @@ __device__ void producer(const AttnArgs &a, uint8_t *smem, int fb0, int fb1, int
 
 // A producer warp with the plan's stage copy lists (AttnArgs::stages): for each of its stages
 // (gs mod NP == pw), wait until the slot is free, then lanes 0-7 issue the stage's pieces as the
-// list gives them and lane 8 writes the stage's tag and escape-entry words and announces the
+// list gives them and lane 8 writes the stage's escape-entry words and announces the
 // stage's bytes on the slot's full barrier.  Each lane keeps its word of the lists of its next PF
 // stages in registers, loaded PF stages ahead.  On a timeout it reports DERR_TIMEOUT and waits
 // (bounded) for the copies it issued before it returns.
@@ -696,7 +693,6 @@ __device__ void producer_listed(const AttnArgs &a, uint8_t *smem, int fb0, int f
         if (lane < 8 && w.z != 0u)
             bulk_g2s(dslot + w.w, reinterpret_cast<const void *>((uint64_t(w.y) << 32) | w.x), w.z, full);
         if (lane == 8) {
-            sts_u32(dslot + uint32_t(C::S_TAG), uint32_t(gs));
             if (!BF16IN) {
                 sts_u32(dslot + uint32_t(C::S_INFO), (w.w & 1u) ? ((dslot + w.x) | 1u) : 0u);
                 sts_u32(dslot + uint32_t(C::S_INFO + 4), (w.w & 2u) ? ((dslot + w.y) | 1u) : 0u);
@@ -1012,28 +1008,20 @@ __device__ void consumer(const AttnArgs &a, uint8_t *smem, int w, int lane, int 
 // Wait until stage gs of the CTA has landed in its slot.  The slot's full barrier alone cannot tell
 // stage gs from stage gs - 2 NSLOT: a warp that skips stages may start waiting while the slot's
 // previous stage (gs - NSLOT) is still in flight, and the parity test would then pass one phase
-// early.  So the warp first reads the stage tag, which the producer writes once the slot is free
-// for stage gs (stage gs - NSLOT landed and was released) and before the arrive that completes
-// stage gs's phase; only when the tag is gs does it test the barrier.  The tag is read with acquire
-// semantics, so the test after it sees at least the phase of stage gs - NSLOT completed, and then
-// passes only when stage gs has landed; the slot then holds stage gs until this warp arrives on the
-// slot's empty barrier.  Returns false after kStageWaitUs (the decision is the warp's, uniform).
+// early.  So the warp first waits until stage gs - NSLOT has been released (the slot's empty
+// barrier completes that use's phase; its next phase needs this warp's own arrive for stage gs, so
+// the parity identifies it).  From then on the full barrier's pending phase is stage gs's, and the
+// second wait passes only when stage gs has landed.  Both waits are mbarrier tests, which suspend
+// the warp while the phase is incomplete instead of spinning on the issue slots the other warps
+// need.  Returns false after kStageWaitUs (the decision is the warp's, uniform).
 template <int D, bool CP>
 __device__ __forceinline__ bool wait_stage(uint32_t sb, int gs) {
     using C = Cfg<D, CP>;
-    const int slot = gs % C::NSLOT;
-    const uint32_t full = ring_bar<D, CP>(sb, slot);
-    const uint32_t tag = sb + uint32_t(slot * C::SLOT + C::S_TAG);
-    const uint32_t par = uint32_t((gs / C::NSLOT) & 1);
-    uint64_t t0 = 0;
-    for (;;) {
-        const bool ok = lds_acquire_u32(tag) == uint32_t(gs) && mbar_try_wait(full, par);
-        if (__all_sync(FULL, ok)) return true;
-        const uint64_t now = global_ns();
-        if (t0 == 0) t0 = now;
-        const bool late = now - t0 > uint64_t(kStageWaitUs) * 1000ull;
-        if (__shfl_sync(FULL, late ? 1 : 0, 0) != 0) return false;
-    }
+    const int slot = gs % C::NSLOT, use = gs / C::NSLOT;
+    if (use > 0 &&
+        !uni(mbar_wait_bounded(ring_bar<D, CP>(sb, C::NSLOT + slot), uint32_t((use - 1) & 1), kStageWaitUs)))
+        return false;
+    return uni(mbar_wait_bounded(ring_bar<D, CP>(sb, slot), uint32_t(use & 1), kStageWaitUs));
 }
 
 // A consumer warp when every block takes the same number of stages (spb): stage s of the range is
@@ -1115,8 +1103,6 @@ __global__ void __launch_bounds__(Cfg<D, CP>::THREADS, 1) attn_kernel(const Attn
             mbar_init(ring_bar<D, CP>(sb, j), 1);               // full: the producer's arrive + bytes
             // empty: one arrive per consumer warp, or per tile group when the warps go by tile
             mbar_init(ring_bar<D, CP>(sb, C::NSLOT + j), by_tile ? C::TPP : C::NW);
-            // no stage yet (shared memory keeps whatever an earlier CTA left there)
-            sts_u32(sb + uint32_t(j * C::SLOT + C::S_TAG), 0xFFFFFFFFu);
         }
         fence_mbar_init();
         // a step whose preparation reported an error (its escape records are incomplete) runs no work
