@@ -111,6 +111,12 @@ template <int D, bool CP = false> struct Cfg {
     // current one: with slots shared between the producers, a producer could test the slot's empty
     // barrier for a phase two uses back and pass one phase early.
     static_assert(NSLOT % NP == 0, "each ring slot is served by one producer warp");
+    // A consumer warp's tile groups are NW groups apart, so its stages at most ceil(NW / TPP) apart.
+    // Its wait for stage gs tests the slot's empty barrier for the release of stage gs - NSLOT by
+    // parity, which is only sound while the barrier is at most one phase behind: stage gs - 2 NSLOT
+    // must be released already.  It is when the warp's previous stage (issued, so every stage
+    // before it was issued, each after its slot's previous release) is at least gs - NSLOT.
+    static_assert((NW + TPP - 1) / TPP <= NSLOT, "a consumer warp's stages are at most NSLOT apart");
     static_assert(32 % C8 == 0 && NIT >= 1, "a warp step covers whole rows");
     static_assert((TSB * D) % 4096 == 0, "stage offsets keep every section's 16-byte alignment");
 };
@@ -354,28 +360,40 @@ __device__ __forceinline__ void zero_rows(const StoreMap<D> &sm, int from, int l
     }
 }
 
+// The escape-record entries where the second, third, ... of a warp's NT tiles begin: entry i belongs
+// to tile tile(i).
+template <int NT> struct EscBounds {
+    int b[NT > 1 ? NT - 1 : 1];
+    __device__ __forceinline__ int tile(int i) const {
+        int k = 0;
+#pragma unroll
+        for (int j = 0; j + 1 < NT; ++j) k += i >= b[j] ? 1 : 0;
+        return k;
+    }
+};
+
 // Store escapes [e0, e1) of a block over their elements in the warp's NT tiles: record entry i
 // (byte of the element in its 16-token tile | escape word << 16) is the u32 at ents + 4 i -- a
-// shared address of the staged copy, or (HBM variant) the record in global memory.  Entries from
-// em on belong to the second tile.  Elements in rows at or past `rows` (counted from the first
-// tile's first row) are skipped; bytes are even.
-__device__ __forceinline__ void esc_store(uint32_t xb, uint32_t e, bool second, int rows, int tile_bytes,
+// shared address of the staged copy, or (HBM variant) the record in global memory; it belongs to
+// tile k.  Elements in rows at or past `rows` (counted from the first tile's first row) are
+// skipped; bytes are even.
+__device__ __forceinline__ void esc_store(uint32_t xb, uint32_t e, int k, int rows, int tile_bytes,
                                           int row_bytes) {
-    const int rt = rows - (second ? kTileTokens : 0);
+    const int rt = rows - k * kTileTokens;
     if ((e & 0xFFFFu) < uint32_t(max(rt, 0)) * uint32_t(row_bytes))
-        sts_u16(xb + (second ? uint32_t(tile_bytes) : 0u) + (e & 0xFFFEu), e >> 16);
+        sts_u16(xb + uint32_t(k * tile_bytes) + (e & 0xFFFEu), e >> 16);
 }
 template <int D>
-__device__ __forceinline__ void esc_patch(uint32_t xb, uint32_t ents, int e0, int e1, int em, int rows,
-                                          int lane) {
+__device__ __forceinline__ void esc_patch(uint32_t xb, uint32_t ents, int e0, int e1,
+                                          const EscBounds<Cfg<D>::NT> &eb, int rows, int lane) {
     for (int i = e0 + lane; i < e1; i += 32)
-        esc_store(xb, lds_u32(ents + 4u * uint32_t(i)), i >= em, rows, Cfg<D>::TILE1, 2 * D);
+        esc_store(xb, lds_u32(ents + 4u * uint32_t(i)), eb.tile(i), rows, Cfg<D>::TILE1, 2 * D);
 }
 template <int D>
-__device__ __noinline__ void esc_patch_hbm(uint32_t xb, const uint32_t *ents, int e0, int e1, int em,
-                                           int rows, int lane) {
+__device__ __noinline__ void esc_patch_hbm(uint32_t xb, const uint32_t *ents, int e0, int e1,
+                                           const EscBounds<Cfg<D>::NT> eb, int rows, int lane) {
     for (int i = e0 + lane; i < e1; i += 32)
-        esc_store(xb, __ldg(ents + i), i >= em, rows, Cfg<D>::TILE1, 2 * D);
+        esc_store(xb, __ldg(ents + i), eb.tile(i), rows, Cfg<D>::TILE1, 2 * D);
 }
 
 // ---- tiles on the tensor cores ------------------------------------------------------------------
@@ -759,10 +777,12 @@ __device__ __forceinline__ void tile_tensor(const AttnArgs &a, const BlockDesc &
     const uint32_t cb = reg + uint32_t(TT * tw * (D * mode / 8));
     // The tiles' escapes [e0, e1) are fetched before the decode, one entry per lane (more than 32
     // occur only in escape-dense blocks; those lanes take the rest after the first 32), so that only
-    // their stores follow the decode.  Entries from em on are the second tile's.
+    // their stores follow the decode.  EscBounds says which tile each entry is in.
     constexpr int NT = C::NT;
     const int e0 = esc_ms(bd, T, g16), e1 = esc_ms(bd, T, g16 + NT);
-    const int em = NT > 1 ? esc_ms(bd, T, g16 + 1) : e1;
+    EscBounds<NT> eb;
+#pragma unroll
+    for (int j = 0; j + 1 < NT; ++j) eb.b[j] = esc_ms(bd, T, g16 + 1 + j);
     uint32_t ents = 0u, ent = 0u;
     if (e1 > e0) {
         ents = lds_u32(info);  // the producer's word for this stage and tensor
@@ -785,12 +805,12 @@ __device__ __forceinline__ void tile_tensor(const AttnArgs &a, const BlockDesc &
         // entry: the element's byte in its tile (bits 0-15, even) | its BF16 word << 16; elements
         // in rows at or past `rows` are skipped
         __syncwarp();  // the decoded words are in place before escapes overwrite some
-        if (e0 + lane < e1) esc_store(xb, ent, e0 + lane >= em, rows, C::TILE1, 2 * D);
+        if (e0 + lane < e1) esc_store(xb, ent, eb.tile(e0 + lane), rows, C::TILE1, 2 * D);
         if (e1 - e0 > 32) {
             if (ents & 1u)
-                esc_patch<D>(xb, ents & ~1u, e0 + 32, e1, em, rows, lane);
+                esc_patch<D>(xb, ents & ~1u, e0 + 32, e1, eb, rows, lane);
             else
-                esc_patch_hbm<D>(xb, a.esc + (T ? vd.v_rec : vd.k_rec) + kEscRecHead, e0 + 32, e1, em,
+                esc_patch_hbm<D>(xb, a.esc + (T ? vd.v_rec : vd.k_rec) + kEscRecHead, e0 + 32, e1, eb,
                                  rows, lane);
         }
     }
