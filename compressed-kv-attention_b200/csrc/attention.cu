@@ -8,17 +8,20 @@
 //    (one CTA per SM).  A CTA streams its blocks through a shared-memory ring of stages; a stage
 //    is up to TSB tokens of one block: the block's descriptor, and per tensor its base exponents,
 //    sign/mantissa rows, packed residual codes and the escape-record entries of those tokens (or
-//    raw BF16 rows).  Two producer warps (alternate stages) issue a stage as a handful of 1-D bulk
-//    copies of the TMA engine, one per lane, that complete on the slot's "full" mbarrier; only the compressed bytes cross HBM
-//    (plus, for a coded block with escapes, its escape record: 4 bytes per escape word and a
-//    64-byte count header, built once per plan).
-//  * The consumer warps (15, or 7 at D = 256) share every stage: the stage's 16-token tiles go round-robin
-//    over them (tile j of the CTA to warp j mod NW), each warp keeping its own online-softmax
-//    state.  A warp rebuilds its tile's K rows into BF16 words in its private tile (16 rows of D
-//    BF16 values, 16-byte chunks swizzled so that neither the decode stores nor the ldmatrix
-//    reads conflict on banks): per pair of elements two byte permutes, one multiply-add that adds
-//    the residual to the base exponent, and one bit-select.  Escape words are stored over their
-//    elements, one 16-bit store each, at the tile byte the escape record gives.
+//    raw BF16 rows).  One producer warp issues each stage from its copy list (built once per plan
+//    by stage_table_kernel): lanes 0-7 each issue one 1-D bulk copy of the TMA engine, completing
+//    on the slot's "full" mbarrier.  Only the compressed bytes cross HBM (plus, for a coded block
+//    with escapes, its escape record: 4 bytes per escape word and a 64-byte count header, built
+//    once per plan).  Steps whose blocks are all coded use a 6-slot ring sized for coded stages,
+//    others a 4-slot ring that also takes raw rows.
+//  * The consumer warps (15 at D <= 64, 11 at D = 128, 7 at D = 256) share every stage: the
+//    stage's 16-token tiles go to them in groups, round-robin (group j of the CTA to warp j mod
+//    NW), each warp keeping its own online-softmax state.  A warp rebuilds its tiles' K rows into
+//    BF16 words in its private tiles (16 rows of D BF16 values, 16-byte chunks swizzled so that
+//    neither the decode stores nor the ldmatrix reads conflict on banks): per pair of elements two
+//    byte permutes, one multiply-add that adds the residual to the base exponent, and one
+//    bit-select.  Escape words are stored over their elements, one 16-bit store each, at the tile
+//    byte the escape record gives.
 //  * S = K Q^T on the tensor cores (mma.sync m16n8k16, tokens x queries, fp32 accumulate), the
 //    online softmax on the S fragment (lane (g, t) holds queries 2t and 2t+1, which are also the
 //    output columns it accumulates), then the tile's V rows replace K in the tile and
