@@ -1155,7 +1155,7 @@ __global__ void __launch_bounds__(Cfg<D, CP>::THREADS, 1) attn_kernel(const Attn
 // the sums run over fixed slices of the states, so the result is deterministic.  A state of a
 // warp that saw none of the unit's tokens has m = -inf and l = 0 (written so, or initialised so
 // by init_partials_kernel and never written) and adds nothing; its accumulators are not read.
-constexpr int kCombineThreads = 256;
+constexpr int kCombineThreads = 512;
 constexpr int kMaxSegments = 4096;
 
 template <int D>
