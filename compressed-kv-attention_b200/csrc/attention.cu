@@ -1273,14 +1273,15 @@ __global__ void fold_kernel(const float *__restrict__ parts, int n_parts, int n_
 // ---- worker ranges -----------------------------------------------------------------------------
 
 // Cost of one flat block for the worker split, per attended token and tensor: 4 with 4-bit
-// residuals, 5 with 2- or 3-bit ones (more unpacking), 2 for raw rows; plus 1 per escape word, which
-// costs a lane one staged load and one store.  (Weighting escapes near a token's cost, as an
-// earlier model did, starved the workers that hold escape-dense blocks and left the others
-// about 10 % more work than a balanced split.)
+// residuals, 5 with 2- or 3-bit ones (more unpacking), 2 for raw rows; plus 1 per 8 escape words
+// (a staged escape costs a lane one shared load and one store, about a thirtieth of a token's
+// decode per tensor).  Heavier escape weights starved the CTAs that hold escape-dense blocks: at
+// 1 per escape word the CTAs holding config[1]'s 2-bit layer-0 K blocks (8 % escapes) finished
+// after 48 of the kernel's 74 us; at 1 per 8 the spread is 66-73 us.
 __device__ __forceinline__ uint64_t mode_cost(int mode) { return mode == 4 ? 4u : (mode == 0 ? 2u : 5u); }
 __device__ __forceinline__ uint64_t block_cost(const FlatBlock &b, bool by_tokens) {
     if (by_tokens) return uint64_t(b.valid);
-    return uint64_t(b.valid) * (mode_cost(b.k_mode) + mode_cost(b.v_mode)) + uint64_t(b.k_nesc) + b.v_nesc;
+    return uint64_t(b.valid) * (mode_cost(b.k_mode) + mode_cost(b.v_mode)) + (uint64_t(b.k_nesc) + b.v_nesc) / 8;
 }
 
 // One CTA: range_begin[w] = first block whose cost prefix reaches w * total / nw.
