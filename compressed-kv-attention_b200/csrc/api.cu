@@ -540,7 +540,7 @@ static int plan_create_impl(const kvx_unit *units, int n_units, int n_q, int dim
         for (int t = 0; t <= p->n_ranges; ++t) tb[size_t(t)] = t;
         e = cudaMemcpy(p->range_begin, tb.data(), tb.size() * sizeof(int64_t), cudaMemcpyHostToDevice);
     } else {
-        e = launch_split(p->flat, total, p->n_ranges, by_tokens, p->range_begin, nullptr);
+        e = launch_split(p->flat, total, p->n_ranges, by_tokens, dim, p->range_begin, nullptr);
         if (e == cudaSuccess)
             e = cudaMemcpy(tb.data(), p->range_begin, tb.size() * sizeof(int64_t),
                            cudaMemcpyDeviceToHost);

@@ -1285,14 +1285,23 @@ __device__ __forceinline__ uint64_t block_cost(const FlatBlock &b, bool by_token
 }
 
 // One CTA: range_begin[w] = first block whose cost prefix reaches w * total / nw.
+// Block b's cost plus unit_cost when it starts a unit: a CTA whose range reaches into another unit
+// pays that unit's query loads, state flushes and fresh softmax states in every consumer warp
+// (measured at config[1]: CTAs spanning two units took 1.4 us, about 1.7 blocks, longer).
+__device__ __forceinline__ uint64_t range_cost(const FlatBlock *flat, int64_t b, bool by_tokens, uint64_t unit_cost) {
+    const FlatBlock f = load_flat(flat, b);
+    const bool first = b == 0 || load_flat(flat, b - 1).unit != f.unit;
+    return block_cost(f, by_tokens) + (first ? unit_cost : 0u);
+}
+
 __global__ void __launch_bounds__(1024) split_kernel(const FlatBlock *flat, int64_t n, int nw,
-                                                     bool by_tokens, int64_t *range_begin) {
+                                                     bool by_tokens, uint64_t unit_cost, int64_t *range_begin) {
     __shared__ unsigned long long part[1024];
     const int t = threadIdx.x, T = blockDim.x;
     const int64_t chunk = (n + T - 1) / T;
     const int64_t lo = min(n, t * chunk), hi = min(n, lo + chunk);
     unsigned long long sum = 0;
-    for (int64_t b = lo; b < hi; ++b) sum += block_cost(load_flat(flat, b), by_tokens);
+    for (int64_t b = lo; b < hi; ++b) sum += range_cost(flat, b, by_tokens, unit_cost);
     part[t] = sum;
     __syncthreads();
     for (int o = 1; o < T; o <<= 1) {  // inclusive scan
@@ -1311,7 +1320,7 @@ __global__ void __launch_bounds__(1024) split_kernel(const FlatBlock *flat, int6
     // worker w starts after the block whose cost interval (c, c + cost] holds w * total / nw
     int w = int(c * uint64_t(nw) / (total ? total : 1));
     for (int64_t b = lo; b < hi; ++b) {
-        const unsigned long long cn = c + block_cost(load_flat(flat, b), by_tokens);
+        const unsigned long long cn = c + range_cost(flat, b, by_tokens, unit_cost);
         while (w < nw && uint64_t(w) * total / nw <= c) ++w;
         while (w < nw && uint64_t(w) * total / nw <= cn) range_begin[w++] = b + 1;
         c = cn;
@@ -1543,9 +1552,12 @@ cudaError_t launch_attention(int dim, bool bf16_input, bool compact, const AttnA
     }
 }
 
-cudaError_t launch_split(const FlatBlock *flat, int64_t n_blocks, int n_ranges, bool by_tokens,
+cudaError_t launch_split(const FlatBlock *flat, int64_t n_blocks, int n_ranges, bool by_tokens, int dim,
                          int64_t *range_begin, cudaStream_t s) {
-    split_kernel<<<1, 1024, 0, s>>>(flat, n_blocks, n_ranges, by_tokens, range_begin);
+    // a unit start costs about 1.5 blocks of 128 tokens at dim 64 (2 x 4 per token and tensor), and
+    // about as much time at other widths (its query loads and flushes are latency-bound)
+    const uint64_t unit_cost = (by_tokens ? 192u : 1536u) * 64u / uint64_t(dim > 0 ? dim : 64);
+    split_kernel<<<1, 1024, 0, s>>>(flat, n_blocks, n_ranges, by_tokens, unit_cost, range_begin);
     return cudaGetLastError();
 }
 

@@ -227,7 +227,7 @@ cudaError_t launch_esc_fill(const UnitDev *units, const FlatBlock *flat, int64_t
 // Cost-balanced CTA ranges over the flat block list: range_begin[0..n_ranges].  by_tokens: every
 // attended token costs the same whatever the block's encoding (the split then depends only on
 // the token counts, so an XKV step and a BF16 step over the same tokens get the same ranges).
-cudaError_t launch_split(const FlatBlock *flat, int64_t n_blocks, int n_ranges, bool by_tokens,
+cudaError_t launch_split(const FlatBlock *flat, int64_t n_blocks, int n_ranges, bool by_tokens, int dim,
                          int64_t *range_begin, cudaStream_t s);
 bool attention_dim_supported(int dim);
 
