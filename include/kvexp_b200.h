@@ -164,7 +164,10 @@ typedef struct kvx_plan_s *kvx_plan;
 /* Build a reusable launch plan for a fixed set of units (host array of n_units descriptors).
  * block_tokens is the encode block size (the tile split of the BF16 kernel).  The plan uploads
  * the descriptors, cuts the step's blocks into one range of about equal decode cost per SM, and
- * owns the scratch for the partial softmax states. */
+ * owns the scratch for the partial softmax states.  Its device memory per (unit, block): a 32 B
+ * flat entry, a 128 B descriptor, 4 dim B of merge words, the escape records (4 B per escape word
+ * plus 64 B per coded block with escapes) and 144 B of stage copy lists per ring stage (one stage
+ * per 128-token block at dim <= 64, two at 128, four at 256). */
 KVX_API int kvx_plan_create(const kvx_unit *units, int n_units, int n_q, int dim, int block_tokens,
                     kvx_plan *plan);
 /* Launch one decode step for every unit on `stream` (a cudaStream_t; NULL = default stream).
