@@ -70,15 +70,8 @@ __device__ inline void mbar_init(uint32_t bar, uint32_t count) {
 __device__ inline void fence_mbar_init() {
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
 }
-__device__ inline void fence_proxy_async() {
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-}
 __device__ inline void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
-                 : "memory");
-}
-__device__ inline void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
-    asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(bytes)
                  : "memory");
 }
 __device__ inline void mbar_arrive(uint32_t bar) {
@@ -145,35 +138,15 @@ __device__ inline void mma_bf16(float &d0, float &d1, float &d2, float &d3, uint
         : "+f"(d0), "+f"(d1), "+f"(d2), "+f"(d3)
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
-// Pack two floats to bf16x2 (round to nearest even): hi <- a, lo <- b.
-__device__ inline uint32_t pack_bf16x2(float a, float b) {
-    uint32_t r;
-    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(a), "f"(b));
-    return r;
-}
 __device__ inline uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
     uint32_t r;
     asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(sel));
     return r;
 }
-__device__ inline float bf16lo_to_f32(uint32_t x) { return __uint_as_float(x << 16); }
-__device__ inline float bf16hi_to_f32(uint32_t x) { return __uint_as_float(x & 0xFFFF0000u); }
 
 __device__ inline uint32_t lds_u32(uint32_t a) {
     uint32_t v;
     asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a));
-    return v;
-}
-// Shared-memory load with acquire semantics at CTA scope: operations after it (an mbarrier test
-// included) observe at least what was visible to its writer when the loaded value was stored.
-__device__ inline uint32_t lds_acquire_u32(uint32_t a) {
-    uint32_t v;
-    asm volatile("ld.acquire.cta.shared::cta.u32 %0, [%1];" : "=r"(v) : "r"(a) : "memory");
-    return v;
-}
-__device__ inline uint32_t lds_u16(uint32_t a) {
-    unsigned short v;
-    asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(a));
     return v;
 }
 __device__ inline void lds_v4(uint32_t a, uint32_t &x, uint32_t &y, uint32_t &z, uint32_t &w) {
@@ -194,11 +167,6 @@ __device__ inline uint32_t lanemask_lt() {
     uint32_t m;
     asm("mov.u32 %0, %%lanemask_lt;" : "=r"(m));
     return m;
-}
-
-// Named barrier for a subset of warps (count threads).
-__device__ inline void named_bar(int id, int count) {
-    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
 
 }  // namespace kvx
